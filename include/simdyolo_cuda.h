@@ -1,0 +1,174 @@
+/*
+ * simdyolo_cuda.h - C ABI of the B200 (sm_100a) detection-head fine-tuning path.
+ *
+ * The reference (SimdYolo, C#/.NET) trains the detection head one image at a time on the CPU
+ * (src/SimdYolo.Training/YoloTrainer.cs:185-199) and offloads only large GEMMs through
+ * IComputeBackend.MatMul (src/SimdYolo/Compute.cs:11-25).  This library moves the whole inner
+ * batch loop behind one call: frozen backbone forward, Detect-head forward/backward with
+ * per-image training BatchNorm, DFL + CIoU + BCE loss with the task-aligned assigner, the
+ * optional NCCL gradient all-reduce and the SGD-momentum / AdamW update.
+ *
+ * Conventions: plain C types; host pointers unless a name says "device"; the caller owns every
+ * buffer it passes and may reuse it as soon as a call returns (calls are synchronous).  Tensors
+ * use the reference layouts: NCHW activations, OIHW weights, float32.  A session is not
+ * reentrant (the C# host serialises calls, YoloTrainer.cs:163-168).
+ *
+ * Status codes map onto the reference's exceptions:
+ *   SY_ERR_INVALID_ARGUMENT  -> ArgumentException            (e.g. DetectionLoss.cs:21,30,51)
+ *   SY_ERR_UNSUPPORTED_SHAPE -> NotSupportedException        (HeadOperations.cs:34, TrainingHeadSchema.cs:44)
+ *   SY_ERR_NONFINITE         -> ArithmeticException          (YoloTrainer.cs:193,196; TrainingParameter.cs:40)
+ *   SY_ERR_COMM, SY_ERR_DEVICE, SY_ERR_OUT_OF_MEMORY -> InvalidOperationException (VulkanBackend.cs:323 style)
+ */
+#ifndef SIMDYOLO_CUDA_H
+#define SIMDYOLO_CUDA_H
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SY_API __attribute__((visibility("default")))
+#else
+#define SY_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t sy_status;
+#define SY_OK 0
+#define SY_ERR_INVALID_ARGUMENT 1
+#define SY_ERR_UNSUPPORTED_SHAPE 2
+#define SY_ERR_NONFINITE 3
+#define SY_ERR_COMM 4
+#define SY_ERR_DEVICE 5
+#define SY_ERR_OUT_OF_MEMORY 6
+
+/* TrainingBox (src/SimdYolo.Training/TrainingTypes.cs:50): class id and xyxy in input pixels. */
+typedef struct sy_box {
+    int32_t class_id;
+    float x1, y1, x2, y2;
+} sy_box;
+
+/* One block of a head branch (DetectionHead.cs:28-75, validated like TrainingHeadSchema.cs:36-46):
+ * Conv/DWConv (has_bn = 1: conv without bias -> BatchNorm -> SiLU) or the final Conv2d
+ * (has_bn = 0, has_bias = 1).  Kernel 1 or 3, stride 1, same padding. */
+typedef struct sy_block {
+    int32_t ic, oc, k, groups, has_bn, has_bias;
+} sy_block;
+
+#define SY_OPT_SGD 0
+#define SY_OPT_ADAMW 1
+#define SY_BACKBONE_NONE 0    /* features are supplied by the caller (cached features)       */
+#define SY_BACKBONE_YOLOV8 1  /* YOLOv8 detection trunk (Conv, C2f, SPPF, Upsample, Concat) */
+
+typedef struct sy_config {
+    int32_t struct_size;        /* sizeof(sy_config) */
+    int32_t device;             /* CUDA device ordinal */
+    int32_t rank, world_size;   /* data-parallel group: one process per GPU */
+    uint8_t nccl_id[128];       /* from sy_cuda_nccl_unique_id on rank 0; ignored when world_size == 1 */
+    int32_t image_size;         /* square input S (multiple of 32) */
+    int32_t max_batch;          /* images per step on this rank */
+    int32_t max_boxes;          /* ground-truth boxes per image (<= 100) */
+    int32_t num_classes;        /* nc */
+    int32_t reg_max;            /* 16 (DFL) */
+    int32_t backbone;           /* SY_BACKBONE_* */
+    float width_mult, depth_mult;
+    int32_t max_channels;
+    int32_t feature_channels[3];/* P3/P4/P5 channels when backbone == SY_BACKBONE_NONE */
+    int32_t n_box_blocks, n_cls_blocks;
+    sy_block box_blocks[3][8];  /* cv2.{0,1,2} */
+    sy_block cls_blocks[3][8];  /* cv3.{0,1,2} */
+    float bn_eps, bn_momentum;  /* DetectionHead.cs:71 (PT defaults 1e-3 / 0.03) */
+    int32_t optimizer;          /* SY_OPT_* */
+    float lr, momentum, weight_decay;
+    float beta1, beta2, adam_eps;
+} sy_config;
+
+/* Per-step results, summed over the global batch (all ranks). */
+typedef struct sy_step_stats {
+    double box, cls, dfl;       /* loss sums; YoloTrainer divides by the batch (YoloTrainer.cs:198) */
+    int64_t positives;
+    int32_t images;             /* global images in the step */
+    int32_t box_has_grad;       /* box branch connected (any positive), DetectionLoss.cs:101 */
+    double grad_checksum;       /* sum of |g| over the averaged head gradient before the update */
+    double device_ms;           /* device time of the step (CUDA events) */
+} sy_step_stats;
+
+typedef struct sy_tensor_info {
+    char name[96];              /* DetectionHead.Snapshot name, e.g. "cv2.0.0.conv.weight" */
+    int32_t kind;               /* 0 parameter, 1 buffer (BN running mean/var/num_batches_tracked) */
+    int32_t rank;
+    int32_t shape[4];
+    int64_t numel;
+} sy_tensor_info;
+
+typedef struct sy_session sy_session;
+
+/* ---- session (replaces YoloTrainer's inner batch loop, YoloTrainer.cs:185-199) ---- */
+SY_API sy_status sy_cuda_nccl_unique_id(uint8_t out[128]);
+SY_API sy_status sy_cuda_create(const sy_config *config, sy_session **out);
+SY_API sy_status sy_cuda_destroy(sy_session *session);
+SY_API const char *sy_cuda_last_error(const sy_session *session);   /* NULL session: last global error */
+
+/* Snapshot-ordered tensors (DetectionHead.Snapshot / Restore, DetectionHead.cs:124-142). */
+SY_API int32_t sy_cuda_tensor_count(const sy_session *session);
+SY_API sy_status sy_cuda_tensor_info(const sy_session *session, int32_t index, sy_tensor_info *out);
+SY_API sy_status sy_cuda_set_tensor(sy_session *session, int32_t index, const float *host, int64_t count);
+SY_API sy_status sy_cuda_get_tensor(const sy_session *session, int32_t index, float *host, int64_t count);
+/* Optimizer state of a parameter tensor (TrainingParameter.Velocity, YoloTrainer.cs:135-141);
+ * moment 0 = SGD velocity / AdamW first moment, 1 = AdamW second moment. */
+SY_API sy_status sy_cuda_set_optimizer_state(sy_session *session, int32_t index, int32_t moment, const float *host,
+                                      int64_t count);
+SY_API sy_status sy_cuda_get_optimizer_state(const sy_session *session, int32_t index, int32_t moment, float *host,
+                                      int64_t count);
+/* Frozen backbone weights with BatchNorm folded (PtModel.cs:128-144): for every conv in trunk
+ * order, OIHW weight then bias. */
+SY_API int64_t sy_cuda_backbone_param_count(const sy_session *session);
+SY_API sy_status sy_cuda_set_backbone(sy_session *session, const float *host, int64_t count);
+
+/* One optimizer step over `images` RGB24 images (images * S * S * 3 bytes, HWC, letterboxed to S)
+ * with boxes[counts[0] + ... + counts[images-1]] in input pixels. */
+SY_API sy_status sy_cuda_step(sy_session *session, const uint8_t *rgb, const sy_box *boxes, const int32_t *counts,
+                       int32_t images, sy_step_stats *out);
+/* Same step from cached frozen features (YoloTrainer.cs:257-261): features[l] is NCHW
+ * [images][C_l][S/8/2^l][S/8/2^l]. */
+SY_API sy_status sy_cuda_step_features(sy_session *session, const float *const features[3], const sy_box *boxes,
+                                const int32_t *counts, int32_t images, sy_step_stats *out);
+/* Gradient of the last step (summed over images, before the update), parameter order. */
+SY_API sy_status sy_cuda_get_last_gradients(const sy_session *session, float *host, int64_t count);
+/* Frozen features of the last step (NCHW per level), for parity checks. */
+SY_API sy_status sy_cuda_get_last_features(const sy_session *session, int32_t level, float *host, int64_t count);
+
+/* ---- standalone operators (same algorithms as the session, host buffers) ---- */
+
+/* DetectionLoss.Compute (DetectionLoss.cs:19-149) for a batch: boxes[l] NCHW [images][4*reg_max][H_l][W_l],
+ * classes[l] NCHW [images][nc][H_l][W_l]; per-image losses out_loss[images][3] (box, cls, dfl),
+ * positives[images]; optional assigned[images][A] (gt index or -1) and scores[images][A];
+ * optional gradients with the same shapes as the inputs. */
+SY_API sy_status sy_cuda_detection_loss(int32_t device, int32_t images, int32_t levels, const int32_t *hs, const int32_t *ws,
+                                 const float *strides, int32_t nc, int32_t reg_max, const float *const *boxes,
+                                 const float *const *classes, const sy_box *truth, const int32_t *counts,
+                                 float *out_loss, int32_t *positives, int32_t *assigned, float *scores,
+                                 float *const *box_grads, float *const *class_grads);
+
+/* HeadOperations.Conv (HeadOperations.cs:29-82) batched: x NCHW [n][ic][h][w], w OIHW [oc][ic][k][k],
+ * stride 1, padding k/2.  forward: y = conv(x, w) (+ bias);  backward_data: dx = conv^T(dy, w);
+ * backward_filter: dw = sum_n dy (*) x (overwrites dw).  k in {1, 3}. */
+SY_API sy_status sy_cuda_conv2d_forward(int32_t device, const float *x, int32_t n, int32_t ic, int32_t h, int32_t w,
+                                 const float *weight, int32_t oc, int32_t k, const float *bias, float *y);
+SY_API sy_status sy_cuda_conv2d_backward_data(int32_t device, const float *dy, int32_t n, int32_t oc, int32_t h, int32_t w,
+                                       const float *weight, int32_t ic, int32_t k, float *dx);
+SY_API sy_status sy_cuda_conv2d_backward_filter(int32_t device, const float *x, const float *dy, int32_t n, int32_t ic,
+                                         int32_t oc, int32_t h, int32_t w, int32_t k, float *dw);
+
+/* IComputeBackend.MatMul (Compute.cs:11-25): C[m,n] = A[m,k] * B[k,n], row-major, C overwritten. */
+SY_API sy_status sy_cuda_matmul(int32_t device, const float *a, const float *b, float *c, int32_t m, int32_t n, int32_t k);
+
+/* TrainingParameter.Update (TrainingParameter.cs:21-43) on one tensor: returns SY_ERR_NONFINITE when
+ * the result is not finite.  has_grad == 0 leaves everything untouched. */
+SY_API sy_status sy_cuda_sgd_update(int32_t device, float *weight, float *velocity, float *grad, int64_t count, float lr,
+                             float momentum, float weight_decay, int32_t images, int32_t has_grad);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,468 @@
+"""simdyolo_b200: B200-native detection-head fine-tuning step behind a C ABI.
+
+The CUDA library (libsimdyolo_cuda.so, built from csrc/ for sm_100a) implements the hot path of
+SimdYolo.Training (YoloTrainer's batch loop: frozen backbone forward, Detect head forward/backward,
+DFL + CIoU + BCE loss with the task-aligned assigner, SGD-momentum / AdamW, NCCL all-reduce).
+This module is the Python mirror of the reference's host API over that ABI (ctypes), used by the
+tests and bench.py.  There is no CPU fallback: every compute call goes to the CUDA library.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libsimdyolo_cuda.so")
+
+SY_OK = 0
+SY_ERR_INVALID_ARGUMENT = 1
+SY_ERR_UNSUPPORTED_SHAPE = 2
+SY_ERR_NONFINITE = 3
+SY_ERR_COMM = 4
+SY_ERR_DEVICE = 5
+SY_ERR_OUT_OF_MEMORY = 6
+SY_OPT_SGD = 0
+SY_OPT_ADAMW = 1
+SY_BACKBONE_NONE = 0
+SY_BACKBONE_YOLOV8 = 1
+
+
+class SyError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"[{status}] {message}")
+        self.status = status
+
+
+class InvalidArgument(SyError, ValueError):
+    """ArgumentException in the reference."""
+
+
+class UnsupportedShape(SyError, NotImplementedError):
+    """NotSupportedException in the reference."""
+
+
+class NonFinite(SyError, ArithmeticError):
+    """ArithmeticException in the reference (YoloTrainer.cs:193,196; TrainingParameter.cs:40)."""
+
+
+def _raise(status: int, message: str):
+    cls = {SY_ERR_INVALID_ARGUMENT: InvalidArgument, SY_ERR_UNSUPPORTED_SHAPE: UnsupportedShape,
+           SY_ERR_NONFINITE: NonFinite}.get(status, SyError)
+    raise cls(status, message)
+
+
+class Box(C.Structure):
+    _fields_ = [("class_id", C.c_int32), ("x1", C.c_float), ("y1", C.c_float), ("x2", C.c_float), ("y2", C.c_float)]
+
+
+class Block(C.Structure):
+    _fields_ = [("ic", C.c_int32), ("oc", C.c_int32), ("k", C.c_int32), ("groups", C.c_int32),
+                ("has_bn", C.c_int32), ("has_bias", C.c_int32)]
+
+
+class Config(C.Structure):
+    _fields_ = [("struct_size", C.c_int32), ("device", C.c_int32), ("rank", C.c_int32), ("world_size", C.c_int32),
+                ("nccl_id", C.c_uint8 * 128), ("image_size", C.c_int32), ("max_batch", C.c_int32),
+                ("max_boxes", C.c_int32), ("num_classes", C.c_int32), ("reg_max", C.c_int32),
+                ("backbone", C.c_int32), ("width_mult", C.c_float), ("depth_mult", C.c_float),
+                ("max_channels", C.c_int32), ("feature_channels", C.c_int32 * 3), ("n_box_blocks", C.c_int32),
+                ("n_cls_blocks", C.c_int32), ("box_blocks", (Block * 8) * 3), ("cls_blocks", (Block * 8) * 3),
+                ("bn_eps", C.c_float), ("bn_momentum", C.c_float), ("optimizer", C.c_int32), ("lr", C.c_float),
+                ("momentum", C.c_float), ("weight_decay", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float),
+                ("adam_eps", C.c_float)]
+
+
+class StepStats(C.Structure):
+    _fields_ = [("box", C.c_double), ("cls", C.c_double), ("dfl", C.c_double), ("positives", C.c_int64),
+                ("images", C.c_int32), ("box_has_grad", C.c_int32), ("grad_checksum", C.c_double),
+                ("device_ms", C.c_double)]
+
+
+class TensorInfo(C.Structure):
+    _fields_ = [("name", C.c_char * 96), ("kind", C.c_int32), ("rank", C.c_int32), ("shape", C.c_int32 * 4),
+                ("numel", C.c_int64)]
+
+
+_lib = None
+
+
+def lib():
+    """Load the CUDA library; fails loudly when it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m simdyolo_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        vp, fp, ip = C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_int32)
+        st = C.c_int32
+        L.sy_cuda_last_error.restype = C.c_char_p
+        L.sy_cuda_last_error.argtypes = [vp]
+        L.sy_cuda_nccl_unique_id.argtypes = [C.POINTER(C.c_uint8)]
+        L.sy_cuda_create.argtypes = [C.POINTER(Config), C.POINTER(vp)]
+        L.sy_cuda_destroy.argtypes = [vp]
+        L.sy_cuda_tensor_count.argtypes = [vp]
+        L.sy_cuda_tensor_count.restype = C.c_int32
+        L.sy_cuda_tensor_info.argtypes = [vp, C.c_int32, C.POINTER(TensorInfo)]
+        for name in ("sy_cuda_set_tensor", "sy_cuda_get_tensor"):
+            getattr(L, name).argtypes = [vp, C.c_int32, fp, C.c_int64]
+        for name in ("sy_cuda_set_optimizer_state", "sy_cuda_get_optimizer_state"):
+            getattr(L, name).argtypes = [vp, C.c_int32, C.c_int32, fp, C.c_int64]
+        L.sy_cuda_backbone_param_count.argtypes = [vp]
+        L.sy_cuda_backbone_param_count.restype = C.c_int64
+        L.sy_cuda_set_backbone.argtypes = [vp, fp, C.c_int64]
+        L.sy_cuda_step.argtypes = [vp, C.POINTER(C.c_uint8), C.POINTER(Box), ip, C.c_int32, C.POINTER(StepStats)]
+        L.sy_cuda_step_features.argtypes = [vp, C.POINTER(fp), C.POINTER(Box), ip, C.c_int32, C.POINTER(StepStats)]
+        L.sy_cuda_get_last_gradients.argtypes = [vp, fp, C.c_int64]
+        L.sy_cuda_get_last_features.argtypes = [vp, C.c_int32, fp, C.c_int64]
+        L.sy_cuda_detection_loss.argtypes = [C.c_int32, C.c_int32, C.c_int32, ip, ip, fp, C.c_int32, C.c_int32,
+                                             C.POINTER(fp), C.POINTER(fp), C.POINTER(Box), ip, fp, ip, ip, fp,
+                                             C.POINTER(fp), C.POINTER(fp)]
+        L.sy_cuda_conv2d_forward.argtypes = [C.c_int32, fp, C.c_int32, C.c_int32, C.c_int32, C.c_int32, fp, C.c_int32,
+                                             C.c_int32, fp, fp]
+        L.sy_cuda_conv2d_backward_data.argtypes = [C.c_int32, fp, C.c_int32, C.c_int32, C.c_int32, C.c_int32, fp,
+                                                   C.c_int32, C.c_int32, fp]
+        L.sy_cuda_conv2d_backward_filter.argtypes = [C.c_int32, fp, fp, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                                     C.c_int32, C.c_int32, fp]
+        L.sy_cuda_matmul.argtypes = [C.c_int32, fp, fp, fp, C.c_int32, C.c_int32, C.c_int32]
+        L.sy_cuda_sgd_update.argtypes = [C.c_int32, fp, fp, fp, C.c_int64, C.c_float, C.c_float, C.c_float, C.c_int32,
+                                         C.c_int32]
+        for name in dir(L):
+            pass
+        _lib = L
+    return _lib
+
+
+EXPORTED = ["sy_cuda_nccl_unique_id", "sy_cuda_create", "sy_cuda_destroy", "sy_cuda_last_error",
+            "sy_cuda_tensor_count", "sy_cuda_tensor_info", "sy_cuda_set_tensor", "sy_cuda_get_tensor",
+            "sy_cuda_set_optimizer_state", "sy_cuda_get_optimizer_state", "sy_cuda_backbone_param_count",
+            "sy_cuda_set_backbone", "sy_cuda_step", "sy_cuda_step_features", "sy_cuda_get_last_gradients",
+            "sy_cuda_get_last_features", "sy_cuda_detection_loss", "sy_cuda_conv2d_forward",
+            "sy_cuda_conv2d_backward_data", "sy_cuda_conv2d_backward_filter", "sy_cuda_matmul", "sy_cuda_sgd_update"]
+
+
+def _check(status: int, session=None):
+    if status != SY_OK:
+        msg = lib().sy_cuda_last_error(session)
+        _raise(status, msg.decode() if msg else "")
+
+
+def _fp(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+def _ip(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_int32))
+
+
+# ------------------------------------------------------------------ model description
+
+def _make_div8(x: float) -> int:
+    return int(np.ceil(np.float32(x) / np.float32(8.0))) * 8
+
+
+def yolov8_channels(width: float, max_channels: int):
+    ch = lambda c: _make_div8(np.float32(min(c, max_channels)) * np.float32(width))
+    return ch(256), ch(512), ch(1024)
+
+
+def yolov8_backbone_convs(width: float, depth: float, max_channels: int):
+    """(oc, ic, k) of every conv of the YOLOv8 trunk in parameter order (weights then bias)."""
+    ch = lambda c: _make_div8(np.float32(min(c, max_channels)) * np.float32(width))
+    dep = lambda n: max(int(np.floor(n * depth + 0.5)), 1)
+    c64, c128, c256, c512, c1024 = ch(64), ch(128), ch(256), ch(512), ch(1024)
+    n3, n6 = dep(3), dep(6)
+    convs = []
+
+    def conv(ic, oc, k):
+        convs.append((oc, ic, k))
+
+    def c2f(c1, c2, n):
+        c = c2 // 2
+        conv(c1, 2 * c, 1)
+        for _ in range(n):
+            conv(c, c, 3)
+            conv(c, c, 3)
+        conv((2 + n) * c, c2, 1)
+
+    conv(3, c64, 3)
+    conv(c64, c128, 3)
+    c2f(c128, c128, n3)
+    conv(c128, c256, 3)
+    c2f(c256, c256, n6)
+    conv(c256, c512, 3)
+    c2f(c512, c512, n6)
+    conv(c512, c1024, 3)
+    c2f(c1024, c1024, n3)
+    conv(c1024, c1024 // 2, 1)
+    conv(c1024 // 2 * 4, c1024, 1)
+    c2f(c1024 + c512, c512, n3)
+    c2f(c512 + c256, c256, n3)
+    conv(c256, c256, 3)
+    c2f(c256 + c512, c512, n3)
+    conv(c512, c512, 3)
+    c2f(c512 + c1024, c1024, n3)
+    return convs
+
+
+def detect_head_blocks(feature_channels, nc: int, reg_max: int = 16):
+    """Ultralytics Detect head: cv2 = Conv(c,c2,3), Conv(c2,c2,3), Conv2d(c2,4*reg_max,1);
+    cv3 = Conv(c,c3,3), Conv(c3,c3,3), Conv2d(c3,nc,1) with c2 = max(16, ch0/4, 4*reg_max),
+    c3 = max(ch0, min(nc, 100))."""
+    ch0 = feature_channels[0]
+    c2 = max(16, ch0 // 4, 4 * reg_max)
+    c3 = max(ch0, min(nc, 100))
+    box, cls = [], []
+    for c in feature_channels:
+        box.append([(c, c2, 3, 1, 1, 0), (c2, c2, 3, 1, 1, 0), (c2, 4 * reg_max, 1, 1, 0, 1)])
+        cls.append([(c, c3, 3, 1, 1, 0), (c3, c3, 3, 1, 1, 0), (c3, nc, 1, 1, 0, 1)])
+    return box, cls
+
+
+MODELS = {
+    # name: (width, depth, max_channels)
+    "yolov8n": (0.25, 0.33, 1024),
+    "yolov8s": (0.50, 0.33, 1024),
+    "yolov8l": (1.00, 1.00, 512),
+}
+
+
+def make_config(model: str = "yolov8n", image_size: int = 640, max_batch: int = 8, max_boxes: int = 8,
+                num_classes: int = 80, device: int = 0, rank: int = 0, world_size: int = 1, nccl_id: bytes = b"",
+                backbone: bool = True, optimizer: int = SY_OPT_SGD, lr: float = 0.01, momentum: float = 0.937,
+                weight_decay: float = 5e-4, beta1: float = 0.9, beta2: float = 0.999, adam_eps: float = 1e-8,
+                bn_eps: float = 1e-3, bn_momentum: float = 0.03) -> Config:
+    width, depth, max_ch = MODELS[model]
+    feats = yolov8_channels(width, max_ch)
+    cfg = Config()
+    cfg.struct_size = C.sizeof(Config)
+    cfg.device, cfg.rank, cfg.world_size = device, rank, world_size
+    for i, b in enumerate(nccl_id[:128]):
+        cfg.nccl_id[i] = b
+    cfg.image_size, cfg.max_batch, cfg.max_boxes = image_size, max_batch, max_boxes
+    cfg.num_classes, cfg.reg_max = num_classes, 16
+    cfg.backbone = SY_BACKBONE_YOLOV8 if backbone else SY_BACKBONE_NONE
+    cfg.width_mult, cfg.depth_mult, cfg.max_channels = width, depth, max_ch
+    for i in range(3):
+        cfg.feature_channels[i] = feats[i]
+    box, cls = detect_head_blocks(feats, num_classes)
+    cfg.n_box_blocks, cfg.n_cls_blocks = len(box[0]), len(cls[0])
+    for lvl in range(3):
+        for i, b in enumerate(box[lvl]):
+            cfg.box_blocks[lvl][i] = Block(*b)
+        for i, b in enumerate(cls[lvl]):
+            cfg.cls_blocks[lvl][i] = Block(*b)
+    cfg.bn_eps, cfg.bn_momentum = bn_eps, bn_momentum
+    cfg.optimizer, cfg.lr, cfg.momentum, cfg.weight_decay = optimizer, lr, momentum, weight_decay
+    cfg.beta1, cfg.beta2, cfg.adam_eps = beta1, beta2, adam_eps
+    return cfg
+
+
+# ------------------------------------------------------------------ session
+
+class Session:
+    """One data-parallel rank of the fine-tuning step (YoloTrainer's batch loop on the GPU)."""
+
+    def __init__(self, config: Config):
+        self.config = config
+        h = C.c_void_p()
+        _check(lib().sy_cuda_create(C.byref(config), C.byref(h)))
+        self._h = h
+        n = lib().sy_cuda_tensor_count(h)
+        self.tensors = []
+        for i in range(n):
+            info = TensorInfo()
+            _check(lib().sy_cuda_tensor_info(h, i, C.byref(info)), h)
+            self.tensors.append(dict(index=i, name=info.name.decode(), kind=info.kind,
+                                     shape=tuple(info.shape[:info.rank]), numel=int(info.numel)))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().sy_cuda_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    @property
+    def params(self):
+        return [t for t in self.tensors if t["kind"] == 0]
+
+    def set_tensor(self, index: int, values: np.ndarray):
+        v = np.ascontiguousarray(values, np.float32).ravel()
+        _check(lib().sy_cuda_set_tensor(self._h, index, _fp(v), v.size), self._h)
+
+    def get_tensor(self, index: int) -> np.ndarray:
+        t = self.tensors[index]
+        out = np.zeros(t["numel"], np.float32)
+        _check(lib().sy_cuda_get_tensor(self._h, index, _fp(out), out.size), self._h)
+        return out.reshape(t["shape"]) if t["shape"] else out
+
+    def set_optimizer_state(self, index: int, moment: int, values: np.ndarray):
+        v = np.ascontiguousarray(values, np.float32).ravel()
+        _check(lib().sy_cuda_set_optimizer_state(self._h, index, moment, _fp(v), v.size), self._h)
+
+    def get_optimizer_state(self, index: int, moment: int = 0) -> np.ndarray:
+        t = self.tensors[index]
+        out = np.zeros(t["numel"], np.float32)
+        _check(lib().sy_cuda_get_optimizer_state(self._h, index, moment, _fp(out), out.size), self._h)
+        return out
+
+    def backbone_param_count(self) -> int:
+        return int(lib().sy_cuda_backbone_param_count(self._h))
+
+    def set_backbone(self, values: np.ndarray):
+        v = np.ascontiguousarray(values, np.float32).ravel()
+        _check(lib().sy_cuda_set_backbone(self._h, _fp(v), v.size), self._h)
+
+    def flat_params(self) -> np.ndarray:
+        return np.concatenate([self.get_tensor(t["index"]).ravel() for t in self.params])
+
+    def flat_buffers(self) -> np.ndarray:
+        return np.concatenate([self.get_tensor(t["index"]).ravel() for t in self.tensors if t["kind"] == 1])
+
+    def set_flat_params(self, flat: np.ndarray):
+        off = 0
+        for t in self.params:
+            self.set_tensor(t["index"], flat[off:off + t["numel"]])
+            off += t["numel"]
+
+    def set_flat_buffers(self, flat: np.ndarray):
+        off = 0
+        for t in self.tensors:
+            if t["kind"] == 1:
+                self.set_tensor(t["index"], flat[off:off + t["numel"]])
+                off += t["numel"]
+
+    def flat_velocity(self, moment: int = 0) -> np.ndarray:
+        return np.concatenate([self.get_optimizer_state(t["index"], moment) for t in self.params])
+
+    @staticmethod
+    def _boxes(boxes_per_image):
+        counts = np.array([len(b) for b in boxes_per_image], np.int32)
+        flat = [bx for b in boxes_per_image for bx in b]
+        arr = (Box * max(1, len(flat)))()
+        for i, (c, x1, y1, x2, y2) in enumerate(flat):
+            arr[i] = Box(int(c), float(x1), float(y1), float(x2), float(y2))
+        return arr, counts
+
+    def step(self, images: np.ndarray, boxes_per_image) -> StepStats:
+        """images: uint8 [B, S, S, 3] RGB (letterboxed); boxes_per_image: list of (cls, x1, y1, x2, y2)."""
+        img = np.ascontiguousarray(images, np.uint8)
+        arr, counts = self._boxes(boxes_per_image)
+        stats = StepStats()
+        _check(lib().sy_cuda_step(self._h, img.ctypes.data_as(C.POINTER(C.c_uint8)), arr, _ip(counts), img.shape[0],
+                                  C.byref(stats)), self._h)
+        return stats
+
+    def step_features(self, features, boxes_per_image) -> StepStats:
+        feats = [np.ascontiguousarray(f, np.float32) for f in features]
+        arr, counts = self._boxes(boxes_per_image)
+        ptrs = (C.POINTER(C.c_float) * 3)(*[_fp(f) for f in feats])
+        stats = StepStats()
+        _check(lib().sy_cuda_step_features(self._h, ptrs, arr, _ip(counts), feats[0].shape[0], C.byref(stats)),
+               self._h)
+        return stats
+
+    def last_gradients(self) -> np.ndarray:
+        n = sum(t["numel"] for t in self.params)
+        out = np.zeros(n, np.float32)
+        _check(lib().sy_cuda_get_last_gradients(self._h, _fp(out), n), self._h)
+        return out
+
+    def last_features(self, level: int, shape) -> np.ndarray:
+        out = np.zeros(int(np.prod(shape)), np.float32)
+        _check(lib().sy_cuda_get_last_features(self._h, level, _fp(out), out.size), self._h)
+        return out.reshape(shape)
+
+
+def nccl_unique_id() -> bytes:
+    buf = (C.c_uint8 * 128)()
+    _check(lib().sy_cuda_nccl_unique_id(buf))
+    return bytes(buf)
+
+
+# ------------------------------------------------------------------ standalone operators
+
+def detection_loss(boxes, classes, strides, truth, nc, device=0, with_grad=True):
+    """DetectionLoss.Compute on the GPU for a batch.  boxes[l]: [B, 64, H, W]; classes[l]: [B, nc, H, W];
+    truth: list (per image) of (cls, x1, y1, x2, y2).  Returns (loss[B,3], positives[B], assigned[B,A],
+    scores[B,A], dbox list, dcls list)."""
+    bl = [np.ascontiguousarray(b, np.float32) for b in boxes]
+    cl = [np.ascontiguousarray(c, np.float32) for c in classes]
+    B = bl[0].shape[0]
+    hs = np.array([b.shape[2] for b in bl], np.int32)
+    ws = np.array([b.shape[3] for b in bl], np.int32)
+    st = np.array(strides, np.float32)
+    A = int((hs * ws).sum())
+    arr, counts = Session._boxes(truth)
+    loss = np.zeros((B, 3), np.float32)
+    pos = np.zeros(B, np.int32)
+    assigned = np.zeros((B, A), np.int32)
+    scores = np.zeros((B, A), np.float32)
+    db = [np.zeros_like(b) for b in bl] if with_grad else None
+    dc = [np.zeros_like(c) for c in cl] if with_grad else None
+    P = C.POINTER(C.c_float) * len(bl)
+    _check(lib().sy_cuda_detection_loss(device, B, len(bl), _ip(hs), _ip(ws), _fp(st), nc, 16, P(*map(_fp, bl)),
+                                        P(*map(_fp, cl)), arr, _ip(counts), _fp(loss), _ip(pos), _ip(assigned),
+                                        _fp(scores), P(*map(_fp, db)) if with_grad else None,
+                                        P(*map(_fp, dc)) if with_grad else None))
+    return loss, pos, assigned, scores, db, dc
+
+
+def conv2d_forward(x, w, bias=None, device=0):
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    n, ic, h, wd = x.shape
+    oc, _, k, _ = w.shape
+    y = np.zeros((n, oc, h, wd), np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    _check(lib().sy_cuda_conv2d_forward(device, _fp(x), n, ic, h, wd, _fp(w), oc, k, None if b is None else _fp(b),
+                                        _fp(y)))
+    return y
+
+
+def conv2d_backward_data(dy, w, device=0):
+    dy = np.ascontiguousarray(dy, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    n, oc, h, wd = dy.shape
+    _, ic, k, _ = w.shape
+    dx = np.zeros((n, ic, h, wd), np.float32)
+    _check(lib().sy_cuda_conv2d_backward_data(device, _fp(dy), n, oc, h, wd, _fp(w), ic, k, _fp(dx)))
+    return dx
+
+
+def conv2d_backward_filter(x, dy, k, device=0):
+    x = np.ascontiguousarray(x, np.float32)
+    dy = np.ascontiguousarray(dy, np.float32)
+    n, ic, h, wd = x.shape
+    oc = dy.shape[1]
+    dw = np.zeros((oc, ic, k, k), np.float32)
+    _check(lib().sy_cuda_conv2d_backward_filter(device, _fp(x), _fp(dy), n, ic, oc, h, wd, k, _fp(dw)))
+    return dw
+
+
+def matmul(a, b, device=0):
+    """IComputeBackend.MatMul (Compute.cs:11-25): C = A @ B, row-major."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.zeros((m, n), np.float32)
+    _check(lib().sy_cuda_matmul(device, _fp(a), _fp(b), _fp(c), m, n, k))
+    return c
+
+
+def sgd_update(w, v, g, lr, momentum, wd, images, has_grad=True, device=0):
+    """TrainingParameter.Update on float32 arrays in place; raises NonFinite like the reference."""
+    _check(lib().sy_cuda_sgd_update(device, _fp(w), _fp(v), _fp(g), w.size, lr, momentum, wd, images, int(has_grad)))

@@ -1,0 +1,485 @@
+// tcgen05 implicit-GEMM convolutions for sm_100a (TF32 inputs, FP32 accumulation in TMEM).
+//
+// Forward / data-gradient kernel (conv_fwd_tc): persistent, one 128-row tile of the padded
+// activation matrix per iteration.  Warp 0 issues TMA loads (A: 128 rows x 32 channels of the
+// input, shifted by the tap's row offset; B: N rows x 32 k of the K-major weights), warp 1 issues
+// tcgen05.mma (K = 8 per instruction) into one of two TMEM accumulators, warps 2-5 drain the other
+// accumulator (bias, SiLU, residual, halo masking) while the next tile accumulates.
+//
+// Weight-gradient kernel (conv_wgrad_tc): split-K over pixel rows.  Both operands are read in
+// their natural channels-last layout and fed to the tensor cores as MN-major (transposed)
+// matrices: A = input channels (4 blocks of 32, each one (tap, channel block)), B = output-grad
+// channels; K = pixel rows.  Partial sums go to a workspace that a second kernel reduces.
+//
+// Replaces the reference's im2col + GEMM (HeadOperations.cs:39-47 forward, :58-70 wgrad / dgrad,
+// TrainingMatMul.cs:14-49) and the Vulkan SGEMM shader it dispatches to (shaders/gemm.comp).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <stdexcept>
+#include <string>
+
+#include "kernels.h"
+
+namespace sy {
+
+// ------------------------------------------------------------------ tensor-map creation
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p)
+            throw std::runtime_error("cuTensorMapEncodeTiled unavailable");
+        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2D fp32 tensor map: inner dimension `inner` elements (contiguous), `outer` rows `pitch_floats`
+// apart; box (box_inner, box_outer) with 128-byte swizzle; out-of-bounds elements read as zero.
+static CUtensorMap make_map_2d(const float* base, long inner, long outer, long pitch_floats, int box_inner,
+                               int box_outer) {
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (pitch_floats * 4) % 16 != 0)
+        throw std::runtime_error("tensor map base / pitch not 16-byte aligned");
+    CUtensorMap map;
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)pitch_floats * 4};
+    cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = get_encode()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return map;
+}
+
+static int num_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    }
+    return n;
+}
+
+// ------------------------------------------------------------------ forward / dgrad kernel
+struct FwdParams {
+    int num_tiles;
+    int taps, kchunks, kpad;
+    int shift[9];
+    int n;          // MMA N (multiple of 16, <= 256)
+    int n_valid;    // channels stored
+    int n0;         // first weight row of this launch
+    int stages;
+    int acc_cols;   // TMEM columns between the two accumulators
+    int alloc_cols;
+    float* out;
+    int out_pitch;
+    const float* bias;
+    const float* residual;
+    int res_pitch;
+    int silu;
+    int mask;
+    Grid grid;
+    int* err;
+};
+
+constexpr int kFwdThreads = 192;
+constexpr int kTileM = 128;
+constexpr int kABytes = kTileM * 128;  // 128 rows x 32 fp32
+
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    conv_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const FwdParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int b_bytes = p.n * 128;
+    const int stage_bytes = (kABytes + b_bytes + 1023) & ~1023;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * stage_bytes);
+    uint64_t* empty = full + p.stages;
+    uint64_t* tfull = empty + p.stages;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.stages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 128);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, p.alloc_cols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int kblocks = p.taps * p.kchunks;
+    const uint32_t tx_bytes = kABytes + b_bytes;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+                const int m0 = tile * kTileM;
+                for (int kb = 0; kb < kblocks; kb++, it++) {
+                    const int s = it % p.stages;
+                    const uint32_t ph = (it / p.stages) & 1;
+                    if (!(ok = mbar_wait(&empty[s], ph ^ 1, p.err, 1))) break;
+                    const int t = kb / p.kchunks, c = kb - t * p.kchunks;
+                    uint8_t* sa = smem + s * stage_bytes;
+                    mbar_arrive_expect_tx(&full[s], tx_bytes);
+                    tma_load_2d(sa, &tmA, &full[s], c * 32, m0 + p.shift[t]);
+                    tma_load_2d(sa + kABytes, &tmB, &full[s], t * p.kpad + c * 32, p.n0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_tf32(p.n, 0, 0);
+            int it = 0, local = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, local++) {
+                const int acc = local & 1;
+                const uint32_t aph = (local >> 1) & 1;
+                if (!(ok = mbar_wait(&tempty[acc], aph ^ 1, p.err, 2))) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + acc * p.acc_cols;
+                for (int kb = 0; kb < kblocks; kb++, it++) {
+                    const int s = it % p.stages;
+                    const uint32_t ph = (it / p.stages) & 1;
+                    if (!(ok = mbar_wait(&full[s], ph, p.err, 3))) break;
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + s * stage_bytes);
+                    const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        uint64_t ad = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+                        uint64_t bd = smem_desc_sw128(b_addr + k * 32, 16, 1024);
+                        mma_tf32(d, ad, bd, idesc, (kb | k) != 0);
+                    }
+                    mma_commit(&empty[s]);
+                }
+                mma_commit(&tfull[acc]);
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
+            const int acc = local & 1;
+            const uint32_t aph = (local >> 1) & 1;
+            if (!mbar_wait(&tfull[acc], aph, p.err, 4)) break;
+            tc_fence_after();
+            const long m = (long)tile * kTileM + row;
+            const int r = (int)(m % p.grid.rows);
+            const bool inside = !p.mask || p.grid.interior(r);
+            float* orow = p.out + m * (long)p.out_pitch;
+            const float* rrow = p.residual ? p.residual + m * (long)p.res_pitch : nullptr;
+            for (int j = 0; j < p.n; j += 16) {
+                float v[16];
+                tmem_ld16(tmem_base + acc * p.acc_cols + ((uint32_t)(q * 32) << 16) + j, v);
+                if (j >= p.n_valid) continue;
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    float x = v[i];
+                    if (p.bias) x += p.bias[p.n0 + j + i];
+                    if (p.silu) x = silu_f(x);
+                    if (rrow) x += rrow[j + i];
+                    v[i] = inside ? x : 0.0f;
+                }
+                if (j + 16 <= p.n_valid) {
+                    float4* dst = reinterpret_cast<float4*>(orow + j);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                } else {
+                    for (int i = 0; i < 16 && j + i < p.n_valid; i++) orow[j + i] = v[i];
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, p.alloc_cols);
+    }
+}
+
+static int pow2_at_least(int v) {
+    int r = 32;
+    while (r < v) r <<= 1;
+    return r;
+}
+
+void conv_tc_forward(const View& in, const float* wk, int n_rows, int n_out, int taps, int shift_sign,
+                     const Grid& grid, const View& out, const ConvEpilogue& ep, int* err, cudaStream_t stream) {
+    const int kchunks = (in.channels + 31) / 32, kpad = kchunks * 32;
+    if (in.rows % kTileM != 0) throw std::runtime_error("conv_tc_forward: rows not a multiple of 128");
+    if ((out.pitch % 4) != 0 || (reinterpret_cast<uintptr_t>(out.base) & 15) != 0)
+        throw std::runtime_error("conv_tc_forward: output not 16-byte aligned");
+    CUtensorMap ta = make_map_2d(in.base, in.channels, in.rows, in.pitch, 32, kTileM);
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(conv_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        attr_set = true;
+    }
+    for (int n0 = 0; n0 < n_out; n0 += 256) {
+        const int n_valid = std::min(256, n_out - n0);
+        const int n = (n_valid + 15) / 16 * 16;
+        CUtensorMap tb = make_map_2d(wk, (long)taps * kpad, n_rows, (long)taps * kpad, 32, n);
+        FwdParams p;
+        p.num_tiles = (int)(in.rows / kTileM);
+        p.taps = taps;
+        p.kchunks = kchunks;
+        p.kpad = kpad;
+        for (int t = 0; t < 9; t++) p.shift[t] = 0;
+        if (taps == 9)
+            for (int t = 0; t < 9; t++) p.shift[t] = shift_sign * ((t / 3 - 1) * grid.wp + (t % 3 - 1));
+        p.n = n;
+        p.n_valid = n_valid;
+        p.n0 = n0;
+        const int stage_bytes = (kABytes + n * 128 + 1023) & ~1023;
+        p.stages = std::min(8, (int)((220 * 1024) / stage_bytes));
+        p.alloc_cols = pow2_at_least(2 * n);
+        p.acc_cols = p.alloc_cols / 2;
+        p.out = out.base + n0;
+        p.out_pitch = out.pitch;
+        p.bias = ep.bias;
+        p.residual = ep.residual ? ep.residual + n0 : nullptr;
+        p.res_pitch = ep.res_pitch;
+        p.silu = ep.silu;
+        p.mask = ep.mask_halo;
+        p.grid = grid;
+        p.err = err;
+        const size_t smem = 1024 + (size_t)p.stages * stage_bytes + (2 * p.stages + 4) * 8 + 16;
+        const int grid_x = std::min(p.num_tiles, num_sms());
+        conv_fwd_tc_kernel<<<grid_x, kFwdThreads, smem, stream>>>(ta, tb, p);
+    }
+}
+
+// ------------------------------------------------------------------ weight-gradient kernel
+struct WgradParams {
+    int taps, kchunks;       // input-channel blocks of 32 per tap
+    int total_chunks;        // taps * kchunks
+    int shift[9];
+    int n;                   // output-gradient channels (MMA N, multiple of 16)
+    int nblocks;             // ceil(n / 32)
+    long rows;               // pixel rows (K)
+    long rows_per_split;     // multiple of 32
+    int stages;
+    int alloc_cols;
+    int oob_channel;         // channel coordinate that lies outside the input view (zero fill)
+    float* ws;               // [split][m_tiles * 128][n]
+    int m_tiles;
+    int* err;
+};
+
+constexpr int kWgradBK = 32;                    // pixel rows per stage
+constexpr int kWgradBlockBytes = kWgradBK * 128;  // one 32-channel x 32-row box
+
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    conv_wgrad_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmG,
+                         const WgradParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int a_bytes = 4 * kWgradBlockBytes;
+    const int b_bytes = p.nblocks * kWgradBlockBytes;
+    const int stage_bytes = a_bytes + b_bytes;  // multiples of 4096
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * stage_bytes);
+    uint64_t* empty = full + p.stages;
+    uint64_t* tfull = empty + p.stages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m_tile = blockIdx.x, split = blockIdx.y;
+    const long k_begin = (long)split * p.rows_per_split;
+    const long k_end = p.rows < k_begin + p.rows_per_split ? p.rows : k_begin + p.rows_per_split;
+    const int kblocks = k_end > k_begin ? (int)((k_end - k_begin + kWgradBK - 1) / kWgradBK) : 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.stages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&tfull[0], 1);
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmX);
+        prefetch_tmap(&tmG);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, p.alloc_cols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int ch_coord[4], tap_shift[4];
+            for (int j = 0; j < 4; j++) {
+                int g = m_tile * 4 + j;
+                if (g < p.total_chunks) {
+                    int t = g / p.kchunks, cb = g - t * p.kchunks;
+                    ch_coord[j] = cb * 32;
+                    tap_shift[j] = p.shift[t];
+                } else {
+                    ch_coord[j] = p.oob_channel;
+                    tap_shift[j] = 0;
+                }
+            }
+            for (int kb = 0; kb < kblocks; kb++) {
+                const int s = kb % p.stages;
+                const uint32_t ph = (kb / p.stages) & 1;
+                if (!mbar_wait(&empty[s], ph ^ 1, p.err, 11)) break;
+                const int r0 = (int)(k_begin + (long)kb * kWgradBK);
+                uint8_t* sa = smem + s * stage_bytes;
+                mbar_arrive_expect_tx(&full[s], stage_bytes);
+                for (int j = 0; j < 4; j++)
+                    tma_load_2d(sa + j * kWgradBlockBytes, &tmX, &full[s], ch_coord[j], r0 + tap_shift[j]);
+                for (int j = 0; j < p.nblocks; j++)
+                    tma_load_2d(sa + a_bytes + j * kWgradBlockBytes, &tmG, &full[s], j * 32, r0);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_tf32(p.n, 1, 1);
+            for (int kb = 0; kb < kblocks; kb++) {
+                const int s = kb % p.stages;
+                const uint32_t ph = (kb / p.stages) & 1;
+                if (!mbar_wait(&full[s], ph, p.err, 12)) break;
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(smem + s * stage_bytes);
+                const uint32_t b_addr = a_addr + a_bytes;
+#pragma unroll
+                for (int k = 0; k < kWgradBK / 8; k++) {
+                    uint64_t ad = smem_desc_sw128(a_addr + k * 1024, kWgradBlockBytes, 1024);
+                    uint64_t bd = smem_desc_sw128(b_addr + k * 1024, kWgradBlockBytes, 1024);
+                    mma_tf32(tmem_base, ad, bd, idesc, (kb | k) != 0);
+                }
+                mma_commit(&empty[s]);
+            }
+            mma_commit(&tfull[0]);
+        }
+    } else {
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        float* dst = p.ws + ((long)split * p.m_tiles * kTileM + (long)m_tile * kTileM + row) * p.n;
+        if (kblocks == 0) {
+            for (int j = 0; j < p.n; j++) dst[j] = 0.0f;
+        } else if (mbar_wait(&tfull[0], 0, p.err, 13)) {
+            tc_fence_after();
+            for (int j = 0; j < p.n; j += 16) {
+                float v[16];
+                tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + j, v);
+                float4* d4 = reinterpret_cast<float4*>(dst + j);
+#pragma unroll
+                for (int i = 0; i < 4; i++) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, p.alloc_cols);
+    }
+}
+
+// dw[(o * ic + c) * taps + t] = sum_s ws[s][(t * kchunks + c / 32) * 32 + c % 32][o]
+__global__ void wgrad_reduce_kernel(const float* ws, int splits, long split_stride, int n, int ic, int taps,
+                                    int kchunks, float* dw) {
+    const long total = (long)n * ic * taps;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int t = (int)(i % taps);
+        const long rest = i / taps;
+        const int c = (int)(rest % ic);
+        const int o = (int)(rest / ic);
+        const long row = (long)(t * kchunks + c / 32) * 32 + (c % 32);
+        float s = 0.0f;
+        for (int k = 0; k < splits; k++) s += ws[k * split_stride + row * n + o];
+        dw[i] = s;
+    }
+}
+
+static int wgrad_splits(int m_tiles, long rows) {
+    const long kblocks = (rows + kWgradBK - 1) / kWgradBK;
+    int target = std::max(1, (2 * num_sms()) / std::max(1, m_tiles));
+    return (int)std::min<long>(target, std::max<long>(1, kblocks / 8));
+}
+
+size_t wgrad_workspace_floats(int ic, int oc, int taps, long rows) {
+    const int kchunks = (ic + 31) / 32;
+    const int m_tiles = (taps * kchunks + 3) / 4;
+    const int n = (oc + 15) / 16 * 16;
+    // upper bound on splits independent of the device
+    const long kblocks = (rows + kWgradBK - 1) / kWgradBK;
+    const long splits = std::min<long>(std::max(1, 2 * 160 / m_tiles), std::max<long>(1, kblocks / 8));
+    return (size_t)splits * m_tiles * kTileM * n;
+}
+
+void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, float* dw, float* ws, int* err,
+                   cudaStream_t stream) {
+    if (dy.channels > 256) throw std::runtime_error("conv_tc_wgrad: more than 256 output channels");
+    if (x.rows != dy.rows) throw std::runtime_error("conv_tc_wgrad: row mismatch");
+    WgradParams p;
+    p.taps = taps;
+    p.kchunks = (x.channels + 31) / 32;
+    p.total_chunks = taps * p.kchunks;
+    for (int t = 0; t < 9; t++) p.shift[t] = 0;
+    if (taps == 9)
+        for (int t = 0; t < 9; t++) p.shift[t] = (t / 3 - 1) * grid.wp + (t % 3 - 1);
+    p.n = (dy.channels + 15) / 16 * 16;
+    p.nblocks = (p.n + 31) / 32;
+    p.rows = x.rows;
+    p.m_tiles = (p.total_chunks + 3) / 4;
+    int splits = std::min(wgrad_splits(p.m_tiles, p.rows), (int)(wgrad_workspace_floats(x.channels, dy.channels, taps,
+                                                                                         x.rows) /
+                                                                  ((size_t)p.m_tiles * kTileM * p.n)));
+    splits = std::max(1, splits);
+    const long kblocks = (p.rows + kWgradBK - 1) / kWgradBK;
+    p.rows_per_split = ((kblocks + splits - 1) / splits) * kWgradBK;
+    p.oob_channel = p.kchunks * 32;
+    const int stage_bytes = (4 + p.nblocks) * kWgradBlockBytes;
+    p.stages = std::min(8, (int)((220 * 1024) / stage_bytes));
+    p.alloc_cols = pow2_at_least(p.n);
+    p.ws = ws;
+    p.err = err;
+    CUtensorMap tx = make_map_2d(x.base, x.channels, x.rows, x.pitch, 32, kWgradBK);
+    CUtensorMap tg = make_map_2d(dy.base, dy.channels, dy.rows, dy.pitch, 32, kWgradBK);
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(conv_wgrad_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        attr_set = true;
+    }
+    const size_t smem = 1024 + (size_t)p.stages * stage_bytes + (2 * p.stages + 2) * 8 + 16;
+    conv_wgrad_tc_kernel<<<dim3(p.m_tiles, splits), kFwdThreads, smem, stream>>>(tx, tg, p);
+    const long split_stride = (long)p.m_tiles * kTileM * p.n;
+    const long total = (long)dy.channels * x.channels * taps;
+    const int blocks = (int)std::min<long>(4096, (total + 255) / 256);
+    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, splits, split_stride, p.n, x.channels, taps, p.kchunks, dw);
+}
+
+}  // namespace sy

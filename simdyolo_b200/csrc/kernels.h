@@ -1,0 +1,129 @@
+// Host-side launch interface of the sm_100a kernels.  All pointers are device pointers; all
+// activations use the padded channels-last layout described in common.cuh (sy::Grid).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace sy {
+
+// ---------------------------------------------------------------- tensor views
+// A channels-last activation view: `base` points at channel 0 of the view in row 0,
+// `pitch` floats between consecutive rows, `channels` channels visible, `rows` total rows.
+struct View {
+    float* base;
+    int pitch;
+    int channels;
+    long rows;
+};
+
+// ---------------------------------------------------------------- convolution (tcgen05)
+// Implicit-GEMM convolution over the padded layout, stride 1, k in {1,3}:
+//   out[m, n] = epilogue( sum_t sum_c in[m + shift[t], c] * wk[n, t * kpad + c] )
+// wk is K-major [n_rows][taps * kpad] (kpad = round_up(in.channels, 32)).  Used for forward
+// convs (weights in [oc][tap][ic] order) and for data gradients (weights [ic][tap][oc] with
+// negated shifts).  Halo / dead rows of `out` are written as zero.
+struct ConvEpilogue {
+    const float* bias = nullptr;      // per output channel
+    int silu = 0;
+    const float* residual = nullptr;  // added after SiLU (Bottleneck shortcut)
+    int res_pitch = 0;
+    int mask_halo = 1;                // 0: every row is a valid output (plain GEMM use)
+};
+
+// shift_sign = +1 for a forward conv, -1 for the data gradient (taps read dy at m - shift[t]).
+void conv_tc_forward(const View& in, const float* wk, int n_rows, int n_out, int taps, int shift_sign,
+                     const Grid& grid, const View& out, const ConvEpilogue& ep, int* err, cudaStream_t stream);
+
+// Weight gradient: dw[o, c, t] = sum_m dy[m, o] * x[m + shift[t], c], written to `dw` in OIHW order
+// (dw[(o * ic + c) * taps + t]), fully overwritten.  `ws` is scratch of wgrad_workspace_floats() floats.
+size_t wgrad_workspace_floats(int ic, int oc, int taps, long rows);
+void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, float* dw, float* ws, int* err,
+                   cudaStream_t stream);
+
+// ---------------------------------------------------------------- convolution (SIMT)
+// Direct implicit-GEMM convolution for any stride (used for stride-2 backbone convs and for
+// the 3-channel stem).  Interior outputs only; weights OHWI [oc][k*k][ic].
+void conv_simt_forward(const View& in, const Grid& gin, const float* w_ohwi, int oc, int k, int stride,
+                       const View& out, const Grid& gout, int batch, const ConvEpilogue& ep, cudaStream_t stream);
+
+// ---------------------------------------------------------------- layout helpers
+void nchw_to_padded(const float* src, int batch, int c, const Grid& g, const View& dst, cudaStream_t stream);
+void padded_to_nchw(const View& src, int batch, int c, const Grid& g, float* dst, cudaStream_t stream);
+void rgb_to_padded(const uint8_t* rgb, int batch, int size, const Grid& g, const View& dst, cudaStream_t stream);
+// OIHW -> [oc][t][kpad] (forward) and OIHW -> [ic][t][kpad_o] (data gradient)
+void weights_fwd_layout(const float* oihw, int oc, int ic, int taps, int kpad, float* dst, cudaStream_t stream);
+void weights_dgrad_layout(const float* oihw, int oc, int ic, int taps, int kpad_o, float* dst, cudaStream_t stream);
+void weights_ohwi(const float* oihw, int oc, int ic, int taps, float* dst, cudaStream_t stream);
+
+// ---------------------------------------------------------------- backbone helpers
+void maxpool5_padded(const View& in, const View& out, int batch, const Grid& g, cudaStream_t stream);
+void upsample2_padded(const View& in, const Grid& gin, const View& out, const Grid& gout, int batch,
+                      cudaStream_t stream);
+
+// ---------------------------------------------------------------- BatchNorm (training, per image)
+// stats[(b * c + ch) * 2 + {0,1}] = (mean, biased variance) of image b over the interior pixels.
+void bn_stats(const View& y, int batch, const Grid& g, float* stats, cudaStream_t stream);
+// a = SiLU(gamma * (y - mean) * inv + beta) at interior rows, 0 elsewhere; xhat not stored.
+void bn_silu_apply(const View& y, const float* stats, const float* gamma, const float* beta, float eps, int batch,
+                   const Grid& g, const View& a, cudaStream_t stream);
+// Backward through SiLU and BN.  g: gradient w.r.t. a.  Writes dy (w.r.t. y) with zero halo and
+// per-image partials red[(b * c + ch) * 2 + {0,1}] = (sum dz, sum dz * xhat); dgamma/dbeta are
+// accumulated over images in image order.
+void bn_silu_backward(const View& y, const View& g, const float* stats, const float* gamma, const float* beta,
+                      float eps, int batch, const Grid& gr, float* red, const View& dy, float* dgamma, float* dbeta,
+                      cudaStream_t stream);
+// Running statistics: for each BN channel, r <- (1-m) r + m * s_i for images i in order, over
+// `ranks` blocks of `batch` images each `rank_stride` floats apart (all-gathered ranks).
+void bn_running_update(const float* stats, long rank_stride, int ranks, int batch, int c, int spatial, float momentum,
+                       float* rmean, float* rvar, float* tracked, cudaStream_t stream);
+// Bias gradient of the final conv: db[n] += sum over images and interior pixels of g[m, n].
+// `part` is scratch of batch * channels floats.
+void bias_grad(const View& g, int batch, const Grid& gr, float* part, float* db, cudaStream_t stream);
+
+// ---------------------------------------------------------------- loss / assigner
+struct LevelIO {
+    const float* box;   // [rows][pitch] raw DFL logits (4 * bins channels)
+    const float* cls;   // [rows][pitch] raw class logits
+    float* dbox;        // gradients (same layout), may be null when !backward
+    float* dcls;
+    int box_pitch, cls_pitch;
+    Grid grid;
+    float stride;
+};
+struct TruthBox {
+    int cls;
+    float x1, y1, x2, y2;
+};
+// Per image loss outputs: loss[b * 4 + {0,1,2}] = (box, cls, dfl), positives[b], connected[b].
+struct LossOut {
+    float* loss;
+    int* positives;
+    int* connected;
+    int* assigned;     // [batch][anchors] (may be null)
+    float* scores;     // [batch][anchors] (may be null)
+};
+size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int bins);
+void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int bins, const TruthBox* truth,
+                    const int* box_offsets, int max_boxes, int topk, float grad_scale, int backward, void* workspace,
+                    const LossOut& out, cudaStream_t stream);
+
+// ---------------------------------------------------------------- optimizer
+struct ParamSegment {
+    long offset, length;
+    int decay;     // conv weights
+    int group;     // 0: always connected, 1: box branch (skipped when no image connected it)
+};
+// SGD-momentum (TrainingParameter.Update) or AdamW over segments; flags[g] gates group g.
+// Reports non-finite values through *nonfinite.  Gradients are zeroed after the update.
+void optimizer_step(int optimizer, float* params, float* vel, float* vel2, float* grad, const ParamSegment* segs,
+                    int nsegs, const int* group_has_grad, const int* group_steps, float lr, float momentum, float wd,
+                    float beta1, float beta2, float adam_eps, float inv_images, int* nonfinite, cudaStream_t stream);
+void check_finite(const float* v, long n, int* flag, cudaStream_t stream);
+// part[kAbsSumBlocks] = block partial sums of |v| (fixed order, summed on the host)
+constexpr int kAbsSumBlocks = 64;
+void abs_sum_partials(const float* v, long n, double* part, cudaStream_t stream);
+
+}  // namespace sy

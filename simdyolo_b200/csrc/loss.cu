@@ -1,0 +1,618 @@
+// Detection loss on device: DFL decode, task-aligned assigner (TAL), BCE, CIoU and DFL with their
+// gradients (DetectionLoss.Compute, src/SimdYolo.Training/DetectionLoss.cs:19-149; CIoU and its
+// forward-mode derivatives BoxMath.Ciou / Differential, DetectionLoss.cs:154-183).
+//
+// Everything that decides the assignment (DFL softmax expectation, decoded boxes, inside test,
+// CIoU value, sigmoid, metric, top-k order) is evaluated with round-to-nearest intrinsics and the
+// deterministic exp / atan of common.cuh in the reference's expression order, so the assigned
+// anchor sets equal the CPU restatement bit for bit.  Loss values and gradients use ordinary
+// arithmetic (tolerance-checked).
+//
+// Kernels per step:  decode (image x anchor) -> topk (gt x image) -> assign (image) ->
+//                    bce (anchor rows) -> box (positives) -> finalize (image).
+#include <algorithm>
+
+#include "kernels.h"
+
+namespace sy {
+
+namespace {
+
+constexpr int kMaxLevels = 3;
+constexpr int kMaxTopk = 16;
+constexpr int kMaxSel = 1024;  // max boxes * topk handled by one image's assignment
+
+struct LossParams {
+    LevelIO lv[kMaxLevels];
+    int nlevels;
+    int level_start[kMaxLevels + 1];
+    int anchors;
+    int batch, nc, bins, topk;
+    float grad_scale;
+    int backward;
+    const TruthBox* truth;
+    const int* box_off;   // [batch + 1]
+    int max_boxes;
+    // workspace
+    float* dec;           // [batch][anchors][4] decoded xyxy (pixels)
+    float* expv;          // [batch][anchors][4] expected distances
+    int* sel;             // [batch][max_boxes][topk] anchor or -1
+    int* pos_anchor;      // [batch][kMaxSel]
+    int* pos_gt;
+    float* pos_score;
+    int* pos_count;       // [batch]
+    float* score_sum;     // [batch]
+    double* bce_part;     // [batch][bce_blocks]
+    int bce_blocks;
+    float* pos_box;       // [batch][kMaxSel] box loss term
+    float* pos_dfl;       // [batch][kMaxSel] dfl loss term
+    LossOut out;
+};
+
+// ---------------------------------------------------------------- exact float helpers
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
+
+// Differential (DetectionLoss.cs:154-164): value plus 4 partial derivatives.
+struct Dif {
+    float v, g[4];
+};
+__device__ __forceinline__ Dif dconst(float v) { return Dif{v, {0.f, 0.f, 0.f, 0.f}}; }
+__device__ __forceinline__ Dif dvar(float v, int i) {
+    Dif r{v, {0.f, 0.f, 0.f, 0.f}};
+    r.g[i] = 1.f;
+    return r;
+}
+__device__ __forceinline__ Dif dadd(const Dif& a, const Dif& b) {
+    Dif r;
+    r.v = fadd(a.v, b.v);
+#pragma unroll
+    for (int i = 0; i < 4; i++) r.g[i] = fadd(a.g[i], b.g[i]);
+    return r;
+}
+__device__ __forceinline__ Dif dsub(const Dif& a, const Dif& b) {
+    Dif r;
+    r.v = fsub(a.v, b.v);
+#pragma unroll
+    for (int i = 0; i < 4; i++) r.g[i] = fsub(a.g[i], b.g[i]);
+    return r;
+}
+__device__ __forceinline__ Dif dmul(const Dif& a, const Dif& b) {
+    Dif r;
+    r.v = fmul(a.v, b.v);
+#pragma unroll
+    for (int i = 0; i < 4; i++) r.g[i] = fadd(fmul(a.g[i], b.v), fmul(b.g[i], a.v));
+    return r;
+}
+__device__ __forceinline__ Dif ddiv(const Dif& a, const Dif& b) {
+    Dif r;
+    r.v = fdiv(a.v, b.v);
+    const float d = fmul(b.v, b.v);
+#pragma unroll
+    for (int i = 0; i < 4; i++) r.g[i] = fdiv(fsub(fmul(a.g[i], b.v), fmul(b.g[i], a.v)), d);
+    return r;
+}
+__device__ __forceinline__ Dif dmin(const Dif& a, const Dif& b) {
+    if (a.v < b.v) return a;
+    if (a.v > b.v) return b;
+    Dif r;
+    r.v = a.v;
+#pragma unroll
+    for (int i = 0; i < 4; i++) r.g[i] = fmul(fadd(a.g[i], b.g[i]), .5f);
+    return r;
+}
+__device__ __forceinline__ Dif dmax(const Dif& a, const Dif& b) {
+    if (a.v > b.v) return a;
+    if (a.v < b.v) return b;
+    Dif r;
+    r.v = a.v;
+#pragma unroll
+    for (int i = 0; i < 4; i++) r.g[i] = fmul(fadd(a.g[i], b.g[i]), .5f);
+    return r;
+}
+__device__ __forceinline__ Dif datan(const Dif& a) {
+    Dif r;
+    r.v = det_atanf(a.v);
+    const float d = fadd(1.f, fmul(a.v, a.v));
+#pragma unroll
+    for (int i = 0; i < 4; i++) r.g[i] = fdiv(a.g[i], d);
+    return r;
+}
+
+// BoxMath.Ciou (DetectionLoss.cs:171-183); alpha is a stopped gradient.
+__device__ float ciou(const float p[4], const float t[4], float* grad) {
+    const float eps = 1e-7f;
+    const Dif x1 = dvar(p[0], 0), y1 = dvar(p[1], 1), x2 = dvar(p[2], 2), y2 = dvar(p[3], 3);
+    const Dif w1 = dsub(x2, x1), h1 = dadd(dsub(y2, y1), dconst(eps));
+    const float w2 = fsub(t[2], t[0]), h2 = fadd(fsub(t[3], t[1]), eps);
+    const Dif iw = dmax(dsub(dmin(x2, dconst(t[2])), dmax(x1, dconst(t[0]))), dconst(0.f));
+    const Dif ih = dmax(dsub(dmin(y2, dconst(t[3])), dmax(y1, dconst(t[1]))), dconst(0.f));
+    const Dif inter = dmul(iw, ih);
+    const Dif uni = dadd(dsub(dadd(dmul(w1, h1), dconst(fmul(w2, h2))), inter), dconst(eps));
+    const Dif iou = ddiv(inter, uni);
+    const Dif cw = dsub(dmax(x2, dconst(t[2])), dmin(x1, dconst(t[0])));
+    const Dif ch = dsub(dmax(y2, dconst(t[3])), dmin(y1, dconst(t[1])));
+    const Dif dx = dsub(dsub(dconst(fadd(t[0], t[2])), x1), x2);
+    const Dif dy = dsub(dsub(dconst(fadd(t[1], t[3])), y1), y2);
+    const Dif rho = ddiv(dadd(dmul(dx, dx), dmul(dy, dy)), dconst(4.0f));
+    const float pi = 3.14159265358979323846f;
+    const float vscale = fdiv(4.0f, fmul(pi, pi));
+    Dif v = dsub(datan(dconst(fdiv(w2, h2))), datan(ddiv(w1, h1)));
+    v = dmul(dmul(v, v), dconst(vscale));
+    const float alpha = fdiv(v.v, fadd(fadd(fsub(v.v, iou.v), 1.f), eps));
+    const Dif c2 = dadd(dadd(dmul(cw, cw), dmul(ch, ch)), dconst(eps));
+    const Dif res = dsub(dsub(iou, ddiv(rho, c2)), dmul(v, dconst(alpha)));
+    if (grad)
+        for (int i = 0; i < 4; i++) grad[i] = res.g[i];
+    return res.v;
+}
+
+__device__ __forceinline__ void anchor_location(const LossParams& p, int a, int& level, int& row, float& cx, float& cy,
+                                                float& stride) {
+    level = 0;
+    while (level + 1 < p.nlevels && a >= p.level_start[level + 1]) level++;
+    const int pix = a - p.level_start[level];
+    const Grid& g = p.lv[level].grid;
+    const int y = pix / g.w, x = pix - y * g.w;
+    row = g.row(y, x);
+    stride = p.lv[level].stride;
+    cx = fmul(fadd((float)x, .5f), stride);
+    cy = fmul(fadd((float)y, .5f), stride);
+}
+
+// Inside test with small-box expansion (DetectionLoss.cs:57-60) and alignment metric (:62-63).
+__device__ __forceinline__ void tal_metric(const LossParams& p, int b, int a, const TruthBox& box, bool& inside,
+                                           float& overlap, float& metric) {
+    int level, row;
+    float cx, cy, st;
+    anchor_location(p, a, level, row, cx, cy, st);
+    const float s0 = p.lv[0].stride;
+    const float s1 = p.nlevels > 1 ? p.lv[1].stride : fmul(s0, 2.f);
+    const float bx = fmul(fadd(box.x1, box.x2), .5f), by = fmul(fadd(box.y1, box.y2), .5f);
+    const float bw = fsub(box.x2, box.x1), bh = fsub(box.y2, box.y1);
+    const float cw = bw < s0 ? s1 : bw, chh = bh < s0 ? s1 : bh;
+    inside = fsub(cx, fsub(bx, fmul(cw, .5f))) > 1e-9f && fsub(fadd(bx, fmul(cw, .5f)), cx) > 1e-9f &&
+             fsub(cy, fsub(by, fmul(chh, .5f))) > 1e-9f && fsub(fadd(by, fmul(chh, .5f)), cy) > 1e-9f;
+    overlap = 0.f;
+    metric = 0.f;
+    if (!inside) return;
+    const float* d = p.dec + ((long)b * p.anchors + a) * 4;
+    const float pb[4] = {d[0], d[1], d[2], d[3]};
+    const float tb[4] = {box.x1, box.y1, box.x2, box.y2};
+    const float c = ciou(pb, tb, nullptr);
+    overlap = fmaxf(0.f, c);
+    const LevelIO& L = p.lv[level];
+    const float s = det_sigmoid(L.cls[(long)b * L.grid.rows * L.cls_pitch + (long)row * L.cls_pitch + box.cls]);
+    metric = fmul(__fsqrt_rn(s), det_pow6(overlap));
+}
+
+// ---------------------------------------------------------------- 1. decode
+__global__ void decode_kernel(LossParams p) {
+    const long total = (long)p.batch * p.anchors;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int b = (int)(i / p.anchors), a = (int)(i - (long)b * p.anchors);
+        int level, row;
+        float cx, cy, st;
+        anchor_location(p, a, level, row, cx, cy, st);
+        const LevelIO& L = p.lv[level];
+        const float* t = L.box + ((long)b * L.grid.rows + row) * L.box_pitch;
+        float e[4];
+        for (int d = 0; d < 4; d++) {
+            if (p.bins == 1) {
+                e[d] = t[d];
+                continue;
+            }
+            float maximum = -INFINITY;
+            for (int k = 0; k < 16; k++) maximum = fmaxf(maximum, t[d * 16 + k]);
+            float ex[16];
+            float sum = 0.f;
+            for (int k = 0; k < 16; k++) {
+                ex[k] = det_expf(fsub(t[d * 16 + k], maximum));
+                sum = fadd(sum, ex[k]);
+            }
+            float dist = 0.f;
+            for (int k = 0; k < 16; k++) dist = fadd(dist, fmul(fdiv(ex[k], sum), (float)k));
+            e[d] = dist;
+        }
+        float* ev = p.expv + i * 4;
+        float* dv = p.dec + i * 4;
+        for (int d = 0; d < 4; d++) ev[d] = e[d];
+        dv[0] = fsub(cx, fmul(e[0], st));
+        dv[1] = fsub(cy, fmul(e[1], st));
+        dv[2] = fadd(cx, fmul(e[2], st));
+        dv[3] = fadd(cy, fmul(e[3], st));
+    }
+}
+
+// ---------------------------------------------------------------- 2. per-GT top-k
+// Key order = (metric desc, anchor asc) as the bounded PriorityQueue of (metric, -anchor)
+// (DetectionLoss.cs:65).  metric >= 0, so its bit pattern orders like the value.
+__device__ __forceinline__ unsigned long long make_key(float metric, int a) {
+    return ((unsigned long long)__float_as_uint(metric) << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)a);
+}
+
+__global__ void __launch_bounds__(256) topk_kernel(LossParams p) {
+    const int g = blockIdx.x, b = blockIdx.y;
+    const int n = p.box_off[b + 1] - p.box_off[b];
+    int* sel = p.sel + ((long)b * p.max_boxes + g) * p.topk;
+    if (g >= n) {
+        for (int k = threadIdx.x; k < p.topk; k += blockDim.x) sel[k] = -1;
+        return;
+    }
+    const TruthBox box = p.truth[p.box_off[b] + g];
+    unsigned long long list[kMaxTopk];
+    int cnt = 0;
+    for (int a = threadIdx.x; a < p.anchors; a += blockDim.x) {
+        bool inside;
+        float ov, m;
+        tal_metric(p, b, a, box, inside, ov, m);
+        const unsigned long long key = make_key(m, a);
+        if (cnt == p.topk && key <= list[cnt - 1]) continue;
+        int pos = cnt < p.topk ? cnt++ : cnt - 1;
+        while (pos > 0 && list[pos - 1] < key) {
+            list[pos] = list[pos - 1];
+            pos--;
+        }
+        list[pos] = key;
+    }
+    __shared__ unsigned long long wbest[8];
+    __shared__ unsigned long long best_s;
+    int head = 0;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int k = 0; k < p.topk; k++) {
+        unsigned long long cand = head < cnt ? list[head] : 0ull;
+        unsigned long long m = cand;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            unsigned long long other = __shfl_xor_sync(0xffffffffu, m, o);
+            m = other > m ? other : m;
+        }
+        if (lane == 0) wbest[warp] = m;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long bm = 0ull;
+            for (int w = 0; w < (int)(blockDim.x >> 5); w++) bm = wbest[w] > bm ? wbest[w] : bm;
+            best_s = bm;
+        }
+        __syncthreads();
+        const unsigned long long bm = best_s;
+        if (bm != 0ull && cand == bm) {
+            head++;
+            const int a = (int)(0xFFFFFFFFu - (unsigned)(bm & 0xFFFFFFFFull));
+            bool inside;
+            float ov, mm;
+            tal_metric(p, b, a, box, inside, ov, mm);
+            sel[k] = inside ? a : -1;
+        } else if (bm == 0ull && threadIdx.x == 0) {
+            sel[k] = -1;
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------- 3. per-image assignment
+// Conflicts (DetectionLoss.cs:69-81), max alignment / overlap per GT (:92-94), scores and their
+// sum in anchor order (:95-98).
+__global__ void __launch_bounds__(256) assign_kernel(LossParams p) {
+    const int b = blockIdx.x;
+    const int n = p.box_off[b + 1] - p.box_off[b];
+    const TruthBox* truth = p.truth + p.box_off[b];
+    __shared__ int anc[kMaxSel];
+    __shared__ int own[kMaxSel];
+    __shared__ float al[kMaxSel], ov[kMaxSel];
+    __shared__ float max_al[128], max_ov[128];
+    __shared__ int count_s;
+    // dense outputs of this image start cleared
+    if (p.out.assigned)
+        for (int a = threadIdx.x; a < p.anchors; a += blockDim.x) p.out.assigned[(long)b * p.anchors + a] = -1;
+    if (p.out.scores)
+        for (int a = threadIdx.x; a < p.anchors; a += blockDim.x) p.out.scores[(long)b * p.anchors + a] = 0.f;
+    // gather the selected (gt, anchor) pairs, in gt order then rank order
+    if (threadIdx.x == 0) {
+        int c = 0;
+        for (int g = 0; g < n; g++)
+            for (int k = 0; k < p.topk; k++) {
+                int a = p.sel[((long)b * p.max_boxes + g) * p.topk + k];
+                if (a < 0) continue;
+                bool dup = false;
+                for (int j = 0; j < c; j++)
+                    if (anc[j] == a) {
+                        dup = true;
+                        own[j] = -2;  // selected by more than one GT
+                        break;
+                    }
+                if (!dup && c < kMaxSel) {
+                    anc[c] = a;
+                    own[c] = g;
+                    c++;
+                }
+            }
+        // sort by anchor index (insertion sort; c <= boxes * topk)
+        for (int i = 1; i < c; i++) {
+            int a = anc[i], o = own[i], j = i - 1;
+            while (j >= 0 && anc[j] > a) {
+                anc[j + 1] = anc[j];
+                own[j + 1] = own[j];
+                j--;
+            }
+            anc[j + 1] = a;
+            own[j + 1] = o;
+        }
+        count_s = c;
+    }
+    for (int g = threadIdx.x; g < 128; g += blockDim.x) {
+        max_al[g] = 0.f;
+        max_ov[g] = 0.f;
+    }
+    __syncthreads();
+    const int c = count_s;
+    // conflicts: argmax overlap over ALL gts, strict >, best starts at -1 (first max wins)
+    for (int i = threadIdx.x; i < c; i += blockDim.x) {
+        const int a = anc[i];
+        int chosen = own[i];
+        if (chosen == -2) {
+            float best = -1.f;
+            for (int g = 0; g < n; g++) {
+                bool inside;
+                float o, m;
+                tal_metric(p, b, a, truth[g], inside, o, m);
+                if (o > best) {
+                    best = o;
+                    chosen = g;
+                }
+            }
+            own[i] = chosen;
+        }
+        bool inside;
+        float o, m;
+        tal_metric(p, b, a, truth[chosen], inside, o, m);
+        al[i] = m;
+        ov[i] = o;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < c; i++) {
+            const int g = own[i];
+            max_al[g] = fmaxf(max_al[g], al[i]);
+            max_ov[g] = fmaxf(max_ov[g], ov[i]);
+        }
+        float sum = 0.f;
+        for (int i = 0; i < c; i++) {
+            const int g = own[i];
+            const float s = fdiv(fmul(al[i], max_ov[g]), fadd(max_al[g], 1e-9f));
+            sum = fadd(sum, s);
+            p.pos_anchor[(long)b * kMaxSel + i] = anc[i];
+            p.pos_gt[(long)b * kMaxSel + i] = g;
+            p.pos_score[(long)b * kMaxSel + i] = s;
+            if (p.out.assigned) p.out.assigned[(long)b * p.anchors + anc[i]] = g;
+            if (p.out.scores) p.out.scores[(long)b * p.anchors + anc[i]] = s;
+        }
+        p.pos_count[b] = c;
+        p.score_sum[b] = fmaxf(1.f, sum);
+    }
+}
+
+// ---------------------------------------------------------------- 4. BCE over all anchors x classes
+// (DetectionLoss.cs:104-111).  One warp per anchor row, lanes over classes.
+__global__ void __launch_bounds__(256) bce_kernel(LossParams p, const int* dense_assigned, const float* dense_scores) {
+    const int b = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float inv = .5f / p.score_sum[b];
+    double acc = 0.0;
+    for (int a = blockIdx.x * 8 + warp; a < p.anchors; a += gridDim.x * 8) {
+        int level, row;
+        float cx, cy, st;
+        anchor_location(p, a, level, row, cx, cy, st);
+        const LevelIO& L = p.lv[level];
+        const long off = ((long)b * L.grid.rows + row) * L.cls_pitch;
+        const int g = dense_assigned[(long)b * p.anchors + a];
+        const int tcls = g >= 0 ? p.truth[p.box_off[b] + g].cls : -1;
+        const float w = g >= 0 ? dense_scores[(long)b * p.anchors + a] : 0.f;
+        float part = 0.f;
+        for (int c = lane; c < p.nc; c += 32) {
+            const float x = L.cls[off + c];
+            const float t = c == tcls ? w : 0.f;
+            part += (fmaxf(x, 0.f) - x * t + logf(1.f + expf(-fabsf(x)))) * inv;
+            if (p.backward) {
+                const float s = x >= 0.f ? 1.f / (1.f + expf(-x)) : expf(x) / (1.f + expf(x));
+                L.dcls[off + c] = (s - t) * inv * p.grad_scale;
+            }
+        }
+        acc += (double)part;
+    }
+    acc = warp_sum_d(acc);
+    __shared__ double red[8];
+    if (lane == 0) red[warp] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < 8; w++) t += red[w];
+        p.bce_part[(long)b * p.bce_blocks + blockIdx.x] = t;
+    }
+}
+
+// ---------------------------------------------------------------- 5. CIoU + DFL for positives
+// (DetectionLoss.cs:112-146).  One warp per positive; lane l handles bins of side l / 16 ... via loop.
+__global__ void __launch_bounds__(256) box_kernel(LossParams p) {
+    const int b = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int i = blockIdx.x * 8 + warp;
+    if (i >= p.pos_count[b]) return;
+    const int a = p.pos_anchor[(long)b * kMaxSel + i];
+    const int g = p.pos_gt[(long)b * kMaxSel + i];
+    const float weight = p.pos_score[(long)b * kMaxSel + i];
+    const float ss = p.score_sum[b];
+    const TruthBox tb = p.truth[p.box_off[b] + g];
+    int level, row;
+    float cx, cy, st;
+    anchor_location(p, a, level, row, cx, cy, st);
+    const LevelIO& L = p.lv[level];
+    const float* dec = p.dec + ((long)b * p.anchors + a) * 4;
+    const float* ex = p.expv + ((long)b * p.anchors + a) * 4;
+    const float invs = 1.f / st;
+    const float pg[4] = {dec[0] * invs, dec[1] * invs, dec[2] * invs, dec[3] * invs};
+    const float tg[4] = {tb.x1 * invs, tb.y1 * invs, tb.x2 * invs, tb.y2 * invs};
+    float cg[4];
+    const float ci = ciou(pg, tg, cg);
+    const float box_scale = 7.5f * weight / ss;
+    float coord[4];
+    for (int d = 0; d < 4; d++) coord[d] = -cg[d] * (box_scale * p.grad_scale);
+    const float dist_grad[4] = {-coord[0], -coord[1], coord[2], coord[3]};
+    const float dists[4] = {(cx - tb.x1) / st, (cy - tb.y1) / st, (tb.x2 - cx) / st, (tb.y2 - cy) / st};
+    const long off = ((long)b * L.grid.rows + row) * L.box_pitch;
+    const float* t = L.box + off;
+    float dfl = 0.f;
+    if (p.bins == 1) {
+        for (int d = 0; d < 4; d++) {
+            const float extent = (float)(d % 2 == 0 ? p.lv[0].grid.w : p.lv[0].grid.h) * p.lv[0].stride;
+            const float norm = st / extent, delta = ex[d] - dists[d];
+            const float l1 = 1.5f * weight / (4 * ss);
+            dfl += fabsf(delta) * norm * l1;
+            if (p.backward && lane == 0) {
+                const float sign = delta > 0 ? 1.f : delta < 0 ? -1.f : 0.f;
+                L.dbox[off + d] = dist_grad[d] + sign * norm * l1 * p.grad_scale;
+            }
+        }
+    } else {
+        const float scale = 1.5f * weight / (4 * ss);
+        for (int d = 0; d < 4; d++) {
+            const float hi = 16 - 1 - .01f;
+            float target = dists[d];
+            target = target < 0 ? 0 : target > hi ? hi : target;
+            const int left = (int)target;
+            const float rw = target - left;
+            // lanes 0..15 hold the bins of this side
+            const float v = lane < 16 ? t[d * 16 + lane] : -INFINITY;
+            float mx = v;
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            mx = __shfl_sync(0xffffffffu, mx, 0);
+            const float e = lane < 16 ? expf(v - mx) : 0.f;
+            const float es = __shfl_sync(0xffffffffu, warp_sum(e), 0);
+            const float log_sum = mx + logf(es);
+            const float vl = t[d * 16 + left], vr = t[d * 16 + left + 1];
+            dfl += scale * (log_sum - (1 - rw) * vl - rw * vr);
+            if (p.backward && lane < 16) {
+                // probabilities of the decode (det_expf softmax), as the reference reuses them
+                float mxd = -INFINITY;
+                for (int k = 0; k < 16; k++) mxd = fmaxf(mxd, t[d * 16 + k]);
+                float sum = 0.f, mine = 0.f;
+                for (int k = 0; k < 16; k++) {
+                    const float ek = det_expf(fsub(t[d * 16 + k], mxd));
+                    sum = fadd(sum, ek);
+                    if (k == lane) mine = ek;
+                }
+                const float pr = fdiv(mine, sum);
+                const float tp = lane == left ? 1 - rw : lane == left + 1 ? rw : 0.f;
+                L.dbox[off + d * 16 + lane] = pr * (lane - ex[d]) * dist_grad[d] + scale * (pr - tp) * p.grad_scale;
+            }
+        }
+    }
+    if (lane == 0) {
+        p.pos_box[(long)b * kMaxSel + i] = (1 - ci) * box_scale;
+        p.pos_dfl[(long)b * kMaxSel + i] = dfl;
+    }
+}
+
+// ---------------------------------------------------------------- 6. per-image totals
+__global__ void finalize_kernel(LossParams p) {
+    const int b = blockIdx.x;
+    if (threadIdx.x != 0) return;
+    double cls = 0.0;
+    for (int k = 0; k < p.bce_blocks; k++) cls += p.bce_part[(long)b * p.bce_blocks + k];
+    float box = 0.f, dfl = 0.f;
+    const int c = p.pos_count[b];
+    for (int i = 0; i < c; i++) {
+        box += p.pos_box[(long)b * kMaxSel + i];
+        dfl += p.pos_dfl[(long)b * kMaxSel + i];
+    }
+    p.out.loss[b * 4 + 0] = box;
+    p.out.loss[b * 4 + 1] = (float)cls;
+    p.out.loss[b * 4 + 2] = dfl;
+    p.out.loss[b * 4 + 3] = 0.f;
+    p.out.positives[b] = c;
+    p.out.connected[b] = (p.backward && c > 0) ? 1 : 0;
+}
+
+constexpr int kBceBlocks = 64;
+
+size_t align_up(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace
+
+size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int topk) {
+    size_t s = 0;
+    s += align_up((size_t)batch * anchors * 4 * sizeof(float)) * 2;  // dec, expv
+    s += align_up((size_t)batch * max_boxes * topk * sizeof(int));   // sel
+    s += align_up((size_t)batch * kMaxSel * sizeof(int)) * 2;        // pos anchor / gt
+    s += align_up((size_t)batch * kMaxSel * sizeof(float)) * 3;      // score, box, dfl terms
+    s += align_up((size_t)batch * sizeof(int));                      // pos count
+    s += align_up((size_t)batch * sizeof(float));                    // score sum
+    s += align_up((size_t)batch * kBceBlocks * sizeof(double));      // bce partials
+    s += align_up((size_t)batch * anchors * sizeof(int));            // dense assigned (if not given)
+    s += align_up((size_t)batch * anchors * sizeof(float));          // dense scores (if not given)
+    return s;
+}
+
+void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int bins, const TruthBox* truth,
+                    const int* box_offsets, int max_boxes, int topk, float grad_scale, int backward, void* workspace,
+                    const LossOut& out, cudaStream_t stream) {
+    LossParams p;
+    p.nlevels = nlevels;
+    p.level_start[0] = 0;
+    for (int l = 0; l < nlevels; l++) {
+        p.lv[l] = levels[l];
+        p.level_start[l + 1] = p.level_start[l] + levels[l].grid.h * levels[l].grid.w;
+    }
+    p.anchors = p.level_start[nlevels];
+    p.batch = batch;
+    p.nc = nc;
+    p.bins = bins;
+    p.topk = topk;
+    p.grad_scale = grad_scale;
+    p.backward = backward;
+    p.truth = truth;
+    p.box_off = box_offsets;
+    p.max_boxes = max_boxes;
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    auto take = [&](size_t bytes) {
+        uint8_t* r = w;
+        w += align_up(bytes);
+        return r;
+    };
+    p.dec = (float*)take((size_t)batch * p.anchors * 4 * sizeof(float));
+    p.expv = (float*)take((size_t)batch * p.anchors * 4 * sizeof(float));
+    p.sel = (int*)take((size_t)batch * max_boxes * topk * sizeof(int));
+    p.pos_anchor = (int*)take((size_t)batch * kMaxSel * sizeof(int));
+    p.pos_gt = (int*)take((size_t)batch * kMaxSel * sizeof(int));
+    p.pos_score = (float*)take((size_t)batch * kMaxSel * sizeof(float));
+    p.pos_box = (float*)take((size_t)batch * kMaxSel * sizeof(float));
+    p.pos_dfl = (float*)take((size_t)batch * kMaxSel * sizeof(float));
+    p.pos_count = (int*)take((size_t)batch * sizeof(int));
+    p.score_sum = (float*)take((size_t)batch * sizeof(float));
+    p.bce_part = (double*)take((size_t)batch * kBceBlocks * sizeof(double));
+    p.bce_blocks = kBceBlocks;
+    int* dense_a = (int*)take((size_t)batch * p.anchors * sizeof(int));
+    float* dense_s = (float*)take((size_t)batch * p.anchors * sizeof(float));
+    p.out = out;
+    if (!p.out.assigned) p.out.assigned = dense_a;
+    if (!p.out.scores) p.out.scores = dense_s;
+
+    const long total = (long)batch * p.anchors;
+    decode_kernel<<<(int)std::min<long>(148L * 32, (total + 255) / 256), 256, 0, stream>>>(p);
+    if (max_boxes > 0) topk_kernel<<<dim3(max_boxes, batch), 256, 0, stream>>>(p);
+    assign_kernel<<<batch, 256, 0, stream>>>(p);
+    if (backward)
+        for (int l = 0; l < nlevels; l++) {
+            const LevelIO& L = levels[l];
+            // box gradients are sparse: clear the whole level, positives are scattered below
+            cudaMemsetAsync(L.dbox, 0, (size_t)batch * L.grid.rows * L.box_pitch * sizeof(float), stream);
+        }
+    bce_kernel<<<dim3(kBceBlocks, batch), 256, 0, stream>>>(p, p.out.assigned, p.out.scores);
+    box_kernel<<<dim3((max_boxes * topk + 7) / 8 > 0 ? (max_boxes * topk + 7) / 8 : 1, batch), 256, 0, stream>>>(p);
+    finalize_kernel<<<batch, 32, 0, stream>>>(p);
+}
+
+}  // namespace sy

@@ -1,0 +1,758 @@
+// Session: model plan, device buffers and the fine-tuning step.
+//
+// Step order (one CUDA stream):
+//   upload images + boxes -> frozen YOLOv8 trunk (PtModel.Run up to Detect, PtModel.cs:184-203)
+//   -> head forward per level, box branch then class branch (DetectionHead.Forward, :89-98)
+//   -> DetectionLoss on device -> head backward (reverse block order, GradientTape.Backward)
+//   -> finiteness (YoloTrainer.cs:193,196) -> [NCCL all-reduce over ranks]
+//   -> BN running statistics in image order -> SGD / AdamW (TrainingParameter.Update)
+//   -> refresh the derived weight layouts used by the next step's convs.
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "session.h"
+
+namespace sy {
+
+
+#define SY_CUDA(call)                                                                                    \
+    do {                                                                                                 \
+        cudaError_t e_ = (call);                                                                         \
+        if (e_ != cudaSuccess)                                                                           \
+            throw SyError(e_ == cudaErrorMemoryAllocation ? SY_ERR_OUT_OF_MEMORY : SY_ERR_DEVICE,        \
+                          std::string(#call) + ": " + cudaGetErrorString(e_));                           \
+    } while (0)
+
+// ------------------------------------------------------------------ NCCL (loaded at run time)
+typedef struct { char internal[128]; } nccl_unique_id_t;
+struct NcclApi {
+    void* lib = nullptr;
+    int (*GetUniqueId)(nccl_unique_id_t*) = nullptr;
+    int (*CommInitRank)(void**, int, nccl_unique_id_t, int) = nullptr;
+    int (*AllReduce)(const void*, void*, size_t, int, int, void*, cudaStream_t) = nullptr;
+    int (*AllGather)(const void*, void*, size_t, int, void*, cudaStream_t) = nullptr;
+    int (*CommDestroy)(void*) = nullptr;
+    int (*CommAbort)(void*) = nullptr;
+    const char* (*GetErrorString)(int) = nullptr;
+    bool load() {
+        if (lib) return true;
+        lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!lib) lib = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!lib) return false;
+        GetUniqueId = (decltype(GetUniqueId))dlsym(lib, "ncclGetUniqueId");
+        CommInitRank = (decltype(CommInitRank))dlsym(lib, "ncclCommInitRank");
+        AllReduce = (decltype(AllReduce))dlsym(lib, "ncclAllReduce");
+        AllGather = (decltype(AllGather))dlsym(lib, "ncclAllGather");
+        CommDestroy = (decltype(CommDestroy))dlsym(lib, "ncclCommDestroy");
+        CommAbort = (decltype(CommAbort))dlsym(lib, "ncclCommAbort");
+        GetErrorString = (decltype(GetErrorString))dlsym(lib, "ncclGetErrorString");
+        return GetUniqueId && CommInitRank && AllReduce && AllGather && CommDestroy && GetErrorString;
+    }
+};
+static NcclApi g_nccl;
+constexpr int kNcclFloat = 7, kNcclDouble = 8, kNcclSum = 0;
+
+int nccl_unique_id(uint8_t out[128]) {
+    if (!g_nccl.load()) return SY_ERR_COMM;
+    nccl_unique_id_t id;
+    if (g_nccl.GetUniqueId(&id) != 0) return SY_ERR_COMM;
+    std::memcpy(out, id.internal, 128);
+    return SY_OK;
+}
+
+// ------------------------------------------------------------------ helpers
+static View slice(const View& v, int c0, int n) { return View{v.base + c0, v.pitch, n, v.rows}; }
+static int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+void* Session::dalloc(size_t bytes) {
+    void* p = nullptr;
+    SY_CUDA(cudaMalloc(&p, std::max<size_t>(bytes, 256)));
+    SY_CUDA(cudaMemsetAsync(p, 0, std::max<size_t>(bytes, 256), stream_));
+    allocations_.push_back(p);
+    return p;
+}
+
+View Session::alloc_view(int channels, const Grid& g) {
+    const int pitch = round_up(channels, 4);
+    const long rows = (long)B_ * g.rows;
+    float* p = static_cast<float*>(dalloc((size_t)rows * pitch * sizeof(float)));
+    return View{p, pitch, channels, rows};
+}
+
+// ------------------------------------------------------------------ construction
+Session::Session(const sy_config& c) : cfg(c) {
+    if (c.struct_size != (int)sizeof(sy_config)) throw SyError(SY_ERR_INVALID_ARGUMENT, "sy_config size mismatch");
+    if (c.image_size < 64 || c.image_size > 1280 || c.image_size % 32 != 0)
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "image_size must be a multiple of 32 in [64, 1280]");
+    if (c.max_batch < 1 || c.max_batch > 1024) throw SyError(SY_ERR_INVALID_ARGUMENT, "max_batch out of range");
+    if (c.max_boxes < 0 || c.max_boxes > 100) throw SyError(SY_ERR_INVALID_ARGUMENT, "max_boxes out of range");
+    if (c.num_classes < 1 || c.num_classes > 256) throw SyError(SY_ERR_INVALID_ARGUMENT, "num_classes out of range");
+    if (c.reg_max != 16) throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "only reg_max = 16 (DFL) is supported");
+    if (c.world_size < 1 || c.rank < 0 || c.rank >= c.world_size)
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "bad rank / world_size");
+    if (!(c.lr > 0) || !(c.momentum >= 0 && c.momentum < 1) || !(c.weight_decay >= 0))
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "bad optimizer hyper-parameters");
+    device_ = c.device;
+    SY_CUDA(cudaSetDevice(device_));
+    SY_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    SY_CUDA(cudaEventCreate(&ev0_));
+    SY_CUDA(cudaEventCreate(&ev1_));
+    B_ = c.max_batch;
+    for (int l = 0; l < 3; l++) levels_[l] = make_grid(c.image_size >> (3 + l), c.image_size >> (3 + l));
+    if (c.backbone == SY_BACKBONE_YOLOV8) {
+        build_backbone();
+    } else if (c.backbone == SY_BACKBONE_NONE) {
+        for (int l = 0; l < 3; l++) {
+            if (c.feature_channels[l] < 1) throw SyError(SY_ERR_INVALID_ARGUMENT, "feature_channels required");
+            feat_ch_[l] = c.feature_channels[l];
+            features_[l] = alloc_view(feat_ch_[l], levels_[l]);
+        }
+        size_t most = 0;
+        for (int l = 0; l < 3; l++) most = std::max(most, (size_t)B_ * feat_ch_[l] * levels_[l].h * levels_[l].w);
+        feat_stage_ = static_cast<float*>(dalloc(most * sizeof(float)));
+    } else {
+        throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "unknown backbone");
+    }
+    build_head();
+    // loss, truth, outputs
+    const int anchors = levels_[0].h * levels_[0].w + levels_[1].h * levels_[1].w + levels_[2].h * levels_[2].w;
+    loss_ws_ = dalloc(loss_workspace_bytes(B_, anchors, std::max(1, c.max_boxes), 10));
+    d_truth_ = static_cast<TruthBox*>(dalloc(sizeof(TruthBox) * (size_t)B_ * std::max(1, c.max_boxes)));
+    d_box_off_ = static_cast<int*>(dalloc(sizeof(int) * (B_ + 1)));
+    d_loss_ = static_cast<float*>(dalloc(sizeof(float) * 4 * B_));
+    d_pos_ = static_cast<int*>(dalloc(sizeof(int) * B_));
+    d_conn_ = static_cast<int*>(dalloc(sizeof(int) * B_));
+    d_flags_ = static_cast<int*>(dalloc(sizeof(int) * 16));
+    d_abs_ = static_cast<double*>(dalloc(sizeof(double) * kAbsSumBlocks));
+    SY_CUDA(cudaMallocHost(&h_truth_, sizeof(TruthBox) * (size_t)B_ * std::max(1, c.max_boxes)));
+    SY_CUDA(cudaMallocHost(&h_box_off_, sizeof(int) * (B_ + 1)));
+    SY_CUDA(cudaMallocHost(&h_flags_, sizeof(int) * 16));
+    SY_CUDA(cudaMallocHost(&h_loss_, sizeof(float) * 4 * B_));
+    SY_CUDA(cudaMallocHost(&h_pos_, sizeof(int) * B_));
+    SY_CUDA(cudaMallocHost(&h_conn_, sizeof(int) * B_));
+    SY_CUDA(cudaMallocHost(&h_abs_, sizeof(double) * kAbsSumBlocks));
+    if (c.backbone == SY_BACKBONE_YOLOV8) {
+        SY_CUDA(cudaMallocHost(&h_rgb_, (size_t)B_ * c.image_size * c.image_size * 3));
+        d_rgb_ = static_cast<uint8_t*>(dalloc((size_t)B_ * c.image_size * c.image_size * 3));
+    }
+    if (c.world_size > 1) {
+        if (!g_nccl.load()) throw SyError(SY_ERR_COMM, "libnccl.so.2 not found");
+        nccl_ = &g_nccl;
+        nccl_unique_id_t id;
+        std::memcpy(id.internal, c.nccl_id, 128);
+        int r = g_nccl.CommInitRank(&comm_, c.world_size, id, c.rank);
+        if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclCommInitRank: ") + g_nccl.GetErrorString(r));
+    }
+    SY_CUDA(cudaStreamSynchronize(stream_));
+}
+
+Session::~Session() {
+    if (stream_) cudaStreamSynchronize(stream_);
+    if (comm_ && nccl_) nccl_->CommDestroy(comm_);
+    for (void* p : allocations_) cudaFree(p);
+    for (void* p : {(void*)h_truth_, (void*)h_box_off_, (void*)h_flags_, (void*)h_loss_, (void*)h_pos_,
+                    (void*)h_conn_, (void*)h_abs_, (void*)h_rgb_})
+        if (p) cudaFreeHost(p);
+    if (ev0_) cudaEventDestroy(ev0_);
+    if (ev1_) cudaEventDestroy(ev1_);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+// ------------------------------------------------------------------ frozen trunk plan
+// YOLOv8 detection trunk: layer list, channel rule make_divisible(min(c, max) * width, 8) and
+// depth rule max(round(n * depth), 1); BatchNorm already folded into conv weight + bias.
+void Session::build_backbone() {
+    const int S = cfg.image_size;
+    auto chan = [&](int c) {
+        float x = (float)std::min(c, cfg.max_channels) * cfg.width_mult;
+        return (int)std::ceil(x / 8.0f) * 8;
+    };
+    auto depth = [&](int n) { return std::max((int)std::lround(n * cfg.depth_mult), 1); };
+    const int c64 = chan(64), c128 = chan(128), c256 = chan(256), c512 = chan(512), c1024 = chan(1024);
+    const int n3 = depth(3), n6 = depth(6);
+    const Grid gS = make_grid(S, S), g2 = make_grid(S / 2, S / 2), g4 = make_grid(S / 4, S / 4);
+    const Grid g8 = levels_[0], g16 = levels_[1], g32 = levels_[2];
+    long poff = 0;
+    auto conv = [&](const View& in, const Grid& gin, int oc, int k, int s, const View& out, const Grid& gout,
+                    const View* res) {
+        BackboneOp op;
+        op.type = 0;
+        op.ic = in.channels;
+        op.oc = oc;
+        op.k = k;
+        op.stride = s;
+        op.w_off = poff;
+        poff += (long)oc * op.ic * k * k;
+        op.b_off = poff;
+        poff += oc;
+        op.in = in;
+        op.out = out;
+        op.gin = gin;
+        op.gout = gout;
+        if (res) {
+            op.res = *res;
+            op.has_res = true;
+        }
+        bops_.push_back(op);
+    };
+    auto c2f = [&](const View& in, const Grid& g, int c2, int n, bool shortcut, const View& out) {
+        const int c = c2 / 2;
+        View cat = alloc_view((2 + n) * c, g);
+        View tmp = alloc_view(c, g);
+        conv(in, g, 2 * c, 1, 1, slice(cat, 0, 2 * c), g, nullptr);
+        for (int i = 0; i < n; i++) {
+            View src = slice(cat, (1 + i) * c, c), dst = slice(cat, (2 + i) * c, c);
+            conv(src, g, c, 3, 1, tmp, g, nullptr);
+            conv(tmp, g, c, 3, 1, dst, g, shortcut ? &src : nullptr);
+        }
+        conv(cat, g, c2, 1, 1, out, g, nullptr);
+    };
+    auto sppf = [&](const View& in, const Grid& g, int c2, const View& out) {
+        const int c = in.channels / 2;
+        View cat = alloc_view(4 * c, g);
+        conv(in, g, c, 1, 1, slice(cat, 0, c), g, nullptr);
+        for (int i = 0; i < 3; i++) {
+            BackboneOp op;
+            op.type = 1;
+            op.in = slice(cat, i * c, c);
+            op.out = slice(cat, (i + 1) * c, c);
+            op.gin = op.gout = g;
+            bops_.push_back(op);
+        }
+        conv(cat, g, c2, 1, 1, out, g, nullptr);
+    };
+    auto upsample = [&](const View& in, const Grid& gin, const View& out, const Grid& gout) {
+        BackboneOp op;
+        op.type = 2;
+        op.in = in;
+        op.out = out;
+        op.gin = gin;
+        op.gout = gout;
+        bops_.push_back(op);
+    };
+    img_grid_ = gS;
+    View img4 = alloc_view(4, gS);
+    img_ = View{img4.base, 4, 3, img4.rows};
+    View b0 = alloc_view(c64, g2);
+    conv(img_, gS, c64, 3, 2, b0, g2, nullptr);
+    View b1 = alloc_view(c128, g4);
+    conv(b0, g2, c128, 3, 2, b1, g4, nullptr);
+    View b2 = alloc_view(c128, g4);
+    c2f(b1, g4, c128, n3, true, b2);
+    View b3 = alloc_view(c256, g8);
+    conv(b2, g4, c256, 3, 2, b3, g8, nullptr);
+    View cat14 = alloc_view(c512 + c256, g8);
+    View l4 = slice(cat14, c512, c256);
+    c2f(b3, g8, c256, n6, true, l4);
+    View b5 = alloc_view(c512, g16);
+    conv(l4, g8, c512, 3, 2, b5, g16, nullptr);
+    View cat11 = alloc_view(c1024 + c512, g16);
+    View l6 = slice(cat11, c1024, c512);
+    c2f(b5, g16, c512, n6, true, l6);
+    View b7 = alloc_view(c1024, g32);
+    conv(l6, g16, c1024, 3, 2, b7, g32, nullptr);
+    View b8 = alloc_view(c1024, g32);
+    c2f(b7, g32, c1024, n3, true, b8);
+    View cat20 = alloc_view(c512 + c1024, g32);
+    View l9 = slice(cat20, c512, c1024);
+    sppf(b8, g32, c1024, l9);
+    upsample(l9, g32, slice(cat11, 0, c1024), g16);
+    View cat17 = alloc_view(c256 + c512, g16);
+    View l12 = slice(cat17, c256, c512);
+    c2f(cat11, g16, c512, n3, false, l12);
+    upsample(l12, g16, slice(cat14, 0, c512), g8);
+    View p3 = alloc_view(c256, g8);
+    c2f(cat14, g8, c256, n3, false, p3);
+    conv(p3, g8, c256, 3, 2, slice(cat17, 0, c256), g16, nullptr);
+    View p4 = alloc_view(c512, g16);
+    c2f(cat17, g16, c512, n3, false, p4);
+    conv(p4, g16, c512, 3, 2, slice(cat20, 0, c512), g32, nullptr);
+    View p5 = alloc_view(c1024, g32);
+    c2f(cat20, g32, c1024, n3, false, p5);
+    features_[0] = p3;
+    features_[1] = p4;
+    features_[2] = p5;
+    feat_ch_[0] = c256;
+    feat_ch_[1] = c512;
+    feat_ch_[2] = c1024;
+    n_backbone = poff;
+    backbone_params_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)poff));
+    for (auto& op : bops_) {
+        if (op.type != 0) continue;
+        const int taps = op.k * op.k;
+        if (op.stride == 1)
+            op.wk = static_cast<float*>(dalloc(sizeof(float) * (size_t)op.oc * taps * round_up(op.ic, 32)));
+        else
+            op.wk = static_cast<float*>(dalloc(sizeof(float) * (size_t)op.oc * taps * op.ic));
+    }
+}
+
+int Session::set_backbone(const float* host, long count) {
+    if (cfg.backbone != SY_BACKBONE_YOLOV8 || count != n_backbone)
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "backbone parameter count mismatch");
+    SY_CUDA(cudaMemcpyAsync(backbone_params_, host, sizeof(float) * count, cudaMemcpyHostToDevice, stream_));
+    for (auto& op : bops_) {
+        if (op.type != 0) continue;
+        const int taps = op.k * op.k;
+        if (op.stride == 1)
+            weights_fwd_layout(backbone_params_ + op.w_off, op.oc, op.ic, taps, round_up(op.ic, 32), op.wk, stream_);
+        else
+            weights_ohwi(backbone_params_ + op.w_off, op.oc, op.ic, taps, op.wk, stream_);
+    }
+    SY_CUDA(cudaStreamSynchronize(stream_));
+    backbone_ready_ = true;
+    return SY_OK;
+}
+
+void Session::forward_backbone(int batch) {
+    for (auto& op : bops_) {
+        View in = op.in, out = op.out;
+        if (op.type == 1) {
+            maxpool5_padded(in, out, batch, op.gin, stream_);
+        } else if (op.type == 2) {
+            upsample2_padded(in, op.gin, out, op.gout, batch, stream_);
+        } else {
+            ConvEpilogue ep;
+            ep.bias = backbone_params_ + op.b_off;
+            ep.silu = 1;
+            if (op.has_res) {
+                ep.residual = op.res.base;
+                ep.res_pitch = op.res.pitch;
+            }
+            if (op.stride == 1) {
+                // the tcgen05 kernel works on whole 128-row tiles: restrict the views to `batch` images
+                View i2 = in, o2 = out;
+                i2.rows = o2.rows = (long)batch * op.gin.rows;
+                conv_tc_forward(i2, op.wk, op.oc, op.oc, op.k * op.k, 1, op.gin, o2, ep, d_flags_, stream_);
+            } else {
+                conv_simt_forward(in, op.gin, op.wk, op.oc, op.k, op.stride, out, op.gout, batch, ep, stream_);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ head plan
+static std::string block_path(int i, int n) {
+    if (n == 5) {
+        static const char* p[5] = {"0.0", "0.1", "1.0", "1.1", "2"};
+        return p[i];
+    }
+    return std::to_string(i);
+}
+
+void Session::build_head() {
+    long poff = 0, qoff = 0;
+    for (int br = 0; br < 6; br++) {
+        Branch branch;
+        branch.level = br % 3;
+        branch.box = br < 3;
+        const int l = branch.level;
+        const int n = branch.box ? cfg.n_box_blocks : cfg.n_cls_blocks;
+        if (n < 1 || n > 8) throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "head branch needs 1..8 blocks");
+        const sy_block* blocks = branch.box ? cfg.box_blocks[l] : cfg.cls_blocks[l];
+        const std::string prefix = std::string(branch.box ? "cv2." : "cv3.") + std::to_string(l);
+        int ic = feat_ch_[l];
+        for (int i = 0; i < n; i++) {
+            HeadBlock hb;
+            hb.b = blocks[i];
+            const sy_block& b = hb.b;
+            if (b.ic != ic || b.oc < 1 || b.oc > 256 || !(b.k == 1 || b.k == 3) || b.groups != 1)
+                throw SyError(SY_ERR_UNSUPPORTED_SHAPE,
+                              "head conv must be k 1 or 3, groups 1, <= 256 channels, chained channels (" + prefix + ")");
+            if ((i == n - 1) == (b.has_bn != 0)) throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "only the last block is a Conv2d");
+            hb.taps = b.k * b.k;
+            const std::string path = prefix + "." + block_path(i, n);
+            const long wn = (long)b.oc * b.ic * b.k * b.k;
+            auto add_param = [&](const std::string& name, std::vector<int> shape, long numel, int decay) {
+                TensorEntry e{name, 0, shape, poff, numel, branch.box ? 1 : 0, decay};
+                tensors.push_back(e);
+                long off = poff;
+                poff += numel;
+                return off;
+            };
+            hb.w_off = add_param(path + (b.has_bn ? ".conv.weight" : ".weight"), {b.oc, b.ic, b.k, b.k}, wn, 1);
+            if (b.has_bias) hb.b_off = add_param(path + (b.has_bn ? ".conv.bias" : ".bias"), {b.oc}, b.oc, 0);
+            if (b.has_bn) {
+                hb.g_off = add_param(path + ".bn.weight", {b.oc}, b.oc, 0);
+                hb.be_off = add_param(path + ".bn.bias", {b.oc}, b.oc, 0);
+            }
+            ic = b.oc;
+            branch.blocks.push_back(hb);
+        }
+        const int expect = branch.box ? 4 * cfg.reg_max : cfg.num_classes;
+        if (branch.blocks.back().b.oc != expect)
+            throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "head output channels must be 4*reg_max (box) or nc (class)");
+        branches_.push_back(std::move(branch));
+    }
+    n_params = poff;
+    // buffers after all parameters (Snapshot order: parameters, then BN buffers)
+    for (auto& branch : branches_) {
+        const std::string prefix = std::string(branch.box ? "cv2." : "cv3.") + std::to_string(branch.level);
+        const int n = (int)branch.blocks.size();
+        for (int i = 0; i < n; i++) {
+            HeadBlock& hb = branch.blocks[i];
+            if (!hb.b.has_bn) continue;
+            const std::string path = prefix + "." + block_path(i, n);
+            hb.rm_off = qoff;
+            tensors.push_back(TensorEntry{path + ".bn.running_mean", 1, {hb.b.oc}, qoff, hb.b.oc, 0, 0});
+            qoff += hb.b.oc;
+            hb.rv_off = qoff;
+            tensors.push_back(TensorEntry{path + ".bn.running_var", 1, {hb.b.oc}, qoff, hb.b.oc, 0, 0});
+            qoff += hb.b.oc;
+            hb.nt_off = qoff;
+            tensors.push_back(TensorEntry{path + ".bn.num_batches_tracked", 1, {}, qoff, 1, 0, 0});
+            qoff += 1;
+        }
+    }
+    n_buffers = qoff;
+    params_ = static_cast<float*>(dalloc(sizeof(float) * n_params));
+    grads_ = static_cast<float*>(dalloc(sizeof(float) * n_params));
+    last_grads_ = static_cast<float*>(dalloc(sizeof(float) * n_params));
+    vel_ = static_cast<float*>(dalloc(sizeof(float) * n_params));
+    vel2_ = static_cast<float*>(dalloc(sizeof(float) * n_params));
+    buffers_ = static_cast<float*>(dalloc(sizeof(float) * std::max(1L, n_buffers)));
+    // running variance starts at 1 (fresh BatchNorm2d) until set_tensor overwrites it
+    {
+        std::vector<float> init(n_buffers, 0.0f);
+        for (auto& br : branches_)
+            for (auto& hb : br.blocks)
+                if (hb.b.has_bn)
+                    for (int c = 0; c < hb.b.oc; c++) init[hb.rv_off + c] = 1.0f;
+        SY_CUDA(cudaMemcpy(buffers_, init.data(), sizeof(float) * n_buffers, cudaMemcpyHostToDevice));
+    }
+    // optimizer segments: one per parameter tensor
+    std::vector<ParamSegment> segs;
+    for (auto& t : tensors)
+        if (t.kind == 0) segs.push_back(ParamSegment{t.offset, t.numel, t.decay, t.group});
+    nsegs_ = (int)segs.size();
+    d_segs_ = static_cast<ParamSegment*>(dalloc(sizeof(ParamSegment) * segs.size()));
+    SY_CUDA(cudaMemcpy(d_segs_, segs.data(), sizeof(ParamSegment) * segs.size(), cudaMemcpyHostToDevice));
+    // activations and gradients
+    size_t ws = 0;
+    int max_oc = 0;
+    for (auto& branch : branches_) {
+        const Grid& g = levels_[branch.level];
+        View x = features_[branch.level];
+        for (auto& hb : branch.blocks) {
+            const sy_block& b = hb.b;
+            hb.x = x;
+            hb.y = alloc_view(b.oc, g);
+            hb.g = alloc_view(b.oc, g);
+            if (b.has_bn) {
+                hb.a = alloc_view(b.oc, g);
+                hb.dy = alloc_view(b.oc, g);
+                hb.stats_off = bn_channels_;
+                bn_channels_ += b.oc;
+                hb.red = static_cast<float*>(dalloc(sizeof(float) * 2 * B_ * b.oc));
+            } else {
+                hb.dy = hb.g;
+            }
+            hb.kpad_in = round_up(b.ic, 32);
+            hb.kpad_out = round_up(b.oc, 32);
+            hb.w_fwd = static_cast<float*>(dalloc(sizeof(float) * (size_t)b.oc * hb.taps * hb.kpad_in));
+            hb.w_dgrad = static_cast<float*>(dalloc(sizeof(float) * (size_t)b.ic * hb.taps * hb.kpad_out));
+            ws = std::max(ws, wgrad_workspace_floats(b.ic, b.oc, hb.taps, (long)B_ * g.rows));
+            max_oc = std::max(max_oc, b.oc);
+            x = b.has_bn ? hb.a : hb.y;
+        }
+    }
+    // per-image BN statistics of all layers in one block ([layer][image][channel][2]) so that
+    // data-parallel ranks can exchange them with a single all-gather
+    bn_stats_all_ = static_cast<float*>(dalloc(sizeof(float) * 2 * (size_t)B_ * std::max(1L, bn_channels_)));
+    bn_gather_ = static_cast<float*>(
+        dalloc(sizeof(float) * 2 * (size_t)B_ * std::max(1L, bn_channels_) * cfg.world_size));
+    for (auto& branch : branches_)
+        for (auto& hb : branch.blocks)
+            if (hb.b.has_bn) hb.stats = bn_stats_all_ + 2 * (size_t)B_ * hb.stats_off;
+    wgrad_ws_ = static_cast<float*>(dalloc(sizeof(float) * ws));
+    bias_part_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)B_ * max_oc));
+}
+
+void Session::refresh_head_weights() {
+    for (auto& branch : branches_)
+        for (auto& hb : branch.blocks) {
+            weights_fwd_layout(params_ + hb.w_off, hb.b.oc, hb.b.ic, hb.taps, hb.kpad_in, hb.w_fwd, stream_);
+            weights_dgrad_layout(params_ + hb.w_off, hb.b.oc, hb.b.ic, hb.taps, hb.kpad_out, hb.w_dgrad, stream_);
+        }
+}
+
+static View rows_of(View v, int batch, const Grid& g) {
+    v.rows = (long)batch * g.rows;
+    return v;
+}
+
+void Session::forward_head(int batch) {
+    for (auto& branch : branches_) {
+        const Grid& g = levels_[branch.level];
+        for (auto& hb : branch.blocks) {
+            ConvEpilogue ep;
+            if (hb.b.has_bias) ep.bias = params_ + hb.b_off;
+            conv_tc_forward(rows_of(hb.x, batch, g), hb.w_fwd, hb.b.oc, hb.b.oc, hb.taps, 1, g,
+                            rows_of(hb.y, batch, g), ep, d_flags_, stream_);
+            if (hb.b.has_bn) {
+                bn_stats(hb.y, batch, g, hb.stats, stream_);
+                bn_silu_apply(hb.y, hb.stats, params_ + hb.g_off, params_ + hb.be_off, cfg.bn_eps, batch, g, hb.a,
+                              stream_);
+            }
+        }
+    }
+}
+
+void Session::backward_head(int batch) {
+    for (int l = 2; l >= 0; l--)
+        for (int kind = 1; kind >= 0; kind--) {
+            Branch& branch = branches_[kind * 3 + l];
+            const Grid& g = levels_[l];
+            for (int i = (int)branch.blocks.size() - 1; i >= 0; i--) {
+                HeadBlock& hb = branch.blocks[i];
+                if (hb.b.has_bn)
+                    bn_silu_backward(hb.y, hb.g, hb.stats, params_ + hb.g_off, params_ + hb.be_off, cfg.bn_eps, batch,
+                                     g, hb.red, hb.dy, grads_ + hb.g_off, grads_ + hb.be_off, stream_);
+                if (hb.b.has_bias) bias_grad(hb.dy, batch, g, bias_part_, grads_ + hb.b_off, stream_);
+                conv_tc_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off,
+                              wgrad_ws_, d_flags_, stream_);
+                if (i > 0) {
+                    HeadBlock& prev = branch.blocks[i - 1];
+                    ConvEpilogue ep;
+                    conv_tc_forward(rows_of(hb.dy, batch, g), hb.w_dgrad, hb.b.ic, hb.b.ic, hb.taps, -1, g,
+                                    rows_of(prev.g, batch, g), ep, d_flags_, stream_);
+                }
+            }
+        }
+}
+
+// ------------------------------------------------------------------ step
+int Session::step(const uint8_t* rgb, const float* const* features, const sy_box* boxes, const int32_t* counts,
+                  int images, sy_step_stats* out) {
+    if (images < 1 || images > B_) throw SyError(SY_ERR_INVALID_ARGUMENT, "images out of range");
+    if (!counts || (!boxes && images > 0)) throw SyError(SY_ERR_INVALID_ARGUMENT, "counts / boxes missing");
+    SY_CUDA(cudaSetDevice(device_));
+    // validate and stage ground truth (TrainingDataset.ParseLabels guarantees, DetectionLoss.cs:51)
+    long k = 0;
+    h_box_off_[0] = 0;
+    for (int b = 0; b < images; b++) {
+        if (counts[b] < 0 || counts[b] > cfg.max_boxes) throw SyError(SY_ERR_INVALID_ARGUMENT, "box count out of range");
+        for (int j = 0; j < counts[b]; j++, k++) {
+            const sy_box& bx = boxes[k];
+            if (bx.class_id < 0 || bx.class_id >= cfg.num_classes)
+                throw SyError(SY_ERR_INVALID_ARGUMENT, "class id out of range");
+            if (!std::isfinite(bx.x1) || !std::isfinite(bx.y1) || !std::isfinite(bx.x2) || !std::isfinite(bx.y2))
+                throw SyError(SY_ERR_INVALID_ARGUMENT, "box coordinates not finite");
+            h_truth_[k] = TruthBox{bx.class_id, bx.x1, bx.y1, bx.x2, bx.y2};
+        }
+        h_box_off_[b + 1] = (int)k;
+    }
+    if (rgb && (cfg.backbone != SY_BACKBONE_YOLOV8 || !backbone_ready_))
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "backbone weights not set");
+    SY_CUDA(cudaEventRecord(ev0_, stream_));
+    if (k > 0)
+        SY_CUDA(cudaMemcpyAsync(d_truth_, h_truth_, sizeof(TruthBox) * k, cudaMemcpyHostToDevice, stream_));
+    SY_CUDA(cudaMemcpyAsync(d_box_off_, h_box_off_, sizeof(int) * (images + 1), cudaMemcpyHostToDevice, stream_));
+    SY_CUDA(cudaMemsetAsync(d_flags_, 0, sizeof(int) * 16, stream_));
+    if (rgb) {
+        const size_t bytes = (size_t)images * cfg.image_size * cfg.image_size * 3;
+        std::memcpy(h_rgb_, rgb, bytes);
+        SY_CUDA(cudaMemcpyAsync(d_rgb_, h_rgb_, bytes, cudaMemcpyHostToDevice, stream_));
+        rgb_to_padded(d_rgb_, images, cfg.image_size, img_grid_, img_, stream_);
+        forward_backbone(images);
+    } else {
+        if (!features) throw SyError(SY_ERR_INVALID_ARGUMENT, "features missing");
+        for (int l = 0; l < 3; l++) {
+            const Grid& g = levels_[l];
+            const size_t n = (size_t)images * feat_ch_[l] * g.h * g.w;
+            SY_CUDA(cudaMemcpyAsync(feat_stage_, features[l], n * sizeof(float), cudaMemcpyHostToDevice, stream_));
+            nchw_to_padded(feat_stage_, images, feat_ch_[l], g, features_[l], stream_);
+        }
+    }
+    forward_head(images);
+    // loss
+    LevelIO lv[3];
+    for (int l = 0; l < 3; l++) {
+        HeadBlock& bb = branches_[l].blocks.back();
+        HeadBlock& cb = branches_[3 + l].blocks.back();
+        lv[l] = LevelIO{bb.y.base, cb.y.base, bb.g.base, cb.g.base, bb.y.pitch, cb.y.pitch, levels_[l],
+                        (float)(8 << l)};
+    }
+    LossOut lo{d_loss_, d_pos_, d_conn_, nullptr, nullptr};
+    detection_loss(lv, 3, images, cfg.num_classes, cfg.reg_max, d_truth_, d_box_off_, std::max(1, cfg.max_boxes), 10,
+                   1.0f, 1, loss_ws_, lo, stream_);
+    backward_head(images);
+    SY_CUDA(cudaMemcpyAsync(last_grads_, grads_, sizeof(float) * n_params, cudaMemcpyDeviceToDevice, stream_));
+    check_finite(grads_, n_params, d_flags_ + 1, stream_);
+    abs_sum_partials(grads_, n_params, d_abs_, stream_);
+    SY_CUDA(cudaMemcpyAsync(h_loss_, d_loss_, sizeof(float) * 4 * images, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaMemcpyAsync(h_pos_, d_pos_, sizeof(int) * images, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaMemcpyAsync(h_conn_, d_conn_, sizeof(int) * images, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaMemcpyAsync(h_flags_, d_flags_, sizeof(int) * 16, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaMemcpyAsync(h_abs_, d_abs_, sizeof(double) * kAbsSumBlocks, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaStreamSynchronize(stream_));
+    if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "device wait limit exceeded (code " + std::to_string(h_flags_[0]) + ")");
+    double box = 0, cls = 0, dfl = 0, abs_sum = 0;
+    long positives = 0;
+    int connected = 0;
+    bool finite = h_flags_[1] == 0;
+    for (int b = 0; b < images; b++) {
+        box += h_loss_[4 * b];
+        cls += h_loss_[4 * b + 1];
+        dfl += h_loss_[4 * b + 2];
+        if (!std::isfinite(h_loss_[4 * b] + h_loss_[4 * b + 1] + h_loss_[4 * b + 2])) finite = false;
+        positives += h_pos_[b];
+        connected |= h_conn_[b];
+    }
+    for (int i = 0; i < kAbsSumBlocks; i++) abs_sum += h_abs_[i];
+    int global_images = images;
+    if (comm_) {
+        // one all-reduce for the gradient bucket, one for the scalars (sum): loss parts,
+        // positives, connected count, non-finite count, images
+        int r = nccl_->AllReduce(grads_, grads_, (size_t)n_params, kNcclFloat, kNcclSum, comm_, stream_);
+        if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllReduce: ") + nccl_->GetErrorString(r));
+        double* hs = reinterpret_cast<double*>(h_abs_);  // reuse pinned scratch (>= 8 doubles)
+        hs[0] = box;
+        hs[1] = cls;
+        hs[2] = dfl;
+        hs[3] = (double)positives;
+        hs[4] = connected;
+        hs[5] = finite ? 0.0 : 1.0;
+        hs[6] = images;
+        double* ds = d_abs_;
+        SY_CUDA(cudaMemcpyAsync(ds, hs, sizeof(double) * 7, cudaMemcpyHostToDevice, stream_));
+        r = nccl_->AllReduce(ds, ds, 7, kNcclDouble, kNcclSum, comm_, stream_);
+        if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllReduce: ") + nccl_->GetErrorString(r));
+        SY_CUDA(cudaMemcpyAsync(hs, ds, sizeof(double) * 7, cudaMemcpyDeviceToHost, stream_));
+        SY_CUDA(cudaStreamSynchronize(stream_));
+        box = hs[0];
+        cls = hs[1];
+        dfl = hs[2];
+        positives = (long)hs[3];
+        connected = hs[4] > 0;
+        finite = hs[5] == 0;
+        global_images = (int)hs[6];
+    }
+    if (!finite) {
+        SY_CUDA(cudaMemsetAsync(grads_, 0, sizeof(float) * n_params, stream_));
+        SY_CUDA(cudaStreamSynchronize(stream_));
+        throw SyError(SY_ERR_NONFINITE, "non-finite loss or gradient; parameters not updated");
+    }
+    // BN running statistics, global images in order (HeadOperations.cs:164-165): ranks
+    // all-gather their per-image statistics and every rank folds rank 0's images, then rank 1's...
+    const float* stats_src = bn_stats_all_;
+    int ranks = 1;
+    const size_t stats_floats = 2 * (size_t)B_ * bn_channels_;
+    if (comm_) {
+        int r = nccl_->AllGather(bn_stats_all_, bn_gather_, stats_floats, kNcclFloat, comm_, stream_);
+        if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllGather: ") + nccl_->GetErrorString(r));
+        stats_src = bn_gather_;
+        ranks = cfg.world_size;
+    }
+    for (auto& branch : branches_)
+        for (auto& hb : branch.blocks)
+            if (hb.b.has_bn) {
+                const Grid& g = levels_[branch.level];
+                bn_running_update(stats_src + 2 * (size_t)B_ * hb.stats_off, (long)stats_floats, ranks, images,
+                                  hb.b.oc, g.h * g.w, cfg.bn_momentum, buffers_ + hb.rm_off, buffers_ + hb.rv_off,
+                                  buffers_ + hb.nt_off, stream_);
+            }
+    // update
+    h_flags_[2] = 1;
+    h_flags_[3] = connected ? 1 : 0;
+    if (cfg.optimizer == SY_OPT_ADAMW) {
+        adam_steps_[0]++;
+        if (connected) adam_steps_[1]++;
+    }
+    h_flags_[4] = adam_steps_[0];
+    h_flags_[5] = adam_steps_[1];
+    h_flags_[1] = 0;
+    SY_CUDA(cudaMemcpyAsync(d_flags_ + 1, h_flags_ + 1, sizeof(int) * 5, cudaMemcpyHostToDevice, stream_));
+    optimizer_step(cfg.optimizer, params_, vel_, vel2_, grads_, d_segs_, nsegs_, d_flags_ + 2, d_flags_ + 4, cfg.lr,
+                   cfg.momentum, cfg.weight_decay, cfg.beta1, cfg.beta2, cfg.adam_eps, 1.0f / (float)global_images,
+                   d_flags_ + 1, stream_);
+    refresh_head_weights();
+    SY_CUDA(cudaEventRecord(ev1_, stream_));
+    SY_CUDA(cudaMemcpyAsync(h_flags_, d_flags_, sizeof(int) * 2, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaStreamSynchronize(stream_));
+    last_batch_ = images;
+    if (out) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, ev0_, ev1_);
+        out->box = box;
+        out->cls = cls;
+        out->dfl = dfl;
+        out->positives = positives;
+        out->images = global_images;
+        out->box_has_grad = connected;
+        out->grad_checksum = abs_sum / global_images;
+        out->device_ms = ms;
+    }
+    if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "device wait limit exceeded");
+    if (h_flags_[1]) throw SyError(SY_ERR_NONFINITE, "non-finite parameters after the update");
+    return SY_OK;
+}
+
+// ------------------------------------------------------------------ tensors
+int Session::set_tensor(int index, const float* host, long count) {
+    if (index < 0 || index >= (int)tensors.size()) throw SyError(SY_ERR_INVALID_ARGUMENT, "tensor index");
+    const TensorEntry& t = tensors[index];
+    if (count != t.numel || !host) throw SyError(SY_ERR_INVALID_ARGUMENT, "tensor size mismatch");
+    float* dst = (t.kind == 0 ? params_ : buffers_) + t.offset;
+    SY_CUDA(cudaMemcpyAsync(dst, host, sizeof(float) * count, cudaMemcpyHostToDevice, stream_));
+    if (t.kind == 0) refresh_head_weights();
+    SY_CUDA(cudaStreamSynchronize(stream_));
+    return SY_OK;
+}
+
+int Session::get_tensor(int index, float* host, long count) const {
+    if (index < 0 || index >= (int)tensors.size()) throw SyError(SY_ERR_INVALID_ARGUMENT, "tensor index");
+    const TensorEntry& t = tensors[index];
+    if (count != t.numel || !host) throw SyError(SY_ERR_INVALID_ARGUMENT, "tensor size mismatch");
+    const float* src = (t.kind == 0 ? params_ : buffers_) + t.offset;
+    SY_CUDA(cudaMemcpy(host, src, sizeof(float) * count, cudaMemcpyDeviceToHost));
+    return SY_OK;
+}
+
+int Session::set_opt_state(int index, int moment, const float* host, long count) {
+    if (index < 0 || index >= (int)tensors.size() || tensors[index].kind != 0 || moment < 0 || moment > 1)
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "optimizer state index");
+    const TensorEntry& t = tensors[index];
+    if (count != t.numel || !host) throw SyError(SY_ERR_INVALID_ARGUMENT, "tensor size mismatch");
+    for (long i = 0; i < count; i++)
+        if (!std::isfinite(host[i])) throw SyError(SY_ERR_INVALID_ARGUMENT, "optimizer state not finite");
+    SY_CUDA(cudaMemcpy((moment ? vel2_ : vel_) + t.offset, host, sizeof(float) * count, cudaMemcpyHostToDevice));
+    return SY_OK;
+}
+
+int Session::get_opt_state(int index, int moment, float* host, long count) const {
+    if (index < 0 || index >= (int)tensors.size() || tensors[index].kind != 0 || moment < 0 || moment > 1)
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "optimizer state index");
+    const TensorEntry& t = tensors[index];
+    if (count != t.numel || !host) throw SyError(SY_ERR_INVALID_ARGUMENT, "tensor size mismatch");
+    SY_CUDA(cudaMemcpy(host, (moment ? vel2_ : vel_) + t.offset, sizeof(float) * count, cudaMemcpyDeviceToHost));
+    return SY_OK;
+}
+
+int Session::get_last_gradients(float* host, long count) const {
+    if (count != n_params || !host) throw SyError(SY_ERR_INVALID_ARGUMENT, "gradient size mismatch");
+    SY_CUDA(cudaMemcpy(host, last_grads_, sizeof(float) * count, cudaMemcpyDeviceToHost));
+    return SY_OK;
+}
+
+int Session::get_last_features(int level, float* host, long count) const {
+    if (level < 0 || level > 2 || !host) throw SyError(SY_ERR_INVALID_ARGUMENT, "level");
+    const Grid& g = levels_[level];
+    const long n = (long)last_batch_ * feat_ch_[level] * g.h * g.w;
+    if (count != n) throw SyError(SY_ERR_INVALID_ARGUMENT, "feature size mismatch");
+    float* tmp = nullptr;
+    SY_CUDA(cudaMalloc(&tmp, sizeof(float) * n));
+    padded_to_nchw(features_[level], last_batch_, feat_ch_[level], g, tmp, stream_);
+    cudaError_t e = cudaMemcpyAsync(host, tmp, sizeof(float) * n, cudaMemcpyDeviceToHost, stream_);
+    cudaStreamSynchronize(stream_);
+    cudaFree(tmp);
+    SY_CUDA(e);
+    return SY_OK;
+}
+
+}  // namespace sy

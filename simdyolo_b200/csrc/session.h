@@ -1,0 +1,147 @@
+// Training session: owns the device state of one data-parallel rank and runs the fine-tuning step
+// (YoloTrainer.Train inner loop, src/SimdYolo.Training/YoloTrainer.cs:185-199) on the GPU.
+#pragma once
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/simdyolo_cuda.h"
+#include "kernels.h"
+
+namespace sy {
+
+// Error carrying an sy_status code; thrown inside the library, converted at the C ABI.
+struct SyError : std::runtime_error {
+    int code;
+    SyError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+struct TensorEntry {
+    std::string name;
+    int kind;            // 0 parameter, 1 buffer
+    std::vector<int> shape;
+    long offset;         // in params (kind 0) or buffers (kind 1)
+    long numel;
+    int group;           // parameters: 0 always connected, 1 box branch
+    int decay;
+};
+
+struct HeadBlock {
+    sy_block b;
+    int taps;
+    long w_off = -1, b_off = -1, g_off = -1, be_off = -1;
+    long rm_off = -1, rv_off = -1, nt_off = -1;
+    float* w_fwd = nullptr;     // [oc][taps][kpad_in]
+    float* w_dgrad = nullptr;   // [ic][taps][kpad_out]
+    int kpad_in = 0, kpad_out = 0;
+    View x{}, y{}, a{}, g{}, dy{};
+    float* stats = nullptr;     // [B][oc][2] inside the session's contiguous statistics block
+    long stats_off = 0;         // channel offset of this layer in that block
+    float* red = nullptr;       // [B][oc][2]
+};
+
+struct Branch {
+    int level;
+    bool box;
+    std::vector<HeadBlock> blocks;
+};
+
+struct BackboneOp {
+    int type;                   // 0 conv, 1 maxpool5, 2 upsample2
+    int ic = 0, oc = 0, k = 0, stride = 1;
+    long w_off = 0, b_off = 0;
+    float* wk = nullptr;        // K-major (stride 1) or OHWI (stride 2)
+    View in{}, out{}, res{};
+    Grid gin{}, gout{};
+    bool has_res = false;
+};
+
+struct NcclApi;
+
+class Session {
+public:
+    explicit Session(const sy_config& cfg);
+    ~Session();
+
+    sy_config cfg;
+    std::string error;
+
+    // public operations (return sy_status)
+    int step(const uint8_t* rgb, const float* const* features, const sy_box* boxes, const int32_t* counts,
+             int images, sy_step_stats* out);
+    int set_tensor(int index, const float* host, long count);
+    int get_tensor(int index, float* host, long count) const;
+    int set_opt_state(int index, int moment, const float* host, long count);
+    int get_opt_state(int index, int moment, float* host, long count) const;
+    int set_backbone(const float* host, long count);
+    int get_last_gradients(float* host, long count) const;
+    int get_last_features(int level, float* host, long count) const;
+
+    std::vector<TensorEntry> tensors;
+    long n_params = 0, n_buffers = 0, n_backbone = 0;
+
+private:
+    void build_backbone();
+    void build_head();
+    void forward_backbone(int batch);
+    void forward_head(int batch);
+    void backward_head(int batch);
+    void refresh_head_weights();
+    View alloc_view(int channels, const Grid& g);
+    void* dalloc(size_t bytes);
+
+    int device_ = 0;
+    cudaStream_t stream_ = nullptr;
+    cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
+    std::vector<void*> allocations_;
+    int B_ = 0;
+    Grid levels_[3];
+    int feat_ch_[3] = {0, 0, 0};
+    View features_[3];
+    // backbone
+    std::vector<BackboneOp> bops_;
+    float* backbone_params_ = nullptr;
+    uint8_t* d_rgb_ = nullptr;
+    uint8_t* h_rgb_ = nullptr;   // pinned staging
+    View img_{};
+    Grid img_grid_{};
+    bool backbone_ready_ = false;
+    // head
+    std::vector<Branch> branches_;
+    float* params_ = nullptr;
+    float* grads_ = nullptr;
+    float* last_grads_ = nullptr;
+    float* vel_ = nullptr;
+    float* vel2_ = nullptr;
+    float* buffers_ = nullptr;
+    float* wgrad_ws_ = nullptr;
+    float* feat_stage_ = nullptr;
+    float* bn_stats_all_ = nullptr;
+    float* bn_gather_ = nullptr;
+    long bn_channels_ = 0;
+    float* bias_part_ = nullptr;
+    void* loss_ws_ = nullptr;
+    TruthBox* d_truth_ = nullptr;
+    int* d_box_off_ = nullptr;
+    TruthBox* h_truth_ = nullptr;
+    int* h_box_off_ = nullptr;
+    float* d_loss_ = nullptr;
+    int* d_pos_ = nullptr;
+    int* d_conn_ = nullptr;
+    int* d_flags_ = nullptr;     // [0] device error, [1] nonfinite, [2..3] group has_grad, [4..5] adam steps
+    int* h_flags_ = nullptr;
+    float* h_loss_ = nullptr;
+    int* h_pos_ = nullptr;
+    int* h_conn_ = nullptr;
+    double* d_abs_ = nullptr;
+    double* h_abs_ = nullptr;
+    ParamSegment* d_segs_ = nullptr;
+    int nsegs_ = 0;
+    int adam_steps_[2] = {0, 0};
+    int last_batch_ = 0;
+    NcclApi* nccl_ = nullptr;
+    void* comm_ = nullptr;
+};
+
+}  // namespace sy

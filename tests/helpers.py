@@ -1,0 +1,85 @@
+"""Shared test helpers: build oracle descriptors from the product's model description, and run the
+oracle's head-only step (YoloTrainer.cs:185-197 with cached features) for parity checks."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+import simdyolo_b200 as sy
+from oracle import oracle as O
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def head_desc(cfg: sy.Config) -> O.HeadDesc:
+    d = O.HeadDesc()
+    d.levels = 3
+    d.nc = cfg.num_classes
+    d.bins = cfg.reg_max
+    for l in range(3):
+        s = cfg.image_size >> (3 + l)
+        d.hs[l] = s
+        d.ws[l] = s
+        d.strides[l] = float(8 << l)
+    d.n_box_blocks = cfg.n_box_blocks
+    d.n_cls_blocks = cfg.n_cls_blocks
+    for l in range(3):
+        for i in range(cfg.n_box_blocks):
+            b = cfg.box_blocks[l][i]
+            d.box_blocks[l][i] = O.Block(b.ic, b.oc, b.k, b.groups, b.has_bn, b.has_bias)
+        for i in range(cfg.n_cls_blocks):
+            b = cfg.cls_blocks[l][i]
+            d.cls_blocks[l][i] = O.Block(b.ic, b.oc, b.k, b.groups, b.has_bn, b.has_bias)
+    d.bn_eps = cfg.bn_eps
+    d.bn_momentum = cfg.bn_momentum
+    return d
+
+
+def backbone_desc(cfg: sy.Config) -> O.BackboneDesc:
+    return O.BackboneDesc(cfg.image_size, cfg.width_mult, cfg.depth_mult, cfg.max_channels)
+
+
+def oracle_head_step(cfg: sy.Config, tensors, params, buffers, velocity, features, truth):
+    """Head forward / loss / backward per image, gradients summed in image order, then
+    TrainingParameter.Update for every tensor.  Returns (losses[B] dicts, grad, params, buffers,
+    velocity) with arrays updated copies."""
+    L = O.lib()
+    d = head_desc(cfg)
+    params = params.astype(np.float32).copy()
+    buffers = buffers.astype(np.float32).copy()
+    velocity = velocity.astype(np.float32).copy()
+    grad = np.zeros_like(params)
+    losses = []
+    connected_any = False
+    B = features[0].shape[0]
+    for b in range(B):
+        feats = [np.ascontiguousarray(f[b], np.float32) for f in features]
+        VP = C.c_void_p * 3
+        fp = VP(*[f.ctypes.data_as(C.c_void_p) for f in feats])
+        out = O.Loss()
+        conn = np.zeros(1, np.int32)
+        tb = O.boxes(truth[b])
+        rc = L.syo_head_image(C.byref(d), params, buffers, fp, tb, len(truth[b]), grad, C.byref(out), 1, conn)
+        assert rc == 0
+        losses.append(dict(box=out.box, cls=out.cls, dfl=out.dfl, positives=out.positives))
+        connected_any |= bool(conn[0])
+    summed = grad.copy()
+    off = 0
+    for t in tensors:
+        if t["kind"] != 0:
+            continue
+        n = t["numel"]
+        box = t["name"].startswith("cv2")
+        decay = t["name"].endswith("conv.weight") or (t["name"].endswith(".weight") and len(t["shape"]) == 4)
+        has = connected_any if box else True
+        w, v, g = params[off:off + n].copy(), velocity[off:off + n].copy(), grad[off:off + n].copy()
+        rc = O.sgd_update(w, v, g, cfg.lr, cfg.momentum, cfg.weight_decay if decay else 0.0, B, has)
+        assert rc == 0
+        params[off:off + n], velocity[off:off + n] = w, v
+        off += n
+    return losses, summed, params, buffers, velocity, connected_any

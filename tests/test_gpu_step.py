@@ -1,0 +1,148 @@
+"""GPU parity of the whole fine-tuning step (session API) against the CPU oracle.
+
+The oracle runs the reference's sequential loop (YoloTrainer.cs:185-197): per image head forward with
+training BatchNorm, DetectionLoss, backward, gradients summed in image order, then
+TrainingParameter.Update for every tensor.  The GPU step must agree within the TF32 bound of 2e-3
+relative L2 on loss, gradients, parameter updates and BN running statistics.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import simdyolo_b200 as sy
+from simdyolo_b200 import data
+from oracle import oracle as O
+from tests.helpers import backbone_desc, head_desc, oracle_head_step, rel_l2
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+def make_session(image_size, batch, backbone, nc=80, seed=0, max_boxes=8, model="yolov8n"):
+    cfg = sy.make_config(model, image_size=image_size, max_batch=batch, max_boxes=max_boxes, num_classes=nc,
+                         backbone=backbone)
+    s = sy.Session(cfg)
+    params, buffers = data.head_params(s, seed)
+    s.set_flat_params(params)
+    s.set_flat_buffers(buffers)
+    return s, cfg, params, buffers
+
+
+def features_for(cfg, batch, rng):
+    feats = []
+    for l in range(3):
+        h = cfg.image_size >> (3 + l)
+        feats.append((rng.standard_normal((batch, cfg.feature_channels[l], h, h)) * 0.7 + 0.2).astype(np.float32))
+    return feats
+
+
+@pytest.mark.parametrize("image_size,batch,nboxes", [(128, 3, (1, 4)), (256, 2, (1, 8))])
+def test_step_from_features_matches_oracle(image_size, batch, nboxes):
+    rng = np.random.default_rng(5)
+    s, cfg, params, buffers = make_session(image_size, batch, backbone=False)
+    feats = features_for(cfg, batch, rng)
+    _, truth = data.synthetic_batch(rng, batch, image_size, cfg.num_classes, boxes=nboxes,
+                                    wh=(8.0, image_size / 2))
+    stats = s.step_features(feats, truth)
+    grad = s.last_gradients()
+    losses, ograd, oparams, obuffers, ovel, conn = oracle_head_step(cfg, s.tensors, params, buffers,
+                                                                    np.zeros_like(params), feats, truth)
+    obox = sum(l["box"] for l in losses)
+    ocls = sum(l["cls"] for l in losses)
+    odfl = sum(l["dfl"] for l in losses)
+    assert abs(stats.cls - ocls) <= TOL * abs(ocls)
+    assert abs(stats.box - obox) <= TOL * max(abs(obox), 1.0)
+    assert abs(stats.dfl - odfl) <= TOL * max(abs(odfl), 1.0)
+    assert stats.positives == sum(l["positives"] for l in losses)
+    assert stats.box_has_grad == int(conn)
+    assert rel_l2(grad, ograd) < TOL
+    new_params = s.flat_params()
+    assert rel_l2(new_params - params, oparams - params) < TOL
+    assert rel_l2(s.flat_velocity(), ovel) < TOL
+    assert rel_l2(s.flat_buffers(), obuffers) < TOL
+
+
+def test_step_without_boxes_skips_box_branch():
+    """Background-only batch: the box branch has no gradient, so its parameters and velocity stay
+    bit-identical (TrainingParameter.cs:24 / DetectionLoss.cs:101)."""
+    rng = np.random.default_rng(9)
+    s, cfg, params, buffers = make_session(128, 2, backbone=False)
+    feats = features_for(cfg, 2, rng)
+    stats = s.step_features(feats, [[], []])
+    assert stats.positives == 0 and stats.box_has_grad == 0
+    off = 0
+    new = s.flat_params()
+    for t in s.params:
+        n = t["numel"]
+        if t["name"].startswith("cv2"):
+            assert new[off:off + n].tobytes() == params[off:off + n].tobytes(), t["name"]
+        else:
+            assert not np.array_equal(new[off:off + n], params[off:off + n]) or t["name"].endswith("bn.bias"), t["name"]
+        off += n
+
+
+def test_invalid_boxes_are_rejected():
+    s, cfg, _, _ = make_session(128, 1, backbone=False)
+    feats = features_for(cfg, 1, np.random.default_rng(0))
+    with pytest.raises(ValueError):
+        s.step_features(feats, [[(cfg.num_classes, 0, 0, 10, 10)]])
+    with pytest.raises(ValueError):
+        s.step_features(feats, [[(0, 0, 0, 10, 10)] * (cfg.max_boxes + 1)])
+
+
+def test_full_step_backbone_and_head_match_oracle():
+    image_size, batch = 128, 2
+    rng = np.random.default_rng(11)
+    s, cfg, params, buffers = make_session(image_size, batch, backbone=True)
+    bparams = data.backbone_params(sy.MODELS["yolov8n"], seed=0)
+    s.set_backbone(bparams)
+    images, truth = data.synthetic_batch(rng, batch, image_size, cfg.num_classes, boxes=(1, 6), wh=(8.0, 64.0))
+    stats = s.step(images, truth)
+    # frozen features
+    bd = backbone_desc(cfg)
+    feats = []
+    for l in range(3):
+        h = image_size >> (3 + l)
+        feats.append(np.zeros((batch, cfg.feature_channels[l], h, h), np.float32))
+    for b in range(batch):
+        f = [np.zeros((cfg.feature_channels[l], image_size >> (3 + l), image_size >> (3 + l)), np.float32)
+             for l in range(3)]
+        O.lib().syo_backbone_forward(C.byref(bd), bparams, images[b].ctypes.data_as(C.POINTER(C.c_uint8)), *f)
+        for l in range(3):
+            feats[l][b] = f[l]
+    for l in range(3):
+        got = s.last_features(l, feats[l].shape)
+        assert rel_l2(got, feats[l]) < TOL, f"level {l}"
+    losses, ograd, oparams, obuffers, ovel, conn = oracle_head_step(cfg, s.tensors, params, buffers,
+                                                                    np.zeros_like(params), feats, truth)
+    assert abs(stats.cls - sum(l["cls"] for l in losses)) <= TOL * abs(sum(l["cls"] for l in losses))
+    assert rel_l2(s.last_gradients(), ograd) < 5 * TOL
+    assert rel_l2(s.flat_params() - params, oparams - params) < 5 * TOL
+
+
+def test_oracle_full_step_matches_session_loss_over_steps():
+    """Config-0 style run (scaled down): several SGD steps; losses track the oracle's full step."""
+    image_size, batch, steps = 128, 2, 3
+    rng = np.random.default_rng(21)
+    s, cfg, params, buffers = make_session(image_size, batch, backbone=True)
+    bparams = data.backbone_params(sy.MODELS["yolov8n"], seed=0)
+    s.set_backbone(bparams)
+    bd, hd = backbone_desc(cfg), head_desc(cfg)
+    op, ob = params.copy(), buffers.copy()
+    ov, ov2 = np.zeros_like(params), np.zeros_like(params)
+    opt = O.Optim(cfg.lr, cfg.momentum, cfg.weight_decay, 0, cfg.beta1, cfg.beta2, cfg.adam_eps)
+    for _ in range(steps):
+        images, truth = data.synthetic_batch(rng, batch, image_size, cfg.num_classes, boxes=(1, 6), wh=(8.0, 64.0))
+        stats = s.step(images, truth)
+        flat = [bx for t in truth for bx in t]
+        tb = O.boxes(flat)
+        counts = np.array([len(t) for t in truth], np.int32)
+        ptrs = (C.c_void_p * batch)(*[images[b].ctypes.data_as(C.c_void_p) for b in range(batch)])
+        res = O.StepResult()
+        O.lib().syo_train_step(C.byref(bd), bparams, C.byref(hd), op, ob, ov, ov2, C.byref(opt), ptrs, tb, counts,
+                               batch, 0, None, C.byref(res))
+        assert res.status == 0
+        total = stats.box + stats.cls + stats.dfl
+        assert abs(total - (res.box + res.cls + res.dfl)) <= 5 * TOL * (res.box + res.cls + res.dfl)
+    assert rel_l2(s.flat_params() - params, op - params) < 1e-2
