@@ -7,6 +7,8 @@
 // batch-of-one convs, so a batch of B images needs B x C statistics.  Reductions are written per
 // (image, channel) and folded over images in image order, so results do not depend on timing.
 #include <algorithm>
+#include <stdexcept>
+#include <string>
 
 #include "kernels.h"
 
@@ -205,6 +207,7 @@ int blocks_for(long n) { return (int)std::min<long>(148L * 64, std::max<long>(1,
 void bn_stats(const View& y, int batch, const Grid& g, float* stats, cudaStream_t stream) {
     dim3 grid((y.channels + 31) / 32, batch);
     bn_stats_kernel<<<grid, 256, 0, stream>>>(y.base, y.pitch, y.channels, g, stats);
+    launch_check("bn_stats_kernel");
 }
 
 void bn_silu_apply(const View& y, const float* stats, const float* gamma, const float* beta, float eps, int batch,
@@ -212,6 +215,7 @@ void bn_silu_apply(const View& y, const float* stats, const float* gamma, const 
     long n = (long)batch * g.rows * y.channels;
     bn_apply_kernel<<<blocks_for(n), 256, 0, stream>>>(y.base, y.pitch, stats, gamma, beta, eps, y.channels, batch, g,
                                                        a.base, a.pitch);
+    launch_check("bn_apply_kernel");
 }
 
 void bn_silu_backward(const View& y, const View& gv, const float* stats, const float* gamma, const float* beta,
@@ -221,22 +225,28 @@ void bn_silu_backward(const View& y, const View& gv, const float* stats, const f
     dim3 grid((c + 31) / 32, batch);
     bn_bwd_reduce_kernel<<<grid, 256, 0, stream>>>(y.base, y.pitch, gv.base, gv.pitch, stats, gamma, beta, eps, c, gr,
                                                    red);
+    launch_check("bn_bwd_reduce_kernel");
     long n = (long)batch * gr.rows * c;
     bn_bwd_apply_kernel<<<blocks_for(n), 256, 0, stream>>>(y.base, y.pitch, gv.base, gv.pitch, stats, red, gamma,
                                                            beta, eps, c, batch, gr, dy.base, dy.pitch);
+    launch_check("bn_bwd_apply_kernel");
     bn_param_grad_kernel<<<(c + 127) / 128, 128, 0, stream>>>(red, batch, c, dgamma, dbeta);
+    launch_check("bn_param_grad_kernel");
 }
 
 void bn_running_update(const float* stats, long rank_stride, int ranks, int batch, int c, int spatial, float momentum,
                        float* rmean, float* rvar, float* tracked, cudaStream_t stream) {
     bn_running_kernel<<<(c + 127) / 128, 128, 0, stream>>>(stats, rank_stride, ranks, batch, c, spatial, momentum,
                                                            rmean, rvar, tracked);
+    launch_check("bn_running_kernel");
 }
 
 void bias_grad(const View& gv, int batch, const Grid& gr, float* part, float* db, cudaStream_t stream) {
     dim3 grid((gv.channels + 31) / 32, batch);
     bias_partial_kernel<<<grid, 256, 0, stream>>>(gv.base, gv.pitch, gv.channels, gr, part);
+    launch_check("bias_partial_kernel");
     bias_fold_kernel<<<(gv.channels + 127) / 128, 128, 0, stream>>>(part, batch, gv.channels, db);
+    launch_check("bias_fold_kernel");
 }
 
 }  // namespace sy

@@ -254,17 +254,21 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// Shared-memory matrix descriptor for a 128B-swizzled canonical layout (sm_100 version bits).
-//   K-major: rows of 128 B (32 fp32 along K), 8-row groups 1024 B apart (SBO); LBO unused.
-//   MN-major: 128 B along MN per K row, K rows 128 B apart, 8-row K groups at SBO,
-//             successive 128 B MN blocks at LBO.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// Shared-memory matrix descriptors (sm_100 version bits).
+//   K-major, SWIZZLE_128B (layout type 2): rows of 128 B (32 fp32 along K), 16 B chunks XOR-ed
+//     with (row % 8), 8-row groups 1024 B apart (SBO); LBO unused.  Matches TMA SWIZZLE_128B.
+//   MN-major fp32/tf32, SWIZZLE_128B_BASE32B (layout type 1): the only MN-major layout tf32
+//     accepts.  Each K row holds 128 B (32 elements) along MN, 32 B chunks XOR-ed with (row % 4),
+//     4-row K groups SBO apart, successive 128 B MN blocks LBO apart.  Matches TMA
+//     SWIZZLE_128B_ATOM_32B.
+constexpr uint32_t kLayoutSw128 = 2, kLayoutSw128Base32 = 1;
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout) {
     uint64_t d = 0;
     d |= (uint64_t)((addr >> 4) & 0x3FFFu);
     d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
     d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
     d |= (uint64_t)1 << 46;  // descriptor version for sm_100
-    d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+    d |= (uint64_t)layout << 61;
     return d;
 }
 

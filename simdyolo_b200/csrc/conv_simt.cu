@@ -6,6 +6,8 @@
 // upsample2_padded is nn.Upsample(scale 2, nearest) written into a concat slice.
 #include <algorithm>
 #include <stdexcept>
+#include <string>
+#include <stdexcept>
 
 #include "kernels.h"
 
@@ -229,6 +231,11 @@ int blocks_for(long n) { return (int)std::min<long>(65535L * 16, std::max<long>(
 
 }  // namespace
 
+void launch_check(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
 void conv_simt_forward(const View& in, const Grid& gin, const float* w_ohwi, int oc, int k, int stride,
                        const View& out, const Grid& gout, int batch, const ConvEpilogue& ep, cudaStream_t stream) {
     SimtParams p;
@@ -252,41 +259,49 @@ void conv_simt_forward(const View& in, const Grid& gin, const float* w_ohwi, int
     p.res_pitch = ep.res_pitch;
     dim3 grid((unsigned)((p.m_total + BM - 1) / BM), (unsigned)((oc + BN - 1) / BN));
     conv_simt_kernel<<<grid, 256, 0, stream>>>(p);
+    launch_check("conv_simt_kernel");
 }
 
 void nchw_to_padded(const float* src, int batch, int c, const Grid& g, const View& dst, cudaStream_t stream) {
     long n = (long)batch * c * g.h * g.w;
     nchw_to_padded_kernel<<<blocks_for(n), 256, 0, stream>>>(src, batch, c, g, dst.base, dst.pitch);
+    launch_check("nchw_to_padded_kernel");
 }
 
 void padded_to_nchw(const View& src, int batch, int c, const Grid& g, float* dst, cudaStream_t stream) {
     long n = (long)batch * c * g.h * g.w;
     padded_to_nchw_kernel<<<blocks_for(n), 256, 0, stream>>>(src.base, src.pitch, batch, c, g, dst);
+    launch_check("padded_to_nchw_kernel");
 }
 
 void rgb_to_padded(const uint8_t* rgb, int batch, int size, const Grid& g, const View& dst, cudaStream_t stream) {
     long n = (long)batch * size * size;
     rgb_to_padded_kernel<<<blocks_for(n), 256, 0, stream>>>(rgb, batch, size, g, dst.base, dst.pitch);
+    launch_check("rgb_to_padded_kernel");
 }
 
 void weights_fwd_layout(const float* oihw, int oc, int ic, int taps, int kpad, float* dst, cudaStream_t stream) {
     long n = (long)oc * taps * kpad;
     weights_fwd_kernel<<<blocks_for(n), 256, 0, stream>>>(oihw, oc, ic, taps, kpad, dst);
+    launch_check("weights_fwd_kernel");
 }
 
 void weights_dgrad_layout(const float* oihw, int oc, int ic, int taps, int kpad_o, float* dst, cudaStream_t stream) {
     long n = (long)ic * taps * kpad_o;
     weights_dgrad_kernel<<<blocks_for(n), 256, 0, stream>>>(oihw, oc, ic, taps, kpad_o, dst);
+    launch_check("weights_dgrad_kernel");
 }
 
 void weights_ohwi(const float* oihw, int oc, int ic, int taps, float* dst, cudaStream_t stream) {
     long n = (long)oc * taps * ic;
     weights_ohwi_kernel<<<blocks_for(n), 256, 0, stream>>>(oihw, oc, ic, taps, dst);
+    launch_check("weights_ohwi_kernel");
 }
 
 void maxpool5_padded(const View& in, const View& out, int batch, const Grid& g, cudaStream_t stream) {
     long n = (long)batch * g.h * g.w * in.channels;
     maxpool5_kernel<<<blocks_for(n), 256, 0, stream>>>(in.base, in.pitch, out.base, out.pitch, in.channels, batch, g);
+    launch_check("maxpool5_kernel");
 }
 
 void upsample2_padded(const View& in, const Grid& gin, const View& out, const Grid& gout, int batch,
@@ -294,6 +309,7 @@ void upsample2_padded(const View& in, const Grid& gin, const View& out, const Gr
     long n = (long)batch * gout.h * gout.w * in.channels;
     upsample2_kernel<<<blocks_for(n), 256, 0, stream>>>(in.base, in.pitch, gin, out.base, out.pitch, gout,
                                                         in.channels, batch);
+    launch_check("upsample2_kernel");
 }
 
 }  // namespace sy

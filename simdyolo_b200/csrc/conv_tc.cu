@@ -39,9 +39,10 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 }
 
 // 2D fp32 tensor map: inner dimension `inner` elements (contiguous), `outer` rows `pitch_floats`
-// apart; box (box_inner, box_outer) with 128-byte swizzle; out-of-bounds elements read as zero.
+// apart; box (box_inner, box_outer); out-of-bounds elements read as zero.  K-major operands use
+// the 128-byte swizzle, MN-major (transposed) tf32 operands the 128-byte swizzle of 32-byte atoms.
 static CUtensorMap make_map_2d(const float* base, long inner, long outer, long pitch_floats, int box_inner,
-                               int box_outer) {
+                               int box_outer, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (pitch_floats * 4) % 16 != 0)
         throw std::runtime_error("tensor map base / pitch not 16-byte aligned");
     CUtensorMap map;
@@ -50,7 +51,7 @@ static CUtensorMap make_map_2d(const float* base, long inner, long outer, long p
     cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = get_encode()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
-                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
     return map;
@@ -170,8 +171,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     const uint32_t b_addr = a_addr + kABytes;
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
-                        uint64_t ad = smem_desc_sw128(a_addr + k * 32, 16, 1024);
-                        uint64_t bd = smem_desc_sw128(b_addr + k * 32, 16, 1024);
+                        uint64_t ad = smem_desc(a_addr + k * 32, 16, 1024, kLayoutSw128);
+                        uint64_t bd = smem_desc(b_addr + k * 32, 16, 1024, kLayoutSw128);
                         mma_tf32(d, ad, bd, idesc, (kb | k) != 0);
                     }
                     mma_commit(&empty[s]);
@@ -273,6 +274,7 @@ void conv_tc_forward(const View& in, const float* wk, int n_rows, int n_out, int
         const size_t smem = 1024 + (size_t)p.stages * stage_bytes + (2 * p.stages + 4) * 8 + 16;
         const int grid_x = std::min(p.num_tiles, num_sms());
         conv_fwd_tc_kernel<<<grid_x, kFwdThreads, smem, stream>>>(ta, tb, p);
+        launch_check("conv_fwd_tc_kernel");
     }
 }
 
@@ -375,8 +377,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 const uint32_t b_addr = a_addr + a_bytes;
 #pragma unroll
                 for (int k = 0; k < kWgradBK / 8; k++) {
-                    uint64_t ad = smem_desc_sw128(a_addr + k * 1024, kWgradBlockBytes, 1024);
-                    uint64_t bd = smem_desc_sw128(b_addr + k * 1024, kWgradBlockBytes, 1024);
+                    // 8 K rows = two 4-row swizzle groups of 512 B
+                    uint64_t ad = smem_desc(a_addr + k * 1024, kWgradBlockBytes, 512, kLayoutSw128Base32);
+                    uint64_t bd = smem_desc(b_addr + k * 1024, kWgradBlockBytes, 512, kLayoutSw128Base32);
                     mma_tf32(tmem_base, ad, bd, idesc, (kb | k) != 0);
                 }
                 mma_commit(&empty[s]);
@@ -467,8 +470,9 @@ void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, fl
     p.alloc_cols = pow2_at_least(p.n);
     p.ws = ws;
     p.err = err;
-    CUtensorMap tx = make_map_2d(x.base, x.channels, x.rows, x.pitch, 32, kWgradBK);
-    CUtensorMap tg = make_map_2d(dy.base, dy.channels, dy.rows, dy.pitch, 32, kWgradBK);
+    CUtensorMap tx = make_map_2d(x.base, x.channels, x.rows, x.pitch, 32, kWgradBK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    CUtensorMap tg = make_map_2d(dy.base, dy.channels, dy.rows, dy.pitch, 32, kWgradBK,
+                                 CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     static bool attr_set = false;
     if (!attr_set) {
         cudaFuncSetAttribute(conv_wgrad_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -476,10 +480,12 @@ void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, fl
     }
     const size_t smem = 1024 + (size_t)p.stages * stage_bytes + (2 * p.stages + 2) * 8 + 16;
     conv_wgrad_tc_kernel<<<dim3(p.m_tiles, splits), kFwdThreads, smem, stream>>>(tx, tg, p);
+    launch_check("conv_wgrad_tc_kernel");
     const long split_stride = (long)p.m_tiles * kTileM * p.n;
     const long total = (long)dy.channels * x.channels * taps;
     const int blocks = (int)std::min<long>(4096, (total + 255) / 256);
     wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, splits, split_stride, p.n, x.channels, taps, p.kchunks, dw);
+    launch_check("wgrad_reduce_kernel");
 }
 
 }  // namespace sy

@@ -9,6 +9,9 @@
 
 namespace sy {
 
+// Raises when the most recent kernel launch on this thread failed (bad configuration, etc.).
+void launch_check(const char* what);
+
 // ---------------------------------------------------------------- tensor views
 // A channels-last activation view: `base` points at channel 0 of the view in row 0,
 // `pitch` floats between consecutive rows, `channels` channels visible, `rows` total rows.

@@ -11,6 +11,8 @@
 // Kernels per step:  decode (image x anchor) -> topk (gt x image) -> assign (image) ->
 //                    bce (anchor rows) -> box (positives) -> finalize (image).
 #include <algorithm>
+#include <stdexcept>
+#include <string>
 
 #include "kernels.h"
 
@@ -602,8 +604,11 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
 
     const long total = (long)batch * p.anchors;
     decode_kernel<<<(int)std::min<long>(148L * 32, (total + 255) / 256), 256, 0, stream>>>(p);
+    launch_check("decode_kernel");
     if (max_boxes > 0) topk_kernel<<<dim3(max_boxes, batch), 256, 0, stream>>>(p);
+    launch_check("topk_kernel");
     assign_kernel<<<batch, 256, 0, stream>>>(p);
+    launch_check("assign_kernel");
     if (backward)
         for (int l = 0; l < nlevels; l++) {
             const LevelIO& L = levels[l];
@@ -611,8 +616,11 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
             cudaMemsetAsync(L.dbox, 0, (size_t)batch * L.grid.rows * L.box_pitch * sizeof(float), stream);
         }
     bce_kernel<<<dim3(kBceBlocks, batch), 256, 0, stream>>>(p, p.out.assigned, p.out.scores);
+    launch_check("bce_kernel");
     box_kernel<<<dim3((max_boxes * topk + 7) / 8 > 0 ? (max_boxes * topk + 7) / 8 : 1, batch), 256, 0, stream>>>(p);
+    launch_check("box_kernel");
     finalize_kernel<<<batch, 32, 0, stream>>>(p);
+    launch_check("finalize_kernel");
 }
 
 }  // namespace sy

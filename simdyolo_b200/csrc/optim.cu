@@ -7,6 +7,8 @@
 // results reported (:40).  AdamW follows torch.optim.AdamW (decoupled decay, bias correction);
 // the reference has no AdamW.  Gradients are cleared after the update.
 #include <algorithm>
+#include <stdexcept>
+#include <string>
 
 #include "kernels.h"
 
@@ -93,6 +95,7 @@ __global__ void abs_sum_kernel(const float* v, long n, double* part) {
 
 void abs_sum_partials(const float* v, long n, double* part, cudaStream_t stream) {
     abs_sum_kernel<<<kAbsSumBlocks, 256, 0, stream>>>(v, n, part);
+    launch_check("abs_sum_kernel");
 }
 
 void optimizer_step(int optimizer, float* params, float* vel, float* vel2, float* grad, const ParamSegment* segs,
@@ -117,11 +120,13 @@ void optimizer_step(int optimizer, float* params, float* vel, float* vel2, float
     p.inv_images = inv_images;
     p.nonfinite = nonfinite;
     optimizer_kernel<<<dim3(16, nsegs), 256, 0, stream>>>(p);
+    launch_check("optimizer_kernel");
 }
 
 void check_finite(const float* v, long n, int* flag, cudaStream_t stream) {
     int blocks = (int)std::min<long>(148L * 8, std::max<long>(1, (n + 255) / 256));
     finite_kernel<<<blocks, 256, 0, stream>>>(v, n, flag);
+    launch_check("finite_kernel");
 }
 
 }  // namespace sy

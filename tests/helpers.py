@@ -64,7 +64,8 @@ def oracle_head_step(cfg: sy.Config, tensors, params, buffers, velocity, feature
         out = O.Loss()
         conn = np.zeros(1, np.int32)
         tb = O.boxes(truth[b])
-        rc = L.syo_head_image(C.byref(d), params, buffers, fp, tb, len(truth[b]), grad, C.byref(out), 1, conn)
+        rc = L.syo_head_image(C.byref(d), params, buffers, fp, tb, len(truth[b]), grad, C.byref(out), 1,
+                              conn.ctypes.data_as(C.POINTER(C.c_int32)))
         assert rc == 0
         losses.append(dict(box=out.box, cls=out.cls, dfl=out.dfl, positives=out.positives))
         connected_any |= bool(conn[0])

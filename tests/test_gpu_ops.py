@@ -83,7 +83,10 @@ def test_matmul_seam(m, n, k):
     a = np.sin(np.arange(m * k, dtype=np.float32) * np.float32(.13)).reshape(m, k).astype(np.float32)
     b = np.cos(np.arange(k * n, dtype=np.float32) * np.float32(.17)).reshape(k, n).astype(np.float32)
     c = sy.matmul(a, b)
-    assert rel_l2(c, a.astype(np.float64) @ b.astype(np.float64)) < TF32_TOL
+    ref = a.astype(np.float64) @ b.astype(np.float64)
+    # TF32 keeps 10 mantissa bits of each operand: |error| <= 2^-9 * sum_k |a_ik b_kj| (+ fp32 accumulation)
+    bound = 2.0 ** -9 * (np.abs(a).astype(np.float64) @ np.abs(b).astype(np.float64)) + 1e-6
+    assert np.all(np.abs(c - ref) <= bound)
 
 
 def test_sgd_known_answer_on_gpu():
@@ -148,8 +151,10 @@ def test_assigner_and_loss_match_oracle(seed, size, nc, nboxes):
         assert np.array_equal(assigned[b], oa), f"image {b}: assignment differs"
         assert np.array_equal(scores[b], os_), f"image {b}: target scores differ"
         assert pos[b] == ol["positives"]
+        # the reference (and the oracle) accumulate the 672k BCE terms in float, the GPU in double:
+        # float summation alone moves the sum by ~1e-5 relative
         for got, want in zip(loss[b], (ol["box"], ol["cls"], ol["dfl"])):
-            assert abs(got - want) <= 1e-5 * max(1.0, abs(want))
+            assert abs(got - want) <= 1e-4 * max(1.0, abs(want))
         for l in range(3):
             assert rel_l2(dc[l][b], odc[l]) < 1e-5
             if ol["positives"]:
