@@ -133,6 +133,10 @@ SY_API sy_status sy_cuda_step(sy_session *session, const uint8_t *rgb, const sy_
  * [images][C_l][S/8/2^l][S/8/2^l]. */
 SY_API sy_status sy_cuda_step_features(sy_session *session, const float *const features[3], const sy_box *boxes,
                                 const int32_t *counts, int32_t images, sy_step_stats *out);
+/* Same step with the RGB24 images already in device memory of the session's GPU (rgb_device:
+ * images * S * S * 3 bytes, caller-owned). */
+SY_API sy_status sy_cuda_step_device(sy_session *session, const uint8_t *rgb_device, const sy_box *boxes,
+                                     const int32_t *counts, int32_t images, sy_step_stats *out);
 /* Gradient of the last step (summed over images, before the update), parameter order. */
 SY_API sy_status sy_cuda_get_last_gradients(const sy_session *session, float *host, int64_t count);
 /* Frozen features of the last step (NCHW per level), for parity checks. */
@@ -162,6 +166,15 @@ SY_API sy_status sy_cuda_conv2d_backward_filter(int32_t device, const float *x, 
 
 /* IComputeBackend.MatMul (Compute.cs:11-25): C[m,n] = A[m,k] * B[k,n], row-major, C overwritten. */
 SY_API sy_status sy_cuda_matmul(int32_t device, const float *a, const float *b, float *c, int32_t m, int32_t n, int32_t k);
+
+/* Measurement helpers (no counterpart in the reference, which times with Stopwatch).
+ * sy_cuda_launch_count: kernels this library has launched in the process so far.
+ * sy_cuda_bench_conv: device time in ms per launch (CUDA events, `iters` back-to-back launches after
+ * one warm-up) of one convolution pass on device-resident data: kind 0 forward, 1 data gradient,
+ * 2 weight gradient; shapes as in sy_cuda_conv2d_*. */
+SY_API int64_t sy_cuda_launch_count(void);
+SY_API sy_status sy_cuda_bench_conv(int32_t device, int32_t kind, int32_t n, int32_t ic, int32_t oc, int32_t h,
+                                    int32_t w, int32_t k, int32_t iters, double *ms_per_launch);
 
 /* TrainingParameter.Update (TrainingParameter.cs:21-43) on one tensor: returns SY_ERR_NONFINITE when
  * the result is not finite.  has_grad == 0 leaves everything untouched. */

@@ -17,6 +17,11 @@
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#else
+static int omp_in_parallel(void) { return 1; }
+#endif
 #include "syo.h"
 
 /* cols[(c*k+ky)*k+kx][y*w+x] = x[c][y+ky-p][x+kx-p] or 0 (HeadOperations.cs:39-45) */
@@ -58,6 +63,8 @@ static void col2im_add(const float *cols, int ic, int h, int w, int k, float *dx
 static void matmul(const float *a, const float *b, float *c, int m, int n, int k)
 {
     memset(c, 0, sizeof(float) * (size_t)m * n);
+    /* rows are independent: split them over idle threads (each row keeps the serial k order) */
+#pragma omp parallel for schedule(static) if (!omp_in_parallel() && (long)m * n * k > (1L << 20))
     for (int i = 0; i < m; i++) {
         float *crow = c + (size_t)i * n;
         for (int p = 0; p < k; p++) {
@@ -71,6 +78,7 @@ static void matmul(const float *a, const float *b, float *c, int m, int n, int k
 /* TrainingMatMul.RightTransposed: C[m,n] = A[m,k] * B[n,k]^T (overwrite) */
 void syo_right_transposed(const float *a, const float *b, float *c, int m, int n, int k)
 {
+#pragma omp parallel for schedule(static) if (!omp_in_parallel() && (long)m * n * k > (1L << 20))
     for (int i = 0; i < m; i++)
         for (int j = 0; j < n; j++) {
             const float *ar = a + (size_t)i * k, *br = b + (size_t)j * k;

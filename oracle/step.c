@@ -315,6 +315,7 @@ static void bb_conv(bb_params *bp, const float *x, int ic, int h, int w, int oc,
                     }
                 }
             }
+#pragma omp parallel for schedule(static) if (!omp_in_parallel() && (long)oc * kk * so > (1L << 20))
     for (int o = 0; o < oc; o++) {
         float *yr = y + (size_t)o * so;
         for (int p = 0; p < so; p++) yr[p] = 0;
@@ -526,7 +527,10 @@ void syo_train_step(const syo_backbone_desc *bd, const float *backbone_params, c
     syo_backbone_feature_channels(bd, ch);
 #ifdef _OPENMP
     if (threads <= 0) threads = omp_get_max_threads();
-#pragma omp parallel for schedule(dynamic, 1) num_threads(threads)
+    /* one image per thread; a single image instead spreads its GEMM rows over the threads */
+    int team = threads < batch ? threads : batch;
+    omp_set_num_threads(threads);
+#pragma omp parallel for schedule(dynamic, 1) num_threads(team)
 #endif
     for (int b = 0; b < batch; b++) {
         float *feat[3];

@@ -128,8 +128,11 @@ def lib():
         L.sy_cuda_matmul.argtypes = [C.c_int32, fp, fp, fp, C.c_int32, C.c_int32, C.c_int32]
         L.sy_cuda_sgd_update.argtypes = [C.c_int32, fp, fp, fp, C.c_int64, C.c_float, C.c_float, C.c_float, C.c_int32,
                                          C.c_int32]
-        for name in dir(L):
-            pass
+        L.sy_cuda_step_device.argtypes = [vp, C.c_void_p, C.POINTER(Box), ip, C.c_int32, C.POINTER(StepStats)]
+        L.sy_cuda_launch_count.argtypes = []
+        L.sy_cuda_launch_count.restype = C.c_int64
+        L.sy_cuda_bench_conv.argtypes = [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                         C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_double)]
         _lib = L
     return _lib
 
@@ -139,7 +142,8 @@ EXPORTED = ["sy_cuda_nccl_unique_id", "sy_cuda_create", "sy_cuda_destroy", "sy_c
             "sy_cuda_set_optimizer_state", "sy_cuda_get_optimizer_state", "sy_cuda_backbone_param_count",
             "sy_cuda_set_backbone", "sy_cuda_step", "sy_cuda_step_features", "sy_cuda_get_last_gradients",
             "sy_cuda_get_last_features", "sy_cuda_detection_loss", "sy_cuda_conv2d_forward",
-            "sy_cuda_conv2d_backward_data", "sy_cuda_conv2d_backward_filter", "sy_cuda_matmul", "sy_cuda_sgd_update"]
+            "sy_cuda_conv2d_backward_data", "sy_cuda_conv2d_backward_filter", "sy_cuda_matmul", "sy_cuda_sgd_update",
+            "sy_cuda_step_device", "sy_cuda_launch_count", "sy_cuda_bench_conv"]
 
 
 def _check(status: int, session=None):
@@ -365,6 +369,14 @@ class Session:
                                   C.byref(stats)), self._h)
         return stats
 
+    def step_device(self, images_device_ptr: int, batch: int, boxes_per_image) -> StepStats:
+        """Step with the uint8 [B, S, S, 3] images already in this GPU's memory (device pointer)."""
+        arr, counts = self._boxes(boxes_per_image)
+        stats = StepStats()
+        _check(lib().sy_cuda_step_device(self._h, C.c_void_p(images_device_ptr), arr, _ip(counts), batch,
+                                         C.byref(stats)), self._h)
+        return stats
+
     def step_features(self, features, boxes_per_image) -> StepStats:
         feats = [np.ascontiguousarray(f, np.float32) for f in features]
         arr, counts = self._boxes(boxes_per_image)
@@ -384,6 +396,18 @@ class Session:
         out = np.zeros(int(np.prod(shape)), np.float32)
         _check(lib().sy_cuda_get_last_features(self._h, level, _fp(out), out.size), self._h)
         return out.reshape(shape)
+
+
+def launch_count() -> int:
+    """Kernels launched by the CUDA library in this process so far."""
+    return int(lib().sy_cuda_launch_count())
+
+
+def bench_conv(kind: int, n: int, ic: int, oc: int, h: int, w: int, k: int, iters: int = 10, device: int = 0) -> float:
+    """Device ms per launch of one conv pass (0 forward, 1 data gradient, 2 weight gradient)."""
+    ms = C.c_double()
+    _check(lib().sy_cuda_bench_conv(device, kind, n, ic, oc, h, w, k, iters, C.byref(ms)))
+    return ms.value
 
 
 def nccl_unique_id() -> bytes:

@@ -78,6 +78,12 @@ sy::View padded(Scratch& s, int n, int c, const sy::Grid& g) {
     return sy::View{s.get<float>((size_t)rows * pitch), pitch, c, rows};
 }
 
+void conv_shape_check(int n, int ic, int oc, int h, int w, int k) {
+    if (n < 1 || ic < 1 || oc < 1 || h < 1 || w < 1 || !(k == 1 || k == 3))
+        throw sy::SyError(SY_ERR_UNSUPPORTED_SHAPE, "conv: batch, channels and size must be positive, k in {1,3}");
+    if (ic > 4096 || oc > 4096) throw sy::SyError(SY_ERR_UNSUPPORTED_SHAPE, "conv: too many channels");
+}
+
 void check_device(int device) {
     int count = 0;
     if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count)
@@ -168,13 +174,77 @@ sy_status sy_cuda_set_backbone(sy_session* session, const float* host, int64_t c
 sy_status sy_cuda_step(sy_session* session, const uint8_t* rgb, const sy_box* boxes, const int32_t* counts,
                        int32_t images, sy_step_stats* out) {
     if (!session || !rgb) return SY_ERR_INVALID_ARGUMENT;
-    return guarded(session, [&] { return session->impl->step(rgb, nullptr, boxes, counts, images, out); });
+    return guarded(session, [&] { return session->impl->step(rgb, false, nullptr, boxes, counts, images, out); });
+}
+
+sy_status sy_cuda_step_device(sy_session* session, const uint8_t* rgb_device, const sy_box* boxes,
+                              const int32_t* counts, int32_t images, sy_step_stats* out) {
+    if (!session || !rgb_device) return SY_ERR_INVALID_ARGUMENT;
+    return guarded(session,
+                   [&] { return session->impl->step(rgb_device, true, nullptr, boxes, counts, images, out); });
 }
 
 sy_status sy_cuda_step_features(sy_session* session, const float* const features[3], const sy_box* boxes,
                                 const int32_t* counts, int32_t images, sy_step_stats* out) {
     if (!session || !features) return SY_ERR_INVALID_ARGUMENT;
-    return guarded(session, [&] { return session->impl->step(nullptr, features, boxes, counts, images, out); });
+    return guarded(session,
+                   [&] { return session->impl->step(nullptr, false, features, boxes, counts, images, out); });
+}
+
+int64_t sy_cuda_launch_count(void) { return sy::launch_count(); }
+
+sy_status sy_cuda_bench_conv(int32_t device, int32_t kind, int32_t n, int32_t ic, int32_t oc, int32_t h, int32_t w,
+                             int32_t k, int32_t iters, double* ms_per_launch) {
+    return guarded(nullptr, [&] {
+        if (!ms_per_launch || kind < 0 || kind > 2 || iters < 1)
+            throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "bench_conv: bad arguments");
+        conv_shape_check(n, ic, oc, h, w, k);
+        check_device(device);
+        Scratch s;
+        const sy::Grid g = sy::make_grid(h, w);
+        const int taps = k * k;
+        sy::View vx = padded(s, n, ic, g), vy = padded(s, n, oc, g);
+        // deterministic non-trivial data (values do not matter for timing)
+        {
+            std::vector<float> hx((size_t)vx.rows * vx.pitch), hy((size_t)vy.rows * vy.pitch);
+            for (size_t i = 0; i < hx.size(); i++) hx[i] = (float)((i * 2654435761u) % 1000) * 1e-3f - .5f;
+            for (size_t i = 0; i < hy.size(); i++) hy[i] = (float)((i * 40503u) % 1000) * 1e-3f - .5f;
+            CK(cudaMemcpy(vx.base, hx.data(), hx.size() * 4, cudaMemcpyHostToDevice));
+            CK(cudaMemcpy(vy.base, hy.data(), hy.size() * 4, cudaMemcpyHostToDevice));
+        }
+        const int kpad_i = (ic + 31) / 32 * 32, kpad_o = (oc + 31) / 32 * 32;
+        float* wfwd = s.get<float>((size_t)oc * taps * kpad_i);
+        float* wdg = s.get<float>((size_t)ic * taps * kpad_o);
+        float* dw = s.get<float>((size_t)oc * ic * taps);
+        float* wsp = s.get<float>(sy::wgrad_workspace_floats(ic, oc, taps, vx.rows));
+        int* err = s.get<int>(1);
+        cudaStream_t st;
+        CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+        cudaEvent_t e0, e1;
+        CK(cudaEventCreate(&e0));
+        CK(cudaEventCreate(&e1));
+        auto run = [&] {
+            sy::ConvEpilogue ep;
+            if (kind == 0) sy::conv_tc_forward(vx, wfwd, oc, oc, taps, 1, g, vy, ep, err, st);
+            else if (kind == 1) sy::conv_tc_forward(vy, wdg, ic, ic, taps, -1, g, vx, ep, err, st);
+            else sy::conv_tc_wgrad(vx, vy, taps, g, dw, wsp, err, st);
+        };
+        run();
+        CK(cudaEventRecord(e0, st));
+        for (int i = 0; i < iters; i++) run();
+        CK(cudaEventRecord(e1, st));
+        CK(cudaEventSynchronize(e1));
+        float ms = 0.f;
+        CK(cudaEventElapsedTime(&ms, e0, e1));
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        cudaStreamDestroy(st);
+        int e = 0;
+        CK(cudaMemcpy(&e, err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (e) throw sy::SyError(SY_ERR_DEVICE, "conv kernel wait limit exceeded");
+        *ms_per_launch = ms / iters;
+        return SY_OK;
+    });
 }
 
 sy_status sy_cuda_get_last_gradients(const sy_session* session, float* host, int64_t count) {
@@ -273,11 +343,6 @@ sy_status sy_cuda_detection_loss(int32_t device, int32_t images, int32_t levels,
     });
 }
 
-static void conv_shape_check(int n, int ic, int oc, int h, int w, int k) {
-    if (n < 1 || ic < 1 || oc < 1 || h < 1 || w < 1 || !(k == 1 || k == 3))
-        throw sy::SyError(SY_ERR_UNSUPPORTED_SHAPE, "conv: batch, channels and size must be positive, k in {1,3}");
-    if (ic > 4096 || oc > 4096) throw sy::SyError(SY_ERR_UNSUPPORTED_SHAPE, "conv: too many channels");
-}
 
 sy_status sy_cuda_conv2d_forward(int32_t device, const float* x, int32_t n, int32_t ic, int32_t h, int32_t w,
                                  const float* weight, int32_t oc, int32_t k, const float* bias, float* y) {

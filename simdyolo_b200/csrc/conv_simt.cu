@@ -5,9 +5,9 @@
 // run on the tcgen05 kernels in conv_tc.cu.  maxpool5_padded is SPPF's MaxPool2d(5, 1, 2);
 // upsample2_padded is nn.Upsample(scale 2, nearest) written into a concat slice.
 #include <algorithm>
+#include <atomic>
 #include <stdexcept>
 #include <string>
-#include <stdexcept>
 
 #include "kernels.h"
 
@@ -231,10 +231,15 @@ int blocks_for(long n) { return (int)std::min<long>(65535L * 16, std::max<long>(
 
 }  // namespace
 
+static std::atomic<long long> g_launches{0};
+
 void launch_check(const char* what) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
+
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
 void conv_simt_forward(const View& in, const Grid& gin, const float* w_ohwi, int oc, int k, int stride,
                        const View& out, const Grid& gout, int batch, const ConvEpilogue& ep, cudaStream_t stream) {

@@ -10,7 +10,9 @@
 namespace sy {
 
 // Raises when the most recent kernel launch on this thread failed (bad configuration, etc.).
+// Every launch site calls it once, so it also counts this library's kernel launches.
 void launch_check(const char* what);
+long long launch_count();
 
 // ---------------------------------------------------------------- tensor views
 // A channels-last activation view: `base` points at channel 0 of the view in row 0,

@@ -527,8 +527,8 @@ void Session::backward_head(int batch) {
 }
 
 // ------------------------------------------------------------------ step
-int Session::step(const uint8_t* rgb, const float* const* features, const sy_box* boxes, const int32_t* counts,
-                  int images, sy_step_stats* out) {
+int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
+                  const int32_t* counts, int images, sy_step_stats* out) {
     if (images < 1 || images > B_) throw SyError(SY_ERR_INVALID_ARGUMENT, "images out of range");
     if (!counts || (!boxes && images > 0)) throw SyError(SY_ERR_INVALID_ARGUMENT, "counts / boxes missing");
     SY_CUDA(cudaSetDevice(device_));
@@ -556,9 +556,21 @@ int Session::step(const uint8_t* rgb, const float* const* features, const sy_box
     SY_CUDA(cudaMemsetAsync(d_flags_, 0, sizeof(int) * 16, stream_));
     if (rgb) {
         const size_t bytes = (size_t)images * cfg.image_size * cfg.image_size * 3;
-        std::memcpy(h_rgb_, rgb, bytes);
-        SY_CUDA(cudaMemcpyAsync(d_rgb_, h_rgb_, bytes, cudaMemcpyHostToDevice, stream_));
-        rgb_to_padded(d_rgb_, images, cfg.image_size, img_grid_, img_, stream_);
+        const uint8_t* src = d_rgb_;
+        if (rgb_on_device) {
+            src = rgb;
+        } else {
+            // pinned caller memory is copied directly; pageable memory goes through pinned staging
+            cudaPointerAttributes attr;
+            const bool pinned = cudaPointerGetAttributes(&attr, rgb) == cudaSuccess && attr.type == cudaMemoryTypeHost;
+            cudaGetLastError();
+            if (!pinned) {
+                std::memcpy(h_rgb_, rgb, bytes);
+                rgb = h_rgb_;
+            }
+            SY_CUDA(cudaMemcpyAsync(d_rgb_, rgb, bytes, cudaMemcpyHostToDevice, stream_));
+        }
+        rgb_to_padded(src, images, cfg.image_size, img_grid_, img_, stream_);
         forward_backbone(images);
     } else {
         if (!features) throw SyError(SY_ERR_INVALID_ARGUMENT, "features missing");
@@ -672,8 +684,8 @@ int Session::step(const uint8_t* rgb, const float* const* features, const sy_box
                    cfg.momentum, cfg.weight_decay, cfg.beta1, cfg.beta2, cfg.adam_eps, 1.0f / (float)global_images,
                    d_flags_ + 1, stream_);
     refresh_head_weights();
-    SY_CUDA(cudaEventRecord(ev1_, stream_));
     SY_CUDA(cudaMemcpyAsync(h_flags_, d_flags_, sizeof(int) * 2, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaEventRecord(ev1_, stream_));
     SY_CUDA(cudaStreamSynchronize(stream_));
     last_batch_ = images;
     if (out) {

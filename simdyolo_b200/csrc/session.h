@@ -68,8 +68,9 @@ public:
     std::string error;
 
     // public operations (return sy_status)
-    int step(const uint8_t* rgb, const float* const* features, const sy_box* boxes, const int32_t* counts,
-             int images, sy_step_stats* out);
+    // rgb: host (or, with rgb_on_device, device) images; features: host NCHW features instead.
+    int step(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
+             const int32_t* counts, int images, sy_step_stats* out);
     int set_tensor(int index, const float* host, long count);
     int get_tensor(int index, float* host, long count) const;
     int set_opt_state(int index, int moment, const float* host, long count);

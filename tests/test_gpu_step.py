@@ -111,14 +111,18 @@ def test_full_step_backbone_and_head_match_oracle():
         O.lib().syo_backbone_forward(C.byref(bd), bparams, images[b].ctypes.data_as(C.POINTER(C.c_uint8)), *f)
         for l in range(3):
             feats[l][b] = f[l]
+    gpu_feats = []
     for l in range(3):
         got = s.last_features(l, feats[l].shape)
         assert rel_l2(got, feats[l]) < TOL, f"level {l}"
+        gpu_feats.append(got)
+    # head parity on the GPU's own frozen features (TF32 feature differences could move a top-10
+    # boundary of the assigner; the assigner itself is checked bit-exact in test_gpu_ops)
     losses, ograd, oparams, obuffers, ovel, conn = oracle_head_step(cfg, s.tensors, params, buffers,
-                                                                    np.zeros_like(params), feats, truth)
+                                                                    np.zeros_like(params), gpu_feats, truth)
     assert abs(stats.cls - sum(l["cls"] for l in losses)) <= TOL * abs(sum(l["cls"] for l in losses))
-    assert rel_l2(s.last_gradients(), ograd) < 5 * TOL
-    assert rel_l2(s.flat_params() - params, oparams - params) < 5 * TOL
+    assert rel_l2(s.last_gradients(), ograd) < TOL
+    assert rel_l2(s.flat_params() - params, oparams - params) < TOL
 
 
 def test_oracle_full_step_matches_session_loss_over_steps():
