@@ -164,6 +164,21 @@ SY_API sy_status sy_cuda_conv2d_backward_data(int32_t device, const float *dy, i
 SY_API sy_status sy_cuda_conv2d_backward_filter(int32_t device, const float *x, const float *dy, int32_t n, int32_t ic,
                                          int32_t oc, int32_t h, int32_t w, int32_t k, float *dw);
 
+/* Allocation-free weight gradient: no counterpart in the reference.  For callers that cannot call
+ * cudaMalloc (inside a CUDA graph capture, under an external memory pool or an embedding runtime
+ * that owns all device memory): same result as sy_cuda_conv2d_backward_filter, but every buffer is
+ * caller-owned device memory and the split-K scratch is a fixed 16 MiB static device array per GPU
+ * (shapes needing more return SY_ERR_UNSUPPORTED_SHAPE).  x / dy use the library's padded
+ * channels-last layout: image b, pixel (y, x) at row b * R + (y + 1) * (w + 2) + (x + 1) with
+ * R = round_up((h + 2) * (w + 2), 128), rows of round_up(C, 4) floats, halo rows zero.  dw is OIHW.
+ * The first call on a device looks up the static array's device address: make it before any stream
+ * capture.  Calls share the array, so calls that overlap on the GPU race; the call returns after
+ * `stream` (NULL = legacy default stream) has finished it. */
+SY_API sy_status sy_cuda_conv2d_backward_filter_static(int32_t device, const float *x_padded_device,
+                                                       const float *dy_padded_device, int32_t n, int32_t ic,
+                                                       int32_t oc, int32_t h, int32_t w, int32_t k, float *dw_device,
+                                                       void *stream);
+
 /* IComputeBackend.MatMul (Compute.cs:11-25): C[m,n] = A[m,k] * B[k,n], row-major, C overwritten. */
 SY_API sy_status sy_cuda_matmul(int32_t device, const float *a, const float *b, float *c, int32_t m, int32_t n, int32_t k);
 

@@ -128,6 +128,9 @@ def lib():
         L.sy_cuda_matmul.argtypes = [C.c_int32, fp, fp, fp, C.c_int32, C.c_int32, C.c_int32]
         L.sy_cuda_sgd_update.argtypes = [C.c_int32, fp, fp, fp, C.c_int64, C.c_float, C.c_float, C.c_float, C.c_int32,
                                          C.c_int32]
+        L.sy_cuda_conv2d_backward_filter_static.argtypes = [C.c_int32, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32,
+                                                            C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                                            C.c_void_p]
         L.sy_cuda_step_device.argtypes = [vp, C.c_void_p, C.POINTER(Box), ip, C.c_int32, C.POINTER(StepStats)]
         L.sy_cuda_launch_count.argtypes = []
         L.sy_cuda_launch_count.restype = C.c_int64
@@ -143,7 +146,8 @@ EXPORTED = ["sy_cuda_nccl_unique_id", "sy_cuda_create", "sy_cuda_destroy", "sy_c
             "sy_cuda_set_backbone", "sy_cuda_step", "sy_cuda_step_features", "sy_cuda_get_last_gradients",
             "sy_cuda_get_last_features", "sy_cuda_detection_loss", "sy_cuda_conv2d_forward",
             "sy_cuda_conv2d_backward_data", "sy_cuda_conv2d_backward_filter", "sy_cuda_matmul", "sy_cuda_sgd_update",
-            "sy_cuda_step_device", "sy_cuda_launch_count", "sy_cuda_bench_conv"]
+            "sy_cuda_step_device", "sy_cuda_launch_count", "sy_cuda_bench_conv",
+            "sy_cuda_conv2d_backward_filter_static"]
 
 
 def _check(status: int, session=None):
@@ -474,6 +478,22 @@ def conv2d_backward_filter(x, dy, k, device=0):
     dw = np.zeros((oc, ic, k, k), np.float32)
     _check(lib().sy_cuda_conv2d_backward_filter(device, _fp(x), _fp(dy), n, ic, oc, h, wd, k, _fp(dw)))
     return dw
+
+
+def padded_rows(h: int, w: int) -> int:
+    """Rows per image of the library's padded channels-last layout (one-pixel zero halo, 128-row tiles)."""
+    return ((h + 2) * (w + 2) + 127) // 128 * 128
+
+
+def conv2d_backward_filter_static(x_padded_ptr: int, dy_padded_ptr: int, n: int, ic: int, oc: int, h: int, w: int,
+                                  k: int, dw_ptr: int, stream_ptr: int = 0, device: int = 0):
+    """Weight gradient for callers that cannot allocate: device pointers only, scratch in a static
+    device array (see include/simdyolo_cuda.h)."""
+    status = lib().sy_cuda_conv2d_backward_filter_static(device, C.c_void_p(x_padded_ptr), C.c_void_p(dy_padded_ptr),
+                                                         n, ic, oc, h, w, k, C.c_void_p(dw_ptr),
+                                                         C.c_void_p(stream_ptr) if stream_ptr else None)
+    if status != SY_OK:
+        _raise(status, "conv2d_backward_filter_static failed")
 
 
 def matmul(a, b, device=0):
