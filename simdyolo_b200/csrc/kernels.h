@@ -69,8 +69,10 @@ void upsample2_padded(const View& in, const Grid& gin, const View& out, const Gr
                       cudaStream_t stream);
 
 // ---------------------------------------------------------------- BatchNorm (training, per image)
+// Scratch (floats) the reductions below need for `channels` channels of `batch` images.
+size_t bn_workspace_floats(int batch, int channels);
 // stats[(b * c + ch) * 2 + {0,1}] = (mean, biased variance) of image b over the interior pixels.
-void bn_stats(const View& y, int batch, const Grid& g, float* stats, cudaStream_t stream);
+void bn_stats(const View& y, int batch, const Grid& g, float* stats, float* ws, cudaStream_t stream);
 // a = SiLU(gamma * (y - mean) * inv + beta) at interior rows, 0 elsewhere; xhat not stored.
 void bn_silu_apply(const View& y, const float* stats, const float* gamma, const float* beta, float eps, int batch,
                    const Grid& g, const View& a, cudaStream_t stream);
@@ -79,14 +81,14 @@ void bn_silu_apply(const View& y, const float* stats, const float* gamma, const 
 // accumulated over images in image order.
 void bn_silu_backward(const View& y, const View& g, const float* stats, const float* gamma, const float* beta,
                       float eps, int batch, const Grid& gr, float* red, const View& dy, float* dgamma, float* dbeta,
-                      cudaStream_t stream);
+                      float* ws, cudaStream_t stream);
 // Running statistics: for each BN channel, r <- (1-m) r + m * s_i for images i in order, over
 // `ranks` blocks of `batch` images each `rank_stride` floats apart (all-gathered ranks).
 void bn_running_update(const float* stats, long rank_stride, int ranks, int batch, int c, int spatial, float momentum,
                        float* rmean, float* rvar, float* tracked, cudaStream_t stream);
 // Bias gradient of the final conv: db[n] += sum over images and interior pixels of g[m, n].
-// `part` is scratch of batch * channels floats.
-void bias_grad(const View& g, int batch, const Grid& gr, float* part, float* db, cudaStream_t stream);
+// `ws` is scratch of bn_workspace_floats(batch, channels) floats.
+void bias_grad(const View& g, int batch, const Grid& gr, float* ws, float* db, cudaStream_t stream);
 
 // ---------------------------------------------------------------- loss / assigner
 struct LevelIO {

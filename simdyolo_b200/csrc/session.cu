@@ -470,7 +470,7 @@ void Session::build_head() {
         for (auto& hb : branch.blocks)
             if (hb.b.has_bn) hb.stats = bn_stats_all_ + 2 * (size_t)B_ * hb.stats_off;
     wgrad_ws_ = static_cast<float*>(dalloc(sizeof(float) * ws));
-    bias_part_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)B_ * max_oc));
+    bias_part_ = static_cast<float*>(dalloc(sizeof(float) * bn_workspace_floats(B_, max_oc)));
 }
 
 void Session::refresh_head_weights() {
@@ -495,7 +495,7 @@ void Session::forward_head(int batch) {
             conv_tc_forward(rows_of(hb.x, batch, g), hb.w_fwd, hb.b.oc, hb.b.oc, hb.taps, 1, g,
                             rows_of(hb.y, batch, g), ep, d_flags_, stream_);
             if (hb.b.has_bn) {
-                bn_stats(hb.y, batch, g, hb.stats, stream_);
+                bn_stats(hb.y, batch, g, hb.stats, bias_part_, stream_);
                 bn_silu_apply(hb.y, hb.stats, params_ + hb.g_off, params_ + hb.be_off, cfg.bn_eps, batch, g, hb.a,
                               stream_);
             }
@@ -512,7 +512,7 @@ void Session::backward_head(int batch) {
                 HeadBlock& hb = branch.blocks[i];
                 if (hb.b.has_bn)
                     bn_silu_backward(hb.y, hb.g, hb.stats, params_ + hb.g_off, params_ + hb.be_off, cfg.bn_eps, batch,
-                                     g, hb.red, hb.dy, grads_ + hb.g_off, grads_ + hb.be_off, stream_);
+                                     g, hb.red, hb.dy, grads_ + hb.g_off, grads_ + hb.be_off, bias_part_, stream_);
                 if (hb.b.has_bias) bias_grad(hb.dy, batch, g, bias_part_, grads_ + hb.b_off, stream_);
                 conv_tc_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off,
                               wgrad_ws_, d_flags_, stream_);
