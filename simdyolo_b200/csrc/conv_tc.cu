@@ -86,6 +86,12 @@ struct FwdParams {
     int silu;
     int mask;
     Grid grid;
+    // optional parity-split copy of the output (input of a stride-2 consumer, see kernels.h)
+    float* phase;
+    int phase_pitch;
+    int phase_wp;        // consumer output grid: padded width
+    int phase_rows;      // consumer output grid: rows per image
+    long phase_stride;   // rows between parity planes (batch * phase_rows)
     int* err;
 };
 
@@ -190,10 +196,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             if (!mbar_wait(&tfull[acc], aph, p.err, 4)) break;
             tc_fence_after();
             const long m = (long)tile * kTileM + row;
-            const int r = (int)(m % p.grid.rows);
+            const long img = m / p.grid.rows;
+            const int r = (int)(m - img * p.grid.rows);
             const bool inside = !p.mask || p.grid.interior(r);
             float* orow = p.out + m * (long)p.out_pitch;
             const float* rrow = p.residual ? p.residual + m * (long)p.res_pitch : nullptr;
+            // parity-split copy: padded pixel (py, px) -> plane (py&1, px&1), cell (py>>1, px>>1)
+            float* prow = nullptr;
+            if (p.phase && inside) {
+                const int py = r / p.grid.wp, px = r - py * p.grid.wp;
+                const long prow_index = ((py & 1) * 2 + (px & 1)) * p.phase_stride + img * p.phase_rows +
+                                        (long)(py >> 1) * p.phase_wp + (px >> 1);
+                prow = p.phase + prow_index * p.phase_pitch;
+            }
             for (int j = 0; j < p.n; j += 16) {
                 float v[16];
                 tmem_ld16(tmem_base + acc * p.acc_cols + ((uint32_t)(q * 32) << 16) + j, v);
@@ -210,8 +225,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     float4* dst = reinterpret_cast<float4*>(orow + j);
 #pragma unroll
                     for (int i = 0; i < 4; i++) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                    if (prow) {
+                        float4* pd = reinterpret_cast<float4*>(prow + j);
+#pragma unroll
+                        for (int i = 0; i < 4; i++)
+                            pd[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                    }
                 } else {
                     for (int i = 0; i < 16 && j + i < p.n_valid; i++) orow[j + i] = v[i];
+                    if (prow)
+                        for (int i = 0; i < 16 && j + i < p.n_valid; i++) prow[j + i] = v[i];
                 }
             }
             tc_fence_before();
@@ -231,12 +254,16 @@ static int pow2_at_least(int v) {
     return r;
 }
 
-void conv_tc_forward(const View& in, const float* wk, int n_rows, int n_out, int taps, int shift_sign,
-                     const Grid& grid, const View& out, const ConvEpilogue& ep, int* err, cudaStream_t stream) {
+// Shared launcher: `m_rows` output rows (tiles of 128), A rows read at m + shift[t].
+static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, const float* wk, int n_rows, int n_out,
+                       const Grid& grid, const View& out, const ConvEpilogue& ep, const PhaseOut* phase, int* err,
+                       cudaStream_t stream) {
     const int kchunks = (in.channels + 31) / 32, kpad = kchunks * 32;
-    if (in.rows % kTileM != 0) throw std::runtime_error("conv_tc_forward: rows not a multiple of 128");
+    if (m_rows % kTileM != 0) throw std::runtime_error("conv_tc: output rows not a multiple of 128");
     if ((out.pitch % 4) != 0 || (reinterpret_cast<uintptr_t>(out.base) & 15) != 0)
-        throw std::runtime_error("conv_tc_forward: output not 16-byte aligned");
+        throw std::runtime_error("conv_tc: output not 16-byte aligned");
+    if (phase && ((phase->pitch % 4) != 0 || (reinterpret_cast<uintptr_t>(phase->base) & 15) != 0))
+        throw std::runtime_error("conv_tc: parity copy not 16-byte aligned");
     CUtensorMap ta = make_map_2d(in.base, in.channels, in.rows, in.pitch, 32, kTileM);
     static bool attr_set = false;
     if (!attr_set) {
@@ -248,13 +275,11 @@ void conv_tc_forward(const View& in, const float* wk, int n_rows, int n_out, int
         const int n = (n_valid + 15) / 16 * 16;
         CUtensorMap tb = make_map_2d(wk, (long)taps * kpad, n_rows, (long)taps * kpad, 32, n);
         FwdParams p;
-        p.num_tiles = (int)(in.rows / kTileM);
+        p.num_tiles = (int)(m_rows / kTileM);
         p.taps = taps;
         p.kchunks = kchunks;
         p.kpad = kpad;
-        for (int t = 0; t < 9; t++) p.shift[t] = 0;
-        if (taps == 9)
-            for (int t = 0; t < 9; t++) p.shift[t] = shift_sign * ((t / 3 - 1) * grid.wp + (t % 3 - 1));
+        for (int t = 0; t < 9; t++) p.shift[t] = t < taps ? shift[t] : 0;
         p.n = n;
         p.n_valid = n_valid;
         p.n0 = n0;
@@ -270,12 +295,39 @@ void conv_tc_forward(const View& in, const float* wk, int n_rows, int n_out, int
         p.silu = ep.silu;
         p.mask = ep.mask_halo;
         p.grid = grid;
+        p.phase = phase ? phase->base + n0 : nullptr;
+        p.phase_pitch = phase ? phase->pitch : 0;
+        p.phase_wp = phase ? phase->consumer.wp : 0;
+        p.phase_rows = phase ? phase->consumer.rows : 0;
+        p.phase_stride = phase ? phase->plane_rows : 0;
         p.err = err;
         const size_t smem = 1024 + (size_t)p.stages * stage_bytes + (2 * p.stages + 4) * 8 + 16;
         const int grid_x = std::min(p.num_tiles, num_sms());
         conv_fwd_tc_kernel<<<grid_x, kFwdThreads, smem, stream>>>(ta, tb, p);
         launch_check("conv_fwd_tc_kernel");
     }
+}
+
+void conv_tc_forward(const View& in, const float* wk, int n_rows, int n_out, int taps, int shift_sign,
+                     const Grid& grid, const View& out, const ConvEpilogue& ep, int* err, cudaStream_t stream,
+                     const PhaseOut* phase) {
+    int shift[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+    if (taps == 9)
+        for (int t = 0; t < 9; t++) shift[t] = shift_sign * ((t / 3 - 1) * grid.wp + (t % 3 - 1));
+    launch_fwd(in, in.rows, shift, taps, wk, n_rows, n_out, grid, out, ep, phase, err, stream);
+}
+
+void conv_tc_strided(const View& phase_in, long plane_rows, long m_rows, const float* wk, int oc, const Grid& gout,
+                     const View& out, const ConvEpilogue& ep, int* err, cudaStream_t stream, const PhaseOut* phase) {
+    // tap (ky, kx) of output pixel m reads padded input (2 oy + ky, 2 ox + kx): parity plane
+    // (ky & 1, kx & 1), cell (oy + ky / 2, ox + kx / 2) = row m + (ky / 2 - 1) wp + (kx / 2 - 1)
+    int shift[9];
+    for (int t = 0; t < 9; t++) {
+        const int ky = t / 3, kx = t % 3;
+        shift[t] = (int)(((ky & 1) * 2 + (kx & 1)) * plane_rows + ((ky >> 1) - 1) * gout.wp + ((kx >> 1) - 1));
+    }
+    if (phase_in.rows != 4 * plane_rows) throw std::runtime_error("conv_tc_strided: parity input rows");
+    launch_fwd(phase_in, m_rows, shift, 9, wk, oc, oc, gout, out, ep, phase, err, stream);
 }
 
 // ------------------------------------------------------------------ weight-gradient kernel

@@ -38,9 +38,28 @@ struct ConvEpilogue {
     int mask_halo = 1;                // 0: every row is a valid output (plain GEMM use)
 };
 
+// Parity-split copy of a feature map, the input format of a 3x3 stride-2 conv.  Padded pixel
+// (py, px) of an H x W map (H, W even) goes to plane (py & 1) * 2 + (px & 1), cell (py / 2, px / 2),
+// laid out like the consumer's (H/2 x W/2) padded output grid: plane q, image b, cell (sy, sx) is row
+// q * plane_rows + b * consumer.rows + sy * consumer.wp + sx.  With this layout every tap of the
+// stride-2 conv is a constant row offset, so it runs on the same implicit-GEMM kernel.
+struct PhaseOut {
+    float* base = nullptr;   // plane 0, row 0, first channel of this view
+    int pitch = 0;
+    Grid consumer{};         // output grid of the stride-2 consumer
+    long plane_rows = 0;     // rows per plane (max batch * consumer.rows)
+};
+
 // shift_sign = +1 for a forward conv, -1 for the data gradient (taps read dy at m - shift[t]).
+// `phase` (optional) also writes the parity-split copy of the output.
 void conv_tc_forward(const View& in, const float* wk, int n_rows, int n_out, int taps, int shift_sign,
-                     const Grid& grid, const View& out, const ConvEpilogue& ep, int* err, cudaStream_t stream);
+                     const Grid& grid, const View& out, const ConvEpilogue& ep, int* err, cudaStream_t stream,
+                     const PhaseOut* phase = nullptr);
+// 3x3 stride-2 conv on tensor cores: phase_in holds 4 planes of plane_rows rows (PhaseOut layout),
+// m_rows = images * gout.rows output rows are computed.
+void conv_tc_strided(const View& phase_in, long plane_rows, long m_rows, const float* wk, int oc, const Grid& gout,
+                     const View& out, const ConvEpilogue& ep, int* err, cudaStream_t stream,
+                     const PhaseOut* phase = nullptr);
 
 // Weight gradient: dw[o, c, t] = sum_m dy[m, o] * x[m + shift[t], c], written to `dw` in OIHW order
 // (dw[(o * ic + c) * taps + t]), fully overwritten.  `ws` is scratch of wgrad_workspace_floats() floats.
@@ -48,20 +67,15 @@ size_t wgrad_workspace_floats(int ic, int oc, int taps, long rows);
 void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, float* dw, float* ws, int* err,
                    cudaStream_t stream);
 
-// ---------------------------------------------------------------- convolution (SIMT)
-// Direct implicit-GEMM convolution for any stride (used for stride-2 backbone convs and for
-// the 3-channel stem).  Interior outputs only; weights OHWI [oc][k*k][ic].
-void conv_simt_forward(const View& in, const Grid& gin, const float* w_ohwi, int oc, int k, int stride,
-                       const View& out, const Grid& gout, int batch, const ConvEpilogue& ep, cudaStream_t stream);
-
-// ---------------------------------------------------------------- layout helpers
+// ---------------------------------------------------------------- layout helpers (layout.cu)
 void nchw_to_padded(const float* src, int batch, int c, const Grid& g, const View& dst, cudaStream_t stream);
 void padded_to_nchw(const View& src, int batch, int c, const Grid& g, float* dst, cudaStream_t stream);
 void rgb_to_padded(const uint8_t* rgb, int batch, int size, const Grid& g, const View& dst, cudaStream_t stream);
+// Letterboxed RGB24 (identity scale, value / 255) written as the parity-split input of the stem.
+void rgb_to_phase(const uint8_t* rgb, int batch, int size, const PhaseOut& dst, cudaStream_t stream);
 // OIHW -> [oc][t][kpad] (forward) and OIHW -> [ic][t][kpad_o] (data gradient)
 void weights_fwd_layout(const float* oihw, int oc, int ic, int taps, int kpad, float* dst, cudaStream_t stream);
 void weights_dgrad_layout(const float* oihw, int oc, int ic, int taps, int kpad_o, float* dst, cudaStream_t stream);
-void weights_ohwi(const float* oihw, int oc, int ic, int taps, float* dst, cudaStream_t stream);
 
 // ---------------------------------------------------------------- backbone helpers
 void maxpool5_padded(const View& in, const View& out, int batch, const Grid& g, cudaStream_t stream);

@@ -1,0 +1,248 @@
+// Layout conversions and the small memory-bound kernels of the frozen trunk.
+//
+// nchw_to_padded / padded_to_nchw convert between the reference layout and the padded
+// channels-last layout; rgb_to_phase is the identity-scale letterbox (YoloDetector.cs:445-514)
+// written as the stem's parity-split input; weights_*_layout build the K-major operands of the
+// tensor-core convs; maxpool5_padded is SPPF's MaxPool2d(5, 1, 2); upsample2_padded is
+// nn.Upsample(scale 2, nearest) written into a concat slice.  launch_check lives here too.
+#include <algorithm>
+#include <atomic>
+#include <stdexcept>
+#include <string>
+
+#include "kernels.h"
+
+namespace sy {
+
+namespace {
+
+__global__ void nchw_to_padded_kernel(const float* src, int batch, int c, Grid g, float* dst, int pitch) {
+    long total = (long)batch * c * g.h * g.w;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        int x = (int)(i % g.w);
+        long r = i / g.w;
+        int y = (int)(r % g.h);
+        r /= g.h;
+        int ch = (int)(r % c);
+        int b = (int)(r / c);
+        dst[((long)b * g.rows + g.row(y, x)) * pitch + ch] = src[i];
+    }
+}
+
+__global__ void padded_to_nchw_kernel(const float* src, int pitch, int batch, int c, Grid g, float* dst) {
+    long total = (long)batch * c * g.h * g.w;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        int x = (int)(i % g.w);
+        long r = i / g.w;
+        int y = (int)(r % g.h);
+        r /= g.h;
+        int ch = (int)(r % c);
+        int b = (int)(r / c);
+        dst[i] = src[((long)b * g.rows + g.row(y, x)) * pitch + ch];
+    }
+}
+
+// ImagePreprocessor.Letterbox at identity scale (YoloDetector.cs:445-514): value / 255.
+__global__ void rgb_to_padded_kernel(const uint8_t* rgb, int batch, int size, Grid g, float* dst, int pitch) {
+    long total = (long)batch * size * size;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        int x = (int)(i % size);
+        long r = i / size;
+        int y = (int)(r % size);
+        int b = (int)(r / size);
+        const uint8_t* px = rgb + i * 3;
+        float* d = dst + ((long)b * g.rows + g.row(y, x)) * pitch;
+        d[0] = __fdiv_rn((float)px[0], 255.0f);
+        d[1] = __fdiv_rn((float)px[1], 255.0f);
+        d[2] = __fdiv_rn((float)px[2], 255.0f);
+    }
+}
+
+__global__ void weights_fwd_kernel(const float* w, int oc, int ic, int taps, int kpad, float* dst) {
+    long total = (long)oc * taps * kpad;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        int c = (int)(i % kpad);
+        long r = i / kpad;
+        int t = (int)(r % taps);
+        int o = (int)(r / taps);
+        dst[i] = c < ic ? w[((long)o * ic + c) * taps + t] : 0.0f;
+    }
+}
+
+__global__ void weights_dgrad_kernel(const float* w, int oc, int ic, int taps, int kpad_o, float* dst) {
+    long total = (long)ic * taps * kpad_o;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        int o = (int)(i % kpad_o);
+        long r = i / kpad_o;
+        int t = (int)(r % taps);
+        int c = (int)(r / taps);
+        dst[i] = o < oc ? w[((long)o * ic + c) * taps + t] : 0.0f;
+    }
+}
+
+// Vector of V consecutive channels (V = 4 when channels and pitches allow float4 access).
+template <int V>
+struct Vec {
+    float v[V];
+};
+template <int V>
+__device__ __forceinline__ Vec<V> load_vec(const float* p) {
+    Vec<V> r;
+    if constexpr (V == 4) {
+        const float4 t = *reinterpret_cast<const float4*>(p);
+        r.v[0] = t.x;
+        r.v[1] = t.y;
+        r.v[2] = t.z;
+        r.v[3] = t.w;
+    } else {
+        r.v[0] = *p;
+    }
+    return r;
+}
+template <int V>
+__device__ __forceinline__ void store_vec(float* p, const Vec<V>& r) {
+    if constexpr (V == 4)
+        *reinterpret_cast<float4*>(p) = make_float4(r.v[0], r.v[1], r.v[2], r.v[3]);
+    else
+        *p = r.v[0];
+}
+
+// MaxPool2d(5, stride 1, padding 2); padded positions never win.
+template <int V>
+__global__ void maxpool5_kernel(const float* in, int in_pitch, float* out, int out_pitch, int c, int batch, Grid g) {
+    const int cv = c / V;
+    const long total = (long)batch * g.h * g.w * cv;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const long pix = i / cv;
+        const int ch = (int)(i - pix * cv) * V;
+        const int b = (int)(pix / (g.h * g.w));
+        const int rem = (int)(pix - (long)b * g.h * g.w);
+        const int y = rem / g.w, x = rem - y * g.w;
+        Vec<V> m;
+        for (int k = 0; k < V; k++) m.v[k] = -INFINITY;
+        for (int dy = -2; dy <= 2; dy++) {
+            const int yy = y + dy;
+            if (yy < 0 || yy >= g.h) continue;
+            for (int dx = -2; dx <= 2; dx++) {
+                const int xx = x + dx;
+                if (xx < 0 || xx >= g.w) continue;
+                const Vec<V> t = load_vec<V>(in + ((long)b * g.rows + g.row(yy, xx)) * in_pitch + ch);
+                for (int k = 0; k < V; k++) m.v[k] = fmaxf(m.v[k], t.v[k]);
+            }
+        }
+        store_vec<V>(out + ((long)b * g.rows + g.row(y, x)) * out_pitch + ch, m);
+    }
+}
+
+template <int V>
+__global__ void upsample2_kernel(const float* in, int in_pitch, Grid gin, float* out, int out_pitch, Grid gout, int c,
+                                 int batch) {
+    const int cv = c / V;
+    const long total = (long)batch * gout.h * gout.w * cv;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const long pix = i / cv;
+        const int ch = (int)(i - pix * cv) * V;
+        const int b = (int)(pix / (gout.h * gout.w));
+        const int rem = (int)(pix - (long)b * gout.h * gout.w);
+        const int y = rem / gout.w, x = rem - y * gout.w;
+        store_vec<V>(out + ((long)b * gout.rows + gout.row(y, x)) * out_pitch + ch,
+                     load_vec<V>(in + ((long)b * gin.rows + gin.row(y / 2, x / 2)) * in_pitch + ch));
+    }
+}
+
+// Identity-scale letterbox written straight into the stem's parity-split input (PhaseOut layout),
+// 4 floats per pixel (r, g, b, 0).
+__global__ void rgb_to_phase_kernel(const uint8_t* rgb, int batch, int size, PhaseOut dst) {
+    const long total = (long)batch * size * size;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int b = (int)(i / ((long)size * size));
+        const int rem = (int)(i - (long)b * size * size);
+        const int py = rem / size + 1, px = rem - (rem / size) * size + 1;
+        const uint8_t* s = rgb + i * 3;
+        const long row = ((py & 1) * 2 + (px & 1)) * dst.plane_rows + (long)b * dst.consumer.rows +
+                         (long)(py >> 1) * dst.consumer.wp + (px >> 1);
+        *reinterpret_cast<float4*>(dst.base + row * dst.pitch) =
+            make_float4(__fdiv_rn((float)s[0], 255.0f), __fdiv_rn((float)s[1], 255.0f),
+                        __fdiv_rn((float)s[2], 255.0f), 0.0f);
+    }
+}
+
+int blocks_for(long n) { return (int)std::min<long>(65535L * 16, std::max<long>(1, (n + 255) / 256)); }
+
+}  // namespace
+
+static std::atomic<long long> g_launches{0};
+
+void launch_check(const char* what) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+void nchw_to_padded(const float* src, int batch, int c, const Grid& g, const View& dst, cudaStream_t stream) {
+    long n = (long)batch * c * g.h * g.w;
+    nchw_to_padded_kernel<<<blocks_for(n), 256, 0, stream>>>(src, batch, c, g, dst.base, dst.pitch);
+    launch_check("nchw_to_padded_kernel");
+}
+
+void padded_to_nchw(const View& src, int batch, int c, const Grid& g, float* dst, cudaStream_t stream) {
+    long n = (long)batch * c * g.h * g.w;
+    padded_to_nchw_kernel<<<blocks_for(n), 256, 0, stream>>>(src.base, src.pitch, batch, c, g, dst);
+    launch_check("padded_to_nchw_kernel");
+}
+
+void rgb_to_padded(const uint8_t* rgb, int batch, int size, const Grid& g, const View& dst, cudaStream_t stream) {
+    long n = (long)batch * size * size;
+    rgb_to_padded_kernel<<<blocks_for(n), 256, 0, stream>>>(rgb, batch, size, g, dst.base, dst.pitch);
+    launch_check("rgb_to_padded_kernel");
+}
+
+void weights_fwd_layout(const float* oihw, int oc, int ic, int taps, int kpad, float* dst, cudaStream_t stream) {
+    long n = (long)oc * taps * kpad;
+    weights_fwd_kernel<<<blocks_for(n), 256, 0, stream>>>(oihw, oc, ic, taps, kpad, dst);
+    launch_check("weights_fwd_kernel");
+}
+
+void weights_dgrad_layout(const float* oihw, int oc, int ic, int taps, int kpad_o, float* dst, cudaStream_t stream) {
+    long n = (long)ic * taps * kpad_o;
+    weights_dgrad_kernel<<<blocks_for(n), 256, 0, stream>>>(oihw, oc, ic, taps, kpad_o, dst);
+    launch_check("weights_dgrad_kernel");
+}
+
+void maxpool5_padded(const View& in, const View& out, int batch, const Grid& g, cudaStream_t stream) {
+    const bool vec = in.channels % 4 == 0 && in.pitch % 4 == 0 && out.pitch % 4 == 0 &&
+                     (reinterpret_cast<uintptr_t>(in.base) & 15) == 0 && (reinterpret_cast<uintptr_t>(out.base) & 15) == 0;
+    const long n = (long)batch * g.h * g.w * (vec ? in.channels / 4 : in.channels);
+    if (vec)
+        maxpool5_kernel<4><<<blocks_for(n), 256, 0, stream>>>(in.base, in.pitch, out.base, out.pitch, in.channels,
+                                                              batch, g);
+    else
+        maxpool5_kernel<1><<<blocks_for(n), 256, 0, stream>>>(in.base, in.pitch, out.base, out.pitch, in.channels,
+                                                              batch, g);
+    launch_check("maxpool5_kernel");
+}
+
+void upsample2_padded(const View& in, const Grid& gin, const View& out, const Grid& gout, int batch,
+                      cudaStream_t stream) {
+    const bool vec = in.channels % 4 == 0 && in.pitch % 4 == 0 && out.pitch % 4 == 0 &&
+                     (reinterpret_cast<uintptr_t>(in.base) & 15) == 0 && (reinterpret_cast<uintptr_t>(out.base) & 15) == 0;
+    const long n = (long)batch * gout.h * gout.w * (vec ? in.channels / 4 : in.channels);
+    if (vec)
+        upsample2_kernel<4><<<blocks_for(n), 256, 0, stream>>>(in.base, in.pitch, gin, out.base, out.pitch, gout,
+                                                               in.channels, batch);
+    else
+        upsample2_kernel<1><<<blocks_for(n), 256, 0, stream>>>(in.base, in.pitch, gin, out.base, out.pitch, gout,
+                                                               in.channels, batch);
+    launch_check("upsample2_kernel");
+}
+
+void rgb_to_phase(const uint8_t* rgb, int batch, int size, const PhaseOut& dst, cudaStream_t stream) {
+    if (dst.pitch != 4) throw std::runtime_error("rgb_to_phase: stem input pitch must be 4");
+    const long n = (long)batch * size * size;
+    rgb_to_phase_kernel<<<blocks_for(n), 256, 0, stream>>>(rgb, batch, size, dst);
+    launch_check("rgb_to_phase_kernel");
+}
+
+}  // namespace sy

@@ -198,6 +198,32 @@ void Session::build_backbone() {
             op.res = *res;
             op.has_res = true;
         }
+        if (s == 2) {
+            // parity-split copy of the input, laid out on this conv's output grid
+            if (gin.h != 2 * gout.h || gin.w != 2 * gout.w || k != 3)
+                throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "stride-2 conv needs k 3 and an even input");
+            const int pitch = round_up(op.ic, 4);
+            op.phase_plane_rows = (long)B_ * gout.rows;
+            float* buf = static_cast<float*>(dalloc(sizeof(float) * (size_t)pitch * 4 * op.phase_plane_rows));
+            // the stem reads its (r, g, b, 0) pixels as 4 channels; the 4th weight column is zero
+            const int vis = in.base == img_.base ? pitch : op.ic;
+            op.phase_in = View{buf, pitch, vis, 4 * op.phase_plane_rows};
+            const PhaseOut po{buf, pitch, gout, op.phase_plane_rows};
+            if (in.base == img_.base) {
+                stem_phase_ = po;
+            } else {
+                // the most recent conv that wrote exactly this view also writes the parity copy
+                bool found = false;
+                for (auto it = bops_.rbegin(); it != bops_.rend(); ++it)
+                    if (it->type == 0 && it->out.base == in.base && it->out.channels == in.channels) {
+                        it->has_phase_out = true;
+                        it->phase_out = po;
+                        found = true;
+                        break;
+                    }
+                if (!found) throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "stride-2 conv input has no producing conv");
+            }
+        }
         bops_.push_back(op);
     };
     auto c2f = [&](const View& in, const Grid& g, int c2, int n, bool shortcut, const View& out) {
@@ -236,8 +262,8 @@ void Session::build_backbone() {
         bops_.push_back(op);
     };
     img_grid_ = gS;
-    View img4 = alloc_view(4, gS);
-    img_ = View{img4.base, 4, 3, img4.rows};
+    // the image itself only exists as the stem's parity-split input; img_ just names it
+    img_ = View{static_cast<float*>(dalloc(256)), 4, 3, 0};
     View b0 = alloc_view(c64, g2);
     conv(img_, gS, c64, 3, 2, b0, g2, nullptr);
     View b1 = alloc_view(c128, g4);
@@ -285,10 +311,7 @@ void Session::build_backbone() {
     for (auto& op : bops_) {
         if (op.type != 0) continue;
         const int taps = op.k * op.k;
-        if (op.stride == 1)
-            op.wk = static_cast<float*>(dalloc(sizeof(float) * (size_t)op.oc * taps * round_up(op.ic, 32)));
-        else
-            op.wk = static_cast<float*>(dalloc(sizeof(float) * (size_t)op.oc * taps * op.ic));
+        op.wk = static_cast<float*>(dalloc(sizeof(float) * (size_t)op.oc * taps * round_up(op.ic, 32)));
     }
 }
 
@@ -299,10 +322,7 @@ int Session::set_backbone(const float* host, long count) {
     for (auto& op : bops_) {
         if (op.type != 0) continue;
         const int taps = op.k * op.k;
-        if (op.stride == 1)
-            weights_fwd_layout(backbone_params_ + op.w_off, op.oc, op.ic, taps, round_up(op.ic, 32), op.wk, stream_);
-        else
-            weights_ohwi(backbone_params_ + op.w_off, op.oc, op.ic, taps, op.wk, stream_);
+        weights_fwd_layout(backbone_params_ + op.w_off, op.oc, op.ic, taps, round_up(op.ic, 32), op.wk, stream_);
     }
     SY_CUDA(cudaStreamSynchronize(stream_));
     backbone_ready_ = true;
@@ -324,13 +344,15 @@ void Session::forward_backbone(int batch) {
                 ep.residual = op.res.base;
                 ep.res_pitch = op.res.pitch;
             }
+            const PhaseOut* po = op.has_phase_out ? &op.phase_out : nullptr;
             if (op.stride == 1) {
                 // the tcgen05 kernel works on whole 128-row tiles: restrict the views to `batch` images
                 View i2 = in, o2 = out;
                 i2.rows = o2.rows = (long)batch * op.gin.rows;
-                conv_tc_forward(i2, op.wk, op.oc, op.oc, op.k * op.k, 1, op.gin, o2, ep, d_flags_, stream_);
+                conv_tc_forward(i2, op.wk, op.oc, op.oc, op.k * op.k, 1, op.gin, o2, ep, d_flags_, stream_, po);
             } else {
-                conv_simt_forward(in, op.gin, op.wk, op.oc, op.k, op.stride, out, op.gout, batch, ep, stream_);
+                conv_tc_strided(op.phase_in, op.phase_plane_rows, (long)batch * op.gout.rows, op.wk, op.oc, op.gout,
+                                out, ep, d_flags_, stream_, po);
             }
         }
     }
@@ -570,7 +592,7 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
             }
             SY_CUDA(cudaMemcpyAsync(d_rgb_, rgb, bytes, cudaMemcpyHostToDevice, stream_));
         }
-        rgb_to_padded(src, images, cfg.image_size, img_grid_, img_, stream_);
+        rgb_to_phase(src, images, cfg.image_size, stem_phase_, stream_);
         forward_backbone(images);
     } else {
         if (!features) throw SyError(SY_ERR_INVALID_ARGUMENT, "features missing");

@@ -51,10 +51,14 @@ struct BackboneOp {
     int type;                   // 0 conv, 1 maxpool5, 2 upsample2
     int ic = 0, oc = 0, k = 0, stride = 1;
     long w_off = 0, b_off = 0;
-    float* wk = nullptr;        // K-major (stride 1) or OHWI (stride 2)
+    float* wk = nullptr;        // K-major [oc][tap][round_up(ic, 32)]
     View in{}, out{}, res{};
     Grid gin{}, gout{};
     bool has_res = false;
+    View phase_in{};            // stride 2: parity-split input (4 planes)
+    long phase_plane_rows = 0;
+    bool has_phase_out = false; // this conv's output feeds a stride-2 conv
+    PhaseOut phase_out{};
 };
 
 struct NcclApi;
@@ -107,6 +111,7 @@ private:
     uint8_t* h_rgb_ = nullptr;   // pinned staging
     View img_{};
     Grid img_grid_{};
+    PhaseOut stem_phase_{};      // parity-split image written by the preprocessing
     bool backbone_ready_ = false;
     // head
     std::vector<Branch> branches_;
