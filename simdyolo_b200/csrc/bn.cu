@@ -192,23 +192,29 @@ __global__ void __launch_bounds__(kThreads) bn_bwd_partial_kernel(const float* y
     }
 }
 
-// red[b][ch] = (sum dz, sum dz xhat) folded over splits; dgamma / dbeta accumulate over images in order.
-__global__ void bn_bwd_final_kernel(const float* part, int batch, int c, int splits, float* red, float* dgamma,
-                                    float* dbeta) {
+// red[b][ch] = (sum dz, sum dz xhat) folded over the splits, one thread per (image, channel).
+__global__ void bn_bwd_final_kernel(const float* part, int batch, int c, int splits, float* red) {
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)batch * c) return;
+    const int b = (int)(i / c), ch = (int)(i - (long)b * c);
+    float t1 = 0.0f, t2 = 0.0f;
+    for (int s = 0; s < splits; s++) {
+        const float* o = part + (((long)b * splits + s) * c + ch) * 2;
+        t1 += o[0];
+        t2 += o[1];
+    }
+    red[i * 2 + 0] = t1;
+    red[i * 2 + 1] = t2;
+}
+
+// dgamma += sum_b red[b][ch][1], dbeta += sum_b red[b][ch][0], images in order.
+__global__ void bn_param_grad_kernel(const float* red, int batch, int c, float* dgamma, float* dbeta) {
     const int ch = blockIdx.x * blockDim.x + threadIdx.x;
     if (ch >= c) return;
     float dg = dgamma[ch], db = dbeta[ch];
     for (int b = 0; b < batch; b++) {
-        float t1 = 0.0f, t2 = 0.0f;
-        for (int s = 0; s < splits; s++) {
-            const float* o = part + (((long)b * splits + s) * c + ch) * 2;
-            t1 += o[0];
-            t2 += o[1];
-        }
-        red[((long)b * c + ch) * 2 + 0] = t1;
-        red[((long)b * c + ch) * 2 + 1] = t2;
-        dg += t2;
-        db += t1;
+        db += red[((long)b * c + ch) * 2 + 0];
+        dg += red[((long)b * c + ch) * 2 + 1];
     }
     dgamma[ch] = dg;
     dbeta[ch] = db;
@@ -304,12 +310,21 @@ __global__ void __launch_bounds__(kThreads) bias_partial_kernel(const float* gr,
     }
 }
 
-__global__ void bias_fold_kernel(const float* part, int batch, int c, int splits, float* db) {
+// per_image[b][ch] = sum over the splits of image b (one thread per (image, channel))
+__global__ void bias_image_kernel(const float* part, int batch, int c, int splits, float* per_image) {
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)batch * c) return;
+    const int b = (int)(i / c), ch = (int)(i - (long)b * c);
+    float acc = 0.0f;
+    for (int s = 0; s < splits; s++) acc += part[((long)b * splits + s) * c + ch];
+    per_image[i] = acc;
+}
+
+__global__ void bias_fold_kernel(const float* per_image, int batch, int c, float* db) {
     const int ch = blockIdx.x * blockDim.x + threadIdx.x;
     if (ch >= c) return;
     float acc = db[ch];
-    for (int b = 0; b < batch; b++)
-        for (int s = 0; s < splits; s++) acc += part[((long)b * splits + s) * c + ch];
+    for (int b = 0; b < batch; b++) acc += per_image[(long)b * c + ch];
     db[ch] = acc;
 }
 
@@ -351,8 +366,10 @@ void bn_silu_backward(const View& y, const View& gv, const float* stats, const f
     bn_bwd_partial_kernel<<<dim3(sp.cgroups, batch, sp.splits), kThreads, 0, stream>>>(
         y.base, y.pitch, gv.base, gv.pitch, stats, gamma, beta, eps, c, gr, sp.splits, ws);
     launch_check("bn_bwd_partial_kernel");
-    bn_bwd_final_kernel<<<(c + 127) / 128, 128, 0, stream>>>(ws, batch, c, sp.splits, red, dgamma, dbeta);
+    bn_bwd_final_kernel<<<(int)(((long)batch * c + 127) / 128), 128, 0, stream>>>(ws, batch, c, sp.splits, red);
     launch_check("bn_bwd_final_kernel");
+    bn_param_grad_kernel<<<(c + 127) / 128, 128, 0, stream>>>(red, batch, c, dgamma, dbeta);
+    launch_check("bn_param_grad_kernel");
     const long rows = (long)batch * gr.rows;
     const bool vec = c % 4 == 0;
     const long n = rows * (vec ? c / 4 : c);
@@ -377,7 +394,11 @@ void bias_grad(const View& gv, int batch, const Grid& gr, float* ws, float* db, 
     bias_partial_kernel<<<dim3(sp.cgroups, batch, sp.splits), kThreads, 0, stream>>>(gv.base, gv.pitch, gv.channels,
                                                                                    gr, sp.splits, ws);
     launch_check("bias_partial_kernel");
-    bias_fold_kernel<<<(gv.channels + 127) / 128, 128, 0, stream>>>(ws, batch, gv.channels, sp.splits, db);
+    float* per_image = ws + (size_t)batch * sp.splits * gv.channels;
+    bias_image_kernel<<<(int)(((long)batch * gv.channels + 127) / 128), 128, 0, stream>>>(ws, batch, gv.channels,
+                                                                                         sp.splits, per_image);
+    launch_check("bias_image_kernel");
+    bias_fold_kernel<<<(gv.channels + 127) / 128, 128, 0, stream>>>(per_image, batch, gv.channels, db);
     launch_check("bias_fold_kernel");
 }
 

@@ -152,6 +152,57 @@ __global__ void upsample2_kernel(const float* in, int in_pitch, Grid gin, float*
 
 // Identity-scale letterbox written straight into the stem's parity-split input (PhaseOut layout),
 // 4 floats per pixel (r, g, b, 0).
+// One thread per output pixel of the stem: 27 inputs (u8 / 255) x OC outputs, bias, SiLU.
+template <int OC>
+__global__ void __launch_bounds__(256) stem_conv_kernel(const uint8_t* rgb, int batch, int size, const float* w,
+                                                        const float* bias, float* out, int out_pitch, Grid gout,
+                                                        PhaseOut phase, int has_phase) {
+    __shared__ float ws[OC * 27];
+    __shared__ float bs[OC];
+    for (int i = threadIdx.x; i < OC * 27; i += blockDim.x) ws[i] = w[i];
+    for (int i = threadIdx.x; i < OC; i += blockDim.x) bs[i] = bias[i];
+    __syncthreads();
+    const int ho = gout.h, wo = gout.w;
+    const long total = (long)batch * ho * wo;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int b = (int)(i / ((long)ho * wo));
+        const int rem = (int)(i - (long)b * ho * wo);
+        const int oy = rem / wo, ox = rem - oy * wo;
+        float in[27];
+#pragma unroll
+        for (int ky = 0; ky < 3; ky++)
+#pragma unroll
+            for (int kx = 0; kx < 3; kx++) {
+                const int iy = 2 * oy + ky - 1, ix = 2 * ox + kx - 1;
+                const bool ok = iy >= 0 && iy < size && ix >= 0 && ix < size;
+                const uint8_t* p = rgb + (((long)b * size + (ok ? iy : 0)) * size + (ok ? ix : 0)) * 3;
+#pragma unroll
+                for (int c = 0; c < 3; c++) in[c * 9 + ky * 3 + kx] = ok ? __fdiv_rn((float)p[c], 255.0f) : 0.0f;
+            }
+        float acc[OC];
+#pragma unroll
+        for (int o = 0; o < OC; o++) {
+            float s = 0.0f;
+#pragma unroll
+            for (int q = 0; q < 27; q++) s = fmaf(ws[o * 27 + q], in[q], s);
+            acc[o] = silu_f(s + bs[o]);
+        }
+        float* dst = out + ((long)b * gout.rows + gout.row(oy, ox)) * out_pitch;
+#pragma unroll
+        for (int o = 0; o < OC; o += 4)
+            *reinterpret_cast<float4*>(dst + o) = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
+        if (has_phase) {
+            const int py = oy + 1, px = ox + 1;
+            float* pd = phase.base + (((py & 1) * 2 + (px & 1)) * phase.plane_rows + (long)b * phase.consumer.rows +
+                                      (long)(py >> 1) * phase.consumer.wp + (px >> 1)) *
+                                         phase.pitch;
+#pragma unroll
+            for (int o = 0; o < OC; o += 4)
+                *reinterpret_cast<float4*>(pd + o) = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
+        }
+    }
+}
+
 __global__ void rgb_to_phase_kernel(const uint8_t* rgb, int batch, int size, PhaseOut dst) {
     const long total = (long)batch * size * size;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
@@ -236,6 +287,24 @@ void upsample2_padded(const View& in, const Grid& gin, const View& out, const Gr
         upsample2_kernel<1><<<blocks_for(n), 256, 0, stream>>>(in.base, in.pitch, gin, out.base, out.pitch, gout,
                                                                in.channels, batch);
     launch_check("upsample2_kernel");
+}
+
+void stem_conv(const uint8_t* rgb, int batch, int size, const float* w, const float* bias, int oc, const View& out,
+               const Grid& gout, const PhaseOut* phase, cudaStream_t stream) {
+    if (out.pitch % 4 != 0 || (phase && phase->pitch % 4 != 0))
+        throw std::runtime_error("stem_conv: pitches must be multiples of 4");
+    const long n = (long)batch * gout.h * gout.w;
+    const int blocks = (int)std::min<long>(148L * 8, std::max<long>(1, (n + 255) / 256));
+    const PhaseOut ph = phase ? *phase : PhaseOut{};
+    const int hp = phase ? 1 : 0;
+    switch (oc) {
+        case 16: stem_conv_kernel<16><<<blocks, 256, 0, stream>>>(rgb, batch, size, w, bias, out.base, out.pitch, gout, ph, hp); break;
+        case 32: stem_conv_kernel<32><<<blocks, 256, 0, stream>>>(rgb, batch, size, w, bias, out.base, out.pitch, gout, ph, hp); break;
+        case 48: stem_conv_kernel<48><<<blocks, 256, 0, stream>>>(rgb, batch, size, w, bias, out.base, out.pitch, gout, ph, hp); break;
+        case 64: stem_conv_kernel<64><<<blocks, 256, 0, stream>>>(rgb, batch, size, w, bias, out.base, out.pitch, gout, ph, hp); break;
+        default: throw std::runtime_error("stem_conv: output channels must be 16, 32, 48 or 64");
+    }
+    launch_check("stem_conv_kernel");
 }
 
 void rgb_to_phase(const uint8_t* rgb, int batch, int size, const PhaseOut& dst, cudaStream_t stream) {

@@ -198,20 +198,16 @@ void Session::build_backbone() {
             op.res = *res;
             op.has_res = true;
         }
-        if (s == 2) {
+        if (s == 2 && in.base != img_.base) {  // the stem reads the RGB24 image directly (stem_conv)
             // parity-split copy of the input, laid out on this conv's output grid
             if (gin.h != 2 * gout.h || gin.w != 2 * gout.w || k != 3)
                 throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "stride-2 conv needs k 3 and an even input");
             const int pitch = round_up(op.ic, 4);
             op.phase_plane_rows = (long)B_ * gout.rows;
             float* buf = static_cast<float*>(dalloc(sizeof(float) * (size_t)pitch * 4 * op.phase_plane_rows));
-            // the stem reads its (r, g, b, 0) pixels as 4 channels; the 4th weight column is zero
-            const int vis = in.base == img_.base ? pitch : op.ic;
-            op.phase_in = View{buf, pitch, vis, 4 * op.phase_plane_rows};
+            op.phase_in = View{buf, pitch, op.ic, 4 * op.phase_plane_rows};
             const PhaseOut po{buf, pitch, gout, op.phase_plane_rows};
-            if (in.base == img_.base) {
-                stem_phase_ = po;
-            } else {
+            {
                 // the most recent conv that wrote exactly this view also writes the parity copy
                 bool found = false;
                 for (auto it = bops_.rbegin(); it != bops_.rend(); ++it)
@@ -329,10 +325,13 @@ int Session::set_backbone(const float* host, long count) {
     return SY_OK;
 }
 
-void Session::forward_backbone(int batch) {
+void Session::forward_backbone(int batch, const uint8_t* rgb_device) {
     for (auto& op : bops_) {
         View in = op.in, out = op.out;
-        if (op.type == 1) {
+        if (op.type == 0 && in.base == img_.base) {
+            stem_conv(rgb_device, batch, cfg.image_size, backbone_params_ + op.w_off, backbone_params_ + op.b_off, op.oc,
+                      out, op.gout, op.has_phase_out ? &op.phase_out : nullptr, stream_);
+        } else if (op.type == 1) {
             maxpool5_padded(in, out, batch, op.gin, stream_);
         } else if (op.type == 2) {
             upsample2_padded(in, op.gin, out, op.gout, batch, stream_);
@@ -592,8 +591,7 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
             }
             SY_CUDA(cudaMemcpyAsync(d_rgb_, rgb, bytes, cudaMemcpyHostToDevice, stream_));
         }
-        rgb_to_phase(src, images, cfg.image_size, stem_phase_, stream_);
-        forward_backbone(images);
+        forward_backbone(images, src);
     } else {
         if (!features) throw SyError(SY_ERR_INVALID_ARGUMENT, "features missing");
         for (int l = 0; l < 3; l++) {

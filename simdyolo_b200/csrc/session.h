@@ -89,7 +89,7 @@ public:
 private:
     void build_backbone();
     void build_head();
-    void forward_backbone(int batch);
+    void forward_backbone(int batch, const uint8_t* rgb_device);
     void forward_head(int batch);
     void backward_head(int batch);
     void refresh_head_weights();
@@ -111,7 +111,6 @@ private:
     uint8_t* h_rgb_ = nullptr;   // pinned staging
     View img_{};
     Grid img_grid_{};
-    PhaseOut stem_phase_{};      // parity-split image written by the preprocessing
     bool backbone_ready_ = false;
     // head
     std::vector<Branch> branches_;
