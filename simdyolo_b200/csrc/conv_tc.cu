@@ -76,7 +76,8 @@ struct FwdParams {
     int n_valid;    // channels stored
     int n0;         // first weight row of this launch
     int stages;
-    int acc_cols;   // TMEM columns between the two accumulators
+    int nacc;       // TMEM accumulator stages (2..8)
+    int acc_cols;   // TMEM columns per accumulator
     int alloc_cols;
     float* out;
     int out_pitch;
@@ -95,9 +96,12 @@ struct FwdParams {
     int* err;
 };
 
-constexpr int kFwdThreads = 192;
+constexpr int kFwdThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kEpiThreads = 256;
 constexpr int kTileM = 128;
 constexpr int kABytes = kTileM * 128;  // 128 rows x 32 fp32
+
+__device__ __forceinline__ float silu_fast(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
 __global__ void __launch_bounds__(kFwdThreads, 1)
     conv_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -109,8 +113,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * stage_bytes);
     uint64_t* empty = full + p.stages;
     uint64_t* tfull = empty + p.stages;
-    uint64_t* tempty = tfull + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* tempty = tfull + p.nacc;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + p.nacc);
+    float* bias_s = reinterpret_cast<float*>(tmem_slot + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -118,12 +123,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int a = 0; a < 2; a++) {
+        for (int a = 0; a < p.nacc; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 128);
+            mbar_init(&tempty[a], kEpiThreads);
         }
         fence_barrier_init();
     }
+    if (warp >= 2)
+        for (int i = threadIdx.x - 64; i < p.n; i += kEpiThreads)
+            bias_s[i] = (p.bias && i < p.n_valid) ? p.bias[p.n0 + i] : 0.0f;
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
@@ -163,8 +171,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             int it = 0, local = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, local++) {
-                const int acc = local & 1;
-                const uint32_t aph = (local >> 1) & 1;
+                const int acc = local % p.nacc;
+                const uint32_t aph = (local / p.nacc) & 1;
                 if (!(ok = mbar_wait(&tempty[acc], aph ^ 1, p.err, 2))) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + acc * p.acc_cols;
@@ -187,12 +195,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             }
         }
     } else {
+        // two warps per TMEM lane quadrant; they take alternate 16-column chunks
         const int q = warp & 3;
+        const int half = (warp - 2) >> 2;
         const int row = q * 32 + lane;
         int local = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
-            const int acc = local & 1;
-            const uint32_t aph = (local >> 1) & 1;
+            const int acc = local % p.nacc;
+            const uint32_t aph = (local / p.nacc) & 1;
             if (!mbar_wait(&tfull[acc], aph, p.err, 4)) break;
             tc_fence_after();
             const long m = (long)tile * kTileM + row;
@@ -209,19 +219,33 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                                         (long)(py >> 1) * p.phase_wp + (px >> 1);
                 prow = p.phase + prow_index * p.phase_pitch;
             }
-            for (int j = 0; j < p.n; j += 16) {
+            for (int j = half * 16; j < p.n; j += 32) {
                 float v[16];
                 tmem_ld16(tmem_base + acc * p.acc_cols + ((uint32_t)(q * 32) << 16) + j, v);
                 if (j >= p.n_valid) continue;
+                const bool full16 = j + 16 <= p.n_valid;
+                float res[16];
+                if (rrow && full16 && inside) {
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float4 t = *reinterpret_cast<const float4*>(rrow + j + 4 * i);
+                        res[4 * i] = t.x;
+                        res[4 * i + 1] = t.y;
+                        res[4 * i + 2] = t.z;
+                        res[4 * i + 3] = t.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) res[i] = (rrow && inside && j + i < p.n_valid) ? rrow[j + i] : 0.0f;
+                }
 #pragma unroll
                 for (int i = 0; i < 16; i++) {
-                    float x = v[i];
-                    if (p.bias) x += p.bias[p.n0 + j + i];
-                    if (p.silu) x = silu_f(x);
-                    if (rrow) x += rrow[j + i];
+                    float x = v[i] + bias_s[j + i];
+                    if (p.silu) x = silu_fast(x);
+                    x += res[i];
                     v[i] = inside ? x : 0.0f;
                 }
-                if (j + 16 <= p.n_valid) {
+                if (full16) {
                     float4* dst = reinterpret_cast<float4*>(orow + j);
 #pragma unroll
                     for (int i = 0; i < 4; i++) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
@@ -285,8 +309,9 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         p.n0 = n0;
         const int stage_bytes = (kABytes + n * 128 + 1023) & ~1023;
         p.stages = std::min(8, (int)((220 * 1024) / stage_bytes));
-        p.alloc_cols = pow2_at_least(2 * n);
-        p.acc_cols = p.alloc_cols / 2;
+        p.acc_cols = pow2_at_least(n);
+        p.nacc = std::max(2, std::min(8, 512 / p.acc_cols));
+        p.alloc_cols = p.nacc * p.acc_cols;
         p.out = out.base + n0;
         p.out_pitch = out.pitch;
         p.bias = ep.bias;
@@ -301,7 +326,7 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         p.phase_rows = phase ? phase->consumer.rows : 0;
         p.phase_stride = phase ? phase->plane_rows : 0;
         p.err = err;
-        const size_t smem = 1024 + (size_t)p.stages * stage_bytes + (2 * p.stages + 4) * 8 + 16;
+        const size_t smem = 1024 + (size_t)p.stages * stage_bytes + (2 * p.stages + 2 * p.nacc) * 8 + 16 + n * 4;
         const int grid_x = std::min(p.num_tiles, num_sms());
         conv_fwd_tc_kernel<<<grid_x, kFwdThreads, smem, stream>>>(ta, tb, p);
         launch_check("conv_fwd_tc_kernel");
@@ -347,10 +372,11 @@ struct WgradParams {
     int* err;
 };
 
+constexpr int kWgradThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kWgradBK = 32;                    // pixel rows per stage
 constexpr int kWgradBlockBytes = kWgradBK * 128;  // one 32-channel x 32-row box
 
-__global__ void __launch_bounds__(kFwdThreads, 1)
+__global__ void __launch_bounds__(kWgradThreads, 1)
     conv_wgrad_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmG,
                          const WgradParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -531,7 +557,7 @@ void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, fl
         attr_set = true;
     }
     const size_t smem = 1024 + (size_t)p.stages * stage_bytes + (2 * p.stages + 2) * 8 + 16;
-    conv_wgrad_tc_kernel<<<dim3(p.m_tiles, splits), kFwdThreads, smem, stream>>>(tx, tg, p);
+    conv_wgrad_tc_kernel<<<dim3(p.m_tiles, splits), kWgradThreads, smem, stream>>>(tx, tg, p);
     launch_check("conv_wgrad_tc_kernel");
     const long split_stride = (long)p.m_tiles * kTileM * p.n;
     const long total = (long)dy.channels * x.channels * taps;
