@@ -38,7 +38,7 @@ WORKLOAD = ("config 2: YOLOv8n head fine-tune step (frozen backbone+neck fwd, De
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--batch", type=int, default=64, help="images per GPU")
@@ -216,11 +216,9 @@ def run_ours(args, rank, world, local_rank, dist):
     from simdyolo_b200 import data
 
     torch.cuda.set_device(local_rank)
-    nccl_id = b""
-    if world > 1:
-        obj = [sy.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        nccl_id = obj[0]
+    from simdyolo_b200 import dp
+
+    nccl_id = dp.broadcast_nccl_id(dist, rank) if world > 1 else b""
     cfg = sy.make_config(args.model, image_size=args.image, max_batch=args.batch, max_boxes=8, num_classes=80,
                          device=local_rank, rank=rank, world_size=world, nccl_id=nccl_id)
     sess = sy.Session(cfg)
@@ -242,11 +240,7 @@ def run_ours(args, rank, world, local_rank, dist):
         torch.cuda.synchronize()
 
     def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return dp.max_over_ranks(dist, v)
 
     for i in range(args.warmup):
         sess.step_device(dev_images[i % nbatches].data_ptr(), args.batch, truths[i % nbatches])

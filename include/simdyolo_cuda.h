@@ -137,7 +137,7 @@ SY_API sy_status sy_cuda_step_features(sy_session *session, const float *const f
  * images * S * S * 3 bytes, caller-owned). */
 SY_API sy_status sy_cuda_step_device(sy_session *session, const uint8_t *rgb_device, const sy_box *boxes,
                                      const int32_t *counts, int32_t images, sy_step_stats *out);
-/* Gradient of the last step (summed over images, before the update), parameter order. */
+/* Gradient of the last step (summed over the images of every rank, before the update), parameter order. */
 SY_API sy_status sy_cuda_get_last_gradients(const sy_session *session, float *host, int64_t count);
 /* Frozen features of the last step (NCHW per level), for parity checks. */
 SY_API sy_status sy_cuda_get_last_features(const sy_session *session, int32_t level, float *host, int64_t count);

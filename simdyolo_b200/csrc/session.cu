@@ -614,6 +614,12 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
     detection_loss(lv, 3, images, cfg.num_classes, cfg.reg_max, d_truth_, d_box_off_, std::max(1, cfg.max_boxes), 10,
                    1.0f, 1, loss_ws_, lo, stream_);
     backward_head(images);
+    if (comm_) {
+        // the gradient bucket is summed over ranks before anything reads it, so the finiteness
+        // check, the checksum and the kept copy all see the global gradient
+        int r = nccl_->AllReduce(grads_, grads_, (size_t)n_params, kNcclFloat, kNcclSum, comm_, stream_);
+        if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllReduce: ") + nccl_->GetErrorString(r));
+    }
     SY_CUDA(cudaMemcpyAsync(last_grads_, grads_, sizeof(float) * n_params, cudaMemcpyDeviceToDevice, stream_));
     check_finite(grads_, n_params, d_flags_ + 1, stream_);
     abs_sum_partials(grads_, n_params, d_abs_, stream_);
@@ -639,10 +645,7 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
     for (int i = 0; i < kAbsSumBlocks; i++) abs_sum += h_abs_[i];
     int global_images = images;
     if (comm_) {
-        // one all-reduce for the gradient bucket, one for the scalars (sum): loss parts,
-        // positives, connected count, non-finite count, images
-        int r = nccl_->AllReduce(grads_, grads_, (size_t)n_params, kNcclFloat, kNcclSum, comm_, stream_);
-        if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllReduce: ") + nccl_->GetErrorString(r));
+        // scalars summed over ranks: loss parts, positives, connected count, non-finite count, images
         double* hs = reinterpret_cast<double*>(h_abs_);  // reuse pinned scratch (>= 8 doubles)
         hs[0] = box;
         hs[1] = cls;
@@ -653,7 +656,7 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
         hs[6] = images;
         double* ds = d_abs_;
         SY_CUDA(cudaMemcpyAsync(ds, hs, sizeof(double) * 7, cudaMemcpyHostToDevice, stream_));
-        r = nccl_->AllReduce(ds, ds, 7, kNcclDouble, kNcclSum, comm_, stream_);
+        int r = nccl_->AllReduce(ds, ds, 7, kNcclDouble, kNcclSum, comm_, stream_);
         if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllReduce: ") + nccl_->GetErrorString(r));
         SY_CUDA(cudaMemcpyAsync(hs, ds, sizeof(double) * 7, cudaMemcpyDeviceToHost, stream_));
         SY_CUDA(cudaStreamSynchronize(stream_));
@@ -664,6 +667,12 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
         connected = hs[4] > 0;
         finite = hs[5] == 0;
         global_images = (int)hs[6];
+        // the running-statistics fold below walks `images` images of every rank in rank order
+        if (global_images != images * cfg.world_size) {
+            SY_CUDA(cudaMemsetAsync(grads_, 0, sizeof(float) * n_params, stream_));
+            SY_CUDA(cudaStreamSynchronize(stream_));
+            throw SyError(SY_ERR_INVALID_ARGUMENT, "data-parallel ranks must step the same number of images");
+        }
     }
     if (!finite) {
         SY_CUDA(cudaMemsetAsync(grads_, 0, sizeof(float) * n_params, stream_));
