@@ -45,6 +45,8 @@ def parse():
     p.add_argument("--image", type=int, default=640)
     p.add_argument("--model", default="yolov8n")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--conv-sweep", action="store_true",
+                   help="config 1: time forward / dgrad / wgrad of the isolated head convs (one JSON line each)")
     return p.parse_args()
 
 
@@ -208,6 +210,64 @@ def run_reference(args, rank, world):
     return line
 
 
+# ---------------------------------------------------------------- config 1: isolated head-conv sweep
+
+# (name, ic, oc, H = W, k): 3x3 stride-1 pad-1 at P3/P4/P5 and the 1x1 box / cls convs per level
+CONV_SWEEP = [("P3 3x3 64->64", 64, 64, 80, 3), ("P4 3x3 128->64", 128, 64, 40, 3), ("P5 3x3 256->64", 256, 64, 20, 3),
+              ("P3 1x1 64->64", 64, 64, 80, 1), ("P3 1x1 64->80", 64, 80, 80, 1),
+              ("P4 1x1 64->64", 64, 64, 40, 1), ("P4 1x1 64->80", 64, 80, 40, 1),
+              ("P5 1x1 64->64", 64, 64, 20, 1), ("P5 1x1 64->80", 64, 80, 20, 1)]
+
+
+def oracle_conv_ms(ic, oc, hw, k, reps=2):
+    """Per-image ms of the reference's CPU conv (im2col + GEMM, restated in oracle/): forward,
+    weight gradient, data gradient (the backward with dx minus the one without)."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((ic, hw, hw)).astype(np.float32)
+    w = (rng.standard_normal((oc, ic, k, k)) * np.sqrt(2.0 / (ic * k * k))).astype(np.float32)
+    dy = rng.standard_normal((oc, hw, hw)).astype(np.float32)
+
+    def best(fn):
+        t = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            t.append(time.perf_counter() - t0)
+        return 1000.0 * min(t)
+    fwd = best(lambda: O.conv_forward(x, w))
+    wgrad = best(lambda: O.conv_backward(x, w, dy, with_dx=False))
+    both = best(lambda: O.conv_backward(x, w, dy, with_dx=True))
+    return fwd, wgrad, max(both - wgrad, 0.0)
+
+
+def run_conv_sweep(args):
+    import simdyolo_b200 as sy
+    peaks, src = measured_peaks()
+    tf32_peak = peaks["bf16_tflops"] / 2.0
+    n = args.batch
+    threads = cpu_threads()
+    for name, ic, oc, hw, k in CONV_SWEEP:
+        cpu = oracle_conv_ms(ic, oc, hw, k)
+        for kind, pas in enumerate(("fwd", "dgrad", "wgrad")):
+            ms = sy.bench_conv(kind, n, ic, oc, hw, hw, k, iters=20)
+            flops = 2.0 * n * oc * ic * k * k * hw * hw
+            tflops = flops / (ms / 1000.0) / 1e12
+            cpu_ms = cpu[kind] * n
+            print(json.dumps({
+                "metric": "head conv pass TFLOP/s", "value": tflops, "unit": "TFLOP/s", "n_gpus": 1,
+                "higher_is_better": True, "dtype": "tf32", "data": "synthetic", "ms_per_launch": ms,
+                "config": {"workload": "config 1: isolated head conv, N=%d, FP32 in / TF32 tensor cores" % n,
+                           "conv": name, "pass": pas, "n": n, "ic": ic, "oc": oc, "hw": hw, "k": k},
+                "roofline": {"bound": "tensor", "achieved": tflops, "peak": tf32_peak, "unit": "TFLOP/s",
+                             "frac": tflops / tf32_peak,
+                             "peak_note": f"dense TF32 = 1/2 of the {src} bf16 GEMM rate"},
+                "cpu_baseline": {"value": flops / (cpu_ms / 1000.0) / 1e12, "unit": "TFLOP/s", "cores": threads,
+                                 "kind": "port", "ms": cpu_ms,
+                                 "sample": "one image through the oracle's im2col + GEMM conv, scaled by N"},
+            }), flush=True)
+
+
 # ---------------------------------------------------------------- our arm
 
 def run_ours(args, rank, world, local_rank, dist):
@@ -309,6 +369,10 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.conv_sweep:
+        if rank == 0:
+            run_conv_sweep(args)
+        return
     if args.impl == "reference":
         # the reference is a single-process CPU trainer: rank 0 runs it, other ranks exit at once
         line = run_reference(args, rank, world)

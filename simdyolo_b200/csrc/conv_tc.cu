@@ -68,16 +68,38 @@ static int num_sms() {
 }
 
 // ------------------------------------------------------------------ forward / dgrad kernel
+// A CTA tile is T consecutive 128-row sub-tiles (M = 128 T output rows).  The taps are split into
+// groups whose row shifts lie close together (one group for a stride-1 conv; one per parity plane
+// for a stride-2 conv).  For each 32-channel chunk and group, one haloed A region
+//   rows [m0 + lo_g, m0 + lo_g + 128 T + span_g)
+// is loaded with 64-row TMA boxes, and every tap of the group reads it at its own row offset: the
+// MMA descriptor start moves by whole 128-byte rows, which the SWIZZLE_128B layout allows because
+// both TMA and the tensor core swizzle on absolute shared-memory address bits.  Each input row is
+// then fetched (128 T + span) / (128 T) times instead of once per tap.  Weights stay resident in
+// shared memory when they fit, else they stream per (tap, chunk) through their own ring.
+constexpr int kMaxGroups = 4;
+constexpr int kBoxRows = 64;                 // rows per A TMA box (8 KB)
+
 struct FwdParams {
-    int num_tiles;
-    int taps, kchunks, kpad;
-    int shift[9];
+    int num_tiles;       // CTA tiles of 128 T rows
+    int sub_tiles;       // 128-row sub-tiles of output in total
+    int T;
+    int kchunks, kpad;
+    int ngroups;
+    int g_lo[kMaxGroups];      // first A row of the group's region, relative to the tile's first row
+    int g_boxes[kMaxGroups];   // 64-row boxes loaded per region
+    int g_ntaps[kMaxGroups];
+    int tap_t[9];              // weight tap of the j-th tap (group order)
+    int tap_off[9];            // A row offset of the j-th tap inside its group's region
+    int taps;
     int n;          // MMA N (multiple of 16, <= 256)
     int n_valid;    // channels stored
     int n0;         // first weight row of this launch
-    int stages;
-    int nacc;       // TMEM accumulator stages (2..8)
-    int acc_cols;   // TMEM columns per accumulator
+    int a_stages, a_stage_bytes;
+    int b_stages;   // 0: all weights resident
+    int b_region_bytes;
+    int nacc;       // TMEM accumulator stages
+    int acc_cols;   // TMEM columns per sub-tile accumulator
     int alloc_cols;
     float* out;
     int out_pitch;
@@ -99,7 +121,6 @@ struct FwdParams {
 constexpr int kFwdThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int kEpiThreads = 256;
 constexpr int kTileM = 128;
-constexpr int kABytes = kTileM * 128;  // 128 rows x 32 fp32
 
 __device__ __forceinline__ float silu_fast(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
@@ -108,20 +129,34 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                        const FwdParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int b_bytes = p.n * 128;
-    const int stage_bytes = (kABytes + b_bytes + 1023) & ~1023;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * stage_bytes);
-    uint64_t* empty = full + p.stages;
-    uint64_t* tfull = empty + p.stages;
+    const int b_bytes = p.n * 128;          // one (tap, chunk) weight block; multiple of 2048
+    uint8_t* a_ring = smem;
+    uint8_t* b_region = smem + p.a_stages * p.a_stage_bytes;
+    const bool resident = p.b_stages == 0;
+    const int nb = resident ? 1 : p.b_stages;
+    uint64_t* afull = reinterpret_cast<uint64_t*>(b_region + p.b_region_bytes);
+    uint64_t* aempty = afull + p.a_stages;
+    uint64_t* bfull = aempty + p.a_stages;
+    uint64_t* bempty = bfull + nb;
+    uint64_t* tfull = bempty + nb;
     uint64_t* tempty = tfull + p.nacc;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + p.nacc);
-    float* bias_s = reinterpret_cast<float*>(tmem_slot + 4);
+    int* tap_s = reinterpret_cast<int*>(tmem_slot + 4);     // [9] weight tap, [9] A row offset
+    float* bias_s = reinterpret_cast<float*>(tap_s + 20);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x < 9) {
+        tap_s[threadIdx.x] = p.tap_t[threadIdx.x];
+        tap_s[9 + threadIdx.x] = p.tap_off[threadIdx.x];
+    }
     if (threadIdx.x == 0) {
-        for (int s = 0; s < p.stages; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+        for (int s = 0; s < p.a_stages; s++) {
+            mbar_init(&afull[s], 1);
+            mbar_init(&aempty[s], 1);
+        }
+        for (int s = 0; s < nb; s++) {
+            mbar_init(&bfull[s], 1);
+            mbar_init(&bempty[s], 1);
         }
         for (int a = 0; a < p.nacc; a++) {
             mbar_init(&tfull[a], 1);
@@ -144,121 +179,186 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int kblocks = p.taps * p.kchunks;
-    const uint32_t tx_bytes = kABytes + b_bytes;
+    const int tile_rows = kTileM * p.T;
 
     if (warp == 0) {
         if (lane == 0) {
-            int it = 0;
             bool ok = true;
+            if (resident) {
+                mbar_arrive_expect_tx(&bfull[0], (uint32_t)(p.taps * p.kchunks * b_bytes));
+                for (int t = 0; t < p.taps; t++)
+                    for (int c = 0; c < p.kchunks; c++)
+                        tma_load_2d(b_region + (t * p.kchunks + c) * b_bytes, &tmB, &bfull[0], t * p.kpad + c * 32,
+                                    p.n0);
+            }
+            int ia = 0, ib = 0;
             for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-                const int m0 = tile * kTileM;
-                for (int kb = 0; kb < kblocks; kb++, it++) {
-                    const int s = it % p.stages;
-                    const uint32_t ph = (it / p.stages) & 1;
-                    if (!(ok = mbar_wait(&empty[s], ph ^ 1, p.err, 1))) break;
-                    const int t = kb / p.kchunks, c = kb - t * p.kchunks;
-                    uint8_t* sa = smem + s * stage_bytes;
-                    mbar_arrive_expect_tx(&full[s], tx_bytes);
-                    tma_load_2d(sa, &tmA, &full[s], c * 32, m0 + p.shift[t]);
-                    tma_load_2d(sa + kABytes, &tmB, &full[s], t * p.kpad + c * 32, p.n0);
+                const int m0 = tile * tile_rows;
+                for (int c = 0; ok && c < p.kchunks; c++) {
+                    int j = 0;
+                    for (int g = 0; ok && g < p.ngroups; g++) {
+                        const int sa = ia % p.a_stages;
+                        if (!(ok = mbar_wait(&aempty[sa], ((ia / p.a_stages) & 1) ^ 1, p.err, 1))) break;
+                        uint8_t* dst = a_ring + sa * p.a_stage_bytes;
+                        mbar_arrive_expect_tx(&afull[sa], (uint32_t)(p.g_boxes[g] * kBoxRows * 128));
+                        for (int bx = 0; bx < p.g_boxes[g]; bx++)
+                            tma_load_2d(dst + bx * kBoxRows * 128, &tmA, &afull[sa], c * 32,
+                                        m0 + p.g_lo[g] + bx * kBoxRows);
+                        ia++;
+                        if (!resident) {
+                            for (int e = 0; e < p.g_ntaps[g]; e++, j++, ib++) {
+                                const int sb = ib % p.b_stages;
+                                if (!(ok = mbar_wait(&bempty[sb], ((ib / p.b_stages) & 1) ^ 1, p.err, 1))) break;
+                                mbar_arrive_expect_tx(&bfull[sb], (uint32_t)b_bytes);
+                                tma_load_2d(b_region + sb * b_bytes, &tmB, &bfull[sb], tap_s[j] * p.kpad + c * 32,
+                                            p.n0);
+                            }
+                        }
+                    }
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t idesc = idesc_tf32(p.n, 0, 0);
-            int it = 0, local = 0;
             bool ok = true;
+            if (resident) {
+                ok = mbar_wait(&bfull[0], 0, p.err, 3);
+                tc_fence_after();
+            }
+            // Descriptors are linear in the start-address field (address >> 4, 14 bits, never
+            // carried out of within shared memory), so every operand descriptor below is a base
+            // descriptor plus a byte offset >> 4: 128-byte rows add 8, a 32-byte K step adds 2,
+            // a 128-row sub-tile adds 1024.
+            const uint64_t a_desc0 = smem_desc(smem_u32(a_ring), 16, 1024, kLayoutSw128);
+            const uint64_t b_desc0 = smem_desc(smem_u32(b_region), 16, 1024, kLayoutSw128);
+            const uint32_t a_stage16 = (uint32_t)p.a_stage_bytes >> 4, b_blk16 = (uint32_t)b_bytes >> 4;
+            const int T = p.T;
+            int ia = 0, ib = 0, local = 0;
             for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, local++) {
                 const int acc = local % p.nacc;
-                const uint32_t aph = (local / p.nacc) & 1;
-                if (!(ok = mbar_wait(&tempty[acc], aph ^ 1, p.err, 2))) break;
+                if (!(ok = mbar_wait(&tempty[acc], ((local / p.nacc) & 1) ^ 1, p.err, 2))) break;
                 tc_fence_after();
-                const uint32_t d = tmem_base + acc * p.acc_cols;
-                for (int kb = 0; kb < kblocks; kb++, it++) {
-                    const int s = it % p.stages;
-                    const uint32_t ph = (it / p.stages) & 1;
-                    if (!(ok = mbar_wait(&full[s], ph, p.err, 3))) break;
-                    tc_fence_after();
-                    const uint32_t a_addr = smem_u32(smem + s * stage_bytes);
-                    const uint32_t b_addr = a_addr + kABytes;
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        uint64_t ad = smem_desc(a_addr + k * 32, 16, 1024, kLayoutSw128);
-                        uint64_t bd = smem_desc(b_addr + k * 32, 16, 1024, kLayoutSw128);
-                        mma_tf32(d, ad, bd, idesc, (kb | k) != 0);
+                const uint32_t d = tmem_base + acc * T * p.acc_cols;
+                const int mt = min(T, p.sub_tiles - tile * T);
+                for (int c = 0; ok && c < p.kchunks; c++) {
+                    int j = 0;
+                    for (int g = 0; ok && g < p.ngroups; g++) {
+                        const int sa = ia % p.a_stages;
+                        if (!(ok = mbar_wait(&afull[sa], (ia / p.a_stages) & 1, p.err, 3))) break;
+                        tc_fence_after();
+                        const uint64_t a_st = a_desc0 + (uint64_t)(sa * a_stage16);
+                        const int jend = j + p.g_ntaps[g];
+                        for (; j < jend; j++) {
+                            uint64_t b_d;
+                            int sb = 0;
+                            if (resident) {
+                                b_d = b_desc0 + (uint64_t)((tap_s[j] * p.kchunks + c) * b_blk16);
+                            } else {
+                                sb = ib % p.b_stages;
+                                if (!(ok = mbar_wait(&bfull[sb], (ib / p.b_stages) & 1, p.err, 3))) break;
+                                tc_fence_after();
+                                b_d = b_desc0 + (uint64_t)(sb * b_blk16);
+                            }
+                            const uint64_t a_t = a_st + (uint64_t)(tap_s[9 + j] * 8);
+                            const uint32_t first = (c == 0 && j == 0) ? 0u : 1u;
+                            for (int i = 0; i < mt; i++) {
+                                const uint64_t a_i = a_t + (uint64_t)(i * 1024);
+                                const uint32_t d_i = d + i * p.acc_cols;
+                                mma_tf32(d_i, a_i, b_d, idesc, first);
+                                mma_tf32(d_i, a_i + 2, b_d + 2, idesc, 1u);
+                                mma_tf32(d_i, a_i + 4, b_d + 4, idesc, 1u);
+                                mma_tf32(d_i, a_i + 6, b_d + 6, idesc, 1u);
+                            }
+                            if (!resident) {
+                                mma_commit(&bempty[sb]);
+                                ib++;
+                            }
+                        }
+                        mma_commit(&aempty[sa]);
+                        ia++;
                     }
-                    mma_commit(&empty[s]);
                 }
                 mma_commit(&tfull[acc]);
             }
         }
     } else {
-        // two warps per TMEM lane quadrant; they take alternate 16-column chunks
+        // two warps per TMEM lane quadrant; they take alternate (sub-tile, 16-column chunk) items
         const int q = warp & 3;
         const int half = (warp - 2) >> 2;
-        const int row = q * 32 + lane;
+        const int nchunks = (p.n + 15) >> 4;
         int local = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
             const int acc = local % p.nacc;
-            const uint32_t aph = (local / p.nacc) & 1;
-            if (!mbar_wait(&tfull[acc], aph, p.err, 4)) break;
+            if (!mbar_wait(&tfull[acc], (local / p.nacc) & 1, p.err, 4)) break;
             tc_fence_after();
-            const long m = (long)tile * kTileM + row;
-            const long img = m / p.grid.rows;
-            const int r = (int)(m - img * p.grid.rows);
-            const bool inside = !p.mask || p.grid.interior(r);
-            float* orow = p.out + m * (long)p.out_pitch;
-            const float* rrow = p.residual ? p.residual + m * (long)p.res_pitch : nullptr;
-            // parity-split copy: padded pixel (py, px) -> plane (py&1, px&1), cell (py>>1, px>>1)
-            float* prow = nullptr;
-            if (p.phase && inside) {
-                const int py = r / p.grid.wp, px = r - py * p.grid.wp;
-                const long prow_index = ((py & 1) * 2 + (px & 1)) * p.phase_stride + img * p.phase_rows +
-                                        (long)(py >> 1) * p.phase_wp + (px >> 1);
-                prow = p.phase + prow_index * p.phase_pitch;
-            }
-            for (int j = half * 16; j < p.n; j += 32) {
+            const int mt = min(p.T, p.sub_tiles - tile * p.T);
+            for (int item = half; item < mt * nchunks; item += 2) {
+                const int i = item / nchunks;
+                const int j = (item - i * nchunks) * 16;
                 float v[16];
-                tmem_ld16(tmem_base + acc * p.acc_cols + ((uint32_t)(q * 32) << 16) + j, v);
+                tmem_ld16(tmem_base + (acc * p.T + i) * p.acc_cols + ((uint32_t)(q * 32) << 16) + j, v);
                 if (j >= p.n_valid) continue;
+                const long m = (long)tile * tile_rows + i * kTileM + q * 32 + lane;
+                const long img = m / p.grid.rows;
+                const int r = (int)(m - img * p.grid.rows);
+                const bool inside = !p.mask || p.grid.interior(r);
+                float* orow = p.out ? p.out + m * (long)p.out_pitch : nullptr;
+                const float* rrow = p.residual ? p.residual + m * (long)p.res_pitch : nullptr;
+                // parity-split copy: padded pixel (py, px) -> plane (py&1, px&1), cell (py>>1, px>>1)
+                float* prow = nullptr;
+                if (p.phase && inside) {
+                    const int py = r / p.grid.wp, px = r - py * p.grid.wp;
+                    const long prow_index = ((py & 1) * 2 + (px & 1)) * p.phase_stride + img * p.phase_rows +
+                                            (long)(py >> 1) * p.phase_wp + (px >> 1);
+                    prow = p.phase + prow_index * p.phase_pitch;
+                }
                 const bool full16 = j + 16 <= p.n_valid;
                 float res[16];
                 if (rrow && full16 && inside) {
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const float4 t = *reinterpret_cast<const float4*>(rrow + j + 4 * i);
-                        res[4 * i] = t.x;
-                        res[4 * i + 1] = t.y;
-                        res[4 * i + 2] = t.z;
-                        res[4 * i + 3] = t.w;
+                    for (int u = 0; u < 4; u++) {
+                        const float4 t = *reinterpret_cast<const float4*>(rrow + j + 4 * u);
+                        res[4 * u] = t.x;
+                        res[4 * u + 1] = t.y;
+                        res[4 * u + 2] = t.z;
+                        res[4 * u + 3] = t.w;
                     }
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 16; i++) res[i] = (rrow && inside && j + i < p.n_valid) ? rrow[j + i] : 0.0f;
+                    for (int u = 0; u < 16; u++) res[u] = (rrow && inside && j + u < p.n_valid) ? rrow[j + u] : 0.0f;
                 }
 #pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    float x = v[i] + bias_s[j + i];
+                for (int u = 0; u < 16; u++) {
+                    float x = v[u] + bias_s[j + u];
                     if (p.silu) x = silu_fast(x);
-                    x += res[i];
-                    v[i] = inside ? x : 0.0f;
+                    x += res[u];
+                    v[u] = inside ? x : 0.0f;
                 }
                 if (full16) {
-                    float4* dst = reinterpret_cast<float4*>(orow + j);
+                    if (orow) {
+                        float4* dst = reinterpret_cast<float4*>(orow + j);
 #pragma unroll
-                    for (int i = 0; i < 4; i++) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                        for (int u = 0; u < 4; u++)
+                            dst[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                    }
                     if (prow) {
                         float4* pd = reinterpret_cast<float4*>(prow + j);
 #pragma unroll
-                        for (int i = 0; i < 4; i++)
-                            pd[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                        for (int u = 0; u < 4; u++)
+                            pd[u] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
                     }
                 } else {
-                    for (int i = 0; i < 16 && j + i < p.n_valid; i++) orow[j + i] = v[i];
-                    if (prow)
-                        for (int i = 0; i < 16 && j + i < p.n_valid; i++) prow[j + i] = v[i];
+                    if (orow) {
+#pragma unroll
+                        for (int u = 0; u < 16; u++)
+                            if (j + u < p.n_valid) orow[j + u] = v[u];
+                    }
+                    if (prow) {
+#pragma unroll
+                        for (int u = 0; u < 16; u++)
+                            if (j + u < p.n_valid) prow[j + u] = v[u];
+                    }
                 }
             }
             tc_fence_before();
@@ -278,7 +378,7 @@ static int pow2_at_least(int v) {
     return r;
 }
 
-// Shared launcher: `m_rows` output rows (tiles of 128), A rows read at m + shift[t].
+// Shared launcher: `m_rows` output rows (multiple of 128), A rows read at m + shift[t].
 static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, const float* wk, int n_rows, int n_out,
                        const Grid& grid, const View& out, const ConvEpilogue& ep, const PhaseOut* phase, int* err,
                        cudaStream_t stream) {
@@ -288,31 +388,107 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         throw std::runtime_error("conv_tc: output not 16-byte aligned");
     if (phase && ((phase->pitch % 4) != 0 || (reinterpret_cast<uintptr_t>(phase->base) & 15) != 0))
         throw std::runtime_error("conv_tc: parity copy not 16-byte aligned");
-    CUtensorMap ta = make_map_2d(in.base, in.channels, in.rows, in.pitch, 32, kTileM);
+    if (taps < 1 || taps > 9) throw std::runtime_error("conv_tc: taps");
+    // tap groups: taps sorted by shift, a new group wherever consecutive shifts are more than `gap`
+    // rows apart.  With gap = wp + 2 a stride-1 3x3 conv is one group (its consecutive shifts differ
+    // by 1 or wp - 2) and a stride-2 conv one group per parity plane (planes lie at least
+    // rows-per-image - wp - 1 > wp + 2 rows apart); if that haloed region does not fit, gap = 2 puts
+    // every kernel row in a group of its own.
+    int order[9];
+    for (int t = 0; t < taps; t++) order[t] = t;
+    std::sort(order, order + taps, [&](int a, int b) { return shift[a] < shift[b] || (shift[a] == shift[b] && a < b); });
+    const long sub_tiles = m_rows / kTileM;
     static bool attr_set = false;
     if (!attr_set) {
         cudaFuncSetAttribute(conv_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         attr_set = true;
     }
+    CUtensorMap ta = make_map_2d(in.base, in.channels, in.rows, in.pitch, 32, kBoxRows);
+    constexpr int kSmemBudget = 216 * 1024;
     for (int n0 = 0; n0 < n_out; n0 += 256) {
         const int n_valid = std::min(256, n_out - n0);
         const int n = (n_valid + 15) / 16 * 16;
-        CUtensorMap tb = make_map_2d(wk, (long)taps * kpad, n_rows, (long)taps * kpad, 32, n);
+        const int b_bytes = n * 128;
+        const int acc_cols = pow2_at_least(n);
+        const int res_bytes = taps * kchunks * b_bytes;
+        const bool resident = res_bytes <= 72 * 1024;
+        const int b_min = resident ? res_bytes : 2 * b_bytes;
+        int ngroups = 0, g_lo[kMaxGroups], g_span[kMaxGroups], g_ntaps[kMaxGroups], tap_t[9], tap_off[9];
+        int T = 0, a_stage = 0;
+        auto stage_bytes = [&](int t_sub) {
+            int rows = 0;
+            for (int g = 0; g < ngroups; g++) rows = std::max(rows, kTileM * t_sub + g_span[g]);
+            return (rows + kBoxRows - 1) / kBoxRows * kBoxRows * 128;
+        };
+        for (int gap : {grid.wp + 2, 2}) {
+            ngroups = 0;
+            bool too_many = false;
+            for (int e = 0; e < taps; e++) {
+                const int t = order[e];
+                if (e == 0 || shift[t] - shift[order[e - 1]] > gap) {
+                    if (ngroups == kMaxGroups) {
+                        too_many = true;
+                        break;
+                    }
+                    g_lo[ngroups] = shift[t];
+                    g_span[ngroups] = 0;
+                    g_ntaps[ngroups] = 0;
+                    ngroups++;
+                }
+                const int g = ngroups - 1;
+                tap_t[e] = t;
+                tap_off[e] = shift[t] - g_lo[g];
+                g_span[g] = tap_off[e];
+                g_ntaps[g]++;
+            }
+            if (too_many) continue;
+            // largest sub-tile count whose accumulators double-buffer in TMEM, whose A region fits
+            // twice next to the weights, and that still leaves two tiles per SM
+            T = 4;
+            while (T > 1 && (2 * T * acc_cols > 512 || 2 * stage_bytes(T) + b_min > kSmemBudget ||
+                             (sub_tiles + T - 1) / T < 2L * num_sms()))
+                T >>= 1;
+            a_stage = stage_bytes(T);
+            if (2 * a_stage + b_min <= kSmemBudget) break;
+            T = 0;
+        }
+        if (T == 0) throw std::runtime_error("conv_tc: haloed tile does not fit shared memory");
         FwdParams p;
-        p.num_tiles = (int)(m_rows / kTileM);
-        p.taps = taps;
+        p.T = T;
+        p.sub_tiles = (int)sub_tiles;
+        p.num_tiles = (int)((sub_tiles + T - 1) / T);
         p.kchunks = kchunks;
         p.kpad = kpad;
-        for (int t = 0; t < 9; t++) p.shift[t] = t < taps ? shift[t] : 0;
+        p.ngroups = ngroups;
+        for (int g = 0; g < kMaxGroups; g++) {
+            p.g_lo[g] = g < ngroups ? g_lo[g] : 0;
+            p.g_boxes[g] = g < ngroups ? (kTileM * T + g_span[g] + kBoxRows - 1) / kBoxRows : 0;
+            p.g_ntaps[g] = g < ngroups ? g_ntaps[g] : 0;
+        }
+        for (int e = 0; e < 9; e++) {
+            p.tap_t[e] = e < taps ? tap_t[e] : 0;
+            p.tap_off[e] = e < taps ? tap_off[e] : 0;
+        }
+        p.taps = taps;
         p.n = n;
         p.n_valid = n_valid;
         p.n0 = n0;
-        const int stage_bytes = (kABytes + n * 128 + 1023) & ~1023;
-        p.stages = std::min(8, (int)((220 * 1024) / stage_bytes));
-        p.acc_cols = pow2_at_least(n);
-        p.nacc = std::max(2, std::min(8, 512 / p.acc_cols));
-        p.alloc_cols = p.nacc * p.acc_cols;
-        p.out = out.base + n0;
+        p.a_stage_bytes = a_stage;
+        // Streamed weights: a (tap, chunk) block feeds only T x 4 MMAs, so the weight ring gets the
+        // depth (up to 16 blocks) and the A ring two regions (each feeds a whole tap group).
+        if (resident) {
+            p.a_stages = std::min(4, (kSmemBudget - res_bytes) / a_stage);
+            p.b_stages = 0;
+            p.b_region_bytes = res_bytes;
+        } else {
+            p.a_stages = 2;
+            p.b_stages = std::min(16, (kSmemBudget - 2 * a_stage) / b_bytes);
+            p.b_region_bytes = p.b_stages * b_bytes;
+        }
+        p.acc_cols = acc_cols;
+        p.nacc = std::max(2, std::min(8, 512 / (T * acc_cols)));
+        p.alloc_cols = pow2_at_least(p.nacc * T * acc_cols);
+        p.out = out.base ? out.base + n0 : nullptr;   // null: only the parity copy is written
         p.out_pitch = out.pitch;
         p.bias = ep.bias;
         p.residual = ep.residual ? ep.residual + n0 : nullptr;
@@ -326,7 +502,12 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         p.phase_rows = phase ? phase->consumer.rows : 0;
         p.phase_stride = phase ? phase->plane_rows : 0;
         p.err = err;
-        const size_t smem = 1024 + (size_t)p.stages * stage_bytes + (2 * p.stages + 2 * p.nacc) * 8 + 16 + n * 4;
+        if (p.alloc_cols > 512) throw std::runtime_error("conv_tc: TMEM columns");
+        CUtensorMap tb = make_map_2d(wk, (long)taps * kpad, n_rows, (long)taps * kpad, 32, n);
+        const int nb = resident ? 1 : p.b_stages;
+        const size_t smem = 1024 + (size_t)p.a_stages * a_stage + p.b_region_bytes +
+                            (2 * p.a_stages + 2 * nb + 2 * p.nacc) * 8 + 16 + 80 + n * 4;
+        if (smem > 227 * 1024) throw std::runtime_error("conv_tc: shared memory");
         const int grid_x = std::min(p.num_tiles, num_sms());
         conv_fwd_tc_kernel<<<grid_x, kFwdThreads, smem, stream>>>(ta, tb, p);
         launch_check("conv_fwd_tc_kernel");

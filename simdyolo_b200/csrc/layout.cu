@@ -153,15 +153,29 @@ __global__ void upsample2_kernel(const float* in, int in_pitch, Grid gin, float*
 // Identity-scale letterbox written straight into the stem's parity-split input (PhaseOut layout),
 // 4 floats per pixel (r, g, b, 0).
 // One thread per output pixel of the stem: 27 inputs (u8 / 255) x OC outputs, bias, SiLU.
+// x / 255 correctly rounded for an integer x in [0, 255]: the product with the rounded reciprocal
+// is within one unit in the last place, and one FMA residual step (Markstein's correction) rounds
+// it to the IEEE quotient; checked against IEEE division for every byte value.
+__device__ __forceinline__ float byte_over_255(uint32_t v) {
+    const float x = (float)v;
+    const float r = 1.0f / 255.0f;
+    const float q = __fmul_rn(x, r);
+    const float e = __fmaf_rn(-q, 255.0f, x);
+    return __fmaf_rn(e, r, q);
+}
+
+// Stem weights by value: kernel parameters live in the constant bank, so every FMA below takes
+// its weight as a constant operand (no shared-memory traffic).
 template <int OC>
-__global__ void __launch_bounds__(256) stem_conv_kernel(const uint8_t* rgb, int batch, int size, const float* w,
-                                                        const float* bias, float* out, int out_pitch, Grid gout,
-                                                        PhaseOut phase, int has_phase) {
-    __shared__ float ws[OC * 27];
-    __shared__ float bs[OC];
-    for (int i = threadIdx.x; i < OC * 27; i += blockDim.x) ws[i] = w[i];
-    for (int i = threadIdx.x; i < OC; i += blockDim.x) bs[i] = bias[i];
-    __syncthreads();
+struct StemParams {
+    float w[OC * 27];   // OIHW [oc][3][3][3]
+    float b[OC];
+};
+
+template <int OC>
+__global__ void __launch_bounds__(256) stem_conv_kernel(const uint8_t* rgb, int batch, int size,
+                                                        const StemParams<OC> sp, float* out, int out_pitch,
+                                                        Grid gout, PhaseOut phase, int has_phase) {
     const int ho = gout.h, wo = gout.w;
     const long total = (long)batch * ho * wo;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
@@ -177,20 +191,22 @@ __global__ void __launch_bounds__(256) stem_conv_kernel(const uint8_t* rgb, int 
                 const bool ok = iy >= 0 && iy < size && ix >= 0 && ix < size;
                 const uint8_t* p = rgb + (((long)b * size + (ok ? iy : 0)) * size + (ok ? ix : 0)) * 3;
 #pragma unroll
-                for (int c = 0; c < 3; c++) in[c * 9 + ky * 3 + kx] = ok ? __fdiv_rn((float)p[c], 255.0f) : 0.0f;
+                for (int c = 0; c < 3; c++) in[c * 9 + ky * 3 + kx] = ok ? byte_over_255(p[c]) : 0.0f;
             }
         float acc[OC];
 #pragma unroll
         for (int o = 0; o < OC; o++) {
             float s = 0.0f;
 #pragma unroll
-            for (int q = 0; q < 27; q++) s = fmaf(ws[o * 27 + q], in[q], s);
-            acc[o] = silu_f(s + bs[o]);
+            for (int q = 0; q < 27; q++) s = fmaf(sp.w[o * 27 + q], in[q], s);
+            acc[o] = silu_f(s + sp.b[o]);
         }
-        float* dst = out + ((long)b * gout.rows + gout.row(oy, ox)) * out_pitch;
+        if (out) {
+            float* dst = out + ((long)b * gout.rows + gout.row(oy, ox)) * out_pitch;
 #pragma unroll
-        for (int o = 0; o < OC; o += 4)
-            *reinterpret_cast<float4*>(dst + o) = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
+            for (int o = 0; o < OC; o += 4)
+                *reinterpret_cast<float4*>(dst + o) = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
+        }
         if (has_phase) {
             const int py = oy + 1, px = ox + 1;
             float* pd = phase.base + (((py & 1) * 2 + (px & 1)) * phase.plane_rows + (long)b * phase.consumer.rows +
@@ -289,19 +305,29 @@ void upsample2_padded(const View& in, const Grid& gin, const View& out, const Gr
     launch_check("upsample2_kernel");
 }
 
-void stem_conv(const uint8_t* rgb, int batch, int size, const float* w, const float* bias, int oc, const View& out,
-               const Grid& gout, const PhaseOut* phase, cudaStream_t stream) {
+template <int OC>
+static void launch_stem(const uint8_t* rgb, int batch, int size, const float* w_host, const float* b_host,
+                        const View& out, const Grid& gout, const PhaseOut& ph, int hp, int blocks, cudaStream_t stream) {
+    StemParams<OC> sp;
+    for (int i = 0; i < OC * 27; i++) sp.w[i] = w_host[i];
+    for (int i = 0; i < OC; i++) sp.b[i] = b_host[i];
+    stem_conv_kernel<OC><<<blocks, 256, 0, stream>>>(rgb, batch, size, sp, out.base, out.pitch, gout, ph, hp);
+}
+
+void stem_conv(const uint8_t* rgb, int batch, int size, const float* w_host, const float* bias_host, int oc,
+               const View& out, const Grid& gout, const PhaseOut* phase, cudaStream_t stream) {
     if (out.pitch % 4 != 0 || (phase && phase->pitch % 4 != 0))
         throw std::runtime_error("stem_conv: pitches must be multiples of 4");
+    if (!out.base && !phase) throw std::runtime_error("stem_conv: no output");
     const long n = (long)batch * gout.h * gout.w;
     const int blocks = (int)std::min<long>(148L * 8, std::max<long>(1, (n + 255) / 256));
     const PhaseOut ph = phase ? *phase : PhaseOut{};
     const int hp = phase ? 1 : 0;
     switch (oc) {
-        case 16: stem_conv_kernel<16><<<blocks, 256, 0, stream>>>(rgb, batch, size, w, bias, out.base, out.pitch, gout, ph, hp); break;
-        case 32: stem_conv_kernel<32><<<blocks, 256, 0, stream>>>(rgb, batch, size, w, bias, out.base, out.pitch, gout, ph, hp); break;
-        case 48: stem_conv_kernel<48><<<blocks, 256, 0, stream>>>(rgb, batch, size, w, bias, out.base, out.pitch, gout, ph, hp); break;
-        case 64: stem_conv_kernel<64><<<blocks, 256, 0, stream>>>(rgb, batch, size, w, bias, out.base, out.pitch, gout, ph, hp); break;
+        case 16: launch_stem<16>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream); break;
+        case 32: launch_stem<32>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream); break;
+        case 48: launch_stem<48>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream); break;
+        case 64: launch_stem<64>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream); break;
         default: throw std::runtime_error("stem_conv: output channels must be 16, 32, 48 or 64");
     }
     launch_check("stem_conv_kernel");

@@ -302,6 +302,26 @@ void Session::build_backbone() {
     feat_ch_[0] = c256;
     feat_ch_[1] = c512;
     feat_ch_[2] = c1024;
+    // A conv whose output is read only through its parity-split copy (by stride-2 convs) skips the
+    // plain write: no other op's input or residual, and no feature map, overlaps that output.
+    auto span_of = [](const View& v) {
+        return std::make_pair(v.base, v.base + (v.rows > 0 ? (v.rows - 1) * (long)v.pitch + v.channels : 0));
+    };
+    auto overlaps = [&](const View& a, const View& b) {
+        const auto x = span_of(a), y = span_of(b);
+        return x.first < y.second && y.first < x.second;
+    };
+    for (auto& op : bops_) {
+        if (op.type != 0 || !op.has_phase_out) continue;
+        bool read = false;
+        for (const auto& q : bops_) {
+            if (&q == &op) continue;
+            if (q.type != 0 || q.stride == 1) read |= overlaps(q.in, op.out);
+            if (q.type == 0 && q.has_res) read |= overlaps(q.res, op.out);
+        }
+        for (int l = 0; l < 3; l++) read |= overlaps(features_[l], op.out);
+        op.plain_out = read;
+    }
     n_backbone = poff;
     backbone_params_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)poff));
     for (auto& op : bops_) {
@@ -317,6 +337,10 @@ int Session::set_backbone(const float* host, long count) {
     SY_CUDA(cudaMemcpyAsync(backbone_params_, host, sizeof(float) * count, cudaMemcpyHostToDevice, stream_));
     for (auto& op : bops_) {
         if (op.type != 0) continue;
+        if (op.in.base == img_.base) {
+            stem_host_.assign(host + op.w_off, host + op.w_off + (long)op.oc * op.ic * 9);
+            stem_host_.insert(stem_host_.end(), host + op.b_off, host + op.b_off + op.oc);
+        }
         const int taps = op.k * op.k;
         weights_fwd_layout(backbone_params_ + op.w_off, op.oc, op.ic, taps, round_up(op.ic, 32), op.wk, stream_);
     }
@@ -328,9 +352,10 @@ int Session::set_backbone(const float* host, long count) {
 void Session::forward_backbone(int batch, const uint8_t* rgb_device) {
     for (auto& op : bops_) {
         View in = op.in, out = op.out;
+        if (op.type == 0 && !op.plain_out) out.base = nullptr;
         if (op.type == 0 && in.base == img_.base) {
-            stem_conv(rgb_device, batch, cfg.image_size, backbone_params_ + op.w_off, backbone_params_ + op.b_off, op.oc,
-                      out, op.gout, op.has_phase_out ? &op.phase_out : nullptr, stream_);
+            stem_conv(rgb_device, batch, cfg.image_size, stem_host_.data(), stem_host_.data() + (long)op.oc * op.ic * 9,
+                      op.oc, out, op.gout, op.has_phase_out ? &op.phase_out : nullptr, stream_);
         } else if (op.type == 1) {
             maxpool5_padded(in, out, batch, op.gin, stream_);
         } else if (op.type == 2) {

@@ -59,6 +59,7 @@ struct BackboneOp {
     long phase_plane_rows = 0;
     bool has_phase_out = false; // this conv's output feeds a stride-2 conv
     PhaseOut phase_out{};
+    bool plain_out = true;      // false: only stride-2 convs read the output, so only the copy is written
 };
 
 struct NcclApi;
@@ -107,6 +108,7 @@ private:
     // backbone
     std::vector<BackboneOp> bops_;
     float* backbone_params_ = nullptr;
+    std::vector<float> stem_host_;   // stem weights then bias (OIHW), host copy for the kernel parameters
     uint8_t* d_rgb_ = nullptr;
     uint8_t* h_rgb_ = nullptr;   // pinned staging
     View img_{};
