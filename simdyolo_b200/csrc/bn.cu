@@ -4,10 +4,12 @@
 // gradient of the final conv (HeadOperations.cs:66).
 //
 // Each image normalises with its own mean / variance over H x W, exactly like the reference's
-// batch-of-one convs, so a batch of B images needs B x C statistics.  Reductions split every
-// (image, channel group) over several blocks of pixels; each block writes (count, mean, M2) or plain
-// sums and a second kernel folds the splits in a fixed order (Chan's pairwise variance update), so
-// results do not depend on timing.  Elementwise passes move float4s and do one division per row.
+// batch-of-one convs, so a batch of B images needs B x C statistics.  The reductions happen in the
+// epilogue of the conv that produces the data (forward: the conv output y; backward: the data
+// gradient g of the next conv), which writes partials per 32-row group; the fold kernels here
+// combine every (image, channel)'s groups in a fixed order (Chan's pairwise variance update for the
+// statistics), so results do not depend on timing.  The apply passes stream float4s with
+// per-(image, channel) coefficients prepared by the folds.
 #include <algorithm>
 #include <stdexcept>
 #include <string>
@@ -42,169 +44,114 @@ __device__ __forceinline__ void split_range(int pixels, int splits, int s, int& 
     p1 = (int)((long)pixels * (s + 1) / splits);
 }
 
-// Partial (count, mean, M2) of one (image, 32 channels, pixel split): two passes over the split.
-__global__ void __launch_bounds__(kThreads) bn_stats_partial_kernel(const float* y, int pitch, int c, Grid g,
-                                                                    int splits, float* part) {
-    __shared__ float red[kWarps][32];
-    __shared__ float mean_s[32];
+// Fold the (count, mean, M2) partials of every (image, channel) over its row groups: block
+// (32 channels, image), warp w takes groups w, w + 8, ...; pass 1 sums count and count * mean, pass 2
+// sums M2_q + n_q (mean_q - mean)^2 (the exact pooled-variance identity), both in double, and the
+// eight warps' sums are added in warp order, so the result is deterministic.
+constexpr int kFoldWarps = 8;
+__global__ void __launch_bounds__(kFoldWarps * 32) bn_stats_fold_kernel(const float* part, int c, int groups,
+                                                                        float eps, float* stats, float* mean_p,
+                                                                        float* inv_p) {
+    __shared__ double r1[kFoldWarps][32], r2[kFoldWarps][32];
+    __shared__ double mean_s[32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int ch = blockIdx.x * 32 + lane, b = blockIdx.y, s = blockIdx.z;
-    int p0, p1;
-    split_range(g.h * g.w, splits, s, p0, p1);
-    const float* base = y + (long)b * g.rows * pitch + ch;
+    const int ch = blockIdx.x * 32 + lane, b = blockIdx.y;
     const bool on = ch < c;
-    float acc = 0.0f;
+    const float* pb = part + (long)b * groups * c * 3;
+    double n = 0.0, sum = 0.0;
     if (on)
-        for (int p = p0 + warp; p < p1; p += kWarps) {
-            const int yy = p / g.w, xx = p - yy * g.w;
-            acc += base[(long)g.row(yy, xx) * pitch];
+        for (int q = warp; q < groups; q += kFoldWarps) {
+            const float* o = pb + ((long)q * c + ch) * 3;
+            n += o[0];
+            sum += (double)o[0] * o[1];
         }
-    red[warp][lane] = acc;
+    r1[warp][lane] = n;
+    r2[warp][lane] = sum;
     __syncthreads();
-    const int n = p1 - p0;
     if (warp == 0) {
-        float t = 0.0f;
-        for (int w = 0; w < kWarps; w++) t += red[w][lane];
-        mean_s[lane] = n > 0 ? t / n : 0.0f;
+        double tn = 0.0, ts = 0.0;
+        for (int w = 0; w < kFoldWarps; w++) {
+            tn += r1[w][lane];
+            ts += r2[w][lane];
+        }
+        mean_s[lane] = tn > 0.0 ? ts / tn : 0.0;
+        r1[0][lane] = tn;
     }
     __syncthreads();
-    const float mean = mean_s[lane];
-    float m2 = 0.0f;
+    const double mean = mean_s[lane], ntot = r1[0][lane];
+    __syncthreads();
+    double m2 = 0.0;
     if (on)
-        for (int p = p0 + warp; p < p1; p += kWarps) {
-            const int yy = p / g.w, xx = p - yy * g.w;
-            const float d = base[(long)g.row(yy, xx) * pitch] - mean;
-            m2 += d * d;
+        for (int q = warp; q < groups; q += kFoldWarps) {
+            const float* o = pb + ((long)q * c + ch) * 3;
+            const double d = (double)o[1] - mean;
+            m2 += (double)o[2] + (double)o[0] * d * d;
         }
-    red[warp][lane] = m2;
+    r2[warp][lane] = m2;
     __syncthreads();
     if (warp == 0 && on) {
-        float t = 0.0f;
-        for (int w = 0; w < kWarps; w++) t += red[w][lane];
-        float* o = part + (((long)b * splits + s) * c + ch) * 3;
-        o[0] = (float)n;
-        o[1] = mean;
-        o[2] = t;
+        double t = 0.0;
+        for (int w = 0; w < kFoldWarps; w++) t += r2[w][lane];
+        const long i = (long)b * c + ch;
+        const float mf = (float)mean, var = (float)(ntot > 0.0 ? t / ntot : 0.0);
+        stats[i * 2 + 0] = mf;
+        stats[i * 2 + 1] = var;
+        mean_p[i] = mf;
+        inv_p[i] = 1.0f / sqrtf(var + eps);
     }
 }
 
-// Fold the splits of every (image, channel) in order; stats = (mean, biased variance).
-__global__ void bn_stats_final_kernel(const float* part, int batch, int c, int splits, float* stats) {
-    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= (long)batch * c) return;
-    const int b = (int)(i / c), ch = (int)(i - (long)b * c);
-    double n = 0.0, mean = 0.0, m2 = 0.0;
-    for (int s = 0; s < splits; s++) {
-        const float* o = part + (((long)b * splits + s) * c + ch) * 3;
-        const double nb = o[0];
-        if (nb == 0.0) continue;
-        const double delta = (double)o[1] - mean, tot = n + nb;
-        mean += delta * nb / tot;
-        m2 += (double)o[2] + delta * delta * n * nb / tot;
-        n = tot;
-    }
-    stats[i * 2 + 0] = (float)mean;
-    stats[i * 2 + 1] = (float)(n > 0 ? m2 / n : 0.0);
-}
-
-// a = SiLU(gamma * (y - mean) * inv + beta) on interior rows, zero on halo / tail rows.
+// a = SiLU(gamma * (y - mean) * inv + beta) on interior rows, zero on halo / tail rows; one image per
+// blockIdx.y.
 template <bool kVec>
-__global__ void bn_apply_kernel(const float* y, int ypitch, const float* stats, const float* gamma, const float* beta,
-                                float eps, int c, long rows, Grid g, float* a, int apitch) {
+__global__ void bn_apply_kernel(const float* y, int ypitch, const float* mean_p, const float* inv_p,
+                                const float* gamma, const float* beta, int c, Grid g, float* a, int apitch) {
+    const int b = blockIdx.y;
     const int per_row = kVec ? c / 4 : c;
-    const long total = rows * per_row;
+    const long total = (long)g.rows * per_row;
+    const long base = (long)b * g.rows;
+    const float* mb = mean_p + (long)b * c;
+    const float* ib = inv_p + (long)b * c;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const long row = i / per_row;
-        const int j = (int)(i - row * per_row);
-        const int b = (int)(row / g.rows), r = (int)(row - (long)b * g.rows);
+        const int r = (int)(i / per_row), j = (int)(i - (long)r * per_row);
+        const long row = base + r;
         const bool in = g.interior(r);
         if (kVec) {
             float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
             if (in) {
                 const float4 v = *reinterpret_cast<const float4*>(y + row * ypitch + 4 * j);
-                float o[4];
-                const float vi[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const int ch = 4 * j + k;
-                    const float mean = stats[((long)b * c + ch) * 2], var = stats[((long)b * c + ch) * 2 + 1];
-                    const float inv = 1.0f / sqrtf(var + eps);
-                    o[k] = silu_f((vi[k] - mean) * inv * gamma[ch] + beta[ch]);
-                }
-                out = make_float4(o[0], o[1], o[2], o[3]);
+                const float4 mv = *reinterpret_cast<const float4*>(mb + 4 * j);
+                const float4 iv = *reinterpret_cast<const float4*>(ib + 4 * j);
+                const int ch = 4 * j;
+                out.x = silu_f((v.x - mv.x) * iv.x * gamma[ch] + beta[ch]);
+                out.y = silu_f((v.y - mv.y) * iv.y * gamma[ch + 1] + beta[ch + 1]);
+                out.z = silu_f((v.z - mv.z) * iv.z * gamma[ch + 2] + beta[ch + 2]);
+                out.w = silu_f((v.w - mv.w) * iv.w * gamma[ch + 3] + beta[ch + 3]);
             }
             *reinterpret_cast<float4*>(a + row * apitch + 4 * j) = out;
         } else {
             float out = 0.0f;
-            if (in) {
-                const float mean = stats[((long)b * c + j) * 2], var = stats[((long)b * c + j) * 2 + 1];
-                const float inv = 1.0f / sqrtf(var + eps);
-                out = silu_f((y[row * ypitch + j] - mean) * inv * gamma[j] + beta[j]);
-            }
+            if (in) out = silu_f((y[row * ypitch + j] - mb[j]) * ib[j] * gamma[j] + beta[j]);
             a[row * apitch + j] = out;
         }
     }
 }
 
-__device__ __forceinline__ float bn_dz(float yv, float gv, float mean, float inv, float ga, float be, float& xh) {
-    xh = (yv - mean) * inv;
-    const float z = xh * ga + be;
-    const float sg = 1.0f / (1.0f + __expf(-z));
-    return gv * (sg + z * sg * (1.0f - sg));
-}
-
-// Partial sums of dz and dz * xhat for one (image, 32 channels, pixel split).
-__global__ void __launch_bounds__(kThreads) bn_bwd_partial_kernel(const float* y, int ypitch, const float* gr,
-                                                                  int gpitch, const float* stats, const float* gamma,
-                                                                  const float* beta, float eps, int c, Grid g,
-                                                                  int splits, float* part) {
-    __shared__ float r1[kWarps][32], r2[kWarps][32];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int ch = blockIdx.x * 32 + lane, b = blockIdx.y, s = blockIdx.z;
-    int p0, p1;
-    split_range(g.h * g.w, splits, s, p0, p1);
-    float s1 = 0.0f, s2 = 0.0f;
-    if (ch < c) {
-        const float mean = stats[((long)b * c + ch) * 2], var = stats[((long)b * c + ch) * 2 + 1];
-        const float inv = 1.0f / sqrtf(var + eps), ga = gamma[ch], be = beta[ch];
-        const long base = (long)b * g.rows;
-        for (int p = p0 + warp; p < p1; p += kWarps) {
-            const int yy = p / g.w, xx = p - yy * g.w;
-            const long row = base + g.row(yy, xx);
-            float xh;
-            const float dz = bn_dz(y[row * ypitch + ch], gr[row * gpitch + ch], mean, inv, ga, be, xh);
-            s1 += dz;
-            s2 += dz * xh;
-        }
-    }
-    r1[warp][lane] = s1;
-    r2[warp][lane] = s2;
-    __syncthreads();
-    if (warp == 0 && ch < c) {
-        float t1 = 0.0f, t2 = 0.0f;
-        for (int w = 0; w < kWarps; w++) {
-            t1 += r1[w][lane];
-            t2 += r2[w][lane];
-        }
-        float* o = part + (((long)b * splits + s) * c + ch) * 2;
-        o[0] = t1;
-        o[1] = t2;
-    }
-}
-
-// red[b][ch] = (sum dz, sum dz xhat) folded over the splits, one thread per (image, channel).
-__global__ void bn_bwd_final_kernel(const float* part, int batch, int c, int splits, float* red) {
+// red[b][ch] = (sum dz, sum dz xhat) folded over the row groups in order; f = gamma inv / n.
+__global__ void bn_bwd_fold_kernel(const float* part, int batch, int c, int groups, float n_pix, const float* inv_p,
+                                   const float* gamma, float* red, float* f_p) {
     const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
     if (i >= (long)batch * c) return;
     const int b = (int)(i / c), ch = (int)(i - (long)b * c);
     float t1 = 0.0f, t2 = 0.0f;
-    for (int s = 0; s < splits; s++) {
-        const float* o = part + (((long)b * splits + s) * c + ch) * 2;
+    for (int q = 0; q < groups; q++) {
+        const float* o = part + (((long)b * groups + q) * c + ch) * 2;
         t1 += o[0];
         t2 += o[1];
     }
     red[i * 2 + 0] = t1;
     red[i * 2 + 1] = t2;
+    f_p[i] = gamma[ch] * inv_p[i] / n_pix;
 }
 
 // dgamma += sum_b red[b][ch][1], dbeta += sum_b red[b][ch][0], images in order.
@@ -220,53 +167,46 @@ __global__ void bn_param_grad_kernel(const float* red, int batch, int c, float* 
     dbeta[ch] = db;
 }
 
-// dy = gamma * inv / n * (n * dz - sum dz - xhat * sum dz xhat)  (HeadOperations.cs:185-189)
+// dy = gamma * inv / n * (n * dz - sum dz - xhat * sum dz xhat)  (HeadOperations.cs:185-189), with dz
+// already formed by the data-gradient epilogue; one image per blockIdx.y.
 template <bool kVec>
-__global__ void bn_bwd_apply_kernel(const float* y, int ypitch, const float* gr, int gpitch, const float* stats,
-                                    const float* red, const float* gamma, const float* beta, float eps, int c,
-                                    long rows, Grid g, float* dy, int dpitch) {
+__global__ void bn_bwd_apply_kernel(const float* y, int ypitch, const float* dz, int zpitch, const float* mean_p,
+                                    const float* inv_p, const float* f_p, const float* red, int c, float n, Grid g,
+                                    float* dy, int dpitch) {
+    const int b = blockIdx.y;
     const int per_row = kVec ? c / 4 : c;
-    const long total = rows * per_row;
-    const float n = (float)(g.h * g.w);
+    const long total = (long)g.rows * per_row;
+    const long base = (long)b * g.rows;
+    const float* mb = mean_p + (long)b * c;
+    const float* ib = inv_p + (long)b * c;
+    const float* fb = f_p + (long)b * c;
+    const float* rb = red + (long)b * c * 2;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const long row = i / per_row;
-        const int j = (int)(i - row * per_row);
-        const int b = (int)(row / g.rows), r = (int)(row - (long)b * g.rows);
+        const int r = (int)(i / per_row), j = (int)(i - (long)r * per_row);
+        const long row = base + r;
         const bool in = g.interior(r);
-        const int lanes = kVec ? 4 : 1;
-        float o[4] = {0.f, 0.f, 0.f, 0.f};
-        if (in) {
-            float yv[4] = {0.f, 0.f, 0.f, 0.f}, gv[4] = {0.f, 0.f, 0.f, 0.f};
-            if (kVec) {
-                const float4 a = *reinterpret_cast<const float4*>(y + row * ypitch + 4 * j);
-                const float4 d = *reinterpret_cast<const float4*>(gr + row * gpitch + 4 * j);
-                yv[0] = a.x;
-                yv[1] = a.y;
-                yv[2] = a.z;
-                yv[3] = a.w;
-                gv[0] = d.x;
-                gv[1] = d.y;
-                gv[2] = d.z;
-                gv[3] = d.w;
-            } else {
-                yv[0] = y[row * ypitch + j];
-                gv[0] = gr[row * gpitch + j];
+        if (kVec) {
+            float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (in) {
+                const float4 yv = *reinterpret_cast<const float4*>(y + row * ypitch + 4 * j);
+                const float4 zv = *reinterpret_cast<const float4*>(dz + row * zpitch + 4 * j);
+                const float4 mv = *reinterpret_cast<const float4*>(mb + 4 * j);
+                const float4 iv = *reinterpret_cast<const float4*>(ib + 4 * j);
+                const float4 fv = *reinterpret_cast<const float4*>(fb + 4 * j);
+                const float4 r0 = *reinterpret_cast<const float4*>(rb + 8 * j);
+                const float4 r1 = *reinterpret_cast<const float4*>(rb + 8 * j + 4);
+                out.x = fv.x * (n * zv.x - r0.x - (yv.x - mv.x) * iv.x * r0.y);
+                out.y = fv.y * (n * zv.y - r0.z - (yv.y - mv.y) * iv.y * r0.w);
+                out.z = fv.z * (n * zv.z - r1.x - (yv.z - mv.z) * iv.z * r1.y);
+                out.w = fv.w * (n * zv.w - r1.z - (yv.w - mv.w) * iv.w * r1.w);
             }
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                if (k >= lanes) break;
-                const int ch = kVec ? 4 * j + k : j;
-                const long s = ((long)b * c + ch) * 2;
-                const float inv = 1.0f / sqrtf(stats[s + 1] + eps), ga = gamma[ch];
-                float xh;
-                const float dz = bn_dz(yv[k], gv[k], stats[s], inv, ga, beta[ch], xh);
-                o[k] = ga * inv / n * (n * dz - red[s] - xh * red[s + 1]);
-            }
+            *reinterpret_cast<float4*>(dy + row * dpitch + 4 * j) = out;
+        } else {
+            float out = 0.0f;
+            if (in)
+                out = fb[j] * (n * dz[row * zpitch + j] - rb[2 * j] - (y[row * ypitch + j] - mb[j]) * ib[j] * rb[2 * j + 1]);
+            dy[row * dpitch + j] = out;
         }
-        if (kVec)
-            *reinterpret_cast<float4*>(dy + row * dpitch + 4 * j) = make_float4(o[0], o[1], o[2], o[3]);
-        else
-            dy[row * dpitch + j] = o[0];
     }
 }
 
@@ -328,57 +268,67 @@ __global__ void bias_fold_kernel(const float* per_image, int batch, int c, float
     db[ch] = acc;
 }
 
-int blocks_for(long n) { return (int)std::min<long>(148L * 16, std::max<long>(1, (n + 255) / 256)); }
-
 }  // namespace
 
 size_t bn_workspace_floats(int batch, int channels) { return (size_t)batch * 64 * channels * 3; }
 
-void bn_stats(const View& y, int batch, const Grid& g, float* stats, float* ws, cudaStream_t stream) {
-    const Split sp = choose_split(batch, y.channels, g);
-    bn_stats_partial_kernel<<<dim3(sp.cgroups, batch, sp.splits), kThreads, 0, stream>>>(y.base, y.pitch, y.channels,
-                                                                                       g, sp.splits, ws);
-    launch_check("bn_stats_partial_kernel");
-    const long n = (long)batch * y.channels;
-    bn_stats_final_kernel<<<(int)((n + 127) / 128), 128, 0, stream>>>(ws, batch, y.channels, sp.splits, stats);
-    launch_check("bn_stats_final_kernel");
+size_t bn_partial_floats(int batch, const Grid& g, int channels) {
+    return (size_t)batch * (g.rows / 32) * channels * 3;
 }
 
-void bn_silu_apply(const View& y, const float* stats, const float* gamma, const float* beta, float eps, int batch,
-                   const Grid& g, const View& a, cudaStream_t stream) {
-    const long rows = (long)batch * g.rows;
-    const bool vec = y.channels % 4 == 0;
-    const long n = rows * (vec ? y.channels / 4 : y.channels);
+static dim3 image_grid(long per_image, int batch) {
+    const long want = std::max<long>(1, (148L * 16 + batch - 1) / batch);
+    return dim3((unsigned)std::min<long>(want, std::max<long>(1, (per_image + 255) / 256)), (unsigned)batch);
+}
+
+void bn_stats_fold(const float* part, int batch, const Grid& g, int c, float eps, float* stats, float* coef,
+                   cudaStream_t stream) {
+    const long n = (long)batch * c;
+    bn_stats_fold_kernel<<<dim3((c + 31) / 32, batch), kFoldWarps * 32, 0, stream>>>(part, c, g.rows / 32, eps, stats,
+                                                                                     coef, coef + n);
+    launch_check("bn_stats_fold_kernel");
+}
+
+void bn_silu_apply(const View& y, const float* coef, const float* gamma, const float* beta, int batch, const Grid& g,
+                   const View& a, cudaStream_t stream) {
+    const int c = y.channels;
+    const bool vec = c % 4 == 0 && y.pitch % 4 == 0 && a.pitch % 4 == 0;
+    const long per_image = (long)g.rows * (vec ? c / 4 : c);
+    const float* inv = coef + (long)batch * c;
     if (vec)
-        bn_apply_kernel<true><<<blocks_for(n), 256, 0, stream>>>(y.base, y.pitch, stats, gamma, beta, eps, y.channels,
-                                                                 rows, g, a.base, a.pitch);
+        bn_apply_kernel<true><<<image_grid(per_image, batch), 256, 0, stream>>>(y.base, y.pitch, coef, inv, gamma,
+                                                                                beta, c, g, a.base, a.pitch);
     else
-        bn_apply_kernel<false><<<blocks_for(n), 256, 0, stream>>>(y.base, y.pitch, stats, gamma, beta, eps, y.channels,
-                                                                  rows, g, a.base, a.pitch);
+        bn_apply_kernel<false><<<image_grid(per_image, batch), 256, 0, stream>>>(y.base, y.pitch, coef, inv, gamma,
+                                                                                 beta, c, g, a.base, a.pitch);
     launch_check("bn_apply_kernel");
 }
 
-void bn_silu_backward(const View& y, const View& gv, const float* stats, const float* gamma, const float* beta,
-                      float eps, int batch, const Grid& gr, float* red, const View& dy, float* dgamma, float* dbeta,
-                      float* ws, cudaStream_t stream) {
-    const int c = y.channels;
-    const Split sp = choose_split(batch, c, gr);
-    bn_bwd_partial_kernel<<<dim3(sp.cgroups, batch, sp.splits), kThreads, 0, stream>>>(
-        y.base, y.pitch, gv.base, gv.pitch, stats, gamma, beta, eps, c, gr, sp.splits, ws);
-    launch_check("bn_bwd_partial_kernel");
-    bn_bwd_final_kernel<<<(int)(((long)batch * c + 127) / 128), 128, 0, stream>>>(ws, batch, c, sp.splits, red);
-    launch_check("bn_bwd_final_kernel");
+void bn_backward_fold(const float* part, int batch, const Grid& g, int c, const float* coef, const float* gamma,
+                      float* dgamma, float* dbeta, float* bcoef, cudaStream_t stream) {
+    const long n = (long)batch * c;
+    float* red = bcoef + n;
+    bn_bwd_fold_kernel<<<(int)((n + 127) / 128), 128, 0, stream>>>(part, batch, c, g.rows / 32, (float)(g.h * g.w),
+                                                                  coef + n, gamma, red, bcoef);
+    launch_check("bn_bwd_fold_kernel");
     bn_param_grad_kernel<<<(c + 127) / 128, 128, 0, stream>>>(red, batch, c, dgamma, dbeta);
     launch_check("bn_param_grad_kernel");
-    const long rows = (long)batch * gr.rows;
-    const bool vec = c % 4 == 0;
-    const long n = rows * (vec ? c / 4 : c);
+}
+
+void bn_backward_apply(const View& y, const View& dz, const float* coef, const float* bcoef, int batch, const Grid& g,
+                       const View& dy, cudaStream_t stream) {
+    const int c = y.channels;
+    const bool vec = c % 4 == 0 && y.pitch % 4 == 0 && dz.pitch % 4 == 0 && dy.pitch % 4 == 0;
+    const long per_image = (long)g.rows * (vec ? c / 4 : c);
+    const float* inv = coef + (long)batch * c;
+    const float* red = bcoef + (long)batch * c;
+    const float n = (float)(g.h * g.w);
     if (vec)
-        bn_bwd_apply_kernel<true><<<blocks_for(n), 256, 0, stream>>>(y.base, y.pitch, gv.base, gv.pitch, stats, red,
-                                                                     gamma, beta, eps, c, rows, gr, dy.base, dy.pitch);
+        bn_bwd_apply_kernel<true><<<image_grid(per_image, batch), 256, 0, stream>>>(
+            y.base, y.pitch, dz.base, dz.pitch, coef, inv, bcoef, red, c, n, g, dy.base, dy.pitch);
     else
-        bn_bwd_apply_kernel<false><<<blocks_for(n), 256, 0, stream>>>(y.base, y.pitch, gv.base, gv.pitch, stats, red,
-                                                                      gamma, beta, eps, c, rows, gr, dy.base, dy.pitch);
+        bn_bwd_apply_kernel<false><<<image_grid(per_image, batch), 256, 0, stream>>>(
+            y.base, y.pitch, dz.base, dz.pitch, coef, inv, bcoef, red, c, n, g, dy.base, dy.pitch);
     launch_check("bn_bwd_apply_kernel");
 }
 

@@ -115,14 +115,46 @@ struct FwdParams {
     int phase_wp;        // consumer output grid: padded width
     int phase_rows;      // consumer output grid: rows per image
     long phase_stride;   // rows between parity planes (batch * phase_rows)
+    BnEpilogue bn;       // BatchNorm partials (see kernels.h)
     int* err;
 };
 
-constexpr int kFwdThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
-constexpr int kEpiThreads = 256;
+constexpr int kEpiWarps = 12;     // three per TMEM lane quadrant
+constexpr int kFwdThreads = 64 + 32 * kEpiWarps;   // warp 0 TMA, warp 1 MMA, warps 2-13 epilogue
+constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kTileM = 128;
 
 __device__ __forceinline__ float silu_fast(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
+
+// Sums of 16 per-lane values over the 32 lanes of a warp in 16 shuffles (each butterfly step hands
+// half of the remaining channels to the partner lane): on return every lane L holds the sum of
+// channel L >> 1.  The order of additions is fixed, so results are deterministic.
+__device__ __forceinline__ float warp_sum16(const float (&v)[16], int lane) {
+    float w8[8], w4[4], w2[2];
+    const bool h4 = lane & 16, h3 = lane & 8, h2 = lane & 4, h1 = lane & 2;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const float send = h4 ? v[k] : v[8 + k];
+        const float keep = h4 ? v[8 + k] : v[k];
+        w8[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float send = h3 ? w8[k] : w8[4 + k];
+        const float keep = h3 ? w8[4 + k] : w8[k];
+        w4[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        const float send = h2 ? w4[k] : w4[2 + k];
+        const float keep = h2 ? w4[2 + k] : w4[k];
+        w2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    const float send = h1 ? w2[0] : w2[1];
+    const float keep = h1 ? w2[1] : w2[0];
+    float r = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    return r + __shfl_xor_sync(0xffffffffu, r, 1);
+}
 
 __global__ void __launch_bounds__(kFwdThreads, 1)
     conv_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -143,6 +175,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + p.nacc);
     int* tap_s = reinterpret_cast<int*>(tmem_slot + 4);     // [9] weight tap, [9] A row offset
     float* bias_s = reinterpret_cast<float*>(tap_s + 20);
+    float* gam_s = bias_s + p.n;   // BatchNorm gamma / beta of the layer whose gradient is produced
+    float* bet_s = gam_s + p.n;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x < 9) {
@@ -165,8 +199,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         fence_barrier_init();
     }
     if (warp >= 2)
-        for (int i = threadIdx.x - 64; i < p.n; i += kEpiThreads)
+        for (int i = threadIdx.x - 64; i < p.n; i += kEpiThreads) {
             bias_s[i] = (p.bias && i < p.n_valid) ? p.bias[p.n0 + i] : 0.0f;
+            gam_s[i] = (p.bn.grad_part && i < p.n_valid) ? p.bn.gamma[p.n0 + i] : 0.0f;
+            bet_s[i] = (p.bn.grad_part && i < p.n_valid) ? p.bn.beta[p.n0 + i] : 0.0f;
+        }
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
@@ -283,37 +320,31 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             }
         }
     } else {
-        // two warps per TMEM lane quadrant; they take alternate (sub-tile, 16-column chunk) items
+        // three warps per TMEM lane quadrant; they take every third (sub-tile, 16-column chunk) item.
+        // Global loads of an item (residual, BatchNorm input and coefficients) are issued before
+        // its TMEM load so that their latencies overlap.
         const int q = warp & 3;
-        const int half = (warp - 2) >> 2;
+        const int part = (warp - 2) >> 2;
         const int nchunks = (p.n + 15) >> 4;
+        const bool bn_bwd = p.bn.grad_part != nullptr;
         int local = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
             const int acc = local % p.nacc;
             if (!mbar_wait(&tfull[acc], (local / p.nacc) & 1, p.err, 4)) break;
             tc_fence_after();
             const int mt = min(p.T, p.sub_tiles - tile * p.T);
-            for (int item = half; item < mt * nchunks; item += 2) {
+            for (int item = part; item < mt * nchunks; item += kEpiWarps / 4) {
                 const int i = item / nchunks;
                 const int j = (item - i * nchunks) * 16;
-                float v[16];
-                tmem_ld16(tmem_base + (acc * p.T + i) * p.acc_cols + ((uint32_t)(q * 32) << 16) + j, v);
-                if (j >= p.n_valid) continue;
+                if (j >= p.n_valid) continue;   // warp-uniform
                 const long m = (long)tile * tile_rows + i * kTileM + q * 32 + lane;
                 const long img = m / p.grid.rows;
                 const int r = (int)(m - img * p.grid.rows);
                 const bool inside = !p.mask || p.grid.interior(r);
+                const bool full16 = j + 16 <= p.n_valid;
+                const int chb = p.n0 + j;
                 float* orow = p.out ? p.out + m * (long)p.out_pitch : nullptr;
                 const float* rrow = p.residual ? p.residual + m * (long)p.res_pitch : nullptr;
-                // parity-split copy: padded pixel (py, px) -> plane (py&1, px&1), cell (py>>1, px>>1)
-                float* prow = nullptr;
-                if (p.phase && inside) {
-                    const int py = r / p.grid.wp, px = r - py * p.grid.wp;
-                    const long prow_index = ((py & 1) * 2 + (px & 1)) * p.phase_stride + img * p.phase_rows +
-                                            (long)(py >> 1) * p.phase_wp + (px >> 1);
-                    prow = p.phase + prow_index * p.phase_pitch;
-                }
-                const bool full16 = j + 16 <= p.n_valid;
                 float res[16];
                 if (rrow && full16 && inside) {
 #pragma unroll
@@ -328,12 +359,101 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
                     for (int u = 0; u < 16; u++) res[u] = (rrow && inside && j + u < p.n_valid) ? rrow[j + u] : 0.0f;
                 }
+                float yv[16], mv[16], iv[16];
+                if (bn_bwd) {
+                    const float* yr = p.bn.y + m * (long)p.bn.y_pitch + chb;
+                    const float* mr = p.bn.mean + img * p.bn.channels + chb;
+                    const float* ir = p.bn.inv + img * p.bn.channels + chb;
+                    if (full16) {
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            const float4 t = inside ? *reinterpret_cast<const float4*>(yr + 4 * u)
+                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                            yv[4 * u] = t.x;
+                            yv[4 * u + 1] = t.y;
+                            yv[4 * u + 2] = t.z;
+                            yv[4 * u + 3] = t.w;
+                            const float4 mm = *reinterpret_cast<const float4*>(mr + 4 * u);
+                            mv[4 * u] = mm.x;
+                            mv[4 * u + 1] = mm.y;
+                            mv[4 * u + 2] = mm.z;
+                            mv[4 * u + 3] = mm.w;
+                            const float4 ii = *reinterpret_cast<const float4*>(ir + 4 * u);
+                            iv[4 * u] = ii.x;
+                            iv[4 * u + 1] = ii.y;
+                            iv[4 * u + 2] = ii.z;
+                            iv[4 * u + 3] = ii.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 16; u++) {
+                            const bool ok = j + u < p.n_valid;
+                            yv[u] = (inside && ok) ? yr[u] : 0.0f;
+                            mv[u] = ok ? mr[u] : 0.0f;
+                            iv[u] = ok ? ir[u] : 0.0f;
+                        }
+                    }
+                }
+                float v[16];
+                tmem_ld16(tmem_base + (acc * p.T + i) * p.acc_cols + ((uint32_t)(q * 32) << 16) + j, v);
+                // parity-split copy: padded pixel (py, px) -> plane (py&1, px&1), cell (py>>1, px>>1)
+                float* prow = nullptr;
+                if (p.phase && inside) {
+                    const int py = r / p.grid.wp, px = r - py * p.grid.wp;
+                    const long prow_index = ((py & 1) * 2 + (px & 1)) * p.phase_stride + img * p.phase_rows +
+                                            (long)(py >> 1) * p.phase_wp + (px >> 1);
+                    prow = p.phase + prow_index * p.phase_pitch;
+                }
 #pragma unroll
                 for (int u = 0; u < 16; u++) {
                     float x = v[u] + bias_s[j + u];
                     if (p.silu) x = silu_fast(x);
                     x += res[u];
                     v[u] = inside ? x : 0.0f;
+                }
+                // BatchNorm partials over this warp's 32 rows (one row group, inside one image)
+                const long grp = ((long)tile * tile_rows + i * kTileM + q * 32) >> 5;
+                if (p.bn.stats_part) {
+                    const float cnt = (float)__popc(__ballot_sync(0xffffffffu, inside));
+                    const float mean_l = cnt > 0.0f ? warp_sum16(v, lane) / cnt : 0.0f;   // channel lane >> 1
+                    float d[16];
+#pragma unroll
+                    for (int u = 0; u < 16; u++) {
+                        const float mu = __shfl_sync(0xffffffffu, mean_l, 2 * u);
+                        d[u] = inside ? (v[u] - mu) * (v[u] - mu) : 0.0f;
+                    }
+                    const float m2_l = warp_sum16(d, lane);
+                    const int cu = lane >> 1;
+                    if ((lane & 1) == 0 && j + cu < p.n_valid) {
+                        float* o = p.bn.stats_part + (grp * p.bn.channels + chb + cu) * 3;
+                        o[0] = cnt;
+                        o[1] = mean_l;
+                        o[2] = m2_l;
+                    }
+                }
+                if (bn_bwd) {
+                    // v holds g = dL/da of the BN layer; store dz = dL/dz = g SiLU'(z) instead
+                    float dzx[16];
+#pragma unroll
+                    for (int u = 0; u < 16; u++) {
+                        float xh = 0.0f, dz = 0.0f;
+                        if (inside && j + u < p.n_valid) {
+                            xh = (yv[u] - mv[u]) * iv[u];
+                            const float z = xh * gam_s[j + u] + bet_s[j + u];
+                            const float sg = __fdividef(1.0f, 1.0f + __expf(-z));
+                            dz = v[u] * (sg + z * sg * (1.0f - sg));
+                        }
+                        v[u] = dz;
+                        dzx[u] = dz * xh;
+                    }
+                    const float s1 = warp_sum16(v, lane);
+                    const float s2 = warp_sum16(dzx, lane);
+                    const int cu = lane >> 1;
+                    if ((lane & 1) == 0 && j + cu < p.n_valid) {
+                        float* o = p.bn.grad_part + (grp * p.bn.channels + chb + cu) * 2;
+                        o[0] = s1;
+                        o[1] = s2;
+                    }
                 }
                 if (full16) {
                     if (orow) {
@@ -389,6 +509,10 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
     if (phase && ((phase->pitch % 4) != 0 || (reinterpret_cast<uintptr_t>(phase->base) & 15) != 0))
         throw std::runtime_error("conv_tc: parity copy not 16-byte aligned");
     if (taps < 1 || taps > 9) throw std::runtime_error("conv_tc: taps");
+    if ((ep.bn.stats_part || ep.bn.grad_part) && (grid.rows % 32 != 0 || ep.bn.channels < n_out || !ep.mask_halo))
+        throw std::runtime_error("conv_tc: BatchNorm partials need masked 32-row groups covering every channel");
+    if (ep.bn.grad_part && (ep.bn.y_pitch % 4 != 0 || (reinterpret_cast<uintptr_t>(ep.bn.y) & 15) != 0))
+        throw std::runtime_error("conv_tc: BatchNorm input not 16-byte aligned");
     // tap groups: taps sorted by shift, a new group wherever consecutive shifts are more than `gap`
     // rows apart.  With gap = wp + 2 a stride-1 3x3 conv is one group (its consecutive shifts differ
     // by 1 or wp - 2) and a stride-2 conv one group per parity plane (planes lie at least
@@ -501,12 +625,13 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         p.phase_wp = phase ? phase->consumer.wp : 0;
         p.phase_rows = phase ? phase->consumer.rows : 0;
         p.phase_stride = phase ? phase->plane_rows : 0;
+        p.bn = ep.bn;
         p.err = err;
         if (p.alloc_cols > 512) throw std::runtime_error("conv_tc: TMEM columns");
         CUtensorMap tb = make_map_2d(wk, (long)taps * kpad, n_rows, (long)taps * kpad, 32, n);
         const int nb = resident ? 1 : p.b_stages;
         const size_t smem = 1024 + (size_t)p.a_stages * a_stage + p.b_region_bytes +
-                            (2 * p.a_stages + 2 * nb + 2 * p.nacc) * 8 + 16 + 80 + n * 4;
+                            (2 * p.a_stages + 2 * nb + 2 * p.nacc) * 8 + 16 + 80 + 3 * n * 4;
         if (smem > 227 * 1024) throw std::runtime_error("conv_tc: shared memory");
         const int grid_x = std::min(p.num_tiles, num_sms());
         conv_fwd_tc_kernel<<<grid_x, kFwdThreads, smem, stream>>>(ta, tb, p);

@@ -30,12 +30,33 @@ struct View {
 // wk is K-major [n_rows][taps * kpad] (kpad = round_up(in.channels, 32)).  Used for forward
 // convs (weights in [oc][tap][ic] order) and for data gradients (weights [ic][tap][oc] with
 // negated shifts).  Halo / dead rows of `out` are written as zero.
+// BatchNorm hooks of the epilogue (per-image training BatchNorm of the next / previous layer).
+// Statistics are reduced per 32-row group (a group never spans two images, rows per image being a
+// multiple of 128) and folded per (image, channel) in row-group order by bn_stats_fold /
+// bn_backward_fold.
+struct BnEpilogue {
+    int channels = 0;                 // BN channels (stride of the partial and coefficient arrays)
+    // forward: part[(group * channels + ch) * 3 + {0,1,2}] = (count, mean, M2) of the conv output
+    float* stats_part = nullptr;
+    // backward: the conv output is g = dL/da with a = SiLU(gamma * (y - mean) * inv + beta); the
+    // epilogue stores dz = dL/dz instead and part[(group * channels + ch) * 2 + {0,1}] =
+    // (sum dz, sum dz * xhat) over the group's interior rows.
+    const float* y = nullptr;
+    int y_pitch = 0;
+    const float* mean = nullptr;      // [images][channels]
+    const float* inv = nullptr;       // [images][channels] 1 / sqrt(var + eps)
+    const float* gamma = nullptr;
+    const float* beta = nullptr;
+    float* grad_part = nullptr;
+};
+
 struct ConvEpilogue {
     const float* bias = nullptr;      // per output channel
     int silu = 0;
     const float* residual = nullptr;  // added after SiLU (Bottleneck shortcut)
     int res_pitch = 0;
     int mask_halo = 1;                // 0: every row is a valid output (plain GEMM use)
+    BnEpilogue bn{};
 };
 
 // Parity-split copy of a feature map, the input format of a 3x3 stride-2 conv.  Padded pixel
@@ -89,23 +110,30 @@ void upsample2_padded(const View& in, const Grid& gin, const View& out, const Gr
                       cudaStream_t stream);
 
 // ---------------------------------------------------------------- BatchNorm (training, per image)
-// Scratch (floats) the reductions below need for `channels` channels of `batch` images.
-size_t bn_workspace_floats(int batch, int channels);
-// stats[(b * c + ch) * 2 + {0,1}] = (mean, biased variance) of image b over the interior pixels.
-void bn_stats(const View& y, int batch, const Grid& g, float* stats, float* ws, cudaStream_t stream);
-// a = SiLU(gamma * (y - mean) * inv + beta) at interior rows, 0 elsewhere; xhat not stored.
-void bn_silu_apply(const View& y, const float* stats, const float* gamma, const float* beta, float eps, int batch,
-                   const Grid& g, const View& a, cudaStream_t stream);
-// Backward through SiLU and BN.  g: gradient w.r.t. a.  Writes dy (w.r.t. y) with zero halo and
-// per-image partials red[(b * c + ch) * 2 + {0,1}] = (sum dz, sum dz * xhat); dgamma/dbeta are
-// accumulated over images in image order.
-void bn_silu_backward(const View& y, const View& g, const float* stats, const float* gamma, const float* beta,
-                      float eps, int batch, const Grid& gr, float* red, const View& dy, float* dgamma, float* dbeta,
-                      float* ws, cudaStream_t stream);
+// Floats of the per-32-row-group partials the conv epilogue writes for `channels` channels.
+size_t bn_partial_floats(int batch, const Grid& g, int channels);
+// Fold the epilogue's (count, mean, M2) partials of every (image, channel) in row-group order
+// (Chan's pairwise update, in double): stats[(b * c + ch) * 2 + {0,1}] = (mean, biased variance),
+// coef = [mean plane | inv plane], each [batch][c], inv = 1 / sqrt(var + eps).
+void bn_stats_fold(const float* part, int batch, const Grid& g, int c, float eps, float* stats, float* coef,
+                   cudaStream_t stream);
+// a = SiLU(gamma * (y - mean) * inv + beta) at interior rows, 0 elsewhere (xhat is not stored).
+void bn_silu_apply(const View& y, const float* coef, const float* gamma, const float* beta, int batch, const Grid& g,
+                   const View& a, cudaStream_t stream);
+// Fold the epilogue's (sum dz, sum dz xhat) partials per (image, channel) over the row groups in order;
+// dgamma / dbeta are accumulated over images in image order.  bcoef (3 x batch x c floats) receives
+// [f plane | red], f = gamma inv / n, red[(b * c + ch) * 2 + {0,1}] = (sum dz, sum dz xhat).
+void bn_backward_fold(const float* part, int batch, const Grid& g, int c, const float* coef, const float* gamma,
+                      float* dgamma, float* dbeta, float* bcoef, cudaStream_t stream);
+// dy = f (n dz - sum dz - xhat sum dz xhat)  (HeadOperations.cs:185-189) at interior rows, 0 elsewhere.
+void bn_backward_apply(const View& y, const View& dz, const float* coef, const float* bcoef, int batch, const Grid& g,
+                       const View& dy, cudaStream_t stream);
 // Running statistics: for each BN channel, r <- (1-m) r + m * s_i for images i in order, over
 // `ranks` blocks of `batch` images each `rank_stride` floats apart (all-gathered ranks).
 void bn_running_update(const float* stats, long rank_stride, int ranks, int batch, int c, int spatial, float momentum,
                        float* rmean, float* rvar, float* tracked, cudaStream_t stream);
+// Scratch (floats) bias_grad needs for `channels` channels of `batch` images.
+size_t bn_workspace_floats(int batch, int channels);
 // Bias gradient of the final conv: db[n] += sum over images and interior pixels of g[m, n].
 // `ws` is scratch of bn_workspace_floats(batch, channels) floats.
 void bias_grad(const View& g, int batch, const Grid& gr, float* ws, float* db, cudaStream_t stream);

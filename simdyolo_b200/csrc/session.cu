@@ -481,6 +481,7 @@ void Session::build_head() {
     // activations and gradients
     size_t ws = 0;
     int max_oc = 0;
+    size_t bn_part_floats = 0;
     for (auto& branch : branches_) {
         const Grid& g = levels_[branch.level];
         View x = features_[branch.level];
@@ -494,7 +495,9 @@ void Session::build_head() {
                 hb.dy = alloc_view(b.oc, g);
                 hb.stats_off = bn_channels_;
                 bn_channels_ += b.oc;
-                hb.red = static_cast<float*>(dalloc(sizeof(float) * 2 * B_ * b.oc));
+                hb.coef = static_cast<float*>(dalloc(sizeof(float) * 2 * B_ * b.oc));
+                hb.bcoef = static_cast<float*>(dalloc(sizeof(float) * 3 * B_ * b.oc));
+                bn_part_floats = std::max(bn_part_floats, bn_partial_floats(B_, g, b.oc));
             } else {
                 hb.dy = hb.g;
             }
@@ -517,6 +520,7 @@ void Session::build_head() {
             if (hb.b.has_bn) hb.stats = bn_stats_all_ + 2 * (size_t)B_ * hb.stats_off;
     wgrad_ws_ = static_cast<float*>(dalloc(sizeof(float) * ws));
     bias_part_ = static_cast<float*>(dalloc(sizeof(float) * bn_workspace_floats(B_, max_oc)));
+    bn_part_ = static_cast<float*>(dalloc(sizeof(float) * std::max<size_t>(bn_part_floats, 1)));
 }
 
 void Session::refresh_head_weights() {
@@ -538,12 +542,16 @@ void Session::forward_head(int batch) {
         for (auto& hb : branch.blocks) {
             ConvEpilogue ep;
             if (hb.b.has_bias) ep.bias = params_ + hb.b_off;
+            if (hb.b.has_bn) {
+                ep.bn.channels = hb.b.oc;
+                ep.bn.stats_part = bn_part_;
+            }
             conv_tc_forward(rows_of(hb.x, batch, g), hb.w_fwd, hb.b.oc, hb.b.oc, hb.taps, 1, g,
                             rows_of(hb.y, batch, g), ep, d_flags_, stream_);
             if (hb.b.has_bn) {
-                bn_stats(hb.y, batch, g, hb.stats, bias_part_, stream_);
-                bn_silu_apply(hb.y, hb.stats, params_ + hb.g_off, params_ + hb.be_off, cfg.bn_eps, batch, g, hb.a,
-                              stream_);
+                bn_stats_fold(bn_part_, batch, g, hb.b.oc, cfg.bn_eps, hb.stats, hb.coef, stream_);
+                bn_silu_apply(rows_of(hb.y, batch, g), hb.coef, params_ + hb.g_off, params_ + hb.be_off, batch, g,
+                              rows_of(hb.a, batch, g), stream_);
             }
         }
     }
@@ -556,15 +564,30 @@ void Session::backward_head(int batch) {
             const Grid& g = levels_[l];
             for (int i = (int)branch.blocks.size() - 1; i >= 0; i--) {
                 HeadBlock& hb = branch.blocks[i];
-                if (hb.b.has_bn)
-                    bn_silu_backward(hb.y, hb.g, hb.stats, params_ + hb.g_off, params_ + hb.be_off, cfg.bn_eps, batch,
-                                     g, hb.red, hb.dy, grads_ + hb.g_off, grads_ + hb.be_off, bias_part_, stream_);
+                if (hb.b.has_bn) {
+                    // hb.g holds dz and bn_part_ its partial sums, written by the next block's data-gradient
+                    // epilogue (every BN block is followed by another block)
+                    bn_backward_fold(bn_part_, batch, g, hb.b.oc, hb.coef, params_ + hb.g_off, grads_ + hb.g_off,
+                                     grads_ + hb.be_off, hb.bcoef, stream_);
+                    bn_backward_apply(rows_of(hb.y, batch, g), rows_of(hb.g, batch, g), hb.coef, hb.bcoef, batch, g,
+                                      rows_of(hb.dy, batch, g), stream_);
+                }
                 if (hb.b.has_bias) bias_grad(hb.dy, batch, g, bias_part_, grads_ + hb.b_off, stream_);
                 conv_tc_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off,
                               wgrad_ws_, d_flags_, stream_);
                 if (i > 0) {
                     HeadBlock& prev = branch.blocks[i - 1];
                     ConvEpilogue ep;
+                    if (prev.b.has_bn) {
+                        ep.bn.channels = prev.b.oc;
+                        ep.bn.y = prev.y.base;
+                        ep.bn.y_pitch = prev.y.pitch;
+                        ep.bn.mean = prev.coef;
+                        ep.bn.inv = prev.coef + (long)batch * prev.b.oc;
+                        ep.bn.gamma = params_ + prev.g_off;
+                        ep.bn.beta = params_ + prev.be_off;
+                        ep.bn.grad_part = bn_part_;
+                    }
                     conv_tc_forward(rows_of(hb.dy, batch, g), hb.w_dgrad, hb.b.ic, hb.b.ic, hb.taps, -1, g,
                                     rows_of(prev.g, batch, g), ep, d_flags_, stream_);
                 }

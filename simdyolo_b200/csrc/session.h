@@ -38,7 +38,8 @@ struct HeadBlock {
     View x{}, y{}, a{}, g{}, dy{};
     float* stats = nullptr;     // [B][oc][2] inside the session's contiguous statistics block
     long stats_off = 0;         // channel offset of this layer in that block
-    float* red = nullptr;       // [B][oc][2]
+    float* coef = nullptr;      // [mean plane | inv plane], each [B][oc]
+    float* bcoef = nullptr;     // backward: [f plane | (sum dz, sum dz xhat) per (image, channel)]
 };
 
 struct Branch {
@@ -128,6 +129,7 @@ private:
     float* bn_gather_ = nullptr;
     long bn_channels_ = 0;
     float* bias_part_ = nullptr;
+    float* bn_part_ = nullptr;       // per-32-row-group BatchNorm partials written by conv epilogues
     void* loss_ws_ = nullptr;
     TruthBox* d_truth_ = nullptr;
     int* d_box_off_ = nullptr;
