@@ -188,6 +188,12 @@ SY_API sy_status sy_cuda_matmul(int32_t device, const float *a, const float *b, 
  * one warm-up) of one convolution pass on device-resident data: kind 0 forward, 1 data gradient,
  * 2 weight gradient; shapes as in sy_cuda_conv2d_*. */
 SY_API int64_t sy_cuda_launch_count(void);
+/* sy_cuda_conv_profile: with enable != 0, the following steps of `session` record CUDA events around
+ * every tensor-core convolution launch (trunk forward, head forward, head data gradients) on the
+ * session stream.  Returns, and resets, the totals since the previous call: device ms, algorithmic
+ * GFLOP (2 x MACs of the interior pixels) and the number of convolution launches. */
+SY_API sy_status sy_cuda_conv_profile(sy_session *session, int32_t enable, double *ms, double *gflop,
+                                      int64_t *launches);
 SY_API sy_status sy_cuda_bench_conv(int32_t device, int32_t kind, int32_t n, int32_t ic, int32_t oc, int32_t h,
                                     int32_t w, int32_t k, int32_t iters, double *ms_per_launch);
 

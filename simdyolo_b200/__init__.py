@@ -136,6 +136,8 @@ def lib():
         L.sy_cuda_launch_count.restype = C.c_int64
         L.sy_cuda_bench_conv.argtypes = [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                          C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_double)]
+        L.sy_cuda_conv_profile.argtypes = [vp, st, C.POINTER(C.c_double), C.POINTER(C.c_double),
+                                           C.POINTER(C.c_int64)]
         _lib = L
     return _lib
 
@@ -147,7 +149,7 @@ EXPORTED = ["sy_cuda_nccl_unique_id", "sy_cuda_create", "sy_cuda_destroy", "sy_c
             "sy_cuda_get_last_features", "sy_cuda_detection_loss", "sy_cuda_conv2d_forward",
             "sy_cuda_conv2d_backward_data", "sy_cuda_conv2d_backward_filter", "sy_cuda_matmul", "sy_cuda_sgd_update",
             "sy_cuda_step_device", "sy_cuda_launch_count", "sy_cuda_bench_conv",
-            "sy_cuda_conv2d_backward_filter_static"]
+            "sy_cuda_conv2d_backward_filter_static", "sy_cuda_conv_profile"]
 
 
 def _check(status: int, session=None):
@@ -395,6 +397,13 @@ class Session:
         out = np.zeros(n, np.float32)
         _check(lib().sy_cuda_get_last_gradients(self._h, _fp(out), n), self._h)
         return out
+
+    def conv_profile(self, enable: bool):
+        """Totals (device ms, GFLOP, launches) of the tensor-core conv launches since the previous call;
+        `enable` switches CUDA-event timing of those launches on or off for the following steps."""
+        ms, gf, n = C.c_double(), C.c_double(), C.c_int64()
+        _check(lib().sy_cuda_conv_profile(self._h, int(bool(enable)), C.byref(ms), C.byref(gf), C.byref(n)), self._h)
+        return ms.value, gf.value, n.value
 
     def last_features(self, level: int, shape) -> np.ndarray:
         out = np.zeros(int(np.prod(shape)), np.float32)

@@ -193,6 +193,16 @@ sy_status sy_cuda_step_features(sy_session* session, const float* const features
 
 int64_t sy_cuda_launch_count(void) { return sy::launch_count(); }
 
+sy_status sy_cuda_conv_profile(sy_session* session, int32_t enable, double* ms, double* gflop, int64_t* launches) {
+    if (!session) return SY_ERR_INVALID_ARGUMENT;
+    return guarded(session, [&] {
+        long n = 0;
+        const int r = session->impl->conv_profile(enable, ms, gflop, &n);
+        if (launches) *launches = n;
+        return r;
+    });
+}
+
 sy_status sy_cuda_bench_conv(int32_t device, int32_t kind, int32_t n, int32_t ic, int32_t oc, int32_t h, int32_t w,
                              int32_t k, int32_t iters, double* ms_per_launch) {
     return guarded(nullptr, [&] {

@@ -160,6 +160,7 @@ Session::~Session() {
         if (p) cudaFreeHost(p);
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
+    for (cudaEvent_t e : prof_ev_) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -373,10 +374,14 @@ void Session::forward_backbone(int batch, const uint8_t* rgb_device) {
                 // the tcgen05 kernel works on whole 128-row tiles: restrict the views to `batch` images
                 View i2 = in, o2 = out;
                 i2.rows = o2.rows = (long)batch * op.gin.rows;
+                prof_begin();
                 conv_tc_forward(i2, op.wk, op.oc, op.oc, op.k * op.k, 1, op.gin, o2, ep, d_flags_, stream_, po);
+                prof_end(2.0 * batch * op.oc * op.ic * op.k * op.k * op.gin.h * op.gin.w);
             } else {
+                prof_begin();
                 conv_tc_strided(op.phase_in, op.phase_plane_rows, (long)batch * op.gout.rows, op.wk, op.oc, op.gout,
                                 out, ep, d_flags_, stream_, po);
+                prof_end(2.0 * batch * op.oc * op.ic * 9 * op.gout.h * op.gout.w);
             }
         }
     }
@@ -546,8 +551,10 @@ void Session::forward_head(int batch) {
                 ep.bn.channels = hb.b.oc;
                 ep.bn.stats_part = bn_part_;
             }
+            prof_begin();
             conv_tc_forward(rows_of(hb.x, batch, g), hb.w_fwd, hb.b.oc, hb.b.oc, hb.taps, 1, g,
                             rows_of(hb.y, batch, g), ep, d_flags_, stream_);
+            prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w);
             if (hb.b.has_bn) {
                 bn_stats_fold(bn_part_, batch, g, hb.b.oc, cfg.bn_eps, hb.stats, hb.coef, stream_);
                 bn_silu_apply(rows_of(hb.y, batch, g), hb.coef, params_ + hb.g_off, params_ + hb.be_off, batch, g,
@@ -588,8 +595,10 @@ void Session::backward_head(int batch) {
                         ep.bn.beta = params_ + prev.be_off;
                         ep.bn.grad_part = bn_part_;
                     }
+                    prof_begin();
                     conv_tc_forward(rows_of(hb.dy, batch, g), hb.w_dgrad, hb.b.ic, hb.b.ic, hb.taps, -1, g,
                                     rows_of(prev.g, batch, g), ep, d_flags_, stream_);
+                    prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w);
                 }
             }
         }
@@ -618,6 +627,7 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
     }
     if (rgb && (cfg.backbone != SY_BACKBONE_YOLOV8 || !backbone_ready_))
         throw SyError(SY_ERR_INVALID_ARGUMENT, "backbone weights not set");
+    prof_n_ = 0;
     SY_CUDA(cudaEventRecord(ev0_, stream_));
     if (k > 0)
         SY_CUDA(cudaMemcpyAsync(d_truth_, h_truth_, sizeof(TruthBox) * k, cudaMemcpyHostToDevice, stream_));
@@ -764,6 +774,7 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
     SY_CUDA(cudaMemcpyAsync(h_flags_, d_flags_, sizeof(int) * 2, cudaMemcpyDeviceToHost, stream_));
     SY_CUDA(cudaEventRecord(ev1_, stream_));
     SY_CUDA(cudaStreamSynchronize(stream_));
+    prof_collect();
     last_batch_ = images;
     if (out) {
         float ms = 0.0f;
@@ -779,6 +790,46 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
     }
     if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "device wait limit exceeded");
     if (h_flags_[1]) throw SyError(SY_ERR_NONFINITE, "non-finite parameters after the update");
+    return SY_OK;
+}
+
+// ------------------------------------------------------------------ conv launch timing
+void Session::prof_begin() {
+    if (!prof_) return;
+    while ((int)prof_ev_.size() < 2 * (prof_n_ + 1)) {
+        cudaEvent_t e;
+        SY_CUDA(cudaEventCreate(&e));
+        prof_ev_.push_back(e);
+    }
+    SY_CUDA(cudaEventRecord(prof_ev_[2 * prof_n_], stream_));
+}
+
+void Session::prof_end(double flops) {
+    if (!prof_) return;
+    SY_CUDA(cudaEventRecord(prof_ev_[2 * prof_n_ + 1], stream_));
+    if ((int)prof_flops_.size() <= prof_n_) prof_flops_.resize(prof_n_ + 1);
+    prof_flops_[prof_n_] = flops;
+    prof_n_++;
+}
+
+void Session::prof_collect() {
+    for (int k = 0; k < prof_n_; k++) {
+        float ms = 0.0f;
+        SY_CUDA(cudaEventElapsedTime(&ms, prof_ev_[2 * k], prof_ev_[2 * k + 1]));
+        prof_ms_ += ms;
+        prof_gflop_ += prof_flops_[k] * 1e-9;
+    }
+    prof_launches_ += prof_n_;
+    prof_n_ = 0;
+}
+
+int Session::conv_profile(int enable, double* ms, double* gflop, long* launches) {
+    if (ms) *ms = prof_ms_;
+    if (gflop) *gflop = prof_gflop_;
+    if (launches) *launches = prof_launches_;
+    prof_ms_ = prof_gflop_ = 0.0;
+    prof_launches_ = 0;
+    prof_ = enable != 0;
     return SY_OK;
 }
 

@@ -84,6 +84,9 @@ public:
     int set_backbone(const float* host, long count);
     int get_last_gradients(float* host, long count) const;
     int get_last_features(int level, float* host, long count) const;
+    // Optional CUDA-event timing of every tensor-core convolution launch (forward, stride-2 and
+    // data-gradient passes) on the session stream; returns the totals since the previous call.
+    int conv_profile(int enable, double* ms, double* gflop, long* launches);
 
     std::vector<TensorEntry> tensors;
     long n_params = 0, n_buffers = 0, n_backbone = 0;
@@ -149,6 +152,16 @@ private:
     int nsegs_ = 0;
     int adam_steps_[2] = {0, 0};
     int last_batch_ = 0;
+    // conv launch timing (conv_profile)
+    bool prof_ = false;
+    std::vector<cudaEvent_t> prof_ev_;
+    std::vector<double> prof_flops_;
+    int prof_n_ = 0;
+    double prof_ms_ = 0.0, prof_gflop_ = 0.0;
+    long prof_launches_ = 0;
+    void prof_begin();
+    void prof_end(double flops);
+    void prof_collect();
     NcclApi* nccl_ = nullptr;
     void* comm_ = nullptr;
 };
