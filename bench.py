@@ -48,6 +48,8 @@ def parse():
     p.add_argument("--image", type=int, default=640)
     p.add_argument("--model", default="yolov8n")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--precision", default="tf32", choices=["tf32", "3xtf32"],
+                   help="3xtf32: the FP32 parity mode (three split-operand TF32 passes per convolution)")
     p.add_argument("--conv-sweep", action="store_true",
                    help="config 1: time forward / dgrad / wgrad of the isolated head convs (one JSON line each)")
     return p.parse_args()
@@ -283,7 +285,8 @@ def run_ours(args, rank, world, local_rank, dist):
 
     nccl_id = dp.broadcast_nccl_id(dist, rank) if world > 1 else b""
     cfg = sy.make_config(args.model, image_size=args.image, max_batch=args.batch, max_boxes=8, num_classes=80,
-                         device=local_rank, rank=rank, world_size=world, nccl_id=nccl_id)
+                         device=local_rank, rank=rank, world_size=world, nccl_id=nccl_id,
+                         precision=sy.SY_PRECISION_3XTF32 if args.precision == "3xtf32" else sy.SY_PRECISION_TF32)
     sess = sy.Session(cfg)
     params, buffers = data.head_params(sess, seed=0)
     sess.set_flat_params(params)
@@ -377,7 +380,7 @@ def run_ours(args, rank, world, local_rank, dist):
                                    "peak": tf32_burst, "note": "timed alone: burst TF32 denominator"}
         line = {"metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "tf32",
+                "scaling": "weak", "vs_baseline": None, "dtype": args.precision,
                 "data": "synthetic (seeded uniform RGB24, random-init frozen backbone and head)",
                 "config": {"workload": WORKLOAD, "global_batch": world * args.batch, "per_gpu_batch": args.batch,
                            "image": args.image, "parallelism": f"dp{world}",

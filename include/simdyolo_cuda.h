@@ -57,6 +57,11 @@ typedef struct sy_block {
 
 #define SY_OPT_SGD 0
 #define SY_OPT_ADAMW 1
+/* Tensor-core precision of every convolution in the step.  3xTF32 splits each FP32 operand into a
+ * TF32 value and a TF32 residual and sums three products (small x big, big x small, big x big),
+ * which restores FP32-level agreement with the reference's FP32 arithmetic at 3x the MMA work. */
+#define SY_PRECISION_TF32 0
+#define SY_PRECISION_3XTF32 1
 #define SY_BACKBONE_NONE 0    /* features are supplied by the caller (cached features)       */
 #define SY_BACKBONE_YOLOV8 1  /* YOLOv8 detection trunk (Conv, C2f, SPPF, Upsample, Concat) */
 
@@ -81,6 +86,7 @@ typedef struct sy_config {
     int32_t optimizer;          /* SY_OPT_* */
     float lr, momentum, weight_decay;
     float beta1, beta2, adam_eps;
+    int32_t precision;          /* SY_PRECISION_TF32, or SY_PRECISION_3XTF32 for the FP32 parity mode */
 } sy_config;
 
 /* Per-step results, summed over the global batch (all ranks). */

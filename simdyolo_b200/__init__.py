@@ -25,6 +25,8 @@ SY_ERR_DEVICE = 5
 SY_ERR_OUT_OF_MEMORY = 6
 SY_OPT_SGD = 0
 SY_OPT_ADAMW = 1
+SY_PRECISION_TF32 = 0
+SY_PRECISION_3XTF32 = 1
 SY_BACKBONE_NONE = 0
 SY_BACKBONE_YOLOV8 = 1
 
@@ -71,7 +73,7 @@ class Config(C.Structure):
                 ("n_cls_blocks", C.c_int32), ("box_blocks", (Block * 8) * 3), ("cls_blocks", (Block * 8) * 3),
                 ("bn_eps", C.c_float), ("bn_momentum", C.c_float), ("optimizer", C.c_int32), ("lr", C.c_float),
                 ("momentum", C.c_float), ("weight_decay", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float),
-                ("adam_eps", C.c_float)]
+                ("adam_eps", C.c_float), ("precision", C.c_int32)]
 
 
 class StepStats(C.Structure):
@@ -242,7 +244,7 @@ def make_config(model: str = "yolov8n", image_size: int = 640, max_batch: int = 
                 num_classes: int = 80, device: int = 0, rank: int = 0, world_size: int = 1, nccl_id: bytes = b"",
                 backbone: bool = True, optimizer: int = SY_OPT_SGD, lr: float = 0.01, momentum: float = 0.937,
                 weight_decay: float = 5e-4, beta1: float = 0.9, beta2: float = 0.999, adam_eps: float = 1e-8,
-                bn_eps: float = 1e-3, bn_momentum: float = 0.03) -> Config:
+                bn_eps: float = 1e-3, bn_momentum: float = 0.03, precision: int = SY_PRECISION_TF32) -> Config:
     width, depth, max_ch = MODELS[model]
     feats = yolov8_channels(width, max_ch)
     cfg = Config()
@@ -266,6 +268,7 @@ def make_config(model: str = "yolov8n", image_size: int = 640, max_batch: int = 
     cfg.bn_eps, cfg.bn_momentum = bn_eps, bn_momentum
     cfg.optimizer, cfg.lr, cfg.momentum, cfg.weight_decay = optimizer, lr, momentum, weight_decay
     cfg.beta1, cfg.beta2, cfg.adam_eps = beta1, beta2, adam_eps
+    cfg.precision = precision
     return cfg
 
 

@@ -115,6 +115,8 @@ struct FwdParams {
     int phase_wp;        // consumer output grid: padded width
     int phase_rows;      // consumer output grid: rows per image
     long phase_stride;   // rows between parity planes (batch * phase_rows)
+    const float* pre;    // added to the accumulator first (3xTF32 passes)
+    int pre_pitch;
     BnEpilogue bn;       // BatchNorm partials (see kernels.h)
     int* err;
 };
@@ -359,6 +361,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
                     for (int u = 0; u < 16; u++) res[u] = (rrow && inside && j + u < p.n_valid) ? rrow[j + u] : 0.0f;
                 }
+                float pre[16];
+                if (p.pre) {
+                    const float* pr = p.pre + m * (long)p.pre_pitch + j;
+                    if (full16) {
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            const float4 t = *reinterpret_cast<const float4*>(pr + 4 * u);
+                            pre[4 * u] = t.x;
+                            pre[4 * u + 1] = t.y;
+                            pre[4 * u + 2] = t.z;
+                            pre[4 * u + 3] = t.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 16; u++) pre[u] = j + u < p.n_valid ? pr[u] : 0.0f;
+                    }
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 16; u++) pre[u] = 0.0f;
+                }
                 float yv[16], mv[16], iv[16];
                 if (bn_bwd) {
                     const float* yr = p.bn.y + m * (long)p.bn.y_pitch + chb;
@@ -406,7 +428,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 }
 #pragma unroll
                 for (int u = 0; u < 16; u++) {
-                    float x = v[u] + bias_s[j + u];
+                    float x = (v[u] + pre[u]) + bias_s[j + u];
                     if (p.silu) x = silu_fast(x);
                     x += res[u];
                     v[u] = inside ? x : 0.0f;
@@ -511,6 +533,8 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
     if (taps < 1 || taps > 9) throw std::runtime_error("conv_tc: taps");
     if ((ep.bn.stats_part || ep.bn.grad_part) && (grid.rows % 32 != 0 || ep.bn.channels < n_out || !ep.mask_halo))
         throw std::runtime_error("conv_tc: BatchNorm partials need masked 32-row groups covering every channel");
+    if (ep.pre && ((ep.pre_pitch % 4) != 0 || (reinterpret_cast<uintptr_t>(ep.pre) & 15) != 0))
+        throw std::runtime_error("conv_tc: pre-add input not 16-byte aligned");
     if (ep.bn.grad_part && (ep.bn.y_pitch % 4 != 0 || (reinterpret_cast<uintptr_t>(ep.bn.y) & 15) != 0))
         throw std::runtime_error("conv_tc: BatchNorm input not 16-byte aligned");
     // tap groups: taps sorted by shift, a new group wherever consecutive shifts are more than `gap`
@@ -626,6 +650,8 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         p.phase_rows = phase ? phase->consumer.rows : 0;
         p.phase_stride = phase ? phase->plane_rows : 0;
         p.bn = ep.bn;
+        p.pre = ep.pre ? ep.pre + n0 : nullptr;
+        p.pre_pitch = ep.pre_pitch;
         p.err = err;
         if (p.alloc_cols > 512) throw std::runtime_error("conv_tc: TMEM columns");
         CUtensorMap tb = make_map_2d(wk, (long)taps * kpad, n_rows, (long)taps * kpad, 32, n);
@@ -797,7 +823,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
 
 // dw[(o * ic + c) * taps + t] = sum_s ws[s][(t * kchunks + c / 32) * 32 + c % 32][o]
 __global__ void wgrad_reduce_kernel(const float* ws, int splits, long split_stride, int n, int ic, int taps,
-                                    int kchunks, float* dw) {
+                                    int kchunks, float* dw, int accumulate) {
     const long total = (long)n * ic * taps;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
         const int t = (int)(i % taps);
@@ -807,7 +833,7 @@ __global__ void wgrad_reduce_kernel(const float* ws, int splits, long split_stri
         const long row = (long)(t * kchunks + c / 32) * 32 + (c % 32);
         float s = 0.0f;
         for (int k = 0; k < splits; k++) s += ws[k * split_stride + row * n + o];
-        dw[i] = s;
+        dw[i] = accumulate ? dw[i] + s : s;
     }
 }
 
@@ -828,7 +854,7 @@ size_t wgrad_workspace_floats(int ic, int oc, int taps, long rows) {
 }
 
 void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, float* dw, float* ws, int* err,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, int accumulate) {
     if (dy.channels > 256) throw std::runtime_error("conv_tc_wgrad: more than 256 output channels");
     if (x.rows != dy.rows) throw std::runtime_error("conv_tc_wgrad: row mismatch");
     WgradParams p;
@@ -868,7 +894,8 @@ void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, fl
     const long split_stride = (long)p.m_tiles * kTileM * p.n;
     const long total = (long)dy.channels * x.channels * taps;
     const int blocks = (int)std::min<long>(4096, (total + 255) / 256);
-    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, splits, split_stride, p.n, x.channels, taps, p.kchunks, dw);
+    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, splits, split_stride, p.n, x.channels, taps, p.kchunks, dw,
+                                                    accumulate);
     launch_check("wgrad_reduce_kernel");
 }
 

@@ -56,6 +56,8 @@ struct ConvEpilogue {
     const float* residual = nullptr;  // added after SiLU (Bottleneck shortcut)
     int res_pitch = 0;
     int mask_halo = 1;                // 0: every row is a valid output (plain GEMM use)
+    const float* pre = nullptr;       // added to the accumulator before anything else (3xTF32 passes)
+    int pre_pitch = 0;
     BnEpilogue bn{};
 };
 
@@ -86,7 +88,10 @@ void conv_tc_strided(const View& phase_in, long plane_rows, long m_rows, const f
 // (dw[(o * ic + c) * taps + t]), fully overwritten.  `ws` is scratch of wgrad_workspace_floats() floats.
 size_t wgrad_workspace_floats(int ic, int oc, int taps, long rows);
 void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, float* dw, float* ws, int* err,
-                   cudaStream_t stream);
+                   cudaStream_t stream, int accumulate = 0);   // accumulate: dw += instead of dw =
+// 3xTF32 operand split of a view's channels: big = x rounded to TF32 (nearest, ties away), small =
+// x - big (exact); both written with the view's pitch at the same row / channel positions.
+void tf32_split(const View& src, float* big, float* small, cudaStream_t stream);
 
 // ---------------------------------------------------------------- layout helpers (layout.cu)
 void nchw_to_padded(const float* src, int batch, int c, const Grid& g, const View& dst, cudaStream_t stream);

@@ -333,6 +333,29 @@ void stem_conv(const uint8_t* rgb, int batch, int size, const float* w_host, con
     launch_check("stem_conv_kernel");
 }
 
+__device__ __forceinline__ float tf32_round(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+__global__ void tf32_split_kernel(const float* src, int pitch, int channels, long rows, float* big, float* small) {
+    const long total = rows * channels;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const long r = i / channels;
+        const long idx = r * pitch + (i - r * channels);
+        const float x = src[idx], b = tf32_round(x);
+        big[idx] = b;
+        small[idx] = x - b;
+    }
+}
+
+void tf32_split(const View& src, float* big, float* small, cudaStream_t stream) {
+    const long n = src.rows * src.channels;
+    tf32_split_kernel<<<blocks_for(n), 256, 0, stream>>>(src.base, src.pitch, src.channels, src.rows, big, small);
+    launch_check("tf32_split_kernel");
+}
+
 void rgb_to_phase(const uint8_t* rgb, int batch, int size, const PhaseOut& dst, cudaStream_t stream) {
     if (dst.pitch != 4) throw std::runtime_error("rgb_to_phase: stem input pitch must be 4");
     const long n = (long)batch * size * size;

@@ -80,6 +80,7 @@ void* Session::dalloc(size_t bytes) {
 View Session::alloc_view(int channels, const Grid& g) {
     const int pitch = round_up(channels, 4);
     const long rows = (long)B_ * g.rows;
+    sp_floats_ = std::max(sp_floats_, (size_t)rows * pitch);
     float* p = static_cast<float*>(dalloc((size_t)rows * pitch * sizeof(float)));
     return View{p, pitch, channels, rows};
 }
@@ -97,6 +98,9 @@ Session::Session(const sy_config& c) : cfg(c) {
         throw SyError(SY_ERR_INVALID_ARGUMENT, "bad rank / world_size");
     if (!(c.lr > 0) || !(c.momentum >= 0 && c.momentum < 1) || !(c.weight_decay >= 0))
         throw SyError(SY_ERR_INVALID_ARGUMENT, "bad optimizer hyper-parameters");
+    if (c.precision != SY_PRECISION_TF32 && c.precision != SY_PRECISION_3XTF32)
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "precision must be SY_PRECISION_TF32 or SY_PRECISION_3XTF32");
+    x3_ = c.precision == SY_PRECISION_3XTF32;
     device_ = c.device;
     SY_CUDA(cudaSetDevice(device_));
     SY_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
@@ -119,6 +123,10 @@ Session::Session(const sy_config& c) : cfg(c) {
         throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "unknown backbone");
     }
     build_head();
+    if (x3_) {
+        for (auto& p : sp_) p = static_cast<float*>(dalloc(sizeof(float) * sp_floats_));
+        for (auto& p : wsp_) p = static_cast<float*>(dalloc(sizeof(float) * wsp_floats_));
+    }
     // loss, truth, outputs
     const int anchors = levels_[0].h * levels_[0].w + levels_[1].h * levels_[1].w + levels_[2].h * levels_[2].w;
     loss_ws_ = dalloc(loss_workspace_bytes(B_, anchors, std::max(1, c.max_boxes), 10));
@@ -206,6 +214,7 @@ void Session::build_backbone() {
             const int pitch = round_up(op.ic, 4);
             op.phase_plane_rows = (long)B_ * gout.rows;
             float* buf = static_cast<float*>(dalloc(sizeof(float) * (size_t)pitch * 4 * op.phase_plane_rows));
+            sp_floats_ = std::max(sp_floats_, (size_t)pitch * 4 * op.phase_plane_rows);
             op.phase_in = View{buf, pitch, op.ic, 4 * op.phase_plane_rows};
             const PhaseOut po{buf, pitch, gout, op.phase_plane_rows};
             {
@@ -321,7 +330,7 @@ void Session::build_backbone() {
             if (q.type == 0 && q.has_res) read |= overlaps(q.res, op.out);
         }
         for (int l = 0; l < 3; l++) read |= overlaps(features_[l], op.out);
-        op.plain_out = read;
+        op.plain_out = read || x3_;   // 3xTF32 passes accumulate in the plain output
     }
     n_backbone = poff;
     backbone_params_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)poff));
@@ -329,6 +338,7 @@ void Session::build_backbone() {
         if (op.type != 0) continue;
         const int taps = op.k * op.k;
         op.wk = static_cast<float*>(dalloc(sizeof(float) * (size_t)op.oc * taps * round_up(op.ic, 32)));
+        wsp_floats_ = std::max(wsp_floats_, (size_t)op.oc * taps * round_up(op.ic, 32));
     }
 }
 
@@ -375,12 +385,13 @@ void Session::forward_backbone(int batch, const uint8_t* rgb_device) {
                 View i2 = in, o2 = out;
                 i2.rows = o2.rows = (long)batch * op.gin.rows;
                 prof_begin();
-                conv_tc_forward(i2, op.wk, op.oc, op.oc, op.k * op.k, 1, op.gin, o2, ep, d_flags_, stream_, po);
+                conv_fwd(i2, op.wk, (long)op.oc * op.k * op.k * round_up(op.ic, 32), op.oc, op.oc, op.k * op.k, 1,
+                         op.gin, o2, ep, po);
                 prof_end(2.0 * batch * op.oc * op.ic * op.k * op.k * op.gin.h * op.gin.w);
             } else {
                 prof_begin();
-                conv_tc_strided(op.phase_in, op.phase_plane_rows, (long)batch * op.gout.rows, op.wk, op.oc, op.gout,
-                                out, ep, d_flags_, stream_, po);
+                conv_strided(op.phase_in, op.phase_plane_rows, (long)batch * op.gout.rows, op.wk,
+                             (long)op.oc * 9 * round_up(op.ic, 32), op.oc, op.gout, out, ep, po);
                 prof_end(2.0 * batch * op.oc * op.ic * 9 * op.gout.h * op.gout.w);
             }
         }
@@ -510,6 +521,8 @@ void Session::build_head() {
             hb.kpad_out = round_up(b.oc, 32);
             hb.w_fwd = static_cast<float*>(dalloc(sizeof(float) * (size_t)b.oc * hb.taps * hb.kpad_in));
             hb.w_dgrad = static_cast<float*>(dalloc(sizeof(float) * (size_t)b.ic * hb.taps * hb.kpad_out));
+            wsp_floats_ = std::max(wsp_floats_, std::max((size_t)b.oc * hb.taps * hb.kpad_in,
+                                                         (size_t)b.ic * hb.taps * hb.kpad_out));
             ws = std::max(ws, wgrad_workspace_floats(b.ic, b.oc, hb.taps, (long)B_ * g.rows));
             max_oc = std::max(max_oc, b.oc);
             x = b.has_bn ? hb.a : hb.y;
@@ -552,8 +565,8 @@ void Session::forward_head(int batch) {
                 ep.bn.stats_part = bn_part_;
             }
             prof_begin();
-            conv_tc_forward(rows_of(hb.x, batch, g), hb.w_fwd, hb.b.oc, hb.b.oc, hb.taps, 1, g,
-                            rows_of(hb.y, batch, g), ep, d_flags_, stream_);
+            conv_fwd(rows_of(hb.x, batch, g), hb.w_fwd, (long)hb.b.oc * hb.taps * hb.kpad_in, hb.b.oc, hb.b.oc,
+                     hb.taps, 1, g, rows_of(hb.y, batch, g), ep, nullptr);
             prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w);
             if (hb.b.has_bn) {
                 bn_stats_fold(bn_part_, batch, g, hb.b.oc, cfg.bn_eps, hb.stats, hb.coef, stream_);
@@ -580,8 +593,7 @@ void Session::backward_head(int batch) {
                                       rows_of(hb.dy, batch, g), stream_);
                 }
                 if (hb.b.has_bias) bias_grad(hb.dy, batch, g, bias_part_, grads_ + hb.b_off, stream_);
-                conv_tc_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off,
-                              wgrad_ws_, d_flags_, stream_);
+                conv_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off);
                 if (i > 0) {
                     HeadBlock& prev = branch.blocks[i - 1];
                     ConvEpilogue ep;
@@ -596,8 +608,8 @@ void Session::backward_head(int batch) {
                         ep.bn.grad_part = bn_part_;
                     }
                     prof_begin();
-                    conv_tc_forward(rows_of(hb.dy, batch, g), hb.w_dgrad, hb.b.ic, hb.b.ic, hb.taps, -1, g,
-                                    rows_of(prev.g, batch, g), ep, d_flags_, stream_);
+                    conv_fwd(rows_of(hb.dy, batch, g), hb.w_dgrad, (long)hb.b.ic * hb.taps * hb.kpad_out, hb.b.ic,
+                             hb.b.ic, hb.taps, -1, g, rows_of(prev.g, batch, g), ep, nullptr);
                     prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w);
                 }
             }
@@ -791,6 +803,81 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
     if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "device wait limit exceeded");
     if (h_flags_[1]) throw SyError(SY_ERR_NONFINITE, "non-finite parameters after the update");
     return SY_OK;
+}
+
+// ------------------------------------------------------------------ convolution passes
+// 3xTF32: every FP32 operand x = big + small with big = x rounded to TF32 and small = x - big (exact);
+// the tensor core's TF32 products of (small, big), (big, small) and (big, big) are accumulated in that
+// order (smallest first) through the epilogue's pre-add, and only the last pass applies the layer's
+// bias / activation / residual / BatchNorm hooks / parity copy.  The dropped small x small term is
+// below FP32 rounding.
+View Session::split_view(const View& v, int slot, View* small) {
+    tf32_split(v, sp_[slot], sp_[slot + 1], stream_);
+    *small = View{sp_[slot + 1], v.pitch, v.channels, v.rows};
+    return View{sp_[slot], v.pitch, v.channels, v.rows};
+}
+
+const float* Session::split_weights(const float* wk, long n, const float** small) {
+    tf32_split(View{const_cast<float*>(wk), (int)n, (int)n, 1}, wsp_[0], wsp_[1], stream_);
+    *small = wsp_[1];
+    return wsp_[0];
+}
+
+void Session::conv_fwd(const View& in, const float* wk, long wk_floats, int n_rows, int n_out, int taps, int sign,
+                       const Grid& grid, const View& out, const ConvEpilogue& ep, const PhaseOut* po) {
+    if (!x3_) {
+        conv_tc_forward(in, wk, n_rows, n_out, taps, sign, grid, out, ep, d_flags_, stream_, po);
+        return;
+    }
+    View as;
+    const View ab = split_view(in, 0, &as);
+    const float* ws = nullptr;
+    const float* wb = split_weights(wk, wk_floats, &ws);
+    ConvEpilogue raw;
+    raw.mask_halo = ep.mask_halo;
+    conv_tc_forward(as, wb, n_rows, n_out, taps, sign, grid, out, raw, d_flags_, stream_, nullptr);
+    raw.pre = out.base;
+    raw.pre_pitch = out.pitch;
+    conv_tc_forward(ab, ws, n_rows, n_out, taps, sign, grid, out, raw, d_flags_, stream_, nullptr);
+    ConvEpilogue last = ep;
+    last.pre = out.base;
+    last.pre_pitch = out.pitch;
+    conv_tc_forward(ab, wb, n_rows, n_out, taps, sign, grid, out, last, d_flags_, stream_, po);
+}
+
+void Session::conv_strided(const View& phase_in, long plane_rows, long m_rows, const float* wk, long wk_floats,
+                           int oc, const Grid& gout, const View& out, const ConvEpilogue& ep, const PhaseOut* po) {
+    if (!x3_) {
+        conv_tc_strided(phase_in, plane_rows, m_rows, wk, oc, gout, out, ep, d_flags_, stream_, po);
+        return;
+    }
+    View as;
+    const View ab = split_view(phase_in, 0, &as);
+    const float* ws = nullptr;
+    const float* wb = split_weights(wk, wk_floats, &ws);
+    ConvEpilogue raw;
+    raw.mask_halo = ep.mask_halo;
+    conv_tc_strided(as, plane_rows, m_rows, wb, oc, gout, out, raw, d_flags_, stream_, nullptr);
+    raw.pre = out.base;
+    raw.pre_pitch = out.pitch;
+    conv_tc_strided(ab, plane_rows, m_rows, ws, oc, gout, out, raw, d_flags_, stream_, nullptr);
+    ConvEpilogue last = ep;
+    last.pre = out.base;
+    last.pre_pitch = out.pitch;
+    conv_tc_strided(ab, plane_rows, m_rows, wb, oc, gout, out, last, d_flags_, stream_, po);
+}
+
+void Session::conv_wgrad(const View& x, const View& dy, int taps, const Grid& grid, float* dw) {
+    if (!x3_) {
+        conv_tc_wgrad(x, dy, taps, grid, dw, wgrad_ws_, d_flags_, stream_);
+        return;
+    }
+    View xs, ds;
+    const View xb = split_view(x, 0, &xs);
+    const View db = split_view(dy, 2, &ds);
+    conv_tc_wgrad(xs, db, taps, grid, dw, wgrad_ws_, d_flags_, stream_, 0);
+    conv_tc_wgrad(xb, ds, taps, grid, dw, wgrad_ws_, d_flags_, stream_, 1);
+    conv_tc_wgrad(xb, db, taps, grid, dw, wgrad_ws_, d_flags_, stream_, 1);
 }
 
 // ------------------------------------------------------------------ conv launch timing

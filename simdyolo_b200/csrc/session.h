@@ -99,6 +99,14 @@ private:
     void backward_head(int batch);
     void refresh_head_weights();
     View alloc_view(int channels, const Grid& g);
+    // tensor-core convolutions, in TF32 or (precision 3xTF32) as three split-operand passes
+    void conv_fwd(const View& in, const float* wk, long wk_floats, int n_rows, int n_out, int taps, int sign,
+                  const Grid& grid, const View& out, const ConvEpilogue& ep, const PhaseOut* po);
+    void conv_strided(const View& phase_in, long plane_rows, long m_rows, const float* wk, long wk_floats, int oc,
+                      const Grid& gout, const View& out, const ConvEpilogue& ep, const PhaseOut* po);
+    void conv_wgrad(const View& x, const View& dy, int taps, const Grid& grid, float* dw);
+    View split_view(const View& v, int slot_big, View* small);
+    const float* split_weights(const float* wk, long n, const float** small);
     void* dalloc(size_t bytes);
 
     int device_ = 0;
@@ -152,6 +160,12 @@ private:
     int nsegs_ = 0;
     int adam_steps_[2] = {0, 0};
     int last_batch_ = 0;
+    // 3xTF32 operand split scratch: activations (4 buffers) and weights (2 buffers)
+    bool x3_ = false;
+    float* sp_[4] = {nullptr, nullptr, nullptr, nullptr};
+    size_t sp_floats_ = 0;
+    float* wsp_[2] = {nullptr, nullptr};
+    size_t wsp_floats_ = 0;
     // conv launch timing (conv_profile)
     bool prof_ = false;
     std::vector<cudaEvent_t> prof_ev_;
