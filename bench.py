@@ -29,13 +29,23 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-METRIC = "YOLOv8n head fine-tune images/s @640"
+# Workload presets (the benchmark configurations): model, image size, images per GPU, classes,
+# ground-truth boxes per image and their width / height range in pixels.
+WORKLOADS = {
+    "v8n-640": dict(model="yolov8n", image=640, batch=64, nc=80, boxes=(1, 8), wh=(8.0, 320.0),
+                    metric="YOLOv8n head fine-tune images/s @640",
+                    desc="config 2: YOLOv8n head fine-tune step (frozen backbone+neck fwd, Detect head fwd/bwd with "
+                         "per-image BN, DFL+CIoU+BCE with TAL top-10, SGD lr 0.01 m 0.937 wd 5e-4), 640x640 RGB24, "
+                         "1-8 GT boxes/image, 80 classes"),
+    "v8l-1024": dict(model="yolov8l", image=1024, batch=16, nc=20, boxes=(1, 30), wh=(12.0, 512.0),
+                     metric="YOLOv8l head fine-tune images/s @1024",
+                     desc="config 4: YOLOv8l head fine-tune step with a re-initialised 20-class head, 1024x1024 "
+                          "RGB24, 1-30 GT boxes/image (w/h log-uniform 12-512 px), SGD lr 0.01 m 0.937 wd 5e-4"),
+}
+METRIC = WORKLOADS["v8n-640"]["metric"]
 # mean DRAM bytes (read + write) per conv_fwd_tc_kernel launch of one batch-64 step, from an ncu
 # capture at batch 8 scaled by 8 (profiles/conv_fwd_dram_yolov8n_640.md)
 CONV_DRAM_BYTES_PER_LAUNCH = 8 * (905.531904e6 + 1.27616e6) / 74
-WORKLOAD = ("config 2: YOLOv8n head fine-tune step (frozen backbone+neck fwd, Detect head fwd/bwd with "
-            "per-image BN, DFL+CIoU+BCE with TAL top-10, SGD lr 0.01 m 0.937 wd 5e-4), 640x640 RGB24, "
-            "1-8 GT boxes/image, 80 classes")
 
 
 def parse():
@@ -44,15 +54,24 @@ def parse():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--batch", type=int, default=64, help="images per GPU")
-    p.add_argument("--image", type=int, default=640)
-    p.add_argument("--model", default="yolov8n")
+    p.add_argument("--workload", default="v8n-640", choices=sorted(WORKLOADS))
+    p.add_argument("--batch", type=int, default=None, help="images per GPU (default: the workload's)")
+    p.add_argument("--image", type=int, default=None)
+    p.add_argument("--model", default=None)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--precision", default="tf32", choices=["tf32", "3xtf32"],
                    help="3xtf32: the FP32 parity mode (three split-operand TF32 passes per convolution)")
     p.add_argument("--conv-sweep", action="store_true",
                    help="config 1: time forward / dgrad / wgrad of the isolated head convs (one JSON line each)")
-    return p.parse_args()
+    args = p.parse_args()
+    wl = WORKLOADS[args.workload]
+    args.batch = args.batch or wl["batch"]
+    args.image = args.image or wl["image"]
+    args.model = args.model or wl["model"]
+    args.nc, args.boxes, args.wh = wl["nc"], wl["boxes"], wl["wh"]
+    args.metric, args.workload_desc = wl["metric"], wl["desc"]
+    args.max_boxes = wl["boxes"][1]
+    return args
 
 
 class ClockSampler:
@@ -126,13 +145,13 @@ def cpu_threads():
 
 # ---------------------------------------------------------------- reference arm / CPU baseline
 
-def oracle_step_time(images_u8, truth, threads, model="yolov8n"):
+def oracle_step_time(images_u8, truth, threads, model="yolov8n", nc=80):
     """One step of the CPU restatement of the reference (oracle) over the given images."""
     import simdyolo_b200 as sy
     from simdyolo_b200 import data
     from oracle import oracle as O
     B, S = images_u8.shape[0], images_u8.shape[1]
-    cfg = sy.make_config(model, image_size=S, max_batch=B)
+    cfg = sy.make_config(model, image_size=S, max_batch=B, num_classes=nc)
     bd = O.BackboneDesc(S, cfg.width_mult, cfg.depth_mult, cfg.max_channels)
     hd = O.HeadDesc()
     hd.levels, hd.nc, hd.bins = 3, cfg.num_classes, 16
@@ -170,9 +189,11 @@ def oracle_step_time(images_u8, truth, threads, model="yolov8n"):
 def cpu_baseline(args, threads):
     from simdyolo_b200 import data
     rng = np.random.default_rng(1234)
-    sample = max(1, min(threads, args.batch))
-    imgs, truth = data.synthetic_batch(rng, sample, args.image, 80)
-    dt = oracle_step_time(imgs, truth, threads, args.model)
+    # about 10-30 s of CPU work: one image per thread, or a single image (all threads inside its GEMMs)
+    # for the 1024-pixel workload
+    sample = 1 if args.image >= 1024 else max(1, min(threads, args.batch))
+    imgs, truth = data.synthetic_batch(rng, sample, args.image, args.nc, args.boxes, args.wh)
+    dt = oracle_step_time(imgs, truth, threads, args.model, args.nc)
     return {"value": sample / dt, "unit": "images/s", "cores": threads, "kind": "port",
             "sample": f"one full step (backbone fwd + head fwd/bwd + loss + SGD) over {sample} of the batch's "
                       f"{args.image}x{args.image} images, OpenMP over images, {dt:.1f} s"}
@@ -187,25 +208,25 @@ def run_reference(args, rank, world):
     threads = cpu_threads()
     rng = np.random.default_rng(99)
     # bound the whole run to ~2-3 minutes: calibrate one image, then size the per-step sample
-    imgs, truth = data.synthetic_batch(rng, 1, args.image, 80)
-    t1 = oracle_step_time(imgs, truth, threads, args.model)
+    imgs, truth = data.synthetic_batch(rng, 1, args.image, args.nc, args.boxes, args.wh)
+    t1 = oracle_step_time(imgs, truth, threads, args.model, args.nc)
     budget = 150.0 / max(1, args.steps + args.warmup)
     per_step = int(max(1, min(args.batch, budget / max(t1, 1e-3))))
     if per_step > 1:
         per_step = max(1, min(per_step, threads) if per_step < threads else per_step // threads * threads)
     times = []
     for i in range(args.warmup + args.steps):
-        imgs, truth = data.synthetic_batch(rng, per_step, args.image, 80)
-        dt = oracle_step_time(imgs, truth, threads, args.model)
+        imgs, truth = data.synthetic_batch(rng, per_step, args.image, args.nc, args.boxes, args.wh)
+        dt = oracle_step_time(imgs, truth, threads, args.model, args.nc)
         if i >= args.warmup:
             times.append(dt)
     total = sum(times)
     value = per_step * len(times) / total
-    line = {"metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+    line = {"metric": args.metric, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000 * total / len(times), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
             "impl": "reference",
-            "config": {"workload": WORKLOAD, "global_batch_sampled": per_step, "image": args.image,
+            "config": {"workload": args.workload_desc, "global_batch_sampled": per_step, "image": args.image,
                        "parallelism": "cpu threads", "backbone": "random-init frozen (BN folded)"},
             "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": "port",
                              "sample": f"{per_step} image(s) per step of the {args.batch}-image batch; the "
@@ -284,7 +305,8 @@ def run_ours(args, rank, world, local_rank, dist):
     from simdyolo_b200 import dp
 
     nccl_id = dp.broadcast_nccl_id(dist, rank) if world > 1 else b""
-    cfg = sy.make_config(args.model, image_size=args.image, max_batch=args.batch, max_boxes=8, num_classes=80,
+    cfg = sy.make_config(args.model, image_size=args.image, max_batch=args.batch, max_boxes=args.max_boxes,
+                         num_classes=args.nc,
                          device=local_rank, rank=rank, world_size=world, nccl_id=nccl_id,
                          precision=sy.SY_PRECISION_3XTF32 if args.precision == "3xtf32" else sy.SY_PRECISION_TF32)
     sess = sy.Session(cfg)
@@ -295,7 +317,7 @@ def run_ours(args, rank, world, local_rank, dist):
 
     rng = np.random.default_rng(1000 + rank)
     nbatches = 4
-    batches = [data.synthetic_batch(rng, args.batch, args.image, 80) for _ in range(nbatches)]
+    batches = [data.synthetic_batch(rng, args.batch, args.image, args.nc, args.boxes, args.wh) for _ in range(nbatches)]
     dev_images = [torch.from_numpy(b[0]).to(f"cuda:{local_rank}") for b in batches]
     pinned = [torch.from_numpy(b[0]).pin_memory() for b in batches]
     truths = [b[1] for b in batches]
@@ -361,7 +383,7 @@ def run_ours(args, rank, world, local_rank, dist):
                 "achieved": achieved, "peak": tf32_sustained, "unit": "TFLOP/s", "frac": achieved / tf32_sustained,
                 "peak_note": f"dense TF32 = 1/2 of the {src} sustained bf16 GEMM rate "
                              f"({peaks.get('bf16_tflops_sustained', peaks['bf16_tflops'])} TF/s)",
-                "traffic": CONV_DRAM_BYTES_PER_LAUNCH * args.batch / 64 if args.image == 640 else None,
+                "traffic": CONV_DRAM_BYTES_PER_LAUNCH * args.batch / 64 if args.workload == "v8n-640" else None,
                 "traffic_note": "dram__bytes_read+write per conv_fwd_tc_kernel launch, mean over the 74 launches of "
                                 "one step captured with ncu at batch 8 and scaled by 8 (writes stay in L2 at that "
                                 "size); profiles/conv_fwd_dram_yolov8n_640.md",
@@ -378,11 +400,11 @@ def run_ours(args, rank, world, local_rank, dist):
         tf32_burst = peaks["bf16_tflops"] / 2.0
         roof["wgrad_p3_3x3_64"] = {"achieved": wg, "frac": wg / tf32_burst, "ms_per_launch": ms,
                                    "peak": tf32_burst, "note": "timed alone: burst TF32 denominator"}
-        line = {"metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+        line = {"metric": args.metric, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": args.precision,
                 "data": "synthetic (seeded uniform RGB24, random-init frozen backbone and head)",
-                "config": {"workload": WORKLOAD, "global_batch": world * args.batch, "per_gpu_batch": args.batch,
+                "config": {"workload": args.workload_desc, "global_batch": world * args.batch, "per_gpu_batch": args.batch,
                            "image": args.image, "parallelism": f"dp{world}",
                            "l2": "per-step working set is several GB of activations (>> 126 MB L2); no flush"},
                 "e2e": e2e, "gpu_launches": launches, "wall_s_timed": wall, "roofline": roof}

@@ -822,9 +822,11 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
 }
 
 // dw[(o * ic + c) * taps + t] = sum_s ws[s][(t * kchunks + c / 32) * 32 + c % 32][o]
-__global__ void wgrad_reduce_kernel(const float* ws, int splits, long split_stride, int n, int ic, int taps,
+// `n` is the workspace row stride (the MMA width, output channels rounded up to 16); `oc` the real
+// output channels, which alone bound the rows of dw that are written.
+__global__ void wgrad_reduce_kernel(const float* ws, int splits, long split_stride, int n, int oc, int ic, int taps,
                                     int kchunks, float* dw, int accumulate) {
-    const long total = (long)n * ic * taps;
+    const long total = (long)oc * ic * taps;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
         const int t = (int)(i % taps);
         const long rest = i / taps;
@@ -894,7 +896,8 @@ void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, fl
     const long split_stride = (long)p.m_tiles * kTileM * p.n;
     const long total = (long)dy.channels * x.channels * taps;
     const int blocks = (int)std::min<long>(4096, (total + 255) / 256);
-    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, splits, split_stride, p.n, x.channels, taps, p.kchunks, dw,
+    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, splits, split_stride, p.n, dy.channels, x.channels, taps,
+                                                    p.kchunks, dw,
                                                     accumulate);
     launch_check("wgrad_reduce_kernel");
 }

@@ -64,6 +64,8 @@ def test_conv_backward_data(n, ic, oc, h, w, k):
     (2, 256, 64, 20, 20, 3),
     (2, 64, 80, 20, 20, 1),
     (1, 32, 16, 8, 8, 3),
+    (2, 64, 20, 16, 16, 1),    # output channels not a multiple of the MMA width (20-class head)
+    (2, 48, 20, 12, 12, 3),
 ])
 def test_conv_backward_filter(n, ic, oc, h, w, k):
     rng = np.random.default_rng(3)

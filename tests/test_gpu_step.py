@@ -152,3 +152,39 @@ def test_oracle_full_step_matches_session_loss_over_steps():
         total = stats.box + stats.cls + stats.dfl
         assert abs(total - (res.box + res.cls + res.dfl)) <= 5 * TOL * (res.box + res.cls + res.dfl)
     assert rel_l2(s.flat_params() - params, op - params) < 1e-2
+
+
+def test_v8l_20_class_head_from_features_matches_oracle():
+    """Config-4 head (YOLOv8l widths: P3/P4/P5 = 256/512/512 channels, class hidden 256, re-initialised
+    20-class output) at a reduced image size: exercises N = 256 tiles and streamed weights."""
+    rng = np.random.default_rng(13)
+    s, cfg, params, buffers = make_session(256, 2, backbone=False, nc=20, max_boxes=30, model="yolov8l")
+    feats = features_for(cfg, 2, rng)
+    _, truth = data.synthetic_batch(rng, 2, 256, 20, boxes=(1, 30), wh=(12.0, 128.0))
+    stats = s.step_features(feats, truth)
+    losses, ograd, oparams, obuffers, ovel, conn = oracle_head_step(cfg, s.tensors, params, buffers,
+                                                                    np.zeros_like(params), feats, truth)
+    ocls = sum(l["cls"] for l in losses)
+    assert abs(stats.cls - ocls) <= TOL * abs(ocls)
+    assert stats.positives == sum(l["positives"] for l in losses)
+    assert rel_l2(s.last_gradients(), ograd) < TOL
+    assert rel_l2(s.flat_params() - params, oparams - params) < TOL
+    assert rel_l2(s.flat_buffers(), obuffers) < TOL
+
+
+def test_v8l_full_step_trunk_features_match_oracle():
+    image_size, batch = 128, 1
+    rng = np.random.default_rng(17)
+    s, cfg, params, buffers = make_session(image_size, batch, backbone=True, nc=20, max_boxes=30, model="yolov8l")
+    bparams = data.backbone_params(sy.MODELS["yolov8l"], seed=0)
+    s.set_backbone(bparams)
+    images, truth = data.synthetic_batch(rng, batch, image_size, 20, boxes=(1, 30), wh=(12.0, 64.0))
+    s.step(images, truth)
+    bd = backbone_desc(cfg)
+    f = [np.zeros((cfg.feature_channels[l], image_size >> (3 + l), image_size >> (3 + l)), np.float32)
+         for l in range(3)]
+    O.lib().syo_backbone_forward(C.byref(bd), bparams, images[0].ctypes.data_as(C.POINTER(C.c_uint8)), *f)
+    for l in range(3):
+        got = s.last_features(l, (1,) + f[l].shape)
+        # 1.5x the single-conv bound: the trunk chains ~70 TF32 convolutions
+        assert rel_l2(got[0], f[l]) < 1.5 * TOL, f"level {l}"

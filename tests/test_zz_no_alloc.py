@@ -50,6 +50,23 @@ def test_static_scratch_matches_allocating_entry_on_consecutive_calls(cases):
         assert rel_l2(got, want) < TF32_TOL
 
 
+def test_static_scratch_writes_only_the_callers_weight_gradient():
+    """Output channels that are not a multiple of the MMA width (20 classes): the entry point writes
+    exactly oc * ic * k * k floats into the caller's buffer and leaves the memory after it untouched."""
+    n, ic, oc, h, w, k = 2, 64, 20, 16, 16, 1
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((n, ic, h, w)).astype(np.float32)
+    dy = rng.standard_normal((n, oc, h, w)).astype(np.float32)
+    xp, dyp = to_padded(x), to_padded(dy)
+    size = oc * ic * k * k
+    buf = torch.full((size + 4096,), 7.0, dtype=torch.float32, device="cuda:0")
+    stream = torch.cuda.current_stream().cuda_stream
+    sy.conv2d_backward_filter_static(xp.data_ptr(), dyp.data_ptr(), n, ic, oc, h, w, k, buf.data_ptr(), stream)
+    out = buf.cpu().numpy()
+    assert np.all(out[size:] == 7.0)
+    assert rel_l2(out[:size].reshape(oc, ic, k, k), sy.conv2d_backward_filter(x, dy, k)) < TF32_TOL
+
+
 def test_static_scratch_rejects_oversized_problems():
     tiny = torch.zeros(16, device="cuda:0")
     with pytest.raises(NotImplementedError):
