@@ -218,17 +218,23 @@ def yolov8_backbone_convs(width: float, depth: float, max_channels: int):
     return convs
 
 
-def detect_head_blocks(feature_channels, nc: int, reg_max: int = 16):
-    """Ultralytics Detect head: cv2 = Conv(c,c2,3), Conv(c2,c2,3), Conv2d(c2,4*reg_max,1);
-    cv3 = Conv(c,c3,3), Conv(c3,c3,3), Conv2d(c3,nc,1) with c2 = max(16, ch0/4, 4*reg_max),
-    c3 = max(ch0, min(nc, 100))."""
+def detect_head_blocks(feature_channels, nc: int, reg_max: int = 16, dw_cls: bool = False):
+    """Ultralytics Detect head: cv2 = Conv(c,c2,3), Conv(c2,c2,3), Conv2d(c2,4*reg_max,1) with
+    c2 = max(16, ch0/4, 4*reg_max), c3 = max(ch0, min(nc, 100)); cv3 = Conv(c,c3,3), Conv(c3,c3,3),
+    Conv2d(c3,nc,1) (YOLOv8), or for YOLO11 (dw_cls) the nested [DWConv(c,c,3), Conv(c,c3,1)],
+    [DWConv(c3,c3,3), Conv(c3,c3,1)], Conv2d(c3,nc,1), flattened to five blocks as the reference's
+    training schema does (DetectionHead.cs:31-36).  Blocks: (ic, oc, k, groups, has_bn, has_bias)."""
     ch0 = feature_channels[0]
     c2 = max(16, ch0 // 4, 4 * reg_max)
     c3 = max(ch0, min(nc, 100))
     box, cls = [], []
     for c in feature_channels:
         box.append([(c, c2, 3, 1, 1, 0), (c2, c2, 3, 1, 1, 0), (c2, 4 * reg_max, 1, 1, 0, 1)])
-        cls.append([(c, c3, 3, 1, 1, 0), (c3, c3, 3, 1, 1, 0), (c3, nc, 1, 1, 0, 1)])
+        if dw_cls:
+            cls.append([(c, c, 3, c, 1, 0), (c, c3, 1, 1, 1, 0), (c3, c3, 3, c3, 1, 0), (c3, c3, 1, 1, 1, 0),
+                        (c3, nc, 1, 1, 0, 1)])
+        else:
+            cls.append([(c, c3, 3, 1, 1, 0), (c3, c3, 3, 1, 1, 0), (c3, nc, 1, 1, 0, 1)])
     return box, cls
 
 
@@ -237,7 +243,13 @@ MODELS = {
     "yolov8n": (0.25, 0.33, 1024),
     "yolov8s": (0.50, 0.33, 1024),
     "yolov8l": (1.00, 1.00, 512),
+    "yolo11s": (0.50, 0.50, 1024),
 }
+
+
+def model_family(model: str) -> str:
+    """'yolo11' (C3k2 / C2PSA trunk, depthwise class branch) or 'yolov8'."""
+    return "yolo11" if model.startswith("yolo11") else "yolov8"
 
 
 def make_config(model: str = "yolov8n", image_size: int = 640, max_batch: int = 8, max_boxes: int = 8,
@@ -258,7 +270,7 @@ def make_config(model: str = "yolov8n", image_size: int = 640, max_batch: int = 
     cfg.width_mult, cfg.depth_mult, cfg.max_channels = width, depth, max_ch
     for i in range(3):
         cfg.feature_channels[i] = feats[i]
-    box, cls = detect_head_blocks(feats, num_classes)
+    box, cls = detect_head_blocks(feats, num_classes, dw_cls=model_family(model) == "yolo11")
     cfg.n_box_blocks, cfg.n_cls_blocks = len(box[0]), len(cls[0])
     for lvl in range(3):
         for i, b in enumerate(box[lvl]):

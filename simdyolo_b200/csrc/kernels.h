@@ -93,6 +93,17 @@ void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, fl
 // x - big (exact); both written with the view's pitch at the same row / channel positions.
 void tf32_split(const View& src, float* big, float* small, cudaStream_t stream);
 
+// ---------------------------------------------------------------- depthwise convolution (dwconv.cu)
+// groups = channels (YOLO11 DWConv), k in {1, 3} (taps 1 or 9), FP32 on CUDA cores.  w: [c][taps].
+// y[m] = sum_t w[c][t] x[m + shift_sign * shift_t] at interior rows, 0 elsewhere; shift_sign -1 is the
+// data gradient.  `bn` as for the tensor-core epilogue: forward statistics partials, or the BatchNorm
+// backward of the layer whose gradient this pass produces (y then receives dz).
+void dw_conv(const View& x, const float* w, int taps, int shift_sign, const Grid& g, const View& y, const BnEpilogue& bn,
+             cudaStream_t stream);
+// dw[c][t] = sum over rows of dy[m][c] * x[m + shift_t][c], overwritten; ws: dw_wgrad_workspace_floats.
+size_t dw_wgrad_workspace_floats(int c, int taps, long rows);
+void dw_wgrad(const View& x, const View& dy, int taps, const Grid& g, float* dw, float* ws, cudaStream_t stream);
+
 // ---------------------------------------------------------------- layout helpers (layout.cu)
 void nchw_to_padded(const float* src, int batch, int c, const Grid& g, const View& dst, cudaStream_t stream);
 void padded_to_nchw(const View& src, int batch, int c, const Grid& g, float* dst, cudaStream_t stream);

@@ -423,13 +423,18 @@ void Session::build_head() {
             HeadBlock hb;
             hb.b = blocks[i];
             const sy_block& b = hb.b;
-            if (b.ic != ic || b.oc < 1 || b.oc > 256 || !(b.k == 1 || b.k == 3) || b.groups != 1)
+            hb.dw = b.groups > 1;
+            if (b.ic != ic || b.oc < 1 || b.oc > 512 || !(b.k == 1 || b.k == 3) ||
+                !(b.groups == 1 || (b.groups == b.ic && b.ic == b.oc)) || (b.groups == 1 && b.oc > 256))
                 throw SyError(SY_ERR_UNSUPPORTED_SHAPE,
-                              "head conv must be k 1 or 3, groups 1, <= 256 channels, chained channels (" + prefix + ")");
+                              "head conv must be k 1 or 3, groups 1 (<= 256 channels) or depthwise (groups = channels "
+                              "<= 512), chained channels (" + prefix + ")");
+            if (hb.dw && (b.has_bias || b.oc % 4 != 0))
+                throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "depthwise head convs need BatchNorm and a multiple of 4 channels");
             if ((i == n - 1) == (b.has_bn != 0)) throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "only the last block is a Conv2d");
             hb.taps = b.k * b.k;
             const std::string path = prefix + "." + block_path(i, n);
-            const long wn = (long)b.oc * b.ic * b.k * b.k;
+            const long wn = (long)b.oc * (b.ic / b.groups) * b.k * b.k;
             auto add_param = [&](const std::string& name, std::vector<int> shape, long numel, int decay) {
                 TensorEntry e{name, 0, shape, poff, numel, branch.box ? 1 : 0, decay};
                 tensors.push_back(e);
@@ -437,7 +442,8 @@ void Session::build_head() {
                 poff += numel;
                 return off;
             };
-            hb.w_off = add_param(path + (b.has_bn ? ".conv.weight" : ".weight"), {b.oc, b.ic, b.k, b.k}, wn, 1);
+            hb.w_off = add_param(path + (b.has_bn ? ".conv.weight" : ".weight"), {b.oc, b.ic / b.groups, b.k, b.k},
+                                 wn, 1);
             if (b.has_bias) hb.b_off = add_param(path + (b.has_bn ? ".conv.bias" : ".bias"), {b.oc}, b.oc, 0);
             if (b.has_bn) {
                 hb.g_off = add_param(path + ".bn.weight", {b.oc}, b.oc, 0);
@@ -517,13 +523,17 @@ void Session::build_head() {
             } else {
                 hb.dy = hb.g;
             }
-            hb.kpad_in = round_up(b.ic, 32);
-            hb.kpad_out = round_up(b.oc, 32);
-            hb.w_fwd = static_cast<float*>(dalloc(sizeof(float) * (size_t)b.oc * hb.taps * hb.kpad_in));
-            hb.w_dgrad = static_cast<float*>(dalloc(sizeof(float) * (size_t)b.ic * hb.taps * hb.kpad_out));
-            wsp_floats_ = std::max(wsp_floats_, std::max((size_t)b.oc * hb.taps * hb.kpad_in,
-                                                         (size_t)b.ic * hb.taps * hb.kpad_out));
-            ws = std::max(ws, wgrad_workspace_floats(b.ic, b.oc, hb.taps, (long)B_ * g.rows));
+            if (hb.dw) {
+                ws = std::max(ws, dw_wgrad_workspace_floats(b.oc, hb.taps, (long)B_ * g.rows));
+            } else {
+                hb.kpad_in = round_up(b.ic, 32);
+                hb.kpad_out = round_up(b.oc, 32);
+                hb.w_fwd = static_cast<float*>(dalloc(sizeof(float) * (size_t)b.oc * hb.taps * hb.kpad_in));
+                hb.w_dgrad = static_cast<float*>(dalloc(sizeof(float) * (size_t)b.ic * hb.taps * hb.kpad_out));
+                wsp_floats_ = std::max(wsp_floats_, std::max((size_t)b.oc * hb.taps * hb.kpad_in,
+                                                             (size_t)b.ic * hb.taps * hb.kpad_out));
+                ws = std::max(ws, wgrad_workspace_floats(b.ic, b.oc, hb.taps, (long)B_ * g.rows));
+            }
             max_oc = std::max(max_oc, b.oc);
             x = b.has_bn ? hb.a : hb.y;
         }
@@ -544,6 +554,7 @@ void Session::build_head() {
 void Session::refresh_head_weights() {
     for (auto& branch : branches_)
         for (auto& hb : branch.blocks) {
+            if (hb.dw) continue;   // depthwise kernels read the [c][taps] parameters directly
             weights_fwd_layout(params_ + hb.w_off, hb.b.oc, hb.b.ic, hb.taps, hb.kpad_in, hb.w_fwd, stream_);
             weights_dgrad_layout(params_ + hb.w_off, hb.b.oc, hb.b.ic, hb.taps, hb.kpad_out, hb.w_dgrad, stream_);
         }
@@ -564,10 +575,15 @@ void Session::forward_head(int batch) {
                 ep.bn.channels = hb.b.oc;
                 ep.bn.stats_part = bn_part_;
             }
-            prof_begin();
-            conv_fwd(rows_of(hb.x, batch, g), hb.w_fwd, (long)hb.b.oc * hb.taps * hb.kpad_in, hb.b.oc, hb.b.oc,
-                     hb.taps, 1, g, rows_of(hb.y, batch, g), ep, nullptr);
-            prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w);
+            if (hb.dw) {
+                dw_conv(rows_of(hb.x, batch, g), params_ + hb.w_off, hb.taps, 1, g, rows_of(hb.y, batch, g), ep.bn,
+                        stream_);
+            } else {
+                prof_begin();
+                conv_fwd(rows_of(hb.x, batch, g), hb.w_fwd, (long)hb.b.oc * hb.taps * hb.kpad_in, hb.b.oc, hb.b.oc,
+                         hb.taps, 1, g, rows_of(hb.y, batch, g), ep, nullptr);
+                prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w);
+            }
             if (hb.b.has_bn) {
                 bn_stats_fold(bn_part_, batch, g, hb.b.oc, cfg.bn_eps, hb.stats, hb.coef, stream_);
                 bn_silu_apply(rows_of(hb.y, batch, g), hb.coef, params_ + hb.g_off, params_ + hb.be_off, batch, g,
@@ -593,7 +609,11 @@ void Session::backward_head(int batch) {
                                       rows_of(hb.dy, batch, g), stream_);
                 }
                 if (hb.b.has_bias) bias_grad(hb.dy, batch, g, bias_part_, grads_ + hb.b_off, stream_);
-                conv_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off);
+                if (hb.dw)
+                    dw_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off,
+                             wgrad_ws_, stream_);
+                else
+                    conv_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off);
                 if (i > 0) {
                     HeadBlock& prev = branch.blocks[i - 1];
                     ConvEpilogue ep;
@@ -607,10 +627,15 @@ void Session::backward_head(int batch) {
                         ep.bn.beta = params_ + prev.be_off;
                         ep.bn.grad_part = bn_part_;
                     }
-                    prof_begin();
-                    conv_fwd(rows_of(hb.dy, batch, g), hb.w_dgrad, (long)hb.b.ic * hb.taps * hb.kpad_out, hb.b.ic,
-                             hb.b.ic, hb.taps, -1, g, rows_of(prev.g, batch, g), ep, nullptr);
-                    prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w);
+                    if (hb.dw) {
+                        dw_conv(rows_of(hb.dy, batch, g), params_ + hb.w_off, hb.taps, -1, g, rows_of(prev.g, batch, g),
+                                ep.bn, stream_);
+                    } else {
+                        prof_begin();
+                        conv_fwd(rows_of(hb.dy, batch, g), hb.w_dgrad, (long)hb.b.ic * hb.taps * hb.kpad_out,
+                                 hb.b.ic, hb.b.ic, hb.taps, -1, g, rows_of(prev.g, batch, g), ep, nullptr);
+                        prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w);
+                    }
                 }
             }
         }

@@ -30,6 +30,7 @@ struct TensorEntry {
 struct HeadBlock {
     sy_block b;
     int taps;
+    bool dw = false;            // depthwise (groups = channels): CUDA-core kernels, weights [c][taps]
     long w_off = -1, b_off = -1, g_off = -1, be_off = -1;
     long rm_off = -1, rv_off = -1, nt_off = -1;
     float* w_fwd = nullptr;     // [oc][taps][kpad_in]

@@ -84,3 +84,33 @@ def oracle_head_step(cfg: sy.Config, tensors, params, buffers, velocity, feature
         params[off:off + n], velocity[off:off + n] = w, v
         off += n
     return losses, summed, params, buffers, velocity, connected_any
+
+
+def oracle_head_step_adamw(cfg: sy.Config, tensors, params, buffers, m1, m2, steps, features, truth):
+    """Same head step followed by AdamW (torch.optim.AdamW form, lr / betas / eps / weight decay of the
+    config) for every tensor; steps = [always-connected group, box group] counts before this step,
+    the box group stepping only when an image connected it.  Returns (losses, grad, params, buffers,
+    m1, m2, steps) as updated copies."""
+    losses, grad, _, buffers_out, _, connected = oracle_head_step(cfg, tensors, params, buffers,
+                                                                  np.zeros_like(params), features, truth)
+    params, m1, m2 = params.astype(np.float32).copy(), m1.astype(np.float32).copy(), m2.astype(np.float32).copy()
+    steps = list(steps)
+    B = features[0].shape[0]
+    off = 0
+    for t in tensors:
+        if t["kind"] != 0:
+            continue
+        n = t["numel"]
+        box = t["name"].startswith("cv2")
+        decay = t["name"].endswith("conv.weight") or (t["name"].endswith(".weight") and len(t["shape"]) == 4)
+        has = connected if box else True
+        w, a, b, g = params[off:off + n].copy(), m1[off:off + n].copy(), m2[off:off + n].copy(), grad[off:off + n].copy()
+        rc = O.lib().syo_adamw_update(w, a, b, g, n, cfg.lr, cfg.beta1, cfg.beta2, cfg.adam_eps,
+                                      cfg.weight_decay if decay else 0.0, steps[1 if box else 0] + 1, B, int(has))
+        assert rc == 0
+        params[off:off + n], m1[off:off + n], m2[off:off + n] = w, a, b
+        off += n
+    steps[0] += 1
+    if connected:
+        steps[1] += 1
+    return losses, grad, params, buffers_out, m1, m2, steps

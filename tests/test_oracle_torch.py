@@ -162,3 +162,28 @@ def test_loss_gradients_match_autograd(seed):
         assert rel_l2(ours, ref.grad) < 1e-4
     for ours, ref in zip(db, tb):
         assert rel_l2(ours, ref.grad) < 1e-3
+
+
+def test_adamw_matches_torch_over_steps():
+    """Config 3's optimizer (the reference has no AdamW): the oracle's update against
+    torch.optim.AdamW on gradients already divided by the image count, with the step skipped for a
+    group without gradient (TrainingParameter.cs:24 semantics)."""
+    rng = np.random.default_rng(8)
+    n, images, lr, wd, b1, b2, eps = 257, 4, 1e-3, 0.05, 0.9, 0.999, 1e-8
+    w0 = rng.standard_normal(n).astype(np.float32)
+    w, m, v = w0.copy(), np.zeros(n, np.float32), np.zeros(n, np.float32)
+    tw = torch.tensor(w0, requires_grad=True)
+    opt = torch.optim.AdamW([tw], lr=lr, betas=(b1, b2), eps=eps, weight_decay=wd)
+    for step in range(1, 6):
+        g = (rng.standard_normal(n) * images).astype(np.float32)
+        gc = g.copy()
+        assert O.lib().syo_adamw_update(w, m, v, gc, n, lr, b1, b2, eps, wd, step, images, 1) == 0
+        assert not gc.any()   # gradients are cleared after the update
+        opt.zero_grad()
+        tw.grad = torch.tensor(g / np.float32(images))
+        opt.step()
+        np.testing.assert_allclose(w, tw.detach().numpy(), rtol=2e-6, atol=1e-7)
+    # no gradient: nothing moves
+    before = w.copy()
+    assert O.lib().syo_adamw_update(w, m, v, np.ones(n, np.float32), n, lr, b1, b2, eps, wd, 6, images, 0) == 0
+    assert np.array_equal(w, before)
