@@ -37,6 +37,12 @@ WORKLOADS = {
                     desc="config 2: YOLOv8n head fine-tune step (frozen backbone+neck fwd, Detect head fwd/bwd with "
                          "per-image BN, DFL+CIoU+BCE with TAL top-10, SGD lr 0.01 m 0.937 wd 5e-4), 640x640 RGB24, "
                          "1-8 GT boxes/image, 80 classes"),
+    "v11s-640": dict(model="yolo11s", image=640, batch=32, nc=80, boxes=(1, 20), wh=(8.0, 320.0),
+                     optimizer="adamw", lr=1e-3, weight_decay=0.05,
+                     metric="YOLO11s head fine-tune images/s @640",
+                     desc="config 3: YOLO11s head fine-tune step (frozen C3k2/SPPF/C2PSA trunk, Detect head with "
+                          "depthwise class branch), 640x640 RGB24, 1-20 GT boxes/image, 80 classes, AdamW lr 1e-3 "
+                          "wd 0.05"),
     "v8l-1024": dict(model="yolov8l", image=1024, batch=16, nc=20, boxes=(1, 30), wh=(12.0, 512.0),
                      metric="YOLOv8l head fine-tune images/s @1024",
                      desc="config 4: YOLOv8l head fine-tune step with a re-initialised 20-class head, 1024x1024 "
@@ -71,6 +77,9 @@ def parse():
     args.nc, args.boxes, args.wh = wl["nc"], wl["boxes"], wl["wh"]
     args.metric, args.workload_desc = wl["metric"], wl["desc"]
     args.max_boxes = wl["boxes"][1]
+    args.optimizer = wl.get("optimizer", "sgd")
+    args.lr = wl.get("lr", 0.01)
+    args.weight_decay = wl.get("weight_decay", 5e-4)
     return args
 
 
@@ -145,14 +154,15 @@ def cpu_threads():
 
 # ---------------------------------------------------------------- reference arm / CPU baseline
 
-def oracle_step_time(images_u8, truth, threads, model="yolov8n", nc=80):
+def oracle_step_time(images_u8, truth, threads, model="yolov8n", nc=80, optimizer="sgd", lr=0.01, weight_decay=5e-4):
     """One step of the CPU restatement of the reference (oracle) over the given images."""
     import simdyolo_b200 as sy
     from simdyolo_b200 import data
     from oracle import oracle as O
     B, S = images_u8.shape[0], images_u8.shape[1]
     cfg = sy.make_config(model, image_size=S, max_batch=B, num_classes=nc)
-    bd = O.BackboneDesc(S, cfg.width_mult, cfg.depth_mult, cfg.max_channels)
+    bd = O.BackboneDesc(S, cfg.width_mult, cfg.depth_mult, cfg.max_channels,
+                        1 if sy.model_family(model) == "yolo11" else 0)
     hd = O.HeadDesc()
     hd.levels, hd.nc, hd.bins = 3, cfg.num_classes, 16
     for l in range(3):
@@ -170,7 +180,7 @@ def oracle_step_time(images_u8, truth, threads, model="yolov8n", nc=80):
     L = O.lib()
     npar, nbuf = L.syo_head_param_count(C.byref(hd)), L.syo_head_buffer_count(C.byref(hd))
     rng = np.random.default_rng(0)
-    bp = data.backbone_params(sy.MODELS[model], 0)
+    bp = data.backbone_params(model, 0)
     params = (rng.uniform(-0.05, 0.05, npar)).astype(np.float32)
     buffers = np.zeros(nbuf, np.float32)
     vel, vel2 = np.zeros(npar, np.float32), np.zeros(npar, np.float32)
@@ -178,7 +188,7 @@ def oracle_step_time(images_u8, truth, threads, model="yolov8n", nc=80):
     flat = [bx for t in truth for bx in t]
     tb = O.boxes(flat)
     counts = np.array([len(t) for t in truth], np.int32)
-    opt = O.Optim(0.01, 0.937, 5e-4, 0, 0.9, 0.999, 1e-8)
+    opt = O.Optim(lr, 0.937, weight_decay, 1 if optimizer == "adamw" else 0, 0.9, 0.999, 1e-8)
     res = O.StepResult()
     t0 = time.perf_counter()
     L.syo_train_step(C.byref(bd), bp, C.byref(hd), params, buffers, vel, vel2, C.byref(opt), ptrs, tb, counts, B,
@@ -193,7 +203,8 @@ def cpu_baseline(args, threads):
     # for the 1024-pixel workload
     sample = 1 if args.image >= 1024 else max(1, min(threads, args.batch))
     imgs, truth = data.synthetic_batch(rng, sample, args.image, args.nc, args.boxes, args.wh)
-    dt = oracle_step_time(imgs, truth, threads, args.model, args.nc)
+    dt = oracle_step_time(imgs, truth, threads, args.model, args.nc, args.optimizer, args.lr,
+                          args.weight_decay)
     return {"value": sample / dt, "unit": "images/s", "cores": threads, "kind": "port",
             "sample": f"one full step (backbone fwd + head fwd/bwd + loss + SGD) over {sample} of the batch's "
                       f"{args.image}x{args.image} images, OpenMP over images, {dt:.1f} s"}
@@ -209,7 +220,8 @@ def run_reference(args, rank, world):
     rng = np.random.default_rng(99)
     # bound the whole run to ~2-3 minutes: calibrate one image, then size the per-step sample
     imgs, truth = data.synthetic_batch(rng, 1, args.image, args.nc, args.boxes, args.wh)
-    t1 = oracle_step_time(imgs, truth, threads, args.model, args.nc)
+    t1 = oracle_step_time(imgs, truth, threads, args.model, args.nc, args.optimizer, args.lr,
+                          args.weight_decay)
     budget = 150.0 / max(1, args.steps + args.warmup)
     per_step = int(max(1, min(args.batch, budget / max(t1, 1e-3))))
     if per_step > 1:
@@ -217,7 +229,8 @@ def run_reference(args, rank, world):
     times = []
     for i in range(args.warmup + args.steps):
         imgs, truth = data.synthetic_batch(rng, per_step, args.image, args.nc, args.boxes, args.wh)
-        dt = oracle_step_time(imgs, truth, threads, args.model, args.nc)
+        dt = oracle_step_time(imgs, truth, threads, args.model, args.nc, args.optimizer, args.lr,
+                          args.weight_decay)
         if i >= args.warmup:
             times.append(dt)
     total = sum(times)
@@ -306,14 +319,15 @@ def run_ours(args, rank, world, local_rank, dist):
 
     nccl_id = dp.broadcast_nccl_id(dist, rank) if world > 1 else b""
     cfg = sy.make_config(args.model, image_size=args.image, max_batch=args.batch, max_boxes=args.max_boxes,
-                         num_classes=args.nc,
+                         num_classes=args.nc, lr=args.lr, weight_decay=args.weight_decay,
+                         optimizer=sy.SY_OPT_ADAMW if args.optimizer == "adamw" else sy.SY_OPT_SGD,
                          device=local_rank, rank=rank, world_size=world, nccl_id=nccl_id,
                          precision=sy.SY_PRECISION_3XTF32 if args.precision == "3xtf32" else sy.SY_PRECISION_TF32)
     sess = sy.Session(cfg)
     params, buffers = data.head_params(sess, seed=0)
     sess.set_flat_params(params)
     sess.set_flat_buffers(buffers)
-    sess.set_backbone(data.backbone_params(sy.MODELS[args.model], seed=0))
+    sess.set_backbone(data.backbone_params(args.model, seed=0))
 
     rng = np.random.default_rng(1000 + rank)
     nbatches = 4

@@ -64,6 +64,7 @@ typedef struct sy_block {
 #define SY_PRECISION_3XTF32 1
 #define SY_BACKBONE_NONE 0    /* features are supplied by the caller (cached features)       */
 #define SY_BACKBONE_YOLOV8 1  /* YOLOv8 detection trunk (Conv, C2f, SPPF, Upsample, Concat) */
+#define SY_BACKBONE_YOLO11 2  /* YOLO11 trunk (Conv, C3k2, C3k, SPPF, C2PSA attention, Upsample, Concat) */
 
 typedef struct sy_config {
     int32_t struct_size;        /* sizeof(sy_config) */

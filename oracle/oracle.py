@@ -43,7 +43,7 @@ class HeadDesc(C.Structure):
 
 class BackboneDesc(C.Structure):
     _fields_ = [("image", C.c_int32), ("width_mult", C.c_float), ("depth_mult", C.c_float),
-                ("max_channels", C.c_int32)]
+                ("max_channels", C.c_int32), ("family", C.c_int32)]
 
 
 class Optim(C.Structure):

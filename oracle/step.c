@@ -294,8 +294,16 @@ static const float *take(bb_params *bp, long n)
     return r;
 }
 
-/* NCHW conv with folded BN bias and SiLU (PtModel.cs Conv/DWConv with act = SiLU) */
+/* NCHW conv with folded BN bias and SiLU, or no activation (PtModel.cs Conv/DWConv; act=False convs
+ * of the YOLO11 attention block have an Identity act) */
+static void bb_conv_act(bb_params *bp, const float *x, int ic, int h, int w, int oc, int k, int s, int act, float *y);
+
 static void bb_conv(bb_params *bp, const float *x, int ic, int h, int w, int oc, int k, int s, float *y)
+{
+    bb_conv_act(bp, x, ic, h, w, oc, k, s, 1, y);
+}
+
+static void bb_conv_act(bb_params *bp, const float *x, int ic, int h, int w, int oc, int k, int s, int act, float *y)
 {
     const float *wt = take(bp, (long)oc * ic * k * k);
     const float *bias = take(bp, oc);
@@ -326,7 +334,7 @@ static void bb_conv(bb_params *bp, const float *x, int ic, int h, int w, int oc,
         }
         for (int p = 0; p < so; p++) {
             float v = yr[p] + bias[o];
-            yr[p] = v / (1.0f + expf(-v));
+            yr[p] = act ? v / (1.0f + expf(-v)) : v;
         }
     }
     free(cols);
@@ -466,10 +474,239 @@ static void run_backbone(const syo_backbone_desc *d, bb_params *bp, const uint8_
 #undef ALLOC
 }
 
+/* ---- YOLO11 trunk (PtModel.cs cases C3k2, C3k, Bottleneck, C2PSA, PSABlock, Attention; layer list
+ * and channel / depth rules of the public YOLO11 definition).  Parameters in call order below. */
+
+/* depthwise conv (groups = channels) with folded BN bias, no activation (the attention's pe conv) */
+static void bb_dwconv(bb_params *bp, const float *x, int c, int h, int w, int k, float *y)
+{
+    const float *wt = take(bp, (long)c * k * k);
+    const float *bias = take(bp, c);
+    if (bp->count_only) return;
+    syo_grouped_conv_forward(x, c, h, w, wt, c, k, c, bias, y);
+}
+
+/* Bottleneck: cv2(cv1(x)) (+ x when shortcut and c1 == c2); cv1 c1 -> c2*e, both 3x3 */
+static void bb_bottleneck(bb_params *bp, const float *x, int c1, int c2, float e, int shortcut, int h, int w, float *y)
+{
+    int c_ = (int)(c2 * e), sp = h * w;
+    float *t = bp->count_only ? NULL : (float *)malloc(sizeof(float) * (size_t)c_ * sp);
+    bb_conv(bp, x, c1, h, w, c_, 3, 1, t);
+    bb_conv(bp, t, c_, h, w, c2, 3, 1, y);
+    if (shortcut && c1 == c2 && !bp->count_only)
+        for (size_t q = 0; q < (size_t)c2 * sp; q++) y[q] += x[q];
+    free(t);
+}
+
+/* C3k: cv3(cat(m(cv1(x)), cv2(x))), m = n Bottlenecks (c_, c_, e = 1), c_ = c2 / 2; order cv1, m, cv2, cv3 */
+static void bb_c3k(bb_params *bp, const float *x, int c1, int c2, int n, int shortcut, int h, int w, float *y)
+{
+    int c_ = (int)(c2 * 0.5f), sp = h * w;
+    float *cat = bp->count_only ? NULL : (float *)malloc(sizeof(float) * (size_t)2 * c_ * sp);
+    float *t = bp->count_only ? NULL : (float *)malloc(sizeof(float) * (size_t)c_ * sp);
+    bb_conv(bp, x, c1, h, w, c_, 1, 1, cat);
+    for (int i = 0; i < n; i++) {
+        bb_bottleneck(bp, cat, c_, c_, 1.0f, shortcut, h, w, t);
+        if (!bp->count_only) memcpy(cat, t, sizeof(float) * (size_t)c_ * sp);
+    }
+    bb_conv(bp, x, c1, h, w, c_, 1, 1, bp->count_only ? NULL : cat + (size_t)c_ * sp);
+    bb_conv(bp, cat, 2 * c_, h, w, c2, 1, 1, y);
+    free(t);
+    free(cat);
+}
+
+/* C3k2: C2f layout (cv1 -> two chunks, n modules on the last chunk, concat, cv2) whose modules are
+ * C3k(c, c, 2) or Bottleneck(c, c, e = 0.5), c = c2 * e */
+static void bb_c3k2(bb_params *bp, const float *x, int c1, int c2, int n, int c3k, float e, int h, int w, float *y)
+{
+    int c = (int)(c2 * e), sp = h * w;
+    float *cat = bp->count_only ? NULL : (float *)malloc(sizeof(float) * (size_t)(2 + n) * c * sp);
+    bb_conv(bp, x, c1, h, w, 2 * c, 1, 1, cat);
+    for (int i = 0; i < n; i++) {
+        const float *in = bp->count_only ? NULL : cat + (size_t)(1 + i) * c * sp;
+        float *out = bp->count_only ? NULL : cat + (size_t)(2 + i) * c * sp;
+        if (c3k) bb_c3k(bp, in, c, c, 2, 1, h, w, out);
+        else bb_bottleneck(bp, in, c, c, 0.5f, 1, h, w, out);
+    }
+    bb_conv(bp, cat, (2 + n) * c, h, w, c2, 1, 1, y);
+    free(cat);
+}
+
+/* Attention (PtModel.cs:429-439): qkv 1x1 (no act) -> per head [q kd | k kd | v hd] channels;
+ * softmax over keys of q^T k * kd^-0.5; out = v attn^T + pe(v) (depthwise 3x3, no act); proj 1x1 (no
+ * act).  Order: qkv, pe, proj. */
+static void bb_attention(bb_params *bp, const float *x, int dim, int heads, int h, int w, float *y)
+{
+    int hd = dim / heads, kd = (int)(hd * 0.5f), n = h * w, hch = dim + 2 * kd * heads;
+    float *qkv = bp->count_only ? NULL : (float *)malloc(sizeof(float) * (size_t)hch * n);
+    bb_conv_act(bp, x, dim, h, w, hch, 1, 1, 0, qkv);
+    float *v = NULL, *att = NULL, *pe = NULL;
+    if (!bp->count_only) {
+        v = (float *)malloc(sizeof(float) * (size_t)dim * n);
+        att = (float *)malloc(sizeof(float) * (size_t)dim * n);
+        pe = (float *)malloc(sizeof(float) * (size_t)dim * n);
+        float scale = 1.0f / sqrtf((float)kd);
+        float *row = (float *)malloc(sizeof(float) * (size_t)n);
+        for (int hh = 0; hh < heads; hh++) {
+            const float *q = qkv + (size_t)hh * (2 * kd + hd) * n, *k = q + (size_t)kd * n, *vv = k + (size_t)kd * n;
+            memcpy(v + (size_t)hh * hd * n, vv, sizeof(float) * (size_t)hd * n);
+            for (int i = 0; i < n; i++) {
+                float m = -INFINITY;
+                for (int j = 0; j < n; j++) {
+                    float sdot = 0.0f;
+                    for (int d2 = 0; d2 < kd; d2++) sdot += q[(size_t)d2 * n + i] * k[(size_t)d2 * n + j];
+                    row[j] = sdot * scale;
+                    if (row[j] > m) m = row[j];
+                }
+                float sum = 0.0f;
+                for (int j = 0; j < n; j++) {
+                    row[j] = expf(row[j] - m);
+                    sum += row[j];
+                }
+                for (int j = 0; j < n; j++) row[j] /= sum;
+                for (int d2 = 0; d2 < hd; d2++) {
+                    float a = 0.0f;
+                    for (int j = 0; j < n; j++) a += vv[(size_t)d2 * n + j] * row[j];
+                    att[((size_t)hh * hd + d2) * n + i] = a;
+                }
+            }
+        }
+        free(row);
+    }
+    bb_dwconv(bp, v, dim, h, w, 3, pe);
+    if (!bp->count_only)
+        for (size_t q = 0; q < (size_t)dim * n; q++) att[q] += pe[q];
+    bb_conv_act(bp, att, dim, h, w, dim, 1, 1, 0, y);
+    free(qkv);
+    free(v);
+    free(att);
+    free(pe);
+}
+
+/* PSABlock: x + attn(x), then + ffn (Conv(c, 2c, 1) SiLU, Conv(2c, c, 1) no act) */
+static void bb_psablock(bb_params *bp, const float *x, int c, int heads, int h, int w, float *y)
+{
+    int sp = h * w;
+    float *t = bp->count_only ? NULL : (float *)malloc(sizeof(float) * (size_t)2 * c * sp);
+    bb_attention(bp, x, c, heads, h, w, y);
+    if (!bp->count_only)
+        for (size_t q = 0; q < (size_t)c * sp; q++) y[q] += x[q];
+    bb_conv(bp, y, c, h, w, 2 * c, 1, 1, t);
+    float *f = bp->count_only ? NULL : (float *)malloc(sizeof(float) * (size_t)c * sp);
+    bb_conv_act(bp, t, 2 * c, h, w, c, 1, 1, 0, f);
+    if (!bp->count_only)
+        for (size_t q = 0; q < (size_t)c * sp; q++) y[q] += f[q];
+    free(t);
+    free(f);
+}
+
+/* C2PSA: cv1 -> chunks (a, b), b through n PSABlocks (heads = c / 64), cv2(cat(a, b)) */
+static void bb_c2psa(bb_params *bp, const float *x, int c1, int n, int h, int w, float *y)
+{
+    int c = (int)(c1 * 0.5f), sp = h * w;
+    float *cat = bp->count_only ? NULL : (float *)malloc(sizeof(float) * (size_t)2 * c * sp);
+    float *t = bp->count_only ? NULL : (float *)malloc(sizeof(float) * (size_t)c * sp);
+    bb_conv(bp, x, c1, h, w, 2 * c, 1, 1, cat);
+    for (int i = 0; i < n; i++) {
+        bb_psablock(bp, bp->count_only ? NULL : cat + (size_t)c * sp, c, c / 64 > 0 ? c / 64 : 1, h, w, t);
+        if (!bp->count_only) memcpy(cat + (size_t)c * sp, t, sizeof(float) * (size_t)c * sp);
+    }
+    bb_conv(bp, cat, 2 * c, h, w, c1, 1, 1, y);
+    free(t);
+    free(cat);
+}
+
+static void run_backbone_11(const syo_backbone_desc *d, bb_params *bp, const uint8_t *rgb, float *p3out, float *p4out,
+                            float *p5out)
+{
+    int S = d->image, co = bp->count_only;
+    int c64 = bb_channels(d, 64), c128 = bb_channels(d, 128), c256 = bb_channels(d, 256);
+    int c512 = bb_channels(d, 512), c1024 = bb_channels(d, 1024);
+    int n2 = bb_depth(d, 2);
+    int s2 = S / 2, s4 = S / 4, s8 = S / 8, s16 = S / 16, s32 = S / 32;
+#define ALLOC(n) (co ? NULL : (float *)malloc(sizeof(float) * (size_t)(n)))
+    float *img = ALLOC(3 * S * S);
+    if (!co)
+        for (int c = 0; c < 3; c++)
+            for (int p = 0; p < S * S; p++) img[(size_t)c * S * S + p] = (float)rgb[(size_t)p * 3 + c] / 255.0f;
+    float *l0 = ALLOC(c64 * s2 * s2);
+    bb_conv(bp, img, 3, S, S, c64, 3, 2, l0);
+    free(img);
+    float *l1 = ALLOC(c128 * s4 * s4);
+    bb_conv(bp, l0, c64, s2, s2, c128, 3, 2, l1);
+    free(l0);
+    float *l2 = ALLOC(c256 * s4 * s4);
+    bb_c3k2(bp, l1, c128, c256, n2, 0, 0.25f, s4, s4, l2);
+    free(l1);
+    float *l3 = ALLOC(c256 * s8 * s8);
+    bb_conv(bp, l2, c256, s4, s4, c256, 3, 2, l3);
+    free(l2);
+    float *l4 = ALLOC(c512 * s8 * s8);
+    bb_c3k2(bp, l3, c256, c512, n2, 0, 0.25f, s8, s8, l4);
+    free(l3);
+    float *l5 = ALLOC(c512 * s16 * s16);
+    bb_conv(bp, l4, c512, s8, s8, c512, 3, 2, l5);
+    float *l6 = ALLOC(c512 * s16 * s16);
+    bb_c3k2(bp, l5, c512, c512, n2, 1, 0.5f, s16, s16, l6);
+    free(l5);
+    float *l7 = ALLOC(c1024 * s32 * s32);
+    bb_conv(bp, l6, c512, s16, s16, c1024, 3, 2, l7);
+    float *l8 = ALLOC(c1024 * s32 * s32);
+    bb_c3k2(bp, l7, c1024, c1024, n2, 1, 0.5f, s32, s32, l8);
+    free(l7);
+    float *l9 = ALLOC(c1024 * s32 * s32);
+    bb_sppf(bp, l8, c1024, s32, s32, c1024, l9);
+    free(l8);
+    float *l10 = ALLOC(c1024 * s32 * s32);
+    bb_c2psa(bp, l9, c1024, n2, s32, s32, l10);
+    free(l9);
+    /* neck */
+    float *cat12 = ALLOC((c1024 + c512) * s16 * s16);
+    if (!co) {
+        upsample2(l10, c1024, s32, s32, cat12);
+        memcpy(cat12 + (size_t)c1024 * s16 * s16, l6, sizeof(float) * (size_t)c512 * s16 * s16);
+    }
+    free(l6);
+    float *l13 = ALLOC(c512 * s16 * s16);
+    bb_c3k2(bp, cat12, c1024 + c512, c512, n2, 0, 0.5f, s16, s16, l13);
+    free(cat12);
+    float *cat15 = ALLOC((c512 + c512) * s8 * s8);
+    if (!co) {
+        upsample2(l13, c512, s16, s16, cat15);
+        memcpy(cat15 + (size_t)c512 * s8 * s8, l4, sizeof(float) * (size_t)c512 * s8 * s8);
+    }
+    free(l4);
+    float *l16 = co ? NULL : p3out;
+    bb_c3k2(bp, cat15, c512 + c512, c256, n2, 0, 0.5f, s8, s8, l16);
+    free(cat15);
+    float *cat18 = ALLOC((c256 + c512) * s16 * s16);
+    bb_conv(bp, l16, c256, s8, s8, c256, 3, 2, cat18);
+    if (!co) memcpy(cat18 + (size_t)c256 * s16 * s16, l13, sizeof(float) * (size_t)c512 * s16 * s16);
+    free(l13);
+    float *l19 = co ? NULL : p4out;
+    bb_c3k2(bp, cat18, c256 + c512, c512, n2, 0, 0.5f, s16, s16, l19);
+    free(cat18);
+    float *cat21 = ALLOC((c512 + c1024) * s32 * s32);
+    bb_conv(bp, l19, c512, s16, s16, c512, 3, 2, cat21);
+    if (!co) memcpy(cat21 + (size_t)c512 * s32 * s32, l10, sizeof(float) * (size_t)c1024 * s32 * s32);
+    free(l10);
+    float *l22 = co ? NULL : p5out;
+    bb_c3k2(bp, cat21, c512 + c1024, c1024, n2, 1, 0.5f, s32, s32, l22);
+    free(cat21);
+#undef ALLOC
+}
+
+static void run_any_backbone(const syo_backbone_desc *d, bb_params *bp, const uint8_t *rgb, float *p3, float *p4,
+                             float *p5)
+{
+    if (d->family == 1) run_backbone_11(d, bp, rgb, p3, p4, p5);
+    else run_backbone(d, bp, rgb, p3, p4, p5);
+}
+
 long syo_backbone_param_count(const syo_backbone_desc *d)
 {
     bb_params bp = {NULL, 0, 1};
-    run_backbone(d, &bp, NULL, NULL, NULL, NULL);
+    run_any_backbone(d, &bp, NULL, NULL, NULL, NULL);
     return bp.off;
 }
 
@@ -484,7 +721,7 @@ void syo_backbone_forward(const syo_backbone_desc *d, const float *params, const
                           float *p5)
 {
     bb_params bp = {params, 0, 0};
-    run_backbone(d, &bp, rgb, p3, p4, p5);
+    run_any_backbone(d, &bp, rgb, p3, p4, p5);
 }
 
 /* ------------------------------------------------------------------ full step */

@@ -111,6 +111,7 @@ typedef struct {
     int32_t image;          /* square input size (multiple of 32) */
     float width_mult, depth_mult;
     int32_t max_channels;
+    int32_t family;         /* 0 YOLOv8 (C2f trunk), 1 YOLO11 (C3k2 / SPPF / C2PSA trunk) */
 } syo_backbone_desc;
 long syo_backbone_param_count(const syo_backbone_desc *d);
 void syo_backbone_feature_channels(const syo_backbone_desc *d, int32_t ch[3]);

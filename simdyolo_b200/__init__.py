@@ -29,6 +29,7 @@ SY_PRECISION_TF32 = 0
 SY_PRECISION_3XTF32 = 1
 SY_BACKBONE_NONE = 0
 SY_BACKBONE_YOLOV8 = 1
+SY_BACKBONE_YOLO11 = 2
 
 
 class SyError(RuntimeError):
@@ -218,6 +219,77 @@ def yolov8_backbone_convs(width: float, depth: float, max_channels: int):
     return convs
 
 
+def yolo11_backbone_convs(width: float, depth: float, max_channels: int):
+    """(oc, ic per group, k) of every conv of the YOLO11 trunk in parameter order (weights then bias),
+    the order in which the trunk builders take them: C3k2 = cv1, modules, cv2; C3k = cv1, bottlenecks,
+    cv2, cv3; Bottleneck = cv1, cv2; C2PSA = cv1, PSABlocks, cv2; PSABlock = attention (qkv, depthwise
+    pe, proj), ffn (two 1x1)."""
+    ch = lambda c: _make_div8(np.float32(min(c, max_channels)) * np.float32(width))
+    n2 = max(int(np.floor(2 * depth + 0.5)), 1)
+    c64, c128, c256, c512, c1024 = ch(64), ch(128), ch(256), ch(512), ch(1024)
+    convs = []
+
+    def conv(ic, oc, k):
+        convs.append((oc, ic, k))
+
+    def bottleneck(c1, c2, e):
+        c_ = int(c2 * e)
+        conv(c1, c_, 3)
+        conv(c_, c2, 3)
+
+    def c3k(c1, c2, n):
+        c_ = int(c2 * 0.5)
+        conv(c1, c_, 1)
+        for _ in range(n):
+            bottleneck(c_, c_, 1.0)
+        conv(c1, c_, 1)
+        conv(2 * c_, c2, 1)
+
+    def c3k2(c1, c2, use_c3k, e):
+        c = int(c2 * e)
+        conv(c1, 2 * c, 1)
+        for _ in range(n2):
+            if use_c3k:
+                c3k(c, c, 2)
+            else:
+                bottleneck(c, c, 0.5)
+        conv((2 + n2) * c, c2, 1)
+
+    def c2psa(c1):
+        c = int(c1 * 0.5)
+        heads = max(c // 64, 1)
+        hd = c // heads
+        kd = int(hd * 0.5)
+        conv(c1, 2 * c, 1)
+        for _ in range(n2):
+            conv(c, c + 2 * kd * heads, 1)   # qkv
+            convs.append((c, 1, 3))          # depthwise positional conv
+            conv(c, c, 1)                    # proj
+            conv(c, 2 * c, 1)                # ffn
+            conv(2 * c, c, 1)
+        conv(2 * c, c1, 1)
+
+    conv(3, c64, 3)
+    conv(c64, c128, 3)
+    c3k2(c128, c256, False, 0.25)
+    conv(c256, c256, 3)
+    c3k2(c256, c512, False, 0.25)
+    conv(c512, c512, 3)
+    c3k2(c512, c512, True, 0.5)
+    conv(c512, c1024, 3)
+    c3k2(c1024, c1024, True, 0.5)
+    conv(c1024, c1024 // 2, 1)   # SPPF
+    conv(c1024 // 2 * 4, c1024, 1)
+    c2psa(c1024)
+    c3k2(c1024 + c512, c512, False, 0.5)
+    c3k2(c512 + c512, c256, False, 0.5)
+    conv(c256, c256, 3)
+    c3k2(c256 + c512, c512, False, 0.5)
+    conv(c512, c512, 3)
+    c3k2(c512 + c1024, c1024, True, 0.5)
+    return convs
+
+
 def detect_head_blocks(feature_channels, nc: int, reg_max: int = 16, dw_cls: bool = False):
     """Ultralytics Detect head: cv2 = Conv(c,c2,3), Conv(c2,c2,3), Conv2d(c2,4*reg_max,1) with
     c2 = max(16, ch0/4, 4*reg_max), c3 = max(ch0, min(nc, 100)); cv3 = Conv(c,c3,3), Conv(c3,c3,3),
@@ -266,7 +338,8 @@ def make_config(model: str = "yolov8n", image_size: int = 640, max_batch: int = 
         cfg.nccl_id[i] = b
     cfg.image_size, cfg.max_batch, cfg.max_boxes = image_size, max_batch, max_boxes
     cfg.num_classes, cfg.reg_max = num_classes, 16
-    cfg.backbone = SY_BACKBONE_YOLOV8 if backbone else SY_BACKBONE_NONE
+    family = model_family(model)
+    cfg.backbone = (SY_BACKBONE_YOLO11 if family == "yolo11" else SY_BACKBONE_YOLOV8) if backbone else SY_BACKBONE_NONE
     cfg.width_mult, cfg.depth_mult, cfg.max_channels = width, depth, max_ch
     for i in range(3):
         cfg.feature_channels[i] = feats[i]

@@ -22,6 +22,7 @@ __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast
 // y[m] = sum_t w[c][t] x[m + sign * shift_t] at interior rows; BatchNorm partials as BnEpilogue says.
 __global__ void __launch_bounds__(kDwThreads) dw_conv_kernel(const float* x, int xpitch, long xrows, const float* w,
                                                              int taps, int sign, int c, Grid g, float* y, int ypitch,
+                                                             const float* bias, const float* res, int rpitch,
                                                              BnEpilogue bn) {
     __shared__ float w_s[32 * 9];
     __shared__ float red[32][33];
@@ -52,6 +53,17 @@ __global__ void __launch_bounds__(kDwThreads) dw_conv_kernel(const float* x, int
             v[2] = fmaf(w_s[(cl + 2) * taps + t], xv.z, v[2]);
             v[3] = fmaf(w_s[(cl + 3) * taps + t], xv.w, v[3]);
         }
+    }
+    if (inside && on && bias) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] += bias[ch + k];
+    }
+    if (inside && on && res) {
+        const float4 rv = ld4(res + m * rpitch + ch);   // may alias y: read before the store below
+        v[0] += rv.x;
+        v[1] += rv.y;
+        v[2] += rv.z;
+        v[3] += rv.w;
     }
     float xh[4] = {0.f, 0.f, 0.f, 0.f};
     if (bn.grad_part && inside && on) {
@@ -181,14 +193,17 @@ static void check_dw(const View& x, const View& y, int taps) {
 }
 
 void dw_conv(const View& x, const float* w, int taps, int shift_sign, const Grid& g, const View& y, const BnEpilogue& bn,
-             cudaStream_t stream) {
+             cudaStream_t stream, const float* bias, const View* residual) {
     check_dw(x, y, taps);
     if (y.rows % 32 != 0) throw std::runtime_error("dw_conv: rows must be whole 32-row groups");
     if ((bn.stats_part || bn.grad_part) && bn.channels < y.channels)
         throw std::runtime_error("dw_conv: BatchNorm partials must cover every channel");
     const dim3 grid((unsigned)(y.rows / 32), (unsigned)((y.channels + 31) / 32));
+    if (residual && (residual->pitch % 4 != 0 || (reinterpret_cast<uintptr_t>(residual->base) & 15)))
+        throw std::runtime_error("dw_conv: residual not 16-byte aligned");
     dw_conv_kernel<<<grid, kDwThreads, 0, stream>>>(x.base, x.pitch, x.rows, w, taps, shift_sign, y.channels, g, y.base,
-                                                   y.pitch, bn);
+                                                   y.pitch, bias, residual ? residual->base : nullptr,
+                                                   residual ? residual->pitch : 0, bn);
     launch_check("dw_conv_kernel");
 }
 

@@ -98,8 +98,15 @@ void tf32_split(const View& src, float* big, float* small, cudaStream_t stream);
 // y[m] = sum_t w[c][t] x[m + shift_sign * shift_t] at interior rows, 0 elsewhere; shift_sign -1 is the
 // data gradient.  `bn` as for the tensor-core epilogue: forward statistics partials, or the BatchNorm
 // backward of the layer whose gradient this pass produces (y then receives dz).
+// Optional per-channel `bias` and `residual` (same rows; may be y itself) are added after the sum.
 void dw_conv(const View& x, const float* w, int taps, int shift_sign, const Grid& g, const View& y, const BnEpilogue& bn,
-             cudaStream_t stream);
+             cudaStream_t stream, const float* bias = nullptr, const View* residual = nullptr);
+// Multi-head self-attention of the YOLO11 C2PSA block over the interior pixels of each image
+// (PtModel.cs Attention, :429-439): qkv holds per head [q key_dim | k key_dim | v head_dim] channels;
+// att[token][h * head_dim + d] = sum_j softmax_j(q_i . k_j * scale) v_j[d]; v_out receives v in that
+// same channel order (the input of the positional depthwise conv).  key_dim 32, head_dim 64.
+void attention(const View& qkv, int batch, const Grid& g, int heads, int key_dim, int head_dim, float scale,
+               const View& att, const View& v_out, cudaStream_t stream);
 // dw[c][t] = sum over rows of dy[m][c] * x[m + shift_t][c], overwritten; ws: dw_wgrad_workspace_floats.
 size_t dw_wgrad_workspace_floats(int c, int taps, long rows);
 void dw_wgrad(const View& x, const View& dy, int taps, const Grid& g, float* dw, float* ws, cudaStream_t stream);

@@ -108,7 +108,7 @@ Session::Session(const sy_config& c) : cfg(c) {
     SY_CUDA(cudaEventCreate(&ev1_));
     B_ = c.max_batch;
     for (int l = 0; l < 3; l++) levels_[l] = make_grid(c.image_size >> (3 + l), c.image_size >> (3 + l));
-    if (c.backbone == SY_BACKBONE_YOLOV8) {
+    if (c.backbone == SY_BACKBONE_YOLOV8 || c.backbone == SY_BACKBONE_YOLO11) {
         build_backbone();
     } else if (c.backbone == SY_BACKBONE_NONE) {
         for (int l = 0; l < 3; l++) {
@@ -144,7 +144,7 @@ Session::Session(const sy_config& c) : cfg(c) {
     SY_CUDA(cudaMallocHost(&h_pos_, sizeof(int) * B_));
     SY_CUDA(cudaMallocHost(&h_conn_, sizeof(int) * B_));
     SY_CUDA(cudaMallocHost(&h_abs_, sizeof(double) * kAbsSumBlocks));
-    if (c.backbone == SY_BACKBONE_YOLOV8) {
+    if (c.backbone != SY_BACKBONE_NONE) {
         SY_CUDA(cudaMallocHost(&h_rgb_, (size_t)B_ * c.image_size * c.image_size * 3));
         d_rgb_ = static_cast<uint8_t*>(dalloc((size_t)B_ * c.image_size * c.image_size * 3));
     }
@@ -173,145 +173,273 @@ Session::~Session() {
 }
 
 // ------------------------------------------------------------------ frozen trunk plan
-// YOLOv8 detection trunk: layer list, channel rule make_divisible(min(c, max) * width, 8) and
-// depth rule max(round(n * depth), 1); BatchNorm already folded into conv weight + bias.
-void Session::build_backbone() {
+// Trunk layer lists follow the public YOLOv8 / YOLO11 definitions: channel rule
+// make_divisible(min(c, max) * width, 8), depth rule max(round(n * depth), 1); BatchNorm is already
+// folded into every conv's weight + bias.  Parameters are taken in the order the builders call.
+static int trunk_channels(const sy_config& c, int ch) {
+    float x = (float)std::min(ch, c.max_channels) * c.width_mult;
+    return (int)std::ceil(x / 8.0f) * 8;
+}
+static int trunk_depth(const sy_config& c, int n) { return std::max((int)std::lround(n * c.depth_mult), 1); }
+
+void Session::tk_conv(const View& in, const Grid& gin, int oc, int k, int s, const View& out, const Grid& gout,
+                      const View* res, int act) {
+    BackboneOp op;
+    op.type = 0;
+    op.ic = in.channels;
+    op.oc = oc;
+    op.k = k;
+    op.stride = s;
+    op.act = act;
+    op.w_off = tk_poff_;
+    tk_poff_ += (long)oc * op.ic * k * k;
+    op.b_off = tk_poff_;
+    tk_poff_ += oc;
+    op.in = in;
+    op.out = out;
+    op.gin = gin;
+    op.gout = gout;
+    if (res) {
+        op.res = *res;
+        op.has_res = true;
+    }
+    if (s == 2 && in.base != img_.base) {  // the stem reads the RGB24 image directly (stem_conv)
+        // parity-split copy of the input, laid out on this conv's output grid
+        if (gin.h != 2 * gout.h || gin.w != 2 * gout.w || k != 3)
+            throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "stride-2 conv needs k 3 and an even input");
+        const int pitch = round_up(op.ic, 4);
+        op.phase_plane_rows = (long)B_ * gout.rows;
+        float* buf = static_cast<float*>(dalloc(sizeof(float) * (size_t)pitch * 4 * op.phase_plane_rows));
+        sp_floats_ = std::max(sp_floats_, (size_t)pitch * 4 * op.phase_plane_rows);
+        op.phase_in = View{buf, pitch, op.ic, 4 * op.phase_plane_rows};
+        const PhaseOut po{buf, pitch, gout, op.phase_plane_rows};
+        // the most recent conv that wrote exactly this view also writes the parity copy
+        bool found = false;
+        for (auto it = bops_.rbegin(); it != bops_.rend(); ++it)
+            if (it->type == 0 && it->out.base == in.base && it->out.channels == in.channels) {
+                it->has_phase_out = true;
+                it->phase_out = po;
+                found = true;
+                break;
+            }
+        if (!found) throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "stride-2 conv input has no producing conv");
+    }
+    bops_.push_back(op);
+}
+
+void Session::tk_sppf(const View& in, const Grid& g, int c2, const View& out) {
+    const int c = in.channels / 2;
+    View cat = alloc_view(4 * c, g);
+    tk_conv(in, g, c, 1, 1, slice(cat, 0, c), g, nullptr);
+    for (int i = 0; i < 3; i++) {
+        BackboneOp op;
+        op.type = 1;
+        op.in = slice(cat, i * c, c);
+        op.out = slice(cat, (i + 1) * c, c);
+        op.gin = op.gout = g;
+        bops_.push_back(op);
+    }
+    tk_conv(cat, g, c2, 1, 1, out, g, nullptr);
+}
+
+void Session::tk_upsample(const View& in, const Grid& gin, const View& out, const Grid& gout) {
+    BackboneOp op;
+    op.type = 2;
+    op.in = in;
+    op.out = out;
+    op.gin = gin;
+    op.gout = gout;
+    bops_.push_back(op);
+}
+
+void Session::build_trunk_v8() {
     const int S = cfg.image_size;
-    auto chan = [&](int c) {
-        float x = (float)std::min(c, cfg.max_channels) * cfg.width_mult;
-        return (int)std::ceil(x / 8.0f) * 8;
-    };
-    auto depth = [&](int n) { return std::max((int)std::lround(n * cfg.depth_mult), 1); };
-    const int c64 = chan(64), c128 = chan(128), c256 = chan(256), c512 = chan(512), c1024 = chan(1024);
-    const int n3 = depth(3), n6 = depth(6);
+    const int c64 = trunk_channels(cfg, 64), c128 = trunk_channels(cfg, 128), c256 = trunk_channels(cfg, 256);
+    const int c512 = trunk_channels(cfg, 512), c1024 = trunk_channels(cfg, 1024);
+    const int n3 = trunk_depth(cfg, 3), n6 = trunk_depth(cfg, 6);
     const Grid gS = make_grid(S, S), g2 = make_grid(S / 2, S / 2), g4 = make_grid(S / 4, S / 4);
     const Grid g8 = levels_[0], g16 = levels_[1], g32 = levels_[2];
-    long poff = 0;
-    auto conv = [&](const View& in, const Grid& gin, int oc, int k, int s, const View& out, const Grid& gout,
-                    const View* res) {
-        BackboneOp op;
-        op.type = 0;
-        op.ic = in.channels;
-        op.oc = oc;
-        op.k = k;
-        op.stride = s;
-        op.w_off = poff;
-        poff += (long)oc * op.ic * k * k;
-        op.b_off = poff;
-        poff += oc;
-        op.in = in;
-        op.out = out;
-        op.gin = gin;
-        op.gout = gout;
-        if (res) {
-            op.res = *res;
-            op.has_res = true;
-        }
-        if (s == 2 && in.base != img_.base) {  // the stem reads the RGB24 image directly (stem_conv)
-            // parity-split copy of the input, laid out on this conv's output grid
-            if (gin.h != 2 * gout.h || gin.w != 2 * gout.w || k != 3)
-                throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "stride-2 conv needs k 3 and an even input");
-            const int pitch = round_up(op.ic, 4);
-            op.phase_plane_rows = (long)B_ * gout.rows;
-            float* buf = static_cast<float*>(dalloc(sizeof(float) * (size_t)pitch * 4 * op.phase_plane_rows));
-            sp_floats_ = std::max(sp_floats_, (size_t)pitch * 4 * op.phase_plane_rows);
-            op.phase_in = View{buf, pitch, op.ic, 4 * op.phase_plane_rows};
-            const PhaseOut po{buf, pitch, gout, op.phase_plane_rows};
-            {
-                // the most recent conv that wrote exactly this view also writes the parity copy
-                bool found = false;
-                for (auto it = bops_.rbegin(); it != bops_.rend(); ++it)
-                    if (it->type == 0 && it->out.base == in.base && it->out.channels == in.channels) {
-                        it->has_phase_out = true;
-                        it->phase_out = po;
-                        found = true;
-                        break;
-                    }
-                if (!found) throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "stride-2 conv input has no producing conv");
-            }
-        }
-        bops_.push_back(op);
-    };
     auto c2f = [&](const View& in, const Grid& g, int c2, int n, bool shortcut, const View& out) {
         const int c = c2 / 2;
         View cat = alloc_view((2 + n) * c, g);
         View tmp = alloc_view(c, g);
-        conv(in, g, 2 * c, 1, 1, slice(cat, 0, 2 * c), g, nullptr);
+        tk_conv(in, g, 2 * c, 1, 1, slice(cat, 0, 2 * c), g, nullptr);
         for (int i = 0; i < n; i++) {
             View src = slice(cat, (1 + i) * c, c), dst = slice(cat, (2 + i) * c, c);
-            conv(src, g, c, 3, 1, tmp, g, nullptr);
-            conv(tmp, g, c, 3, 1, dst, g, shortcut ? &src : nullptr);
+            tk_conv(src, g, c, 3, 1, tmp, g, nullptr);
+            tk_conv(tmp, g, c, 3, 1, dst, g, shortcut ? &src : nullptr);
         }
-        conv(cat, g, c2, 1, 1, out, g, nullptr);
+        tk_conv(cat, g, c2, 1, 1, out, g, nullptr);
     };
-    auto sppf = [&](const View& in, const Grid& g, int c2, const View& out) {
-        const int c = in.channels / 2;
-        View cat = alloc_view(4 * c, g);
-        conv(in, g, c, 1, 1, slice(cat, 0, c), g, nullptr);
-        for (int i = 0; i < 3; i++) {
-            BackboneOp op;
-            op.type = 1;
-            op.in = slice(cat, i * c, c);
-            op.out = slice(cat, (i + 1) * c, c);
-            op.gin = op.gout = g;
-            bops_.push_back(op);
-        }
-        conv(cat, g, c2, 1, 1, out, g, nullptr);
-    };
-    auto upsample = [&](const View& in, const Grid& gin, const View& out, const Grid& gout) {
-        BackboneOp op;
-        op.type = 2;
-        op.in = in;
-        op.out = out;
-        op.gin = gin;
-        op.gout = gout;
-        bops_.push_back(op);
-    };
-    img_grid_ = gS;
-    // the image itself only exists as the stem's parity-split input; img_ just names it
-    img_ = View{static_cast<float*>(dalloc(256)), 4, 3, 0};
     View b0 = alloc_view(c64, g2);
-    conv(img_, gS, c64, 3, 2, b0, g2, nullptr);
+    tk_conv(img_, gS, c64, 3, 2, b0, g2, nullptr);
     View b1 = alloc_view(c128, g4);
-    conv(b0, g2, c128, 3, 2, b1, g4, nullptr);
+    tk_conv(b0, g2, c128, 3, 2, b1, g4, nullptr);
     View b2 = alloc_view(c128, g4);
     c2f(b1, g4, c128, n3, true, b2);
     View b3 = alloc_view(c256, g8);
-    conv(b2, g4, c256, 3, 2, b3, g8, nullptr);
+    tk_conv(b2, g4, c256, 3, 2, b3, g8, nullptr);
     View cat14 = alloc_view(c512 + c256, g8);
     View l4 = slice(cat14, c512, c256);
     c2f(b3, g8, c256, n6, true, l4);
     View b5 = alloc_view(c512, g16);
-    conv(l4, g8, c512, 3, 2, b5, g16, nullptr);
+    tk_conv(l4, g8, c512, 3, 2, b5, g16, nullptr);
     View cat11 = alloc_view(c1024 + c512, g16);
     View l6 = slice(cat11, c1024, c512);
     c2f(b5, g16, c512, n6, true, l6);
     View b7 = alloc_view(c1024, g32);
-    conv(l6, g16, c1024, 3, 2, b7, g32, nullptr);
+    tk_conv(l6, g16, c1024, 3, 2, b7, g32, nullptr);
     View b8 = alloc_view(c1024, g32);
     c2f(b7, g32, c1024, n3, true, b8);
     View cat20 = alloc_view(c512 + c1024, g32);
     View l9 = slice(cat20, c512, c1024);
-    sppf(b8, g32, c1024, l9);
-    upsample(l9, g32, slice(cat11, 0, c1024), g16);
+    tk_sppf(b8, g32, c1024, l9);
+    tk_upsample(l9, g32, slice(cat11, 0, c1024), g16);
     View cat17 = alloc_view(c256 + c512, g16);
     View l12 = slice(cat17, c256, c512);
     c2f(cat11, g16, c512, n3, false, l12);
-    upsample(l12, g16, slice(cat14, 0, c512), g8);
+    tk_upsample(l12, g16, slice(cat14, 0, c512), g8);
     View p3 = alloc_view(c256, g8);
     c2f(cat14, g8, c256, n3, false, p3);
-    conv(p3, g8, c256, 3, 2, slice(cat17, 0, c256), g16, nullptr);
+    tk_conv(p3, g8, c256, 3, 2, slice(cat17, 0, c256), g16, nullptr);
     View p4 = alloc_view(c512, g16);
     c2f(cat17, g16, c512, n3, false, p4);
-    conv(p4, g16, c512, 3, 2, slice(cat20, 0, c512), g32, nullptr);
+    tk_conv(p4, g16, c512, 3, 2, slice(cat20, 0, c512), g32, nullptr);
     View p5 = alloc_view(c1024, g32);
     c2f(cat20, g32, c1024, n3, false, p5);
     features_[0] = p3;
     features_[1] = p4;
     features_[2] = p5;
-    feat_ch_[0] = c256;
-    feat_ch_[1] = c512;
-    feat_ch_[2] = c1024;
+}
+
+// YOLO11 trunk (PtModel.cs cases C3k2, C3k, Bottleneck, C2PSA, PSABlock, Attention).
+void Session::build_trunk_11() {
+    const int S = cfg.image_size;
+    const int c64 = trunk_channels(cfg, 64), c128 = trunk_channels(cfg, 128), c256 = trunk_channels(cfg, 256);
+    const int c512 = trunk_channels(cfg, 512), c1024 = trunk_channels(cfg, 1024);
+    const int n2 = trunk_depth(cfg, 2);
+    const Grid gS = make_grid(S, S), g2 = make_grid(S / 2, S / 2), g4 = make_grid(S / 4, S / 4);
+    const Grid g8 = levels_[0], g16 = levels_[1], g32 = levels_[2];
+    // Bottleneck: cv2(cv1(x)) (+ x); `out` may be `x` itself (the residual is read before the write)
+    auto bottleneck = [&](const View& x, const Grid& g, int c2, float e, bool shortcut, const View& out) {
+        const int c_ = (int)(c2 * e);
+        View t = alloc_view(c_, g);
+        tk_conv(x, g, c_, 3, 1, t, g, nullptr);
+        tk_conv(t, g, c2, 3, 1, out, g, (shortcut && x.channels == c2) ? &x : nullptr);
+    };
+    // C3k: cv3(cat(m(cv1(x)), cv2(x))), m = n Bottlenecks with e = 1
+    auto c3k = [&](const View& x, const Grid& g, int c2, int n, const View& out) {
+        const int c_ = (int)(c2 * 0.5f);
+        View cat = alloc_view(2 * c_, g);
+        View a = slice(cat, 0, c_), b = slice(cat, c_, c_);
+        tk_conv(x, g, c_, 1, 1, a, g, nullptr);
+        for (int i = 0; i < n; i++) bottleneck(a, g, c_, 1.0f, true, a);
+        tk_conv(x, g, c_, 1, 1, b, g, nullptr);
+        tk_conv(cat, g, c2, 1, 1, out, g, nullptr);
+    };
+    // C3k2: C2f layout whose modules are C3k(c, c, 2) or Bottleneck(c, c, e = 0.5)
+    auto c3k2 = [&](const View& x, const Grid& g, int c2, bool use_c3k, float e, const View& out) {
+        const int c = (int)(c2 * e);
+        View cat = alloc_view((2 + n2) * c, g);
+        tk_conv(x, g, 2 * c, 1, 1, slice(cat, 0, 2 * c), g, nullptr);
+        for (int i = 0; i < n2; i++) {
+            View src = slice(cat, (1 + i) * c, c), dst = slice(cat, (2 + i) * c, c);
+            if (use_c3k) c3k(src, g, c, 2, dst);
+            else bottleneck(src, g, c, 0.5f, true, dst);
+        }
+        tk_conv(cat, g, c2, 1, 1, out, g, nullptr);
+    };
+    // PSABlock in place on x: x += proj(attention(qkv(x)) + pe(v)); x += ffn(x)
+    auto psablock = [&](const View& x, const Grid& g, int c, int heads) {
+        const int hd = c / heads, kd = (int)(hd * 0.5f), hch = c + 2 * kd * heads;
+        View qkv = alloc_view(hch, g), att = alloc_view(c, g), v = alloc_view(c, g), t = alloc_view(2 * c, g);
+        tk_conv(x, g, hch, 1, 1, qkv, g, nullptr, 0);
+        BackboneOp at;
+        at.type = 4;
+        at.in = qkv;
+        at.out = att;
+        at.aux = v;
+        at.heads = heads;
+        at.ic = hd;
+        at.oc = kd;
+        at.gin = at.gout = g;
+        bops_.push_back(at);
+        BackboneOp pe;   // depthwise 3x3 positional conv on v, added to the attention output
+        pe.type = 3;
+        pe.ic = pe.oc = c;
+        pe.k = 3;
+        pe.w_off = tk_poff_;
+        tk_poff_ += (long)c * 9;
+        pe.b_off = tk_poff_;
+        tk_poff_ += c;
+        pe.in = v;
+        pe.out = att;
+        pe.res = att;
+        pe.has_res = true;
+        pe.gin = pe.gout = g;
+        bops_.push_back(pe);
+        tk_conv(att, g, c, 1, 1, x, g, &x, 0);
+        tk_conv(x, g, 2 * c, 1, 1, t, g, nullptr);
+        tk_conv(t, g, c, 1, 1, x, g, &x, 0);
+    };
+    auto c2psa = [&](const View& x, const Grid& g, int c1, const View& out) {
+        const int c = (int)(c1 * 0.5f);
+        View cat = alloc_view(2 * c, g);
+        tk_conv(x, g, 2 * c, 1, 1, cat, g, nullptr);
+        for (int i = 0; i < n2; i++) psablock(slice(cat, c, c), g, c, std::max(c / 64, 1));
+        tk_conv(cat, g, c1, 1, 1, out, g, nullptr);
+    };
+    View b0 = alloc_view(c64, g2);
+    tk_conv(img_, gS, c64, 3, 2, b0, g2, nullptr);
+    View b1 = alloc_view(c128, g4);
+    tk_conv(b0, g2, c128, 3, 2, b1, g4, nullptr);
+    View b2 = alloc_view(c256, g4);
+    c3k2(b1, g4, c256, false, 0.25f, b2);
+    View b3 = alloc_view(c256, g8);
+    tk_conv(b2, g4, c256, 3, 2, b3, g8, nullptr);
+    View cat15 = alloc_view(c512 + c512, g8);
+    View l4 = slice(cat15, c512, c512);
+    c3k2(b3, g8, c512, false, 0.25f, l4);
+    View b5 = alloc_view(c512, g16);
+    tk_conv(l4, g8, c512, 3, 2, b5, g16, nullptr);
+    View cat12 = alloc_view(c1024 + c512, g16);
+    View l6 = slice(cat12, c1024, c512);
+    c3k2(b5, g16, c512, true, 0.5f, l6);
+    View b7 = alloc_view(c1024, g32);
+    tk_conv(l6, g16, c1024, 3, 2, b7, g32, nullptr);
+    View b8 = alloc_view(c1024, g32);
+    c3k2(b7, g32, c1024, true, 0.5f, b8);
+    View b9 = alloc_view(c1024, g32);
+    tk_sppf(b8, g32, c1024, b9);
+    View cat21 = alloc_view(c512 + c1024, g32);
+    View l10 = slice(cat21, c512, c1024);
+    c2psa(b9, g32, c1024, l10);
+    tk_upsample(l10, g32, slice(cat12, 0, c1024), g16);
+    View cat18 = alloc_view(c256 + c512, g16);
+    View l13 = slice(cat18, c256, c512);
+    c3k2(cat12, g16, c512, false, 0.5f, l13);
+    tk_upsample(l13, g16, slice(cat15, 0, c512), g8);
+    View p3 = alloc_view(c256, g8);
+    c3k2(cat15, g8, c256, false, 0.5f, p3);
+    tk_conv(p3, g8, c256, 3, 2, slice(cat18, 0, c256), g16, nullptr);
+    View p4 = alloc_view(c512, g16);
+    c3k2(cat18, g16, c512, false, 0.5f, p4);
+    tk_conv(p4, g16, c512, 3, 2, slice(cat21, 0, c512), g32, nullptr);
+    View p5 = alloc_view(c1024, g32);
+    c3k2(cat21, g32, c1024, true, 0.5f, p5);
+    features_[0] = p3;
+    features_[1] = p4;
+    features_[2] = p5;
+}
+
+void Session::build_backbone() {
+    img_grid_ = make_grid(cfg.image_size, cfg.image_size);
+    // the image itself only exists as the stem's parity-split input; img_ just names it
+    img_ = View{static_cast<float*>(dalloc(256)), 4, 3, 0};
+    tk_poff_ = 0;
+    if (cfg.backbone == SY_BACKBONE_YOLO11) build_trunk_11();
+    else build_trunk_v8();
+    for (int l = 0; l < 3; l++) feat_ch_[l] = features_[l].channels;
     // A conv whose output is read only through its parity-split copy (by stride-2 convs) skips the
     // plain write: no other op's input or residual, and no feature map, overlaps that output.
     auto span_of = [](const View& v) {
@@ -327,13 +455,13 @@ void Session::build_backbone() {
         for (const auto& q : bops_) {
             if (&q == &op) continue;
             if (q.type != 0 || q.stride == 1) read |= overlaps(q.in, op.out);
-            if (q.type == 0 && q.has_res) read |= overlaps(q.res, op.out);
+            if (q.has_res) read |= overlaps(q.res, op.out);
         }
         for (int l = 0; l < 3; l++) read |= overlaps(features_[l], op.out);
         op.plain_out = read || x3_;   // 3xTF32 passes accumulate in the plain output
     }
-    n_backbone = poff;
-    backbone_params_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)poff));
+    n_backbone = tk_poff_;
+    backbone_params_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)tk_poff_));
     for (auto& op : bops_) {
         if (op.type != 0) continue;
         const int taps = op.k * op.k;
@@ -343,7 +471,7 @@ void Session::build_backbone() {
 }
 
 int Session::set_backbone(const float* host, long count) {
-    if (cfg.backbone != SY_BACKBONE_YOLOV8 || count != n_backbone)
+    if (cfg.backbone == SY_BACKBONE_NONE || count != n_backbone)
         throw SyError(SY_ERR_INVALID_ARGUMENT, "backbone parameter count mismatch");
     SY_CUDA(cudaMemcpyAsync(backbone_params_, host, sizeof(float) * count, cudaMemcpyHostToDevice, stream_));
     for (auto& op : bops_) {
@@ -371,10 +499,19 @@ void Session::forward_backbone(int batch, const uint8_t* rgb_device) {
             maxpool5_padded(in, out, batch, op.gin, stream_);
         } else if (op.type == 2) {
             upsample2_padded(in, op.gin, out, op.gout, batch, stream_);
+        } else if (op.type == 3) {
+            View i2 = in, o2 = out, r2 = op.res;
+            i2.rows = o2.rows = r2.rows = (long)batch * op.gin.rows;
+            dw_conv(i2, backbone_params_ + op.w_off, op.k * op.k, 1, op.gin, o2, BnEpilogue{}, stream_,
+                    backbone_params_ + op.b_off, op.has_res ? &r2 : nullptr);
+        } else if (op.type == 4) {
+            View i2 = in, o2 = out, a2 = op.aux;
+            i2.rows = o2.rows = a2.rows = (long)batch * op.gin.rows;
+            attention(i2, batch, op.gin, op.heads, op.oc, op.ic, 1.0f / std::sqrt((float)op.oc), o2, a2, stream_);
         } else {
             ConvEpilogue ep;
             ep.bias = backbone_params_ + op.b_off;
-            ep.silu = 1;
+            ep.silu = op.act;
             if (op.has_res) {
                 ep.residual = op.res.base;
                 ep.res_pitch = op.res.pitch;
@@ -662,7 +799,7 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
         }
         h_box_off_[b + 1] = (int)k;
     }
-    if (rgb && (cfg.backbone != SY_BACKBONE_YOLOV8 || !backbone_ready_))
+    if (rgb && (cfg.backbone == SY_BACKBONE_NONE || !backbone_ready_))
         throw SyError(SY_ERR_INVALID_ARGUMENT, "backbone weights not set");
     prof_n_ = 0;
     SY_CUDA(cudaEventRecord(ev0_, stream_));

@@ -50,8 +50,11 @@ struct Branch {
 };
 
 struct BackboneOp {
-    int type;                   // 0 conv, 1 maxpool5, 2 upsample2
+    int type;                   // 0 conv, 1 maxpool5, 2 upsample2, 3 depthwise conv, 4 attention
     int ic = 0, oc = 0, k = 0, stride = 1;
+    int act = 1;                // conv: SiLU (1) or none (0, the YOLO11 attention's convs)
+    View aux{};                 // attention: v in head-major channel order (input of the depthwise conv)
+    int heads = 0;              // attention
     long w_off = 0, b_off = 0;
     float* wk = nullptr;        // K-major [oc][tap][round_up(ic, 32)]
     View in{}, out{}, res{};
@@ -94,6 +97,14 @@ public:
 
 private:
     void build_backbone();
+    void build_trunk_v8();
+    void build_trunk_11();
+    // trunk builders shared by both families (parameters are taken in call order)
+    void tk_conv(const View& in, const Grid& gin, int oc, int k, int s, const View& out, const Grid& gout,
+                 const View* res, int act = 1);
+    void tk_sppf(const View& in, const Grid& g, int c2, const View& out);
+    void tk_upsample(const View& in, const Grid& gin, const View& out, const Grid& gout);
+    long tk_poff_ = 0;
     void build_head();
     void forward_backbone(int batch, const uint8_t* rgb_device);
     void forward_head(int batch);

@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import Session, yolov8_backbone_convs
+from . import MODELS, Session, model_family, yolo11_backbone_convs, yolov8_backbone_convs
 
 
 def synthetic_batch(rng: np.random.Generator, batch: int, size: int, nc: int, boxes=(1, 8), wh=(8.0, 320.0)):
@@ -28,12 +28,19 @@ def synthetic_batch(rng: np.random.Generator, batch: int, size: int, nc: int, bo
     return images, truth
 
 
-def backbone_params(model_args, seed: int) -> np.ndarray:
-    """Random frozen trunk (BatchNorm folded): He-normal weights, small biases, trunk order."""
-    width, depth, max_ch = model_args
+def backbone_params(model, seed: int) -> np.ndarray:
+    """Random frozen trunk (BatchNorm folded): He-normal weights, small biases, trunk order.
+    `model`: a name from MODELS, or a (width, depth, max_channels) tuple of the YOLOv8 family."""
+    if isinstance(model, str):
+        width, depth, max_ch = MODELS[model]
+        convs = (yolo11_backbone_convs if model_family(model) == "yolo11" else yolov8_backbone_convs)(width, depth,
+                                                                                                      max_ch)
+    else:
+        width, depth, max_ch = model
+        convs = yolov8_backbone_convs(width, depth, max_ch)
     rng = np.random.default_rng(seed)
     parts = []
-    for oc, ic, k in yolov8_backbone_convs(width, depth, max_ch):
+    for oc, ic, k in convs:
         std = np.sqrt(2.0 / (ic * k * k)) * 0.8
         parts.append((rng.standard_normal(oc * ic * k * k) * std).astype(np.float32))
         parts.append((rng.standard_normal(oc) * 0.05).astype(np.float32))

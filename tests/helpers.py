@@ -41,7 +41,8 @@ def head_desc(cfg: sy.Config) -> O.HeadDesc:
 
 
 def backbone_desc(cfg: sy.Config) -> O.BackboneDesc:
-    return O.BackboneDesc(cfg.image_size, cfg.width_mult, cfg.depth_mult, cfg.max_channels)
+    return O.BackboneDesc(cfg.image_size, cfg.width_mult, cfg.depth_mult, cfg.max_channels,
+                          1 if cfg.backbone == sy.SY_BACKBONE_YOLO11 else 0)
 
 
 def oracle_head_step(cfg: sy.Config, tensors, params, buffers, velocity, features, truth):

@@ -96,3 +96,42 @@ def test_adamw_steps_match_oracle():
         assert rel_l2(grad, ograd) < TOL
         p = s.flat_params()   # next step from the GPU's parameters (the gradients are compared per step)
         m1, m2 = s.flat_velocity(0), s.flat_velocity(1)
+
+
+def test_yolo11s_full_step_trunk_and_head_match_oracle():
+    """The YOLO11s trunk (C3k2 / C3k / SPPF / C2PSA with attention) from RGB24 on the GPU, then the
+    head step, against the oracle's trunk and head."""
+    import ctypes as C
+
+    from oracle import oracle as O
+    from tests.helpers import backbone_desc
+    image_size, batch = 128, 2
+    rng = np.random.default_rng(51)
+    cfg = sy.make_config("yolo11s", image_size=image_size, max_batch=batch, max_boxes=20)
+    s = sy.Session(cfg)
+    params, buffers = data.head_params(s, 2)
+    s.set_flat_params(params)
+    s.set_flat_buffers(buffers)
+    bparams = data.backbone_params("yolo11s", seed=2)
+    bd = backbone_desc(cfg)
+    assert s.backbone_param_count() == O.lib().syo_backbone_param_count(C.byref(bd)) == bparams.size
+    s.set_backbone(bparams)
+    images, truth = data.synthetic_batch(rng, batch, image_size, cfg.num_classes, boxes=(1, 20), wh=(8.0, 64.0))
+    stats = s.step(images, truth)
+    gpu_feats = []
+    for l in range(3):
+        h = image_size >> (3 + l)
+        want = np.zeros((batch, cfg.feature_channels[l], h, h), np.float32)
+        gpu_feats.append(s.last_features(l, want.shape))
+    for b in range(batch):
+        f = [np.zeros((cfg.feature_channels[l], image_size >> (3 + l), image_size >> (3 + l)), np.float32)
+             for l in range(3)]
+        O.lib().syo_backbone_forward(C.byref(bd), bparams, images[b].ctypes.data_as(C.POINTER(C.c_uint8)), *f)
+        for l in range(3):
+            # the trunk chains ~90 TF32 convolutions
+            assert rel_l2(gpu_feats[l][b], f[l]) < 1.5 * TOL, f"image {b} level {l}"
+    losses, ograd, oparams, obuffers, ovel, conn = oracle_head_step(cfg, s.tensors, params, buffers,
+                                                                    np.zeros_like(params), gpu_feats, truth)
+    ocls = sum(l["cls"] for l in losses)
+    assert abs(stats.cls - ocls) <= TOL * abs(ocls)
+    assert rel_l2(s.last_gradients(), ograd) < 2.5 * TOL
