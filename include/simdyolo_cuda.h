@@ -144,6 +144,14 @@ SY_API sy_status sy_cuda_step_features(sy_session *session, const float *const f
  * images * S * S * 3 bytes, caller-owned). */
 SY_API sy_status sy_cuda_step_device(sy_session *session, const uint8_t *rgb_device, const sy_box *boxes,
                                      const int32_t *counts, int32_t images, sy_step_stats *out);
+/* YoloTrainer.EvaluateLoss (YoloTrainer.cs:237-246): the head with BatchNorm in evaluation mode
+ * (running mean / variance), the loss without gradients; no parameter, buffer or optimizer state
+ * changes.  out->box / cls / dfl / positives are sums over the images of every rank (the reference
+ * reports their mean total, (box + cls + dfl) / images); the gradient fields are zero. */
+SY_API sy_status sy_cuda_eval_loss(sy_session *session, const uint8_t *rgb, const sy_box *boxes, const int32_t *counts,
+                                   int32_t images, sy_step_stats *out);
+SY_API sy_status sy_cuda_eval_loss_features(sy_session *session, const float *const features[3], const sy_box *boxes,
+                                            const int32_t *counts, int32_t images, sy_step_stats *out);
 /* Gradient of the last step (summed over the images of every rank, before the update), parameter order. */
 SY_API sy_status sy_cuda_get_last_gradients(const sy_session *session, float *host, int64_t count);
 /* Frozen features of the last step (NCHW per level), for parity checks. */

@@ -95,6 +95,9 @@ def lib():
                                          C.POINTER(vp), C.POINTER(vp), C.POINTER(Loss), vp, vp]
         L.syo_detection_loss.restype = C.c_int
         L.syo_ciou.argtypes = [fp, fp, fp]; L.syo_ciou.restype = C.c_float
+        L.syo_head_eval_image.argtypes = [C.POINTER(HeadDesc), F32P, F32P, C.POINTER(vp), C.POINTER(Box), C.c_int,
+                                          C.POINTER(Loss)]
+        L.syo_head_eval_image.restype = C.c_int
         L.syo_head_param_count.argtypes = [C.POINTER(HeadDesc)]; L.syo_head_param_count.restype = C.c_long
         L.syo_head_buffer_count.argtypes = [C.POINTER(HeadDesc)]; L.syo_head_buffer_count.restype = C.c_long
         L.syo_head_image.argtypes = [C.POINTER(HeadDesc), F32P, F32P, C.POINTER(vp), C.POINTER(Box), C.c_int, F32P,

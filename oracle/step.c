@@ -120,7 +120,8 @@ static void conv_any_backward(const syo_block *b, const float *x, int h, int w, 
 /* Branch.Forward (DetectionHead.cs:146-157) with running statistics written to bn_stats slots:
  * stats[rm_off..] = this image's mean, stats[rv_off..] = biased variance. */
 static float *branch_forward(const syo_head_desc *d, const block_slot *slots, int n, const float *params,
-                             float *buffers, float *stats, const float *input, int h, int w, block_state *st)
+                             float *buffers, float *stats, const float *input, int h, int w, block_state *st,
+                             int training)
 {
     int spatial = h * w;
     const float *x = input;
@@ -143,7 +144,7 @@ static float *branch_forward(const syo_head_desc *d, const block_slot *slots, in
         memcpy(rm, buffers + slots[i].rm_off, sizeof(float) * b->oc);
         memcpy(rv, buffers + slots[i].rv_off, sizeof(float) * b->oc);
         syo_batchnorm_forward(s->conv, b->oc, spatial, params + slots[i].g_off, params + slots[i].be_off, rm, rv,
-                              d->bn_eps, d->bn_momentum, 1, s->bn_out, s->xhat, s->inv,
+                              d->bn_eps, d->bn_momentum, training, s->bn_out, s->xhat, s->inv,
                               stats + slots[i].rm_off, stats + slots[i].rv_off);
         free(rm);
         free(rv);
@@ -198,7 +199,7 @@ static void free_states(block_state *st, int n)
  * per-channel (mean, biased variance) at the buffer offsets of each BN block. */
 static int head_image_core(const syo_head_desc *d, const float *params, float *buffers, float *stats,
                            const float *const *features, const syo_box *truth, int n_truth, float *grad,
-                           syo_loss *loss, int backward, int *box_connected)
+                           syo_loss *loss, int backward, int *box_connected, int training)
 {
     block_slot slots[6][8];
     int counts[6];
@@ -209,7 +210,7 @@ static int head_image_core(const syo_head_desc *d, const float *params, float *b
         for (int kind = 0; kind < 2; kind++) {
             int br = kind * 3 + l;
             outs[br] = branch_forward(d, slots[br], counts[br], params, buffers, stats, features[l], d->hs[l], d->ws[l],
-                                      states[br]);
+                                      states[br], training);
         }
     const float *boxes[3] = {outs[0], outs[1], outs[2]}, *classes[3] = {outs[3], outs[4], outs[5]};
     float *dbox[3], *dcls[3];
@@ -259,8 +260,22 @@ int syo_head_image(const syo_head_desc *d, const float *params, float *buffers, 
 {
     long nb = syo_head_buffer_count(d);
     float *stats = (float *)calloc(nb ? nb : 1, sizeof(float));
-    int rc = head_image_core(d, params, buffers, stats, features, truth, n_truth, grad, loss, backward, box_connected);
+    int rc = head_image_core(d, params, buffers, stats, features, truth, n_truth, grad, loss, backward, box_connected,
+                             1);
     if (rc == 0) fold_running_stats(d, buffers, stats);
+    free(stats);
+    return rc;
+}
+
+/* YoloTrainer.EvaluateLoss (YoloTrainer.cs:237-246): the head with BatchNorm in evaluation mode
+ * (running mean / variance, HeadOperations.cs:158-166 with training = false), the loss without
+ * gradients; nothing is updated. */
+int syo_head_eval_image(const syo_head_desc *d, const float *params, float *buffers, const float *const *features,
+                        const syo_box *truth, int n_truth, syo_loss *loss)
+{
+    long nb = syo_head_buffer_count(d);
+    float *stats = (float *)calloc(nb ? nb : 1, sizeof(float));
+    int rc = head_image_core(d, params, buffers, stats, features, truth, n_truth, NULL, loss, 0, NULL, 0);
     free(stats);
     return rc;
 }
@@ -775,7 +790,7 @@ void syo_train_step(const syo_backbone_desc *bd, const float *backbone_params, c
         syo_backbone_forward(bd, backbone_params, images[b], feat[0], feat[1], feat[2]);
         const float *cf[3] = {feat[0], feat[1], feat[2]};
         rcs[b] = head_image_core(hd, params, buffers, stats + (size_t)b * nb, cf, truth + box_off[b], counts[b],
-                                 grads + (size_t)b * np, &losses[b], 1, &connected[b]);
+                                 grads + (size_t)b * np, &losses[b], 1, &connected[b], 1);
         for (int l = 0; l < 3; l++) free(feat[l]);
     }
     syo_step_result r;

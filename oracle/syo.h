@@ -106,6 +106,9 @@ int syo_head_image(const syo_head_desc *d, const float *params, float *buffers,
                    const float *const *features, const syo_box *truth, int n_truth,
                    float *grad, syo_loss *loss, int backward, int *box_connected);
 
+int syo_head_eval_image(const syo_head_desc *d, const float *params, float *buffers, const float *const *features,
+                        const syo_box *truth, int n_truth, syo_loss *loss);
+
 /* ---- frozen backbone (backbone.c): YOLOv8-family detection trunk with folded BN ---- */
 typedef struct {
     int32_t image;          /* square input size (multiple of 32) */

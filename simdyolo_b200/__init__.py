@@ -116,7 +116,9 @@ def lib():
         L.sy_cuda_backbone_param_count.restype = C.c_int64
         L.sy_cuda_set_backbone.argtypes = [vp, fp, C.c_int64]
         L.sy_cuda_step.argtypes = [vp, C.POINTER(C.c_uint8), C.POINTER(Box), ip, C.c_int32, C.POINTER(StepStats)]
+        L.sy_cuda_eval_loss.argtypes = L.sy_cuda_step.argtypes
         L.sy_cuda_step_features.argtypes = [vp, C.POINTER(fp), C.POINTER(Box), ip, C.c_int32, C.POINTER(StepStats)]
+        L.sy_cuda_eval_loss_features.argtypes = L.sy_cuda_step_features.argtypes
         L.sy_cuda_get_last_gradients.argtypes = [vp, fp, C.c_int64]
         L.sy_cuda_get_last_features.argtypes = [vp, C.c_int32, fp, C.c_int64]
         L.sy_cuda_detection_loss.argtypes = [C.c_int32, C.c_int32, C.c_int32, ip, ip, fp, C.c_int32, C.c_int32,
@@ -152,7 +154,8 @@ EXPORTED = ["sy_cuda_nccl_unique_id", "sy_cuda_create", "sy_cuda_destroy", "sy_c
             "sy_cuda_get_last_features", "sy_cuda_detection_loss", "sy_cuda_conv2d_forward",
             "sy_cuda_conv2d_backward_data", "sy_cuda_conv2d_backward_filter", "sy_cuda_matmul", "sy_cuda_sgd_update",
             "sy_cuda_step_device", "sy_cuda_launch_count", "sy_cuda_bench_conv",
-            "sy_cuda_conv2d_backward_filter_static", "sy_cuda_conv_profile"]
+            "sy_cuda_conv2d_backward_filter_static", "sy_cuda_conv_profile", "sy_cuda_eval_loss",
+            "sy_cuda_eval_loss_features"]
 
 
 def _check(status: int, session=None):
@@ -478,6 +481,24 @@ class Session:
         stats = StepStats()
         _check(lib().sy_cuda_step_features(self._h, ptrs, arr, _ip(counts), feats[0].shape[0], C.byref(stats)),
                self._h)
+        return stats
+
+    def eval_loss(self, images: np.ndarray, boxes_per_image) -> StepStats:
+        """YoloTrainer.EvaluateLoss on a batch: BatchNorm with running statistics, no update."""
+        img = np.ascontiguousarray(images, np.uint8)
+        arr, counts = self._boxes(boxes_per_image)
+        stats = StepStats()
+        _check(lib().sy_cuda_eval_loss(self._h, img.ctypes.data_as(C.POINTER(C.c_uint8)), arr, _ip(counts),
+                                       img.shape[0], C.byref(stats)), self._h)
+        return stats
+
+    def eval_loss_features(self, features, boxes_per_image) -> StepStats:
+        feats = [np.ascontiguousarray(f, np.float32) for f in features]
+        arr, counts = self._boxes(boxes_per_image)
+        ptrs = (C.POINTER(C.c_float) * 3)(*[_fp(f) for f in feats])
+        stats = StepStats()
+        _check(lib().sy_cuda_eval_loss_features(self._h, ptrs, arr, _ip(counts), feats[0].shape[0],
+                                                C.byref(stats)), self._h)
         return stats
 
     def last_gradients(self) -> np.ndarray:

@@ -137,6 +137,17 @@ __global__ void bn_apply_kernel(const float* y, int ypitch, const float* mean_p,
     }
 }
 
+// Evaluation mode (HeadOperations.cs:158-166 with training = false): every image normalises with the
+// running mean / variance.
+__global__ void bn_eval_coef_kernel(const float* rm, const float* rv, float eps, long n, int c, float* mean_p,
+                                    float* inv_p) {
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int ch = (int)(i % c);
+    mean_p[i] = rm[ch];
+    inv_p[i] = 1.0f / sqrtf(rv[ch] + eps);
+}
+
 // red[b][ch] = (sum dz, sum dz xhat) folded over the row groups in order; f = gamma inv / n.
 __global__ void bn_bwd_fold_kernel(const float* part, int batch, int c, int groups, float n_pix, const float* inv_p,
                                    const float* gamma, float* red, float* f_p) {
@@ -287,6 +298,13 @@ void bn_stats_fold(const float* part, int batch, const Grid& g, int c, float eps
     bn_stats_fold_kernel<<<dim3((c + 31) / 32, batch), kFoldWarps * 32, 0, stream>>>(part, c, g.rows / 32, eps, stats,
                                                                                      coef, coef + n);
     launch_check("bn_stats_fold_kernel");
+}
+
+void bn_eval_coef(const float* rmean, const float* rvar, float eps, int batch, int c, float* coef,
+                  cudaStream_t stream) {
+    const long n = (long)batch * c;
+    bn_eval_coef_kernel<<<(int)((n + 255) / 256), 256, 0, stream>>>(rmean, rvar, eps, n, c, coef, coef + n);
+    launch_check("bn_eval_coef_kernel");
 }
 
 void bn_silu_apply(const View& y, const float* coef, const float* gamma, const float* beta, int batch, const Grid& g,

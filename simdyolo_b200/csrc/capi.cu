@@ -191,6 +191,19 @@ sy_status sy_cuda_step_features(sy_session* session, const float* const features
                    [&] { return session->impl->step(nullptr, false, features, boxes, counts, images, out); });
 }
 
+sy_status sy_cuda_eval_loss(sy_session* session, const uint8_t* rgb, const sy_box* boxes, const int32_t* counts,
+                             int32_t images, sy_step_stats* out) {
+    if (!session || !rgb) return SY_ERR_INVALID_ARGUMENT;
+    return guarded(session, [&] { return session->impl->evaluate(rgb, false, nullptr, boxes, counts, images, out); });
+}
+
+sy_status sy_cuda_eval_loss_features(sy_session* session, const float* const features[3], const sy_box* boxes,
+                                     const int32_t* counts, int32_t images, sy_step_stats* out) {
+    if (!session || !features) return SY_ERR_INVALID_ARGUMENT;
+    return guarded(session,
+                   [&] { return session->impl->evaluate(nullptr, false, features, boxes, counts, images, out); });
+}
+
 int64_t sy_cuda_launch_count(void) { return sy::launch_count(); }
 
 sy_status sy_cuda_conv_profile(sy_session* session, int32_t enable, double* ms, double* gflop, int64_t* launches) {

@@ -140,6 +140,9 @@ size_t bn_partial_floats(int batch, const Grid& g, int channels);
 // coef = [mean plane | inv plane], each [batch][c], inv = 1 / sqrt(var + eps).
 void bn_stats_fold(const float* part, int batch, const Grid& g, int c, float eps, float* stats, float* coef,
                    cudaStream_t stream);
+// Evaluation-mode coefficients: the same [mean plane | inv plane] from the running statistics.
+void bn_eval_coef(const float* rmean, const float* rvar, float eps, int batch, int c, float* coef,
+                  cudaStream_t stream);
 // a = SiLU(gamma * (y - mean) * inv + beta) at interior rows, 0 elsewhere (xhat is not stored).
 void bn_silu_apply(const View& y, const float* coef, const float* gamma, const float* beta, int batch, const Grid& g,
                    const View& a, cudaStream_t stream);

@@ -702,13 +702,13 @@ static View rows_of(View v, int batch, const Grid& g) {
     return v;
 }
 
-void Session::forward_head(int batch) {
+void Session::forward_head(int batch, bool training) {
     for (auto& branch : branches_) {
         const Grid& g = levels_[branch.level];
         for (auto& hb : branch.blocks) {
             ConvEpilogue ep;
             if (hb.b.has_bias) ep.bias = params_ + hb.b_off;
-            if (hb.b.has_bn) {
+            if (hb.b.has_bn && training) {
                 ep.bn.channels = hb.b.oc;
                 ep.bn.stats_part = bn_part_;
             }
@@ -722,7 +722,11 @@ void Session::forward_head(int batch) {
                 prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w);
             }
             if (hb.b.has_bn) {
-                bn_stats_fold(bn_part_, batch, g, hb.b.oc, cfg.bn_eps, hb.stats, hb.coef, stream_);
+                if (training)
+                    bn_stats_fold(bn_part_, batch, g, hb.b.oc, cfg.bn_eps, hb.stats, hb.coef, stream_);
+                else
+                    bn_eval_coef(buffers_ + hb.rm_off, buffers_ + hb.rv_off, cfg.bn_eps, batch, hb.b.oc, hb.coef,
+                                 stream_);
                 bn_silu_apply(rows_of(hb.y, batch, g), hb.coef, params_ + hb.g_off, params_ + hb.be_off, batch, g,
                               rows_of(hb.a, batch, g), stream_);
             }
@@ -779,8 +783,10 @@ void Session::backward_head(int batch) {
 }
 
 // ------------------------------------------------------------------ step
-int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
-                  const int32_t* counts, int images, sy_step_stats* out) {
+// Validate and upload the step's ground truth and images, run the frozen trunk (or stage cached
+// features); shared by the training step and the loss evaluation.
+void Session::prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float* const* features,
+                             const sy_box* boxes, const int32_t* counts, int images) {
     if (images < 1 || images > B_) throw SyError(SY_ERR_INVALID_ARGUMENT, "images out of range");
     if (!counts || (!boxes && images > 0)) throw SyError(SY_ERR_INVALID_ARGUMENT, "counts / boxes missing");
     SY_CUDA(cudaSetDevice(device_));
@@ -833,6 +839,11 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
             nchw_to_padded(feat_stage_, images, feat_ch_[l], g, features_[l], stream_);
         }
     }
+}
+
+int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
+                  const int32_t* counts, int images, sy_step_stats* out) {
+    prepare_inputs(rgb, rgb_on_device, features, boxes, counts, images);
     forward_head(images);
     // loss
     LevelIO lv[3];
@@ -1040,6 +1051,58 @@ void Session::conv_wgrad(const View& x, const View& dy, int taps, const Grid& gr
     conv_tc_wgrad(xs, db, taps, grid, dw, wgrad_ws_, d_flags_, stream_, 0);
     conv_tc_wgrad(xb, ds, taps, grid, dw, wgrad_ws_, d_flags_, stream_, 1);
     conv_tc_wgrad(xb, db, taps, grid, dw, wgrad_ws_, d_flags_, stream_, 1);
+}
+
+// ------------------------------------------------------------------ loss evaluation
+int Session::evaluate(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
+                      const int32_t* counts, int images, sy_step_stats* out) {
+    prepare_inputs(rgb, rgb_on_device, features, boxes, counts, images);
+    forward_head(images, false);
+    LevelIO lv[3];
+    for (int l = 0; l < 3; l++) {
+        HeadBlock& bb = branches_[l].blocks.back();
+        HeadBlock& cb = branches_[3 + l].blocks.back();
+        lv[l] = LevelIO{bb.y.base, cb.y.base, bb.g.base, cb.g.base, bb.y.pitch, cb.y.pitch, levels_[l],
+                        (float)(8 << l)};
+    }
+    LossOut lo{d_loss_, d_pos_, d_conn_, nullptr, nullptr};
+    detection_loss(lv, 3, images, cfg.num_classes, cfg.reg_max, d_truth_, d_box_off_, std::max(1, cfg.max_boxes), 10,
+                   1.0f, 0, loss_ws_, lo, stream_);
+    SY_CUDA(cudaMemcpyAsync(h_loss_, d_loss_, sizeof(float) * 4 * images, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaMemcpyAsync(h_pos_, d_pos_, sizeof(int) * images, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaMemcpyAsync(h_flags_, d_flags_, sizeof(int) * 16, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaStreamSynchronize(stream_));
+    if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "device wait limit exceeded (code " + std::to_string(h_flags_[0]) + ")");
+    double* hs = reinterpret_cast<double*>(h_abs_);   // pinned scratch (>= 8 doubles)
+    hs[0] = hs[1] = hs[2] = hs[3] = 0.0;
+    for (int b = 0; b < images; b++) {
+        hs[0] += h_loss_[4 * b];
+        hs[1] += h_loss_[4 * b + 1];
+        hs[2] += h_loss_[4 * b + 2];
+        hs[3] += h_pos_[b];
+    }
+    hs[4] = images;
+    if (comm_) {
+        SY_CUDA(cudaMemcpyAsync(d_abs_, hs, sizeof(double) * 5, cudaMemcpyHostToDevice, stream_));
+        int r = nccl_->AllReduce(d_abs_, d_abs_, 5, kNcclDouble, kNcclSum, comm_, stream_);
+        if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllReduce: ") + nccl_->GetErrorString(r));
+        SY_CUDA(cudaMemcpyAsync(hs, d_abs_, sizeof(double) * 5, cudaMemcpyDeviceToHost, stream_));
+    }
+    SY_CUDA(cudaEventRecord(ev1_, stream_));
+    SY_CUDA(cudaStreamSynchronize(stream_));
+    last_batch_ = images;
+    if (out) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, ev0_, ev1_);
+        *out = sy_step_stats{};
+        out->box = hs[0];
+        out->cls = hs[1];
+        out->dfl = hs[2];
+        out->positives = (long)hs[3];
+        out->images = (int)hs[4];
+        out->device_ms = ms;
+    }
+    return SY_OK;
 }
 
 // ------------------------------------------------------------------ conv launch timing

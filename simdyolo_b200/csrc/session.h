@@ -81,6 +81,9 @@ public:
     // rgb: host (or, with rgb_on_device, device) images; features: host NCHW features instead.
     int step(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
              const int32_t* counts, int images, sy_step_stats* out);
+    // YoloTrainer.EvaluateLoss: BatchNorm with running statistics, loss without gradients, no update.
+    int evaluate(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
+                 const int32_t* counts, int images, sy_step_stats* out);
     int set_tensor(int index, const float* host, long count);
     int get_tensor(int index, float* host, long count) const;
     int set_opt_state(int index, int moment, const float* host, long count);
@@ -107,7 +110,9 @@ private:
     long tk_poff_ = 0;
     void build_head();
     void forward_backbone(int batch, const uint8_t* rgb_device);
-    void forward_head(int batch);
+    void prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
+                        const int32_t* counts, int images);
+    void forward_head(int batch, bool training = true);
     void backward_head(int batch);
     void refresh_head_weights();
     View alloc_view(int channels, const Grid& g);

@@ -187,3 +187,20 @@ def test_adamw_matches_torch_over_steps():
     before = w.copy()
     assert O.lib().syo_adamw_update(w, m, v, np.ones(n, np.float32), n, lr, b1, b2, eps, wd, 6, images, 0) == 0
     assert np.array_equal(w, before)
+
+
+def test_batchnorm_evaluation_mode_matches_torch():
+    """HeadOperations.BatchNorm with training = false (EvaluateLoss): running statistics, no update."""
+    rng = np.random.default_rng(12)
+    c, h, w = 6, 5, 7
+    x = rng.standard_normal((c, h, w)).astype(np.float32) * 2 + 0.5
+    gamma = rng.uniform(0.5, 1.5, c).astype(np.float32)
+    beta = rng.standard_normal(c).astype(np.float32)
+    rmean = rng.standard_normal(c).astype(np.float32)
+    rvar = rng.uniform(0.5, 2.0, c).astype(np.float32)
+    rm0, rv0 = rmean.copy(), rvar.copy()
+    y = O.batchnorm_forward(x, gamma, beta, rmean, rvar, eps=1e-3, momentum=0.03, training=False)[0]
+    ref = F.batch_norm(torch.tensor(x)[None], torch.tensor(rm0), torch.tensor(rv0), torch.tensor(gamma),
+                       torch.tensor(beta), training=False, eps=1e-3)[0]
+    np.testing.assert_allclose(y.reshape(c, h, w), ref.numpy(), rtol=1e-5, atol=1e-6)
+    assert np.array_equal(rmean, rm0) and np.array_equal(rvar, rv0)
