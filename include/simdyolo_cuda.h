@@ -168,6 +168,16 @@ SY_API sy_status sy_cuda_detection_loss(int32_t device, int32_t images, int32_t 
                                  const float *const *classes, const sy_box *truth, const int32_t *counts,
                                  float *out_loss, int32_t *positives, int32_t *assigned, float *scores,
                                  float *const *box_grads, float *const *class_grads);
+/* The same with the assigner's candidate counts and the gradient scale (DetectionLoss.Compute
+ * arguments topk, topk2, gradientScale, DetectionLoss.cs:48-91): end-to-end heads call it with
+ * (10, 10, w) for the one-to-many branch and (7 or 1, 1, 1 - w) for the one-to-one branch;
+ * reg_max 1 is the L1 box loss of YOLO26 (DetectionLoss.cs:123-131). */
+SY_API sy_status sy_cuda_detection_loss_ex(int32_t device, int32_t images, int32_t levels, const int32_t *hs,
+                                           const int32_t *ws, const float *strides, int32_t nc, int32_t reg_max,
+                                           const float *const *boxes, const float *const *classes, const sy_box *truth,
+                                           const int32_t *counts, int32_t topk, int32_t topk2, float grad_scale,
+                                           float *out_loss, int32_t *positives, int32_t *assigned, float *scores,
+                                           float *const *box_grads, float *const *class_grads);
 
 /* HeadOperations.Conv (HeadOperations.cs:29-82) batched: x NCHW [n][ic][h][w], w OIHW [oc][ic][k][k],
  * stride 1, padding k/2.  forward: y = conv(x, w) (+ bias);  backward_data: dx = conv^T(dy, w);

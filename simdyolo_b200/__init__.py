@@ -124,6 +124,9 @@ def lib():
         L.sy_cuda_detection_loss.argtypes = [C.c_int32, C.c_int32, C.c_int32, ip, ip, fp, C.c_int32, C.c_int32,
                                              C.POINTER(fp), C.POINTER(fp), C.POINTER(Box), ip, fp, ip, ip, fp,
                                              C.POINTER(fp), C.POINTER(fp)]
+        L.sy_cuda_detection_loss_ex.argtypes = [C.c_int32, C.c_int32, C.c_int32, ip, ip, fp, C.c_int32, C.c_int32,
+                                                C.POINTER(fp), C.POINTER(fp), C.POINTER(Box), ip, C.c_int32, C.c_int32,
+                                                C.c_float, fp, ip, ip, fp, C.POINTER(fp), C.POINTER(fp)]
         L.sy_cuda_conv2d_forward.argtypes = [C.c_int32, fp, C.c_int32, C.c_int32, C.c_int32, C.c_int32, fp, C.c_int32,
                                              C.c_int32, fp, fp]
         L.sy_cuda_conv2d_backward_data.argtypes = [C.c_int32, fp, C.c_int32, C.c_int32, C.c_int32, C.c_int32, fp,
@@ -155,7 +158,7 @@ EXPORTED = ["sy_cuda_nccl_unique_id", "sy_cuda_create", "sy_cuda_destroy", "sy_c
             "sy_cuda_conv2d_backward_data", "sy_cuda_conv2d_backward_filter", "sy_cuda_matmul", "sy_cuda_sgd_update",
             "sy_cuda_step_device", "sy_cuda_launch_count", "sy_cuda_bench_conv",
             "sy_cuda_conv2d_backward_filter_static", "sy_cuda_conv_profile", "sy_cuda_eval_loss",
-            "sy_cuda_eval_loss_features"]
+            "sy_cuda_eval_loss_features", "sy_cuda_detection_loss_ex"]
 
 
 def _check(status: int, session=None):
@@ -540,10 +543,11 @@ def nccl_unique_id() -> bytes:
 
 # ------------------------------------------------------------------ standalone operators
 
-def detection_loss(boxes, classes, strides, truth, nc, device=0, with_grad=True):
-    """DetectionLoss.Compute on the GPU for a batch.  boxes[l]: [B, 64, H, W]; classes[l]: [B, nc, H, W];
-    truth: list (per image) of (cls, x1, y1, x2, y2).  Returns (loss[B,3], positives[B], assigned[B,A],
-    scores[B,A], dbox list, dcls list)."""
+def detection_loss(boxes, classes, strides, truth, nc, device=0, with_grad=True, reg_max=16, topk=10, topk2=10,
+                   grad_scale=1.0):
+    """DetectionLoss.Compute on the GPU for a batch.  boxes[l]: [B, 4 * reg_max, H, W]; classes[l]:
+    [B, nc, H, W]; truth: list (per image) of (cls, x1, y1, x2, y2).  Returns (loss[B,3], positives[B],
+    assigned[B,A], scores[B,A], dbox list, dcls list)."""
     bl = [np.ascontiguousarray(b, np.float32) for b in boxes]
     cl = [np.ascontiguousarray(c, np.float32) for c in classes]
     B = bl[0].shape[0]
@@ -559,10 +563,11 @@ def detection_loss(boxes, classes, strides, truth, nc, device=0, with_grad=True)
     db = [np.zeros_like(b) for b in bl] if with_grad else None
     dc = [np.zeros_like(c) for c in cl] if with_grad else None
     P = C.POINTER(C.c_float) * len(bl)
-    _check(lib().sy_cuda_detection_loss(device, B, len(bl), _ip(hs), _ip(ws), _fp(st), nc, 16, P(*map(_fp, bl)),
-                                        P(*map(_fp, cl)), arr, _ip(counts), _fp(loss), _ip(pos), _ip(assigned),
-                                        _fp(scores), P(*map(_fp, db)) if with_grad else None,
-                                        P(*map(_fp, dc)) if with_grad else None))
+    _check(lib().sy_cuda_detection_loss_ex(device, B, len(bl), _ip(hs), _ip(ws), _fp(st), nc, reg_max,
+                                           P(*map(_fp, bl)), P(*map(_fp, cl)), arr, _ip(counts), topk, topk2,
+                                           grad_scale, _fp(loss), _ip(pos), _ip(assigned), _fp(scores),
+                                           P(*map(_fp, db)) if with_grad else None,
+                                           P(*map(_fp, dc)) if with_grad else None))
     return loss, pos, assigned, scores, db, dc
 
 

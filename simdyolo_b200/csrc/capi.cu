@@ -289,9 +289,20 @@ sy_status sy_cuda_detection_loss(int32_t device, int32_t images, int32_t levels,
                                  const float* const* classes, const sy_box* truth, const int32_t* counts,
                                  float* out_loss, int32_t* positives, int32_t* assigned, float* scores,
                                  float* const* box_grads, float* const* class_grads) {
+    return sy_cuda_detection_loss_ex(device, images, levels, hs, ws, strides, nc, reg_max, boxes, classes, truth, counts,
+                                     10, 10, 1.0f, out_loss, positives, assigned, scores, box_grads, class_grads);
+}
+
+sy_status sy_cuda_detection_loss_ex(int32_t device, int32_t images, int32_t levels, const int32_t* hs,
+                                    const int32_t* ws, const float* strides, int32_t nc, int32_t reg_max,
+                                    const float* const* boxes, const float* const* classes, const sy_box* truth,
+                                    const int32_t* counts, int32_t topk, int32_t topk2, float grad_scale,
+                                    float* out_loss, int32_t* positives, int32_t* assigned, float* scores,
+                                    float* const* box_grads, float* const* class_grads) {
     return guarded(nullptr, [&] {
         if (images < 1 || levels < 1 || levels > 3 || !hs || !ws || !strides || !boxes || !classes || !counts ||
-            !out_loss || nc < 1 || reg_max != 16)
+            !out_loss || nc < 1 || !(reg_max == 16 || reg_max == 1) || topk < 1 || topk > 64 || topk2 < 1 ||
+            topk2 > topk || !std::isfinite(grad_scale))
             throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "detection_loss: bad arguments");
         check_device(device);
         Scratch s;
@@ -338,11 +349,12 @@ sy_status sy_cuda_detection_loss(int32_t device, int32_t images, int32_t levels,
         int* d_off = s.get<int>(images + 1);
         CK(cudaMemcpy(d_truth, tb.data(), tb.size() * sizeof(sy::TruthBox), cudaMemcpyHostToDevice));
         CK(cudaMemcpy(d_off, off.data(), off.size() * sizeof(int), cudaMemcpyHostToDevice));
-        void* ws_ = s.get<uint8_t>(sy::loss_workspace_bytes(images, anchors, std::max(1, max_boxes), 10));
+        void* ws_ = s.get<uint8_t>(sy::loss_workspace_bytes(images, anchors, std::max(1, max_boxes), topk));
         sy::LossOut lo{s.get<float>(4 * images), s.get<int>(images), s.get<int>(images), s.get<int>((size_t)images * anchors),
                        s.get<float>((size_t)images * anchors)};
-        sy::detection_loss(lv, levels, images, nc, reg_max, d_truth, d_off, std::max(1, max_boxes), 10, 1.0f,
-                           backward ? 1 : 0, ws_, lo, 0);
+        if (max_boxes * topk > 1024) throw sy::SyError(SY_ERR_UNSUPPORTED_SHAPE, "detection_loss: boxes * topk > 1024");
+        sy::detection_loss(lv, levels, images, nc, reg_max, d_truth, d_off, std::max(1, max_boxes), topk, topk2,
+                           grad_scale, backward ? 1 : 0, ws_, lo, 0);
         CK(cudaGetLastError());
         std::vector<float> loss(4 * images);
         CK(cudaMemcpy(loss.data(), lo.loss, loss.size() * sizeof(float), cudaMemcpyDeviceToHost));

@@ -188,7 +188,7 @@ struct LossOut {
 };
 size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int bins);
 void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int bins, const TruthBox* truth,
-                    const int* box_offsets, int max_boxes, int topk, float grad_scale, int backward, void* workspace,
+                    const int* box_offsets, int max_boxes, int topk, int topk2, float grad_scale, int backward, void* workspace,
                     const LossOut& out, cudaStream_t stream);
 
 // ---------------------------------------------------------------- optimizer

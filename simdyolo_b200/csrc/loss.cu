@@ -29,7 +29,7 @@ struct LossParams {
     int nlevels;
     int level_start[kMaxLevels + 1];
     int anchors;
-    int batch, nc, bins, topk;
+    int batch, nc, bins, topk, topk2;
     float grad_scale;
     int backward;
     const TruthBox* truth;
@@ -306,6 +306,7 @@ __global__ void __launch_bounds__(256) assign_kernel(LossParams p) {
     __shared__ float al[kMaxSel], ov[kMaxSel];
     __shared__ float max_al[128], max_ov[128];
     __shared__ int count_s;
+    __shared__ bool keep_s[kMaxSel];
     // dense outputs of this image start cleared
     if (p.out.assigned)
         for (int a = threadIdx.x; a < p.anchors; a += blockDim.x) p.out.assigned[(long)b * p.anchors + a] = -1;
@@ -374,7 +375,37 @@ __global__ void __launch_bounds__(256) assign_kernel(LossParams p) {
         ov[i] = o;
     }
     __syncthreads();
+    if (threadIdx.x == 0 && p.topk2 != p.topk) {
+        // second top-k after the conflicts (DetectionLoss.cs:83-91): per GT keep the topk2 anchors
+        // ranked by (alignment if selected else 0) descending, then by anchor index.  Selected anchors
+        // with positive alignment come first; a selected anchor with zero alignment survives only if
+        // it is among the lowest-index anchors of zero key that fill the remaining slots.
+        for (int i = 0; i < c; i++) {
+            const int g = own[i];
+            int better = 0, pos_below = 0, npos = 0;
+            for (int j = 0; j < c; j++) {
+                if (own[j] != g || !(al[j] > 0.f)) continue;
+                npos++;
+                if (anc[j] < anc[i]) pos_below++;
+                if (al[j] > al[i] || (al[j] == al[i] && anc[j] < anc[i])) better++;
+            }
+            if (al[i] > 0.f) keep_s[i] = better < p.topk2;
+            else keep_s[i] = npos < p.topk2 && anc[i] - pos_below < p.topk2 - npos;
+        }
+        int kept = 0;   // compact after every decision (the decisions read the whole list)
+        for (int i = 0; i < c; i++)
+            if (keep_s[i]) {
+                anc[kept] = anc[i];
+                own[kept] = own[i];
+                al[kept] = al[i];
+                ov[kept] = ov[i];
+                kept++;
+            }
+        count_s = kept;
+    }
+    __syncthreads();
     if (threadIdx.x == 0) {
+        const int c = count_s;
         for (int i = 0; i < c; i++) {
             const int g = own[i];
             max_al[g] = fmaxf(max_al[g], al[i]);
@@ -559,7 +590,7 @@ size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int topk) {
 }
 
 void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int bins, const TruthBox* truth,
-                    const int* box_offsets, int max_boxes, int topk, float grad_scale, int backward, void* workspace,
+                    const int* box_offsets, int max_boxes, int topk, int topk2, float grad_scale, int backward, void* workspace,
                     const LossOut& out, cudaStream_t stream) {
     LossParams p;
     p.nlevels = nlevels;
@@ -573,6 +604,8 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
     p.nc = nc;
     p.bins = bins;
     p.topk = topk;
+    p.topk2 = topk2;
+    if (topk2 < 1 || topk2 > topk) throw std::runtime_error("detection_loss: topk2 must be in [1, topk]");
     p.grad_scale = grad_scale;
     p.backward = backward;
     p.truth = truth;

@@ -855,7 +855,7 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
     }
     LossOut lo{d_loss_, d_pos_, d_conn_, nullptr, nullptr};
     detection_loss(lv, 3, images, cfg.num_classes, cfg.reg_max, d_truth_, d_box_off_, std::max(1, cfg.max_boxes), 10,
-                   1.0f, 1, loss_ws_, lo, stream_);
+                   10, 1.0f, 1, loss_ws_, lo, stream_);
     backward_head(images);
     if (comm_) {
         // the gradient bucket is summed over ranks before anything reads it, so the finiteness
@@ -1067,7 +1067,7 @@ int Session::evaluate(const uint8_t* rgb, bool rgb_on_device, const float* const
     }
     LossOut lo{d_loss_, d_pos_, d_conn_, nullptr, nullptr};
     detection_loss(lv, 3, images, cfg.num_classes, cfg.reg_max, d_truth_, d_box_off_, std::max(1, cfg.max_boxes), 10,
-                   1.0f, 0, loss_ws_, lo, stream_);
+                   10, 1.0f, 0, loss_ws_, lo, stream_);
     SY_CUDA(cudaMemcpyAsync(h_loss_, d_loss_, sizeof(float) * 4 * images, cudaMemcpyDeviceToHost, stream_));
     SY_CUDA(cudaMemcpyAsync(h_pos_, d_pos_, sizeof(int) * images, cudaMemcpyDeviceToHost, stream_));
     SY_CUDA(cudaMemcpyAsync(h_flags_, d_flags_, sizeof(int) * 16, cudaMemcpyDeviceToHost, stream_));

@@ -177,3 +177,34 @@ def test_assigner_ties_resolve_to_lowest_anchor():
     _, _, _, oa, os_ = O.detection_loss([b[0] for b in boxes], [c[0] for c in classes], [8.0, 16.0, 32.0], truth[0], nc)
     assert np.array_equal(assigned[0], oa) and np.array_equal(scores[0], os_)
     assert pos[0] > 0
+
+
+@pytest.mark.parametrize("reg_max,topk,topk2,scale,seed", [
+    (16, 7, 1, 0.3, 4),    # YOLO26 one-to-one branch early in the progressive schedule
+    (16, 1, 1, 1.0, 5),    # YOLOv10 one-to-one branch
+    (1, 10, 10, 0.8, 6),   # reg_max 1: L1 box loss instead of DFL
+    (1, 7, 1, 0.2, 7),
+])
+def test_end_to_end_loss_variants_match_oracle(reg_max, topk, topk2, scale, seed):
+    """DetectionLoss.Compute with the end-to-end heads' arguments (DetectionLoss.cs:48-91, :123-131):
+    the second top-k after the conflicts, reg_max 1 and the gradient scale; assignment bit-exact."""
+    rng = np.random.default_rng(seed)
+    batch, size, nc = 3, 320, 20
+    boxes, classes, truth = random_head_outputs(rng, batch, size, nc, 12)
+    if reg_max == 1:
+        # raw distances (grid units) instead of DFL logits
+        boxes = [np.abs(b[:, :4]) * 2.0 + 0.5 for b in boxes]
+    loss, pos, assigned, scores, db, dc = sy.detection_loss(boxes, classes, [8.0, 16.0, 32.0], truth, nc,
+                                                            reg_max=reg_max, topk=topk, topk2=topk2, grad_scale=scale)
+    for b in range(batch):
+        ol, odb, odc, oa, os_ = O.detection_loss([x[b] for x in boxes], [x[b] for x in classes], [8.0, 16.0, 32.0],
+                                                 truth[b], nc, bins=reg_max, topk=topk, topk2=topk2, grad_scale=scale)
+        assert np.array_equal(assigned[b], oa), f"image {b}: assignment differs"
+        assert np.array_equal(scores[b], os_), f"image {b}: target scores differ"
+        assert pos[b] == ol["positives"]
+        for got, want in zip(loss[b], (ol["box"], ol["cls"], ol["dfl"])):
+            assert abs(got - want) <= 1e-4 * max(1.0, abs(want))
+        for l in range(3):
+            assert rel_l2(dc[l][b], odc[l]) < 1e-5
+            if ol["positives"]:
+                assert rel_l2(db[l][b], odb[l]) < 1e-4 or np.abs(odb[l]).max() == 0
