@@ -75,19 +75,25 @@ typedef struct sy_config {
     int32_t max_batch;          /* images per step on this rank */
     int32_t max_boxes;          /* ground-truth boxes per image (<= 100) */
     int32_t num_classes;        /* nc */
-    int32_t reg_max;            /* 16 (DFL) */
+    int32_t reg_max;            /* 16 (DFL) or 1 (direct distances, end-to-end heads only) */
     int32_t backbone;           /* SY_BACKBONE_* */
     float width_mult, depth_mult;
     int32_t max_channels;
     int32_t feature_channels[3];/* P3/P4/P5 channels when backbone == SY_BACKBONE_NONE */
     int32_t n_box_blocks, n_cls_blocks;
-    sy_block box_blocks[3][8];  /* cv2.{0,1,2} */
-    sy_block cls_blocks[3][8];  /* cv3.{0,1,2} */
+    sy_block box_blocks[3][8];  /* cv2.{0,1,2} (and one2one_cv2.{0,1,2} with end_to_end) */
+    sy_block cls_blocks[3][8];  /* cv3.{0,1,2} (and one2one_cv3.{0,1,2} with end_to_end) */
     float bn_eps, bn_momentum;  /* DetectionHead.cs:71 (PT defaults 1e-3 / 0.03) */
     int32_t optimizer;          /* SY_OPT_* */
     float lr, momentum, weight_decay;
     float beta1, beta2, adam_eps;
     int32_t precision;          /* SY_PRECISION_TF32, or SY_PRECISION_3XTF32 for the FP32 parity mode */
+    /* TrainingHeadSchema (src/SimdYolo/TrainingHeadSchema.cs:7-21): end_to_end = 1 adds the
+     * one2one_cv2 / one2one_cv3 branches (YOLOv10 / YOLO26 heads), trained with a second loss
+     * (DetectionHead.cs:105-115); with reg_max 1 the loss is the progressive one whose one-to-many
+     * weight follows DetectionHead.ProgressiveWeight(epoch, schedule_epochs). */
+    int32_t end_to_end;
+    int32_t schedule_epochs;    /* LossScheduleEpochs (YoloTrainer.cs:106): TrainingOptions.Epochs */
 } sy_config;
 
 /* Per-step results, summed over the global batch (all ranks). */
@@ -95,7 +101,7 @@ typedef struct sy_step_stats {
     double box, cls, dfl;       /* loss sums; YoloTrainer divides by the batch (YoloTrainer.cs:198) */
     int64_t positives;
     int32_t images;             /* global images in the step */
-    int32_t box_has_grad;       /* box branch connected (any positive), DetectionLoss.cs:101 */
+    int32_t box_has_grad;       /* bit 0: cv2 connected (any positive, DetectionLoss.cs:101); bit 1: one2one_cv2 */
     double grad_checksum;       /* sum of |g| over the averaged head gradient before the update */
     double device_ms;           /* device time of the step (CUDA events) */
 } sy_step_stats;
@@ -152,6 +158,9 @@ SY_API sy_status sy_cuda_eval_loss(sy_session *session, const uint8_t *rgb, cons
                                    int32_t images, sy_step_stats *out);
 SY_API sy_status sy_cuda_eval_loss_features(sy_session *session, const float *const features[3], const sy_box *boxes,
                                             const int32_t *counts, int32_t images, sy_step_stats *out);
+/* The completed-epoch counter YoloTrainer passes to DetectionHead.Loss (YoloTrainer.cs:192); it only
+ * matters for progressive end-to-end heads.  Evaluation always uses epoch 0 (YoloTrainer.cs:243). */
+SY_API sy_status sy_cuda_set_epoch(sy_session *session, int32_t epoch);
 /* Gradient of the last step (summed over the images of every rank, before the update), parameter order. */
 SY_API sy_status sy_cuda_get_last_gradients(const sy_session *session, float *host, int64_t count);
 /* Frozen features of the last step (NCHW per level), for parity checks. */

@@ -335,8 +335,9 @@ int syo_adamw_update(float *w, float *m, float *v, float *grad, long n, float lr
     return 0;
 }
 
-/* DetectionHead.ProgressiveWeight (DetectionHead.cs:120) */
-float syo_progressive_weight(int epoch, int epochs)
+/* DetectionHead.ProgressiveWeight (DetectionHead.cs:120); the product and the sum round separately
+ * as in the reference, so no fused multiply-add */
+__attribute__((optimize("fp-contract=off"))) float syo_progressive_weight(int epoch, int epochs)
 {
     int denom = epochs - 1 > 1 ? epochs - 1 : 1;
     float t = 1 - (float)epoch / denom;

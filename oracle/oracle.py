@@ -38,7 +38,8 @@ class HeadDesc(C.Structure):
     _fields_ = [("levels", C.c_int32), ("nc", C.c_int32), ("bins", C.c_int32), ("hs", C.c_int32 * 3),
                 ("ws", C.c_int32 * 3), ("strides", C.c_float * 3), ("n_box_blocks", C.c_int32),
                 ("n_cls_blocks", C.c_int32), ("box_blocks", (Block * 8) * 3), ("cls_blocks", (Block * 8) * 3),
-                ("bn_eps", C.c_float), ("bn_momentum", C.c_float)]
+                ("bn_eps", C.c_float), ("bn_momentum", C.c_float), ("end_to_end", C.c_int32),
+                ("epoch", C.c_int32), ("schedule_epochs", C.c_int32)]
 
 
 class BackboneDesc(C.Structure):
@@ -48,7 +49,7 @@ class BackboneDesc(C.Structure):
 
 class Optim(C.Structure):
     _fields_ = [("lr", C.c_float), ("momentum", C.c_float), ("weight_decay", C.c_float), ("optimizer", C.c_int32),
-                ("beta1", C.c_float), ("beta2", C.c_float), ("adam_eps", C.c_float), ("adam_step", C.c_int32 * 2)]
+                ("beta1", C.c_float), ("beta2", C.c_float), ("adam_eps", C.c_float), ("adam_step", C.c_int32 * 3)]
 
 
 class StepResult(C.Structure):

@@ -12,7 +12,8 @@
  *                    (PtModel.cs:202-203).
  *
  * Parameters are one flat float array in DetectionHead.Snapshot order (DetectionHead.cs:124-130):
- * branches cv2.0, cv2.1, cv2.2, cv3.0, cv3.1, cv3.2; per block weight, [bias], [bn gamma, beta].
+ * branches cv2.0, cv2.1, cv2.2, cv3.0, cv3.1, cv3.2 (then, for end-to-end heads, one2one_cv2.0-2 and
+ * one2one_cv3.0-2); per block weight, [bias], [bn gamma, beta].
  * Buffers: per BN block running_mean, running_var, num_batches_tracked (one float).
  * Images run in parallel over OpenMP threads; BN running statistics and gradient sums are then
  * applied in image order, so the result equals the reference's sequential loop.
@@ -27,20 +28,28 @@
 
 /* ------------------------------------------------------------------ head layout */
 
+/* Branch order (DetectionHead.cs:20-26): cv2.0-2, cv3.0-2, and with end_to_end one2one_cv2.0-2,
+ * one2one_cv3.0-2 built from the same block lists. */
+static int n_branches(const syo_head_desc *d) { return d->end_to_end ? 12 : 6; }
+
 static const syo_block *branch_blocks(const syo_head_desc *d, int branch, int *count)
 {
     int level = branch % 3;
-    if (branch < 3) { *count = d->n_box_blocks; return d->box_blocks[level]; }
+    if ((branch / 3) % 2 == 0) { *count = d->n_box_blocks; return d->box_blocks[level]; }
     *count = d->n_cls_blocks;
     return d->cls_blocks[level];
 }
+
+/* gradient group of a branch: 0 class branches (always connected), 1 cv2, 2 one2one_cv2 (a box
+ * branch receives a gradient only when its loss assigned a positive, DetectionLoss.cs:101) */
+static int branch_group(int branch) { return branch < 3 ? 1 : (branch >= 6 && branch < 9) ? 2 : 0; }
 
 static long block_weight_count(const syo_block *b) { return (long)b->oc * (b->ic / b->groups) * b->k * b->k; }
 
 long syo_head_param_count(const syo_head_desc *d)
 {
     long total = 0;
-    for (int br = 0; br < 6; br++) {
+    for (int br = 0; br < n_branches(d); br++) {
         int n;
         const syo_block *blocks = branch_blocks(d, br, &n);
         for (int i = 0; i < n; i++) {
@@ -55,7 +64,7 @@ long syo_head_param_count(const syo_head_desc *d)
 long syo_head_buffer_count(const syo_head_desc *d)
 {
     long total = 0;
-    for (int br = 0; br < 6; br++) {
+    for (int br = 0; br < n_branches(d); br++) {
         int n;
         const syo_block *blocks = branch_blocks(d, br, &n);
         for (int i = 0; i < n; i++)
@@ -74,7 +83,7 @@ static int slots_for_branch(const syo_head_desc *d, int branch, block_slot *out)
 {
     long p = 0, q = 0;
     int n = 0;
-    for (int br = 0; br < 6; br++) {
+    for (int br = 0; br < n_branches(d); br++) {
         int cnt;
         const syo_block *blocks = branch_blocks(d, br, &cnt);
         for (int i = 0; i < cnt; i++) {
@@ -196,48 +205,79 @@ static void free_states(block_state *st, int n)
 }
 
 /* Head loss of one image without touching running statistics; stats receives this image's
- * per-channel (mean, biased variance) at the buffer offsets of each BN block. */
+ * per-channel (mean, biased variance) at the buffer offsets of each BN block.
+ * DetectionHead.Loss (DetectionHead.cs:105-115): the one-to-many branches with the top-10 assigner;
+ * with end_to_end also the one-to-one branches (top-k 1, or 7 for the progressive loss, and a second
+ * top-1 after conflicts), each loss's gradients scaled by its weight (ProgressiveWeight for the
+ * progressive loss, else 1) and the reported parts summed with the same weights.
+ * box_connected: bit 0 cv2, bit 1 one2one_cv2. */
 static int head_image_core(const syo_head_desc *d, const float *params, float *buffers, float *stats,
                            const float *const *features, const syo_box *truth, int n_truth, float *grad,
                            syo_loss *loss, int backward, int *box_connected, int training)
 {
-    block_slot slots[6][8];
-    int counts[6];
-    block_state states[6][8];
-    float *outs[6];
-    for (int br = 0; br < 6; br++) counts[br] = slots_for_branch(d, br, slots[br]);
-    for (int l = 0; l < 3; l++)
-        for (int kind = 0; kind < 2; kind++) {
-            int br = kind * 3 + l;
-            outs[br] = branch_forward(d, slots[br], counts[br], params, buffers, stats, features[l], d->hs[l], d->ws[l],
-                                      states[br], training);
+    block_slot slots[12][8];
+    int counts[12];
+    block_state states[12][8];
+    float *outs[12];
+    const int nbr = n_branches(d), sets = nbr / 6;
+    for (int br = 0; br < nbr; br++) counts[br] = slots_for_branch(d, br, slots[br]);
+    for (int set = 0; set < sets; set++)
+        for (int l = 0; l < 3; l++)
+            for (int kind = 0; kind < 2; kind++) {
+                int br = set * 6 + kind * 3 + l;
+                outs[br] = branch_forward(d, slots[br], counts[br], params, buffers, stats, features[l], d->hs[l],
+                                          d->ws[l], states[br], training);
+            }
+    const int progressive = d->end_to_end && d->bins == 1;
+    const float many_w = progressive ? syo_progressive_weight(d->epoch, d->schedule_epochs) : 1.0f;
+    const float one_w = progressive ? 1 - many_w : 1.0f;
+    syo_loss parts[2];
+    memset(parts, 0, sizeof parts);
+    int rc = 0, connected = 0;
+    for (int set = 0; set < sets && rc == 0; set++) {
+        const int o = set * 6;
+        const float *boxes[3] = {outs[o], outs[o + 1], outs[o + 2]};
+        const float *classes[3] = {outs[o + 3], outs[o + 4], outs[o + 5]};
+        float *dbox[3], *dcls[3];
+        for (int l = 0; l < 3; l++) {
+            size_t spatial = (size_t)d->hs[l] * d->ws[l];
+            dbox[l] = (float *)calloc(4 * d->bins * spatial, sizeof(float));
+            dcls[l] = (float *)calloc(d->nc * spatial, sizeof(float));
         }
-    const float *boxes[3] = {outs[0], outs[1], outs[2]}, *classes[3] = {outs[3], outs[4], outs[5]};
-    float *dbox[3], *dcls[3];
-    for (int l = 0; l < 3; l++) {
-        size_t spatial = (size_t)d->hs[l] * d->ws[l];
-        dbox[l] = (float *)calloc(4 * d->bins * spatial, sizeof(float));
-        dcls[l] = (float *)calloc(d->nc * spatial, sizeof(float));
-    }
-    int rc = syo_detection_loss(boxes, classes, d->hs, d->ws, d->strides, 3, d->nc, d->bins, truth, n_truth, 10, 10,
-                                1.0f, backward, dbox, dcls, loss, NULL, NULL);
-    if (box_connected) *box_connected = loss->connected;
-    if (rc == 0 && backward) {
-        for (int l = 2; l >= 0; l--) {
-            branch_backward(slots[3 + l], counts[3 + l], params, grad, states[3 + l], dcls[l], d->hs[l], d->ws[l]);
-            if (loss->connected)
-                branch_backward(slots[l], counts[l], params, grad, states[l], dbox[l], d->hs[l], d->ws[l]);
+        const int topk = set == 0 ? 10 : progressive ? 7 : 1, topk2 = set == 0 ? 10 : 1;
+        const float weight = set == 0 ? many_w : one_w;
+        rc = syo_detection_loss(boxes, classes, d->hs, d->ws, d->strides, 3, d->nc, d->bins, truth, n_truth, topk,
+                                topk2, weight, backward, dbox, dcls, &parts[set], NULL, NULL);
+        connected |= (parts[set].connected ? 1 : 0) << set;
+        if (rc == 0 && backward) {
+            for (int l = 2; l >= 0; l--) {
+                branch_backward(slots[o + 3 + l], counts[o + 3 + l], params, grad, states[o + 3 + l], dcls[l],
+                                d->hs[l], d->ws[l]);
+                if (parts[set].connected)
+                    branch_backward(slots[o + l], counts[o + l], params, grad, states[o + l], dbox[l], d->hs[l],
+                                    d->ws[l]);
+            }
         }
+        for (int l = 0; l < 3; l++) { free(dbox[l]); free(dcls[l]); }
     }
-    for (int l = 0; l < 3; l++) { free(dbox[l]); free(dcls[l]); }
-    for (int br = 0; br < 6; br++) free_states(states[br], counts[br]);
+    if (d->end_to_end) {
+        loss->box = parts[0].box * many_w + parts[1].box * one_w;
+        loss->cls = parts[0].cls * many_w + parts[1].cls * one_w;
+        loss->dfl = parts[0].dfl * many_w + parts[1].dfl * one_w;
+        loss->positives = parts[0].positives + parts[1].positives;
+    } else {
+        *loss = parts[0];
+    }
+    loss->connected = connected;
+    if (box_connected) *box_connected = connected;
+    for (int br = 0; br < nbr; br++) free_states(states[br], counts[br]);
     return rc;
 }
 
 /* fold one image's BN statistics into the running buffers (HeadOperations.cs:164-165, DetectionHead.cs:154) */
 static void fold_running_stats(const syo_head_desc *d, float *buffers, const float *stats)
 {
-    for (int br = 0; br < 6; br++) {
+    for (int br = 0; br < n_branches(d); br++) {
         block_slot slots[8];
         int n = slots_for_branch(d, br, slots);
         for (int i = 0; i < n; i++) {
@@ -742,20 +782,20 @@ void syo_backbone_forward(const syo_backbone_desc *d, const float *params, const
 /* ------------------------------------------------------------------ full step */
 
 /* segment flags per head parameter: box branch or not, decay (conv weights only, DetectionHead.cs:59-60) */
-static void param_segments(const syo_head_desc *d, long *offs, long *lens, int *is_box, int *decay, int *count)
+static void param_segments(const syo_head_desc *d, long *offs, long *lens, int *group, int *decay, int *count)
 {
     int n = 0;
     long p = 0;
-    for (int br = 0; br < 6; br++) {
+    for (int br = 0; br < n_branches(d); br++) {
         int cnt;
         const syo_block *blocks = branch_blocks(d, br, &cnt);
         for (int i = 0; i < cnt; i++) {
             long wl = block_weight_count(&blocks[i]);
-            offs[n] = p; lens[n] = wl; is_box[n] = br < 3; decay[n] = 1; n++; p += wl;
-            if (blocks[i].has_bias) { offs[n] = p; lens[n] = blocks[i].oc; is_box[n] = br < 3; decay[n] = 0; n++; p += blocks[i].oc; }
+            offs[n] = p; lens[n] = wl; group[n] = branch_group(br); decay[n] = 1; n++; p += wl;
+            if (blocks[i].has_bias) { offs[n] = p; lens[n] = blocks[i].oc; group[n] = branch_group(br); decay[n] = 0; n++; p += blocks[i].oc; }
             if (blocks[i].has_bn) {
-                offs[n] = p; lens[n] = blocks[i].oc; is_box[n] = br < 3; decay[n] = 0; n++; p += blocks[i].oc;
-                offs[n] = p; lens[n] = blocks[i].oc; is_box[n] = br < 3; decay[n] = 0; n++; p += blocks[i].oc;
+                offs[n] = p; lens[n] = blocks[i].oc; group[n] = branch_group(br); decay[n] = 0; n++; p += blocks[i].oc;
+                offs[n] = p; lens[n] = blocks[i].oc; group[n] = branch_group(br); decay[n] = 0; n++; p += blocks[i].oc;
             }
         }
     }
@@ -811,11 +851,11 @@ void syo_train_step(const syo_backbone_desc *bd, const float *backbone_params, c
     if (r.status == 0 && (!finite || !syo_all_finite(grad, np))) r.status = 3;  /* YoloTrainer.cs:196 */
     if (grad_out) memcpy(grad_out, grad, sizeof(float) * np);
     if (r.status == 0) {
-        long offs[512], lens[512];
-        int is_box[512], decay[512], nseg = 0;
-        param_segments(hd, offs, lens, is_box, decay, &nseg);
+        long offs[1024], lens[1024];
+        int group[1024], decay[1024], nseg = 0;
+        param_segments(hd, offs, lens, group, decay, &nseg);
         for (int s = 0; s < nseg; s++) {
-            int has = is_box[s] ? any_connected : 1;
+            int has = group[s] ? (any_connected >> (group[s] - 1)) & 1 : 1;
             int bad;
             if (opt->optimizer == 0)
                 bad = syo_sgd_update(params + offs[s], velocity + offs[s], grad + offs[s], lens[s], opt->lr, opt->momentum,
@@ -823,7 +863,7 @@ void syo_train_step(const syo_backbone_desc *bd, const float *backbone_params, c
             else
                 bad = syo_adamw_update(params + offs[s], velocity + offs[s], velocity2 + offs[s], grad + offs[s], lens[s],
                                        opt->lr, opt->beta1, opt->beta2, opt->adam_eps, decay[s] ? opt->weight_decay : 0.0f,
-                                       opt->adam_step[is_box[s]] + 1, batch, has);
+                                       opt->adam_step[group[s]] + 1, batch, has);
             if (bad) { r.status = 3; break; }
         }
     }

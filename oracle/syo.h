@@ -91,17 +91,23 @@ typedef struct {
     syo_block box_blocks[3][8]; /* per level */
     syo_block cls_blocks[3][8];
     float bn_eps, bn_momentum;
+    /* TrainingHeadSchema (TrainingHeadSchema.cs:7-12): end_to_end adds one2one_cv2 / one2one_cv3
+     * branches built like cv2 / cv3; bins == 1 with end_to_end is the progressive (YOLO26) loss.
+     * epoch / schedule_epochs feed DetectionHead.ProgressiveWeight. */
+    int32_t end_to_end;
+    int32_t epoch, schedule_epochs;
 } syo_head_desc;
 
 /* Number of floats in the flat parameter array and in the flat buffer array (Snapshot order:
- * cv2.0, cv2.1, cv2.2, cv3.0, cv3.1, cv3.2; per block weight, [bias], [gamma, beta]). */
+ * cv2.0, cv2.1, cv2.2, cv3.0, cv3.1, cv3.2, then with end_to_end one2one_cv2.0-2, one2one_cv3.0-2;
+ * per block weight, [bias], [gamma, beta]). */
 long syo_head_param_count(const syo_head_desc *d);
 long syo_head_buffer_count(const syo_head_desc *d);
 
 /* One image: head forward (training BN: running stats updated in place), loss, backward.
  * features[l]: [C_l, H_l, W_l].  grads accumulated into grad (flat, param order).
  * bn_stats (optional) receives per BN channel (mean, biased var) of this image in param order.
- * box_has_grad: set to 1 when the box branch was connected for this image. */
+ * box_connected: bit 0 set when cv2 was connected for this image, bit 1 when one2one_cv2 was. */
 int syo_head_image(const syo_head_desc *d, const float *params, float *buffers,
                    const float *const *features, const syo_box *truth, int n_truth,
                    float *grad, syo_loss *loss, int backward, int *box_connected);
@@ -127,7 +133,7 @@ typedef struct {
     float lr, momentum, weight_decay;
     int32_t optimizer;     /* 0 SGD, 1 AdamW */
     float beta1, beta2, adam_eps;
-    int32_t adam_step[2];  /* AdamW steps already taken: [0] always-connected params, [1] box branch */
+    int32_t adam_step[3];  /* AdamW steps already taken: [0] always-connected params, [1] cv2, [2] one2one_cv2 */
 } syo_optim;
 
 typedef struct { double box, cls, dfl; int64_t positives; int32_t box_has_grad; int32_t status; } syo_step_result;

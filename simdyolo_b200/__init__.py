@@ -74,7 +74,8 @@ class Config(C.Structure):
                 ("n_cls_blocks", C.c_int32), ("box_blocks", (Block * 8) * 3), ("cls_blocks", (Block * 8) * 3),
                 ("bn_eps", C.c_float), ("bn_momentum", C.c_float), ("optimizer", C.c_int32), ("lr", C.c_float),
                 ("momentum", C.c_float), ("weight_decay", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float),
-                ("adam_eps", C.c_float), ("precision", C.c_int32)]
+                ("adam_eps", C.c_float), ("precision", C.c_int32), ("end_to_end", C.c_int32),
+                ("schedule_epochs", C.c_int32)]
 
 
 class StepStats(C.Structure):
@@ -120,6 +121,7 @@ def lib():
         L.sy_cuda_step_features.argtypes = [vp, C.POINTER(fp), C.POINTER(Box), ip, C.c_int32, C.POINTER(StepStats)]
         L.sy_cuda_eval_loss_features.argtypes = L.sy_cuda_step_features.argtypes
         L.sy_cuda_get_last_gradients.argtypes = [vp, fp, C.c_int64]
+        L.sy_cuda_set_epoch.argtypes = [vp, C.c_int32]
         L.sy_cuda_get_last_features.argtypes = [vp, C.c_int32, fp, C.c_int64]
         L.sy_cuda_detection_loss.argtypes = [C.c_int32, C.c_int32, C.c_int32, ip, ip, fp, C.c_int32, C.c_int32,
                                              C.POINTER(fp), C.POINTER(fp), C.POINTER(Box), ip, fp, ip, ip, fp,
@@ -158,7 +160,7 @@ EXPORTED = ["sy_cuda_nccl_unique_id", "sy_cuda_create", "sy_cuda_destroy", "sy_c
             "sy_cuda_conv2d_backward_data", "sy_cuda_conv2d_backward_filter", "sy_cuda_matmul", "sy_cuda_sgd_update",
             "sy_cuda_step_device", "sy_cuda_launch_count", "sy_cuda_bench_conv",
             "sy_cuda_conv2d_backward_filter_static", "sy_cuda_conv_profile", "sy_cuda_eval_loss",
-            "sy_cuda_eval_loss_features", "sy_cuda_detection_loss_ex"]
+            "sy_cuda_eval_loss_features", "sy_cuda_detection_loss_ex", "sy_cuda_set_epoch"]
 
 
 def _check(status: int, session=None):
@@ -325,6 +327,12 @@ MODELS = {
 }
 
 
+def tensor_group(name: str) -> int:
+    """Optimizer group of a head tensor: 0 class branches (always receive a gradient), 1 cv2, 2
+    one2one_cv2 (a box branch receives one only when its loss assigned a positive)."""
+    return 1 if name.startswith("cv2.") else 2 if name.startswith("one2one_cv2.") else 0
+
+
 def model_family(model: str) -> str:
     """'yolo11' (C3k2 / C2PSA trunk, depthwise class branch) or 'yolov8'."""
     return "yolo11" if model.startswith("yolo11") else "yolov8"
@@ -334,7 +342,11 @@ def make_config(model: str = "yolov8n", image_size: int = 640, max_batch: int = 
                 num_classes: int = 80, device: int = 0, rank: int = 0, world_size: int = 1, nccl_id: bytes = b"",
                 backbone: bool = True, optimizer: int = SY_OPT_SGD, lr: float = 0.01, momentum: float = 0.937,
                 weight_decay: float = 5e-4, beta1: float = 0.9, beta2: float = 0.999, adam_eps: float = 1e-8,
-                bn_eps: float = 1e-3, bn_momentum: float = 0.03, precision: int = SY_PRECISION_TF32) -> Config:
+                bn_eps: float = 1e-3, bn_momentum: float = 0.03, precision: int = SY_PRECISION_TF32,
+                end_to_end: bool = False, reg_max: int = 16, schedule_epochs: int = 100) -> Config:
+    """Session description for `model`'s trunk and Detect head.  end_to_end adds the one2one_cv2 /
+    one2one_cv3 branches (YOLOv10 v10Detect with reg_max 16; YOLO26-style progressive loss with
+    reg_max 1, TrainingHeadSchema.cs:17-21); schedule_epochs is the progressive schedule length."""
     width, depth, max_ch = MODELS[model]
     feats = yolov8_channels(width, max_ch)
     cfg = Config()
@@ -343,13 +355,13 @@ def make_config(model: str = "yolov8n", image_size: int = 640, max_batch: int = 
     for i, b in enumerate(nccl_id[:128]):
         cfg.nccl_id[i] = b
     cfg.image_size, cfg.max_batch, cfg.max_boxes = image_size, max_batch, max_boxes
-    cfg.num_classes, cfg.reg_max = num_classes, 16
+    cfg.num_classes, cfg.reg_max = num_classes, reg_max
     family = model_family(model)
     cfg.backbone = (SY_BACKBONE_YOLO11 if family == "yolo11" else SY_BACKBONE_YOLOV8) if backbone else SY_BACKBONE_NONE
     cfg.width_mult, cfg.depth_mult, cfg.max_channels = width, depth, max_ch
     for i in range(3):
         cfg.feature_channels[i] = feats[i]
-    box, cls = detect_head_blocks(feats, num_classes, dw_cls=model_family(model) == "yolo11")
+    box, cls = detect_head_blocks(feats, num_classes, reg_max, dw_cls=model_family(model) == "yolo11")
     cfg.n_box_blocks, cfg.n_cls_blocks = len(box[0]), len(cls[0])
     for lvl in range(3):
         for i, b in enumerate(box[lvl]):
@@ -360,6 +372,7 @@ def make_config(model: str = "yolov8n", image_size: int = 640, max_batch: int = 
     cfg.optimizer, cfg.lr, cfg.momentum, cfg.weight_decay = optimizer, lr, momentum, weight_decay
     cfg.beta1, cfg.beta2, cfg.adam_eps = beta1, beta2, adam_eps
     cfg.precision = precision
+    cfg.end_to_end, cfg.schedule_epochs = int(bool(end_to_end)), schedule_epochs
     return cfg
 
 
@@ -503,6 +516,10 @@ class Session:
         _check(lib().sy_cuda_eval_loss_features(self._h, ptrs, arr, _ip(counts), feats[0].shape[0],
                                                 C.byref(stats)), self._h)
         return stats
+
+    def set_epoch(self, epoch: int):
+        """Completed epochs, fed to the progressive end-to-end loss weight (DetectionHead.ProgressiveWeight)."""
+        _check(lib().sy_cuda_set_epoch(self._h, epoch), self._h)
 
     def last_gradients(self) -> np.ndarray:
         n = sum(t["numel"] for t in self.params)

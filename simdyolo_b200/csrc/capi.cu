@@ -270,6 +270,11 @@ sy_status sy_cuda_bench_conv(int32_t device, int32_t kind, int32_t n, int32_t ic
     });
 }
 
+sy_status sy_cuda_set_epoch(sy_session* session, int32_t epoch) {
+    if (!session) return SY_ERR_INVALID_ARGUMENT;
+    return guarded(session, [&] { return session->impl->set_epoch(epoch); });
+}
+
 sy_status sy_cuda_get_last_gradients(const sy_session* session, float* host, int64_t count) {
     if (!session) return SY_ERR_INVALID_ARGUMENT;
     sy_session* s = const_cast<sy_session*>(session);

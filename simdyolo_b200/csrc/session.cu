@@ -93,7 +93,16 @@ Session::Session(const sy_config& c) : cfg(c) {
     if (c.max_batch < 1 || c.max_batch > 1024) throw SyError(SY_ERR_INVALID_ARGUMENT, "max_batch out of range");
     if (c.max_boxes < 0 || c.max_boxes > 100) throw SyError(SY_ERR_INVALID_ARGUMENT, "max_boxes out of range");
     if (c.num_classes < 1 || c.num_classes > 256) throw SyError(SY_ERR_INVALID_ARGUMENT, "num_classes out of range");
-    if (c.reg_max != 16) throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "only reg_max = 16 (DFL) is supported");
+    // TrainingHeadSchema.Read (TrainingHeadSchema.cs:17-21): 16 bins, or 1 (direct distances) on
+    // end-to-end heads only; end-to-end with one bin is the progressive loss
+    if (c.reg_max != 16 && c.reg_max != 1)
+        throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "reg_max must be 16 (DFL) or 1 (direct distances)");
+    if (c.end_to_end != 0 && c.end_to_end != 1) throw SyError(SY_ERR_INVALID_ARGUMENT, "end_to_end must be 0 or 1");
+    if (c.reg_max == 1 && !c.end_to_end)
+        throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "reg_max 1 needs the one2one branches (end_to_end)");
+    if (c.schedule_epochs < 0) throw SyError(SY_ERR_INVALID_ARGUMENT, "schedule_epochs must not be negative");
+    n_sets_ = c.end_to_end ? 2 : 1;
+    progressive_ = c.end_to_end && c.reg_max == 1;
     if (c.world_size < 1 || c.rank < 0 || c.rank >= c.world_size)
         throw SyError(SY_ERR_INVALID_ARGUMENT, "bad rank / world_size");
     if (!(c.lr > 0) || !(c.momentum >= 0 && c.momentum < 1) || !(c.weight_decay >= 0))
@@ -132,17 +141,18 @@ Session::Session(const sy_config& c) : cfg(c) {
     loss_ws_ = dalloc(loss_workspace_bytes(B_, anchors, std::max(1, c.max_boxes), 10));
     d_truth_ = static_cast<TruthBox*>(dalloc(sizeof(TruthBox) * (size_t)B_ * std::max(1, c.max_boxes)));
     d_box_off_ = static_cast<int*>(dalloc(sizeof(int) * (B_ + 1)));
-    d_loss_ = static_cast<float*>(dalloc(sizeof(float) * 4 * B_));
-    d_pos_ = static_cast<int*>(dalloc(sizeof(int) * B_));
-    d_conn_ = static_cast<int*>(dalloc(sizeof(int) * B_));
+    // per branch set: [set][image] loss parts, positives and box connection
+    d_loss_ = static_cast<float*>(dalloc(sizeof(float) * 4 * 2 * B_));
+    d_pos_ = static_cast<int*>(dalloc(sizeof(int) * 2 * B_));
+    d_conn_ = static_cast<int*>(dalloc(sizeof(int) * 2 * B_));
     d_flags_ = static_cast<int*>(dalloc(sizeof(int) * 16));
     d_abs_ = static_cast<double*>(dalloc(sizeof(double) * kAbsSumBlocks));
     SY_CUDA(cudaMallocHost(&h_truth_, sizeof(TruthBox) * (size_t)B_ * std::max(1, c.max_boxes)));
     SY_CUDA(cudaMallocHost(&h_box_off_, sizeof(int) * (B_ + 1)));
     SY_CUDA(cudaMallocHost(&h_flags_, sizeof(int) * 16));
-    SY_CUDA(cudaMallocHost(&h_loss_, sizeof(float) * 4 * B_));
-    SY_CUDA(cudaMallocHost(&h_pos_, sizeof(int) * B_));
-    SY_CUDA(cudaMallocHost(&h_conn_, sizeof(int) * B_));
+    SY_CUDA(cudaMallocHost(&h_loss_, sizeof(float) * 4 * 2 * B_));
+    SY_CUDA(cudaMallocHost(&h_pos_, sizeof(int) * 2 * B_));
+    SY_CUDA(cudaMallocHost(&h_conn_, sizeof(int) * 2 * B_));
     SY_CUDA(cudaMallocHost(&h_abs_, sizeof(double) * kAbsSumBlocks));
     if (c.backbone != SY_BACKBONE_NONE) {
         SY_CUDA(cudaMallocHost(&h_rgb_, (size_t)B_ * c.image_size * c.image_size * 3));
@@ -544,17 +554,27 @@ static std::string block_path(int i, int n) {
     return std::to_string(i);
 }
 
+// Branch name prefix in DetectionHead order (DetectionHead.cs:20-26, TrainingHeadSchema.cs:12).
+static std::string branch_prefix(const Branch& b) {
+    static const char* names[2][2] = {{"cv3.", "cv2."}, {"one2one_cv3.", "one2one_cv2."}};
+    return std::string(names[b.set][b.box ? 1 : 0]) + std::to_string(b.level);
+}
+
 void Session::build_head() {
     long poff = 0, qoff = 0;
-    for (int br = 0; br < 6; br++) {
+    // cv2.0-2, cv3.0-2, then for end-to-end heads one2one_cv2.0-2, one2one_cv3.0-2 with the same
+    // block lists (the one-to-one branches are copies of the one-to-many ones in the source model)
+    for (int br = 0; br < 6 * n_sets_; br++) {
         Branch branch;
         branch.level = br % 3;
-        branch.box = br < 3;
+        branch.box = (br / 3) % 2 == 0;
+        branch.set = br / 6;
+        branch.group = branch.box ? 1 + branch.set : 0;
         const int l = branch.level;
         const int n = branch.box ? cfg.n_box_blocks : cfg.n_cls_blocks;
         if (n < 1 || n > 8) throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "head branch needs 1..8 blocks");
         const sy_block* blocks = branch.box ? cfg.box_blocks[l] : cfg.cls_blocks[l];
-        const std::string prefix = std::string(branch.box ? "cv2." : "cv3.") + std::to_string(l);
+        const std::string prefix = branch_prefix(branch);
         int ic = feat_ch_[l];
         for (int i = 0; i < n; i++) {
             HeadBlock hb;
@@ -573,7 +593,7 @@ void Session::build_head() {
             const std::string path = prefix + "." + block_path(i, n);
             const long wn = (long)b.oc * (b.ic / b.groups) * b.k * b.k;
             auto add_param = [&](const std::string& name, std::vector<int> shape, long numel, int decay) {
-                TensorEntry e{name, 0, shape, poff, numel, branch.box ? 1 : 0, decay};
+                TensorEntry e{name, 0, shape, poff, numel, branch.group, decay};
                 tensors.push_back(e);
                 long off = poff;
                 poff += numel;
@@ -597,7 +617,7 @@ void Session::build_head() {
     n_params = poff;
     // buffers after all parameters (Snapshot order: parameters, then BN buffers)
     for (auto& branch : branches_) {
-        const std::string prefix = std::string(branch.box ? "cv2." : "cv3.") + std::to_string(branch.level);
+        const std::string prefix = branch_prefix(branch);
         const int n = (int)branch.blocks.size();
         for (int i = 0; i < n; i++) {
             HeadBlock& hb = branch.blocks[i];
@@ -735,51 +755,123 @@ void Session::forward_head(int batch, bool training) {
 }
 
 void Session::backward_head(int batch) {
-    for (int l = 2; l >= 0; l--)
-        for (int kind = 1; kind >= 0; kind--) {
-            Branch& branch = branches_[kind * 3 + l];
-            const Grid& g = levels_[l];
-            for (int i = (int)branch.blocks.size() - 1; i >= 0; i--) {
-                HeadBlock& hb = branch.blocks[i];
-                if (hb.b.has_bn) {
-                    // hb.g holds dz and bn_part_ its partial sums, written by the next block's data-gradient
-                    // epilogue (every BN block is followed by another block)
-                    bn_backward_fold(bn_part_, batch, g, hb.b.oc, hb.coef, params_ + hb.g_off, grads_ + hb.g_off,
-                                     grads_ + hb.be_off, hb.bcoef, stream_);
-                    bn_backward_apply(rows_of(hb.y, batch, g), rows_of(hb.g, batch, g), hb.coef, hb.bcoef, batch, g,
-                                      rows_of(hb.dy, batch, g), stream_);
-                }
-                if (hb.b.has_bias) bias_grad(hb.dy, batch, g, bias_part_, grads_ + hb.b_off, stream_);
-                if (hb.dw)
-                    dw_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off,
-                             wgrad_ws_, stream_);
-                else
-                    conv_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off);
-                if (i > 0) {
-                    HeadBlock& prev = branch.blocks[i - 1];
-                    ConvEpilogue ep;
-                    if (prev.b.has_bn) {
-                        ep.bn.channels = prev.b.oc;
-                        ep.bn.y = prev.y.base;
-                        ep.bn.y_pitch = prev.y.pitch;
-                        ep.bn.mean = prev.coef;
-                        ep.bn.inv = prev.coef + (long)batch * prev.b.oc;
-                        ep.bn.gamma = params_ + prev.g_off;
-                        ep.bn.beta = params_ + prev.be_off;
-                        ep.bn.grad_part = bn_part_;
+    for (int set = n_sets_ - 1; set >= 0; set--)
+        for (int l = 2; l >= 0; l--)
+            for (int kind = 1; kind >= 0; kind--) {
+                Branch& branch = branches_[set * 6 + kind * 3 + l];
+                const Grid& g = levels_[l];
+                for (int i = (int)branch.blocks.size() - 1; i >= 0; i--) {
+                    HeadBlock& hb = branch.blocks[i];
+                    if (hb.b.has_bn) {
+                        // hb.g holds dz and bn_part_ its partial sums, written by the next block's data-gradient
+                        // epilogue (every BN block is followed by another block)
+                        bn_backward_fold(bn_part_, batch, g, hb.b.oc, hb.coef, params_ + hb.g_off, grads_ + hb.g_off,
+                                         grads_ + hb.be_off, hb.bcoef, stream_);
+                        bn_backward_apply(rows_of(hb.y, batch, g), rows_of(hb.g, batch, g), hb.coef, hb.bcoef, batch, g,
+                                          rows_of(hb.dy, batch, g), stream_);
                     }
-                    if (hb.dw) {
-                        dw_conv(rows_of(hb.dy, batch, g), params_ + hb.w_off, hb.taps, -1, g, rows_of(prev.g, batch, g),
-                                ep.bn, stream_);
-                    } else {
-                        prof_begin();
-                        conv_fwd(rows_of(hb.dy, batch, g), hb.w_dgrad, (long)hb.b.ic * hb.taps * hb.kpad_out,
-                                 hb.b.ic, hb.b.ic, hb.taps, -1, g, rows_of(prev.g, batch, g), ep, nullptr);
-                        prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w);
+                    if (hb.b.has_bias) bias_grad(hb.dy, batch, g, bias_part_, grads_ + hb.b_off, stream_);
+                    if (hb.dw)
+                        dw_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off,
+                                 wgrad_ws_, stream_);
+                    else
+                        conv_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off);
+                    if (i > 0) {
+                        HeadBlock& prev = branch.blocks[i - 1];
+                        ConvEpilogue ep;
+                        if (prev.b.has_bn) {
+                            ep.bn.channels = prev.b.oc;
+                            ep.bn.y = prev.y.base;
+                            ep.bn.y_pitch = prev.y.pitch;
+                            ep.bn.mean = prev.coef;
+                            ep.bn.inv = prev.coef + (long)batch * prev.b.oc;
+                            ep.bn.gamma = params_ + prev.g_off;
+                            ep.bn.beta = params_ + prev.be_off;
+                            ep.bn.grad_part = bn_part_;
+                        }
+                        if (hb.dw) {
+                            dw_conv(rows_of(hb.dy, batch, g), params_ + hb.w_off, hb.taps, -1, g, rows_of(prev.g, batch, g),
+                                    ep.bn, stream_);
+                        } else {
+                            prof_begin();
+                            conv_fwd(rows_of(hb.dy, batch, g), hb.w_dgrad, (long)hb.b.ic * hb.taps * hb.kpad_out,
+                                     hb.b.ic, hb.b.ic, hb.taps, -1, g, rows_of(prev.g, batch, g), ep, nullptr);
+                            prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w);
+                        }
                     }
                 }
             }
+}
+
+// ------------------------------------------------------------------ loss
+// DetectionHead.ProgressiveWeight (DetectionHead.cs:120) for progressive heads, else both weights 1;
+// the product and the sum round separately, as in the reference.
+void Session::loss_weights(int epoch, float w[2]) const {
+    if (!progressive_) {
+        w[0] = w[1] = 1.0f;
+        return;
+    }
+    const float t = std::max(1.0f - (float)epoch / (float)std::max(cfg.schedule_epochs - 1, 1), 0.0f);
+    const float scaled = t * 0.7f;
+    w[0] = scaled + 0.1f;
+    w[1] = 1.0f - w[0];
+}
+
+// DetectionHead.Loss (DetectionHead.cs:105-115): the one-to-many set with the top-10 assigner; an
+// end-to-end head adds the one-to-one set with top-k 1 (7 when progressive) and a second top-1 after
+// conflicts.  Each set's output gradients are scaled by its weight.
+void Session::launch_losses(int images, int backward, int epoch) {
+    float w[2];
+    loss_weights(epoch, w);
+    for (int set = 0; set < n_sets_; set++) {
+        LevelIO lv[3];
+        for (int l = 0; l < 3; l++) {
+            HeadBlock& bb = branches_[set * 6 + l].blocks.back();
+            HeadBlock& cb = branches_[set * 6 + 3 + l].blocks.back();
+            lv[l] = LevelIO{bb.y.base, cb.y.base, bb.g.base, cb.g.base, bb.y.pitch, cb.y.pitch, levels_[l],
+                            (float)(8 << l)};
         }
+        LossOut lo{d_loss_ + (size_t)4 * B_ * set, d_pos_ + (size_t)B_ * set, d_conn_ + (size_t)B_ * set, nullptr,
+                   nullptr};
+        const int topk = set == 0 ? 10 : (progressive_ ? 7 : 1), topk2 = set == 0 ? 10 : 1;
+        detection_loss(lv, 3, images, cfg.num_classes, cfg.reg_max, d_truth_, d_box_off_, std::max(1, cfg.max_boxes),
+                       topk, topk2, cfg.end_to_end ? w[set] : 1.0f, backward, loss_ws_, lo, stream_);
+    }
+}
+
+// Per image the reported parts are a.Part * w0 + b.Part * w1 in float (DetectionHead.cs:114), summed
+// over the images in double; positives add up; `finite` checks every image's total (YoloTrainer.cs:193).
+void Session::combine_losses(int images, int epoch, double* box, double* cls, double* dfl, long* positives,
+                             int* connected, bool* finite) const {
+    float w[2];
+    loss_weights(epoch, w);
+    *box = *cls = *dfl = 0.0;
+    *positives = 0;
+    *connected = 0;
+    for (int b = 0; b < images; b++) {
+        float part[3];
+        for (int k = 0; k < 3; k++) {
+            part[k] = h_loss_[4 * b + k];
+            if (n_sets_ == 2) {
+                const float one = h_loss_[4 * ((size_t)B_ + b) + k] * w[1];
+                part[k] = part[k] * w[0] + one;
+            }
+        }
+        *box += part[0];
+        *cls += part[1];
+        *dfl += part[2];
+        if (!std::isfinite(part[0] + part[1] + part[2])) *finite = false;
+        for (int set = 0; set < n_sets_; set++) {
+            *positives += h_pos_[(size_t)B_ * set + b];
+            if (h_conn_[(size_t)B_ * set + b]) *connected |= 1 << set;
+        }
+    }
+}
+
+int Session::set_epoch(int epoch) {
+    if (epoch < 0) throw SyError(SY_ERR_INVALID_ARGUMENT, "epoch must not be negative");
+    epoch_ = epoch;
+    return SY_OK;
 }
 
 // ------------------------------------------------------------------ step
@@ -845,17 +937,7 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
                   const int32_t* counts, int images, sy_step_stats* out) {
     prepare_inputs(rgb, rgb_on_device, features, boxes, counts, images);
     forward_head(images);
-    // loss
-    LevelIO lv[3];
-    for (int l = 0; l < 3; l++) {
-        HeadBlock& bb = branches_[l].blocks.back();
-        HeadBlock& cb = branches_[3 + l].blocks.back();
-        lv[l] = LevelIO{bb.y.base, cb.y.base, bb.g.base, cb.g.base, bb.y.pitch, cb.y.pitch, levels_[l],
-                        (float)(8 << l)};
-    }
-    LossOut lo{d_loss_, d_pos_, d_conn_, nullptr, nullptr};
-    detection_loss(lv, 3, images, cfg.num_classes, cfg.reg_max, d_truth_, d_box_off_, std::max(1, cfg.max_boxes), 10,
-                   10, 1.0f, 1, loss_ws_, lo, stream_);
+    launch_losses(images, 1, epoch_);
     backward_head(images);
     if (comm_) {
         // the gradient bucket is summed over ranks before anything reads it, so the finiteness
@@ -866,48 +948,43 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
     SY_CUDA(cudaMemcpyAsync(last_grads_, grads_, sizeof(float) * n_params, cudaMemcpyDeviceToDevice, stream_));
     check_finite(grads_, n_params, d_flags_ + 1, stream_);
     abs_sum_partials(grads_, n_params, d_abs_, stream_);
-    SY_CUDA(cudaMemcpyAsync(h_loss_, d_loss_, sizeof(float) * 4 * images, cudaMemcpyDeviceToHost, stream_));
-    SY_CUDA(cudaMemcpyAsync(h_pos_, d_pos_, sizeof(int) * images, cudaMemcpyDeviceToHost, stream_));
-    SY_CUDA(cudaMemcpyAsync(h_conn_, d_conn_, sizeof(int) * images, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaMemcpyAsync(h_loss_, d_loss_, sizeof(float) * 4 * 2 * B_, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaMemcpyAsync(h_pos_, d_pos_, sizeof(int) * 2 * B_, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaMemcpyAsync(h_conn_, d_conn_, sizeof(int) * 2 * B_, cudaMemcpyDeviceToHost, stream_));
     SY_CUDA(cudaMemcpyAsync(h_flags_, d_flags_, sizeof(int) * 16, cudaMemcpyDeviceToHost, stream_));
     SY_CUDA(cudaMemcpyAsync(h_abs_, d_abs_, sizeof(double) * kAbsSumBlocks, cudaMemcpyDeviceToHost, stream_));
     SY_CUDA(cudaStreamSynchronize(stream_));
     if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "device wait limit exceeded (code " + std::to_string(h_flags_[0]) + ")");
     double box = 0, cls = 0, dfl = 0, abs_sum = 0;
     long positives = 0;
-    int connected = 0;
+    int connected = 0;   // bit s: the box branch of set s received a gradient
     bool finite = h_flags_[1] == 0;
-    for (int b = 0; b < images; b++) {
-        box += h_loss_[4 * b];
-        cls += h_loss_[4 * b + 1];
-        dfl += h_loss_[4 * b + 2];
-        if (!std::isfinite(h_loss_[4 * b] + h_loss_[4 * b + 1] + h_loss_[4 * b + 2])) finite = false;
-        positives += h_pos_[b];
-        connected |= h_conn_[b];
-    }
+    combine_losses(images, epoch_, &box, &cls, &dfl, &positives, &connected, &finite);
     for (int i = 0; i < kAbsSumBlocks; i++) abs_sum += h_abs_[i];
     int global_images = images;
     if (comm_) {
-        // scalars summed over ranks: loss parts, positives, connected count, non-finite count, images
+        // scalars summed over ranks: loss parts, positives, connection counts of both box groups,
+        // non-finite count, images
         double* hs = reinterpret_cast<double*>(h_abs_);  // reuse pinned scratch (>= 8 doubles)
         hs[0] = box;
         hs[1] = cls;
         hs[2] = dfl;
         hs[3] = (double)positives;
-        hs[4] = connected;
+        hs[4] = connected & 1;
         hs[5] = finite ? 0.0 : 1.0;
         hs[6] = images;
+        hs[7] = (connected >> 1) & 1;
         double* ds = d_abs_;
-        SY_CUDA(cudaMemcpyAsync(ds, hs, sizeof(double) * 7, cudaMemcpyHostToDevice, stream_));
-        int r = nccl_->AllReduce(ds, ds, 7, kNcclDouble, kNcclSum, comm_, stream_);
+        SY_CUDA(cudaMemcpyAsync(ds, hs, sizeof(double) * 8, cudaMemcpyHostToDevice, stream_));
+        int r = nccl_->AllReduce(ds, ds, 8, kNcclDouble, kNcclSum, comm_, stream_);
         if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllReduce: ") + nccl_->GetErrorString(r));
-        SY_CUDA(cudaMemcpyAsync(hs, ds, sizeof(double) * 7, cudaMemcpyDeviceToHost, stream_));
+        SY_CUDA(cudaMemcpyAsync(hs, ds, sizeof(double) * 8, cudaMemcpyDeviceToHost, stream_));
         SY_CUDA(cudaStreamSynchronize(stream_));
         box = hs[0];
         cls = hs[1];
         dfl = hs[2];
         positives = (long)hs[3];
-        connected = hs[4] > 0;
+        connected = (hs[4] > 0 ? 1 : 0) | (hs[7] > 0 ? 2 : 0);
         finite = hs[5] == 0;
         global_images = (int)hs[6];
         // the running-statistics fold below walks `images` images of every rank in rank order
@@ -941,18 +1018,17 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
                                   hb.b.oc, g.h * g.w, cfg.bn_momentum, buffers_ + hb.rm_off, buffers_ + hb.rv_off,
                                   buffers_ + hb.nt_off, stream_);
             }
-    // update
-    h_flags_[2] = 1;
-    h_flags_[3] = connected ? 1 : 0;
-    if (cfg.optimizer == SY_OPT_ADAMW) {
-        adam_steps_[0]++;
-        if (connected) adam_steps_[1]++;
+    // update: flags [2..4] gate the optimizer groups (class branches, cv2, one2one_cv2), [5..7] hold
+    // their AdamW step counts (TrainingParameter steps only when it received a gradient)
+    const int has[3] = {1, connected & 1, (connected >> 1) & 1};
+    for (int gi = 0; gi < 3; gi++) {
+        h_flags_[2 + gi] = has[gi];
+        if (cfg.optimizer == SY_OPT_ADAMW && has[gi]) adam_steps_[gi]++;
+        h_flags_[5 + gi] = adam_steps_[gi];
     }
-    h_flags_[4] = adam_steps_[0];
-    h_flags_[5] = adam_steps_[1];
     h_flags_[1] = 0;
-    SY_CUDA(cudaMemcpyAsync(d_flags_ + 1, h_flags_ + 1, sizeof(int) * 5, cudaMemcpyHostToDevice, stream_));
-    optimizer_step(cfg.optimizer, params_, vel_, vel2_, grads_, d_segs_, nsegs_, d_flags_ + 2, d_flags_ + 4, cfg.lr,
+    SY_CUDA(cudaMemcpyAsync(d_flags_ + 1, h_flags_ + 1, sizeof(int) * 7, cudaMemcpyHostToDevice, stream_));
+    optimizer_step(cfg.optimizer, params_, vel_, vel2_, grads_, d_segs_, nsegs_, d_flags_ + 2, d_flags_ + 5, cfg.lr,
                    cfg.momentum, cfg.weight_decay, cfg.beta1, cfg.beta2, cfg.adam_eps, 1.0f / (float)global_images,
                    d_flags_ + 1, stream_);
     refresh_head_weights();
@@ -1058,29 +1134,20 @@ int Session::evaluate(const uint8_t* rgb, bool rgb_on_device, const float* const
                       const int32_t* counts, int images, sy_step_stats* out) {
     prepare_inputs(rgb, rgb_on_device, features, boxes, counts, images);
     forward_head(images, false);
-    LevelIO lv[3];
-    for (int l = 0; l < 3; l++) {
-        HeadBlock& bb = branches_[l].blocks.back();
-        HeadBlock& cb = branches_[3 + l].blocks.back();
-        lv[l] = LevelIO{bb.y.base, cb.y.base, bb.g.base, cb.g.base, bb.y.pitch, cb.y.pitch, levels_[l],
-                        (float)(8 << l)};
-    }
-    LossOut lo{d_loss_, d_pos_, d_conn_, nullptr, nullptr};
-    detection_loss(lv, 3, images, cfg.num_classes, cfg.reg_max, d_truth_, d_box_off_, std::max(1, cfg.max_boxes), 10,
-                   10, 1.0f, 0, loss_ws_, lo, stream_);
-    SY_CUDA(cudaMemcpyAsync(h_loss_, d_loss_, sizeof(float) * 4 * images, cudaMemcpyDeviceToHost, stream_));
-    SY_CUDA(cudaMemcpyAsync(h_pos_, d_pos_, sizeof(int) * images, cudaMemcpyDeviceToHost, stream_));
+    // EvaluateLoss passes epoch 0 to DetectionHead.Loss (YoloTrainer.cs:243)
+    launch_losses(images, 0, 0);
+    SY_CUDA(cudaMemcpyAsync(h_loss_, d_loss_, sizeof(float) * 4 * 2 * B_, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaMemcpyAsync(h_pos_, d_pos_, sizeof(int) * 2 * B_, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaMemcpyAsync(h_conn_, d_conn_, sizeof(int) * 2 * B_, cudaMemcpyDeviceToHost, stream_));
     SY_CUDA(cudaMemcpyAsync(h_flags_, d_flags_, sizeof(int) * 16, cudaMemcpyDeviceToHost, stream_));
     SY_CUDA(cudaStreamSynchronize(stream_));
     if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "device wait limit exceeded (code " + std::to_string(h_flags_[0]) + ")");
     double* hs = reinterpret_cast<double*>(h_abs_);   // pinned scratch (>= 8 doubles)
-    hs[0] = hs[1] = hs[2] = hs[3] = 0.0;
-    for (int b = 0; b < images; b++) {
-        hs[0] += h_loss_[4 * b];
-        hs[1] += h_loss_[4 * b + 1];
-        hs[2] += h_loss_[4 * b + 2];
-        hs[3] += h_pos_[b];
-    }
+    long positives = 0;
+    int connected = 0;
+    bool finite = true;
+    combine_losses(images, 0, &hs[0], &hs[1], &hs[2], &positives, &connected, &finite);
+    hs[3] = (double)positives;
     hs[4] = images;
     if (comm_) {
         SY_CUDA(cudaMemcpyAsync(d_abs_, hs, sizeof(double) * 5, cudaMemcpyHostToDevice, stream_));

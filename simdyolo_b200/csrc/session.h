@@ -46,6 +46,8 @@ struct HeadBlock {
 struct Branch {
     int level;
     bool box;
+    int set = 0;                // 0 one-to-many (cv2 / cv3), 1 one-to-one (one2one_cv2 / one2one_cv3)
+    int group = 0;              // optimizer group: 0 class branches, 1 cv2, 2 one2one_cv2
     std::vector<HeadBlock> blocks;
 };
 
@@ -84,6 +86,7 @@ public:
     // YoloTrainer.EvaluateLoss: BatchNorm with running statistics, loss without gradients, no update.
     int evaluate(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
                  const int32_t* counts, int images, sy_step_stats* out);
+    int set_epoch(int epoch);
     int set_tensor(int index, const float* host, long count);
     int get_tensor(int index, float* host, long count) const;
     int set_opt_state(int index, int moment, const float* host, long count);
@@ -113,6 +116,12 @@ private:
     void prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
                         const int32_t* counts, int images);
     void forward_head(int batch, bool training = true);
+    // DetectionHead.Loss: one loss per branch set, gradients scaled by the set's weight
+    void launch_losses(int images, int backward, int epoch);
+    void loss_weights(int epoch, float w[2]) const;
+    // per-image weighted loss parts of the launched losses (after the stream synchronized)
+    void combine_losses(int images, int epoch, double* box, double* cls, double* dfl, long* positives,
+                        int* connected, bool* finite) const;
     void backward_head(int batch);
     void refresh_head_weights();
     View alloc_view(int channels, const Grid& g);
@@ -175,7 +184,10 @@ private:
     double* h_abs_ = nullptr;
     ParamSegment* d_segs_ = nullptr;
     int nsegs_ = 0;
-    int adam_steps_[2] = {0, 0};
+    int adam_steps_[3] = {0, 0, 0};   // AdamW steps per optimizer group
+    int n_sets_ = 1;                  // 2 with the one-to-one branches
+    bool progressive_ = false;        // end-to-end with reg_max 1 (TrainingHeadSchema.Progressive)
+    int epoch_ = 0;
     int last_batch_ = 0;
     // 3xTF32 operand split scratch: activations (4 buffers) and weights (2 buffers)
     bool x3_ = false;

@@ -68,7 +68,8 @@ def head_params(session: Session, seed: int, image_size: int = 640) -> tuple[np.
             else:  # final conv bias
                 level = int(name.split(".")[1])
                 stride = 8 << level
-                v = np.full(n, 1.0) if name.startswith("cv2") else np.full(n, np.log(5.0 / nc / (640.0 / stride) ** 2))
+                box = "cv2" in name.split(".")[0]
+                v = np.full(n, 1.0) if box else np.full(n, np.log(5.0 / nc / (640.0 / stride) ** 2))
             params.append(v.astype(np.float32))
         else:
             v = np.ones(n) if name.endswith("running_var") else np.zeros(n)

@@ -16,7 +16,7 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def head_desc(cfg: sy.Config) -> O.HeadDesc:
+def head_desc(cfg: sy.Config, epoch: int = 0) -> O.HeadDesc:
     d = O.HeadDesc()
     d.levels = 3
     d.nc = cfg.num_classes
@@ -37,6 +37,9 @@ def head_desc(cfg: sy.Config) -> O.HeadDesc:
             d.cls_blocks[l][i] = O.Block(b.ic, b.oc, b.k, b.groups, b.has_bn, b.has_bias)
     d.bn_eps = cfg.bn_eps
     d.bn_momentum = cfg.bn_momentum
+    d.end_to_end = cfg.end_to_end
+    d.epoch = epoch
+    d.schedule_epochs = cfg.schedule_epochs
     return d
 
 
@@ -45,18 +48,18 @@ def backbone_desc(cfg: sy.Config) -> O.BackboneDesc:
                           1 if cfg.backbone == sy.SY_BACKBONE_YOLO11 else 0)
 
 
-def oracle_head_step(cfg: sy.Config, tensors, params, buffers, velocity, features, truth):
+def oracle_head_step(cfg: sy.Config, tensors, params, buffers, velocity, features, truth, epoch: int = 0):
     """Head forward / loss / backward per image, gradients summed in image order, then
     TrainingParameter.Update for every tensor.  Returns (losses[B] dicts, grad, params, buffers,
-    velocity) with arrays updated copies."""
+    velocity, connected) with arrays updated copies; connected: bit 0 cv2, bit 1 one2one_cv2."""
     L = O.lib()
-    d = head_desc(cfg)
+    d = head_desc(cfg, epoch)
     params = params.astype(np.float32).copy()
     buffers = buffers.astype(np.float32).copy()
     velocity = velocity.astype(np.float32).copy()
     grad = np.zeros_like(params)
     losses = []
-    connected_any = False
+    connected_any = 0
     B = features[0].shape[0]
     for b in range(B):
         feats = [np.ascontiguousarray(f[b], np.float32) for f in features]
@@ -69,16 +72,16 @@ def oracle_head_step(cfg: sy.Config, tensors, params, buffers, velocity, feature
                               conn.ctypes.data_as(C.POINTER(C.c_int32)))
         assert rc == 0
         losses.append(dict(box=out.box, cls=out.cls, dfl=out.dfl, positives=out.positives))
-        connected_any |= bool(conn[0])
+        connected_any |= int(conn[0])
     summed = grad.copy()
     off = 0
     for t in tensors:
         if t["kind"] != 0:
             continue
         n = t["numel"]
-        box = t["name"].startswith("cv2")
+        group = sy.tensor_group(t["name"])
         decay = t["name"].endswith("conv.weight") or (t["name"].endswith(".weight") and len(t["shape"]) == 4)
-        has = connected_any if box else True
+        has = bool((connected_any >> (group - 1)) & 1) if group else True
         w, v, g = params[off:off + n].copy(), velocity[off:off + n].copy(), grad[off:off + n].copy()
         rc = O.sgd_update(w, v, g, cfg.lr, cfg.momentum, cfg.weight_decay if decay else 0.0, B, has)
         assert rc == 0
@@ -87,31 +90,31 @@ def oracle_head_step(cfg: sy.Config, tensors, params, buffers, velocity, feature
     return losses, summed, params, buffers, velocity, connected_any
 
 
-def oracle_head_step_adamw(cfg: sy.Config, tensors, params, buffers, m1, m2, steps, features, truth):
+def oracle_head_step_adamw(cfg: sy.Config, tensors, params, buffers, m1, m2, steps, features, truth, epoch=0):
     """Same head step followed by AdamW (torch.optim.AdamW form, lr / betas / eps / weight decay of the
-    config) for every tensor; steps = [always-connected group, box group] counts before this step,
-    the box group stepping only when an image connected it.  Returns (losses, grad, params, buffers,
-    m1, m2, steps) as updated copies."""
+    config) for every tensor; steps = per optimizer group (class branches, cv2, one2one_cv2) counts
+    before this step, a box group stepping only when an image connected it.  Returns (losses, grad,
+    params, buffers, m1, m2, steps) as updated copies."""
     losses, grad, _, buffers_out, _, connected = oracle_head_step(cfg, tensors, params, buffers,
-                                                                  np.zeros_like(params), features, truth)
+                                                                  np.zeros_like(params), features, truth, epoch)
     params, m1, m2 = params.astype(np.float32).copy(), m1.astype(np.float32).copy(), m2.astype(np.float32).copy()
-    steps = list(steps)
+    steps = list(steps) + [0] * (3 - len(steps))
+    has_group = [True, bool(connected & 1), bool(connected & 2)]
     B = features[0].shape[0]
     off = 0
     for t in tensors:
         if t["kind"] != 0:
             continue
         n = t["numel"]
-        box = t["name"].startswith("cv2")
+        group = sy.tensor_group(t["name"])
         decay = t["name"].endswith("conv.weight") or (t["name"].endswith(".weight") and len(t["shape"]) == 4)
-        has = connected if box else True
+        has = has_group[group]
         w, a, b, g = params[off:off + n].copy(), m1[off:off + n].copy(), m2[off:off + n].copy(), grad[off:off + n].copy()
         rc = O.lib().syo_adamw_update(w, a, b, g, n, cfg.lr, cfg.beta1, cfg.beta2, cfg.adam_eps,
-                                      cfg.weight_decay if decay else 0.0, steps[1 if box else 0] + 1, B, int(has))
+                                      cfg.weight_decay if decay else 0.0, steps[group] + 1, B, int(has))
         assert rc == 0
         params[off:off + n], m1[off:off + n], m2[off:off + n] = w, a, b
         off += n
-    steps[0] += 1
-    if connected:
-        steps[1] += 1
+    for gi in range(3):
+        steps[gi] += int(has_group[gi])
     return losses, grad, params, buffers_out, m1, m2, steps
