@@ -228,6 +228,12 @@ SY_API int64_t sy_cuda_launch_count(void);
  * GFLOP (2 x MACs of the interior pixels) and the number of convolution launches. */
 SY_API sy_status sy_cuda_conv_profile(sy_session *session, int32_t enable, double *ms, double *gflop,
                                       int64_t *launches);
+/* Per-launch device ms, GFLOP and shape of the tensor-core conv launches of the most recent profiled
+ * step, in launch order; shapes (optional) receives 6 ints per launch: pass (0 trunk stride 1, 1 trunk
+ * stride 2, 2 head forward, 3 head data gradient), input channels, output channels, taps, output
+ * height, output width.  *count receives the number of launches. */
+SY_API sy_status sy_cuda_conv_profile_launches(const sy_session *session, double *ms, double *gflop,
+                                               int32_t *shapes, int32_t capacity, int32_t *count);
 SY_API sy_status sy_cuda_bench_conv(int32_t device, int32_t kind, int32_t n, int32_t ic, int32_t oc, int32_t h,
                                     int32_t w, int32_t k, int32_t iters, double *ms_per_launch);
 

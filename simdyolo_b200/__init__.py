@@ -148,6 +148,8 @@ def lib():
                                          C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_double)]
         L.sy_cuda_conv_profile.argtypes = [vp, st, C.POINTER(C.c_double), C.POINTER(C.c_double),
                                            C.POINTER(C.c_int64)]
+        L.sy_cuda_conv_profile_launches.argtypes = [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), ip, st,
+                                                    C.POINTER(C.c_int32)]
         _lib = L
     return _lib
 
@@ -160,7 +162,8 @@ EXPORTED = ["sy_cuda_nccl_unique_id", "sy_cuda_create", "sy_cuda_destroy", "sy_c
             "sy_cuda_conv2d_backward_data", "sy_cuda_conv2d_backward_filter", "sy_cuda_matmul", "sy_cuda_sgd_update",
             "sy_cuda_step_device", "sy_cuda_launch_count", "sy_cuda_bench_conv",
             "sy_cuda_conv2d_backward_filter_static", "sy_cuda_conv_profile", "sy_cuda_eval_loss",
-            "sy_cuda_eval_loss_features", "sy_cuda_detection_loss_ex", "sy_cuda_set_epoch"]
+            "sy_cuda_eval_loss_features", "sy_cuda_detection_loss_ex", "sy_cuda_set_epoch",
+            "sy_cuda_conv_profile_launches"]
 
 
 def _check(status: int, session=None):
@@ -533,6 +536,16 @@ class Session:
         ms, gf, n = C.c_double(), C.c_double(), C.c_int64()
         _check(lib().sy_cuda_conv_profile(self._h, int(bool(enable)), C.byref(ms), C.byref(gf), C.byref(n)), self._h)
         return ms.value, gf.value, n.value
+
+    def conv_profile_launches(self):
+        """[(ms, GFLOP, (pass, ic, oc, taps, h, w))] of every tensor-core conv launch of the most recent
+        profiled step; pass 0 trunk stride 1, 1 trunk stride 2, 2 head forward, 3 head data gradient."""
+        n = C.c_int32()
+        _check(lib().sy_cuda_conv_profile_launches(self._h, None, None, None, 0, C.byref(n)), self._h)
+        m = max(1, n.value)
+        ms, gf, sh = (C.c_double * m)(), (C.c_double * m)(), (C.c_int32 * (6 * m))()
+        _check(lib().sy_cuda_conv_profile_launches(self._h, ms, gf, sh, n.value, C.byref(n)), self._h)
+        return [(ms[i], gf[i], tuple(sh[6 * i:6 * i + 6])) for i in range(n.value)]
 
     def last_features(self, level: int, shape) -> np.ndarray:
         out = np.zeros(int(np.prod(shape)), np.float32)

@@ -216,6 +216,18 @@ sy_status sy_cuda_conv_profile(sy_session* session, int32_t enable, double* ms, 
     });
 }
 
+sy_status sy_cuda_conv_profile_launches(const sy_session* session, double* ms, double* gflop, int32_t* shapes,
+                                        int32_t capacity, int32_t* count) {
+    if (!session || capacity < 0) return SY_ERR_INVALID_ARGUMENT;
+    sy_session* s = const_cast<sy_session*>(session);
+    return guarded(s, [&] {
+        int n = 0;
+        const int r = s->impl->conv_profile_launches(ms, gflop, shapes, capacity, &n);
+        if (count) *count = n;
+        return r;
+    });
+}
+
 sy_status sy_cuda_bench_conv(int32_t device, int32_t kind, int32_t n, int32_t ic, int32_t oc, int32_t h, int32_t w,
                              int32_t k, int32_t iters, double* ms_per_launch) {
     return guarded(nullptr, [&] {

@@ -10,6 +10,7 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstring>
 #include <stdexcept>
@@ -534,12 +535,14 @@ void Session::forward_backbone(int batch, const uint8_t* rgb_device) {
                 prof_begin();
                 conv_fwd(i2, op.wk, (long)op.oc * op.k * op.k * round_up(op.ic, 32), op.oc, op.oc, op.k * op.k, 1,
                          op.gin, o2, ep, po);
-                prof_end(2.0 * batch * op.oc * op.ic * op.k * op.k * op.gin.h * op.gin.w);
+                prof_end(2.0 * batch * op.oc * op.ic * op.k * op.k * op.gin.h * op.gin.w,
+                         {0, op.ic, op.oc, op.k * op.k, op.gin.h, op.gin.w});
             } else {
                 prof_begin();
                 conv_strided(op.phase_in, op.phase_plane_rows, (long)batch * op.gout.rows, op.wk,
                              (long)op.oc * 9 * round_up(op.ic, 32), op.oc, op.gout, out, ep, po);
-                prof_end(2.0 * batch * op.oc * op.ic * 9 * op.gout.h * op.gout.w);
+                prof_end(2.0 * batch * op.oc * op.ic * 9 * op.gout.h * op.gout.w,
+                         {1, op.ic, op.oc, 9, op.gout.h, op.gout.w});
             }
         }
     }
@@ -739,7 +742,8 @@ void Session::forward_head(int batch, bool training) {
                 prof_begin();
                 conv_fwd(rows_of(hb.x, batch, g), hb.w_fwd, (long)hb.b.oc * hb.taps * hb.kpad_in, hb.b.oc, hb.b.oc,
                          hb.taps, 1, g, rows_of(hb.y, batch, g), ep, nullptr);
-                prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w);
+                prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w,
+                         {2, hb.b.ic, hb.b.oc, hb.taps, g.h, g.w});
             }
             if (hb.b.has_bn) {
                 if (training)
@@ -796,7 +800,8 @@ void Session::backward_head(int batch) {
                             prof_begin();
                             conv_fwd(rows_of(hb.dy, batch, g), hb.w_dgrad, (long)hb.b.ic * hb.taps * hb.kpad_out,
                                      hb.b.ic, hb.b.ic, hb.taps, -1, g, rows_of(prev.g, batch, g), ep, nullptr);
-                            prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w);
+                            prof_end(2.0 * batch * hb.b.oc * hb.b.ic * hb.taps * g.h * g.w,
+                                     {3, hb.b.oc, hb.b.ic, hb.taps, g.h, g.w});
                         }
                     }
                 }
@@ -1183,23 +1188,46 @@ void Session::prof_begin() {
     SY_CUDA(cudaEventRecord(prof_ev_[2 * prof_n_], stream_));
 }
 
-void Session::prof_end(double flops) {
+void Session::prof_end(double flops, const std::array<int, 6>& shape) {
     if (!prof_) return;
     SY_CUDA(cudaEventRecord(prof_ev_[2 * prof_n_ + 1], stream_));
-    if ((int)prof_flops_.size() <= prof_n_) prof_flops_.resize(prof_n_ + 1);
+    if ((int)prof_flops_.size() <= prof_n_) {
+        prof_flops_.resize(prof_n_ + 1);
+        prof_shape_.resize(prof_n_ + 1);
+    }
     prof_flops_[prof_n_] = flops;
+    prof_shape_[prof_n_] = shape;
     prof_n_++;
 }
 
 void Session::prof_collect() {
+    if (prof_n_ > 0) {
+        prof_last_ms_.assign(prof_n_, 0.0);
+        prof_last_gflop_.assign(prof_n_, 0.0);
+        prof_last_shape_.assign(prof_shape_.begin(), prof_shape_.begin() + prof_n_);
+    }
     for (int k = 0; k < prof_n_; k++) {
         float ms = 0.0f;
         SY_CUDA(cudaEventElapsedTime(&ms, prof_ev_[2 * k], prof_ev_[2 * k + 1]));
         prof_ms_ += ms;
         prof_gflop_ += prof_flops_[k] * 1e-9;
+        prof_last_ms_[k] = ms;
+        prof_last_gflop_[k] = prof_flops_[k] * 1e-9;
     }
     prof_launches_ += prof_n_;
     prof_n_ = 0;
+}
+
+int Session::conv_profile_launches(double* ms, double* gflop, int* shapes, int capacity, int* count) const {
+    const int n = (int)prof_last_ms_.size();
+    if (count) *count = n;
+    for (int k = 0; k < std::min(n, capacity); k++) {
+        if (ms) ms[k] = prof_last_ms_[k];
+        if (gflop) gflop[k] = prof_last_gflop_[k];
+        if (shapes)
+            for (int j = 0; j < 6; j++) shapes[6 * k + j] = prof_last_shape_[k][j];
+    }
+    return SY_OK;
 }
 
 int Session::conv_profile(int enable, double* ms, double* gflop, long* launches) {

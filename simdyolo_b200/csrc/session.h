@@ -1,6 +1,7 @@
 // Training session: owns the device state of one data-parallel rank and runs the fine-tuning step
 // (YoloTrainer.Train inner loop, src/SimdYolo.Training/YoloTrainer.cs:185-199) on the GPU.
 #pragma once
+#include <array>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -97,6 +98,10 @@ public:
     // Optional CUDA-event timing of every tensor-core convolution launch (forward, stride-2 and
     // data-gradient passes) on the session stream; returns the totals since the previous call.
     int conv_profile(int enable, double* ms, double* gflop, long* launches);
+    // Per-launch (ms, GFLOP, shape) of the most recent profiled step, in launch order; shape =
+    // (pass, input channels, output channels, taps, output height, output width) with pass 0 trunk
+    // stride 1, 1 trunk stride 2, 2 head forward, 3 head data gradient.
+    int conv_profile_launches(double* ms, double* gflop, int* shapes, int capacity, int* count) const;
 
     std::vector<TensorEntry> tensors;
     long n_params = 0, n_buffers = 0, n_backbone = 0;
@@ -201,9 +206,11 @@ private:
     std::vector<double> prof_flops_;
     int prof_n_ = 0;
     double prof_ms_ = 0.0, prof_gflop_ = 0.0;
+    std::vector<double> prof_last_ms_, prof_last_gflop_;
+    std::vector<std::array<int, 6>> prof_shape_, prof_last_shape_;
     long prof_launches_ = 0;
     void prof_begin();
-    void prof_end(double flops);
+    void prof_end(double flops, const std::array<int, 6>& shape);
     void prof_collect();
     NcclApi* nccl_ = nullptr;
     void* comm_ = nullptr;
