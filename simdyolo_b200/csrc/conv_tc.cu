@@ -99,6 +99,7 @@ struct FwdParams {
     int b_stages;   // 0: all weights resident
     int b_region_bytes;
     int nacc;       // TMEM accumulator stages
+    int ksplit;     // 2: (T = 1) MMA warp w sums K steps 2w, 2w+1 into its own accumulator, the epilogue adds both
     int acc_cols;   // TMEM columns per sub-tile accumulator
     int alloc_cols;
     float* out;
@@ -121,8 +122,14 @@ struct FwdParams {
     int* err;
 };
 
+// A single thread issues at most one tcgen05.mma about every 73 cycles (measured on B200 for
+// M128 x N<=128 x K8 tf32), far below the tensor core's rate at N = 16-128; two issuing warps, each
+// owning alternate 128-row sub-tiles (or, with one sub-tile per tile, alternate pairs of K steps)
+// in separate accumulators, double the issue rate.
+constexpr int kMmaWarps = 2;
 constexpr int kEpiWarps = 12;     // three per TMEM lane quadrant
-constexpr int kFwdThreads = 64 + 32 * kEpiWarps;   // warp 0 TMA, warp 1 MMA, warps 2-13 epilogue
+constexpr int kEpiWarp0 = 1 + kMmaWarps;
+constexpr int kFwdThreads = 32 * (kEpiWarp0 + kEpiWarps);   // warp 0 TMA, warps 1-2 MMA, 3-14 epilogue
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kTileM = 128;
 
@@ -188,20 +195,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.a_stages; s++) {
             mbar_init(&afull[s], 1);
-            mbar_init(&aempty[s], 1);
+            mbar_init(&aempty[s], kMmaWarps);
         }
         for (int s = 0; s < nb; s++) {
             mbar_init(&bfull[s], 1);
-            mbar_init(&bempty[s], 1);
+            mbar_init(&bempty[s], kMmaWarps);
         }
         for (int a = 0; a < p.nacc; a++) {
-            mbar_init(&tfull[a], 1);
+            mbar_init(&tfull[a], kMmaWarps);
             mbar_init(&tempty[a], kEpiThreads);
         }
         fence_barrier_init();
     }
-    if (warp >= 2)
-        for (int i = threadIdx.x - 64; i < p.n; i += kEpiThreads) {
+    if (warp >= kEpiWarp0)
+        for (int i = threadIdx.x - 32 * kEpiWarp0; i < p.n; i += kEpiThreads) {
             bias_s[i] = (p.bias && i < p.n_valid) ? p.bias[p.n0 + i] : 0.0f;
             gam_s[i] = (p.bn.grad_part && i < p.n_valid) ? p.bn.gamma[p.n0 + i] : 0.0f;
             bet_s[i] = (p.bn.grad_part && i < p.n_valid) ? p.bn.beta[p.n0 + i] : 0.0f;
@@ -257,7 +264,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 }
             }
         }
-    } else if (warp == 1) {
+    } else if (warp <= kMmaWarps) {
+        // MMA warp w issues the MMAs of sub-tiles w, w + kMmaWarps, ... and commits every stage
+        // release and accumulator hand-off (those barriers count kMmaWarps arrivals)
+        const int w = warp - 1;
         if (lane == 0) {
             const uint32_t idesc = idesc_tf32(p.n, 0, 0);
             bool ok = true;
@@ -274,11 +284,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             const uint32_t a_stage16 = (uint32_t)p.a_stage_bytes >> 4, b_blk16 = (uint32_t)b_bytes >> 4;
             const int T = p.T;
             int ia = 0, ib = 0, local = 0;
+            const int slots = T * p.ksplit;   // accumulators per stage
             for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, local++) {
                 const int acc = local % p.nacc;
                 if (!(ok = mbar_wait(&tempty[acc], ((local / p.nacc) & 1) ^ 1, p.err, 2))) break;
                 tc_fence_after();
-                const uint32_t d = tmem_base + acc * T * p.acc_cols;
+                const uint32_t d = tmem_base + acc * slots * p.acc_cols;
                 const int mt = min(T, p.sub_tiles - tile * T);
                 for (int c = 0; ok && c < p.kchunks; c++) {
                     int j = 0;
@@ -301,13 +312,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                             }
                             const uint64_t a_t = a_st + (uint64_t)(tap_s[9 + j] * 8);
                             const uint32_t first = (c == 0 && j == 0) ? 0u : 1u;
-                            for (int i = 0; i < mt; i++) {
-                                const uint64_t a_i = a_t + (uint64_t)(i * 1024);
-                                const uint32_t d_i = d + i * p.acc_cols;
-                                mma_tf32(d_i, a_i, b_d, idesc, first);
-                                mma_tf32(d_i, a_i + 2, b_d + 2, idesc, 1u);
-                                mma_tf32(d_i, a_i + 4, b_d + 4, idesc, 1u);
-                                mma_tf32(d_i, a_i + 6, b_d + 6, idesc, 1u);
+                            if (p.ksplit == 2) {
+                                // one sub-tile: this warp's K steps 2w, 2w+1 into accumulator w
+                                const uint32_t d_w = d + w * p.acc_cols;
+                                mma_tf32(d_w, a_t + 4 * w, b_d + 4 * w, idesc, first);
+                                mma_tf32(d_w, a_t + 4 * w + 2, b_d + 4 * w + 2, idesc, 1u);
+                            } else {
+                                for (int i = w; i < mt; i += kMmaWarps) {
+                                    const uint64_t a_i = a_t + (uint64_t)(i * 1024);
+                                    const uint32_t d_i = d + i * p.acc_cols;
+                                    mma_tf32(d_i, a_i, b_d, idesc, first);
+                                    mma_tf32(d_i, a_i + 2, b_d + 2, idesc, 1u);
+                                    mma_tf32(d_i, a_i + 4, b_d + 4, idesc, 1u);
+                                    mma_tf32(d_i, a_i + 6, b_d + 6, idesc, 1u);
+                                }
                             }
                             if (!resident) {
                                 mma_commit(&bempty[sb]);
@@ -326,7 +344,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         // Global loads of an item (residual, BatchNorm input and coefficients) are issued before
         // its TMEM load so that their latencies overlap.
         const int q = warp & 3;
-        const int part = (warp - 2) >> 2;
+        const int part = (warp - kEpiWarp0) >> 2;
         const int nchunks = (p.n + 15) >> 4;
         const bool bn_bwd = p.bn.grad_part != nullptr;
         int local = 0;
@@ -417,7 +435,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     }
                 }
                 float v[16];
-                tmem_ld16(tmem_base + (acc * p.T + i) * p.acc_cols + ((uint32_t)(q * 32) << 16) + j, v);
+                if (p.ksplit == 2) {
+                    float v1[16];
+                    const uint32_t t0 = tmem_base + acc * 2 * p.acc_cols + ((uint32_t)(q * 32) << 16) + j;
+                    tmem_ld16(t0, v);
+                    tmem_ld16(t0 + p.acc_cols, v1);
+#pragma unroll
+                    for (int u = 0; u < 16; u++) v[u] += v1[u];
+                } else {
+                    tmem_ld16(tmem_base + (acc * p.T + i) * p.acc_cols + ((uint32_t)(q * 32) << 16) + j, v);
+                }
                 // parity-split copy: padded pixel (py, px) -> plane (py&1, px&1), cell (py>>1, px>>1)
                 float* prow = nullptr;
                 if (p.phase && inside) {
@@ -634,8 +661,9 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
             p.b_region_bytes = p.b_stages * b_bytes;
         }
         p.acc_cols = acc_cols;
-        p.nacc = std::max(2, std::min(8, 512 / (T * acc_cols)));
-        p.alloc_cols = pow2_at_least(p.nacc * T * acc_cols);
+        p.ksplit = (T == 1 && 4 * acc_cols <= 512) ? 2 : 1;
+        p.nacc = std::max(2, std::min(8, 512 / (T * p.ksplit * acc_cols)));
+        p.alloc_cols = pow2_at_least(p.nacc * T * p.ksplit * acc_cols);
         p.out = out.base ? out.base + n0 : nullptr;   // null: only the parity copy is written
         p.out_pitch = out.pitch;
         p.bias = ep.bias;
@@ -697,6 +725,7 @@ struct WgradParams {
     long rows;               // pixel rows (K)
     long rows_per_split;     // multiple of 32
     int stages;
+    int acc_stride;          // TMEM columns between the MMA warps' accumulators (power of two >= n)
     int alloc_cols;
     int oob_channel;         // channel coordinate that lies outside the input view (zero fill)
     float* ws;               // [split][m_tiles * 128][n]
@@ -704,7 +733,10 @@ struct WgradParams {
     int* err;
 };
 
-constexpr int kWgradThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+// warp 0 TMA, warps 1-2 MMA (warp 1 + w issues the K steps k with k % 2 == w of every stage into its
+// own accumulator, for the issue rate; the epilogue adds the two), warps 3-6 epilogue
+constexpr int kWgradMmaWarps = 2;
+constexpr int kWgradThreads = 32 * (1 + kWgradMmaWarps + 4);
 constexpr int kWgradBK = 32;                    // pixel rows per stage
 constexpr int kWgradBlockBytes = kWgradBK * 128;  // one 32-channel x 32-row box
 
@@ -730,9 +762,9 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], kWgradMmaWarps);
         }
-        mbar_init(&tfull[0], 1);
+        mbar_init(&tfull[0], kWgradMmaWarps);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -775,9 +807,11 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
                     tma_load_2d(sa + a_bytes + j * kWgradBlockBytes, &tmG, &full[s], j * 32, r0);
             }
         }
-    } else if (warp == 1) {
+    } else if (warp <= kWgradMmaWarps) {
+        const int w = warp - 1;
         if (lane == 0) {
             const uint32_t idesc = idesc_tf32(p.n, 1, 1);
+            const uint32_t d = tmem_base + w * p.acc_stride;
             for (int kb = 0; kb < kblocks; kb++) {
                 const int s = kb % p.stages;
                 const uint32_t ph = (kb / p.stages) & 1;
@@ -786,11 +820,11 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
                 const uint32_t a_addr = smem_u32(smem + s * stage_bytes);
                 const uint32_t b_addr = a_addr + a_bytes;
 #pragma unroll
-                for (int k = 0; k < kWgradBK / 8; k++) {
+                for (int k = w; k < kWgradBK / 8; k += kWgradMmaWarps) {
                     // 8 K rows = two 4-row swizzle groups of 512 B
                     uint64_t ad = smem_desc(a_addr + k * 1024, kWgradBlockBytes, 512, kLayoutSw128Base32);
                     uint64_t bd = smem_desc(b_addr + k * 1024, kWgradBlockBytes, 512, kLayoutSw128Base32);
-                    mma_tf32(tmem_base, ad, bd, idesc, (kb | k) != 0);
+                    mma_tf32(d, ad, bd, idesc, (kb != 0 || k >= kWgradMmaWarps) ? 1u : 0u);
                 }
                 mma_commit(&empty[s]);
             }
@@ -805,8 +839,11 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
         } else if (mbar_wait(&tfull[0], 0, p.err, 13)) {
             tc_fence_after();
             for (int j = 0; j < p.n; j += 16) {
-                float v[16];
+                float v[16], v1[16];
                 tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + j, v);
+                tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + p.acc_stride + j, v1);
+#pragma unroll
+                for (int i = 0; i < 16; i++) v[i] += v1[i];
                 float4* d4 = reinterpret_cast<float4*>(dst + j);
 #pragma unroll
                 for (int i = 0; i < 4; i++) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
@@ -879,7 +916,9 @@ void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, fl
     p.oob_channel = p.kchunks * 32;
     const int stage_bytes = (4 + p.nblocks) * kWgradBlockBytes;
     p.stages = std::min(8, (int)((220 * 1024) / stage_bytes));
-    p.alloc_cols = pow2_at_least(p.n);
+    p.acc_stride = pow2_at_least(p.n);
+    p.alloc_cols = kWgradMmaWarps * p.acc_stride;
+    if (p.alloc_cols > 512) throw std::runtime_error("conv_tc_wgrad: TMEM columns");
     p.ws = ws;
     p.err = err;
     CUtensorMap tx = make_map_2d(x.base, x.channels, x.rows, x.pitch, 32, kWgradBK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
