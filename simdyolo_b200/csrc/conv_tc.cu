@@ -122,15 +122,22 @@ struct FwdParams {
     int* err;
 };
 
-// A single thread issues at most one tcgen05.mma about every 73 cycles (measured on B200 for
-// M128 x N<=128 x K8 tf32), far below the tensor core's rate at N = 16-128; two issuing warps, each
-// owning alternate 128-row sub-tiles (or, with one sub-tile per tile, alternate pairs of K steps)
-// in separate accumulators, double the issue rate.
+// MMA issue, as measured on B200 for M128 x N64 x K8 tf32 MMAs: a warp that issues from warp-uniform
+// code (elect.sync) sustains one MMA per ~53 cycles, one lane alone in a diverged branch one per ~75;
+// two such warps (alternate 128-row sub-tiles, or with one sub-tile per tile alternate pairs of K
+// steps, in separate accumulators) reach the tensor core's rate at N = 64 (~48 cycles per MMA).  Any
+// shared-memory access by an issuing warp, an mbarrier wait included, waits behind that warp's queued
+// MMA operand reads (~1200 cycles with a few dozen MMAs in flight), so the issuing warps touch no
+// shared memory: a separate waiter warp performs every mbarrier wait of the MMA side and releases the
+// issuing warps through a named barrier, which costs them a few cycles.
 constexpr int kMmaWarps = 2;
+constexpr int kWaitWarp = 1;
+constexpr int kMmaWarp0 = 2;
 constexpr int kEpiWarps = 12;     // three per TMEM lane quadrant
-constexpr int kEpiWarp0 = 1 + kMmaWarps;
-constexpr int kFwdThreads = 32 * (kEpiWarp0 + kEpiWarps);   // warp 0 TMA, warps 1-2 MMA, 3-14 epilogue
+constexpr int kEpiWarp0 = kMmaWarp0 + kMmaWarps;
+constexpr int kFwdThreads = 32 * (kEpiWarp0 + kEpiWarps);   // warp 0 TMA, 1 waiter, 2-3 MMA, 4-15 epilogue
 constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kMmaBar = 1, kMmaBarThreads = 32 * (1 + kMmaWarps);   // waiter + MMA warps
 constexpr int kTileM = 128;
 
 __device__ __forceinline__ float silu_fast(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
@@ -167,7 +174,7 @@ __device__ __forceinline__ float warp_sum16(const float (&v)[16], int lane) {
 
 __global__ void __launch_bounds__(kFwdThreads, 1)
     conv_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                       const FwdParams p) {
+                       const __grid_constant__ FwdParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int b_bytes = p.n * 128;          // one (tap, chunk) weight block; multiple of 2048
@@ -264,80 +271,94 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 }
             }
         }
-    } else if (warp <= kMmaWarps) {
-        // MMA warp w issues the MMAs of sub-tiles w, w + kMmaWarps, ... and commits every stage
-        // release and accumulator hand-off (those barriers count kMmaWarps arrivals)
-        const int w = warp - 1;
-        if (lane == 0) {
-            const uint32_t idesc = idesc_tf32(p.n, 0, 0);
-            bool ok = true;
-            if (resident) {
-                ok = mbar_wait(&bfull[0], 0, p.err, 3);
-                tc_fence_after();
-            }
-            // Descriptors are linear in the start-address field (address >> 4, 14 bits, never
-            // carried out of within shared memory), so every operand descriptor below is a base
-            // descriptor plus a byte offset >> 4: 128-byte rows add 8, a 32-byte K step adds 2,
-            // a 128-row sub-tile adds 1024.
-            const uint64_t a_desc0 = smem_desc(smem_u32(a_ring), 16, 1024, kLayoutSw128);
-            const uint64_t b_desc0 = smem_desc(smem_u32(b_region), 16, 1024, kLayoutSw128);
-            const uint32_t a_stage16 = (uint32_t)p.a_stage_bytes >> 4, b_blk16 = (uint32_t)b_bytes >> 4;
-            const int T = p.T;
-            int ia = 0, ib = 0, local = 0;
-            const int slots = T * p.ksplit;   // accumulators per stage
-            for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, local++) {
-                const int acc = local % p.nacc;
-                if (!(ok = mbar_wait(&tempty[acc], ((local / p.nacc) & 1) ^ 1, p.err, 2))) break;
-                tc_fence_after();
-                const uint32_t d = tmem_base + acc * slots * p.acc_cols;
-                const int mt = min(T, p.sub_tiles - tile * T);
-                for (int c = 0; ok && c < p.kchunks; c++) {
-                    int j = 0;
-                    for (int g = 0; ok && g < p.ngroups; g++) {
-                        const int sa = ia % p.a_stages;
-                        if (!(ok = mbar_wait(&afull[sa], (ia / p.a_stages) & 1, p.err, 3))) break;
-                        tc_fence_after();
-                        const uint64_t a_st = a_desc0 + (uint64_t)(sa * a_stage16);
-                        const int jend = j + p.g_ntaps[g];
-                        for (; j < jend; j++) {
-                            uint64_t b_d;
-                            int sb = 0;
-                            if (resident) {
-                                b_d = b_desc0 + (uint64_t)((tap_s[j] * p.kchunks + c) * b_blk16);
-                            } else {
-                                sb = ib % p.b_stages;
-                                if (!(ok = mbar_wait(&bfull[sb], (ib / p.b_stages) & 1, p.err, 3))) break;
-                                tc_fence_after();
-                                b_d = b_desc0 + (uint64_t)(sb * b_blk16);
-                            }
-                            const uint64_t a_t = a_st + (uint64_t)(tap_s[9 + j] * 8);
-                            const uint32_t first = (c == 0 && j == 0) ? 0u : 1u;
-                            if (p.ksplit == 2) {
-                                // one sub-tile: this warp's K steps 2w, 2w+1 into accumulator w
-                                const uint32_t d_w = d + w * p.acc_cols;
-                                mma_tf32(d_w, a_t + 4 * w, b_d + 4 * w, idesc, first);
-                                mma_tf32(d_w, a_t + 4 * w + 2, b_d + 4 * w + 2, idesc, 1u);
-                            } else {
-                                for (int i = w; i < mt; i += kMmaWarps) {
-                                    const uint64_t a_i = a_t + (uint64_t)(i * 1024);
-                                    const uint32_t d_i = d + i * p.acc_cols;
-                                    mma_tf32(d_i, a_i, b_d, idesc, first);
-                                    mma_tf32(d_i, a_i + 2, b_d + 2, idesc, 1u);
-                                    mma_tf32(d_i, a_i + 4, b_d + 4, idesc, 1u);
-                                    mma_tf32(d_i, a_i + 6, b_d + 6, idesc, 1u);
-                                }
-                            }
-                            if (!resident) {
-                                mma_commit(&bempty[sb]);
-                                ib++;
+    } else if (warp == kWaitWarp) {
+        // every wait of the MMA side, in the MMA warps' order; each ends with a named-barrier hand-off.
+        // After a timed-out wait the remaining waits are skipped (the hand-offs continue, so the MMA
+        // warps, the epilogue and the producer all still finish; the error flag reports the failure).
+        bool live = true;
+        auto event = [&](uint64_t* bar, uint32_t parity, int code) {
+            if (live) live = mbar_wait(bar, parity, p.err, code);
+            named_bar_sync(kMmaBar, kMmaBarThreads);
+        };
+        if (resident) event(&bfull[0], 0, 3);
+        int ia = 0, ib = 0, local = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
+            event(&tempty[local % p.nacc], ((local / p.nacc) & 1) ^ 1, 2);
+            for (int c = 0; c < p.kchunks; c++)
+                for (int g = 0; g < p.ngroups; g++) {
+                    event(&afull[ia % p.a_stages], (ia / p.a_stages) & 1, 3);
+                    ia++;
+                    if (!resident)
+                        for (int e = 0; e < p.g_ntaps[g]; e++, ib++)
+                            event(&bfull[ib % p.b_stages], (ib / p.b_stages) & 1, 3);
+                }
+        }
+    } else if (warp < kEpiWarp0) {
+        // MMA warp w (whole warp, elect.sync issues) takes sub-tiles w, w + kMmaWarps, ... and commits
+        // every stage release and accumulator hand-off (those barriers count kMmaWarps arrivals)
+        const int w = warp - kMmaWarp0;
+        const uint32_t idesc = idesc_tf32(p.n, 0, 0);
+        if (resident) named_bar_sync(kMmaBar, kMmaBarThreads);
+        // Descriptors are linear in the start-address field (address >> 4, 14 bits, never
+        // carried out of within shared memory), so every operand descriptor below is a base
+        // descriptor plus a byte offset >> 4: 128-byte rows add 8, a 32-byte K step adds 2,
+        // a 128-row sub-tile adds 1024.
+        const uint64_t a_desc0 = smem_desc(smem_u32(a_ring), 16, 1024, kLayoutSw128);
+        const uint64_t b_desc0 = smem_desc(smem_u32(b_region), 16, 1024, kLayoutSw128);
+        const uint32_t a_stage16 = (uint32_t)p.a_stage_bytes >> 4, b_blk16 = (uint32_t)b_bytes >> 4;
+        const int T = p.T;
+        int ia = 0, ib = 0, local = 0;
+        const int slots = T * p.ksplit;   // accumulators per stage
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
+            const int acc = local % p.nacc;
+            named_bar_sync(kMmaBar, kMmaBarThreads);   // accumulator stage drained by the epilogue
+            tc_fence_after();
+            const uint32_t d = tmem_base + acc * slots * p.acc_cols;
+            const int mt = min(T, p.sub_tiles - tile * T);
+            for (int c = 0; c < p.kchunks; c++) {
+                int j = 0;
+                for (int g = 0; g < p.ngroups; g++) {
+                    const int sa = ia % p.a_stages;
+                    named_bar_sync(kMmaBar, kMmaBarThreads);   // A region loaded
+                    const uint64_t a_st = a_desc0 + (uint64_t)(sa * a_stage16);
+                    const int jend = j + p.g_ntaps[g];
+                    for (; j < jend; j++) {
+                        uint64_t b_d;
+                        int sb = 0;
+                        if (resident) {
+                            b_d = b_desc0 + (uint64_t)((p.tap_t[j] * p.kchunks + c) * b_blk16);
+                        } else {
+                            sb = ib % p.b_stages;
+                            named_bar_sync(kMmaBar, kMmaBarThreads);   // weight block loaded
+                            b_d = b_desc0 + (uint64_t)(sb * b_blk16);
+                        }
+                        const uint64_t a_t = a_st + (uint64_t)(p.tap_off[j] * 8);
+                        const uint32_t first = (c == 0 && j == 0) ? 0u : 1u;
+                        if (p.ksplit == 2) {
+                            // one sub-tile: this warp's K steps 2w, 2w+1 into accumulator w
+                            const uint32_t d_w = d + w * p.acc_cols;
+                            mma_tf32_elect(d_w, a_t + 4 * w, b_d + 4 * w, idesc, first);
+                            mma_tf32_elect(d_w, a_t + 4 * w + 2, b_d + 4 * w + 2, idesc, 1u);
+                        } else {
+                            for (int i = w; i < mt; i += kMmaWarps) {
+                                const uint64_t a_i = a_t + (uint64_t)(i * 1024);
+                                const uint32_t d_i = d + i * p.acc_cols;
+                                mma_tf32_elect(d_i, a_i, b_d, idesc, first);
+                                mma_tf32_elect(d_i, a_i + 2, b_d + 2, idesc, 1u);
+                                mma_tf32_elect(d_i, a_i + 4, b_d + 4, idesc, 1u);
+                                mma_tf32_elect(d_i, a_i + 6, b_d + 6, idesc, 1u);
                             }
                         }
-                        mma_commit(&aempty[sa]);
-                        ia++;
+                        if (!resident) {
+                            mma_commit_elect(&bempty[sb]);
+                            ib++;
+                        }
                     }
+                    mma_commit_elect(&aempty[sa]);
+                    ia++;
                 }
-                mma_commit(&tfull[acc]);
             }
+            mma_commit_elect(&tfull[acc]);
         }
     } else {
         // three warps per TMEM lane quadrant; they take every third (sub-tile, 16-column chunk) item.
@@ -733,16 +754,20 @@ struct WgradParams {
     int* err;
 };
 
-// warp 0 TMA, warps 1-2 MMA (warp 1 + w issues the K steps k with k % 2 == w of every stage into its
-// own accumulator, for the issue rate; the epilogue adds the two), warps 3-6 epilogue
+// warp 0 TMA, warp 1 waiter (every mbarrier wait of the MMA side, handed on through a named barrier:
+// an MMA-issuing warp that touches shared memory waits behind its own queued MMA operand reads),
+// warps 2-3 MMA (warp 2 + w issues the K steps k with k % 2 == w of every stage into its own
+// accumulator, for the issue rate; the epilogue adds the two), warps 4-7 epilogue
 constexpr int kWgradMmaWarps = 2;
-constexpr int kWgradThreads = 32 * (1 + kWgradMmaWarps + 4);
-constexpr int kWgradBK = 32;                    // pixel rows per stage
-constexpr int kWgradBlockBytes = kWgradBK * 128;  // one 32-channel x 32-row box
+constexpr int kWgradWaitWarp = 1, kWgradMmaWarp0 = 2;
+constexpr int kWgradThreads = 32 * (2 + kWgradMmaWarps + 4);
+constexpr int kWgradBar = 1, kWgradBarThreads = 32 * (1 + kWgradMmaWarps);
+constexpr int kWgradBK = 64;                    // pixel rows per stage
+constexpr int kWgradBlockBytes = kWgradBK * 128;  // one 32-channel x 64-row box
 
 __global__ void __launch_bounds__(kWgradThreads, 1)
     conv_wgrad_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmG,
-                         const WgradParams p) {
+                         const __grid_constant__ WgradParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int a_bytes = 4 * kWgradBlockBytes;
@@ -807,29 +832,34 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
                     tma_load_2d(sa + a_bytes + j * kWgradBlockBytes, &tmG, &full[s], j * 32, r0);
             }
         }
-    } else if (warp <= kWgradMmaWarps) {
-        const int w = warp - 1;
-        if (lane == 0) {
-            const uint32_t idesc = idesc_tf32(p.n, 1, 1);
-            const uint32_t d = tmem_base + w * p.acc_stride;
-            for (int kb = 0; kb < kblocks; kb++) {
-                const int s = kb % p.stages;
-                const uint32_t ph = (kb / p.stages) & 1;
-                if (!mbar_wait(&full[s], ph, p.err, 12)) break;
-                tc_fence_after();
-                const uint32_t a_addr = smem_u32(smem + s * stage_bytes);
-                const uint32_t b_addr = a_addr + a_bytes;
-#pragma unroll
-                for (int k = w; k < kWgradBK / 8; k += kWgradMmaWarps) {
-                    // 8 K rows = two 4-row swizzle groups of 512 B
-                    uint64_t ad = smem_desc(a_addr + k * 1024, kWgradBlockBytes, 512, kLayoutSw128Base32);
-                    uint64_t bd = smem_desc(b_addr + k * 1024, kWgradBlockBytes, 512, kLayoutSw128Base32);
-                    mma_tf32(d, ad, bd, idesc, (kb != 0 || k >= kWgradMmaWarps) ? 1u : 0u);
-                }
-                mma_commit(&empty[s]);
-            }
-            mma_commit(&tfull[0]);
+    } else if (warp == kWgradWaitWarp) {
+        // after a timed-out wait the remaining waits are skipped; the hand-offs continue so that
+        // every warp finishes (the error flag reports the failure)
+        bool live = true;
+        for (int kb = 0; kb < kblocks; kb++) {
+            if (live) live = mbar_wait(&full[kb % p.stages], (kb / p.stages) & 1, p.err, 12);
+            named_bar_sync(kWgradBar, kWgradBarThreads);
         }
+    } else if (warp < kWgradMmaWarp0 + kWgradMmaWarps) {
+        const int w = warp - kWgradMmaWarp0;
+        const uint32_t idesc = idesc_tf32(p.n, 1, 1);
+        const uint32_t d = tmem_base + w * p.acc_stride;
+        const uint32_t stage0 = smem_u32(smem);
+        for (int kb = 0; kb < kblocks; kb++) {
+            const int s = kb % p.stages;
+            named_bar_sync(kWgradBar, kWgradBarThreads);   // stage loaded
+            const uint32_t a_addr = stage0 + s * stage_bytes;
+            const uint32_t b_addr = a_addr + a_bytes;
+#pragma unroll
+            for (int k = w; k < kWgradBK / 8; k += kWgradMmaWarps) {
+                // 8 K rows = two 4-row swizzle groups of 512 B
+                uint64_t ad = smem_desc(a_addr + k * 1024, kWgradBlockBytes, 512, kLayoutSw128Base32);
+                uint64_t bd = smem_desc(b_addr + k * 1024, kWgradBlockBytes, 512, kLayoutSw128Base32);
+                mma_tf32_elect(d, ad, bd, idesc, (kb != 0 || k >= kWgradMmaWarps) ? 1u : 0u);
+            }
+            mma_commit_elect(&empty[s]);
+        }
+        mma_commit_elect(&tfull[0]);
     } else {
         const int q = warp & 3;
         const int row = q * 32 + lane;
