@@ -120,6 +120,8 @@ struct FwdParams {
     int pre_pitch;
     BnEpilogue bn;       // BatchNorm partials (see kernels.h)
     int* err;
+    int sub_per_img;     // 128-row sub-tiles per image (grid.rows / 128)
+    float inv_wp;        // 1 / grid.wp, rounded
 };
 
 // MMA issue, as measured on B200 for M128 x N64 x K8 tf32 MMAs: a warp that issues from warp-uniform
@@ -133,10 +135,12 @@ struct FwdParams {
 constexpr int kMmaWarps = 2;
 constexpr int kWaitWarp = 1;
 constexpr int kMmaWarp0 = 2;
-constexpr int kEpiWarps = 12;     // three per TMEM lane quadrant
+// Epilogue warps: two or three per TMEM lane quadrant (warps 4.. after the TMA, waiter and MMA warps).
+// Two keep the whole block within 170 registers a thread, so the plain and BatchNorm-statistics
+// epilogues run without spills (about 10 % faster on 1x1 layers); the BatchNorm-backward epilogue, with
+// more work per element, runs faster with three despite the 128-register cap.
 constexpr int kEpiWarp0 = kMmaWarp0 + kMmaWarps;
-constexpr int kFwdThreads = 32 * (kEpiWarp0 + kEpiWarps);   // warp 0 TMA, 1 waiter, 2-3 MMA, 4-15 epilogue
-constexpr int kEpiThreads = 32 * kEpiWarps;
+__host__ __device__ constexpr int fwd_threads(int epi_warps) { return 32 * (kEpiWarp0 + epi_warps); }
 constexpr int kMmaBar = 1, kMmaBarThreads = 32 * (1 + kMmaWarps);   // waiter + MMA warps
 constexpr int kTileM = 128;
 
@@ -172,9 +176,11 @@ __device__ __forceinline__ float warp_sum16(const float (&v)[16], int lane) {
     return r + __shfl_xor_sync(0xffffffffu, r, 1);
 }
 
-__global__ void __launch_bounds__(kFwdThreads, 1)
+template <int kEpiWarps>
+__global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
     conv_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ FwdParams p) {
+    constexpr int kEpiThreads = 32 * kEpiWarps;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int b_bytes = p.n * 128;          // one (tap, chunk) weight block; multiple of 2048
@@ -374,14 +380,28 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             if (!mbar_wait(&tfull[acc], (local / p.nacc) & 1, p.err, 4)) break;
             tc_fence_after();
             const int mt = min(p.T, p.sub_tiles - tile * p.T);
-            for (int item = part; item < mt * nchunks; item += kEpiWarps / 4) {
-                const int i = item / nchunks;
-                const int j = (item - i * nchunks) * 16;
+            // items (sub-tile i, 16-column chunk cj) in steps of kEpiWarps / 4, with 32-bit index math
+            // advanced incrementally (a 128-row sub-tile never spans two images)
+            const int sub0 = tile * p.T;
+            const int img0 = sub0 / p.sub_per_img, rem0 = sub0 - img0 * p.sub_per_img;
+            int i = part / nchunks, cj = part - (part / nchunks) * nchunks;
+            for (; i < mt; cj += kEpiWarps / 4, i += cj / nchunks, cj %= nchunks) {
+                const int j = cj * 16;
                 if (j >= p.n_valid) continue;   // warp-uniform
-                const long m = (long)tile * tile_rows + i * kTileM + q * 32 + lane;
-                const long img = m / p.grid.rows;
-                const int r = (int)(m - img * p.grid.rows);
-                const bool inside = !p.mask || p.grid.interior(r);
+                int rem = rem0 + i, img = img0;
+                while (rem >= p.sub_per_img) {
+                    rem -= p.sub_per_img;
+                    img++;
+                }
+                const long m = (long)(sub0 + i) * kTileM + q * 32 + lane;
+                const int r = rem * kTileM + q * 32 + lane;
+                bool inside = true;
+                if (p.mask) {
+                    // r / wp from a float reciprocal: exact for r < 2^22 (the quotient of r + 1/2 lies at
+                    // least 1 / (2 wp) from an integer, the rounding error is below (r + 1/2) 2^-23 / wp)
+                    const int py = __float2int_rd(((float)r + 0.5f) * p.inv_wp), px = r - py * p.grid.wp;
+                    inside = py >= 1 && py <= p.grid.h && px >= 1 && px <= p.grid.w;
+                }
                 const bool full16 = j + 16 <= p.n_valid;
                 const int chb = p.n0 + j;
                 float* orow = p.out ? p.out + m * (long)p.out_pitch : nullptr;
@@ -596,7 +616,8 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
     const long sub_tiles = m_rows / kTileM;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaFuncSetAttribute(conv_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(conv_fwd_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(conv_fwd_tc_kernel<12>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         attr_set = true;
     }
     CUtensorMap ta = make_map_2d(in.base, in.channels, in.rows, in.pitch, 32, kBoxRows);
@@ -702,6 +723,9 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         p.pre = ep.pre ? ep.pre + n0 : nullptr;
         p.pre_pitch = ep.pre_pitch;
         p.err = err;
+        p.sub_per_img = grid.rows / kTileM;
+        p.inv_wp = 1.0f / (float)grid.wp;
+        if (grid.rows % kTileM != 0 || grid.rows >= (1 << 22)) throw std::runtime_error("conv_tc: rows per image");
         if (p.alloc_cols > 512) throw std::runtime_error("conv_tc: TMEM columns");
         CUtensorMap tb = make_map_2d(wk, (long)taps * kpad, n_rows, (long)taps * kpad, 32, n);
         const int nb = resident ? 1 : p.b_stages;
@@ -709,7 +733,10 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
                             (2 * p.a_stages + 2 * nb + 2 * p.nacc) * 8 + 16 + 80 + 3 * n * 4;
         if (smem > 227 * 1024) throw std::runtime_error("conv_tc: shared memory");
         const int grid_x = std::min(p.num_tiles, num_sms());
-        conv_fwd_tc_kernel<<<grid_x, kFwdThreads, smem, stream>>>(ta, tb, p);
+        if (ep.bn.grad_part)
+            conv_fwd_tc_kernel<12><<<grid_x, fwd_threads(12), smem, stream>>>(ta, tb, p);
+        else
+            conv_fwd_tc_kernel<8><<<grid_x, fwd_threads(8), smem, stream>>>(ta, tb, p);
         launch_check("conv_fwd_tc_kernel");
     }
 }
