@@ -241,6 +241,10 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
+// floor(n / d) for 0 <= n < 2^22 from inv = 1.0f / d (rounded): (n + 1/2) / d lies at least 1 / (2d)
+// from an integer, and the float error is below (n + 1/2) 2^-23 / d, so rounding down is exact.
+__device__ __forceinline__ int fast_div(int n, float inv) { return __float2int_rd(((float)n + 0.5f) * inv); }
+
 // Warp-wide forms: the whole (converged) warp executes them and elect.sync picks the lane that issues
 // the MMA / commit (always the same lane for a full warp, so commits track that lane's MMAs).  Issuing
 // from warp-uniform code is much cheaper than from a single diverged lane.

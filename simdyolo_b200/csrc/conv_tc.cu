@@ -915,21 +915,24 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
     }
 }
 
-// dw[(o * ic + c) * taps + t] = sum_s ws[s][(t * kchunks + c / 32) * 32 + c % 32][o]
-// `n` is the workspace row stride (the MMA width, output channels rounded up to 16); `oc` the real
-// output channels, which alone bound the rows of dw that are written.
+// dw[(o * ic + c) * taps + t] = sum_s ws[s][(t * kchunks + c / 32) * 32 + c % 32][o], splits summed in
+// order.  Consecutive threads take consecutive output channels o, so the workspace reads of a warp are
+// contiguous.  `n` is the workspace row stride (the MMA width, output channels rounded up to 16); `oc`
+// the real output channels, which alone bound the rows of dw that are written.
 __global__ void wgrad_reduce_kernel(const float* ws, int splits, long split_stride, int n, int oc, int ic, int taps,
                                     int kchunks, float* dw, int accumulate) {
     const long total = (long)oc * ic * taps;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const int t = (int)(i % taps);
-        const long rest = i / taps;
-        const int c = (int)(rest % ic);
-        const int o = (int)(rest / ic);
+        const int o = (int)(i % oc);
+        const int tc = (int)(i / oc);
+        const int t = tc / ic, c = tc - t * ic;
         const long row = (long)(t * kchunks + c / 32) * 32 + (c % 32);
+        const float* src = ws + row * n + o;
         float s = 0.0f;
-        for (int k = 0; k < splits; k++) s += ws[k * split_stride + row * n + o];
-        dw[i] = accumulate ? dw[i] + s : s;
+#pragma unroll 8
+        for (int k = 0; k < splits; k++) s += src[k * split_stride];
+        const long di = ((long)o * ic + c) * taps + t;
+        dw[di] = accumulate ? dw[di] + s : s;
     }
 }
 

@@ -108,45 +108,46 @@ __device__ __forceinline__ void store_vec(float* p, const Vec<V>& r) {
 }
 
 // MaxPool2d(5, stride 1, padding 2); padded positions never win.
+// SPPF max pool 5x5 / stride 1 / pad 2 (PtModel.cs SPPF): blockIdx.x = image * h + y (one output pixel
+// row), blockIdx.y and the threads over (x, channel vector); 32-bit index math.
 template <int V>
-__global__ void maxpool5_kernel(const float* in, int in_pitch, float* out, int out_pitch, int c, int batch, Grid g) {
+__global__ void maxpool5_kernel(const float* in, int in_pitch, float* out, int out_pitch, int c, int batch, Grid g,
+                                float inv_cv) {
     const int cv = c / V;
-    const long total = (long)batch * g.h * g.w * cv;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const long pix = i / cv;
-        const int ch = (int)(i - pix * cv) * V;
-        const int b = (int)(pix / (g.h * g.w));
-        const int rem = (int)(pix - (long)b * g.h * g.w);
-        const int y = rem / g.w, x = rem - y * g.w;
+    const int b = blockIdx.x / g.h, y = blockIdx.x - b * g.h;
+    const long base = (long)b * g.rows;
+    const int n = g.w * cv;
+    for (int k = blockIdx.y * blockDim.x + threadIdx.x; k < n; k += gridDim.y * blockDim.x) {
+        const int x = fast_div(k, inv_cv), ch = (k - x * cv) * V;
         Vec<V> m;
-        for (int k = 0; k < V; k++) m.v[k] = -INFINITY;
+        for (int q = 0; q < V; q++) m.v[q] = -INFINITY;
         for (int dy = -2; dy <= 2; dy++) {
             const int yy = y + dy;
             if (yy < 0 || yy >= g.h) continue;
             for (int dx = -2; dx <= 2; dx++) {
                 const int xx = x + dx;
                 if (xx < 0 || xx >= g.w) continue;
-                const Vec<V> t = load_vec<V>(in + ((long)b * g.rows + g.row(yy, xx)) * in_pitch + ch);
-                for (int k = 0; k < V; k++) m.v[k] = fmaxf(m.v[k], t.v[k]);
+                const Vec<V> t = load_vec<V>(in + (base + g.row(yy, xx)) * in_pitch + ch);
+                for (int q = 0; q < V; q++) m.v[q] = fmaxf(m.v[q], t.v[q]);
             }
         }
-        store_vec<V>(out + ((long)b * g.rows + g.row(y, x)) * out_pitch + ch, m);
+        store_vec<V>(out + (base + g.row(y, x)) * out_pitch + ch, m);
     }
 }
 
+// Nearest 2x upsample into a (concatenation) slice: blockIdx.x = image * gout.h + y, blockIdx.y and the
+// threads over (x, channel vector).
 template <int V>
 __global__ void upsample2_kernel(const float* in, int in_pitch, Grid gin, float* out, int out_pitch, Grid gout, int c,
-                                 int batch) {
+                                 int batch, float inv_cv) {
     const int cv = c / V;
-    const long total = (long)batch * gout.h * gout.w * cv;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const long pix = i / cv;
-        const int ch = (int)(i - pix * cv) * V;
-        const int b = (int)(pix / (gout.h * gout.w));
-        const int rem = (int)(pix - (long)b * gout.h * gout.w);
-        const int y = rem / gout.w, x = rem - y * gout.w;
-        store_vec<V>(out + ((long)b * gout.rows + gout.row(y, x)) * out_pitch + ch,
-                     load_vec<V>(in + ((long)b * gin.rows + gin.row(y / 2, x / 2)) * in_pitch + ch));
+    const int b = blockIdx.x / gout.h, y = blockIdx.x - b * gout.h;
+    const float* src = in + ((long)b * gin.rows + gin.row(y / 2, 0)) * in_pitch;
+    float* dst = out + ((long)b * gout.rows + gout.row(y, 0)) * out_pitch;
+    const int n = gout.w * cv;
+    for (int k = blockIdx.y * blockDim.x + threadIdx.x; k < n; k += gridDim.y * blockDim.x) {
+        const int x = fast_div(k, inv_cv), ch = (k - x * cv) * V;
+        store_vec<V>(dst + (long)x * out_pitch + ch, load_vec<V>(src + (long)(x / 2) * in_pitch + ch));
     }
 }
 
@@ -281,13 +282,16 @@ void weights_dgrad_layout(const float* oihw, int oc, int ic, int taps, int kpad_
 void maxpool5_padded(const View& in, const View& out, int batch, const Grid& g, cudaStream_t stream) {
     const bool vec = in.channels % 4 == 0 && in.pitch % 4 == 0 && out.pitch % 4 == 0 &&
                      (reinterpret_cast<uintptr_t>(in.base) & 15) == 0 && (reinterpret_cast<uintptr_t>(out.base) & 15) == 0;
-    const long n = (long)batch * g.h * g.w * (vec ? in.channels / 4 : in.channels);
+    const int cv = vec ? in.channels / 4 : in.channels;
+    const int n = g.w * cv;
+    if (n >= (1 << 22)) throw std::runtime_error("maxpool5: map too large");
+    const dim3 grid((unsigned)(batch * g.h), (unsigned)((n + 255) / 256));
     if (vec)
-        maxpool5_kernel<4><<<blocks_for(n), 256, 0, stream>>>(in.base, in.pitch, out.base, out.pitch, in.channels,
-                                                              batch, g);
+        maxpool5_kernel<4><<<grid, 256, 0, stream>>>(in.base, in.pitch, out.base, out.pitch, in.channels, batch, g,
+                                                     1.0f / (float)cv);
     else
-        maxpool5_kernel<1><<<blocks_for(n), 256, 0, stream>>>(in.base, in.pitch, out.base, out.pitch, in.channels,
-                                                              batch, g);
+        maxpool5_kernel<1><<<grid, 256, 0, stream>>>(in.base, in.pitch, out.base, out.pitch, in.channels, batch, g,
+                                                     1.0f / (float)cv);
     launch_check("maxpool5_kernel");
 }
 
@@ -295,13 +299,16 @@ void upsample2_padded(const View& in, const Grid& gin, const View& out, const Gr
                       cudaStream_t stream) {
     const bool vec = in.channels % 4 == 0 && in.pitch % 4 == 0 && out.pitch % 4 == 0 &&
                      (reinterpret_cast<uintptr_t>(in.base) & 15) == 0 && (reinterpret_cast<uintptr_t>(out.base) & 15) == 0;
-    const long n = (long)batch * gout.h * gout.w * (vec ? in.channels / 4 : in.channels);
+    const int cv = vec ? in.channels / 4 : in.channels;
+    const int n = gout.w * cv;
+    if (n >= (1 << 22)) throw std::runtime_error("upsample2: map too large");
+    const dim3 grid((unsigned)(batch * gout.h), (unsigned)((n + 255) / 256));
     if (vec)
-        upsample2_kernel<4><<<blocks_for(n), 256, 0, stream>>>(in.base, in.pitch, gin, out.base, out.pitch, gout,
-                                                               in.channels, batch);
+        upsample2_kernel<4><<<grid, 256, 0, stream>>>(in.base, in.pitch, gin, out.base, out.pitch, gout, in.channels,
+                                                      batch, 1.0f / (float)cv);
     else
-        upsample2_kernel<1><<<blocks_for(n), 256, 0, stream>>>(in.base, in.pitch, gin, out.base, out.pitch, gout,
-                                                               in.channels, batch);
+        upsample2_kernel<1><<<grid, 256, 0, stream>>>(in.base, in.pitch, gin, out.base, out.pitch, gout, in.channels,
+                                                      batch, 1.0f / (float)cv);
     launch_check("upsample2_kernel");
 }
 

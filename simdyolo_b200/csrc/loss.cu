@@ -447,9 +447,11 @@ __global__ void __launch_bounds__(256) bce_kernel(LossParams p, const int* dense
         for (int c = lane; c < p.nc; c += 32) {
             const float x = L.cls[off + c];
             const float t = c == tcls ? w : 0.f;
-            part += (fmaxf(x, 0.f) - x * t + logf(1.f + expf(-fabsf(x)))) * inv;
+            // e = exp(-|x|) serves both the stable log-sum-exp and the sigmoid (HeadOperations.cs:222)
+            const float e = __expf(-fabsf(x));
+            part += (fmaxf(x, 0.f) - x * t + log1pf(e)) * inv;
             if (p.backward) {
-                const float s = x >= 0.f ? 1.f / (1.f + expf(-x)) : expf(x) / (1.f + expf(x));
+                const float s = __fdividef(x >= 0.f ? 1.f : e, 1.f + e);
                 L.dcls[off + c] = (s - t) * inv * p.grad_scale;
             }
         }
