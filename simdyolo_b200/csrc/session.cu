@@ -12,6 +12,7 @@
 #include <algorithm>
 #include <array>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -111,6 +112,7 @@ Session::Session(const sy_config& c) : cfg(c) {
     if (c.precision != SY_PRECISION_TF32 && c.precision != SY_PRECISION_3XTF32)
         throw SyError(SY_ERR_INVALID_ARGUMENT, "precision must be SY_PRECISION_TF32 or SY_PRECISION_3XTF32");
     x3_ = c.precision == SY_PRECISION_3XTF32;
+    if (const char* e = std::getenv("SIMDYOLO_CUDA_GRAPHS")) use_graphs_ = std::strcmp(e, "0") != 0;
     device_ = c.device;
     SY_CUDA(cudaSetDevice(device_));
     SY_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
@@ -170,8 +172,15 @@ Session::Session(const sy_config& c) : cfg(c) {
     SY_CUDA(cudaStreamSynchronize(stream_));
 }
 
+void Session::clear_graphs() {
+    for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
+    graphs_.clear();
+    graph_seen_.clear();
+}
+
 Session::~Session() {
     if (stream_) cudaStreamSynchronize(stream_);
+    clear_graphs();
     if (comm_ && nccl_) nccl_->CommDestroy(comm_);
     for (void* p : allocations_) cudaFree(p);
     for (void* p : {(void*)h_truth_, (void*)h_box_off_, (void*)h_flags_, (void*)h_loss_, (void*)h_pos_,
@@ -495,6 +504,7 @@ int Session::set_backbone(const float* host, long count) {
         weights_fwd_layout(backbone_params_ + op.w_off, op.oc, op.ic, taps, round_up(op.ic, 32), op.wk, stream_);
     }
     SY_CUDA(cudaStreamSynchronize(stream_));
+    clear_graphs();   // the stem's weights travel by value inside captured launches
     backbone_ready_ = true;
     return SY_OK;
 }
@@ -883,7 +893,7 @@ int Session::set_epoch(int epoch) {
 // Validate and upload the step's ground truth and images, run the frozen trunk (or stage cached
 // features); shared by the training step and the loss evaluation.
 void Session::prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float* const* features,
-                             const sy_box* boxes, const int32_t* counts, int images) {
+                             const sy_box* boxes, const int32_t* counts, int images, bool defer_backbone) {
     if (images < 1 || images > B_) throw SyError(SY_ERR_INVALID_ARGUMENT, "images out of range");
     if (!counts || (!boxes && images > 0)) throw SyError(SY_ERR_INVALID_ARGUMENT, "counts / boxes missing");
     SY_CUDA(cudaSetDevice(device_));
@@ -926,8 +936,10 @@ void Session::prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float
             }
             SY_CUDA(cudaMemcpyAsync(d_rgb_, rgb, bytes, cudaMemcpyHostToDevice, stream_));
         }
-        forward_backbone(images, src);
+        rgb_src_ = src;
+        if (!defer_backbone) forward_backbone(images, src);
     } else {
+        rgb_src_ = nullptr;
         if (!features) throw SyError(SY_ERR_INVALID_ARGUMENT, "features missing");
         for (int l = 0; l < 3; l++) {
             const Grid& g = levels_[l];
@@ -940,10 +952,44 @@ void Session::prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float
 
 int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
                   const int32_t* counts, int images, sy_step_stats* out) {
-    prepare_inputs(rgb, rgb_on_device, features, boxes, counts, images);
-    forward_head(images);
-    launch_losses(images, 1, epoch_);
-    backward_head(images);
+    const bool graph = use_graphs_ && !prof_;
+    prepare_inputs(rgb, rgb_on_device, features, boxes, counts, images, graph);
+    const bool trunk = rgb != nullptr;
+    auto device_work = [&] {
+        if (graph && trunk) forward_backbone(images, rgb_src_);
+        forward_head(images);
+        launch_losses(images, 1, epoch_);
+        backward_head(images);
+    };
+    if (!graph) {
+        device_work();
+    } else {
+        float w[2];
+        loss_weights(epoch_, w);
+        const GraphKey key{images, trunk ? (const void*)rgb_src_ : nullptr, w[0], w[1]};
+        auto it = graphs_.find(key);
+        if (it == graphs_.end() && graph_seen_[key]++ > 0 && graphs_.size() < 16) {
+            cudaGraph_t g = nullptr;
+            SY_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+            try {
+                device_work();
+            } catch (...) {
+                cudaStreamEndCapture(stream_, &g);
+                if (g) cudaGraphDestroy(g);
+                throw;
+            }
+            SY_CUDA(cudaStreamEndCapture(stream_, &g));
+            cudaGraphExec_t exec = nullptr;
+            const cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+            cudaGraphDestroy(g);
+            SY_CUDA(e);
+            it = graphs_.emplace(key, exec).first;
+        }
+        if (it != graphs_.end())
+            SY_CUDA(cudaGraphLaunch(it->second, stream_));
+        else
+            device_work();
+    }
     if (comm_) {
         // the gradient bucket is summed over ranks before anything reads it, so the finiteness
         // check, the checksum and the kept copy all see the global gradient

@@ -2,6 +2,8 @@
 // (YoloTrainer.Train inner loop, src/SimdYolo.Training/YoloTrainer.cs:185-199) on the GPU.
 #pragma once
 #include <array>
+#include <map>
+#include <tuple>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -119,7 +121,7 @@ private:
     void build_head();
     void forward_backbone(int batch, const uint8_t* rgb_device);
     void prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
-                        const int32_t* counts, int images);
+                        const int32_t* counts, int images, bool defer_backbone = false);
     void forward_head(int batch, bool training = true);
     // DetectionHead.Loss: one loss per branch set, gradients scaled by the set's weight
     void launch_losses(int images, int backward, int epoch);
@@ -193,6 +195,16 @@ private:
     int n_sets_ = 1;                  // 2 with the one-to-one branches
     bool progressive_ = false;        // end-to-end with reg_max 1 (TrainingHeadSchema.Progressive)
     int epoch_ = 0;
+    // CUDA graphs of the device work of a training step (trunk forward, head forward, losses, head
+    // backward), one per (images, image source, loss weights); a key is captured the second time it is
+    // seen (the first run is eager and settles every one-time set-up).  Disabled while conv launches are
+    // profiled, or with SIMDYOLO_CUDA_GRAPHS=0 in the environment.
+    using GraphKey = std::tuple<int, const void*, float, float>;
+    std::map<GraphKey, cudaGraphExec_t> graphs_;
+    std::map<GraphKey, int> graph_seen_;
+    bool use_graphs_ = true;
+    const uint8_t* rgb_src_ = nullptr;   // device images of the current step (deferred trunk forward)
+    void clear_graphs();
     int last_batch_ = 0;
     // 3xTF32 operand split scratch: activations (4 buffers) and weights (2 buffers)
     bool x3_ = false;
