@@ -148,21 +148,38 @@ __global__ void bn_eval_coef_kernel(const float* rm, const float* rv, float eps,
     inv_p[i] = 1.0f / sqrtf(rv[ch] + eps);
 }
 
-// red[b][ch] = (sum dz, sum dz xhat) folded over the row groups in order; f = gamma inv / n.
-__global__ void bn_bwd_fold_kernel(const float* part, int batch, int c, int groups, float n_pix, const float* inv_p,
-                                   const float* gamma, float* red, float* f_p) {
-    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= (long)batch * c) return;
-    const int b = (int)(i / c), ch = (int)(i - (long)b * c);
+// red[b][ch] = (sum dz, sum dz xhat) folded over the row groups; f = gamma inv / n.  Block (32 channels,
+// image): warp w sums groups w, w + 8, ... and the eight warps' sums are added in warp order, so the
+// result is deterministic.
+__global__ void __launch_bounds__(kFoldWarps * 32) bn_bwd_fold_kernel(const float* part, int batch, int c, int groups,
+                                                                      float n_pix, const float* inv_p,
+                                                                      const float* gamma, float* red, float* f_p) {
+    __shared__ float r1[kFoldWarps][32], r2[kFoldWarps][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int ch = blockIdx.x * 32 + lane, b = blockIdx.y;
+    const bool on = ch < c;
     float t1 = 0.0f, t2 = 0.0f;
-    for (int q = 0; q < groups; q++) {
-        const float* o = part + (((long)b * groups + q) * c + ch) * 2;
-        t1 += o[0];
-        t2 += o[1];
+    if (on)
+#pragma unroll 4
+        for (int q = warp; q < groups; q += kFoldWarps) {
+            const float* o = part + (((long)b * groups + q) * c + ch) * 2;
+            t1 += o[0];
+            t2 += o[1];
+        }
+    r1[warp][lane] = t1;
+    r2[warp][lane] = t2;
+    __syncthreads();
+    if (warp == 0 && on) {
+        float s1 = 0.0f, s2 = 0.0f;
+        for (int w = 0; w < kFoldWarps; w++) {
+            s1 += r1[w][lane];
+            s2 += r2[w][lane];
+        }
+        const long i = (long)b * c + ch;
+        red[i * 2 + 0] = s1;
+        red[i * 2 + 1] = s2;
+        f_p[i] = gamma[ch] * inv_p[i] / n_pix;
     }
-    red[i * 2 + 0] = t1;
-    red[i * 2 + 1] = t2;
-    f_p[i] = gamma[ch] * inv_p[i] / n_pix;
 }
 
 // dgamma += sum_b red[b][ch][1], dbeta += sum_b red[b][ch][0], images in order.
@@ -170,6 +187,7 @@ __global__ void bn_param_grad_kernel(const float* red, int batch, int c, float* 
     const int ch = blockIdx.x * blockDim.x + threadIdx.x;
     if (ch >= c) return;
     float dg = dgamma[ch], db = dbeta[ch];
+#pragma unroll 8
     for (int b = 0; b < batch; b++) {
         db += red[((long)b * c + ch) * 2 + 0];
         dg += red[((long)b * c + ch) * 2 + 1];
@@ -275,6 +293,7 @@ __global__ void bias_fold_kernel(const float* per_image, int batch, int c, float
     const int ch = blockIdx.x * blockDim.x + threadIdx.x;
     if (ch >= c) return;
     float acc = db[ch];
+#pragma unroll 8
     for (int b = 0; b < batch; b++) acc += per_image[(long)b * c + ch];
     db[ch] = acc;
 }
@@ -326,8 +345,9 @@ void bn_backward_fold(const float* part, int batch, const Grid& g, int c, const 
                       float* dgamma, float* dbeta, float* bcoef, cudaStream_t stream) {
     const long n = (long)batch * c;
     float* red = bcoef + n;
-    bn_bwd_fold_kernel<<<(int)((n + 127) / 128), 128, 0, stream>>>(part, batch, c, g.rows / 32, (float)(g.h * g.w),
-                                                                  coef + n, gamma, red, bcoef);
+    bn_bwd_fold_kernel<<<dim3((c + 31) / 32, batch), kFoldWarps * 32, 0, stream>>>(part, batch, c, g.rows / 32,
+                                                                                  (float)(g.h * g.w), coef + n, gamma,
+                                                                                  red, bcoef);
     launch_check("bn_bwd_fold_kernel");
     bn_param_grad_kernel<<<(c + 127) / 128, 128, 0, stream>>>(red, batch, c, dgamma, dbeta);
     launch_check("bn_param_grad_kernel");

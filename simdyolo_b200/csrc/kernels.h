@@ -126,6 +126,14 @@ void stem_conv(const uint8_t* rgb, int batch, int size, const float* w_host, con
 // OIHW -> [oc][t][kpad] (forward) and OIHW -> [ic][t][kpad_o] (data gradient)
 void weights_fwd_layout(const float* oihw, int oc, int ic, int taps, int kpad, float* dst, cudaStream_t stream);
 void weights_dgrad_layout(const float* oihw, int oc, int ic, int taps, int kpad_o, float* dst, cudaStream_t stream);
+// Both layouts of many conv weights in one launch: table[i] describes weight tensor i (device array).
+struct WeightLayoutJob {
+    const float* oihw;
+    int oc, ic, taps, kpad_in, kpad_out;
+    float* fwd;     // [oc][taps][kpad_in]
+    float* dgrad;   // [ic][taps][kpad_out]
+};
+void weights_layout_batch(const WeightLayoutJob* table_device, int jobs, long max_elems, cudaStream_t stream);
 
 // ---------------------------------------------------------------- backbone helpers
 void maxpool5_padded(const View& in, const View& out, int batch, const Grid& g, cudaStream_t stream);

@@ -80,6 +80,26 @@ __global__ void weights_dgrad_kernel(const float* w, int oc, int ic, int taps, i
     }
 }
 
+// blockIdx.y = job; the forward layout then the data-gradient layout of that job's weights.
+__global__ void weights_layout_batch_kernel(const WeightLayoutJob* table) {
+    const WeightLayoutJob jb = table[blockIdx.y];
+    const long nf = (long)jb.oc * jb.taps * jb.kpad_in, nd = (long)jb.ic * jb.taps * jb.kpad_out;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < nf + nd; i += (long)gridDim.x * blockDim.x) {
+        if (i < nf) {
+            const int c = (int)(i % jb.kpad_in);
+            const long r = i / jb.kpad_in;
+            const int t = (int)(r % jb.taps), o = (int)(r / jb.taps);
+            jb.fwd[i] = c < jb.ic ? jb.oihw[((long)o * jb.ic + c) * jb.taps + t] : 0.0f;
+        } else {
+            const long k = i - nf;
+            const int o = (int)(k % jb.kpad_out);
+            const long r = k / jb.kpad_out;
+            const int t = (int)(r % jb.taps), c = (int)(r / jb.taps);
+            jb.dgrad[k] = o < jb.oc ? jb.oihw[((long)o * jb.ic + c) * jb.taps + t] : 0.0f;
+        }
+    }
+}
+
 // Vector of V consecutive channels (V = 4 when channels and pitches allow float4 access).
 template <int V>
 struct Vec {
@@ -173,42 +193,34 @@ struct StemParams {
     float b[OC];
 };
 
-// One block per output row (blockIdx.x = image * ho + oy): the three input rows it needs are read
-// once, coalesced, and converted (u8 / 255) into shared memory as [row][channel][size + 2] with zero
-// columns at both ends; each thread then forms its pixels' 27 inputs from shared memory.  32-bit index
-// math; the SiLU uses the fast exponential and reciprocal.
 template <int OC>
 __global__ void __launch_bounds__(256) stem_conv_kernel(const uint8_t* rgb, int batch, int size,
                                                         const StemParams<OC> sp, float* out, int out_pitch,
                                                         Grid gout, PhaseOut phase, int has_phase) {
-    extern __shared__ float rows_s[];   // [3][3][size + 2]
-    const int ho = gout.h, wo = gout.w, sw = size + 2;
-    const int b = blockIdx.x / ho, oy = blockIdx.x - b * ho;
-    for (int k = threadIdx.x; k < 3 * sw; k += blockDim.x) {
-        const int ry = k / sw, x = k - ry * sw;
-        const int iy = 2 * oy + ry - 1, ix = x - 1;
-        const bool ok = iy >= 0 && iy < size && ix >= 0 && ix < size;
-        const uint8_t* px = rgb + (((long)b * size + (ok ? iy : 0)) * size + (ok ? ix : 0)) * 3;
-#pragma unroll
-        for (int c = 0; c < 3; c++) rows_s[(ry * 3 + c) * sw + x] = ok ? byte_over_255(px[c]) : 0.0f;
-    }
-    __syncthreads();
-    for (int ox = threadIdx.x; ox < wo; ox += blockDim.x) {
+    const int ho = gout.h, wo = gout.w;
+    const long total = (long)batch * ho * wo;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int b = (int)(i / ((long)ho * wo));
+        const int rem = (int)(i - (long)b * ho * wo);
+        const int oy = rem / wo, ox = rem - oy * wo;
         float in[27];
 #pragma unroll
         for (int ky = 0; ky < 3; ky++)
 #pragma unroll
-            for (int kx = 0; kx < 3; kx++)
+            for (int kx = 0; kx < 3; kx++) {
+                const int iy = 2 * oy + ky - 1, ix = 2 * ox + kx - 1;
+                const bool ok = iy >= 0 && iy < size && ix >= 0 && ix < size;
+                const uint8_t* p = rgb + (((long)b * size + (ok ? iy : 0)) * size + (ok ? ix : 0)) * 3;
 #pragma unroll
-                for (int c = 0; c < 3; c++) in[c * 9 + ky * 3 + kx] = rows_s[(ky * 3 + c) * sw + 2 * ox + kx];
+                for (int c = 0; c < 3; c++) in[c * 9 + ky * 3 + kx] = ok ? byte_over_255(p[c]) : 0.0f;
+            }
         float acc[OC];
 #pragma unroll
         for (int o = 0; o < OC; o++) {
             float s = 0.0f;
 #pragma unroll
             for (int q = 0; q < 27; q++) s = fmaf(sp.w[o * 27 + q], in[q], s);
-            s += sp.b[o];
-            acc[o] = __fdividef(s, 1.0f + __expf(-s));
+            acc[o] = silu_f(s + sp.b[o]);
         }
         if (out) {
             float* dst = out + ((long)b * gout.rows + gout.row(oy, ox)) * out_pitch;
@@ -287,6 +299,13 @@ void weights_dgrad_layout(const float* oihw, int oc, int ic, int taps, int kpad_
     launch_check("weights_dgrad_kernel");
 }
 
+void weights_layout_batch(const WeightLayoutJob* table_device, int jobs, long max_elems, cudaStream_t stream) {
+    if (jobs < 1 || jobs > 65535) throw std::runtime_error("weights_layout_batch: job count");
+    const int bx = (int)std::min<long>(64, std::max<long>(1, (max_elems + 255) / 256));
+    weights_layout_batch_kernel<<<dim3(bx, jobs), 256, 0, stream>>>(table_device);
+    launch_check("weights_layout_batch_kernel");
+}
+
 void maxpool5_padded(const View& in, const View& out, int batch, const Grid& g, cudaStream_t stream) {
     const bool vec = in.channels % 4 == 0 && in.pitch % 4 == 0 && out.pitch % 4 == 0 &&
                      (reinterpret_cast<uintptr_t>(in.base) & 15) == 0 && (reinterpret_cast<uintptr_t>(out.base) & 15) == 0;
@@ -322,18 +341,11 @@ void upsample2_padded(const View& in, const Grid& gin, const View& out, const Gr
 
 template <int OC>
 static void launch_stem(const uint8_t* rgb, int batch, int size, const float* w_host, const float* b_host,
-                        const View& out, const Grid& gout, const PhaseOut& ph, int hp, cudaStream_t stream) {
+                        const View& out, const Grid& gout, const PhaseOut& ph, int hp, int blocks, cudaStream_t stream) {
     StemParams<OC> sp;
     for (int i = 0; i < OC * 27; i++) sp.w[i] = w_host[i];
     for (int i = 0; i < OC; i++) sp.b[i] = b_host[i];
-    const size_t smem = sizeof(float) * 9 * (size_t)(size + 2);
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(stem_conv_kernel<OC>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-        attr_set = true;
-    }
-    stem_conv_kernel<OC><<<batch * gout.h, 256, smem, stream>>>(rgb, batch, size, sp, out.base, out.pitch, gout, ph,
-                                                                hp);
+    stem_conv_kernel<OC><<<blocks, 256, 0, stream>>>(rgb, batch, size, sp, out.base, out.pitch, gout, ph, hp);
 }
 
 void stem_conv(const uint8_t* rgb, int batch, int size, const float* w_host, const float* bias_host, int oc,
@@ -341,15 +353,15 @@ void stem_conv(const uint8_t* rgb, int batch, int size, const float* w_host, con
     if (out.pitch % 4 != 0 || (phase && phase->pitch % 4 != 0))
         throw std::runtime_error("stem_conv: pitches must be multiples of 4");
     if (!out.base && !phase) throw std::runtime_error("stem_conv: no output");
-    if (gout.h != size / 2 || gout.w != size / 2 || 9 * (size + 2) * 4 > 64 * 1024)
-        throw std::runtime_error("stem_conv: image size");
+    const long n = (long)batch * gout.h * gout.w;
+    const int blocks = (int)std::min<long>(148L * 8, std::max<long>(1, (n + 255) / 256));
     const PhaseOut ph = phase ? *phase : PhaseOut{};
     const int hp = phase ? 1 : 0;
     switch (oc) {
-        case 16: launch_stem<16>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, stream); break;
-        case 32: launch_stem<32>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, stream); break;
-        case 48: launch_stem<48>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, stream); break;
-        case 64: launch_stem<64>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, stream); break;
+        case 16: launch_stem<16>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream); break;
+        case 32: launch_stem<32>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream); break;
+        case 48: launch_stem<48>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream); break;
+        case 64: launch_stem<64>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream); break;
         default: throw std::runtime_error("stem_conv: output channels must be 16, 32, 48 or 64");
     }
     launch_check("stem_conv_kernel");

@@ -722,12 +722,24 @@ void Session::build_head() {
 }
 
 void Session::refresh_head_weights() {
-    for (auto& branch : branches_)
-        for (auto& hb : branch.blocks) {
-            if (hb.dw) continue;   // depthwise kernels read the [c][taps] parameters directly
-            weights_fwd_layout(params_ + hb.w_off, hb.b.oc, hb.b.ic, hb.taps, hb.kpad_in, hb.w_fwd, stream_);
-            weights_dgrad_layout(params_ + hb.w_off, hb.b.oc, hb.b.ic, hb.taps, hb.kpad_out, hb.w_dgrad, stream_);
-        }
+    if (!d_layout_jobs_) {
+        // depthwise kernels read the [c][taps] parameters directly; every other head conv gets its
+        // forward and data-gradient layouts from one batched launch
+        std::vector<WeightLayoutJob> jobs;
+        for (auto& branch : branches_)
+            for (auto& hb : branch.blocks) {
+                if (hb.dw) continue;
+                jobs.push_back(WeightLayoutJob{params_ + hb.w_off, hb.b.oc, hb.b.ic, hb.taps, hb.kpad_in, hb.kpad_out,
+                                               hb.w_fwd, hb.w_dgrad});
+                layout_max_elems_ = std::max(layout_max_elems_, (long)hb.taps * (hb.b.oc * hb.kpad_in +
+                                                                                  hb.b.ic * hb.kpad_out));
+            }
+        n_layout_jobs_ = (int)jobs.size();
+        if (n_layout_jobs_ == 0) return;
+        d_layout_jobs_ = static_cast<WeightLayoutJob*>(dalloc(sizeof(WeightLayoutJob) * jobs.size()));
+        SY_CUDA(cudaMemcpy(d_layout_jobs_, jobs.data(), sizeof(WeightLayoutJob) * jobs.size(), cudaMemcpyHostToDevice));
+    }
+    if (n_layout_jobs_ > 0) weights_layout_batch(d_layout_jobs_, n_layout_jobs_, layout_max_elems_, stream_);
 }
 
 static View rows_of(View v, int batch, const Grid& g) {

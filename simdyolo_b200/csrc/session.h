@@ -131,6 +131,9 @@ private:
                         int* connected, bool* finite) const;
     void backward_head(int batch);
     void refresh_head_weights();
+    WeightLayoutJob* d_layout_jobs_ = nullptr;   // one job per tensor-core head conv
+    int n_layout_jobs_ = 0;
+    long layout_max_elems_ = 0;
     View alloc_view(int channels, const Grid& g);
     // tensor-core convolutions, in TF32 or (precision 3xTF32) as three split-operand passes
     void conv_fwd(const View& in, const float* wk, long wk_floats, int n_rows, int n_out, int taps, int sign,
