@@ -108,14 +108,16 @@ __global__ void bn_apply_kernel(const float* y, int ypitch, const float* mean_p,
                                 const float* gamma, const float* beta, int c, Grid g, float* a, int apitch) {
     const int b = blockIdx.y;
     const int per_row = kVec ? c / 4 : c;
-    const long total = (long)g.rows * per_row;
+    const int total = g.rows * per_row;   // < 2^22 (checked by the launcher)
+    const float inv_row = 1.0f / (float)per_row, inv_wp = 1.0f / (float)g.wp;
     const long base = (long)b * g.rows;
     const float* mb = mean_p + (long)b * c;
     const float* ib = inv_p + (long)b * c;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const int r = (int)(i / per_row), j = (int)(i - (long)r * per_row);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int r = fast_div(i, inv_row), j = i - r * per_row;
         const long row = base + r;
-        const bool in = g.interior(r);
+        const int py = fast_div(r, inv_wp), px = r - py * g.wp;
+        const bool in = py >= 1 && py <= g.h && px >= 1 && px <= g.w;
         if (kVec) {
             float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
             if (in) {
@@ -204,16 +206,18 @@ __global__ void bn_bwd_apply_kernel(const float* y, int ypitch, const float* dz,
                                     float* dy, int dpitch) {
     const int b = blockIdx.y;
     const int per_row = kVec ? c / 4 : c;
-    const long total = (long)g.rows * per_row;
+    const int total = g.rows * per_row;   // < 2^22 (checked by the launcher)
+    const float inv_row = 1.0f / (float)per_row, inv_wp = 1.0f / (float)g.wp;
     const long base = (long)b * g.rows;
     const float* mb = mean_p + (long)b * c;
     const float* ib = inv_p + (long)b * c;
     const float* fb = f_p + (long)b * c;
     const float* rb = red + (long)b * c * 2;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const int r = (int)(i / per_row), j = (int)(i - (long)r * per_row);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int r = fast_div(i, inv_row), j = i - r * per_row;
         const long row = base + r;
-        const bool in = g.interior(r);
+        const int py = fast_div(r, inv_wp), px = r - py * g.wp;
+        const bool in = py >= 1 && py <= g.h && px >= 1 && px <= g.w;
         if (kVec) {
             float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
             if (in) {
@@ -255,6 +259,42 @@ __global__ void bn_running_kernel(const float* stats, long rank_stride, int rank
         rvar[ch] = rv;
     }
     if (ch == 0 && tracked) tracked[0] += (float)batch * ranks;
+}
+
+// All BatchNorm layers of the head in one launch: blockIdx.y = layer (BnFoldJob table), threads over
+// channels; per channel the images are folded in order, exactly as bn_running_kernel / bn_param_grad_kernel.
+__global__ void bn_running_batch_kernel(const BnFoldJob* jobs, const float* stats, long rank_stride, int ranks,
+                                        int batch, float m) {
+    const BnFoldJob jb = jobs[blockIdx.y];
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+    if (ch < jb.c) {
+        const float* st = stats + jb.stats_off;
+        float rm = jb.rmean[ch], rv = jb.rvar[ch];
+        const float unbias = jb.spatial > 1 ? (float)jb.spatial / (jb.spatial - 1) : 1.0f;
+        for (int r = 0; r < ranks; r++)
+            for (int b = 0; b < batch; b++) {
+                const float* s = st + r * rank_stride + ((long)b * jb.c + ch) * 2;
+                rm = (1 - m) * rm + m * s[0];
+                rv = (1 - m) * rv + m * s[1] * unbias;
+            }
+        jb.rmean[ch] = rm;
+        jb.rvar[ch] = rv;
+    }
+    if (ch == 0 && jb.tracked) jb.tracked[0] += (float)batch * ranks;
+}
+
+__global__ void bn_param_grad_batch_kernel(const BnFoldJob* jobs, int batch) {
+    const BnFoldJob jb = jobs[blockIdx.y];
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+    if (ch >= jb.c) return;
+    const float* red = jb.bcoef + (long)batch * jb.c;   // bcoef = [f plane | (sum dz, sum dz xhat) pairs]
+    float dg = jb.dgamma[ch], db = jb.dbeta[ch];
+    for (int b = 0; b < batch; b++) {
+        db += red[((long)b * jb.c + ch) * 2 + 0];
+        dg += red[((long)b * jb.c + ch) * 2 + 1];
+    }
+    jb.dgamma[ch] = dg;
+    jb.dbeta[ch] = db;
 }
 
 __global__ void __launch_bounds__(kThreads) bias_partial_kernel(const float* gr, int pitch, int c, Grid g, int splits,
@@ -331,6 +371,7 @@ void bn_silu_apply(const View& y, const float* coef, const float* gamma, const f
     const int c = y.channels;
     const bool vec = c % 4 == 0 && y.pitch % 4 == 0 && a.pitch % 4 == 0;
     const long per_image = (long)g.rows * (vec ? c / 4 : c);
+    if (per_image >= (1L << 22)) throw std::runtime_error("bn_silu_apply: image too large");
     const float* inv = coef + (long)batch * c;
     if (vec)
         bn_apply_kernel<true><<<image_grid(per_image, batch), 256, 0, stream>>>(y.base, y.pitch, coef, inv, gamma,
@@ -341,14 +382,27 @@ void bn_silu_apply(const View& y, const float* coef, const float* gamma, const f
     launch_check("bn_apply_kernel");
 }
 
+void bn_running_update_batch(const BnFoldJob* jobs, int njobs, int max_c, const float* stats, long rank_stride,
+                             int ranks, int batch, float momentum, cudaStream_t stream) {
+    bn_running_batch_kernel<<<dim3((max_c + 127) / 128, njobs), 128, 0, stream>>>(jobs, stats, rank_stride, ranks,
+                                                                                   batch, momentum);
+    launch_check("bn_running_batch_kernel");
+}
+
+void bn_param_grad_batch(const BnFoldJob* jobs, int njobs, int max_c, int batch, cudaStream_t stream) {
+    bn_param_grad_batch_kernel<<<dim3((max_c + 127) / 128, njobs), 128, 0, stream>>>(jobs, batch);
+    launch_check("bn_param_grad_batch_kernel");
+}
+
 void bn_backward_fold(const float* part, int batch, const Grid& g, int c, const float* coef, const float* gamma,
-                      float* dgamma, float* dbeta, float* bcoef, cudaStream_t stream) {
+                      float* dgamma, float* dbeta, float* bcoef, cudaStream_t stream, bool param_grad) {
     const long n = (long)batch * c;
     float* red = bcoef + n;
     bn_bwd_fold_kernel<<<dim3((c + 31) / 32, batch), kFoldWarps * 32, 0, stream>>>(part, batch, c, g.rows / 32,
                                                                                   (float)(g.h * g.w), coef + n, gamma,
                                                                                   red, bcoef);
     launch_check("bn_bwd_fold_kernel");
+    if (!param_grad) return;
     bn_param_grad_kernel<<<(c + 127) / 128, 128, 0, stream>>>(red, batch, c, dgamma, dbeta);
     launch_check("bn_param_grad_kernel");
 }
@@ -358,6 +412,7 @@ void bn_backward_apply(const View& y, const View& dz, const float* coef, const f
     const int c = y.channels;
     const bool vec = c % 4 == 0 && y.pitch % 4 == 0 && dz.pitch % 4 == 0 && dy.pitch % 4 == 0;
     const long per_image = (long)g.rows * (vec ? c / 4 : c);
+    if (per_image >= (1L << 22)) throw std::runtime_error("bn_backward_apply: image too large");
     const float* inv = coef + (long)batch * c;
     const float* red = bcoef + (long)batch * c;
     const float n = (float)(g.h * g.w);

@@ -158,12 +158,24 @@ void bn_silu_apply(const View& y, const float* coef, const float* gamma, const f
 // dgamma / dbeta are accumulated over images in image order.  bcoef (3 x batch x c floats) receives
 // [f plane | red], f = gamma inv / n, red[(b * c + ch) * 2 + {0,1}] = (sum dz, sum dz xhat).
 void bn_backward_fold(const float* part, int batch, const Grid& g, int c, const float* coef, const float* gamma,
-                      float* dgamma, float* dbeta, float* bcoef, cudaStream_t stream);
+                      float* dgamma, float* dbeta, float* bcoef, cudaStream_t stream, bool param_grad = true);
 // dy = f (n dz - sum dz - xhat sum dz xhat)  (HeadOperations.cs:185-189) at interior rows, 0 elsewhere.
 void bn_backward_apply(const View& y, const View& dz, const float* coef, const float* bcoef, int batch, const Grid& g,
                        const View& dy, cudaStream_t stream);
 // Running statistics: for each BN channel, r <- (1-m) r + m * s_i for images i in order, over
 // `ranks` blocks of `batch` images each `rank_stride` floats apart (all-gathered ranks).
+// One BatchNorm layer of a batched fold (device table): statistics at `stats_off` floats into the
+// statistics block, running buffers, and the backward sums / parameter gradients.
+struct BnFoldJob {
+    long stats_off;
+    int c, spatial;
+    float *rmean, *rvar, *tracked;
+    const float* bcoef; // bn_backward_fold's output: [f plane (batch x c) | (sum dz, sum dz xhat) pairs]
+    float *dgamma, *dbeta;
+};
+void bn_running_update_batch(const BnFoldJob* jobs, int njobs, int max_c, const float* stats, long rank_stride,
+                             int ranks, int batch, float momentum, cudaStream_t stream);
+void bn_param_grad_batch(const BnFoldJob* jobs, int njobs, int max_c, int batch, cudaStream_t stream);
 void bn_running_update(const float* stats, long rank_stride, int ranks, int batch, int c, int spatial, float momentum,
                        float* rmean, float* rvar, float* tracked, cudaStream_t stream);
 // Scratch (floats) bias_grad needs for `channels` channels of `batch` images.

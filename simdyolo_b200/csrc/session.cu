@@ -716,6 +716,24 @@ void Session::build_head() {
     for (auto& branch : branches_)
         for (auto& hb : branch.blocks)
             if (hb.b.has_bn) hb.stats = bn_stats_all_ + 2 * (size_t)B_ * hb.stats_off;
+    // batched folds over all BatchNorm layers (running statistics, parameter gradients)
+    {
+        std::vector<BnFoldJob> jobs;
+        for (auto& branch : branches_)
+            for (auto& hb : branch.blocks)
+                if (hb.b.has_bn) {
+                    const Grid& g = levels_[branch.level];
+                    jobs.push_back(BnFoldJob{2L * B_ * hb.stats_off, hb.b.oc, g.h * g.w, buffers_ + hb.rm_off,
+                                             buffers_ + hb.rv_off, buffers_ + hb.nt_off, hb.bcoef, grads_ + hb.g_off,
+                                             grads_ + hb.be_off});
+                    bn_max_c_ = std::max(bn_max_c_, hb.b.oc);
+                }
+        n_bn_jobs_ = (int)jobs.size();
+        if (n_bn_jobs_ > 0) {
+            d_bn_jobs_ = static_cast<BnFoldJob*>(dalloc(sizeof(BnFoldJob) * jobs.size()));
+            SY_CUDA(cudaMemcpy(d_bn_jobs_, jobs.data(), sizeof(BnFoldJob) * jobs.size(), cudaMemcpyHostToDevice));
+        }
+    }
     wgrad_ws_ = static_cast<float*>(dalloc(sizeof(float) * ws));
     bias_part_ = static_cast<float*>(dalloc(sizeof(float) * bn_workspace_floats(B_, max_oc)));
     bn_part_ = static_cast<float*>(dalloc(sizeof(float) * std::max<size_t>(bn_part_floats, 1)));
@@ -792,7 +810,7 @@ void Session::backward_head(int batch) {
                         // hb.g holds dz and bn_part_ its partial sums, written by the next block's data-gradient
                         // epilogue (every BN block is followed by another block)
                         bn_backward_fold(bn_part_, batch, g, hb.b.oc, hb.coef, params_ + hb.g_off, grads_ + hb.g_off,
-                                         grads_ + hb.be_off, hb.bcoef, stream_);
+                                         grads_ + hb.be_off, hb.bcoef, stream_, false);
                         bn_backward_apply(rows_of(hb.y, batch, g), rows_of(hb.g, batch, g), hb.coef, hb.bcoef, batch, g,
                                           rows_of(hb.dy, batch, g), stream_);
                     }
@@ -828,6 +846,8 @@ void Session::backward_head(int batch) {
                     }
                 }
             }
+    // BatchNorm gamma / beta gradients of every layer, images folded in order (deferred from the folds)
+    if (n_bn_jobs_ > 0) bn_param_grad_batch(d_bn_jobs_, n_bn_jobs_, bn_max_c_, batch, stream_);
 }
 
 // ------------------------------------------------------------------ loss
@@ -1073,14 +1093,9 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
         stats_src = bn_gather_;
         ranks = cfg.world_size;
     }
-    for (auto& branch : branches_)
-        for (auto& hb : branch.blocks)
-            if (hb.b.has_bn) {
-                const Grid& g = levels_[branch.level];
-                bn_running_update(stats_src + 2 * (size_t)B_ * hb.stats_off, (long)stats_floats, ranks, images,
-                                  hb.b.oc, g.h * g.w, cfg.bn_momentum, buffers_ + hb.rm_off, buffers_ + hb.rv_off,
-                                  buffers_ + hb.nt_off, stream_);
-            }
+    if (n_bn_jobs_ > 0)
+        bn_running_update_batch(d_bn_jobs_, n_bn_jobs_, bn_max_c_, stats_src, (long)stats_floats, ranks, images,
+                                cfg.bn_momentum, stream_);
     // update: flags [2..4] gate the optimizer groups (class branches, cv2, one2one_cv2), [5..7] hold
     // their AdamW step counts (TrainingParameter steps only when it received a gradient)
     const int has[3] = {1, connected & 1, (connected >> 1) & 1};

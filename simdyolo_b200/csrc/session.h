@@ -131,6 +131,8 @@ private:
                         int* connected, bool* finite) const;
     void backward_head(int batch);
     void refresh_head_weights();
+    BnFoldJob* d_bn_jobs_ = nullptr;             // one job per head BatchNorm layer
+    int n_bn_jobs_ = 0, bn_max_c_ = 0;
     WeightLayoutJob* d_layout_jobs_ = nullptr;   // one job per tensor-core head conv
     int n_layout_jobs_ = 0;
     long layout_max_elems_ = 0;
