@@ -305,11 +305,20 @@ __global__ void __launch_bounds__(kThreads) bias_partial_kernel(const float* gr,
     int p0, p1;
     split_range(g.h * g.w, splits, s, p0, p1);
     float acc = 0.0f;
-    if (ch < c)
-        for (int p = p0 + warp; p < p1; p += kWarps) {
-            const int yy = p / g.w, xx = p - yy * g.w;
-            acc += gr[((long)b * g.rows + g.row(yy, xx)) * pitch + ch];
+    if (ch < c) {
+        // pixel p -> (yy, xx) advanced incrementally (no division per pixel)
+        int p = p0 + warp;
+        int yy = p / g.w, xx = p - yy * g.w;
+        const float* img = gr + (long)b * g.rows * pitch + ch;
+        for (; p < p1; p += kWarps) {
+            acc += img[(long)g.row(yy, xx) * pitch];
+            xx += kWarps;
+            while (xx >= g.w) {
+                xx -= g.w;
+                yy++;
+            }
         }
+    }
     red[warp][lane] = acc;
     __syncthreads();
     if (warp == 0 && ch < c) {

@@ -938,7 +938,8 @@ __global__ void wgrad_reduce_kernel(const float* ws, int splits, long split_stri
 
 static int wgrad_splits(int m_tiles, long rows) {
     const long kblocks = (rows + kWgradBK - 1) / kWgradBK;
-    int target = std::max(1, (2 * num_sms()) / std::max(1, m_tiles));
+    // one wave of CTAs (one per SM: the stages take most of shared memory)
+    int target = std::max(1, num_sms() / std::max(1, m_tiles));
     return (int)std::min<long>(target, std::max<long>(1, kblocks / 8));
 }
 
