@@ -97,6 +97,7 @@ struct FwdParams {
     int n0;         // first weight row of this launch
     int a_stages, a_stage_bytes;
     int b_stages;   // 0: all weights resident
+    int b_pack;     // streamed weights: (tap, chunk) blocks per ring stage (few large stages move faster)
     int b_region_bytes;
     int nacc;       // TMEM accumulator stages
     int ksplit;     // 2: (T = 1) MMA warp w sums K steps 2w, 2w+1 into its own accumulator, the epilogue adds both
@@ -265,14 +266,17 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
                                         m0 + p.g_lo[g] + bx * kBoxRows);
                         ia++;
                         if (!resident) {
-                            for (int e = 0; e < p.g_ntaps[g]; e++, j++, ib++) {
+                            for (int e0 = 0; e0 < p.g_ntaps[g]; e0 += p.b_pack, ib++) {
+                                const int np = min(p.b_pack, p.g_ntaps[g] - e0);
                                 const int sb = ib % p.b_stages;
                                 if (!(ok = mbar_wait(&bempty[sb], ((ib / p.b_stages) & 1) ^ 1, p.err, 1))) break;
-                                mbar_arrive_expect_tx(&bfull[sb], (uint32_t)b_bytes);
-                                tma_load_2d(b_region + sb * b_bytes, &tmB, &bfull[sb], tap_s[j] * p.kpad + c * 32,
-                                            p.n0);
+                                mbar_arrive_expect_tx(&bfull[sb], (uint32_t)(np * b_bytes));
+                                for (int k = 0; k < np; k++)
+                                    tma_load_2d(b_region + (sb * p.b_pack + k) * b_bytes, &tmB, &bfull[sb],
+                                                tap_s[j + e0 + k] * p.kpad + c * 32, p.n0);
                             }
                         }
+                        j += p.g_ntaps[g];
                     }
                 }
             }
@@ -295,7 +299,7 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
                     event(&afull[ia % p.a_stages], (ia / p.a_stages) & 1, 3);
                     ia++;
                     if (!resident)
-                        for (int e = 0; e < p.g_ntaps[g]; e++, ib++)
+                        for (int e0 = 0; e0 < p.g_ntaps[g]; e0 += p.b_pack, ib++)
                             event(&bfull[ib % p.b_stages], (ib / p.b_stages) & 1, 3);
                 }
         }
@@ -327,19 +331,10 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
                     const int sa = ia % p.a_stages;
                     named_bar_sync(kMmaBar, kMmaBarThreads);   // A region loaded
                     const uint64_t a_st = a_desc0 + (uint64_t)(sa * a_stage16);
-                    const int jend = j + p.g_ntaps[g];
-                    for (; j < jend; j++) {
-                        uint64_t b_d;
-                        int sb = 0;
-                        if (resident) {
-                            b_d = b_desc0 + (uint64_t)((p.tap_t[j] * p.kchunks + c) * b_blk16);
-                        } else {
-                            sb = ib % p.b_stages;
-                            named_bar_sync(kMmaBar, kMmaBarThreads);   // weight block loaded
-                            b_d = b_desc0 + (uint64_t)(sb * b_blk16);
-                        }
-                        const uint64_t a_t = a_st + (uint64_t)(p.tap_off[j] * 8);
-                        const uint32_t first = (c == 0 && j == 0) ? 0u : 1u;
+                    // the MMAs of tap j against weight block descriptor b_d
+                    auto tap_mmas = [&](int jj, uint64_t b_d) {
+                        const uint64_t a_t = a_st + (uint64_t)(p.tap_off[jj] * 8);
+                        const uint32_t first = (c == 0 && jj == 0) ? 0u : 1u;
                         if (p.ksplit == 2) {
                             // one sub-tile: this warp's K steps 2w, 2w+1 into accumulator w
                             const uint32_t d_w = d + w * p.acc_cols;
@@ -355,9 +350,19 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
                                 mma_tf32_elect(d_i, a_i + 6, b_d + 6, idesc, 1u);
                             }
                         }
-                        if (!resident) {
+                    };
+                    const int jend = j + p.g_ntaps[g];
+                    if (resident) {
+                        for (; j < jend; j++) tap_mmas(j, b_desc0 + (uint64_t)((p.tap_t[j] * p.kchunks + c) * b_blk16));
+                    } else {
+                        // one hand-off and one release per pack of weight blocks
+                        for (; j < jend; ib++) {
+                            const int sb = ib % p.b_stages;
+                            const int np = min(p.b_pack, jend - j);
+                            named_bar_sync(kMmaBar, kMmaBarThreads);   // weight pack loaded
+                            const uint64_t b_st = b_desc0 + (uint64_t)(sb * p.b_pack * b_blk16);
+                            for (int e = 0; e < np; e++, j++) tap_mmas(j, b_st + (uint64_t)(e * b_blk16));
                             mma_commit_elect(&bempty[sb]);
-                            ib++;
                         }
                     }
                     mma_commit_elect(&aempty[sa]);
@@ -696,11 +701,17 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         if (resident) {
             p.a_stages = std::min(4, (kSmemBudget - res_bytes) / a_stage);
             p.b_stages = 0;
+            p.b_pack = 1;
             p.b_region_bytes = res_bytes;
         } else {
             p.a_stages = 2;
-            p.b_stages = std::min(16, (kSmemBudget - 2 * a_stage) / b_bytes);
-            p.b_region_bytes = p.b_stages * b_bytes;
+            // the largest pack that still double-buffers (a TMA handshake per 8 KB block halves the rate)
+            const int budget = kSmemBudget - 2 * a_stage;
+            int max_group_taps = 1;
+            for (int g = 0; g < ngroups; g++) max_group_taps = std::max(max_group_taps, g_ntaps[g]);
+            p.b_pack = std::max(1, std::min(max_group_taps, budget / (2 * b_bytes)));
+            p.b_stages = std::min(16, budget / (p.b_pack * b_bytes));
+            p.b_region_bytes = p.b_stages * p.b_pack * b_bytes;
         }
         p.acc_cols = acc_cols;
         p.ksplit = (T == 1 && 4 * acc_cols <= 512) ? 2 : 1;
