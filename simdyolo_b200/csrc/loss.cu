@@ -191,21 +191,22 @@ __device__ __forceinline__ void tal_metric(const LossParams& p, int b, int a, co
 }
 
 // ---------------------------------------------------------------- 1. decode
+// One thread per (image, anchor, side): the DFL expectation of that side and its decoded coordinate.
 __global__ void decode_kernel(LossParams p) {
-    const long total = (long)p.batch * p.anchors;
+    const long total = (long)p.batch * p.anchors * 4;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const int b = (int)(i / p.anchors), a = (int)(i - (long)b * p.anchors);
+        const long ia = i >> 2;
+        const int d = (int)(i & 3);
+        const int b = (int)(ia / p.anchors), a = (int)(ia - (long)b * p.anchors);
         int level, row;
         float cx, cy, st;
         anchor_location(p, a, level, row, cx, cy, st);
         const LevelIO& L = p.lv[level];
         const float* t = L.box + ((long)b * L.grid.rows + row) * L.box_pitch;
-        float e[4];
-        for (int d = 0; d < 4; d++) {
-            if (p.bins == 1) {
-                e[d] = t[d];
-                continue;
-            }
+        float e;
+        if (p.bins == 1) {
+            e = t[d];
+        } else {
             float maximum = -INFINITY;
             for (int k = 0; k < 16; k++) maximum = fmaxf(maximum, t[d * 16 + k]);
             float ex[16];
@@ -216,15 +217,11 @@ __global__ void decode_kernel(LossParams p) {
             }
             float dist = 0.f;
             for (int k = 0; k < 16; k++) dist = fadd(dist, fmul(fdiv(ex[k], sum), (float)k));
-            e[d] = dist;
+            e = dist;
         }
-        float* ev = p.expv + i * 4;
-        float* dv = p.dec + i * 4;
-        for (int d = 0; d < 4; d++) ev[d] = e[d];
-        dv[0] = fsub(cx, fmul(e[0], st));
-        dv[1] = fsub(cy, fmul(e[1], st));
-        dv[2] = fadd(cx, fmul(e[2], st));
-        dv[3] = fadd(cy, fmul(e[3], st));
+        p.expv[i] = e;
+        const float c = (d & 1) ? cy : cx;
+        p.dec[i] = d < 2 ? fsub(c, fmul(e, st)) : fadd(c, fmul(e, st));
     }
 }
 
@@ -298,6 +295,7 @@ __global__ void __launch_bounds__(256) topk_kernel(LossParams p) {
 // Conflicts (DetectionLoss.cs:69-81), max alignment / overlap per GT (:92-94), scores and their
 // sum in anchor order (:95-98).
 __global__ void __launch_bounds__(256) assign_kernel(LossParams p) {
+    extern __shared__ int owner_s[];   // [anchors]: -1 unselected, g selected by GT g alone, -2 by several
     const int b = blockIdx.x;
     const int n = p.box_off[b + 1] - p.box_off[b];
     const TruthBox* truth = p.truth + p.box_off[b];
@@ -312,38 +310,46 @@ __global__ void __launch_bounds__(256) assign_kernel(LossParams p) {
         for (int a = threadIdx.x; a < p.anchors; a += blockDim.x) p.out.assigned[(long)b * p.anchors + a] = -1;
     if (p.out.scores)
         for (int a = threadIdx.x; a < p.anchors; a += blockDim.x) p.out.scores[(long)b * p.anchors + a] = 0.f;
-    // gather the selected (gt, anchor) pairs, in gt order then rank order
-    if (threadIdx.x == 0) {
-        int c = 0;
-        for (int g = 0; g < n; g++)
-            for (int k = 0; k < p.topk; k++) {
-                int a = p.sel[((long)b * p.max_boxes + g) * p.topk + k];
-                if (a < 0) continue;
-                bool dup = false;
-                for (int j = 0; j < c; j++)
-                    if (anc[j] == a) {
-                        dup = true;
-                        own[j] = -2;  // selected by more than one GT
-                        break;
-                    }
-                if (!dup && c < kMaxSel) {
-                    anc[c] = a;
-                    own[c] = g;
-                    c++;
-                }
+    // the selected (gt, anchor) pairs, compacted in anchor order: an anchor picked by one GT keeps it as
+    // owner, one picked by several is marked -2 (a conflict resolved below); the owner map does not
+    // depend on the order in which the pairs are visited
+    for (int a = threadIdx.x; a < p.anchors; a += blockDim.x) owner_s[a] = -1;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n * p.topk; i += blockDim.x) {
+        const int g = i / p.topk;
+        const int a = p.sel[((long)b * p.max_boxes + g) * p.topk + (i - g * p.topk)];
+        if (a < 0) continue;
+        if (atomicCAS(&owner_s[a], -1, g) != -1) atomicExch(&owner_s[a], -2);
+    }
+    __syncthreads();
+    {
+        // block-wide exclusive scan of "selected" over contiguous anchor ranges per thread
+        __shared__ int part_s[256];
+        const int per = (p.anchors + blockDim.x - 1) / blockDim.x;
+        const int a0 = min(p.anchors, (int)threadIdx.x * per), a1 = min(p.anchors, a0 + per);
+        int cnt = 0;
+        for (int a = a0; a < a1; a++) cnt += owner_s[a] != -1;
+        part_s[threadIdx.x] = cnt;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int run = 0;
+            for (int t = 0; t < (int)blockDim.x; t++) {
+                const int v = part_s[t];
+                part_s[t] = run;
+                run += v;
             }
-        // sort by anchor index (insertion sort; c <= boxes * topk)
-        for (int i = 1; i < c; i++) {
-            int a = anc[i], o = own[i], j = i - 1;
-            while (j >= 0 && anc[j] > a) {
-                anc[j + 1] = anc[j];
-                own[j + 1] = own[j];
-                j--;
-            }
-            anc[j + 1] = a;
-            own[j + 1] = o;
+            count_s = min(run, kMaxSel);
         }
-        count_s = c;
+        __syncthreads();
+        int pos = part_s[threadIdx.x];
+        for (int a = a0; a < a1; a++)
+            if (owner_s[a] != -1) {
+                if (pos < kMaxSel) {
+                    anc[pos] = a;
+                    own[pos] = owner_s[a];
+                }
+                pos++;
+            }
     }
     for (int g = threadIdx.x; g < 128; g += blockDim.x) {
         max_al[g] = 0.f;
@@ -638,11 +644,18 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
     if (!p.out.scores) p.out.scores = dense_s;
 
     const long total = (long)batch * p.anchors;
-    decode_kernel<<<(int)std::min<long>(148L * 32, (total + 255) / 256), 256, 0, stream>>>(p);
+    decode_kernel<<<(int)std::min<long>(148L * 32, (4 * total + 255) / 256), 256, 0, stream>>>(p);
     launch_check("decode_kernel");
     if (max_boxes > 0) topk_kernel<<<dim3(max_boxes, batch), 256, 0, stream>>>(p);
     launch_check("topk_kernel");
-    assign_kernel<<<batch, 256, 0, stream>>>(p);
+    const size_t owner_bytes = sizeof(int) * (size_t)p.anchors;
+    static bool assign_attr = false;
+    if (!assign_attr) {
+        cudaFuncSetAttribute(assign_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        assign_attr = true;
+    }
+    if (owner_bytes > 160 * 1024) throw std::runtime_error("detection_loss: too many anchors");
+    assign_kernel<<<batch, 256, owner_bytes, stream>>>(p);
     launch_check("assign_kernel");
     if (backward)
         for (int l = 0; l < nlevels; l++) {
