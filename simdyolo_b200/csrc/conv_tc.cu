@@ -177,7 +177,12 @@ __device__ __forceinline__ float warp_sum16(const float (&v)[16], int lane) {
     return r + __shfl_xor_sync(0xffffffffu, r, 1);
 }
 
-template <int kEpiWarps>
+// Epilogue modes, each compiled on its own so that the features a launch does not use cost no
+// instructions per item: the trunk's (bias, SiLU, shortcut, halo mask, parity copy), the head
+// forward's (BatchNorm statistics partials), the head data gradient's (BatchNorm backward), and the
+// generic one (any combination, with the pre-added accumulator of the 3xTF32 passes).
+constexpr int kEpiPlain = 0, kEpiStats = 1, kEpiBnBwd = 2, kEpiGeneric = 3;
+template <int kEpiWarps, int kMode>
 __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
     conv_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ FwdParams p) {
@@ -197,7 +202,7 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
     uint64_t* tempty = tfull + p.nacc;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + p.nacc);
     int* tap_s = reinterpret_cast<int*>(tmem_slot + 4);     // [9] weight tap, [9] A row offset
-    float* bias_s = reinterpret_cast<float*>(tap_s + 20);
+    float* bias_s = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(tap_s + 20) + 15) & ~uintptr_t(15));
     float* gam_s = bias_s + p.n;   // BatchNorm gamma / beta of the layer whose gradient is produced
     float* bet_s = gam_s + p.n;
 
@@ -378,26 +383,175 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
         const int q = warp & 3;
         const int part = (warp - kEpiWarp0) >> 2;
         const int nchunks = (p.n + 15) >> 4;
-        const bool bn_bwd = p.bn.grad_part != nullptr;
+        constexpr bool kAny = kMode == kEpiGeneric;
+        const bool bn_bwd = (kMode == kEpiBnBwd || kAny) && p.bn.grad_part != nullptr;
+        const bool bn_stats = (kMode == kEpiStats || kAny) && p.bn.stats_part != nullptr;
+        const float* const pre_in = kAny ? p.pre : nullptr;
+        const float* const res_in = kAny ? p.residual : nullptr;
+        float* const phase_out = kAny ? p.phase : nullptr;
         int local = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
             const int acc = local % p.nacc;
             if (!mbar_wait(&tfull[acc], (local / p.nacc) & 1, p.err, 4)) break;
             tc_fence_after();
             const int mt = min(p.T, p.sub_tiles - tile * p.T);
+            if constexpr (kMode == kEpiPlain) {
+                // items (sub-tile i, 32-column chunk cj) in steps of kEpiWarps / 4; every branch is
+                // warp-uniform and the row index within the image advances without divisions
+                const int nch = (p.n + 31) >> 5;
+                const int sub0 = tile * p.T;
+                int rem = sub0 - (sub0 / p.sub_per_img) * p.sub_per_img;
+                int i = 0, cj = part;
+                while (cj >= nch) {
+                    cj -= nch;
+                    i++;
+                    if (++rem == p.sub_per_img) rem = 0;
+                }
+                while (i < mt) {
+                    const int j = cj * 32;
+                    if (j < p.n_valid) {
+                        const long m = (long)(sub0 + i) * kTileM + q * 32 + lane;
+                        const int r = rem * kTileM + q * 32 + lane;
+                        bool inside = true;
+                        if (p.mask) {
+                            const int py = fast_div(r, p.inv_wp), px = r - py * p.grid.wp;
+                            inside = py >= 1 && py <= p.grid.h && px >= 1 && px <= p.grid.w;
+                        }
+                        // each 16-column half is whole (vector accesses), partial or empty
+                        const bool full0 = j + 16 <= p.n_valid, full1 = j + 32 <= p.n_valid;
+                        float res[32];
+                        const bool has_res = p.residual != nullptr;
+                        if (has_res) {
+                            const float* rr = p.residual + m * (long)p.res_pitch + j;
+#pragma unroll
+                            for (int h = 0; h < 2; h++) {
+                                if ((h ? full1 : full0) && inside) {
+#pragma unroll
+                                    for (int u = 4 * h; u < 4 * h + 4; u++) {
+                                        const float4 t = *reinterpret_cast<const float4*>(rr + 4 * u);
+                                        res[4 * u] = t.x;
+                                        res[4 * u + 1] = t.y;
+                                        res[4 * u + 2] = t.z;
+                                        res[4 * u + 3] = t.w;
+                                    }
+                                } else {
+#pragma unroll
+                                    for (int u = 16 * h; u < 16 * h + 16; u++)
+                                        res[u] = (inside && j + u < p.n_valid) ? rr[u] : 0.0f;
+                                }
+                            }
+                        }
+                        float v[32];
+                        const uint32_t tl = ((uint32_t)(q * 32) << 16) + (uint32_t)j;
+                        if (p.ksplit == 2) {
+                            float v1[32];
+                            tmem_ld32(tmem_base + acc * 2 * p.acc_cols + tl, v);
+                            tmem_ld32(tmem_base + acc * 2 * p.acc_cols + p.acc_cols + tl, v1);
+#pragma unroll
+                            for (int u = 0; u < 32; u++) v[u] += v1[u];
+                        } else {
+                            tmem_ld32(tmem_base + (acc * p.T + i) * p.acc_cols + tl, v);
+                        }
+                        const float4* b4 = reinterpret_cast<const float4*>(bias_s + j);
+                        if (p.silu) {
+#pragma unroll
+                            for (int u = 0; u < 8; u++) {
+                                const float4 b = b4[u];
+                                v[4 * u] = silu_fast(v[4 * u] + b.x);
+                                v[4 * u + 1] = silu_fast(v[4 * u + 1] + b.y);
+                                v[4 * u + 2] = silu_fast(v[4 * u + 2] + b.z);
+                                v[4 * u + 3] = silu_fast(v[4 * u + 3] + b.w);
+                            }
+                        } else {
+#pragma unroll
+                            for (int u = 0; u < 8; u++) {
+                                const float4 b = b4[u];
+                                v[4 * u] += b.x;
+                                v[4 * u + 1] += b.y;
+                                v[4 * u + 2] += b.z;
+                                v[4 * u + 3] += b.w;
+                            }
+                        }
+                        if (has_res) {
+#pragma unroll
+                            for (int u = 0; u < 32; u++) v[u] += res[u];
+                        }
+                        if (!inside) {
+#pragma unroll
+                            for (int u = 0; u < 32; u++) v[u] = 0.0f;
+                        }
+                        float* prow = nullptr;
+                        if (p.phase && inside) {
+                            const int py = fast_div(r, p.inv_wp), px = r - py * p.grid.wp;
+                            const int img = (int)((sub0 + i) / p.sub_per_img);
+                            const long prow_index = ((py & 1) * 2 + (px & 1)) * p.phase_stride + img * p.phase_rows +
+                                                    (long)(py >> 1) * p.phase_wp + (px >> 1);
+                            prow = p.phase + prow_index * p.phase_pitch + j;
+                        }
+                        float* orow = p.out ? p.out + m * (long)p.out_pitch + j : nullptr;
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            if (h ? full1 : full0) {
+                                if (orow) {
+#pragma unroll
+                                    for (int u = 4 * h; u < 4 * h + 4; u++)
+                                        reinterpret_cast<float4*>(orow)[u] =
+                                            make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                                }
+                                if (prow) {
+#pragma unroll
+                                    for (int u = 4 * h; u < 4 * h + 4; u++)
+                                        reinterpret_cast<float4*>(prow)[u] =
+                                            make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                                }
+                            } else if (j + 16 * h < p.n_valid) {
+#pragma unroll
+                                for (int u = 16 * h; u < 16 * h + 16; u++)
+                                    if (j + u < p.n_valid) {
+                                        if (orow) orow[u] = v[u];
+                                        if (prow) prow[u] = v[u];
+                                    }
+                            }
+                        }
+                    }
+                    cj += kEpiWarps / 4;
+                    while (cj >= nch) {
+                        cj -= nch;
+                        i++;
+                        if (++rem == p.sub_per_img) rem = 0;
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(&tempty[acc]);
+                continue;
+            }
             // items (sub-tile i, 16-column chunk cj) in steps of kEpiWarps / 4, with 32-bit index math
             // advanced incrementally (a 128-row sub-tile never spans two images)
             const int sub0 = tile * p.T;
-            const int img0 = sub0 / p.sub_per_img, rem0 = sub0 - img0 * p.sub_per_img;
-            int i = part / nchunks, cj = part - (part / nchunks) * nchunks;
-            for (; i < mt; cj += kEpiWarps / 4, i += cj / nchunks, cj %= nchunks) {
-                const int j = cj * 16;
-                if (j >= p.n_valid) continue;   // warp-uniform
-                int rem = rem0 + i, img = img0;
-                while (rem >= p.sub_per_img) {
-                    rem -= p.sub_per_img;
+            int img = sub0 / p.sub_per_img, rem = sub0 - img * p.sub_per_img;
+            int i = 0, cj = part;
+            auto next_sub = [&] {
+                i++;
+                if (++rem == p.sub_per_img) {
+                    rem = 0;
                     img++;
                 }
+            };
+            while (cj >= nchunks) {
+                cj -= nchunks;
+                next_sub();
+            }
+            for (bool first = true;; first = false) {
+                if (!first) {
+                    cj += kEpiWarps / 4;
+                    while (cj >= nchunks) {
+                        cj -= nchunks;
+                        next_sub();
+                    }
+                }
+                if (i >= mt) break;
+                const int j = cj * 16;
+                if (j >= p.n_valid) continue;   // warp-uniform
                 const long m = (long)(sub0 + i) * kTileM + q * 32 + lane;
                 const int r = rem * kTileM + q * 32 + lane;
                 bool inside = true;
@@ -410,7 +564,7 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
                 const bool full16 = j + 16 <= p.n_valid;
                 const int chb = p.n0 + j;
                 float* orow = p.out ? p.out + m * (long)p.out_pitch : nullptr;
-                const float* rrow = p.residual ? p.residual + m * (long)p.res_pitch : nullptr;
+                const float* rrow = res_in ? res_in + m * (long)p.res_pitch : nullptr;
                 float res[16];
                 if (rrow && full16 && inside) {
 #pragma unroll
@@ -426,8 +580,8 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
                     for (int u = 0; u < 16; u++) res[u] = (rrow && inside && j + u < p.n_valid) ? rrow[j + u] : 0.0f;
                 }
                 float pre[16];
-                if (p.pre) {
-                    const float* pr = p.pre + m * (long)p.pre_pitch + j;
+                if (pre_in) {
+                    const float* pr = pre_in + m * (long)p.pre_pitch + j;
                     if (full16) {
 #pragma unroll
                         for (int u = 0; u < 4; u++) {
@@ -493,11 +647,11 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
                 }
                 // parity-split copy: padded pixel (py, px) -> plane (py&1, px&1), cell (py>>1, px>>1)
                 float* prow = nullptr;
-                if (p.phase && inside) {
+                if (phase_out && inside) {
                     const int py = r / p.grid.wp, px = r - py * p.grid.wp;
                     const long prow_index = ((py & 1) * 2 + (px & 1)) * p.phase_stride + img * p.phase_rows +
                                             (long)(py >> 1) * p.phase_wp + (px >> 1);
-                    prow = p.phase + prow_index * p.phase_pitch;
+                    prow = phase_out + prow_index * p.phase_pitch;
                 }
 #pragma unroll
                 for (int u = 0; u < 16; u++) {
@@ -508,7 +662,7 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
                 }
                 // BatchNorm partials over this warp's 32 rows (one row group, inside one image)
                 const long grp = ((long)tile * tile_rows + i * kTileM + q * 32) >> 5;
-                if (p.bn.stats_part) {
+                if (bn_stats) {
                     const float cnt = (float)__popc(__ballot_sync(0xffffffffu, inside));
                     const float mean_l = cnt > 0.0f ? warp_sum16(v, lane) / cnt : 0.0f;   // channel lane >> 1
                     float d[16];
@@ -621,8 +775,11 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
     const long sub_tiles = m_rows / kTileM;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaFuncSetAttribute(conv_fwd_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        cudaFuncSetAttribute(conv_fwd_tc_kernel<12>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(conv_fwd_tc_kernel<8, kEpiPlain>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(conv_fwd_tc_kernel<8, kEpiStats>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(conv_fwd_tc_kernel<8, kEpiGeneric>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(conv_fwd_tc_kernel<12, kEpiBnBwd>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(conv_fwd_tc_kernel<12, kEpiGeneric>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         attr_set = true;
     }
     CUtensorMap ta = make_map_2d(in.base, in.channels, in.rows, in.pitch, 32, kBoxRows);
@@ -741,13 +898,21 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         CUtensorMap tb = make_map_2d(wk, (long)taps * kpad, n_rows, (long)taps * kpad, 32, n);
         const int nb = resident ? 1 : p.b_stages;
         const size_t smem = 1024 + (size_t)p.a_stages * a_stage + p.b_region_bytes +
-                            (2 * p.a_stages + 2 * nb + 2 * p.nacc) * 8 + 16 + 80 + 3 * n * 4;
+                            (2 * p.a_stages + 2 * nb + 2 * p.nacc) * 8 + 16 + 80 + 16 + 3 * n * 4;
         if (smem > 227 * 1024) throw std::runtime_error("conv_tc: shared memory");
         const int grid_x = std::min(p.num_tiles, num_sms());
-        if (ep.bn.grad_part)
-            conv_fwd_tc_kernel<12><<<grid_x, fwd_threads(12), smem, stream>>>(ta, tb, p);
+        // the specialised epilogues cover the launches without a pre-add whose features they implement
+        const bool other = ep.pre || ((ep.bn.stats_part || ep.bn.grad_part) && (ep.residual || phase));
+        if (ep.bn.grad_part && !other)
+            conv_fwd_tc_kernel<12, kEpiBnBwd><<<grid_x, fwd_threads(12), smem, stream>>>(ta, tb, p);
+        else if (ep.bn.grad_part)
+            conv_fwd_tc_kernel<12, kEpiGeneric><<<grid_x, fwd_threads(12), smem, stream>>>(ta, tb, p);
+        else if (ep.bn.stats_part && !other)
+            conv_fwd_tc_kernel<8, kEpiStats><<<grid_x, fwd_threads(8), smem, stream>>>(ta, tb, p);
+        else if (ep.bn.stats_part || ep.pre)
+            conv_fwd_tc_kernel<8, kEpiGeneric><<<grid_x, fwd_threads(8), smem, stream>>>(ta, tb, p);
         else
-            conv_fwd_tc_kernel<8><<<grid_x, fwd_threads(8), smem, stream>>>(ta, tb, p);
+            conv_fwd_tc_kernel<8, kEpiPlain><<<grid_x, fwd_threads(8), smem, stream>>>(ta, tb, p);
         launch_check("conv_fwd_tc_kernel");
     }
 }
