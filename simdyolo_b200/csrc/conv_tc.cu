@@ -1091,24 +1091,41 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
     }
 }
 
-// dw[(o * ic + c) * taps + t] = sum_s ws[s][(t * kchunks + c / 32) * 32 + c % 32][o], splits summed in
-// order.  Consecutive threads take consecutive output channels o, so the workspace reads of a warp are
-// contiguous.  `n` is the workspace row stride (the MMA width, output channels rounded up to 16); `oc`
-// the real output channels, which alone bound the rows of dw that are written.
-__global__ void wgrad_reduce_kernel(const float* ws, int splits, long split_stride, int n, int oc, int ic, int taps,
-                                    int kchunks, float* dw, int accumulate) {
+// dw[(o * ic + c) * taps + t] = sum_s ws[s][(t * kchunks + c / 32) * 32 + c % 32][o].  A block takes 32
+// consecutive outputs (o fastest, so the workspace reads of a warp are contiguous); its 8 warps sum the
+// splits s = w, w + 8, ... in order and warp 0 adds the 8 partial sums in warp order, so the result is
+// deterministic.  `n` is the workspace row stride (the MMA width, output channels rounded up to 16);
+// `oc` the real output channels, which alone bound the rows of dw that are written.
+constexpr int kReduceWarps = 8;
+__global__ void __launch_bounds__(32 * kReduceWarps)
+    wgrad_reduce_kernel(const float* ws, int splits, long split_stride, int n, int oc, int ic, int taps, int kchunks,
+                        float* dw, int accumulate) {
+    __shared__ float part[kReduceWarps][32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const long total = (long)oc * ic * taps;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const int o = (int)(i % oc);
-        const int tc = (int)(i / oc);
-        const int t = tc / ic, c = tc - t * ic;
-        const long row = (long)(t * kchunks + c / 32) * 32 + (c % 32);
-        const float* src = ws + row * n + o;
+    for (long base = (long)blockIdx.x * 32; base < total; base += (long)gridDim.x * 32) {
+        const long i = base + lane;
         float s = 0.0f;
-#pragma unroll 8
-        for (int k = 0; k < splits; k++) s += src[k * split_stride];
-        const long di = ((long)o * ic + c) * taps + t;
-        dw[di] = accumulate ? dw[di] + s : s;
+        long di = 0;
+        if (i < total) {
+            const int o = (int)(i % oc);
+            const int tc = (int)(i / oc);
+            const int t = tc / ic, c = tc - t * ic;
+            const long row = (long)(t * kchunks + c / 32) * 32 + (c % 32);
+            const float* src = ws + row * n + o;
+#pragma unroll 4
+            for (int k = w; k < splits; k += kReduceWarps) s += src[k * split_stride];
+            di = ((long)o * ic + c) * taps + t;
+        }
+        part[w][lane] = s;
+        __syncthreads();
+        if (w == 0 && i < total) {
+            float r = part[0][lane];
+#pragma unroll
+            for (int q = 1; q < kReduceWarps; q++) r += part[q][lane];
+            dw[di] = accumulate ? dw[di] + r : r;
+        }
+        __syncthreads();
     }
 }
 
@@ -1171,8 +1188,8 @@ void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, fl
     launch_check("conv_wgrad_tc_kernel");
     const long split_stride = (long)p.m_tiles * kTileM * p.n;
     const long total = (long)dy.channels * x.channels * taps;
-    const int blocks = (int)std::min<long>(4096, (total + 255) / 256);
-    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(ws, splits, split_stride, p.n, dy.channels, x.channels, taps,
+    const int blocks = (int)std::min<long>(8 * num_sms(), (total + 31) / 32);
+    wgrad_reduce_kernel<<<blocks, 32 * kReduceWarps, 0, stream>>>(ws, splits, split_stride, p.n, dy.channels, x.channels, taps,
                                                     p.kchunks, dw,
                                                     accumulate);
     launch_check("wgrad_reduce_kernel");
