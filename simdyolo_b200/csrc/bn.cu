@@ -306,18 +306,32 @@ __global__ void __launch_bounds__(kThreads) bias_partial_kernel(const float* gr,
     split_range(g.h * g.w, splits, s, p0, p1);
     float acc = 0.0f;
     if (ch < c) {
-        // pixel p -> (yy, xx) advanced incrementally (no division per pixel)
+        // pixel p -> (yy, xx) advanced incrementally (no division per pixel); four pixels per
+        // iteration into four running sums, so that four loads are in flight
         int p = p0 + warp;
         int yy = p / g.w, xx = p - yy * g.w;
         const float* img = gr + (long)b * g.rows * pitch + ch;
-        for (; p < p1; p += kWarps) {
-            acc += img[(long)g.row(yy, xx) * pitch];
+        auto next_row = [&]() {
+            const int r = g.row(yy, xx);
             xx += kWarps;
             while (xx >= g.w) {
                 xx -= g.w;
                 yy++;
             }
+            return r;
+        };
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        for (; p + 3 * kWarps < p1; p += 4 * kWarps) {
+            const int r0 = next_row(), r1 = next_row(), r2 = next_row(), r3 = next_row();
+            const float v0 = img[(long)r0 * pitch], v1 = img[(long)r1 * pitch];
+            const float v2 = img[(long)r2 * pitch], v3 = img[(long)r3 * pitch];
+            a0 += v0;
+            a1 += v1;
+            a2 += v2;
+            a3 += v3;
         }
+        for (; p < p1; p += kWarps) a0 += img[(long)next_row() * pitch];
+        acc = (a0 + a1) + (a2 + a3);
     }
     red[warp][lane] = acc;
     __syncthreads();
