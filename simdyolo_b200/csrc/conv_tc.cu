@@ -105,6 +105,8 @@ struct FwdParams {
     int alloc_cols;
     float* out;
     int out_pitch;
+    int out_tma;         // 1 (trunk epilogue): the output leaves through per-warp shared-memory tiles and TMA stores
+    int stage_bytes;     // shared memory of those tiles (4 KB per epilogue warp), before the A ring
     const float* bias;
     const float* residual;
     int res_pitch;
@@ -185,13 +187,13 @@ constexpr int kEpiPlain = 0, kEpiStats = 1, kEpiBnBwd = 2, kEpiGeneric = 3;
 template <int kEpiWarps, int kMode>
 __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
     conv_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                       const __grid_constant__ FwdParams p) {
+                       const __grid_constant__ CUtensorMap tmO, const __grid_constant__ FwdParams p) {
     constexpr int kEpiThreads = 32 * kEpiWarps;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int b_bytes = p.n * 128;          // one (tap, chunk) weight block; multiple of 2048
-    uint8_t* a_ring = smem;
-    uint8_t* b_region = smem + p.a_stages * p.a_stage_bytes;
+    uint8_t* a_ring = smem + p.stage_bytes;
+    uint8_t* b_region = a_ring + p.a_stages * p.a_stage_bytes;
     const bool resident = p.b_stages == 0;
     const int nb = resident ? 1 : p.b_stages;
     uint64_t* afull = reinterpret_cast<uint64_t*>(b_region + p.b_region_bytes);
@@ -235,6 +237,7 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
+        if (p.out_tma) prefetch_tmap(&tmO);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, p.alloc_cols);
@@ -389,6 +392,11 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
         const float* const pre_in = kAny ? p.pre : nullptr;
         const float* const res_in = kAny ? p.residual : nullptr;
         float* const phase_out = kAny ? p.phase : nullptr;
+        // trunk mode with out_tma: this warp's output tile, two halves of 32 rows x 16 channels (64 bytes
+        // a row) in the 64-byte swizzle of the output tensor map (16-byte chunk c of row r at chunk
+        // c ^ ((r >> 1) & 3)), so that the 32 rows of one st.shared.v4 fill four whole bank wavefronts
+        float* const stage_w = reinterpret_cast<float*>(smem) + (warp - kEpiWarp0) * 1024;
+        bool stage_busy = false;
         int local = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, local++) {
             const int acc = local % p.nacc;
@@ -488,7 +496,31 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
                                                     (long)(py >> 1) * p.phase_wp + (px >> 1);
                             prow = p.phase + prow_index * p.phase_pitch + j;
                         }
-                        float* orow = p.out ? p.out + m * (long)p.out_pitch + j : nullptr;
+                        float* orow = (p.out && !p.out_tma) ? p.out + m * (long)p.out_pitch + j : nullptr;
+                        if (p.out_tma) {
+                            // the previous stores of this tile have read it; rows in, one TMA store per
+                            // 16-channel half out (channels past n_valid are clipped by the tensor map)
+                            if (stage_busy && lane == 0) bulk_wait_read_all();
+                            __syncwarp();
+                            const int sw = (lane >> 1) & 3;
+                            float4* s0 = reinterpret_cast<float4*>(stage_w + lane * 16);
+                            float4* s1 = reinterpret_cast<float4*>(stage_w + 512 + lane * 16);
+#pragma unroll
+                            for (int u = 0; u < 4; u++) {
+                                s0[u ^ sw] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                                s1[u ^ sw] = make_float4(v[16 + 4 * u], v[16 + 4 * u + 1], v[16 + 4 * u + 2],
+                                                         v[16 + 4 * u + 3]);
+                            }
+                            fence_proxy_async();
+                            __syncwarp();
+                            if (lane == 0) {
+                                const int y0 = (int)(m - lane);
+                                tma_store_2d(&tmO, stage_w, j, y0);
+                                if (j + 16 < p.n_valid) tma_store_2d(&tmO, stage_w + 512, j + 16, y0);
+                                bulk_commit();
+                            }
+                            stage_busy = true;
+                        }
 #pragma unroll
                         for (int h = 0; h < 2; h++) {
                             if (h ? full1 : full0) {
@@ -733,6 +765,7 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
         }
+        if (stage_busy && lane == 0) bulk_wait_all();
     }
     __syncthreads();
     if (warp == 1) {
@@ -798,7 +831,8 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         attr_set = true;
     }
     CUtensorMap ta = make_map_2d(in.base, in.channels, in.rows, in.pitch, 32, kBoxRows);
-    constexpr int kSmemBudget = 216 * 1024;
+    constexpr int kSmemTotal = 216 * 1024;   // A ring + weights (+ the trunk epilogue's output tiles)
+    const bool plain_epilogue = !(ep.bn.grad_part || ep.bn.stats_part || ep.pre);
     for (int n0 = 0; n0 < n_out; n0 += 256) {
         const int n_valid = std::min(256, n_out - n0);
         const int n = (n_valid + 15) / 16 * 16;
@@ -814,54 +848,76 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
             for (int g = 0; g < ngroups; g++) rows = std::max(rows, kTileM * t_sub + g_span[g]);
             return (rows + kBoxRows - 1) / kBoxRows * kBoxRows * 128;
         };
-        for (int gap : {grid.wp + 2, 2}) {
-            ngroups = 0;
-            bool too_many = false;
-            for (int e = 0; e < taps; e++) {
-                const int t = order[e];
-                if (e == 0 || shift[t] - shift[order[e - 1]] > gap) {
-                    if (ngroups == kMaxGroups) {
-                        too_many = true;
-                        break;
+        // tap groups and sub-tiles per CTA tile (T = 0: nothing fits) for `budget` bytes of A ring + weights
+        auto plan = [&](int budget) {
+            for (int gap : {grid.wp + 2, 2}) {
+                ngroups = 0;
+                bool too_many = false;
+                for (int e = 0; e < taps; e++) {
+                    const int t = order[e];
+                    if (e == 0 || shift[t] - shift[order[e - 1]] > gap) {
+                        if (ngroups == kMaxGroups) {
+                            too_many = true;
+                            break;
+                        }
+                        g_lo[ngroups] = shift[t];
+                        g_span[ngroups] = 0;
+                        g_ntaps[ngroups] = 0;
+                        ngroups++;
                     }
-                    g_lo[ngroups] = shift[t];
-                    g_span[ngroups] = 0;
-                    g_ntaps[ngroups] = 0;
-                    ngroups++;
+                    const int g = ngroups - 1;
+                    tap_t[e] = t;
+                    tap_off[e] = shift[t] - g_lo[g];
+                    g_span[g] = tap_off[e];
+                    g_ntaps[g]++;
                 }
-                const int g = ngroups - 1;
-                tap_t[e] = t;
-                tap_off[e] = shift[t] - g_lo[g];
-                g_span[g] = tap_off[e];
-                g_ntaps[g]++;
-            }
-            if (too_many) continue;
-            // largest sub-tile count whose accumulators double-buffer in TMEM, whose A region fits
-            // twice next to the weights, and that still leaves two tiles per SM
-            T = 4;
-            while (T > 1 && (2 * T * acc_cols > 512 || 2 * stage_bytes(T) + b_min > kSmemBudget ||
-                             (sub_tiles + T - 1) / T < 2L * num_sms()))
-                T >>= 1;
-            if (!resident && (long)taps * kchunks * b_bytes >= 256 * 1024) {
-                // large streamed weights are fetched again for every CTA tile, so a small layer may run
-                // faster on fewer, larger tiles: the count of least estimated time among those that fit
-                // (measured: 18 % faster at 576-720 KB of weights a tile; at 144 KB the deeper weight
-                // ring of the smaller tile wins, so the rule above stands there)
-                double best = 0.0;
-                int pick = 0;
-                for (int t = 4; t >= 1; t >>= 1) {
-                    if (2 * t * acc_cols > 512 || 2 * stage_bytes(t) + b_min > kSmemBudget) continue;
-                    const double c = fwd_tile_cost(sub_tiles, t, stage_bytes(t), ngroups, kchunks, taps, b_bytes, n);
-                    if (pick == 0 || c < best) {
-                        pick = t;
-                        best = c;
+                if (too_many) continue;
+                // largest sub-tile count whose accumulators double-buffer in TMEM, whose A region fits
+                // twice next to the weights, and that still leaves two tiles per SM
+                T = 4;
+                while (T > 1 && (2 * T * acc_cols > 512 || 2 * stage_bytes(T) + b_min > budget ||
+                                 (sub_tiles + T - 1) / T < 2L * num_sms()))
+                    T >>= 1;
+                if (!resident && (long)taps * kchunks * b_bytes >= 256 * 1024) {
+                    // large streamed weights are fetched again for every CTA tile, so a small layer may run
+                    // faster on fewer, larger tiles: the count of least estimated time among those that fit
+                    // (measured: 18 % faster at 576-720 KB of weights a tile; at 144 KB the deeper weight
+                    // ring of the smaller tile wins, so the rule above stands there)
+                    double best = 0.0;
+                    int pick = 0;
+                    for (int t = 4; t >= 1; t >>= 1) {
+                        if (2 * t * acc_cols > 512 || 2 * stage_bytes(t) + b_min > budget) continue;
+                        const double c = fwd_tile_cost(sub_tiles, t, stage_bytes(t), ngroups, kchunks, taps, b_bytes, n);
+                        if (pick == 0 || c < best) {
+                            pick = t;
+                            best = c;
+                        }
                     }
+                    if (pick > 0) T = pick;
                 }
-                if (pick > 0) T = pick;
+                a_stage = stage_bytes(T);
+                if (2 * a_stage + b_min <= budget) return;
+                T = 0;
             }
-            a_stage = stage_bytes(T);
-            if (2 * a_stage + b_min <= kSmemBudget) break;
-            T = 0;
+        };
+        // the trunk epilogue sends its output through shared-memory tiles and TMA stores (8 warps x 4 KB)
+        // unless their room would cost sub-tiles per CTA tile, a finer tap grouping or (resident weights)
+        // an A stage that a layer of several tap groups uses; outputs of 16 channels (64-byte rows) keep
+        // the direct stores, which measured faster for them
+        int kSmemBudget = kSmemTotal, stage_total = 0;
+        plan(kSmemTotal);
+        if (plain_epilogue && out.base && T > 0 && n_valid > 16) {
+            const int T_full = T, groups_full = ngroups, staged = 8 * 4096;
+            auto a_ring_depth = [&](int budget) { return std::min(4, (budget - res_bytes) / a_stage); };
+            const int depth_full = resident ? a_ring_depth(kSmemTotal) : 0;
+            plan(kSmemTotal - staged);
+            const int depth = resident && T > 0 ? a_ring_depth(kSmemTotal - staged) : 0;
+            if (T == T_full && ngroups == groups_full && depth >= (ngroups > 1 ? depth_full : std::min(depth_full, 2))) {
+                kSmemBudget = kSmemTotal - staged;
+                stage_total = staged;
+            } else {
+                plan(kSmemTotal);
+            }
         }
         if (T == 0) throw std::runtime_error("conv_tc: haloed tile does not fit shared memory");
         FwdParams p;
@@ -908,6 +964,8 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         p.alloc_cols = pow2_at_least(p.nacc * T * p.ksplit * acc_cols);
         p.out = out.base ? out.base + n0 : nullptr;   // null: only the parity copy is written
         p.out_pitch = out.pitch;
+        p.out_tma = stage_total > 0 ? 1 : 0;
+        p.stage_bytes = stage_total;
         p.bias = ep.bias;
         p.residual = ep.residual ? ep.residual + n0 : nullptr;
         p.res_pitch = ep.res_pitch;
@@ -929,22 +987,24 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         if (p.alloc_cols > 512) throw std::runtime_error("conv_tc: TMEM columns");
         CUtensorMap tb = make_map_2d(wk, (long)taps * kpad, n_rows, (long)taps * kpad, 32, n);
         const int nb = resident ? 1 : p.b_stages;
-        const size_t smem = 1024 + (size_t)p.a_stages * a_stage + p.b_region_bytes +
+        const CUtensorMap to =
+            p.out_tma ? make_map_2d(p.out, n_valid, m_rows, out.pitch, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B) : ta;
+        const size_t smem = 1024 + (size_t)stage_total + (size_t)p.a_stages * a_stage + p.b_region_bytes +
                             (2 * p.a_stages + 2 * nb + 2 * p.nacc) * 8 + 16 + 80 + 16 + 3 * n * 4;
         if (smem > 227 * 1024) throw std::runtime_error("conv_tc: shared memory");
         const int grid_x = std::min(p.num_tiles, num_sms());
         // the specialised epilogues cover the launches without a pre-add whose features they implement
         const bool other = ep.pre || ((ep.bn.stats_part || ep.bn.grad_part) && (ep.residual || phase));
         if (ep.bn.grad_part && !other)
-            conv_fwd_tc_kernel<12, kEpiBnBwd><<<grid_x, fwd_threads(12), smem, stream>>>(ta, tb, p);
+            conv_fwd_tc_kernel<12, kEpiBnBwd><<<grid_x, fwd_threads(12), smem, stream>>>(ta, tb, to, p);
         else if (ep.bn.grad_part)
-            conv_fwd_tc_kernel<12, kEpiGeneric><<<grid_x, fwd_threads(12), smem, stream>>>(ta, tb, p);
+            conv_fwd_tc_kernel<12, kEpiGeneric><<<grid_x, fwd_threads(12), smem, stream>>>(ta, tb, to, p);
         else if (ep.bn.stats_part && !other)
-            conv_fwd_tc_kernel<8, kEpiStats><<<grid_x, fwd_threads(8), smem, stream>>>(ta, tb, p);
+            conv_fwd_tc_kernel<8, kEpiStats><<<grid_x, fwd_threads(8), smem, stream>>>(ta, tb, to, p);
         else if (ep.bn.stats_part || ep.pre)
-            conv_fwd_tc_kernel<8, kEpiGeneric><<<grid_x, fwd_threads(8), smem, stream>>>(ta, tb, p);
+            conv_fwd_tc_kernel<8, kEpiGeneric><<<grid_x, fwd_threads(8), smem, stream>>>(ta, tb, to, p);
         else
-            conv_fwd_tc_kernel<8, kEpiPlain><<<grid_x, fwd_threads(8), smem, stream>>>(ta, tb, p);
+            conv_fwd_tc_kernel<8, kEpiPlain><<<grid_x, fwd_threads(8), smem, stream>>>(ta, tb, to, p);
         launch_check("conv_fwd_tc_kernel");
     }
 }
