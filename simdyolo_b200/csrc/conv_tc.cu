@@ -1,10 +1,12 @@
 // tcgen05 implicit-GEMM convolutions for sm_100a (TF32 inputs, FP32 accumulation in TMEM).
 //
-// Forward / data-gradient kernel (conv_fwd_tc): persistent, one 128-row tile of the padded
-// activation matrix per iteration.  Warp 0 issues TMA loads (A: 128 rows x 32 channels of the
-// input, shifted by the tap's row offset; B: N rows x 32 k of the K-major weights), warp 1 issues
-// tcgen05.mma (K = 8 per instruction) into one of two TMEM accumulators, warps 2-5 drain the other
-// accumulator (bias, SiLU, residual, halo masking) while the next tile accumulates.
+// Forward / data-gradient kernel (conv_fwd_tc): persistent, one CTA tile of T 128-row sub-tiles of
+// the padded activation matrix per iteration.  Warp 0 issues TMA loads (A: haloed row regions x 32
+// channels of the input, read by every tap of a tap group at its row offset; B: N rows x 32 k of the
+// K-major weights), warp 1 performs every mbarrier wait of the MMA side, warps 2-3 issue tcgen05.mma
+// (K = 8 per instruction) into double-buffered TMEM accumulators, and warps 4.. drain the other
+// accumulator (bias, SiLU, shortcut, halo masking, BatchNorm partials) while the next tile
+// accumulates.
 //
 // Weight-gradient kernel (conv_wgrad_tc): split-K over pixel rows.  Both operands are read in
 // their natural channels-last layout and fed to the tensor cores as MN-major (transposed)
@@ -380,7 +382,8 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
             mma_commit_elect(&tfull[acc]);
         }
     } else {
-        // three warps per TMEM lane quadrant; they take every third (sub-tile, 16-column chunk) item.
+        // kEpiWarps / 4 warps per TMEM lane quadrant; each takes every (kEpiWarps / 4)-th (sub-tile,
+        // column chunk) item.
         // Global loads of an item (residual, BatchNorm input and coefficients) are issued before
         // its TMEM load so that their latencies overlap.
         const int q = warp & 3;
