@@ -12,6 +12,19 @@ namespace sy {
 // Raises when the most recent kernel launch on this thread failed (bad configuration, etc.).
 // Every launch site calls it once, so it also counts this library's kernel launches.
 void launch_check(const char* what);
+
+// True the first time it is called with `devices` while a given device is current (for per-device
+// one-time set-up such as kernel attributes, which CUDA keeps per device); always true on device
+// ordinals of 64 and above.
+inline bool once_per_device(uint64_t& devices) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return true;
+    const uint64_t bit = 1ull << dev;
+    if (devices & bit) return false;
+    devices |= bit;
+    return true;
+}
 long long launch_count();
 
 // ---------------------------------------------------------------- tensor views

@@ -649,11 +649,9 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
     if (max_boxes > 0) topk_kernel<<<dim3(max_boxes, batch), 256, 0, stream>>>(p);
     launch_check("topk_kernel");
     const size_t owner_bytes = sizeof(int) * (size_t)p.anchors;
-    static bool assign_attr = false;
-    if (!assign_attr) {
+    static uint64_t attr_devices = 0;   // devices whose kernel attribute is set
+    if (once_per_device(attr_devices))
         cudaFuncSetAttribute(assign_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-        assign_attr = true;
-    }
     if (owner_bytes > 160 * 1024) throw std::runtime_error("detection_loss: too many anchors");
     assign_kernel<<<batch, 256, owner_bytes, stream>>>(p);
     launch_check("assign_kernel");
