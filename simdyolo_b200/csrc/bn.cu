@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kFoldWarps * 32) bn_stats_fold_kernel(const fl
 // blockIdx.y.
 template <bool kVec>
 __global__ void bn_apply_kernel(const float* y, int ypitch, const float* mean_p, const float* inv_p,
-                                const float* gamma, const float* beta, int c, Grid g, float* a, int apitch) {
+                                const float* gamma, const float* beta, int c, Grid g, float* a, int apitch, int rnd) {
     const int b = blockIdx.y;
     const int per_row = kVec ? c / 4 : c;
     const int total = g.rows * per_row;   // < 2^22 (checked by the launcher)
@@ -129,12 +129,13 @@ __global__ void bn_apply_kernel(const float* y, int ypitch, const float* mean_p,
                 out.y = silu_f((v.y - mv.y) * iv.y * gamma[ch + 1] + beta[ch + 1]);
                 out.z = silu_f((v.z - mv.z) * iv.z * gamma[ch + 2] + beta[ch + 2]);
                 out.w = silu_f((v.w - mv.w) * iv.w * gamma[ch + 3] + beta[ch + 3]);
+                if (rnd) out = make_float4(tf32_rna(out.x), tf32_rna(out.y), tf32_rna(out.z), tf32_rna(out.w));
             }
             *reinterpret_cast<float4*>(a + row * apitch + 4 * j) = out;
         } else {
             float out = 0.0f;
             if (in) out = silu_f((y[row * ypitch + j] - mb[j]) * ib[j] * gamma[j] + beta[j]);
-            a[row * apitch + j] = out;
+            a[row * apitch + j] = rnd ? tf32_rna(out) : out;
         }
     }
 }
@@ -203,7 +204,7 @@ __global__ void bn_param_grad_kernel(const float* red, int batch, int c, float* 
 template <bool kVec>
 __global__ void bn_bwd_apply_kernel(const float* y, int ypitch, const float* dz, int zpitch, const float* mean_p,
                                     const float* inv_p, const float* f_p, const float* red, int c, float n, Grid g,
-                                    float* dy, int dpitch) {
+                                    float* dy, int dpitch, int rnd) {
     const int b = blockIdx.y;
     const int per_row = kVec ? c / 4 : c;
     const int total = g.rows * per_row;   // < 2^22 (checked by the launcher)
@@ -232,13 +233,14 @@ __global__ void bn_bwd_apply_kernel(const float* y, int ypitch, const float* dz,
                 out.y = fv.y * (n * zv.y - r0.z - (yv.y - mv.y) * iv.y * r0.w);
                 out.z = fv.z * (n * zv.z - r1.x - (yv.z - mv.z) * iv.z * r1.y);
                 out.w = fv.w * (n * zv.w - r1.z - (yv.w - mv.w) * iv.w * r1.w);
+                if (rnd) out = make_float4(tf32_rna(out.x), tf32_rna(out.y), tf32_rna(out.z), tf32_rna(out.w));
             }
             *reinterpret_cast<float4*>(dy + row * dpitch + 4 * j) = out;
         } else {
             float out = 0.0f;
             if (in)
                 out = fb[j] * (n * dz[row * zpitch + j] - rb[2 * j] - (y[row * ypitch + j] - mb[j]) * ib[j] * rb[2 * j + 1]);
-            dy[row * dpitch + j] = out;
+            dy[row * dpitch + j] = rnd ? tf32_rna(out) : out;
         }
     }
 }
@@ -361,6 +363,147 @@ __global__ void bias_fold_kernel(const float* per_image, int batch, int c, float
     db[ch] = acc;
 }
 
+// ---------------------------------------------------------------- centred weight gradient (kernels.h)
+// Partial sums of x over a slice of the interior pixels of one image: block (32 channels, image, slice),
+// lane = channel, warp w takes pixels w, w + 8, ... of the slice into four running sums (four loads in
+// flight); the warps' sums are added in warp order.  part[(b * splits + s) * c + ch].
+__global__ void __launch_bounds__(kThreads) feature_sum_kernel(const float* x, int pitch, int c, Grid g, int splits,
+                                                               float* part) {
+    __shared__ float red[kWarps][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int ch = blockIdx.x * 32 + lane, b = blockIdx.y, s = blockIdx.z;
+    int p0, p1;
+    split_range(g.h * g.w, splits, s, p0, p1);
+    float acc = 0.0f;
+    if (ch < c) {
+        const float* img = x + (long)b * g.rows * pitch + ch;
+        float a[4] = {0.f, 0.f, 0.f, 0.f};
+        int p = p0 + warp;
+        for (; p + 3 * kWarps < p1; p += 4 * kWarps) {
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int q = p + k * kWarps, yy = q / g.w, xx = q - yy * g.w;
+                a[k] += img[(long)g.row(yy, xx) * pitch];
+            }
+        }
+        for (; p < p1; p += kWarps) {
+            const int yy = p / g.w, xx = p - yy * g.w;
+            a[0] += img[(long)g.row(yy, xx) * pitch];
+        }
+        acc = (a[0] + a[1]) + (a[2] + a[3]);
+    }
+    red[warp][lane] = acc;
+    __syncthreads();
+    if (warp == 0 && ch < c) {
+        float t = 0.0f;
+        for (int w = 0; w < kWarps; w++) t += red[w][lane];
+        part[((long)b * splits + s) * c + ch] = t;
+    }
+}
+
+// mean[b][ch] = (sum of the slices in order) / pixels
+__global__ void feature_mean_fold_kernel(const float* part, int batch, int c, int splits, float inv_pixels,
+                                         float* mean) {
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)batch * c) return;
+    const int b = (int)(i / c), ch = (int)(i - (long)b * c);
+    double t = 0.0;
+    for (int s = 0; s < splits; s++) t += part[((long)b * splits + s) * c + ch];
+    mean[i] = (float)(t * inv_pixels);
+}
+
+// xc = x - mean[b][ch] at interior rows, 0 elsewhere; one image per blockIdx.y, float4 when kVec.
+template <bool kVec>
+__global__ void feature_center_kernel(const float* x, int xpitch, const float* mean, int c, Grid g, float* xc,
+                                      int cpitch, int rnd) {
+    const int b = blockIdx.y;
+    const int per_row = kVec ? c / 4 : c;
+    const int total = g.rows * per_row;   // < 2^22 (checked by the launcher)
+    const float inv_row = 1.0f / (float)per_row, inv_wp = 1.0f / (float)g.wp;
+    const long base = (long)b * g.rows;
+    const float* mb = mean + (long)b * c;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int r = fast_div(i, inv_row), j = i - r * per_row;
+        const long row = base + r;
+        const int py = fast_div(r, inv_wp), px = r - py * g.wp;
+        const bool in = py >= 1 && py <= g.h && px >= 1 && px <= g.w;
+        if (kVec) {
+            float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (in) {
+                const float4 v = *reinterpret_cast<const float4*>(x + row * xpitch + 4 * j);
+                const float4 m = *reinterpret_cast<const float4*>(mb + 4 * j);
+                out = make_float4(v.x - m.x, v.y - m.y, v.z - m.z, v.w - m.w);
+                if (rnd) out = make_float4(tf32_rna(out.x), tf32_rna(out.y), tf32_rna(out.z), tf32_rna(out.w));
+            }
+            *reinterpret_cast<float4*>(xc + row * cpitch + 4 * j) = out;
+        } else {
+            float out = in ? x[row * xpitch + j] - mb[j] : 0.0f;
+            xc[row * cpitch + j] = rnd ? tf32_rna(out) : out;
+        }
+    }
+}
+
+// Edge-strip sums of dy per (image, channel): block (32 channels, image), lane = channel; warp w takes
+// strip elements w, w + 8, ... of the top row, bottom row, left column and right column (double, warps
+// added in order).  With `part` the sum over all interior pixels is taken from its slices
+// (feature_sum_kernel), else it is 0: the gradient of a conv that feeds a per-image BatchNorm sums to
+// exactly zero over the pixels of each (image, channel), so the identity holds with the exact value 0,
+// and the rounding of the stored dy then stays out of the correction.
+// T[b][t][o]: tap t = (ky, kx) reads source offset (ky - 1, kx - 1), which leaves the map for the top row
+// when ky = 0, the bottom row when ky = 2, and likewise for the columns (inclusion-exclusion adds the
+// corner back).
+__global__ void __launch_bounds__(kFoldWarps * 32) tap_border_sums_kernel(const float* dy, int pitch, int c, Grid g,
+                                                                          int taps, const float* part, int splits,
+                                                                          float* tsum) {
+    __shared__ double r[4][kFoldWarps][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int ch = blockIdx.x * 32 + lane, b = blockIdx.y;
+    const float* img = dy + (long)b * g.rows * pitch + ch;
+    double e[4] = {0.0, 0.0, 0.0, 0.0};   // top, bottom, left, right
+    if (ch < c && taps == 9) {
+        const int n = 2 * g.w + 2 * g.h;
+        for (int k = warp; k < n; k += kFoldWarps) {
+            int yy, xx, side;
+            if (k < g.w) {
+                side = 0; yy = 0; xx = k;
+            } else if (k < 2 * g.w) {
+                side = 1; yy = g.h - 1; xx = k - g.w;
+            } else if (k < 2 * g.w + g.h) {
+                side = 2; yy = k - 2 * g.w; xx = 0;
+            } else {
+                side = 3; yy = k - 2 * g.w - g.h; xx = g.w - 1;
+            }
+            e[side] += img[(long)g.row(yy, xx) * pitch];
+        }
+    }
+    for (int k = 0; k < 4; k++) r[k][warp][lane] = e[k];
+    __syncthreads();
+    if (warp != 0 || ch >= c) return;
+    double t[4] = {0.0, 0.0, 0.0, 0.0};
+    for (int k = 0; k < 4; k++)
+        for (int w = 0; w < kFoldWarps; w++) t[k] += r[k][w][lane];
+    double total = 0.0;
+    if (part)
+        for (int s = 0; s < splits; s++) total += part[((long)b * splits + s) * c + ch];
+    float* out = tsum + (long)b * taps * c + ch;
+    if (taps == 1) {
+        out[0] = (float)total;
+        return;
+    }
+    const double corner[2][2] = {{img[(long)g.row(0, 0) * pitch], img[(long)g.row(0, g.w - 1) * pitch]},
+                                 {img[(long)g.row(g.h - 1, 0) * pitch], img[(long)g.row(g.h - 1, g.w - 1) * pitch]}};
+    for (int ky = 0; ky < 3; ky++)
+        for (int kx = 0; kx < 3; kx++) {
+            double v = total;
+            if (ky == 0) v -= t[0];
+            if (ky == 2) v -= t[1];
+            if (kx == 0) v -= t[2];
+            if (kx == 2) v -= t[3];
+            if (ky != 1 && kx != 1) v += corner[ky == 2][kx == 2];
+            out[(long)(ky * 3 + kx) * c] = (float)v;
+        }
+}
+
 }  // namespace
 
 size_t bn_workspace_floats(int batch, int channels) { return (size_t)batch * 64 * channels * 3; }
@@ -390,18 +533,19 @@ void bn_eval_coef(const float* rmean, const float* rvar, float eps, int batch, i
 }
 
 void bn_silu_apply(const View& y, const float* coef, const float* gamma, const float* beta, int batch, const Grid& g,
-                   const View& a, cudaStream_t stream) {
+                   const View& a, cudaStream_t stream, bool round_tf32) {
     const int c = y.channels;
+    const int rnd = round_tf32 ? 1 : 0;
     const bool vec = c % 4 == 0 && y.pitch % 4 == 0 && a.pitch % 4 == 0;
     const long per_image = (long)g.rows * (vec ? c / 4 : c);
     if (per_image >= (1L << 22)) throw std::runtime_error("bn_silu_apply: image too large");
     const float* inv = coef + (long)batch * c;
     if (vec)
         bn_apply_kernel<true><<<image_grid(per_image, batch), 256, 0, stream>>>(y.base, y.pitch, coef, inv, gamma,
-                                                                                beta, c, g, a.base, a.pitch);
+                                                                                beta, c, g, a.base, a.pitch, rnd);
     else
         bn_apply_kernel<false><<<image_grid(per_image, batch), 256, 0, stream>>>(y.base, y.pitch, coef, inv, gamma,
-                                                                                 beta, c, g, a.base, a.pitch);
+                                                                                 beta, c, g, a.base, a.pitch, rnd);
     launch_check("bn_apply_kernel");
 }
 
@@ -431,8 +575,9 @@ void bn_backward_fold(const float* part, int batch, const Grid& g, int c, const 
 }
 
 void bn_backward_apply(const View& y, const View& dz, const float* coef, const float* bcoef, int batch, const Grid& g,
-                       const View& dy, cudaStream_t stream) {
+                       const View& dy, cudaStream_t stream, bool round_tf32) {
     const int c = y.channels;
+    const int rnd = round_tf32 ? 1 : 0;
     const bool vec = c % 4 == 0 && y.pitch % 4 == 0 && dz.pitch % 4 == 0 && dy.pitch % 4 == 0;
     const long per_image = (long)g.rows * (vec ? c / 4 : c);
     if (per_image >= (1L << 22)) throw std::runtime_error("bn_backward_apply: image too large");
@@ -441,11 +586,57 @@ void bn_backward_apply(const View& y, const View& dz, const float* coef, const f
     const float n = (float)(g.h * g.w);
     if (vec)
         bn_bwd_apply_kernel<true><<<image_grid(per_image, batch), 256, 0, stream>>>(
-            y.base, y.pitch, dz.base, dz.pitch, coef, inv, bcoef, red, c, n, g, dy.base, dy.pitch);
+            y.base, y.pitch, dz.base, dz.pitch, coef, inv, bcoef, red, c, n, g, dy.base, dy.pitch, rnd);
     else
         bn_bwd_apply_kernel<false><<<image_grid(per_image, batch), 256, 0, stream>>>(
-            y.base, y.pitch, dz.base, dz.pitch, coef, inv, bcoef, red, c, n, g, dy.base, dy.pitch);
+            y.base, y.pitch, dz.base, dz.pitch, coef, inv, bcoef, red, c, n, g, dy.base, dy.pitch, rnd);
     launch_check("bn_bwd_apply_kernel");
+}
+
+static int center_splits(int batch, int channels, const Grid& g) {
+    const int cgroups = (channels + 31) / 32;
+    const int want = (148 * 4 + cgroups * batch - 1) / (cgroups * batch);
+    return std::max(1, std::min({want, 64, std::max(1, g.h * g.w / 256)}));
+}
+
+size_t center_workspace_floats(int batch, int channels) { return (size_t)batch * 64 * channels; }
+
+void center_features(const View& x, int batch, const Grid& g, float* mean, float* ws, const View& xc,
+                     bool round_tf32, cudaStream_t stream) {
+    const int c = x.channels;
+    const int splits = center_splits(batch, c, g);
+    feature_sum_kernel<<<dim3((c + 31) / 32, batch, splits), kThreads, 0, stream>>>(x.base, x.pitch, c, g, splits, ws);
+    launch_check("feature_sum_kernel");
+    feature_mean_fold_kernel<<<(int)(((long)batch * c + 127) / 128), 128, 0, stream>>>(ws, batch, c, splits,
+                                                                                         1.0f / (float)(g.h * g.w), mean);
+    launch_check("feature_mean_fold_kernel");
+    const bool vec = c % 4 == 0 && x.pitch % 4 == 0 && xc.pitch % 4 == 0;
+    const long per_image = (long)g.rows * (vec ? c / 4 : c);
+    if (per_image >= (1L << 22)) throw std::runtime_error("center_features: image too large");
+    const int rnd = round_tf32 ? 1 : 0;
+    if (vec)
+        feature_center_kernel<true><<<image_grid(per_image, batch), 256, 0, stream>>>(x.base, x.pitch, mean, c, g,
+                                                                                      xc.base, xc.pitch, rnd);
+    else
+        feature_center_kernel<false><<<image_grid(per_image, batch), 256, 0, stream>>>(x.base, x.pitch, mean, c, g,
+                                                                                       xc.base, xc.pitch, rnd);
+    launch_check("feature_center_kernel");
+}
+
+void tap_border_sums(const View& dy, int batch, const Grid& g, int taps, bool zero_total, float* ws, float* tsum,
+                     cudaStream_t stream) {
+    if (taps != 1 && taps != 9) throw std::runtime_error("tap_border_sums: taps must be 1 or 9");
+    const int c = dy.channels;
+    int splits = 0;
+    if (!zero_total) {
+        splits = center_splits(batch, c, g);
+        feature_sum_kernel<<<dim3((c + 31) / 32, batch, splits), kThreads, 0, stream>>>(dy.base, dy.pitch, c, g, splits,
+                                                                                      ws);
+        launch_check("feature_sum_kernel");
+    }
+    tap_border_sums_kernel<<<dim3((c + 31) / 32, batch), kFoldWarps * 32, 0, stream>>>(
+        dy.base, dy.pitch, c, g, taps, zero_total ? nullptr : ws, splits, tsum);
+    launch_check("tap_border_sums_kernel");
 }
 
 void bn_running_update(const float* stats, long rank_stride, int ranks, int batch, int c, int spatial, float momentum,

@@ -131,6 +131,15 @@ __device__ __forceinline__ float det_pow6(float x) {
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
 
+// x rounded to the nearest TF32 value (10 explicit mantissa bits, ties away from zero).  The tensor
+// core reads an FP32 operand of a kind::tf32 MMA by dropping its low 13 mantissa bits, which shrinks
+// every product by about 2^-10 on average; operands stored already rounded make that error unbiased.
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
 // ------------------------------------------------------------------------------------------
 // Warp / block reductions
 // ------------------------------------------------------------------------------------------
@@ -186,15 +195,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait: gives up after `limit` polls and reports through *err (never traps).
 // The limit is far above any legitimate wait (each try_wait already suspends for a while).
 constexpr uint32_t kSpinLimit = 1u << 22;
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* err, int code, uint32_t limit) {
     uint32_t n = 0;
     while (!mbar_try_wait(bar, parity)) {
-        if (++n > kSpinLimit) {
+        if (++n > limit) {
             if (err) atomicExch(err, code);
             return false;
         }
     }
     return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+    return mbar_wait_limit(bar, parity, err, code, kSpinLimit);
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {

@@ -123,6 +123,7 @@ struct FwdParams {
     long phase_stride;   // rows between parity planes (batch * phase_rows)
     const float* pre;    // added to the accumulator first (3xTF32 passes)
     int pre_pitch;
+    int rnd;             // stored outputs rounded to the nearest TF32 (operands of the next TF32 conv)
     BnEpilogue bn;       // BatchNorm partials (see kernels.h)
     int* err;
     int sub_per_img;     // 128-row sub-tiles per image (grid.rows / 128)
@@ -491,6 +492,10 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
 #pragma unroll
                             for (int u = 0; u < 32; u++) v[u] = 0.0f;
                         }
+                        if (p.rnd) {
+#pragma unroll
+                            for (int u = 0; u < 32; u++) v[u] = tf32_rna(v[u]);
+                        }
                         float* prow = nullptr;
                         if (p.phase && inside) {
                             const int py = fast_div(r, p.inv_wp), px = r - py * p.grid.wp;
@@ -739,6 +744,10 @@ __global__ void __launch_bounds__(fwd_threads(kEpiWarps), 1)
                         o[1] = s2;
                     }
                 }
+                if (p.rnd) {
+#pragma unroll
+                    for (int u = 0; u < 16; u++) v[u] = tf32_rna(v[u]);
+                }
                 if (full16) {
                     if (orow) {
                         float4* dst = reinterpret_cast<float4*>(orow + j);
@@ -982,6 +991,7 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         p.bn = ep.bn;
         p.pre = ep.pre ? ep.pre + n0 : nullptr;
         p.pre_pitch = ep.pre_pitch;
+        p.rnd = ep.round_tf32;
         p.err = err;
         p.sub_per_img = grid.rows / kTileM;
         p.inv_wp = 1.0f / (float)grid.wp;
@@ -1189,11 +1199,12 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
 // consecutive outputs (o fastest, so the workspace reads of a warp are contiguous); its 8 warps sum the
 // splits s = w, w + 8, ... in order and warp 0 adds the 8 partial sums in warp order, so the result is
 // deterministic.  `n` is the workspace row stride (the MMA width, output channels rounded up to 16);
-// `oc` the real output channels, which alone bound the rows of dw that are written.
+// `oc` the real output channels, which alone bound the rows of dw that are written.  With a centred input
+// (WgradCenter) warp 0 also adds sum_b mean[b][c] tsum[b][t][o] (double, images in order).
 constexpr int kReduceWarps = 8;
 __global__ void __launch_bounds__(32 * kReduceWarps)
     wgrad_reduce_kernel(const float* ws, int splits, long split_stride, int n, int oc, int ic, int taps, int kchunks,
-                        float* dw, int accumulate) {
+                        float* dw, int accumulate, WgradCenter center) {
     __shared__ float part[kReduceWarps][32];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const long total = (long)oc * ic * taps;
@@ -1217,6 +1228,15 @@ __global__ void __launch_bounds__(32 * kReduceWarps)
             float r = part[0][lane];
 #pragma unroll
             for (int q = 1; q < kReduceWarps; q++) r += part[q][lane];
+            if (center.mean) {
+                const int o = (int)(i % oc);
+                const int tc = (int)(i / oc);
+                const int t = tc / ic, c = tc - t * ic;
+                double corr = 0.0;
+                for (int b = 0; b < center.batch; b++)
+                    corr += (double)center.mean[(long)b * ic + c] * center.tsum[((long)b * taps + t) * oc + o];
+                r += (float)corr;
+            }
             dw[di] = accumulate ? dw[di] + r : r;
         }
         __syncthreads();
@@ -1241,7 +1261,7 @@ size_t wgrad_workspace_floats(int ic, int oc, int taps, long rows) {
 }
 
 void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, float* dw, float* ws, int* err,
-                   cudaStream_t stream, int accumulate) {
+                   cudaStream_t stream, int accumulate, const WgradCenter* center) {
     if (dy.channels > 256) throw std::runtime_error("conv_tc_wgrad: more than 256 output channels");
     if (x.rows != dy.rows) throw std::runtime_error("conv_tc_wgrad: row mismatch");
     WgradParams p;
@@ -1284,7 +1304,7 @@ void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, fl
     const int blocks = (int)std::min<long>(8 * num_sms(), (total + 31) / 32);
     wgrad_reduce_kernel<<<blocks, 32 * kReduceWarps, 0, stream>>>(ws, splits, split_stride, p.n, dy.channels, x.channels, taps,
                                                     p.kchunks, dw,
-                                                    accumulate);
+                                                    accumulate, center ? *center : WgradCenter{});
     launch_check("wgrad_reduce_kernel");
 }
 

@@ -23,7 +23,7 @@ __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast
 __global__ void __launch_bounds__(kDwThreads) dw_conv_kernel(const float* x, int xpitch, long xrows, const float* w,
                                                              int taps, int sign, int c, Grid g, float* y, int ypitch,
                                                              const float* bias, const float* res, int rpitch,
-                                                             BnEpilogue bn) {
+                                                             BnEpilogue bn, int rnd) {
     __shared__ float w_s[32 * 9];
     __shared__ float red[32][33];
     __shared__ float red2[32][33];
@@ -79,7 +79,11 @@ __global__ void __launch_bounds__(kDwThreads) dw_conv_kernel(const float* x, int
             v[k] = v[k] * (sg + z * sg * (1.0f - sg));
         }
     }
-    if (on) *reinterpret_cast<float4*>(y + m * ypitch + ch) = make_float4(v[0], v[1], v[2], v[3]);
+    if (on) {
+        float4 o = make_float4(v[0], v[1], v[2], v[3]);
+        if (rnd) o = make_float4(tf32_rna(o.x), tf32_rna(o.y), tf32_rna(o.z), tf32_rna(o.w));
+        *reinterpret_cast<float4*>(y + m * ypitch + ch) = o;
+    }
     if (!bn.stats_part && !bn.grad_part) return;
 #pragma unroll
     for (int k = 0; k < 4; k++) {
@@ -193,7 +197,7 @@ static void check_dw(const View& x, const View& y, int taps) {
 }
 
 void dw_conv(const View& x, const float* w, int taps, int shift_sign, const Grid& g, const View& y, const BnEpilogue& bn,
-             cudaStream_t stream, const float* bias, const View* residual) {
+             cudaStream_t stream, const float* bias, const View* residual, bool round_tf32) {
     check_dw(x, y, taps);
     if (y.rows % 32 != 0) throw std::runtime_error("dw_conv: rows must be whole 32-row groups");
     if ((bn.stats_part || bn.grad_part) && bn.channels < y.channels)
@@ -203,7 +207,7 @@ void dw_conv(const View& x, const float* w, int taps, int shift_sign, const Grid
         throw std::runtime_error("dw_conv: residual not 16-byte aligned");
     dw_conv_kernel<<<grid, kDwThreads, 0, stream>>>(x.base, x.pitch, x.rows, w, taps, shift_sign, y.channels, g, y.base,
                                                    y.pitch, bias, residual ? residual->base : nullptr,
-                                                   residual ? residual->pitch : 0, bn);
+                                                   residual ? residual->pitch : 0, bn, round_tf32 ? 1 : 0);
     launch_check("dw_conv_kernel");
 }
 

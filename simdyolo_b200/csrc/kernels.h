@@ -71,6 +71,7 @@ struct ConvEpilogue {
     int mask_halo = 1;                // 0: every row is a valid output (plain GEMM use)
     const float* pre = nullptr;       // added to the accumulator before anything else (3xTF32 passes)
     int pre_pitch = 0;
+    int round_tf32 = 0;               // store outputs rounded to the nearest TF32 (operands of a TF32 conv)
     BnEpilogue bn{};
 };
 
@@ -97,11 +98,39 @@ void conv_tc_strided(const View& phase_in, long plane_rows, long m_rows, const f
                      const View& out, const ConvEpilogue& ep, int* err, cudaStream_t stream,
                      const PhaseOut* phase = nullptr);
 
+// Centred weight gradient of a conv that reads the frozen features (the first conv of every head
+// branch).  Those features carry a large per-(image, channel) mean against a BatchNorm gradient dy whose
+// per-(image, channel) sum vanishes, so sum_m x dy cancels heavily and the tensor core's FP32
+// accumulation loses accuracy in proportion.  With xc = x - mean at interior rows (0 at halo rows) the
+// identity
+//   sum_m x[m + s] dy[m] = sum_m xc[m + s] dy[m] + mean * T[s],  T[s] = sum of dy[m] over the interior m
+//                                                                 whose tap source m + s is interior
+// moves the mean into a small exact correction: conv_tc_wgrad runs on xc, the reduce adds
+// sum_b mean[b][c] T[b][t][o].
+struct WgradCenter {
+    const float* mean = nullptr;   // [batch][ic]
+    const float* tsum = nullptr;   // [batch][taps][oc]
+    int batch = 0;
+};
+// mean[b][c] over the interior pixels of image b; xc = x - mean at interior rows, 0 at halo / tail rows
+// (rounded to the nearest TF32 when round_tf32).  Any per-(image, channel) constant makes the identity
+// exact; the mean makes xc small.  ws: center_workspace_floats(batch, channels) floats.
+size_t center_workspace_floats(int batch, int channels);
+void center_features(const View& x, int batch, const Grid& g, float* mean, float* ws, const View& xc, bool round_tf32,
+                     cudaStream_t stream);
+// T[b][t][o] of the identity above for dy (taps 1 or 9) from the four edge strips and corners of every
+// (image, channel) and the sum over all interior pixels, which is taken as exactly 0 with zero_total (dy
+// is the gradient of a conv followed by a per-image BatchNorm, whose backward sums to zero over the pixels
+// of each (image, channel)).  ws: center_workspace_floats(batch, dy channels) floats.
+void tap_border_sums(const View& dy, int batch, const Grid& g, int taps, bool zero_total, float* ws, float* tsum,
+                     cudaStream_t stream);
+
 // Weight gradient: dw[o, c, t] = sum_m dy[m, o] * x[m + shift[t], c], written to `dw` in OIHW order
 // (dw[(o * ic + c) * taps + t]), fully overwritten.  `ws` is scratch of wgrad_workspace_floats() floats.
 size_t wgrad_workspace_floats(int ic, int oc, int taps, long rows);
 void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, float* dw, float* ws, int* err,
-                   cudaStream_t stream, int accumulate = 0);   // accumulate: dw += instead of dw =
+                   cudaStream_t stream, int accumulate = 0,   // accumulate: dw += instead of dw =
+                   const WgradCenter* center = nullptr);      // x is centred: the reduce adds the correction
 // 3xTF32 operand split of a view's channels: big = x rounded to TF32 (nearest, ties away), small =
 // x - big (exact); both written with the view's pitch at the same row / channel positions.
 void tf32_split(const View& src, float* big, float* small, cudaStream_t stream);
@@ -112,8 +141,9 @@ void tf32_split(const View& src, float* big, float* small, cudaStream_t stream);
 // data gradient.  `bn` as for the tensor-core epilogue: forward statistics partials, or the BatchNorm
 // backward of the layer whose gradient this pass produces (y then receives dz).
 // Optional per-channel `bias` and `residual` (same rows; may be y itself) are added after the sum.
+// round_tf32: store y rounded to the nearest TF32 (when y feeds a TF32 tensor-core conv).
 void dw_conv(const View& x, const float* w, int taps, int shift_sign, const Grid& g, const View& y, const BnEpilogue& bn,
-             cudaStream_t stream, const float* bias = nullptr, const View* residual = nullptr);
+             cudaStream_t stream, const float* bias = nullptr, const View* residual = nullptr, bool round_tf32 = false);
 // Multi-head self-attention of the YOLO11 C2PSA block over the interior pixels of each image
 // (PtModel.cs Attention, :429-439): qkv holds per head [q key_dim | k key_dim | v head_dim] channels;
 // att[token][h * head_dim + d] = sum_j softmax_j(q_i . k_j * scale) v_j[d]; v_out receives v in that
@@ -125,7 +155,9 @@ size_t dw_wgrad_workspace_floats(int c, int taps, long rows);
 void dw_wgrad(const View& x, const View& dy, int taps, const Grid& g, float* dw, float* ws, cudaStream_t stream);
 
 // ---------------------------------------------------------------- layout helpers (layout.cu)
-void nchw_to_padded(const float* src, int batch, int c, const Grid& g, const View& dst, cudaStream_t stream);
+// round_tf32 (here and below): values stored rounded to the nearest TF32, for a TF32 tensor-core consumer.
+void nchw_to_padded(const float* src, int batch, int c, const Grid& g, const View& dst, cudaStream_t stream,
+                    bool round_tf32 = false);
 void padded_to_nchw(const View& src, int batch, int c, const Grid& g, float* dst, cudaStream_t stream);
 void rgb_to_padded(const uint8_t* rgb, int batch, int size, const Grid& g, const View& dst, cudaStream_t stream);
 // Letterboxed RGB24 (identity scale, value / 255) written as the parity-split input of the stem.
@@ -135,9 +167,10 @@ void rgb_to_phase(const uint8_t* rgb, int batch, int size, const PhaseOut& dst, 
 // padded output (skipped when out.base is null) and, when `phase` is given, its parity-split copy.
 // w_host / bias_host: HOST copies, OIHW [oc][3][3][3] (they travel as kernel parameters).
 void stem_conv(const uint8_t* rgb, int batch, int size, const float* w_host, const float* bias_host, int oc,
-               const View& out, const Grid& gout, const PhaseOut* phase, cudaStream_t stream);
+               const View& out, const Grid& gout, const PhaseOut* phase, cudaStream_t stream, bool round_tf32 = false);
 // OIHW -> [oc][t][kpad] (forward) and OIHW -> [ic][t][kpad_o] (data gradient)
-void weights_fwd_layout(const float* oihw, int oc, int ic, int taps, int kpad, float* dst, cudaStream_t stream);
+void weights_fwd_layout(const float* oihw, int oc, int ic, int taps, int kpad, float* dst, cudaStream_t stream,
+                        bool round_tf32 = false);
 void weights_dgrad_layout(const float* oihw, int oc, int ic, int taps, int kpad_o, float* dst, cudaStream_t stream);
 // Both layouts of many conv weights in one launch: table[i] describes weight tensor i (device array).
 struct WeightLayoutJob {
@@ -146,7 +179,8 @@ struct WeightLayoutJob {
     float* fwd;     // [oc][taps][kpad_in]
     float* dgrad;   // [ic][taps][kpad_out]
 };
-void weights_layout_batch(const WeightLayoutJob* table_device, int jobs, long max_elems, cudaStream_t stream);
+void weights_layout_batch(const WeightLayoutJob* table_device, int jobs, long max_elems, cudaStream_t stream,
+                          bool round_tf32 = false);
 
 // ---------------------------------------------------------------- backbone helpers
 void maxpool5_padded(const View& in, const View& out, int batch, const Grid& g, cudaStream_t stream);
@@ -166,7 +200,7 @@ void bn_eval_coef(const float* rmean, const float* rvar, float eps, int batch, i
                   cudaStream_t stream);
 // a = SiLU(gamma * (y - mean) * inv + beta) at interior rows, 0 elsewhere (xhat is not stored).
 void bn_silu_apply(const View& y, const float* coef, const float* gamma, const float* beta, int batch, const Grid& g,
-                   const View& a, cudaStream_t stream);
+                   const View& a, cudaStream_t stream, bool round_tf32 = false);
 // Fold the epilogue's (sum dz, sum dz xhat) partials per (image, channel) over the row groups in order;
 // dgamma / dbeta are accumulated over images in image order.  bcoef (3 x batch x c floats) receives
 // [f plane | red], f = gamma inv / n, red[(b * c + ch) * 2 + {0,1}] = (sum dz, sum dz xhat).
@@ -174,7 +208,7 @@ void bn_backward_fold(const float* part, int batch, const Grid& g, int c, const 
                       float* dgamma, float* dbeta, float* bcoef, cudaStream_t stream, bool param_grad = true);
 // dy = f (n dz - sum dz - xhat sum dz xhat)  (HeadOperations.cs:185-189) at interior rows, 0 elsewhere.
 void bn_backward_apply(const View& y, const View& dz, const float* coef, const float* bcoef, int batch, const Grid& g,
-                       const View& dy, cudaStream_t stream);
+                       const View& dy, cudaStream_t stream, bool round_tf32 = false);
 // Running statistics: for each BN channel, r <- (1-m) r + m * s_i for images i in order, over
 // `ranks` blocks of `batch` images each `rank_stride` floats apart (all-gathered ranks).
 // One BatchNorm layer of a batched fold (device table): statistics at `stats_off` floats into the
@@ -220,9 +254,12 @@ struct LossOut {
     float* scores;     // [batch][anchors] (may be null)
 };
 size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int bins);
+// round_grad: the logit gradients are stored rounded to the nearest TF32 (operands of TF32 convs).
+// serial_cls: the per-image class loss is the reference's float running sum (one term at a time, in its
+// order) instead of the exact sum of the same terms (about 1e-3 apart at 640 x 640).
 void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int bins, const TruthBox* truth,
                     const int* box_offsets, int max_boxes, int topk, int topk2, float grad_scale, int backward, void* workspace,
-                    const LossOut& out, cudaStream_t stream);
+                    const LossOut& out, cudaStream_t stream, bool round_grad = false, bool serial_cls = false);
 
 // ---------------------------------------------------------------- optimizer
 struct ParamSegment {

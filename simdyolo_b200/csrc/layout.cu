@@ -16,7 +16,7 @@ namespace sy {
 
 namespace {
 
-__global__ void nchw_to_padded_kernel(const float* src, int batch, int c, Grid g, float* dst, int pitch) {
+__global__ void nchw_to_padded_kernel(const float* src, int batch, int c, Grid g, float* dst, int pitch, int rnd) {
     long total = (long)batch * c * g.h * g.w;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
         int x = (int)(i % g.w);
@@ -25,7 +25,7 @@ __global__ void nchw_to_padded_kernel(const float* src, int batch, int c, Grid g
         r /= g.h;
         int ch = (int)(r % c);
         int b = (int)(r / c);
-        dst[((long)b * g.rows + g.row(y, x)) * pitch + ch] = src[i];
+        dst[((long)b * g.rows + g.row(y, x)) * pitch + ch] = rnd ? tf32_rna(src[i]) : src[i];
     }
 }
 
@@ -58,14 +58,15 @@ __global__ void rgb_to_padded_kernel(const uint8_t* rgb, int batch, int size, Gr
     }
 }
 
-__global__ void weights_fwd_kernel(const float* w, int oc, int ic, int taps, int kpad, float* dst) {
+__global__ void weights_fwd_kernel(const float* w, int oc, int ic, int taps, int kpad, float* dst, int rnd) {
     long total = (long)oc * taps * kpad;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
         int c = (int)(i % kpad);
         long r = i / kpad;
         int t = (int)(r % taps);
         int o = (int)(r / taps);
-        dst[i] = c < ic ? w[((long)o * ic + c) * taps + t] : 0.0f;
+        const float v = c < ic ? w[((long)o * ic + c) * taps + t] : 0.0f;
+        dst[i] = rnd ? tf32_rna(v) : v;
     }
 }
 
@@ -81,7 +82,7 @@ __global__ void weights_dgrad_kernel(const float* w, int oc, int ic, int taps, i
 }
 
 // blockIdx.y = job; the forward layout then the data-gradient layout of that job's weights.
-__global__ void weights_layout_batch_kernel(const WeightLayoutJob* table) {
+__global__ void weights_layout_batch_kernel(const WeightLayoutJob* table, int rnd) {
     const WeightLayoutJob jb = table[blockIdx.y];
     const long nf = (long)jb.oc * jb.taps * jb.kpad_in, nd = (long)jb.ic * jb.taps * jb.kpad_out;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < nf + nd; i += (long)gridDim.x * blockDim.x) {
@@ -89,13 +90,15 @@ __global__ void weights_layout_batch_kernel(const WeightLayoutJob* table) {
             const int c = (int)(i % jb.kpad_in);
             const long r = i / jb.kpad_in;
             const int t = (int)(r % jb.taps), o = (int)(r / jb.taps);
-            jb.fwd[i] = c < jb.ic ? jb.oihw[((long)o * jb.ic + c) * jb.taps + t] : 0.0f;
+            const float v = c < jb.ic ? jb.oihw[((long)o * jb.ic + c) * jb.taps + t] : 0.0f;
+            jb.fwd[i] = rnd ? tf32_rna(v) : v;
         } else {
             const long k = i - nf;
             const int o = (int)(k % jb.kpad_out);
             const long r = k / jb.kpad_out;
             const int t = (int)(r % jb.taps), c = (int)(r / jb.taps);
-            jb.dgrad[k] = o < jb.oc ? jb.oihw[((long)o * jb.ic + c) * jb.taps + t] : 0.0f;
+            const float v = o < jb.oc ? jb.oihw[((long)o * jb.ic + c) * jb.taps + t] : 0.0f;
+            jb.dgrad[k] = rnd ? tf32_rna(v) : v;
         }
     }
 }
@@ -196,7 +199,7 @@ struct StemParams {
 template <int OC>
 __global__ void __launch_bounds__(256) stem_conv_kernel(const uint8_t* rgb, int batch, int size,
                                                         const StemParams<OC> sp, float* out, int out_pitch,
-                                                        Grid gout, PhaseOut phase, int has_phase) {
+                                                        Grid gout, PhaseOut phase, int has_phase, int rnd) {
     const int ho = gout.h, wo = gout.w;
     const long total = (long)batch * ho * wo;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
@@ -221,6 +224,7 @@ __global__ void __launch_bounds__(256) stem_conv_kernel(const uint8_t* rgb, int 
 #pragma unroll
             for (int q = 0; q < 27; q++) s = fmaf(sp.w[o * 27 + q], in[q], s);
             acc[o] = silu_f(s + sp.b[o]);
+            if (rnd) acc[o] = tf32_rna(acc[o]);
         }
         if (out) {
             float* dst = out + ((long)b * gout.rows + gout.row(oy, ox)) * out_pitch;
@@ -269,9 +273,10 @@ void launch_check(const char* what) {
 
 long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
-void nchw_to_padded(const float* src, int batch, int c, const Grid& g, const View& dst, cudaStream_t stream) {
+void nchw_to_padded(const float* src, int batch, int c, const Grid& g, const View& dst, cudaStream_t stream,
+                    bool round_tf32) {
     long n = (long)batch * c * g.h * g.w;
-    nchw_to_padded_kernel<<<blocks_for(n), 256, 0, stream>>>(src, batch, c, g, dst.base, dst.pitch);
+    nchw_to_padded_kernel<<<blocks_for(n), 256, 0, stream>>>(src, batch, c, g, dst.base, dst.pitch, round_tf32 ? 1 : 0);
     launch_check("nchw_to_padded_kernel");
 }
 
@@ -287,9 +292,10 @@ void rgb_to_padded(const uint8_t* rgb, int batch, int size, const Grid& g, const
     launch_check("rgb_to_padded_kernel");
 }
 
-void weights_fwd_layout(const float* oihw, int oc, int ic, int taps, int kpad, float* dst, cudaStream_t stream) {
+void weights_fwd_layout(const float* oihw, int oc, int ic, int taps, int kpad, float* dst, cudaStream_t stream,
+                        bool round_tf32) {
     long n = (long)oc * taps * kpad;
-    weights_fwd_kernel<<<blocks_for(n), 256, 0, stream>>>(oihw, oc, ic, taps, kpad, dst);
+    weights_fwd_kernel<<<blocks_for(n), 256, 0, stream>>>(oihw, oc, ic, taps, kpad, dst, round_tf32 ? 1 : 0);
     launch_check("weights_fwd_kernel");
 }
 
@@ -299,10 +305,11 @@ void weights_dgrad_layout(const float* oihw, int oc, int ic, int taps, int kpad_
     launch_check("weights_dgrad_kernel");
 }
 
-void weights_layout_batch(const WeightLayoutJob* table_device, int jobs, long max_elems, cudaStream_t stream) {
+void weights_layout_batch(const WeightLayoutJob* table_device, int jobs, long max_elems, cudaStream_t stream,
+                          bool round_tf32) {
     if (jobs < 1 || jobs > 65535) throw std::runtime_error("weights_layout_batch: job count");
     const int bx = (int)std::min<long>(64, std::max<long>(1, (max_elems + 255) / 256));
-    weights_layout_batch_kernel<<<dim3(bx, jobs), 256, 0, stream>>>(table_device);
+    weights_layout_batch_kernel<<<dim3(bx, jobs), 256, 0, stream>>>(table_device, round_tf32 ? 1 : 0);
     launch_check("weights_layout_batch_kernel");
 }
 
@@ -341,15 +348,16 @@ void upsample2_padded(const View& in, const Grid& gin, const View& out, const Gr
 
 template <int OC>
 static void launch_stem(const uint8_t* rgb, int batch, int size, const float* w_host, const float* b_host,
-                        const View& out, const Grid& gout, const PhaseOut& ph, int hp, int blocks, cudaStream_t stream) {
+                        const View& out, const Grid& gout, const PhaseOut& ph, int hp, int blocks, cudaStream_t stream,
+                        int rnd) {
     StemParams<OC> sp;
     for (int i = 0; i < OC * 27; i++) sp.w[i] = w_host[i];
     for (int i = 0; i < OC; i++) sp.b[i] = b_host[i];
-    stem_conv_kernel<OC><<<blocks, 256, 0, stream>>>(rgb, batch, size, sp, out.base, out.pitch, gout, ph, hp);
+    stem_conv_kernel<OC><<<blocks, 256, 0, stream>>>(rgb, batch, size, sp, out.base, out.pitch, gout, ph, hp, rnd);
 }
 
 void stem_conv(const uint8_t* rgb, int batch, int size, const float* w_host, const float* bias_host, int oc,
-               const View& out, const Grid& gout, const PhaseOut* phase, cudaStream_t stream) {
+               const View& out, const Grid& gout, const PhaseOut* phase, cudaStream_t stream, bool round_tf32) {
     if (out.pitch % 4 != 0 || (phase && phase->pitch % 4 != 0))
         throw std::runtime_error("stem_conv: pitches must be multiples of 4");
     if (!out.base && !phase) throw std::runtime_error("stem_conv: no output");
@@ -357,20 +365,15 @@ void stem_conv(const uint8_t* rgb, int batch, int size, const float* w_host, con
     const int blocks = (int)std::min<long>(148L * 8, std::max<long>(1, (n + 255) / 256));
     const PhaseOut ph = phase ? *phase : PhaseOut{};
     const int hp = phase ? 1 : 0;
+    const int rnd = round_tf32 ? 1 : 0;
     switch (oc) {
-        case 16: launch_stem<16>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream); break;
-        case 32: launch_stem<32>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream); break;
-        case 48: launch_stem<48>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream); break;
-        case 64: launch_stem<64>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream); break;
+        case 16: launch_stem<16>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream, rnd); break;
+        case 32: launch_stem<32>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream, rnd); break;
+        case 48: launch_stem<48>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream, rnd); break;
+        case 64: launch_stem<64>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream, rnd); break;
         default: throw std::runtime_error("stem_conv: output channels must be 16, 32, 48 or 64");
     }
     launch_check("stem_conv_kernel");
-}
-
-__device__ __forceinline__ float tf32_round(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
 }
 
 __global__ void tf32_split_kernel(const float* src, int pitch, int channels, long rows, float* big, float* small) {
@@ -378,7 +381,7 @@ __global__ void tf32_split_kernel(const float* src, int pitch, int channels, lon
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
         const long r = i / channels;
         const long idx = r * pitch + (i - r * channels);
-        const float x = src[idx], b = tf32_round(x);
+        const float x = src[idx], b = tf32_rna(x);
         big[idx] = b;
         small[idx] = x - b;
     }

@@ -32,6 +32,8 @@ struct LossParams {
     int batch, nc, bins, topk, topk2;
     float grad_scale;
     int backward;
+    int round_grad;       // logit gradients stored rounded to the nearest TF32 (TF32 conv operands)
+    int serial_cls;       // class loss summed in float one term at a time, in the reference's order
     const TruthBox* truth;
     const int* box_off;   // [batch + 1]
     int max_boxes;
@@ -458,7 +460,8 @@ __global__ void __launch_bounds__(256) bce_kernel(LossParams p, const int* dense
             part += (fmaxf(x, 0.f) - x * t + log1pf(e)) * inv;
             if (p.backward) {
                 const float s = __fdividef(x >= 0.f ? 1.f : e, 1.f + e);
-                L.dcls[off + c] = (s - t) * inv * p.grad_scale;
+                const float gr = (s - t) * inv * p.grad_scale;
+                L.dcls[off + c] = p.round_grad ? tf32_rna(gr) : gr;
             }
         }
         acc += (double)part;
@@ -513,7 +516,8 @@ __global__ void __launch_bounds__(256) box_kernel(LossParams p) {
             dfl += fabsf(delta) * norm * l1;
             if (p.backward && lane == 0) {
                 const float sign = delta > 0 ? 1.f : delta < 0 ? -1.f : 0.f;
-                L.dbox[off + d] = dist_grad[d] + sign * norm * l1 * p.grad_scale;
+                const float gr = dist_grad[d] + sign * norm * l1 * p.grad_scale;
+                L.dbox[off + d] = p.round_grad ? tf32_rna(gr) : gr;
             }
         }
     } else {
@@ -547,7 +551,8 @@ __global__ void __launch_bounds__(256) box_kernel(LossParams p) {
                 }
                 const float pr = fdiv(mine, sum);
                 const float tp = lane == left ? 1 - rw : lane == left + 1 ? rw : 0.f;
-                L.dbox[off + d * 16 + lane] = pr * (lane - ex[d]) * dist_grad[d] + scale * (pr - tp) * p.grad_scale;
+                const float gr = pr * (lane - ex[d]) * dist_grad[d] + scale * (pr - tp) * p.grad_scale;
+                L.dbox[off + d * 16 + lane] = p.round_grad ? tf32_rna(gr) : gr;
             }
         }
     }
@@ -577,6 +582,58 @@ __global__ void finalize_kernel(LossParams p) {
     p.out.connected[b] = (p.backward && c > 0) ? 1 : 0;
 }
 
+// The class loss as the reference accumulates it (DetectionLoss.cs:103-109): one float running sum over
+// anchors in order, and per anchor over the classes in order, of
+//   (max(x, 0) - x t + log(1 + exp(-|x|))) * (0.5 / scoreSum)
+// each operation rounded to nearest, with full-precision expf / logf.  Over the 80 x 8400 terms of a
+// 640-pixel image that sum differs from the exact one by about 1e-3 (each addition to a running sum near
+// 5 rounds a term of about 1e-5 to the running sum's spacing); the reduction in bce_kernel returns the
+// exact sum, this kernel the reference's value.  One block per image: threads 32.. compute the terms of
+// the next chunk of anchors into shared memory while thread 0 adds up the current chunk.
+constexpr int kSerialChunk = 32;   // anchors per chunk
+__global__ void __launch_bounds__(256) bce_serial_kernel(LossParams p, const int* dense_assigned, const float* dense_scores) {
+    extern __shared__ float terms[];   // [2][kSerialChunk * nc]
+    const int b = blockIdx.x;
+    const int per = kSerialChunk * p.nc;
+    const float inv = __fdiv_rn(.5f, p.score_sum[b]);
+    const int chunks = (p.anchors + kSerialChunk - 1) / kSerialChunk;
+    auto fill = [&](int k, int tid, int nthreads) {
+        float* dst = terms + (k & 1) * per;
+        for (int i = tid; i < per; i += nthreads) {
+            const int a = k * kSerialChunk + i / p.nc, c = i - (i / p.nc) * p.nc;
+            float term = 0.f;
+            if (a < p.anchors) {
+                int level, row;
+                float cx, cy, st;
+                anchor_location(p, a, level, row, cx, cy, st);
+                const LevelIO& L = p.lv[level];
+                const float x = L.cls[((long)b * L.grid.rows + row) * L.cls_pitch + c];
+                const int g = dense_assigned[(long)b * p.anchors + a];
+                const float t = (g >= 0 && p.truth[p.box_off[b] + g].cls == c) ? dense_scores[(long)b * p.anchors + a]
+                                                                                : 0.f;
+                const float lg = logf(__fadd_rn(1.f, expf(-fabsf(x))));
+                term = __fmul_rn(__fadd_rn(__fsub_rn(fmaxf(x, 0.f), __fmul_rn(x, t)), lg), inv);
+            }
+            dst[i] = term;
+        }
+    };
+    fill(0, threadIdx.x, blockDim.x);
+    __syncthreads();
+    float acc = 0.f;
+    for (int k = 0; k < chunks; k++) {
+        if (threadIdx.x == 0) {
+            const float* src = terms + (k & 1) * per;
+            const int n = min(per, (p.anchors - k * kSerialChunk) * p.nc);
+#pragma unroll 8
+            for (int i = 0; i < n; i++) acc = __fadd_rn(acc, src[i]);
+        } else if (threadIdx.x >= 32 && k + 1 < chunks) {
+            fill(k + 1, threadIdx.x - 32, blockDim.x - 32);
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) p.out.loss[b * 4 + 1] = acc;
+}
+
 constexpr int kBceBlocks = 64;
 
 size_t align_up(size_t v) { return (v + 255) & ~size_t(255); }
@@ -599,8 +656,10 @@ size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int topk) {
 
 void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int bins, const TruthBox* truth,
                     const int* box_offsets, int max_boxes, int topk, int topk2, float grad_scale, int backward, void* workspace,
-                    const LossOut& out, cudaStream_t stream) {
+                    const LossOut& out, cudaStream_t stream, bool round_grad, bool serial_cls) {
     LossParams p;
+    p.round_grad = round_grad ? 1 : 0;
+    p.serial_cls = serial_cls ? 1 : 0;
     p.nlevels = nlevels;
     p.level_start[0] = 0;
     for (int l = 0; l < nlevels; l++) {
@@ -667,6 +726,12 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
     launch_check("box_kernel");
     finalize_kernel<<<batch, 32, 0, stream>>>(p);
     launch_check("finalize_kernel");
+    if (serial_cls) {
+        const size_t smem = 2 * (size_t)kSerialChunk * nc * sizeof(float);
+        if (smem > 48 * 1024) throw std::runtime_error("detection_loss: too many classes for the serial class sum");
+        bce_serial_kernel<<<batch, 256, smem, stream>>>(p, p.out.assigned, p.out.scores);
+        launch_check("bce_serial_kernel");
+    }
 }
 
 }  // namespace sy

@@ -112,6 +112,7 @@ Session::Session(const sy_config& c) : cfg(c) {
     if (c.precision != SY_PRECISION_TF32 && c.precision != SY_PRECISION_3XTF32)
         throw SyError(SY_ERR_INVALID_ARGUMENT, "precision must be SY_PRECISION_TF32 or SY_PRECISION_3XTF32");
     x3_ = c.precision == SY_PRECISION_3XTF32;
+    rnd_ = !x3_;
     if (const char* e = std::getenv("SIMDYOLO_CUDA_GRAPHS")) use_graphs_ = std::strcmp(e, "0") != 0;
     device_ = c.device;
     SY_CUDA(cudaSetDevice(device_));
@@ -501,7 +502,7 @@ int Session::set_backbone(const float* host, long count) {
             stem_host_.insert(stem_host_.end(), host + op.b_off, host + op.b_off + op.oc);
         }
         const int taps = op.k * op.k;
-        weights_fwd_layout(backbone_params_ + op.w_off, op.oc, op.ic, taps, round_up(op.ic, 32), op.wk, stream_);
+        weights_fwd_layout(backbone_params_ + op.w_off, op.oc, op.ic, taps, round_up(op.ic, 32), op.wk, stream_, rnd_);
     }
     SY_CUDA(cudaStreamSynchronize(stream_));
     clear_graphs();   // the stem's weights travel by value inside captured launches
@@ -515,7 +516,7 @@ void Session::forward_backbone(int batch, const uint8_t* rgb_device) {
         if (op.type == 0 && !op.plain_out) out.base = nullptr;
         if (op.type == 0 && in.base == img_.base) {
             stem_conv(rgb_device, batch, cfg.image_size, stem_host_.data(), stem_host_.data() + (long)op.oc * op.ic * 9,
-                      op.oc, out, op.gout, op.has_phase_out ? &op.phase_out : nullptr, stream_);
+                      op.oc, out, op.gout, op.has_phase_out ? &op.phase_out : nullptr, stream_, rnd_);
         } else if (op.type == 1) {
             maxpool5_padded(in, out, batch, op.gin, stream_);
         } else if (op.type == 2) {
@@ -524,7 +525,7 @@ void Session::forward_backbone(int batch, const uint8_t* rgb_device) {
             View i2 = in, o2 = out, r2 = op.res;
             i2.rows = o2.rows = r2.rows = (long)batch * op.gin.rows;
             dw_conv(i2, backbone_params_ + op.w_off, op.k * op.k, 1, op.gin, o2, BnEpilogue{}, stream_,
-                    backbone_params_ + op.b_off, op.has_res ? &r2 : nullptr);
+                    backbone_params_ + op.b_off, op.has_res ? &r2 : nullptr, rnd_);
         } else if (op.type == 4) {
             View i2 = in, o2 = out, a2 = op.aux;
             i2.rows = o2.rows = a2.rows = (long)batch * op.gin.rows;
@@ -533,6 +534,7 @@ void Session::forward_backbone(int batch, const uint8_t* rgb_device) {
             ConvEpilogue ep;
             ep.bias = backbone_params_ + op.b_off;
             ep.silu = op.act;
+            ep.round_tf32 = rnd_;
             if (op.has_res) {
                 ep.residual = op.res.base;
                 ep.res_pitch = op.res.pitch;
@@ -735,6 +737,24 @@ void Session::build_head() {
         }
     }
     wgrad_ws_ = static_cast<float*>(dalloc(sizeof(float) * ws));
+    // 3xTF32: centred features for the weight gradients of the first tensor-core conv of every branch
+    int max_first_oc = 0;
+    for (auto& branch : branches_) {
+        if (!x3_) break;
+        const HeadBlock& hb = branch.blocks[0];
+        if (hb.dw) continue;
+        const int l = branch.level;
+        if (!feat_mean_[l]) {
+            feat_c_[l] = alloc_view(feat_ch_[l], levels_[l]);
+            feat_mean_[l] = static_cast<float*>(dalloc(sizeof(float) * (size_t)B_ * feat_ch_[l]));
+        }
+        max_first_oc = std::max(max_first_oc, hb.b.oc);
+    }
+    if (max_first_oc > 0) {
+        tap_sums_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)B_ * 9 * max_first_oc));
+        center_ws_ = static_cast<float*>(dalloc(
+            sizeof(float) * center_workspace_floats(B_, std::max({max_first_oc, feat_ch_[0], feat_ch_[1], feat_ch_[2]}))));
+    }
     bias_part_ = static_cast<float*>(dalloc(sizeof(float) * bn_workspace_floats(B_, max_oc)));
     bn_part_ = static_cast<float*>(dalloc(sizeof(float) * std::max<size_t>(bn_part_floats, 1)));
 }
@@ -757,7 +777,7 @@ void Session::refresh_head_weights() {
         d_layout_jobs_ = static_cast<WeightLayoutJob*>(dalloc(sizeof(WeightLayoutJob) * jobs.size()));
         SY_CUDA(cudaMemcpy(d_layout_jobs_, jobs.data(), sizeof(WeightLayoutJob) * jobs.size(), cudaMemcpyHostToDevice));
     }
-    if (n_layout_jobs_ > 0) weights_layout_batch(d_layout_jobs_, n_layout_jobs_, layout_max_elems_, stream_);
+    if (n_layout_jobs_ > 0) weights_layout_batch(d_layout_jobs_, n_layout_jobs_, layout_max_elems_, stream_, rnd_);
 }
 
 static View rows_of(View v, int batch, const Grid& g) {
@@ -792,13 +812,17 @@ void Session::forward_head(int batch, bool training) {
                     bn_eval_coef(buffers_ + hb.rm_off, buffers_ + hb.rv_off, cfg.bn_eps, batch, hb.b.oc, hb.coef,
                                  stream_);
                 bn_silu_apply(rows_of(hb.y, batch, g), hb.coef, params_ + hb.g_off, params_ + hb.be_off, batch, g,
-                              rows_of(hb.a, batch, g), stream_);
+                              rows_of(hb.a, batch, g), stream_, rnd_);
             }
         }
     }
 }
 
 void Session::backward_head(int batch) {
+    for (int l = 0; l < 3; l++)
+        if (feat_mean_[l])
+            center_features(rows_of(features_[l], batch, levels_[l]), batch, levels_[l], feat_mean_[l], center_ws_,
+                            rows_of(feat_c_[l], batch, levels_[l]), rnd_, stream_);
     for (int set = n_sets_ - 1; set >= 0; set--)
         for (int l = 2; l >= 0; l--)
             for (int kind = 1; kind >= 0; kind--) {
@@ -812,14 +836,22 @@ void Session::backward_head(int batch) {
                         bn_backward_fold(bn_part_, batch, g, hb.b.oc, hb.coef, params_ + hb.g_off, grads_ + hb.g_off,
                                          grads_ + hb.be_off, hb.bcoef, stream_, false);
                         bn_backward_apply(rows_of(hb.y, batch, g), rows_of(hb.g, batch, g), hb.coef, hb.bcoef, batch, g,
-                                          rows_of(hb.dy, batch, g), stream_);
+                                          rows_of(hb.dy, batch, g), stream_, rnd_);
                     }
                     if (hb.b.has_bias) bias_grad(hb.dy, batch, g, bias_part_, grads_ + hb.b_off, stream_);
                     if (hb.dw)
                         dw_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off,
                                  wgrad_ws_, stream_);
-                    else
+                    else if (i == 0 && feat_mean_[l]) {
+                        // the first conv reads the frozen features: centred weight gradient (WgradCenter)
+                        tap_border_sums(rows_of(hb.dy, batch, g), batch, g, hb.taps, hb.b.has_bn != 0, center_ws_,
+                                        tap_sums_, stream_);
+                        const WgradCenter center{feat_mean_[l], tap_sums_, batch};
+                        conv_wgrad(rows_of(feat_c_[l], batch, g), rows_of(hb.dy, batch, g), hb.taps, g,
+                                   grads_ + hb.w_off, &center);
+                    } else {
                         conv_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off);
+                    }
                     if (i > 0) {
                         HeadBlock& prev = branch.blocks[i - 1];
                         ConvEpilogue ep;
@@ -882,7 +914,7 @@ void Session::launch_losses(int images, int backward, int epoch) {
                    nullptr};
         const int topk = set == 0 ? 10 : (progressive_ ? 7 : 1), topk2 = set == 0 ? 10 : 1;
         detection_loss(lv, 3, images, cfg.num_classes, cfg.reg_max, d_truth_, d_box_off_, std::max(1, cfg.max_boxes),
-                       topk, topk2, cfg.end_to_end ? w[set] : 1.0f, backward, loss_ws_, lo, stream_);
+                       topk, topk2, cfg.end_to_end ? w[set] : 1.0f, backward, loss_ws_, lo, stream_, rnd_, x3_);
     }
 }
 
@@ -977,7 +1009,7 @@ void Session::prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float
             const Grid& g = levels_[l];
             const size_t n = (size_t)images * feat_ch_[l] * g.h * g.w;
             SY_CUDA(cudaMemcpyAsync(feat_stage_, features[l], n * sizeof(float), cudaMemcpyHostToDevice, stream_));
-            nchw_to_padded(feat_stage_, images, feat_ch_[l], g, features_[l], stream_);
+            nchw_to_padded(feat_stage_, images, feat_ch_[l], g, features_[l], stream_, rnd_);
         }
     }
 }
@@ -1194,15 +1226,16 @@ void Session::conv_strided(const View& phase_in, long plane_rows, long m_rows, c
     conv_tc_strided(ab, plane_rows, m_rows, wb, oc, gout, out, last, d_flags_, stream_, po);
 }
 
-void Session::conv_wgrad(const View& x, const View& dy, int taps, const Grid& grid, float* dw) {
+void Session::conv_wgrad(const View& x, const View& dy, int taps, const Grid& grid, float* dw,
+                         const WgradCenter* center) {
     if (!x3_) {
-        conv_tc_wgrad(x, dy, taps, grid, dw, wgrad_ws_, d_flags_, stream_);
+        conv_tc_wgrad(x, dy, taps, grid, dw, wgrad_ws_, d_flags_, stream_, 0, center);
         return;
     }
     View xs, ds;
     const View xb = split_view(x, 0, &xs);
     const View db = split_view(dy, 2, &ds);
-    conv_tc_wgrad(xs, db, taps, grid, dw, wgrad_ws_, d_flags_, stream_, 0);
+    conv_tc_wgrad(xs, db, taps, grid, dw, wgrad_ws_, d_flags_, stream_, 0, center);
     conv_tc_wgrad(xb, ds, taps, grid, dw, wgrad_ws_, d_flags_, stream_, 1);
     conv_tc_wgrad(xb, db, taps, grid, dw, wgrad_ws_, d_flags_, stream_, 1);
 }

@@ -142,7 +142,8 @@ private:
                   const Grid& grid, const View& out, const ConvEpilogue& ep, const PhaseOut* po);
     void conv_strided(const View& phase_in, long plane_rows, long m_rows, const float* wk, long wk_floats, int oc,
                       const Grid& gout, const View& out, const ConvEpilogue& ep, const PhaseOut* po);
-    void conv_wgrad(const View& x, const View& dy, int taps, const Grid& grid, float* dw);
+    void conv_wgrad(const View& x, const View& dy, int taps, const Grid& grid, float* dw,
+                    const WgradCenter* center = nullptr);
     View split_view(const View& v, int slot_big, View* small);
     const float* split_weights(const float* wk, long n, const float** small);
     void* dalloc(size_t bytes);
@@ -155,6 +156,13 @@ private:
     Grid levels_[3];
     int feat_ch_[3] = {0, 0, 0};
     View features_[3];
+    // 3xTF32 parity mode: centred copies of the features for the first head convs' weight gradients
+    // (WgradCenter): xc = features - per-(image, channel) mean, the means, and the tap border sums of one
+    // dy.  In TF32 the operand rounding, not the accumulation, sets the error, so TF32 runs without them.
+    View feat_c_[3];
+    float* feat_mean_[3] = {nullptr, nullptr, nullptr};
+    float* tap_sums_ = nullptr;
+    float* center_ws_ = nullptr;
     // backbone
     std::vector<BackboneOp> bops_;
     float* backbone_params_ = nullptr;
@@ -213,6 +221,9 @@ private:
     int last_batch_ = 0;
     // 3xTF32 operand split scratch: activations (4 buffers) and weights (2 buffers)
     bool x3_ = false;
+    // TF32 mode: every tensor-core operand (weights, activations, gradients) is stored rounded to the
+    // nearest TF32, so the tensor core's truncation of FP32 operands adds no systematic error
+    bool rnd_ = false;
     float* sp_[4] = {nullptr, nullptr, nullptr, nullptr};
     size_t sp_floats_ = 0;
     float* wsp_[2] = {nullptr, nullptr};

@@ -118,3 +118,177 @@ def oracle_head_step_adamw(cfg: sy.Config, tensors, params, buffers, m1, m2, ste
     for gi in range(3):
         steps[gi] += int(has_group[gi])
     return losses, grad, params, buffers_out, m1, m2, steps
+
+
+def _block_path(i: int, n: int) -> str:
+    return ["0.0", "0.1", "1.0", "1.1", "2"][i] if n == 5 else str(i)
+
+
+def snapshot_tensors(cfg: sy.Config):
+    """The session's tensor list (DetectionHead.Snapshot order, DetectionHead.cs:124-130) restated on the
+    host: every parameter (cv2.0-2, cv3.0-2, then one2one_cv2 / one2one_cv3; per block weight, [bias],
+    [bn gamma, beta]), then per BatchNorm block running_mean, running_var, num_batches_tracked.  Same
+    dict layout as Session.tensors, so seeded initial states can be built without a GPU."""
+    params, buffers = [], []
+    for st in range(2 if cfg.end_to_end else 1):
+        for box in (True, False):
+            for lvl in range(3):
+                prefix = ("one2one_" if st else "") + ("cv2" if box else "cv3") + f".{lvl}"
+                n = cfg.n_box_blocks if box else cfg.n_cls_blocks
+                blocks = cfg.box_blocks[lvl] if box else cfg.cls_blocks[lvl]
+                for i in range(n):
+                    b = blocks[i]
+                    path = f"{prefix}.{_block_path(i, n)}"
+                    conv = path + (".conv" if b.has_bn else "")
+                    params.append((conv + ".weight", (b.oc, b.ic // b.groups, b.k, b.k)))
+                    if b.has_bias:
+                        params.append((conv + ".bias", (b.oc,)))
+                    if b.has_bn:
+                        params.append((path + ".bn.weight", (b.oc,)))
+                        params.append((path + ".bn.bias", (b.oc,)))
+                        buffers += [(path + ".bn.running_mean", (b.oc,)), (path + ".bn.running_var", (b.oc,)),
+                                    (path + ".bn.num_batches_tracked", ())]
+    out = []
+    for kind, items in ((0, params), (1, buffers)):
+        for name, shape in items:
+            out.append(dict(index=len(out), name=name, kind=kind, shape=shape,
+                            numel=int(np.prod(shape, dtype=np.int64))))
+    return out
+
+
+def initial_head_state(cfg: sy.Config, seed: int):
+    """data.head_params for `cfg` without a session: (tensors, params, buffers)."""
+    from types import SimpleNamespace
+
+    from simdyolo_b200 import data
+    tensors = snapshot_tensors(cfg)
+    params, buffers = data.head_params(SimpleNamespace(config=cfg, tensors=tensors), seed)
+    return tensors, params, buffers
+
+
+def tf32_rna(t):
+    """Round a float64 torch tensor to float32, then to the nearest TF32 value (10 mantissa bits, ties away
+    from zero): the rounding cvt.rna.tf32.f32 applies to every tensor-core operand in TF32 mode."""
+    import torch
+    f = t.to(torch.float32).contiguous()
+    bits = f.view(torch.int32)
+    r = torch.bitwise_and(bits + 0x1000, ~0x1FFF)
+    return r.view(torch.float32).to(torch.float64)
+
+
+def _tf32_conv():
+    import torch
+    import torch.nn.functional as F
+
+    class Tf32Conv(torch.autograd.Function):
+        """conv2d in float64 whose operands are TF32-rounded in the forward (input, weight) and in both
+        backward GEMMs (output gradient and weight for the data gradient, input and output gradient for the
+        weight gradient), as the TF32 tensor-core path stores them.  `center` applies the first-conv
+        weight-gradient identity with the exact zero total: the input is centred per channel before the
+        rounding and mean * (-edge strip sums of dy) is added back."""
+
+        @staticmethod
+        def forward(ctx, x, w, pad, center):
+            ctx.save_for_backward(x, w)
+            ctx.pad, ctx.center = pad, center
+            return F.conv2d(tf32_rna(x), tf32_rna(w), padding=pad)
+
+        @staticmethod
+        def backward(ctx, dy):
+            x, w = ctx.saved_tensors
+            dyr = tf32_rna(dy)
+            dx = torch.nn.grad.conv2d_input(x.shape, tf32_rna(w), dyr, padding=ctx.pad)
+            if not ctx.center:
+                dw = torch.nn.grad.conv2d_weight(tf32_rna(x), w.shape, dyr, padding=ctx.pad)
+            else:
+                mu = x.mean((2, 3), keepdim=True)
+                dw = torch.nn.grad.conv2d_weight(tf32_rna(x - mu), w.shape, dyr, padding=ctx.pad)
+                k = w.shape[-1]
+                H, W = dy.shape[2], dy.shape[3]
+                # T[t][o] = -(sum of dy over the pixels whose tap-t source leaves the map)
+                T = torch.zeros(dy.shape[1], k, k, dtype=dy.dtype)
+                for ky in range(k):
+                    for kx in range(k):
+                        sy_, sx = ky - k // 2, kx - k // 2
+                        mask = torch.zeros(H, W, dtype=torch.bool)
+                        if sy_ < 0:
+                            mask[:-sy_, :] = True
+                        if sy_ > 0:
+                            mask[H - sy_:, :] = True
+                        if sx < 0:
+                            mask[:, :-sx] = True
+                        if sx > 0:
+                            mask[:, W - sx:] = True
+                        T[:, ky, kx] = -(dyr[0][:, mask].sum(-1))
+                dw = dw + mu[0, :, 0, 0][None, :, None, None] * T[:, None, :, :]
+            return dx, dw, None, None
+
+    return Tf32Conv
+
+
+def head_gradient_emulated(cfg: sy.Config, tensors, params, features, truth, tf32: bool, center_first: bool = True):
+    """The head gradient of one step in float64: per image the head forward with training BatchNorm
+    (HeadOperations.cs:158-166) and the backward by torch autograd, fed with the oracle's DetectionLoss
+    gradient (DetectionLoss.cs:19-149, float32, evaluated on the float64 outputs rounded to float32),
+    summed over images.  With `tf32`, every conv of the head is evaluated like the TF32 tensor-core path
+    (operands rounded to TF32 in the forward and both backward GEMMs; with `center_first` the first conv
+    of each branch uses the centred weight gradient).  Returns (gradient, positives)."""
+    import torch
+    import torch.nn.functional as F
+    assert not cfg.end_to_end
+    conv = _tf32_conv() if tf32 else None
+    names = [t for t in tensors if t["kind"] == 0]
+    total = np.zeros(sum(t["numel"] for t in names), np.float64)
+    positives = 0
+    for b in range(features[0].shape[0]):
+        ts, off = {}, 0
+        for t in names:
+            ts[t["name"]] = torch.tensor(params[off:off + t["numel"]].astype(np.float64).reshape(t["shape"]),
+                                         requires_grad=True)
+            off += t["numel"]
+        outs = {}
+        for box in (True, False):
+            for lvl in range(3):
+                prefix = ("cv2" if box else "cv3") + f".{lvl}"
+                n = cfg.n_box_blocks if box else cfg.n_cls_blocks
+                blocks = cfg.box_blocks[lvl] if box else cfg.cls_blocks[lvl]
+                x = torch.tensor(features[lvl][b].astype(np.float64))[None]
+                if tf32:
+                    x = tf32_rna(x)
+                for i in range(n):
+                    blk = blocks[i]
+                    assert blk.groups == 1
+                    path = f"{prefix}.{_block_path(i, n)}"
+                    cname = path + (".conv" if blk.has_bn else "")
+                    if tf32:
+                        x = conv.apply(x, ts[cname + ".weight"], blk.k // 2, center_first and i == 0 and bool(blk.has_bn))
+                        if cname + ".bias" in ts:
+                            x = x + ts[cname + ".bias"][None, :, None, None]
+                    else:
+                        x = F.conv2d(x, ts[cname + ".weight"], ts.get(cname + ".bias"), padding=blk.k // 2)
+                    if blk.has_bn:
+                        mean = x.mean((0, 2, 3))
+                        var = x.var((0, 2, 3), unbiased=False)
+                        x = (x - mean[None, :, None, None]) / torch.sqrt(var[None, :, None, None] + cfg.bn_eps)
+                        x = x * ts[path + ".bn.weight"][None, :, None, None] + ts[path + ".bn.bias"][None, :, None, None]
+                        x = F.silu(x)
+                outs[(box, lvl)] = x[0]
+        bl = [outs[(True, l)].detach().numpy().astype(np.float32) for l in range(3)]
+        cl = [outs[(False, l)].detach().numpy().astype(np.float32) for l in range(3)]
+        part, db, dc, _, _ = O.detection_loss(bl, cl, [8.0, 16.0, 32.0], truth[b], cfg.num_classes, bins=cfg.reg_max)
+        positives += part["positives"]
+        pairs = [(outs[(True, l)], torch.tensor(db[l].astype(np.float64))) for l in range(3)]
+        pairs += [(outs[(False, l)], torch.tensor(dc[l].astype(np.float64))) for l in range(3)]
+        torch.autograd.backward([o for o, _ in pairs], [g for _, g in pairs])
+        total += np.concatenate([ts[t["name"]].grad.numpy().ravel() if ts[t["name"]].grad is not None
+                                 else np.zeros(t["numel"]) for t in names])
+    return total, positives
+
+
+def f64_head_gradient(cfg: sy.Config, tensors, params, features, truth):
+    """head_gradient_emulated without TF32 rounding: the exact (float64) head gradient of one step given
+    the oracle's loss gradient.  Sums that cancel heavily (the first conv of every branch reads trunk
+    features with a large per-channel mean against a zero-mean BatchNorm gradient) carry FP32 rounding
+    of about 1e-5 in any FP32 evaluation order; this one has none, so FP32 implementations can be compared
+    by their distance from it."""
+    return head_gradient_emulated(cfg, tensors, params, features, truth, tf32=False)
