@@ -161,6 +161,11 @@ SY_API sy_status sy_cuda_eval_loss_features(sy_session *session, const float *co
 /* The completed-epoch counter YoloTrainer passes to DetectionHead.Loss (YoloTrainer.cs:192); it only
  * matters for progressive end-to-end heads.  Evaluation always uses epoch 0 (YoloTrainer.cs:243). */
 SY_API sy_status sy_cuda_set_epoch(sy_session *session, int32_t epoch);
+/* AdamW steps taken per optimizer group: [0] class branches, [1] cv2, [2] one2one_cv2 (a box group steps only
+ * when an image connected it).  AdamW is not in the reference; with sy_cuda_get/set_optimizer_state these
+ * counts complete the state a resumed AdamW run needs. */
+SY_API sy_status sy_cuda_get_optimizer_steps(const sy_session *session, int32_t steps[3]);
+SY_API sy_status sy_cuda_set_optimizer_steps(sy_session *session, const int32_t steps[3]);
 /* Gradient of the last step (summed over the images of every rank, before the update), parameter order. */
 SY_API sy_status sy_cuda_get_last_gradients(const sy_session *session, float *host, int64_t count);
 /* Frozen features of the last step (NCHW per level), for parity checks. */
@@ -198,16 +203,17 @@ SY_API sy_status sy_cuda_conv2d_backward_data(int32_t device, const float *dy, i
 SY_API sy_status sy_cuda_conv2d_backward_filter(int32_t device, const float *x, const float *dy, int32_t n, int32_t ic,
                                          int32_t oc, int32_t h, int32_t w, int32_t k, float *dw);
 
-/* Allocation-free weight gradient: no counterpart in the reference.  For callers that cannot call
- * cudaMalloc (inside a CUDA graph capture, under an external memory pool or an embedding runtime
- * that owns all device memory): same result as sy_cuda_conv2d_backward_filter, but every buffer is
- * caller-owned device memory and the split-K scratch is a fixed 16 MiB static device array per GPU
- * (shapes needing more return SY_ERR_UNSUPPORTED_SHAPE).  x / dy use the library's padded
- * channels-last layout: image b, pixel (y, x) at row b * R + (y + 1) * (w + 2) + (x + 1) with
- * R = round_up((h + 2) * (w + 2), 128), rows of round_up(C, 4) floats, halo rows zero.  dw is OIHW.
- * The first call on a device looks up the static array's device address: make it before any stream
- * capture.  Calls share the array, so calls that overlap on the GPU race; the call returns after
- * `stream` (NULL = legacy default stream) has finished it. */
+/* Allocation-free weight gradient: no counterpart in the reference.  For hosts that cannot let a library
+ * call cudaMalloc (an embedding runtime or caching allocator that has reserved all device memory for its
+ * own pool, or a serving loop that must not take the driver's allocation locks mid-request): same result as
+ * sy_cuda_conv2d_backward_filter, but every buffer is caller-owned device memory and the split-K scratch is
+ * a fixed 16 MiB static device array per GPU that loads the library (shapes needing more, or with more
+ * than 256 output / 4096 input channels, return SY_ERR_UNSUPPORTED_SHAPE; the message is in
+ * sy_cuda_last_error(NULL)).  x / dy use the library's padded channels-last layout: image b, pixel (y, x)
+ * at row b * R + (y + 1) * (w + 2) + (x + 1) with R = round_up((h + 2) * (w + 2), 128), rows of
+ * round_up(C, 4) floats, halo rows zero.  dw is OIHW.  The first call on a device looks up the static
+ * array's device address.  Calls share the array, so calls that overlap on the GPU race; the call
+ * returns after `stream` (NULL = legacy default stream) has finished it. */
 SY_API sy_status sy_cuda_conv2d_backward_filter_static(int32_t device, const float *x_padded_device,
                                                        const float *dy_padded_device, int32_t n, int32_t ic,
                                                        int32_t oc, int32_t h, int32_t w, int32_t k, float *dw_device,
@@ -236,6 +242,12 @@ SY_API sy_status sy_cuda_conv_profile_launches(const sy_session *session, double
                                                int32_t *shapes, int32_t capacity, int32_t *count);
 SY_API sy_status sy_cuda_bench_conv(int32_t device, int32_t kind, int32_t n, int32_t ic, int32_t oc, int32_t h,
                                     int32_t w, int32_t k, int32_t iters, double *ms_per_launch);
+
+/* Check of the bounded device waits (no counterpart in the reference, whose CPU loops cannot hang): one CTA
+ * waits on an mbarrier that nothing arrives on, gives up after `spins` polls (1 .. 2^22), frees its TMEM and
+ * exits, as every pipelined kernel here does after a timed-out wait.  Returns SY_ERR_DEVICE with *code set to
+ * the wait's error code (21), and the context stays usable. */
+SY_API sy_status sy_cuda_wait_limit_selftest(int32_t device, int32_t spins, int32_t *code);
 
 /* TrainingParameter.Update (TrainingParameter.cs:21-43) on one tensor: returns SY_ERR_NONFINITE when
  * the result is not finite.  has_grad == 0 leaves everything untouched. */

@@ -121,6 +121,9 @@ def lib():
         L.sy_cuda_step_features.argtypes = [vp, C.POINTER(fp), C.POINTER(Box), ip, C.c_int32, C.POINTER(StepStats)]
         L.sy_cuda_eval_loss_features.argtypes = L.sy_cuda_step_features.argtypes
         L.sy_cuda_get_last_gradients.argtypes = [vp, fp, C.c_int64]
+        L.sy_cuda_get_optimizer_steps.argtypes = [vp, ip]
+        L.sy_cuda_set_optimizer_steps.argtypes = [vp, ip]
+        L.sy_cuda_wait_limit_selftest.argtypes = [C.c_int32, C.c_int32, ip]
         L.sy_cuda_set_epoch.argtypes = [vp, C.c_int32]
         L.sy_cuda_get_last_features.argtypes = [vp, C.c_int32, fp, C.c_int64]
         L.sy_cuda_detection_loss.argtypes = [C.c_int32, C.c_int32, C.c_int32, ip, ip, fp, C.c_int32, C.c_int32,
@@ -163,7 +166,8 @@ EXPORTED = ["sy_cuda_nccl_unique_id", "sy_cuda_create", "sy_cuda_destroy", "sy_c
             "sy_cuda_step_device", "sy_cuda_launch_count", "sy_cuda_bench_conv",
             "sy_cuda_conv2d_backward_filter_static", "sy_cuda_conv_profile", "sy_cuda_eval_loss",
             "sy_cuda_eval_loss_features", "sy_cuda_detection_loss_ex", "sy_cuda_set_epoch",
-            "sy_cuda_conv_profile_launches"]
+            "sy_cuda_conv_profile_launches", "sy_cuda_get_optimizer_steps", "sy_cuda_set_optimizer_steps",
+            "sy_cuda_wait_limit_selftest"]
 
 
 def _check(status: int, session=None):
@@ -524,6 +528,16 @@ class Session:
         """Completed epochs, fed to the progressive end-to-end loss weight (DetectionHead.ProgressiveWeight)."""
         _check(lib().sy_cuda_set_epoch(self._h, epoch), self._h)
 
+    def optimizer_steps(self) -> list:
+        """AdamW steps taken per optimizer group (class branches, cv2, one2one_cv2)."""
+        out = np.zeros(3, np.int32)
+        _check(lib().sy_cuda_get_optimizer_steps(self._h, _ip(out)), self._h)
+        return [int(v) for v in out]
+
+    def set_optimizer_steps(self, steps):
+        v = np.ascontiguousarray(steps, np.int32)
+        _check(lib().sy_cuda_set_optimizer_steps(self._h, _ip(v)), self._h)
+
     def last_gradients(self) -> np.ndarray:
         n = sum(t["numel"] for t in self.params)
         out = np.zeros(n, np.float32)
@@ -551,6 +565,16 @@ class Session:
         out = np.zeros(int(np.prod(shape)), np.float32)
         _check(lib().sy_cuda_get_last_features(self._h, level, _fp(out), out.size), self._h)
         return out.reshape(shape)
+
+
+def wait_limit_selftest(spins: int, device: int = 0) -> int:
+    """Runs the bounded-wait check kernel (sy_cuda_wait_limit_selftest): returns the error code the wait
+    reported; raises SyError for anything but the expected SY_ERR_DEVICE from a timed-out wait."""
+    code = np.zeros(1, np.int32)
+    status = lib().sy_cuda_wait_limit_selftest(device, spins, _ip(code))
+    if status not in (SY_OK, SY_ERR_DEVICE):
+        _check(status)
+    return int(code[0])
 
 
 def launch_count() -> int:
@@ -645,8 +669,7 @@ def conv2d_backward_filter_static(x_padded_ptr: int, dy_padded_ptr: int, n: int,
     status = lib().sy_cuda_conv2d_backward_filter_static(device, C.c_void_p(x_padded_ptr), C.c_void_p(dy_padded_ptr),
                                                          n, ic, oc, h, w, k, C.c_void_p(dw_ptr),
                                                          C.c_void_p(stream_ptr) if stream_ptr else None)
-    if status != SY_OK:
-        _raise(status, "conv2d_backward_filter_static failed")
+    _check(status)
 
 
 def matmul(a, b, device=0):

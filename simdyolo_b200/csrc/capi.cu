@@ -29,6 +29,14 @@ void set_global_error(const std::string& m) {
     g_last_error = m;
 }
 
+}  // namespace
+
+namespace sy {
+void set_last_error(const std::string& message) { set_global_error(message); }
+}  // namespace sy
+
+namespace {
+
 template <class F>
 sy_status guarded(sy_session* s, F&& f) {
     try {
@@ -285,6 +293,35 @@ sy_status sy_cuda_bench_conv(int32_t device, int32_t kind, int32_t n, int32_t ic
 sy_status sy_cuda_set_epoch(sy_session* session, int32_t epoch) {
     if (!session) return SY_ERR_INVALID_ARGUMENT;
     return guarded(session, [&] { return session->impl->set_epoch(epoch); });
+}
+
+sy_status sy_cuda_get_optimizer_steps(const sy_session* session, int32_t steps[3]) {
+    if (!session) return SY_ERR_INVALID_ARGUMENT;
+    sy_session* s = const_cast<sy_session*>(session);
+    return guarded(s, [&] { return s->impl->get_optimizer_steps(steps); });
+}
+
+sy_status sy_cuda_set_optimizer_steps(sy_session* session, const int32_t steps[3]) {
+    if (!session) return SY_ERR_INVALID_ARGUMENT;
+    return guarded(session, [&] { return session->impl->set_optimizer_steps(steps); });
+}
+
+sy_status sy_cuda_wait_limit_selftest(int32_t device, int32_t spins, int32_t* code) {
+    return guarded(nullptr, [&] {
+        if (!code || spins < 1 || spins > (int32_t)sy::kSpinLimit)
+            throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "wait_limit_selftest: spins out of range");
+        check_device(device);
+        Scratch s;
+        int* err = s.get<int>(1);
+        CK(cudaMemset(err, 0, sizeof(int)));
+        sy::wait_limit_selftest((uint32_t)spins, 21, err, 0);
+        CK(cudaDeviceSynchronize());
+        int e = 0;
+        CK(cudaMemcpy(&e, err, sizeof(int), cudaMemcpyDeviceToHost));
+        *code = e;
+        if (e) throw sy::SyError(SY_ERR_DEVICE, "device wait limit exceeded (code " + std::to_string(e) + ")");
+        return SY_OK;
+    });
 }
 
 sy_status sy_cuda_get_last_gradients(const sy_session* session, float* host, int64_t count) {

@@ -833,14 +833,14 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
     for (int t = 0; t < taps; t++) order[t] = t;
     std::sort(order, order + taps, [&](int a, int b) { return shift[a] < shift[b] || (shift[a] == shift[b] && a < b); });
     const long sub_tiles = m_rows / kTileM;
-    static uint64_t attr_devices = 0;   // devices whose kernel attributes are set
-    if (once_per_device(attr_devices)) {
-        cudaFuncSetAttribute(conv_fwd_tc_kernel<8, kEpiPlain>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        cudaFuncSetAttribute(conv_fwd_tc_kernel<8, kEpiStats>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        cudaFuncSetAttribute(conv_fwd_tc_kernel<8, kEpiGeneric>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        cudaFuncSetAttribute(conv_fwd_tc_kernel<12, kEpiBnBwd>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        cudaFuncSetAttribute(conv_fwd_tc_kernel<12, kEpiGeneric>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    }
+    static PerDeviceOnce attr_once;   // devices whose kernel attributes are set
+    once_per_device(attr_once, [] {
+        set_max_dynamic_smem(conv_fwd_tc_kernel<8, kEpiPlain>, 227 * 1024, "conv_fwd_tc_kernel attribute");
+        set_max_dynamic_smem(conv_fwd_tc_kernel<8, kEpiStats>, 227 * 1024, "conv_fwd_tc_kernel attribute");
+        set_max_dynamic_smem(conv_fwd_tc_kernel<8, kEpiGeneric>, 227 * 1024, "conv_fwd_tc_kernel attribute");
+        set_max_dynamic_smem(conv_fwd_tc_kernel<12, kEpiBnBwd>, 227 * 1024, "conv_fwd_tc_kernel attribute");
+        set_max_dynamic_smem(conv_fwd_tc_kernel<12, kEpiGeneric>, 227 * 1024, "conv_fwd_tc_kernel attribute");
+    });
     CUtensorMap ta = make_map_2d(in.base, in.channels, in.rows, in.pitch, 32, kBoxRows);
     constexpr int kSmemTotal = 216 * 1024;   // A ring + weights (+ the trunk epilogue's output tiles)
     const bool plain_epilogue = !(ep.bn.grad_part || ep.bn.stats_part || ep.pre);
@@ -1292,10 +1292,9 @@ void conv_tc_wgrad(const View& x, const View& dy, int taps, const Grid& grid, fl
     CUtensorMap tx = make_map_2d(x.base, x.channels, x.rows, x.pitch, 32, kWgradBK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     CUtensorMap tg = make_map_2d(dy.base, dy.channels, dy.rows, dy.pitch, 32, kWgradBK,
                                  CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
-    static uint64_t attr_devices = 0;   // devices whose kernel attributes are set
-    if (once_per_device(attr_devices)) {
-        cudaFuncSetAttribute(conv_wgrad_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    }
+    static PerDeviceOnce attr_once;   // devices whose kernel attributes are set
+    once_per_device(attr_once,
+                    [] { set_max_dynamic_smem(conv_wgrad_tc_kernel, 227 * 1024, "conv_wgrad_tc_kernel attribute"); });
     const size_t smem = 1024 + (size_t)p.stages * stage_bytes + (2 * p.stages + 2) * 8 + 16;
     conv_wgrad_tc_kernel<<<dim3(p.m_tiles, splits), kWgradThreads, smem, stream>>>(tx, tg, p);
     launch_check("conv_wgrad_tc_kernel");

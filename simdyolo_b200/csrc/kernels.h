@@ -5,6 +5,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
 #include "common.cuh"
 
 namespace sy {
@@ -13,17 +17,30 @@ namespace sy {
 // Every launch site calls it once, so it also counts this library's kernel launches.
 void launch_check(const char* what);
 
-// True the first time it is called with `devices` while a given device is current (for per-device
-// one-time set-up such as kernel attributes, which CUDA keeps per device); always true on device
-// ordinals of 64 and above.
-inline bool once_per_device(uint64_t& devices) {
+// Per-device one-time set-up (kernel attributes, which CUDA keeps per device): `setup` runs the first
+// time `once` is used while a given device is current.  The lock is held across the check, the set-up
+// and the record, so a second host thread on the same device waits until the attributes are in place;
+// a set-up that throws is not recorded and runs again on the next call.  Device ordinals of 64 and
+// above run `setup` every time.
+struct PerDeviceOnce {
+    std::mutex mu;
+    uint64_t done = 0;
+};
+template <class F>
+void once_per_device(PerDeviceOnce& once, F&& setup) {
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return true;
-    const uint64_t bit = 1ull << dev;
-    if (devices & bit) return false;
-    devices |= bit;
-    return true;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+    const uint64_t bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0;
+    std::lock_guard<std::mutex> lock(once.mu);
+    if (bit && (once.done & bit)) return;
+    setup();
+    once.done |= bit;
+}
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) that raises on failure.
+template <class K>
+void set_max_dynamic_smem(K* kernel, int bytes, const char* what) {
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 long long launch_count();
 
@@ -181,6 +198,11 @@ struct WeightLayoutJob {
 };
 void weights_layout_batch(const WeightLayoutJob* table_device, int jobs, long max_elems, cudaStream_t stream,
                           bool round_tf32 = false);
+
+// One CTA that allocates TMEM, waits on an mbarrier nothing arrives on, gives up after `spins` polls,
+// writes `code` to *err, frees the TMEM and exits: exercises the bounded-wait path of the pipelined
+// kernels without anything asynchronous in flight.  spins in [1, kSpinLimit].
+void wait_limit_selftest(uint32_t spins, int code, int* err, cudaStream_t stream);
 
 // ---------------------------------------------------------------- backbone helpers
 void maxpool5_padded(const View& in, const View& out, int batch, const Grid& g, cudaStream_t stream);

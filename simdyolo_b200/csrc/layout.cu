@@ -259,6 +259,34 @@ __global__ void rgb_to_phase_kernel(const uint8_t* rgb, int batch, int size, Pha
     }
 }
 
+// Bounded-wait check (wait_limit_selftest): the shape of every pipelined kernel here, with the producer
+// missing.  Warp 0 allocates TMEM, warp 1 waits on an mbarrier that nothing arrives on, gives up after
+// `spins` polls and records `code`; then every warp reaches the closing barrier and warp 0 frees the TMEM,
+// as the conv kernels do after a timed-out wait.  Nothing asynchronous is in flight.
+__global__ void wait_limit_selftest_kernel(uint32_t spins, int code, int* err) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ uint32_t tmem_slot;
+    const int warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(&tmem_slot, 32);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 32) mbar_wait_limit(&bar, 0, err, code, spins);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_slot, 32);
+    }
+}
+
 int blocks_for(long n) { return (int)std::min<long>(65535L * 16, std::max<long>(1, (n + 255) / 256)); }
 
 }  // namespace
@@ -391,6 +419,12 @@ void tf32_split(const View& src, float* big, float* small, cudaStream_t stream) 
     const long n = src.rows * src.channels;
     tf32_split_kernel<<<blocks_for(n), 256, 0, stream>>>(src.base, src.pitch, src.channels, src.rows, big, small);
     launch_check("tf32_split_kernel");
+}
+
+void wait_limit_selftest(uint32_t spins, int code, int* err, cudaStream_t stream) {
+    if (spins < 1 || spins > kSpinLimit) throw std::runtime_error("wait_limit_selftest: spins out of range");
+    wait_limit_selftest_kernel<<<1, 64, 0, stream>>>(spins, code, err);
+    launch_check("wait_limit_selftest_kernel");
 }
 
 void rgb_to_phase(const uint8_t* rgb, int batch, int size, const PhaseOut& dst, cudaStream_t stream) {

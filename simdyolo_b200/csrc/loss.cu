@@ -708,9 +708,8 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
     if (max_boxes > 0) topk_kernel<<<dim3(max_boxes, batch), 256, 0, stream>>>(p);
     launch_check("topk_kernel");
     const size_t owner_bytes = sizeof(int) * (size_t)p.anchors;
-    static uint64_t attr_devices = 0;   // devices whose kernel attribute is set
-    if (once_per_device(attr_devices))
-        cudaFuncSetAttribute(assign_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    static PerDeviceOnce attr_once;   // devices whose kernel attribute is set
+    once_per_device(attr_once, [] { set_max_dynamic_smem(assign_kernel, 160 * 1024, "assign_kernel attribute"); });
     if (owner_bytes > 160 * 1024) throw std::runtime_error("detection_loss: too many anchors");
     assign_kernel<<<batch, 256, owner_bytes, stream>>>(p);
     launch_check("assign_kernel");

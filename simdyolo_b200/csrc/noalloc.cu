@@ -1,21 +1,24 @@
 // Allocation-free variant of the weight-gradient convolution (sy_cuda_conv2d_backward_filter_static).
 //
-// Some callers cannot call cudaMalloc at all: a host that runs inside a CUDA graph capture or a
-// memory-pool-managed process (where a stray cudaMalloc breaks the capture or the pool's accounting),
-// or an embedding runtime whose allocator owns every device byte.  Those callers bring their own
-// input and output buffers; the only extra device memory this kernel needs, its split-K partial
-// sums, lives in the fixed array below instead of a per-call allocation.
+// Some hosts cannot let a library call cudaMalloc: an embedding runtime or caching allocator that has
+// already reserved all device memory for its own pool (a further cudaMalloc fails, or bypasses the pool's
+// accounting so that its limits no longer hold), or a latency-bound serving loop that must not take the
+// driver's allocation locks and implicit synchronisation in the middle of a request.  Those hosts bring
+// their own input and output buffers; the only extra device memory this kernel needs, its split-K partial
+// sums, lives in the fixed array below instead of a per-call allocation, and the call makes no other
+// allocation (no cudaMalloc, cudaFree or allocating library routine).
 //
 // The array is a file-scope __device__ variable: every GPU that loads this library holds its
 // kStaticScratchFloats floats (16 MiB) until the process exits.  In host code `g_static_scratch`
 // names a host-side stand-in, not device memory, so its device address is looked up once per device
 // with cudaGetSymbolAddress (with that device current) and passed to the kernels.  That lookup
-// happens on the first call on each device; make that first call before any stream capture starts.
+// happens on the first call on each device.
 //
 // All calls share the one array and leave the previous call's partial sums in it; nothing has to
-// start at zero because the kernel writes every partial sum it later reads.  Calls that overlap on
-// the GPU (different streams or threads at the same time) race on the array and must be serialised
-// by the caller.
+// start at zero because the kernel writes every partial sum it later reads (the error flag beside it
+// is cleared at the start of every call).  Calls that overlap on the GPU (different streams or host
+// threads at the same time) race on the array and must be serialised by the caller.  Every call waits
+// for its stream to finish before it returns, to read the kernels' error flag.
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -66,7 +69,10 @@ extern "C" sy_status sy_cuda_conv2d_backward_filter_static(int32_t device, const
         if (!x_padded_device || !dy_padded_device || !dw_device || n < 1 || ic < 1 || oc < 1 || h < 1 || w < 1 ||
             !(k == 1 || k == 3))
             throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "conv2d_backward_filter_static: bad arguments");
-        if (oc > 256 || ic > 4096) throw sy::SyError(SY_ERR_UNSUPPORTED_SHAPE, "conv2d_backward_filter_static: oc > 256");
+        if (oc > 256)
+            throw sy::SyError(SY_ERR_UNSUPPORTED_SHAPE, "conv2d_backward_filter_static: more than 256 output channels");
+        if (ic > 4096)
+            throw sy::SyError(SY_ERR_UNSUPPORTED_SHAPE, "conv2d_backward_filter_static: more than 4096 input channels");
         int count = 0;
         if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count || device >= kMaxDevices)
             throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "invalid CUDA device");
@@ -94,8 +100,10 @@ extern "C" sy_status sy_cuda_conv2d_backward_filter_static(int32_t device, const
         if (flag) throw sy::SyError(SY_ERR_DEVICE, "wgrad kernel wait limit exceeded");
         return SY_OK;
     } catch (const sy::SyError& ex) {
+        sy::set_last_error(ex.what());
         return ex.code;
-    } catch (const std::exception&) {
+    } catch (const std::exception& ex) {
+        sy::set_last_error(ex.what());
         return SY_ERR_DEVICE;
     }
 }

@@ -947,6 +947,20 @@ void Session::combine_losses(int images, int epoch, double* box, double* cls, do
     }
 }
 
+int Session::get_optimizer_steps(int32_t steps[3]) const {
+    if (!steps) throw SyError(SY_ERR_INVALID_ARGUMENT, "steps missing");
+    for (int g = 0; g < 3; g++) steps[g] = adam_steps_[g];
+    return SY_OK;
+}
+
+int Session::set_optimizer_steps(const int32_t steps[3]) {
+    if (!steps) throw SyError(SY_ERR_INVALID_ARGUMENT, "steps missing");
+    for (int g = 0; g < 3; g++)
+        if (steps[g] < 0) throw SyError(SY_ERR_INVALID_ARGUMENT, "optimizer step counts must not be negative");
+    for (int g = 0; g < 3; g++) adam_steps_[g] = steps[g];
+    return SY_OK;
+}
+
 int Session::set_epoch(int epoch) {
     if (epoch < 0) throw SyError(SY_ERR_INVALID_ARGUMENT, "epoch must not be negative");
     epoch_ = epoch;

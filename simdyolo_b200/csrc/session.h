@@ -20,6 +20,9 @@ struct SyError : std::runtime_error {
     SyError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
 };
 
+// Records `message` as the process-wide last error returned by sy_cuda_last_error(NULL).
+void set_last_error(const std::string& message);
+
 struct TensorEntry {
     std::string name;
     int kind;            // 0 parameter, 1 buffer
@@ -90,6 +93,9 @@ public:
     int evaluate(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
                  const int32_t* counts, int images, sy_step_stats* out);
     int set_epoch(int epoch);
+    // AdamW steps taken per optimizer group (class branches, cv2, one2one_cv2)
+    int get_optimizer_steps(int32_t steps[3]) const;
+    int set_optimizer_steps(const int32_t steps[3]);
     int set_tensor(int index, const float* host, long count);
     int get_tensor(int index, float* host, long count) const;
     int set_opt_state(int index, int moment, const float* host, long count);

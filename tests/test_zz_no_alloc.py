@@ -1,10 +1,11 @@
 """The allocation-free weight-gradient entry point (sy_cuda_conv2d_backward_filter_static).
 
-It exists for callers that cannot call cudaMalloc (a graph capture in progress, an external pool or
-runtime that owns all device memory): they pass their own device buffers and the split-K scratch is a
-static device array.  Its output must equal the ordinary entry point's (which allocates its scratch)
-within the TF32 tolerance the other GPU tests use, on consecutive calls that reuse the static scratch.
-This file is collected last so a failure here never hides the other tests.
+It exists for hosts that cannot let a library call cudaMalloc (an embedding runtime or caching allocator
+that has reserved all device memory for its own pool, or a serving loop that must not take the driver's
+allocation locks mid-request): they pass their own device buffers and the split-K scratch is a static
+device array.  Its output must equal the ordinary entry point's (which allocates its scratch) within the
+TF32 tolerance the other GPU tests use, on consecutive calls that reuse the static scratch.  This file is
+collected last so a failure here never hides the other tests.
 """
 import numpy as np
 import pytest
@@ -69,6 +70,10 @@ def test_static_scratch_writes_only_the_callers_weight_gradient():
 
 def test_static_scratch_rejects_oversized_problems():
     tiny = torch.zeros(16, device="cuda:0")
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(NotImplementedError, match="scratch"):
         # P3-sized batch of 64: its split-K partial sums exceed the 16 MiB static scratch
         sy.conv2d_backward_filter_static(tiny.data_ptr(), tiny.data_ptr(), 64, 64, 144, 80, 80, 3, tiny.data_ptr())
+    with pytest.raises(NotImplementedError, match="input channels"):
+        sy.conv2d_backward_filter_static(tiny.data_ptr(), tiny.data_ptr(), 1, 5000, 16, 8, 8, 1, tiny.data_ptr())
+    with pytest.raises(NotImplementedError, match="output channels"):
+        sy.conv2d_backward_filter_static(tiny.data_ptr(), tiny.data_ptr(), 1, 16, 300, 8, 8, 1, tiny.data_ptr())
