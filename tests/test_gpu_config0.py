@@ -20,11 +20,16 @@ test_config0_head_gradients_against_float64 measures that distance from a float6
 the GPU to be within 1e-5 of the float64 result.
 
 TF32 mode: loss parts within 2e-3 (the class loss is the exact sum of the terms, which differs from the
-reference's float running sum by about 1.3e-3 at this size).  Gradients within 4e-3 relative L2.  2e-3 is
-below what TF32 operands allow here: the same test evaluates the head in float64 with every conv operand
-rounded to TF32 as the tensor-core path stores it, lands at about 2.7e-3 from the exact gradient, and
-requires the GPU to be within 10 % of that figure.  The trunk's own TF32 rounding (features about 3e-4
-from FP32) adds the rest.
+reference's float running sum by about 1.3e-3 at this size).  Every step's gradient is also checked against
+the oracle's head run from the GPU's own state (its frozen features and its parameters before the step):
+within 2.5e-3 (1.6-2.0e-3 measured, the TF32 operands' own error; test_config0_head_gradients_against_float64
+evaluates the head in float64 with every conv operand rounded to TF32 as the tensor-core path stores it and
+requires the GPU to sit within 10 % of that figure).  Against the oracle's independent trajectory the TF32
+gradients agree to about 3.5e-3 on most steps, but on a few steps (2.5e-2 at most measured) a positive's
+predicted box edge lies within TF32 noise of its ground-truth edge, where the reference's CIoU gradient
+switches branch (the max / min of the enclosing and intersection boxes, DetectionLoss.cs:171-183): that step's
+level gradient then differs by a few percent on one branch.  So the trajectory is held to a median of 4e-3
+per step and 6e-3 on the final parameter update, velocity and BatchNorm buffers.
 """
 import ctypes as C
 
@@ -40,8 +45,10 @@ from tests.helpers import (backbone_desc, f64_head_gradient, head_desc, head_gra
 pytestmark = pytest.mark.gpu
 
 IMAGE, BATCH, STEPS, SEED = 640, 8, 16, 0
-BOUNDS = {sy.SY_PRECISION_3XTF32: dict(loss=1e-5, cls=1e-5, grad=2e-5, state=2e-5),
-          sy.SY_PRECISION_TF32: dict(loss=2e-3, cls=2e-3, grad=4e-3, state=4e-3)}
+BOUNDS = {sy.SY_PRECISION_3XTF32: dict(loss=1e-5, cls=1e-5, features=1e-5, grad_state=2e-5, grad=2e-5, grad_median=2e-5,
+                                       state=2e-5),
+          sy.SY_PRECISION_TF32: dict(loss=2e-3, cls=2e-3, features=2e-3, grad_state=2.5e-3, grad=None, grad_median=4e-3,
+                                     state=6e-3)}
 
 
 def config0(precision, backbone=True):
@@ -82,7 +89,7 @@ def oracle_trajectory():
         assert res.status == 0
         steps.append(dict(box=res.box, cls=res.cls, dfl=res.dfl, positives=res.positives,
                           connected=res.box_has_grad, grad=grad))
-    return dict(steps=steps, params=p, buffers=b, velocity=v, start=params)
+    return dict(steps=steps, params=p, buffers=b, velocity=v, start=params, features=oracle_features(cfg, bparams, images))
 
 
 def oracle_features(cfg, bparams, images):
@@ -108,38 +115,51 @@ def test_config0_sixteen_steps_match_oracle(oracle_run, precision):
     cfg = config0(precision)
     tensors, params, buffers, bparams = initial_state(cfg)
     images, truth = workload()
-    worst = dict(loss=0.0, cls=0.0, grad=0.0, checksum=0.0)
+    shapes = [(BATCH, cfg.feature_channels[l], IMAGE >> (3 + l), IMAGE >> (3 + l)) for l in range(3)]
+    traj = []
     with sy.Session(cfg) as s:
         assert [(t["name"], t["shape"]) for t in s.tensors] == [(t["name"], t["shape"]) for t in tensors]
         s.set_flat_params(params)
         s.set_flat_buffers(buffers)
         s.set_backbone(bparams)
         for k, ref in enumerate(oracle_run["steps"]):
+            p_before, b_before = s.flat_params(), s.flat_buffers()
             st = s.step(images, truth)
             g = s.last_gradients()
+            feats = [s.last_features(l, shapes[l]) for l in range(3)]
+            if k == 0:
+                ferr = max(rel_l2(feats[l], oracle_run["features"][l]) for l in range(3))
+                print(f"trunk features vs oracle: {ferr:.2e}")
+                assert ferr <= bound["features"]
+            # the oracle's head step from the GPU's own state (same features, same parameters)
+            _, og, *_ = oracle_head_step(cfg, tensors, p_before, b_before, np.zeros_like(p_before), feats, truth)
             errs = dict(box=abs(st.box - ref["box"]) / max(abs(ref["box"]), 1e-6),
                         dfl=abs(st.dfl - ref["dfl"]) / max(abs(ref["dfl"]), 1e-6),
                         cls=abs(st.cls - ref["cls"]) / abs(ref["cls"]),
-                        grad=rel_l2(g, ref["grad"]))
+                        grad=rel_l2(g, ref["grad"]), grad_state=rel_l2(g, og))
             # checksum: sum |g| of the batch-averaged gradient, as sy_step_stats reports it
             want_sum = float(np.abs(ref["grad"].astype(np.float64)).sum()) / BATCH
             errs["checksum"] = abs(st.grad_checksum - want_sum) / want_sum
             print(f"step {k:2d}: box {st.box:.6f} cls {st.cls:.6f} dfl {st.dfl:.6f} pos {st.positives} | "
-                  f"rel box {errs['box']:.2e} cls {errs['cls']:.2e} dfl {errs['dfl']:.2e} "
-                  f"grad {errs['grad']:.2e} checksum {errs['checksum']:.2e}")
+                  f"rel box {errs['box']:.2e} cls {errs['cls']:.2e} dfl {errs['dfl']:.2e} | gradient vs oracle "
+                  f"at the GPU's state {errs['grad_state']:.2e}, vs the oracle's trajectory {errs['grad']:.2e} "
+                  f"(checksum {errs['checksum']:.2e})")
             assert st.positives == ref["positives"], (k, st.positives, ref["positives"])
             assert st.box_has_grad == ref["connected"]
             assert errs["box"] <= bound["loss"] and errs["dfl"] <= bound["loss"], (k, errs)
             assert errs["cls"] <= bound["cls"], (k, errs)
-            assert errs["grad"] <= bound["grad"], (k, errs)
-            assert errs["checksum"] <= bound["grad"], (k, errs)
-            worst = {key: max(worst[key], errs[key] if key != "loss" else max(errs["box"], errs["dfl"]))
-                     for key in worst}
+            assert errs["grad_state"] <= bound["grad_state"], (k, errs)
+            if bound["grad"] is not None:
+                assert errs["grad"] <= bound["grad"], (k, errs)
+                assert errs["checksum"] <= bound["grad"], (k, errs)
+            traj.append(errs["grad"])
         start = oracle_run["start"]
         state = dict(update=rel_l2(s.flat_params() - start, oracle_run["params"] - start),
                      velocity=rel_l2(s.flat_velocity(), oracle_run["velocity"]),
                      buffers=rel_l2(s.flat_buffers(), oracle_run["buffers"]))
-    print(f"precision {precision}: worst per-step {worst}; after {STEPS} steps {state}")
+    print(f"precision {precision}: trajectory gradient median {np.median(traj):.2e} max {max(traj):.2e}; "
+          f"after {STEPS} steps {state}")
+    assert np.median(traj) <= bound["grad_median"]
     for key, err in state.items():
         assert err <= bound["state"], (key, err)
 
