@@ -49,9 +49,11 @@ WORKLOADS = {
                           "RGB24, 1-30 GT boxes/image (w/h log-uniform 12-512 px), SGD lr 0.01 m 0.937 wd 5e-4"),
 }
 METRIC = WORKLOADS["v8n-640"]["metric"]
-# mean DRAM bytes (read + write) per conv_fwd_tc_kernel launch of one batch-64 step, from an ncu
-# capture at batch 8 scaled by 8 (profiles/conv_fwd_dram_yolov8n_640.md)
-CONV_DRAM_BYTES_PER_LAUNCH = 8 * (905.531904e6 + 1.27616e6) / 74
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per conv_fwd_tc_kernel launch, mean over the
+# launches of one batch-64 YOLOv8n step at 640x640, measured with ncu on that workload (the command is in
+# the profile summary of this kernel); None for other workloads, which were not captured.
+CONV_DRAM_BYTES_PER_LAUNCH = {"v8n-640": None}
+PASS_NAMES = {0: "trunk", 1: "trunk s2", 2: "head fwd", 3: "head dgrad"}
 
 
 def parse():
@@ -65,6 +67,7 @@ def parse():
     p.add_argument("--image", type=int, default=None)
     p.add_argument("--model", default=None)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-3x", action="store_true", help="skip the 3xTF32 (FP32 parity) timing loop")
     p.add_argument("--precision", default="tf32", choices=["tf32", "3xtf32"],
                    help="3xtf32: the FP32 parity mode (three split-operand TF32 passes per convolution)")
     p.add_argument("--conv-sweep", action="store_true",
@@ -307,6 +310,36 @@ def run_conv_sweep(args):
             }), flush=True)
 
 
+# ---------------------------------------------------------------- per-layer roofline
+
+def layer_classes(launches, batch, hbm_gbs, tf32_tflops):
+    """Per class of tensor-core conv launch (pass, taps, output grid) over one profiled step: launches, device
+    ms, TFLOP/s, algorithmic bytes (each input element, output element and weight moved once; the
+    BatchNorm-backward data gradient also reads the BatchNorm input) and the class's own bound, the larger
+    of bytes / HBM rate and FLOPs / dense TF32 rate; frac = bound time / measured time."""
+    classes = {}
+    for ms, gflop, (ps, ic, oc, taps, h, w) in launches:
+        in_pix = 4 * h * w if ps == 1 else h * w
+        byts = 4.0 * batch * (in_pix * ic + h * w * oc) + 4.0 * oc * ic * taps
+        if ps == 3:
+            byts += 4.0 * batch * h * w * oc
+        key = f"{PASS_NAMES[ps]} {'3x3' if taps == 9 else '1x1'} {h}x{w}"
+        c = classes.setdefault(key, dict(launches=0, ms=0.0, gflop=0.0, bytes=0.0))
+        c["launches"] += 1
+        c["ms"] += ms
+        c["gflop"] += gflop
+        c["bytes"] += byts
+    out = []
+    for key, c in sorted(classes.items(), key=lambda kv: -kv[1]["ms"]):
+        t_hbm = c["bytes"] / (hbm_gbs * 1e9) * 1e3
+        t_tc = c["gflop"] / (tf32_tflops * 1e3) * 1e3
+        bound = "hbm" if t_hbm > t_tc else "tensor"
+        out.append({"class": key, "launches": c["launches"], "ms": round(c["ms"], 4),
+                    "tflops": round(c["gflop"] / c["ms"], 1), "gbs": round(c["bytes"] / c["ms"] / 1e6, 1),
+                    "bound": bound, "frac": round(max(t_hbm, t_tc) / c["ms"], 3)})
+    return out
+
+
 # ---------------------------------------------------------------- our arm
 
 def run_ours(args, rank, world, local_rank, dist):
@@ -363,6 +396,7 @@ def run_ours(args, rank, world, local_rank, dist):
     sess.conv_profile(True)
     for i in range(prof_steps):
         sess.step_device(dev_images[i % nbatches].data_ptr(), args.batch, truths[i % nbatches])
+    per_launch = sess.conv_profile_launches()
     conv_ms, conv_gflop, conv_launches = sess.conv_profile(False)
     barrier()
     dev_ms = max_over_ranks(dev_ms)
@@ -374,16 +408,48 @@ def run_ours(args, rank, world, local_rank, dist):
             sess.step(pinned[i % nbatches].numpy(), truths[i % nbatches])
         barrier()
         e2e_ms = 0.0
+        wall0 = time.perf_counter()
         for i in range(args.steps):
             st = sess.step(pinned[i % nbatches].numpy(), truths[i % nbatches])
             e2e_ms += st.device_ms
         barrier()
+        e2e_wall = max_over_ranks(time.perf_counter() - wall0)
         e2e_ms = max_over_ranks(e2e_ms)
         h2d = args.batch * args.image * args.image * 3 + sum(len(t) for t in truths[0]) * 20 + (args.batch + 1) * 4
         d2h = args.batch * (16 + 4 + 4) + 16 * 4 + 64 * 8 + 2 * 4
         e2e = {"value": world * args.batch * args.steps / (e2e_ms / 1000.0), "unit": "images/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "how": "sy_cuda_step with pinned host images: H2D copy, all kernels, per-image loss D2H"}
+               "wall_value": world * args.batch * args.steps / e2e_wall,
+               "how": "sy_cuda_step with pinned host images: H2D copy, all kernels, per-image loss D2H; value from "
+                      "CUDA events inside each call, wall_value from the host clock around the whole loop "
+                      "(host-side box packing and validation included), max over ranks"}
+
+    # the FP32 parity mode (3xTF32) on the same workload: a second, shorter timed loop
+    x3 = None
+    if args.precision == "tf32" and not args.no_3x:
+        cfg3 = sy.make_config(args.model, image_size=args.image, max_batch=args.batch, max_boxes=args.max_boxes,
+                              num_classes=args.nc, lr=args.lr, weight_decay=args.weight_decay,
+                              optimizer=sy.SY_OPT_ADAMW if args.optimizer == "adamw" else sy.SY_OPT_SGD,
+                              device=local_rank, rank=rank, world_size=world,
+                              nccl_id=dp.broadcast_nccl_id(dist, rank) if world > 1 else b"",
+                              precision=sy.SY_PRECISION_3XTF32)
+        s3 = sy.Session(cfg3)
+        s3.set_flat_params(params)
+        s3.set_flat_buffers(buffers)
+        s3.set_backbone(data.backbone_params(args.model, seed=0))
+        steps3 = max(3, min(10, args.steps))
+        for i in range(3):
+            s3.step_device(dev_images[i % nbatches].data_ptr(), args.batch, truths[i % nbatches])
+        barrier()
+        ms3 = 0.0
+        for i in range(steps3):
+            ms3 += s3.step_device(dev_images[i % nbatches].data_ptr(), args.batch, truths[i % nbatches]).device_ms
+        barrier()
+        ms3 = max_over_ranks(ms3)
+        s3.close()
+        x3 = {"value": world * args.batch * steps3 / (ms3 / 1000.0), "unit": "images/s", "steps": steps3,
+              "ms_per_step": ms3 / steps3,
+              "how": "same workload and inputs, every convolution as three split-operand TF32 passes (FP32 parity)"}
 
     line = None
     if rank == 0:
@@ -397,10 +463,10 @@ def run_ours(args, rank, world, local_rank, dist):
                 "achieved": achieved, "peak": tf32_sustained, "unit": "TFLOP/s", "frac": achieved / tf32_sustained,
                 "peak_note": f"dense TF32 = 1/2 of the {src} sustained bf16 GEMM rate "
                              f"({peaks.get('bf16_tflops_sustained', peaks['bf16_tflops'])} TF/s)",
-                "traffic": CONV_DRAM_BYTES_PER_LAUNCH * args.batch / 64 if args.workload == "v8n-640" else None,
-                "traffic_note": "dram__bytes_read+write per conv_fwd_tc_kernel launch, mean over the 74 launches of "
-                                "one step captured with ncu at batch 8 and scaled by 8 (writes stay in L2 at that "
-                                "size); profiles/conv_fwd_dram_yolov8n_640.md",
+                "traffic": (CONV_DRAM_BYTES_PER_LAUNCH.get(args.workload) if args.batch == 64 and world == 1
+                            and args.precision == "tf32" else None),
+                "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per conv_fwd_tc_kernel launch, mean over "
+                                "the launches of one batch-64 step, from an ncu capture of this workload",
                 "launches": conv_launches, "ms_per_launch": conv_ms / max(1, conv_launches),
                 "how": f"CUDA events on the session stream around each conv launch, {prof_steps} steps run right "
                        f"after the timed region on the same inputs",
@@ -422,6 +488,9 @@ def run_ours(args, rank, world, local_rank, dist):
                            "image": args.image, "parallelism": f"dp{world}",
                            "l2": "per-step working set is several GB of activations (>> 126 MB L2); no flush"},
                 "e2e": e2e, "gpu_launches": launches, "wall_s_timed": wall, "roofline": roof}
+        if x3 is not None:
+            line["3xtf32"] = x3
+        line["roofline"]["layers"] = layer_classes(per_launch, args.batch, peaks["hbm_gbs"], tf32_sustained)
         if world == 1:
             line["cpu_baseline"] = cpu_baseline(args, cpu_threads())
         line["clocks"] = clocks.summary()

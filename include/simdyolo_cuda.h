@@ -94,6 +94,10 @@ typedef struct sy_config {
      * weight follows DetectionHead.ProgressiveWeight(epoch, schedule_epochs). */
     int32_t end_to_end;
     int32_t schedule_epochs;    /* LossScheduleEpochs (YoloTrainer.cs:106): TrainingOptions.Epochs */
+    /* Data-parallel sessions: a step whose collectives have not completed after comm_timeout_ms (0: 300000)
+     * aborts the communicator (ncclCommAbort) and returns SY_ERR_COMM; the session then refuses further steps
+     * and can only be destroyed. */
+    int32_t comm_timeout_ms;
 } sy_config;
 
 /* Per-step results, summed over the global batch (all ranks). */

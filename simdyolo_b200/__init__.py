@@ -75,7 +75,7 @@ class Config(C.Structure):
                 ("bn_eps", C.c_float), ("bn_momentum", C.c_float), ("optimizer", C.c_int32), ("lr", C.c_float),
                 ("momentum", C.c_float), ("weight_decay", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float),
                 ("adam_eps", C.c_float), ("precision", C.c_int32), ("end_to_end", C.c_int32),
-                ("schedule_epochs", C.c_int32)]
+                ("schedule_epochs", C.c_int32), ("comm_timeout_ms", C.c_int32)]
 
 
 class StepStats(C.Structure):
@@ -350,10 +350,12 @@ def make_config(model: str = "yolov8n", image_size: int = 640, max_batch: int = 
                 backbone: bool = True, optimizer: int = SY_OPT_SGD, lr: float = 0.01, momentum: float = 0.937,
                 weight_decay: float = 5e-4, beta1: float = 0.9, beta2: float = 0.999, adam_eps: float = 1e-8,
                 bn_eps: float = 1e-3, bn_momentum: float = 0.03, precision: int = SY_PRECISION_TF32,
-                end_to_end: bool = False, reg_max: int = 16, schedule_epochs: int = 100) -> Config:
+                end_to_end: bool = False, reg_max: int = 16, schedule_epochs: int = 100,
+                comm_timeout_ms: int = 0) -> Config:
     """Session description for `model`'s trunk and Detect head.  end_to_end adds the one2one_cv2 /
     one2one_cv3 branches (YOLOv10 v10Detect with reg_max 16; YOLO26-style progressive loss with
-    reg_max 1, TrainingHeadSchema.cs:17-21); schedule_epochs is the progressive schedule length."""
+    reg_max 1, TrainingHeadSchema.cs:17-21); schedule_epochs is the progressive schedule length.
+    comm_timeout_ms bounds a data-parallel step's wait for its collectives (0: 300 s)."""
     width, depth, max_ch = MODELS[model]
     feats = yolov8_channels(width, max_ch)
     cfg = Config()
@@ -380,6 +382,7 @@ def make_config(model: str = "yolov8n", image_size: int = 640, max_batch: int = 
     cfg.beta1, cfg.beta2, cfg.adam_eps = beta1, beta2, adam_eps
     cfg.precision = precision
     cfg.end_to_end, cfg.schedule_epochs = int(bool(end_to_end)), schedule_epochs
+    cfg.comm_timeout_ms = comm_timeout_ms
     return cfg
 
 

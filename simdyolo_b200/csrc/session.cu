@@ -11,11 +11,13 @@
 
 #include <algorithm>
 #include <array>
+#include <chrono>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
+#include <thread>
 
 #include "session.h"
 
@@ -40,6 +42,7 @@ struct NcclApi {
     int (*AllGather)(const void*, void*, size_t, int, void*, cudaStream_t) = nullptr;
     int (*CommDestroy)(void*) = nullptr;
     int (*CommAbort)(void*) = nullptr;
+    int (*CommGetAsyncError)(void*, int*) = nullptr;
     const char* (*GetErrorString)(int) = nullptr;
     bool load() {
         if (lib) return true;
@@ -52,12 +55,13 @@ struct NcclApi {
         AllGather = (decltype(AllGather))dlsym(lib, "ncclAllGather");
         CommDestroy = (decltype(CommDestroy))dlsym(lib, "ncclCommDestroy");
         CommAbort = (decltype(CommAbort))dlsym(lib, "ncclCommAbort");
+        CommGetAsyncError = (decltype(CommGetAsyncError))dlsym(lib, "ncclCommGetAsyncError");
         GetErrorString = (decltype(GetErrorString))dlsym(lib, "ncclGetErrorString");
-        return GetUniqueId && CommInitRank && AllReduce && AllGather && CommDestroy && GetErrorString;
+        return GetUniqueId && CommInitRank && AllReduce && AllGather && CommDestroy && CommAbort && GetErrorString;
     }
 };
 static NcclApi g_nccl;
-constexpr int kNcclFloat = 7, kNcclDouble = 8, kNcclSum = 0;
+constexpr int kNcclFloat = 7, kNcclSum = 0, kNcclInProgress = 7;
 
 int nccl_unique_id(uint8_t out[128]) {
     if (!g_nccl.load()) return SY_ERR_COMM;
@@ -109,6 +113,8 @@ Session::Session(const sy_config& c) : cfg(c) {
         throw SyError(SY_ERR_INVALID_ARGUMENT, "bad rank / world_size");
     if (!(c.lr > 0) || !(c.momentum >= 0 && c.momentum < 1) || !(c.weight_decay >= 0))
         throw SyError(SY_ERR_INVALID_ARGUMENT, "bad optimizer hyper-parameters");
+    if (c.comm_timeout_ms < 0) throw SyError(SY_ERR_INVALID_ARGUMENT, "comm_timeout_ms must not be negative");
+    comm_timeout_ms_ = c.comm_timeout_ms > 0 ? c.comm_timeout_ms : 300000;
     if (c.precision != SY_PRECISION_TF32 && c.precision != SY_PRECISION_3XTF32)
         throw SyError(SY_ERR_INVALID_ARGUMENT, "precision must be SY_PRECISION_TF32 or SY_PRECISION_3XTF32");
     x3_ = c.precision == SY_PRECISION_3XTF32;
@@ -145,18 +151,13 @@ Session::Session(const sy_config& c) : cfg(c) {
     loss_ws_ = dalloc(loss_workspace_bytes(B_, anchors, std::max(1, c.max_boxes), 10));
     d_truth_ = static_cast<TruthBox*>(dalloc(sizeof(TruthBox) * (size_t)B_ * std::max(1, c.max_boxes)));
     d_box_off_ = static_cast<int*>(dalloc(sizeof(int) * (B_ + 1)));
-    // per branch set: [set][image] loss parts, positives and box connection
-    d_loss_ = static_cast<float*>(dalloc(sizeof(float) * 4 * 2 * B_));
-    d_pos_ = static_cast<int*>(dalloc(sizeof(int) * 2 * B_));
-    d_conn_ = static_cast<int*>(dalloc(sizeof(int) * 2 * B_));
     d_flags_ = static_cast<int*>(dalloc(sizeof(int) * 16));
     d_abs_ = static_cast<double*>(dalloc(sizeof(double) * kAbsSumBlocks));
     SY_CUDA(cudaMallocHost(&h_truth_, sizeof(TruthBox) * (size_t)B_ * std::max(1, c.max_boxes)));
     SY_CUDA(cudaMallocHost(&h_box_off_, sizeof(int) * (B_ + 1)));
     SY_CUDA(cudaMallocHost(&h_flags_, sizeof(int) * 16));
-    SY_CUDA(cudaMallocHost(&h_loss_, sizeof(float) * 4 * 2 * B_));
-    SY_CUDA(cudaMallocHost(&h_pos_, sizeof(int) * 2 * B_));
-    SY_CUDA(cudaMallocHost(&h_conn_, sizeof(int) * 2 * B_));
+    SY_CUDA(cudaMallocHost(&h_rec_, sizeof(float) * (size_t)head_floats_ * c.world_size));
+    SY_CUDA(cudaMallocHost(&h_images_, sizeof(int) * 4));
     SY_CUDA(cudaMallocHost(&h_abs_, sizeof(double) * kAbsSumBlocks));
     if (c.backbone != SY_BACKBONE_NONE) {
         SY_CUDA(cudaMallocHost(&h_rgb_, (size_t)B_ * c.image_size * c.image_size * 3));
@@ -182,10 +183,10 @@ void Session::clear_graphs() {
 Session::~Session() {
     if (stream_) cudaStreamSynchronize(stream_);
     clear_graphs();
-    if (comm_ && nccl_) nccl_->CommDestroy(comm_);
+    if (comm_ && nccl_) nccl_->CommDestroy(comm_);   // an aborted communicator is already gone
     for (void* p : allocations_) cudaFree(p);
-    for (void* p : {(void*)h_truth_, (void*)h_box_off_, (void*)h_flags_, (void*)h_loss_, (void*)h_pos_,
-                    (void*)h_conn_, (void*)h_abs_, (void*)h_rgb_})
+    for (void* p : {(void*)h_truth_, (void*)h_box_off_, (void*)h_flags_, (void*)h_rec_, (void*)h_images_,
+                    (void*)h_abs_, (void*)h_rgb_})
         if (p) cudaFreeHost(p);
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
@@ -712,9 +713,19 @@ void Session::build_head() {
     }
     // per-image BN statistics of all layers in one block ([layer][image][channel][2]) so that
     // data-parallel ranks can exchange them with a single all-gather
-    bn_stats_all_ = static_cast<float*>(dalloc(sizeof(float) * 2 * (size_t)B_ * std::max(1L, bn_channels_)));
-    bn_gather_ = static_cast<float*>(
-        dalloc(sizeof(float) * 2 * (size_t)B_ * std::max(1L, bn_channels_) * cfg.world_size));
+    // This rank's exchange record, all-gathered once per data-parallel step: a head of per-image loss
+    // parts ([set][image][4] floats), positives and box connections ([set][image] ints) and the image
+    // count, then the per-image BatchNorm statistics of every layer ([layer][image][channel][2]).
+    head_floats_ = (8 * B_ + 2 * B_ + 2 * B_ + 1 + 3) / 4 * 4;
+    rec_floats_ = head_floats_ + 2 * (long)B_ * std::max(1L, bn_channels_);
+    rec_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)rec_floats_));
+    d_loss_ = rec_;
+    d_pos_ = reinterpret_cast<int*>(rec_ + 8 * B_);
+    d_conn_ = d_pos_ + 2 * B_;
+    d_images_ = d_conn_ + 2 * B_;
+    bn_stats_all_ = rec_ + head_floats_;
+    if (cfg.world_size > 1)
+        rec_gather_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)rec_floats_ * cfg.world_size));
     for (auto& branch : branches_)
         for (auto& hb : branch.blocks)
             if (hb.b.has_bn) hb.stats = bn_stats_all_ + 2 * (size_t)B_ * hb.stats_off;
@@ -920,19 +931,20 @@ void Session::launch_losses(int images, int backward, int epoch) {
 
 // Per image the reported parts are a.Part * w0 + b.Part * w1 in float (DetectionHead.cs:114), summed
 // over the images in double; positives add up; `finite` checks every image's total (YoloTrainer.cs:193).
-void Session::combine_losses(int images, int epoch, double* box, double* cls, double* dfl, long* positives,
-                             int* connected, bool* finite) const {
+// `head` is one rank's exchange-record head ([set][image][4] loss parts, then [set][image] positives and
+// box connections); the sums accumulate into the outputs, so ranks are added in rank order.
+void Session::combine_losses(const float* head, int images, int epoch, double* box, double* cls, double* dfl,
+                             long* positives, int* connected, bool* finite) const {
     float w[2];
     loss_weights(epoch, w);
-    *box = *cls = *dfl = 0.0;
-    *positives = 0;
-    *connected = 0;
+    const int* pos = reinterpret_cast<const int*>(head + 8 * B_);
+    const int* conn = pos + 2 * B_;
     for (int b = 0; b < images; b++) {
         float part[3];
         for (int k = 0; k < 3; k++) {
-            part[k] = h_loss_[4 * b + k];
+            part[k] = head[4 * b + k];
             if (n_sets_ == 2) {
-                const float one = h_loss_[4 * ((size_t)B_ + b) + k] * w[1];
+                const float one = head[4 * ((size_t)B_ + b) + k] * w[1];
                 part[k] = part[k] * w[0] + one;
             }
         }
@@ -941,8 +953,8 @@ void Session::combine_losses(int images, int epoch, double* box, double* cls, do
         *dfl += part[2];
         if (!std::isfinite(part[0] + part[1] + part[2])) *finite = false;
         for (int set = 0; set < n_sets_; set++) {
-            *positives += h_pos_[(size_t)B_ * set + b];
-            if (h_conn_[(size_t)B_ * set + b]) *connected |= 1 << set;
+            *positives += pos[(size_t)B_ * set + b];
+            if (conn[(size_t)B_ * set + b]) *connected |= 1 << set;
         }
     }
 }
@@ -972,6 +984,8 @@ int Session::set_epoch(int epoch) {
 // features); shared by the training step and the loss evaluation.
 void Session::prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float* const* features,
                              const sy_box* boxes, const int32_t* counts, int images, bool defer_backbone) {
+    if (cfg.world_size > 1 && !comm_)
+        throw SyError(SY_ERR_COMM, "the data-parallel communicator was aborted after a failed step; destroy the session");
     if (images < 1 || images > B_) throw SyError(SY_ERR_INVALID_ARGUMENT, "images out of range");
     if (!counts || (!boxes && images > 0)) throw SyError(SY_ERR_INVALID_ARGUMENT, "counts / boxes missing");
     SY_CUDA(cudaSetDevice(device_));
@@ -998,6 +1012,8 @@ void Session::prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float
         SY_CUDA(cudaMemcpyAsync(d_truth_, h_truth_, sizeof(TruthBox) * k, cudaMemcpyHostToDevice, stream_));
     SY_CUDA(cudaMemcpyAsync(d_box_off_, h_box_off_, sizeof(int) * (images + 1), cudaMemcpyHostToDevice, stream_));
     SY_CUDA(cudaMemsetAsync(d_flags_, 0, sizeof(int) * 16, stream_));
+    h_images_[0] = images;
+    SY_CUDA(cudaMemcpyAsync(d_images_, h_images_, sizeof(int), cudaMemcpyHostToDevice, stream_));
     if (rgb) {
         const size_t bytes = (size_t)images * cfg.image_size * cfg.image_size * 3;
         const uint8_t* src = d_rgb_;
@@ -1068,79 +1084,64 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
         else
             device_work();
     }
+    // Data-parallel exchange, all enqueued before one host wait: the gradient bucket summed over ranks
+    // (so the finiteness check, the checksum and the kept copy all see the global gradient), then one
+    // all-gather of every rank's exchange record (loss parts, positives, connections, image count and the
+    // per-image BatchNorm statistics), whose heads come back to the host in one strided copy.
+    const int ranks = comm_ ? cfg.world_size : 1;
     if (comm_) {
-        // the gradient bucket is summed over ranks before anything reads it, so the finiteness
-        // check, the checksum and the kept copy all see the global gradient
         int r = nccl_->AllReduce(grads_, grads_, (size_t)n_params, kNcclFloat, kNcclSum, comm_, stream_);
         if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllReduce: ") + nccl_->GetErrorString(r));
     }
     SY_CUDA(cudaMemcpyAsync(last_grads_, grads_, sizeof(float) * n_params, cudaMemcpyDeviceToDevice, stream_));
     check_finite(grads_, n_params, d_flags_ + 1, stream_);
     abs_sum_partials(grads_, n_params, d_abs_, stream_);
-    SY_CUDA(cudaMemcpyAsync(h_loss_, d_loss_, sizeof(float) * 4 * 2 * B_, cudaMemcpyDeviceToHost, stream_));
-    SY_CUDA(cudaMemcpyAsync(h_pos_, d_pos_, sizeof(int) * 2 * B_, cudaMemcpyDeviceToHost, stream_));
-    SY_CUDA(cudaMemcpyAsync(h_conn_, d_conn_, sizeof(int) * 2 * B_, cudaMemcpyDeviceToHost, stream_));
+    const size_t head_bytes = sizeof(float) * (size_t)head_floats_;
+    const float* records = rec_;
+    if (comm_) {
+        int r = nccl_->AllGather(rec_, rec_gather_, (size_t)rec_floats_, kNcclFloat, comm_, stream_);
+        if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllGather: ") + nccl_->GetErrorString(r));
+        records = rec_gather_;
+        SY_CUDA(cudaMemcpy2DAsync(h_rec_, head_bytes, rec_gather_, sizeof(float) * (size_t)rec_floats_, head_bytes,
+                                  ranks, cudaMemcpyDeviceToHost, stream_));
+    } else {
+        SY_CUDA(cudaMemcpyAsync(h_rec_, rec_, head_bytes, cudaMemcpyDeviceToHost, stream_));
+    }
     SY_CUDA(cudaMemcpyAsync(h_flags_, d_flags_, sizeof(int) * 16, cudaMemcpyDeviceToHost, stream_));
     SY_CUDA(cudaMemcpyAsync(h_abs_, d_abs_, sizeof(double) * kAbsSumBlocks, cudaMemcpyDeviceToHost, stream_));
-    SY_CUDA(cudaStreamSynchronize(stream_));
+    wait_stream("the gradient all-reduce and record all-gather");
     if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "device wait limit exceeded (code " + std::to_string(h_flags_[0]) + ")");
     double box = 0, cls = 0, dfl = 0, abs_sum = 0;
     long positives = 0;
     int connected = 0;   // bit s: the box branch of set s received a gradient
     bool finite = h_flags_[1] == 0;
-    combine_losses(images, epoch_, &box, &cls, &dfl, &positives, &connected, &finite);
-    for (int i = 0; i < kAbsSumBlocks; i++) abs_sum += h_abs_[i];
-    int global_images = images;
-    if (comm_) {
-        // scalars summed over ranks: loss parts, positives, connection counts of both box groups,
-        // non-finite count, images
-        double* hs = reinterpret_cast<double*>(h_abs_);  // reuse pinned scratch (>= 8 doubles)
-        hs[0] = box;
-        hs[1] = cls;
-        hs[2] = dfl;
-        hs[3] = (double)positives;
-        hs[4] = connected & 1;
-        hs[5] = finite ? 0.0 : 1.0;
-        hs[6] = images;
-        hs[7] = (connected >> 1) & 1;
-        double* ds = d_abs_;
-        SY_CUDA(cudaMemcpyAsync(ds, hs, sizeof(double) * 8, cudaMemcpyHostToDevice, stream_));
-        int r = nccl_->AllReduce(ds, ds, 8, kNcclDouble, kNcclSum, comm_, stream_);
-        if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllReduce: ") + nccl_->GetErrorString(r));
-        SY_CUDA(cudaMemcpyAsync(hs, ds, sizeof(double) * 8, cudaMemcpyDeviceToHost, stream_));
-        SY_CUDA(cudaStreamSynchronize(stream_));
-        box = hs[0];
-        cls = hs[1];
-        dfl = hs[2];
-        positives = (long)hs[3];
-        connected = (hs[4] > 0 ? 1 : 0) | (hs[7] > 0 ? 2 : 0);
-        finite = hs[5] == 0;
-        global_images = (int)hs[6];
+    bool same_images = true;
+    for (int r = 0; r < ranks; r++) {
+        const float* head = h_rec_ + (size_t)head_floats_ * r;
+        const int n = reinterpret_cast<const int*>(head + 8 * B_)[4 * B_];
         // the running-statistics fold below walks `images` images of every rank in rank order
-        if (global_images != images * cfg.world_size) {
-            SY_CUDA(cudaMemsetAsync(grads_, 0, sizeof(float) * n_params, stream_));
-            SY_CUDA(cudaStreamSynchronize(stream_));
-            throw SyError(SY_ERR_INVALID_ARGUMENT, "data-parallel ranks must step the same number of images");
+        if (n != images) {
+            same_images = false;
+            break;
         }
+        combine_losses(head, images, epoch_, &box, &cls, &dfl, &positives, &connected, &finite);
+    }
+    for (int i = 0; i < kAbsSumBlocks; i++) abs_sum += h_abs_[i];
+    const int global_images = images * ranks;
+    if (!same_images) {
+        SY_CUDA(cudaMemsetAsync(grads_, 0, sizeof(float) * n_params, stream_));
+        SY_CUDA(cudaStreamSynchronize(stream_));
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "data-parallel ranks must step the same number of images");
     }
     if (!finite) {
         SY_CUDA(cudaMemsetAsync(grads_, 0, sizeof(float) * n_params, stream_));
         SY_CUDA(cudaStreamSynchronize(stream_));
         throw SyError(SY_ERR_NONFINITE, "non-finite loss or gradient; parameters not updated");
     }
-    // BN running statistics, global images in order (HeadOperations.cs:164-165): ranks
-    // all-gather their per-image statistics and every rank folds rank 0's images, then rank 1's...
-    const float* stats_src = bn_stats_all_;
-    int ranks = 1;
-    const size_t stats_floats = 2 * (size_t)B_ * bn_channels_;
-    if (comm_) {
-        int r = nccl_->AllGather(bn_stats_all_, bn_gather_, stats_floats, kNcclFloat, comm_, stream_);
-        if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllGather: ") + nccl_->GetErrorString(r));
-        stats_src = bn_gather_;
-        ranks = cfg.world_size;
-    }
+    // BN running statistics, global images in order (HeadOperations.cs:164-165): every rank folds rank 0's
+    // images, then rank 1's ..., from the gathered records
     if (n_bn_jobs_ > 0)
-        bn_running_update_batch(d_bn_jobs_, n_bn_jobs_, bn_max_c_, stats_src, (long)stats_floats, ranks, images,
+        bn_running_update_batch(d_bn_jobs_, n_bn_jobs_, bn_max_c_, records + head_floats_, rec_floats_, ranks, images,
                                 cfg.bn_momentum, stream_);
     // update: flags [2..4] gate the optimizer groups (class branches, cv2, one2one_cv2), [5..7] hold
     // their AdamW step counts (TrainingParameter steps only when it received a gradient)
@@ -1261,40 +1262,85 @@ int Session::evaluate(const uint8_t* rgb, bool rgb_on_device, const float* const
     forward_head(images, false);
     // EvaluateLoss passes epoch 0 to DetectionHead.Loss (YoloTrainer.cs:243)
     launch_losses(images, 0, 0);
-    SY_CUDA(cudaMemcpyAsync(h_loss_, d_loss_, sizeof(float) * 4 * 2 * B_, cudaMemcpyDeviceToHost, stream_));
-    SY_CUDA(cudaMemcpyAsync(h_pos_, d_pos_, sizeof(int) * 2 * B_, cudaMemcpyDeviceToHost, stream_));
-    SY_CUDA(cudaMemcpyAsync(h_conn_, d_conn_, sizeof(int) * 2 * B_, cudaMemcpyDeviceToHost, stream_));
-    SY_CUDA(cudaMemcpyAsync(h_flags_, d_flags_, sizeof(int) * 16, cudaMemcpyDeviceToHost, stream_));
-    SY_CUDA(cudaStreamSynchronize(stream_));
-    if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "device wait limit exceeded (code " + std::to_string(h_flags_[0]) + ")");
-    double* hs = reinterpret_cast<double*>(h_abs_);   // pinned scratch (>= 8 doubles)
-    long positives = 0;
-    int connected = 0;
-    bool finite = true;
-    combine_losses(images, 0, &hs[0], &hs[1], &hs[2], &positives, &connected, &finite);
-    hs[3] = (double)positives;
-    hs[4] = images;
+    // every rank's record head (loss parts, positives, image count) in one all-gather, combined on the host
+    // in global image order, so that every rank reports the same sums
+    const int ranks = comm_ ? cfg.world_size : 1;
+    const size_t head_bytes = sizeof(float) * (size_t)head_floats_;
     if (comm_) {
-        SY_CUDA(cudaMemcpyAsync(d_abs_, hs, sizeof(double) * 5, cudaMemcpyHostToDevice, stream_));
-        int r = nccl_->AllReduce(d_abs_, d_abs_, 5, kNcclDouble, kNcclSum, comm_, stream_);
-        if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllReduce: ") + nccl_->GetErrorString(r));
-        SY_CUDA(cudaMemcpyAsync(hs, d_abs_, sizeof(double) * 5, cudaMemcpyDeviceToHost, stream_));
+        int r = nccl_->AllGather(rec_, rec_gather_, (size_t)head_floats_, kNcclFloat, comm_, stream_);
+        if (r != 0) throw SyError(SY_ERR_COMM, std::string("ncclAllGather: ") + nccl_->GetErrorString(r));
+        SY_CUDA(cudaMemcpyAsync(h_rec_, rec_gather_, head_bytes * ranks, cudaMemcpyDeviceToHost, stream_));
+    } else {
+        SY_CUDA(cudaMemcpyAsync(h_rec_, rec_, head_bytes, cudaMemcpyDeviceToHost, stream_));
     }
+    SY_CUDA(cudaMemcpyAsync(h_flags_, d_flags_, sizeof(int) * 16, cudaMemcpyDeviceToHost, stream_));
     SY_CUDA(cudaEventRecord(ev1_, stream_));
-    SY_CUDA(cudaStreamSynchronize(stream_));
+    wait_stream("the loss all-gather");
+    if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "device wait limit exceeded (code " + std::to_string(h_flags_[0]) + ")");
+    double box = 0, cls = 0, dfl = 0;
+    long positives = 0;
+    int connected = 0, total_images = 0;
+    bool finite = true;
+    for (int r = 0; r < ranks; r++) {
+        const float* head = h_rec_ + (size_t)head_floats_ * r;
+        const int n = reinterpret_cast<const int*>(head + 8 * B_)[4 * B_];
+        if (n < 1 || n > B_) throw SyError(SY_ERR_COMM, "corrupt exchange record from rank " + std::to_string(r));
+        combine_losses(head, n, 0, &box, &cls, &dfl, &positives, &connected, &finite);
+        total_images += n;
+    }
     last_batch_ = images;
     if (out) {
         float ms = 0.0f;
         cudaEventElapsedTime(&ms, ev0_, ev1_);
         *out = sy_step_stats{};
-        out->box = hs[0];
-        out->cls = hs[1];
-        out->dfl = hs[2];
-        out->positives = (long)hs[3];
-        out->images = (int)hs[4];
+        out->box = box;
+        out->cls = cls;
+        out->dfl = dfl;
+        out->positives = positives;
+        out->images = total_images;
         out->device_ms = ms;
     }
     return SY_OK;
+}
+
+// ------------------------------------------------------------------ bounded waits on collectives
+// With collectives in flight a peer that has died or stopped stepping would block the stream forever.
+// The host polls the stream instead of blocking on it; NCCL's asynchronous error, or no completion within
+// comm_timeout_ms, aborts the communicator (ncclCommAbort ends this rank's pending collectives), the stream
+// is drained, and the step fails with SY_ERR_COMM.  Without a communicator this is a plain synchronize.
+void Session::wait_stream(const char* what) {
+    if (!comm_) {
+        SY_CUDA(cudaStreamSynchronize(stream_));
+        return;
+    }
+    using clock = std::chrono::steady_clock;
+    const auto start = clock::now();
+    const auto deadline = start + std::chrono::milliseconds(comm_timeout_ms_);
+    for (long polls = 0;; polls++) {
+        const cudaError_t e = cudaStreamQuery(stream_);
+        if (e == cudaSuccess) return;
+        if (e != cudaErrorNotReady) SY_CUDA(e);
+        int async = 0;
+        if (nccl_->CommGetAsyncError && nccl_->CommGetAsyncError(comm_, &async) == 0 && async != 0 &&
+            async != kNcclInProgress)
+            abort_comm(std::string("NCCL reported ") + nccl_->GetErrorString(async) + " during " + what);
+        if (clock::now() > deadline)
+            abort_comm(std::string(what) + " did not complete within " + std::to_string(comm_timeout_ms_) +
+                       " ms (a peer rank stopped or died)");
+        if (polls > 1000) std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+void Session::abort_comm(const std::string& reason) {
+    void* comm = comm_;
+    comm_ = nullptr;   // no further collectives: later steps fail with SY_ERR_COMM
+    nccl_->CommAbort(comm);
+    // the aborted collectives return; give the stream a bounded time to drain
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::seconds(10);
+    while (cudaStreamQuery(stream_) == cudaErrorNotReady && std::chrono::steady_clock::now() < deadline)
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    cudaGetLastError();
+    throw SyError(SY_ERR_COMM, reason + "; the communicator was aborted");
 }
 
 // ------------------------------------------------------------------ conv launch timing

@@ -132,9 +132,12 @@ private:
     // DetectionHead.Loss: one loss per branch set, gradients scaled by the set's weight
     void launch_losses(int images, int backward, int epoch);
     void loss_weights(int epoch, float w[2]) const;
-    // per-image weighted loss parts of the launched losses (after the stream synchronized)
-    void combine_losses(int images, int epoch, double* box, double* cls, double* dfl, long* positives,
-                        int* connected, bool* finite) const;
+    // per-image weighted loss parts of one rank's exchange-record head, accumulated into the outputs
+    void combine_losses(const float* head, int images, int epoch, double* box, double* cls, double* dfl,
+                        long* positives, int* connected, bool* finite) const;
+    // host wait for the stream, bounded by comm_timeout_ms while collectives are in flight
+    void wait_stream(const char* what);
+    [[noreturn]] void abort_comm(const std::string& reason);
     void backward_head(int batch);
     void refresh_head_weights();
     BnFoldJob* d_bn_jobs_ = nullptr;             // one job per head BatchNorm layer
@@ -189,7 +192,6 @@ private:
     float* wgrad_ws_ = nullptr;
     float* feat_stage_ = nullptr;
     float* bn_stats_all_ = nullptr;
-    float* bn_gather_ = nullptr;
     long bn_channels_ = 0;
     float* bias_part_ = nullptr;
     float* bn_part_ = nullptr;       // per-32-row-group BatchNorm partials written by conv epilogues
@@ -198,14 +200,20 @@ private:
     int* d_box_off_ = nullptr;
     TruthBox* h_truth_ = nullptr;
     int* h_box_off_ = nullptr;
+    // exchange record (see build_head): head of loss parts / positives / connections / image count, then
+    // the per-image BatchNorm statistics; its all-gathered copy; the heads on the host
+    float* rec_ = nullptr;
+    float* rec_gather_ = nullptr;
+    long head_floats_ = 0, rec_floats_ = 0;
+    float* h_rec_ = nullptr;
+    int* h_images_ = nullptr;
+    int* d_images_ = nullptr;
+    int comm_timeout_ms_ = 300000;
     float* d_loss_ = nullptr;
     int* d_pos_ = nullptr;
     int* d_conn_ = nullptr;
     int* d_flags_ = nullptr;     // [0] device error, [1] nonfinite, [2..3] group has_grad, [4..5] adam steps
     int* h_flags_ = nullptr;
-    float* h_loss_ = nullptr;
-    int* h_pos_ = nullptr;
-    int* h_conn_ = nullptr;
     double* d_abs_ = nullptr;
     double* h_abs_ = nullptr;
     ParamSegment* d_segs_ = nullptr;

@@ -96,5 +96,62 @@ def nccl_rank(out_dir: str):
         dist.destroy_process_group()
 
 
+def nccl_timeout_rank(out_dir: str):
+    """Failure case (launched by torch.distributed.run on 2 GPUs, NCCL_NVLS_ENABLE=0): both ranks step once,
+    then rank 1 leaves between steps, with nothing of its own in flight.  Rank 0's next step enqueues its
+    collectives, which no peer completes: the session's bounded wait gives up after comm_timeout_ms, aborts
+    the communicator and returns SY_ERR_COMM; the session refuses further steps, closes cleanly, and a fresh
+    single-GPU session on the same device still steps."""
+    import json
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    import simdyolo_b200 as sy
+    from simdyolo_b200 import dp
+
+    local_rank = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local_rank)
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    sess = dp.create_session(dist, "yolov8n", local_rank, 1, image_size=128, comm_timeout_ms=3000)
+    init_session(sess, "yolov8n")
+    from simdyolo_b200 import data
+    imgs, boxes = data.synthetic_batch(np.random.default_rng(5), world, 128, 80)
+    mine, my_boxes = dp.shard(imgs, boxes, rank, world)
+    sess.step(mine, my_boxes)
+    torch.cuda.synchronize()
+    dist.barrier()          # both ranks finished step 1: nothing is in flight
+    if rank == 1:
+        os._exit(0)         # leaves without another word to its peer
+    time.sleep(1.0)
+    res = {}
+    t0 = time.monotonic()
+    try:
+        sess.step(mine, my_boxes)
+        res["status"] = 0
+    except sy.SyError as e:
+        res["status"], res["message"] = e.status, str(e)
+    res["elapsed"] = time.monotonic() - t0
+    try:
+        sess.step(mine, my_boxes)
+        res["second"] = 0
+    except sy.SyError as e:
+        res["second"] = e.status
+    sess.close()
+    cfg = sy.make_config("yolov8n", image_size=128, max_batch=1, device=local_rank)
+    with sy.Session(cfg) as fresh:
+        init_session(fresh, "yolov8n")
+        st = fresh.step(mine, my_boxes)
+        res["fresh_ok"] = bool(np.isfinite(st.cls))
+    with open(os.path.join(out_dir, "timeout.json"), "w") as f:
+        json.dump(res, f)
+    os._exit(0)             # the control-plane group has lost its peer: no collective teardown
+
+
 if __name__ == "__main__":
-    nccl_rank(sys.argv[1])
+    if sys.argv[1] == "timeout":
+        nccl_timeout_rank(sys.argv[2])
+    else:
+        nccl_rank(sys.argv[1])

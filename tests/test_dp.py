@@ -85,3 +85,28 @@ def test_two_gpu_step_matches_single_gpu(tmp_path):
         np.testing.assert_allclose(r["stats"][:, :3], single["stats"][:, :3], rtol=1e-5)
         np.testing.assert_array_equal(r["stats"][:, 3:6], single["stats"][:, 3:6])
         np.testing.assert_allclose(r["stats"][:, 6], single["stats"][:, 6], rtol=1e-4)
+
+
+@pytest.mark.gpu
+def test_peer_that_leaves_ends_the_next_step_with_comm_error(tmp_path):
+    """A rank that leaves between steps: the survivor's next collective is ended by the session's bounded
+    wait (ncclCommAbort after comm_timeout_ms = 3 s) with SY_ERR_COMM instead of blocking forever
+    (VulkanBackend.cs:323-style InvalidOperationException on the C# side)."""
+    import json
+
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import simdyolo_b200 as sy
+
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={free_port()}", dp_cases.__file__, "timeout", str(tmp_path)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    res = json.loads((tmp_path / "timeout.json").read_text())
+    assert res["status"] == sy.SY_ERR_COMM, res
+    assert 2.5 <= res["elapsed"] < 60, res
+    assert res["second"] == sy.SY_ERR_COMM
+    assert res["fresh_ok"]
