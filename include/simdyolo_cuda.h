@@ -108,6 +108,11 @@ typedef struct sy_step_stats {
     int32_t box_has_grad;       /* bit 0: cv2 connected (any positive, DetectionLoss.cs:101); bit 1: one2one_cv2 */
     double grad_checksum;       /* sum of |g| over the averaged head gradient before the update */
     double device_ms;           /* device time of the step (CUDA events) */
+    /* Assigner decisions taken by a margin of at most 16 ulp (GT boxes whose top-k boundary, and conflicted
+     * anchors whose best and second overlap, lie that close): the reference computes the same quantities
+     * with the platform libm (MathF.Exp / Atan / Pow, DetectionLoss.cs:63-65), which may decide these the
+     * other way.  No counterpart in the reference. */
+    int64_t near_ties;
 } sy_step_stats;
 
 typedef struct sy_tensor_info {
@@ -186,7 +191,7 @@ SY_API sy_status sy_cuda_detection_loss(int32_t device, int32_t images, int32_t 
                                  const float *const *classes, const sy_box *truth, const int32_t *counts,
                                  float *out_loss, int32_t *positives, int32_t *assigned, float *scores,
                                  float *const *box_grads, float *const *class_grads);
-/* The same with the assigner's candidate counts and the gradient scale (DetectionLoss.Compute
+/* The same with the assigner's candidate counts (topk 1..15) and the gradient scale (DetectionLoss.Compute
  * arguments topk, topk2, gradientScale, DetectionLoss.cs:48-91): end-to-end heads call it with
  * (10, 10, w) for the one-to-many branch and (7 or 1, 1, 1 - w) for the one-to-one branch;
  * reg_max 1 is the L1 box loss of YOLO26 (DetectionLoss.cs:123-131). */

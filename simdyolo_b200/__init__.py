@@ -81,7 +81,7 @@ class Config(C.Structure):
 class StepStats(C.Structure):
     _fields_ = [("box", C.c_double), ("cls", C.c_double), ("dfl", C.c_double), ("positives", C.c_int64),
                 ("images", C.c_int32), ("box_has_grad", C.c_int32), ("grad_checksum", C.c_double),
-                ("device_ms", C.c_double)]
+                ("device_ms", C.c_double), ("near_ties", C.c_int64)]
 
 
 class TensorInfo(C.Structure):

@@ -355,7 +355,7 @@ sy_status sy_cuda_detection_loss_ex(int32_t device, int32_t images, int32_t leve
                                     float* const* box_grads, float* const* class_grads) {
     return guarded(nullptr, [&] {
         if (images < 1 || levels < 1 || levels > 3 || !hs || !ws || !strides || !boxes || !classes || !counts ||
-            !out_loss || nc < 1 || !(reg_max == 16 || reg_max == 1) || topk < 1 || topk > 64 || topk2 < 1 ||
+            !out_loss || nc < 1 || !(reg_max == 16 || reg_max == 1) || topk < 1 || topk > 15 || topk2 < 1 ||
             topk2 > topk || !std::isfinite(grad_scale))
             throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "detection_loss: bad arguments");
         check_device(device);

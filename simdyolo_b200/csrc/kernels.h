@@ -274,7 +274,12 @@ struct LossOut {
     int* connected;
     int* assigned;     // [batch][anchors] (may be null)
     float* scores;     // [batch][anchors] (may be null)
+    // [batch] (may be null): decisions of the assigner taken by a margin of at most kNearTieUlps ulp, i.e.
+    // GT boxes whose top-k boundary (k-th against (k+1)-th alignment metric) and conflicted anchors whose
+    // best and second overlap lie that close; another libm's exp / atan / pow could decide them the other way
+    int* near_ties = nullptr;
 };
+constexpr unsigned kNearTieUlps = 16;
 size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int bins);
 // round_grad: the logit gradients are stored rounded to the nearest TF32 (operands of TF32 convs).
 // serial_cls: the per-image class loss is the reference's float running sum (one term at a time, in its

@@ -243,15 +243,17 @@ __global__ void __launch_bounds__(256) topk_kernel(LossParams p) {
         return;
     }
     const TruthBox box = p.truth[p.box_off[b] + g];
+    // each thread keeps its best topk + 1 keys (the extra one for the near-tie check); topk < kMaxTopk
     unsigned long long list[kMaxTopk];
+    const int cap = p.topk + 1;
     int cnt = 0;
     for (int a = threadIdx.x; a < p.anchors; a += blockDim.x) {
         bool inside;
         float ov, m;
         tal_metric(p, b, a, box, inside, ov, m);
         const unsigned long long key = make_key(m, a);
-        if (cnt == p.topk && key <= list[cnt - 1]) continue;
-        int pos = cnt < p.topk ? cnt++ : cnt - 1;
+        if (cnt == cap && key <= list[cnt - 1]) continue;
+        int pos = cnt < cap ? cnt++ : cnt - 1;
         while (pos > 0 && list[pos - 1] < key) {
             list[pos] = list[pos - 1];
             pos--;
@@ -262,7 +264,9 @@ __global__ void __launch_bounds__(256) topk_kernel(LossParams p) {
     __shared__ unsigned long long best_s;
     int head = 0;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int k = 0; k < p.topk; k++) {
+    unsigned long long kth = 0ull;   // key of the k-th (last) selected anchor
+    // k = topk: one more round finds the (k+1)-th key, for the near-tie count only
+    for (int k = 0; k <= p.topk; k++) {
         unsigned long long cand = head < cnt ? list[head] : 0ull;
         unsigned long long m = cand;
 #pragma unroll
@@ -279,6 +283,13 @@ __global__ void __launch_bounds__(256) topk_kernel(LossParams p) {
         }
         __syncthreads();
         const unsigned long long bm = best_s;
+        if (k == p.topk) {
+            const unsigned m_k = (unsigned)(kth >> 32), m_next = (unsigned)(bm >> 32);
+            if (threadIdx.x == 0 && p.out.near_ties && m_next > 0u && m_k - m_next <= kNearTieUlps)
+                atomicAdd(&p.out.near_ties[b], 1);
+            break;
+        }
+        if (k == p.topk - 1) kth = bm;
         if (bm != 0ull && cand == bm) {
             head++;
             const int a = (int)(0xFFFFFFFFu - (unsigned)(bm & 0xFFFFFFFFull));
@@ -364,17 +375,23 @@ __global__ void __launch_bounds__(256) assign_kernel(LossParams p) {
         const int a = anc[i];
         int chosen = own[i];
         if (chosen == -2) {
-            float best = -1.f;
+            float best = -1.f, second = -1.f;
             for (int g = 0; g < n; g++) {
                 bool inside;
                 float o, m;
                 tal_metric(p, b, a, truth[g], inside, o, m);
                 if (o > best) {
+                    second = best;
                     best = o;
                     chosen = g;
+                } else if (o > second) {
+                    second = o;
                 }
             }
             own[i] = chosen;
+            if (p.out.near_ties && second > 0.f &&
+                __float_as_uint(best) - __float_as_uint(second) <= kNearTieUlps)
+                atomicAdd(&p.out.near_ties[b], 1);
         }
         bool inside;
         float o, m;
@@ -673,6 +690,7 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
     p.topk = topk;
     p.topk2 = topk2;
     if (topk2 < 1 || topk2 > topk) throw std::runtime_error("detection_loss: topk2 must be in [1, topk]");
+    if (topk < 1 || topk >= kMaxTopk) throw std::runtime_error("detection_loss: topk must be in [1, 15]");
     p.grad_scale = grad_scale;
     p.backward = backward;
     p.truth = truth;
@@ -699,6 +717,7 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
     int* dense_a = (int*)take((size_t)batch * p.anchors * sizeof(int));
     float* dense_s = (float*)take((size_t)batch * p.anchors * sizeof(float));
     p.out = out;
+    if (out.near_ties) cudaMemsetAsync(out.near_ties, 0, sizeof(int) * (size_t)batch, stream);
     if (!p.out.assigned) p.out.assigned = dense_a;
     if (!p.out.scores) p.out.scores = dense_s;
 

@@ -714,15 +714,16 @@ void Session::build_head() {
     // per-image BN statistics of all layers in one block ([layer][image][channel][2]) so that
     // data-parallel ranks can exchange them with a single all-gather
     // This rank's exchange record, all-gathered once per data-parallel step: a head of per-image loss
-    // parts ([set][image][4] floats), positives and box connections ([set][image] ints) and the image
-    // count, then the per-image BatchNorm statistics of every layer ([layer][image][channel][2]).
-    head_floats_ = (8 * B_ + 2 * B_ + 2 * B_ + 1 + 3) / 4 * 4;
+    // parts ([set][image][4] floats), positives, box connections and assigner near ties ([set][image] ints)
+    // and the image count, then the per-image BatchNorm statistics of every layer ([layer][image][channel][2]).
+    head_floats_ = (8 * B_ + 2 * B_ + 2 * B_ + 2 * B_ + 1 + 3) / 4 * 4;
     rec_floats_ = head_floats_ + 2 * (long)B_ * std::max(1L, bn_channels_);
     rec_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)rec_floats_));
     d_loss_ = rec_;
     d_pos_ = reinterpret_cast<int*>(rec_ + 8 * B_);
     d_conn_ = d_pos_ + 2 * B_;
-    d_images_ = d_conn_ + 2 * B_;
+    d_ties_ = d_conn_ + 2 * B_;
+    d_images_ = d_ties_ + 2 * B_;
     bn_stats_all_ = rec_ + head_floats_;
     if (cfg.world_size > 1)
         rec_gather_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)rec_floats_ * cfg.world_size));
@@ -922,7 +923,7 @@ void Session::launch_losses(int images, int backward, int epoch) {
                             (float)(8 << l)};
         }
         LossOut lo{d_loss_ + (size_t)4 * B_ * set, d_pos_ + (size_t)B_ * set, d_conn_ + (size_t)B_ * set, nullptr,
-                   nullptr};
+                   nullptr, d_ties_ + (size_t)B_ * set};
         const int topk = set == 0 ? 10 : (progressive_ ? 7 : 1), topk2 = set == 0 ? 10 : 1;
         detection_loss(lv, 3, images, cfg.num_classes, cfg.reg_max, d_truth_, d_box_off_, std::max(1, cfg.max_boxes),
                        topk, topk2, cfg.end_to_end ? w[set] : 1.0f, backward, loss_ws_, lo, stream_, rnd_, x3_);
@@ -934,11 +935,12 @@ void Session::launch_losses(int images, int backward, int epoch) {
 // `head` is one rank's exchange-record head ([set][image][4] loss parts, then [set][image] positives and
 // box connections); the sums accumulate into the outputs, so ranks are added in rank order.
 void Session::combine_losses(const float* head, int images, int epoch, double* box, double* cls, double* dfl,
-                             long* positives, int* connected, bool* finite) const {
+                             long* positives, int* connected, bool* finite, long* near_ties) const {
     float w[2];
     loss_weights(epoch, w);
     const int* pos = reinterpret_cast<const int*>(head + 8 * B_);
     const int* conn = pos + 2 * B_;
+    const int* ties = conn + 2 * B_;
     for (int b = 0; b < images; b++) {
         float part[3];
         for (int k = 0; k < 3; k++) {
@@ -954,6 +956,7 @@ void Session::combine_losses(const float* head, int images, int epoch, double* b
         if (!std::isfinite(part[0] + part[1] + part[2])) *finite = false;
         for (int set = 0; set < n_sets_; set++) {
             *positives += pos[(size_t)B_ * set + b];
+            *near_ties += ties[(size_t)B_ * set + b];
             if (conn[(size_t)B_ * set + b]) *connected |= 1 << set;
         }
     }
@@ -1112,19 +1115,19 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
     wait_stream("the gradient all-reduce and record all-gather");
     if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "device wait limit exceeded (code " + std::to_string(h_flags_[0]) + ")");
     double box = 0, cls = 0, dfl = 0, abs_sum = 0;
-    long positives = 0;
+    long positives = 0, near_ties = 0;
     int connected = 0;   // bit s: the box branch of set s received a gradient
     bool finite = h_flags_[1] == 0;
     bool same_images = true;
     for (int r = 0; r < ranks; r++) {
         const float* head = h_rec_ + (size_t)head_floats_ * r;
-        const int n = reinterpret_cast<const int*>(head + 8 * B_)[4 * B_];
+        const int n = reinterpret_cast<const int*>(head + 8 * B_)[6 * B_];
         // the running-statistics fold below walks `images` images of every rank in rank order
         if (n != images) {
             same_images = false;
             break;
         }
-        combine_losses(head, images, epoch_, &box, &cls, &dfl, &positives, &connected, &finite);
+        combine_losses(head, images, epoch_, &box, &cls, &dfl, &positives, &connected, &finite, &near_ties);
     }
     for (int i = 0; i < kAbsSumBlocks; i++) abs_sum += h_abs_[i];
     const int global_images = images * ranks;
@@ -1173,6 +1176,7 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
         out->box_has_grad = connected;
         out->grad_checksum = abs_sum / global_images;
         out->device_ms = ms;
+        out->near_ties = near_ties;
     }
     if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "device wait limit exceeded");
     if (h_flags_[1]) throw SyError(SY_ERR_NONFINITE, "non-finite parameters after the update");
@@ -1278,14 +1282,14 @@ int Session::evaluate(const uint8_t* rgb, bool rgb_on_device, const float* const
     wait_stream("the loss all-gather");
     if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "device wait limit exceeded (code " + std::to_string(h_flags_[0]) + ")");
     double box = 0, cls = 0, dfl = 0;
-    long positives = 0;
+    long positives = 0, near_ties = 0;
     int connected = 0, total_images = 0;
     bool finite = true;
     for (int r = 0; r < ranks; r++) {
         const float* head = h_rec_ + (size_t)head_floats_ * r;
-        const int n = reinterpret_cast<const int*>(head + 8 * B_)[4 * B_];
+        const int n = reinterpret_cast<const int*>(head + 8 * B_)[6 * B_];
         if (n < 1 || n > B_) throw SyError(SY_ERR_COMM, "corrupt exchange record from rank " + std::to_string(r));
-        combine_losses(head, n, 0, &box, &cls, &dfl, &positives, &connected, &finite);
+        combine_losses(head, n, 0, &box, &cls, &dfl, &positives, &connected, &finite, &near_ties);
         total_images += n;
     }
     last_batch_ = images;
@@ -1298,6 +1302,7 @@ int Session::evaluate(const uint8_t* rgb, bool rgb_on_device, const float* const
         out->dfl = dfl;
         out->positives = positives;
         out->images = total_images;
+        out->near_ties = near_ties;
         out->device_ms = ms;
     }
     return SY_OK;

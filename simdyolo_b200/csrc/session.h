@@ -134,7 +134,7 @@ private:
     void loss_weights(int epoch, float w[2]) const;
     // per-image weighted loss parts of one rank's exchange-record head, accumulated into the outputs
     void combine_losses(const float* head, int images, int epoch, double* box, double* cls, double* dfl,
-                        long* positives, int* connected, bool* finite) const;
+                        long* positives, int* connected, bool* finite, long* near_ties) const;
     // host wait for the stream, bounded by comm_timeout_ms while collectives are in flight
     void wait_stream(const char* what);
     [[noreturn]] void abort_comm(const std::string& reason);
@@ -208,6 +208,7 @@ private:
     float* h_rec_ = nullptr;
     int* h_images_ = nullptr;
     int* d_images_ = nullptr;
+    int* d_ties_ = nullptr;
     int comm_timeout_ms_ = 300000;
     float* d_loss_ = nullptr;
     int* d_pos_ = nullptr;

@@ -143,7 +143,7 @@ def test_config0_sixteen_steps_match_oracle(oracle_run, precision):
             print(f"step {k:2d}: box {st.box:.6f} cls {st.cls:.6f} dfl {st.dfl:.6f} pos {st.positives} | "
                   f"rel box {errs['box']:.2e} cls {errs['cls']:.2e} dfl {errs['dfl']:.2e} | gradient vs oracle "
                   f"at the GPU's state {errs['grad_state']:.2e}, vs the oracle's trajectory {errs['grad']:.2e} "
-                  f"(checksum {errs['checksum']:.2e})")
+                  f"(checksum {errs['checksum']:.2e}); assigner near ties {st.near_ties}")
             assert st.positives == ref["positives"], (k, st.positives, ref["positives"])
             assert st.box_has_grad == ref["connected"]
             assert errs["box"] <= bound["loss"] and errs["dfl"] <= bound["loss"], (k, errs)

@@ -188,3 +188,23 @@ def test_v8l_full_step_trunk_features_match_oracle():
         got = s.last_features(l, (1,) + f[l].shape)
         # 1.5x the single-conv bound: the trunk chains ~70 TF32 convolutions
         assert rel_l2(got[0], f[l]) < 1.5 * TOL, f"level {l}"
+
+
+def test_assigner_near_ties_are_reported():
+    """Zero features make every anchor of a level predict the same box, so a square ground truth centred on a
+    grid corner sees its anchors in symmetric groups of 4 or 8 with alignment metrics equal up to rounding:
+    the top-10 boundary falls inside such a group, a decision another libm could take the other way
+    (DetectionLoss.cs:63-65), and sy_step_stats.near_ties counts it.  Random features: the count is reported
+    and at most one per ground-truth box and conflicted anchor."""
+    s, cfg, _, _ = make_session(128, 1, backbone=False)
+    feats = [np.zeros((1, cfg.feature_channels[l], 128 >> (3 + l), 128 >> (3 + l)), np.float32) for l in range(3)]
+    truth = [[(3, 32.0, 32.0, 96.0, 96.0)]]
+    st = s.step_features(feats, truth)
+    assert st.positives > 0
+    assert st.near_ties >= 1
+    rng = np.random.default_rng(3)
+    feats = features_for(cfg, 1, rng)
+    _, truth = data.synthetic_batch(rng, 1, 128, cfg.num_classes, boxes=(4, 8), wh=(8.0, 64.0))
+    st = s.step_features(feats, truth)
+    assert 0 <= st.near_ties <= len(truth[0]) + st.positives
+    s.close()
