@@ -52,7 +52,7 @@ METRIC = WORKLOADS["v8n-640"]["metric"]
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per conv_fwd_tc_kernel launch, mean over the
 # launches of one batch-64 YOLOv8n step at 640x640, measured with ncu on that workload (the command is in
 # the profile summary of this kernel); None for other workloads, which were not captured.
-CONV_DRAM_BYTES_PER_LAUNCH = {"v8n-640": None}
+CONV_DRAM_BYTES_PER_LAUNCH = {"v8n-640": 125.74e6}   # 96.11 MB read + 29.63 MB written
 PASS_NAMES = {0: "trunk", 1: "trunk s2", 2: "head fwd", 3: "head dgrad"}
 
 
