@@ -23,22 +23,6 @@ namespace {
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 
-struct Split {
-    int splits;     // pixel splits per (image, channel group)
-    int cgroups;    // channel groups of 32
-};
-
-Split choose_split(int batch, int channels, const Grid& g) {
-    Split s;
-    s.cgroups = (channels + 31) / 32;
-    const int pixels = g.h * g.w;
-    const int want_blocks = 148 * 4;
-    int splits = (want_blocks + s.cgroups * batch - 1) / (s.cgroups * batch);
-    splits = std::min(splits, std::max(1, pixels / 64));
-    s.splits = std::max(1, std::min(splits, 64));
-    return s;
-}
-
 __device__ __forceinline__ void split_range(int pixels, int splits, int s, int& p0, int& p1) {
     p0 = (int)((long)pixels * s / splits);
     p1 = (int)((long)pixels * (s + 1) / splits);
@@ -299,70 +283,6 @@ __global__ void bn_param_grad_batch_kernel(const BnFoldJob* jobs, int batch) {
     jb.dbeta[ch] = db;
 }
 
-__global__ void __launch_bounds__(kThreads) bias_partial_kernel(const float* gr, int pitch, int c, Grid g, int splits,
-                                                                float* part) {
-    __shared__ float red[kWarps][32];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int ch = blockIdx.x * 32 + lane, b = blockIdx.y, s = blockIdx.z;
-    int p0, p1;
-    split_range(g.h * g.w, splits, s, p0, p1);
-    float acc = 0.0f;
-    if (ch < c) {
-        // pixel p -> (yy, xx) advanced incrementally (no division per pixel); four pixels per
-        // iteration into four running sums, so that four loads are in flight
-        int p = p0 + warp;
-        int yy = p / g.w, xx = p - yy * g.w;
-        const float* img = gr + (long)b * g.rows * pitch + ch;
-        auto next_row = [&]() {
-            const int r = g.row(yy, xx);
-            xx += kWarps;
-            while (xx >= g.w) {
-                xx -= g.w;
-                yy++;
-            }
-            return r;
-        };
-        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-        for (; p + 3 * kWarps < p1; p += 4 * kWarps) {
-            const int r0 = next_row(), r1 = next_row(), r2 = next_row(), r3 = next_row();
-            const float v0 = img[(long)r0 * pitch], v1 = img[(long)r1 * pitch];
-            const float v2 = img[(long)r2 * pitch], v3 = img[(long)r3 * pitch];
-            a0 += v0;
-            a1 += v1;
-            a2 += v2;
-            a3 += v3;
-        }
-        for (; p < p1; p += kWarps) a0 += img[(long)next_row() * pitch];
-        acc = (a0 + a1) + (a2 + a3);
-    }
-    red[warp][lane] = acc;
-    __syncthreads();
-    if (warp == 0 && ch < c) {
-        float t = 0.0f;
-        for (int w = 0; w < kWarps; w++) t += red[w][lane];
-        part[((long)b * splits + s) * c + ch] = t;
-    }
-}
-
-// per_image[b][ch] = sum over the splits of image b (one thread per (image, channel))
-__global__ void bias_image_kernel(const float* part, int batch, int c, int splits, float* per_image) {
-    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= (long)batch * c) return;
-    const int b = (int)(i / c), ch = (int)(i - (long)b * c);
-    float acc = 0.0f;
-    for (int s = 0; s < splits; s++) acc += part[((long)b * splits + s) * c + ch];
-    per_image[i] = acc;
-}
-
-__global__ void bias_fold_kernel(const float* per_image, int batch, int c, float* db) {
-    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
-    if (ch >= c) return;
-    float acc = db[ch];
-#pragma unroll 8
-    for (int b = 0; b < batch; b++) acc += per_image[(long)b * c + ch];
-    db[ch] = acc;
-}
-
 // ---------------------------------------------------------------- centred weight gradient (kernels.h)
 // Partial sums of x over a slice of the interior pixels of one image: block (32 channels, image, slice),
 // lane = channel, warp w takes pixels w, w + 8, ... of the slice into four running sums (four loads in
@@ -506,8 +426,6 @@ __global__ void __launch_bounds__(kFoldWarps * 32) tap_border_sums_kernel(const 
 
 }  // namespace
 
-size_t bn_workspace_floats(int batch, int channels) { return (size_t)batch * 64 * channels * 3; }
-
 size_t bn_partial_floats(int batch, const Grid& g, int channels) {
     return (size_t)batch * (g.rows / 32) * channels * 3;
 }
@@ -644,19 +562,6 @@ void bn_running_update(const float* stats, long rank_stride, int ranks, int batc
     bn_running_kernel<<<(c + 127) / 128, 128, 0, stream>>>(stats, rank_stride, ranks, batch, c, spatial, momentum,
                                                            rmean, rvar, tracked);
     launch_check("bn_running_kernel");
-}
-
-void bias_grad(const View& gv, int batch, const Grid& gr, float* ws, float* db, cudaStream_t stream) {
-    const Split sp = choose_split(batch, gv.channels, gr);
-    bias_partial_kernel<<<dim3(sp.cgroups, batch, sp.splits), kThreads, 0, stream>>>(gv.base, gv.pitch, gv.channels,
-                                                                                   gr, sp.splits, ws);
-    launch_check("bias_partial_kernel");
-    float* per_image = ws + (size_t)batch * sp.splits * gv.channels;
-    bias_image_kernel<<<(int)(((long)batch * gv.channels + 127) / 128), 128, 0, stream>>>(ws, batch, gv.channels,
-                                                                                         sp.splits, per_image);
-    launch_check("bias_image_kernel");
-    bias_fold_kernel<<<(gv.channels + 127) / 128, 128, 0, stream>>>(per_image, batch, gv.channels, db);
-    launch_check("bias_fold_kernel");
 }
 
 }  // namespace sy

@@ -403,7 +403,7 @@ sy_status sy_cuda_detection_loss_ex(int32_t device, int32_t images, int32_t leve
         int* d_off = s.get<int>(images + 1);
         CK(cudaMemcpy(d_truth, tb.data(), tb.size() * sizeof(sy::TruthBox), cudaMemcpyHostToDevice));
         CK(cudaMemcpy(d_off, off.data(), off.size() * sizeof(int), cudaMemcpyHostToDevice));
-        void* ws_ = s.get<uint8_t>(sy::loss_workspace_bytes(images, anchors, std::max(1, max_boxes), topk));
+        void* ws_ = s.get<uint8_t>(sy::loss_workspace_bytes(images, anchors, std::max(1, max_boxes), topk, nc));
         sy::LossOut lo{s.get<float>(4 * images), s.get<int>(images), s.get<int>(images), s.get<int>((size_t)images * anchors),
                        s.get<float>((size_t)images * anchors)};
         if (max_boxes * topk > 1024) throw sy::SyError(SY_ERR_UNSUPPORTED_SHAPE, "detection_loss: boxes * topk > 1024");

@@ -247,11 +247,6 @@ void bn_running_update_batch(const BnFoldJob* jobs, int njobs, int max_c, const 
 void bn_param_grad_batch(const BnFoldJob* jobs, int njobs, int max_c, int batch, cudaStream_t stream);
 void bn_running_update(const float* stats, long rank_stride, int ranks, int batch, int c, int spatial, float momentum,
                        float* rmean, float* rvar, float* tracked, cudaStream_t stream);
-// Scratch (floats) bias_grad needs for `channels` channels of `batch` images.
-size_t bn_workspace_floats(int batch, int channels);
-// Bias gradient of the final conv: db[n] += sum over images and interior pixels of g[m, n].
-// `ws` is scratch of bn_workspace_floats(batch, channels) floats.
-void bias_grad(const View& g, int batch, const Grid& gr, float* ws, float* db, cudaStream_t stream);
 
 // ---------------------------------------------------------------- loss / assigner
 struct LevelIO {
@@ -262,6 +257,10 @@ struct LevelIO {
     int box_pitch, cls_pitch;
     Grid grid;
     float stride;
+    // optional (backward only): bias gradients of the convs that produce box / cls, accumulated (+=) here
+    // as the loss writes their output gradients: per image the sum over its anchors, images added in order
+    float* box_bias_grad = nullptr;
+    float* cls_bias_grad = nullptr;
 };
 struct TruthBox {
     int cls;
@@ -280,7 +279,7 @@ struct LossOut {
     int* near_ties = nullptr;
 };
 constexpr unsigned kNearTieUlps = 16;
-size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int bins);
+size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int topk, int nc);
 // round_grad: the logit gradients are stored rounded to the nearest TF32 (operands of TF32 convs).
 // serial_cls: the per-image class loss is the reference's float running sum (one term at a time, in its
 // order) instead of the exact sum of the same terms (about 1e-3 apart at 640 x 640).

@@ -174,9 +174,6 @@ __global__ void upsample2_kernel(const float* in, int in_pitch, Grid gin, float*
     }
 }
 
-// Identity-scale letterbox written straight into the stem's parity-split input (PhaseOut layout),
-// 4 floats per pixel (r, g, b, 0).
-// One thread per output pixel of the stem: 27 inputs (u8 / 255) x OC outputs, bias, SiLU.
 // x / 255 correctly rounded for an integer x in [0, 255]: the product with the rounded reciprocal
 // is within one unit in the last place, and one FMA residual step (Markstein's correction) rounds
 // it to the IEEE quotient; checked against IEEE division for every byte value.
@@ -196,6 +193,7 @@ struct StemParams {
     float b[OC];
 };
 
+// One thread per output pixel of the stem: 27 inputs (u8 / 255) x OC outputs, bias, SiLU.
 template <int OC>
 __global__ void __launch_bounds__(256) stem_conv_kernel(const uint8_t* rgb, int batch, int size,
                                                         const StemParams<OC> sp, float* out, int out_pitch,
@@ -244,6 +242,8 @@ __global__ void __launch_bounds__(256) stem_conv_kernel(const uint8_t* rgb, int 
     }
 }
 
+// Identity-scale letterbox written straight into the stem's parity-split input (PhaseOut layout),
+// 4 floats per pixel (r, g, b, 0).
 __global__ void rgb_to_phase_kernel(const uint8_t* rgb, int batch, int size, PhaseOut dst) {
     const long total = (long)batch * size * size;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {

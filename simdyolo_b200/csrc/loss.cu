@@ -22,6 +22,8 @@ namespace {
 
 constexpr int kMaxLevels = 3;
 constexpr int kMaxTopk = 16;
+constexpr int kMaxBceSlots = 8;   // classes per lane in bce_kernel: 3 (nc <= 96) or 8 (nc <= 256)
+constexpr int kMaxBatchFold = 64;   // images per pass of cls_bias_fold_kernel
 constexpr int kMaxSel = 1024;  // max boxes * topk handled by one image's assignment
 
 struct LossParams {
@@ -48,6 +50,8 @@ struct LossParams {
     float* score_sum;     // [batch]
     double* bce_part;     // [batch][bce_blocks]
     int bce_blocks;
+    float* cls_bias_part; // [batch][level][bce_blocks][nc] block partial sums of the class-logit gradient
+    float* box_bias_part; // [batch][level][64] per-image sums of the box-logit gradient over the positives
     float* pos_box;       // [batch][kMaxSel] box loss term
     float* pos_dfl;       // [batch][kMaxSel] dfl loss term
     LossOut out;
@@ -454,11 +458,19 @@ __global__ void __launch_bounds__(256) assign_kernel(LossParams p) {
 
 // ---------------------------------------------------------------- 4. BCE over all anchors x classes
 // (DetectionLoss.cs:104-111).  One warp per anchor row, lanes over classes.
+template <int kBceSlots>
 __global__ void __launch_bounds__(256) bce_kernel(LossParams p, const int* dense_assigned, const float* dense_scores) {
     const int b = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float inv = .5f / p.score_sum[b];
+    const bool bias = p.backward && p.cls_bias_part;
     double acc = 0.0;
+    // this lane's class-logit gradient sums per (level, class slot c = lane + 32 k), for the bias gradient
+    float bsum[kMaxLevels][kBceSlots];
+#pragma unroll
+    for (int l = 0; l < kMaxLevels; l++)
+#pragma unroll
+        for (int k = 0; k < kBceSlots; k++) bsum[l][k] = 0.f;
     for (int a = blockIdx.x * 8 + warp; a < p.anchors; a += gridDim.x * 8) {
         int level, row;
         float cx, cy, st;
@@ -469,7 +481,10 @@ __global__ void __launch_bounds__(256) bce_kernel(LossParams p, const int* dense
         const int tcls = g >= 0 ? p.truth[p.box_off[b] + g].cls : -1;
         const float w = g >= 0 ? dense_scores[(long)b * p.anchors + a] : 0.f;
         float part = 0.f;
-        for (int c = lane; c < p.nc; c += 32) {
+#pragma unroll
+        for (int k = 0; k < kBceSlots; k++) {
+            const int c = lane + 32 * k;
+            if (c >= p.nc) break;
             const float x = L.cls[off + c];
             const float t = c == tcls ? w : 0.f;
             // e = exp(-|x|) serves both the stable log-sum-exp and the sigmoid (HeadOperations.cs:222)
@@ -479,19 +494,94 @@ __global__ void __launch_bounds__(256) bce_kernel(LossParams p, const int* dense
                 const float s = __fdividef(x >= 0.f ? 1.f : e, 1.f + e);
                 const float gr = (s - t) * inv * p.grad_scale;
                 L.dcls[off + c] = p.round_grad ? tf32_rna(gr) : gr;
+#pragma unroll
+                for (int l = 0; l < kMaxLevels; l++)
+                    if (l == level) bsum[l][k] += gr;
             }
         }
         acc += (double)part;
     }
     acc = warp_sum_d(acc);
     __shared__ double red[8];
+    __shared__ float bred[8][kMaxLevels][kBceSlots * 32];
     if (lane == 0) red[warp] = acc;
+    if (bias)
+#pragma unroll
+        for (int l = 0; l < kMaxLevels; l++)
+#pragma unroll
+            for (int k = 0; k < kBceSlots; k++) bred[warp][l][lane + 32 * k] = bsum[l][k];
     __syncthreads();
     if (threadIdx.x == 0) {
         double t = 0.0;
         for (int w = 0; w < 8; w++) t += red[w];
         p.bce_part[(long)b * p.bce_blocks + blockIdx.x] = t;
     }
+    if (bias)
+        for (int i = threadIdx.x; i < p.nlevels * p.nc; i += blockDim.x) {
+            const int l = i / p.nc, c = i - l * p.nc;
+            float t = 0.f;
+            for (int w = 0; w < 8; w++) t += bred[w][l][c];   // warps in order
+            p.cls_bias_part[(((long)b * kMaxLevels + l) * p.bce_blocks + blockIdx.x) * p.nc + c] = t;
+        }
+}
+
+// Bias gradients of the class convs.  Block (level, 32 classes): lane = class, warp w sums the block partials
+// of images w, w + 8, ... (each image's partials in block order), then warp 0 adds the images in order into
+// the level's bias gradient.
+__global__ void __launch_bounds__(256) cls_bias_fold_kernel(LossParams p) {
+    __shared__ float img_s[kMaxBatchFold][32];
+    const int l = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + lane;
+    const bool on = c < p.nc && p.lv[l].cls_bias_grad != nullptr;
+    for (int b0 = 0; b0 < p.batch; b0 += kMaxBatchFold) {
+        const int nb = min(kMaxBatchFold, p.batch - b0);
+        for (int i = warp; i < nb; i += 8) {
+            float img = 0.f;
+            if (on) {
+                const float* part = p.cls_bias_part + ((long)(b0 + i) * kMaxLevels + l) * p.bce_blocks * p.nc + c;
+#pragma unroll 8
+                for (int k = 0; k < p.bce_blocks; k++) img += part[(long)k * p.nc];
+            }
+            img_s[i][lane] = img;
+        }
+        __syncthreads();
+        if (warp == 0 && on) {
+            float total = 0.f;
+            for (int i = 0; i < nb; i++) total += img_s[i][lane];
+            p.lv[l].cls_bias_grad[c] += total;
+        }
+        __syncthreads();
+    }
+}
+
+// Bias gradients of the box convs: the box-logit gradient is zero except at the positives.  box_bias_image:
+// block per image, thread per channel, the sum over the image's positives in anchor order per level;
+// box_bias_fold: thread per (level, channel), images in order into the level's bias gradient.
+__global__ void box_bias_image_kernel(LossParams p) {
+    const int b = blockIdx.x, ch = threadIdx.x;
+    if (ch >= 4 * p.bins) return;
+    float acc[kMaxLevels] = {0.f, 0.f, 0.f};
+    const int n = p.pos_count[b];
+    for (int i = 0; i < n; i++) {
+        const int a = p.pos_anchor[(long)b * kMaxSel + i];
+        int level, row;
+        float cx, cy, st;
+        anchor_location(p, a, level, row, cx, cy, st);
+        const LevelIO& L = p.lv[level];
+        const float v = L.dbox[((long)b * L.grid.rows + row) * L.box_pitch + ch];
+#pragma unroll
+        for (int l = 0; l < kMaxLevels; l++)
+            if (l == level) acc[l] += v;
+    }
+    for (int l = 0; l < p.nlevels; l++) p.box_bias_part[((long)b * kMaxLevels + l) * 64 + ch] = acc[l];
+}
+
+__global__ void box_bias_fold_kernel(LossParams p) {
+    const int l = blockIdx.y, ch = threadIdx.x;
+    if (ch >= 4 * p.bins || !p.lv[l].box_bias_grad) return;
+    float total = 0.f;
+    for (int b = 0; b < p.batch; b++) total += p.box_bias_part[((long)b * kMaxLevels + l) * 64 + ch];
+    p.lv[l].box_bias_grad[ch] += total;
 }
 
 // ---------------------------------------------------------------- 5. CIoU + DFL for positives
@@ -657,7 +747,7 @@ size_t align_up(size_t v) { return (v + 255) & ~size_t(255); }
 
 }  // namespace
 
-size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int topk) {
+size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int topk, int nc) {
     size_t s = 0;
     s += align_up((size_t)batch * anchors * 4 * sizeof(float)) * 2;  // dec, expv
     s += align_up((size_t)batch * max_boxes * topk * sizeof(int));   // sel
@@ -666,6 +756,8 @@ size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int topk) {
     s += align_up((size_t)batch * sizeof(int));                      // pos count
     s += align_up((size_t)batch * sizeof(float));                    // score sum
     s += align_up((size_t)batch * kBceBlocks * sizeof(double));      // bce partials
+    s += align_up((size_t)batch * kMaxLevels * kBceBlocks * nc * sizeof(float));   // class bias partials
+    s += align_up((size_t)batch * kMaxLevels * 64 * sizeof(float));                // box bias per image
     s += align_up((size_t)batch * anchors * sizeof(int));            // dense assigned (if not given)
     s += align_up((size_t)batch * anchors * sizeof(float));          // dense scores (if not given)
     return s;
@@ -714,6 +806,15 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
     p.score_sum = (float*)take((size_t)batch * sizeof(float));
     p.bce_part = (double*)take((size_t)batch * kBceBlocks * sizeof(double));
     p.bce_blocks = kBceBlocks;
+    p.cls_bias_part = (float*)take((size_t)batch * kMaxLevels * kBceBlocks * nc * sizeof(float));
+    p.box_bias_part = (float*)take((size_t)batch * kMaxLevels * 64 * sizeof(float));
+    bool cls_bias = false, box_bias = false;
+    for (int l = 0; l < nlevels; l++) {
+        cls_bias |= backward && levels[l].cls_bias_grad != nullptr;
+        box_bias |= backward && levels[l].box_bias_grad != nullptr;
+    }
+    if (!cls_bias) p.cls_bias_part = nullptr;
+    if (nc > 32 * kMaxBceSlots) throw std::runtime_error("detection_loss: more than 256 classes");
     int* dense_a = (int*)take((size_t)batch * p.anchors * sizeof(int));
     float* dense_s = (float*)take((size_t)batch * p.anchors * sizeof(float));
     p.out = out;
@@ -738,10 +839,23 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
             // box gradients are sparse: clear the whole level, positives are scattered below
             cudaMemsetAsync(L.dbox, 0, (size_t)batch * L.grid.rows * L.box_pitch * sizeof(float), stream);
         }
-    bce_kernel<<<dim3(kBceBlocks, batch), 256, 0, stream>>>(p, p.out.assigned, p.out.scores);
+    if (nc <= 96)
+        bce_kernel<3><<<dim3(kBceBlocks, batch), 256, 0, stream>>>(p, p.out.assigned, p.out.scores);
+    else
+        bce_kernel<8><<<dim3(kBceBlocks, batch), 256, 0, stream>>>(p, p.out.assigned, p.out.scores);
     launch_check("bce_kernel");
     box_kernel<<<dim3((max_boxes * topk + 7) / 8 > 0 ? (max_boxes * topk + 7) / 8 : 1, batch), 256, 0, stream>>>(p);
     launch_check("box_kernel");
+    if (cls_bias) {
+        cls_bias_fold_kernel<<<dim3((nc + 31) / 32, nlevels), 256, 0, stream>>>(p);
+        launch_check("cls_bias_fold_kernel");
+    }
+    if (box_bias) {
+        box_bias_image_kernel<<<batch, 64, 0, stream>>>(p);
+        launch_check("box_bias_image_kernel");
+        box_bias_fold_kernel<<<dim3(1, nlevels), 64, 0, stream>>>(p);
+        launch_check("box_bias_fold_kernel");
+    }
     finalize_kernel<<<batch, 32, 0, stream>>>(p);
     launch_check("finalize_kernel");
     if (serial_cls) {

@@ -148,7 +148,7 @@ Session::Session(const sy_config& c) : cfg(c) {
     }
     // loss, truth, outputs
     const int anchors = levels_[0].h * levels_[0].w + levels_[1].h * levels_[1].w + levels_[2].h * levels_[2].w;
-    loss_ws_ = dalloc(loss_workspace_bytes(B_, anchors, std::max(1, c.max_boxes), 10));
+    loss_ws_ = dalloc(loss_workspace_bytes(B_, anchors, std::max(1, c.max_boxes), 10, c.num_classes));
     d_truth_ = static_cast<TruthBox*>(dalloc(sizeof(TruthBox) * (size_t)B_ * std::max(1, c.max_boxes)));
     d_box_off_ = static_cast<int*>(dalloc(sizeof(int) * (B_ + 1)));
     d_flags_ = static_cast<int*>(dalloc(sizeof(int) * 16));
@@ -675,7 +675,6 @@ void Session::build_head() {
     SY_CUDA(cudaMemcpy(d_segs_, segs.data(), sizeof(ParamSegment) * segs.size(), cudaMemcpyHostToDevice));
     // activations and gradients
     size_t ws = 0;
-    int max_oc = 0;
     size_t bn_part_floats = 0;
     for (auto& branch : branches_) {
         const Grid& g = levels_[branch.level];
@@ -707,7 +706,6 @@ void Session::build_head() {
                                                              (size_t)b.ic * hb.taps * hb.kpad_out));
                 ws = std::max(ws, wgrad_workspace_floats(b.ic, b.oc, hb.taps, (long)B_ * g.rows));
             }
-            max_oc = std::max(max_oc, b.oc);
             x = b.has_bn ? hb.a : hb.y;
         }
     }
@@ -767,7 +765,6 @@ void Session::build_head() {
         center_ws_ = static_cast<float*>(dalloc(
             sizeof(float) * center_workspace_floats(B_, std::max({max_first_oc, feat_ch_[0], feat_ch_[1], feat_ch_[2]}))));
     }
-    bias_part_ = static_cast<float*>(dalloc(sizeof(float) * bn_workspace_floats(B_, max_oc)));
     bn_part_ = static_cast<float*>(dalloc(sizeof(float) * std::max<size_t>(bn_part_floats, 1)));
 }
 
@@ -850,7 +847,7 @@ void Session::backward_head(int batch) {
                         bn_backward_apply(rows_of(hb.y, batch, g), rows_of(hb.g, batch, g), hb.coef, hb.bcoef, batch, g,
                                           rows_of(hb.dy, batch, g), stream_, rnd_);
                     }
-                    if (hb.b.has_bias) bias_grad(hb.dy, batch, g, bias_part_, grads_ + hb.b_off, stream_);
+                    // the final conv's bias gradient was accumulated by the loss kernels (LevelIO::*_bias_grad)
                     if (hb.dw)
                         dw_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off,
                                  wgrad_ws_, stream_);
@@ -920,7 +917,8 @@ void Session::launch_losses(int images, int backward, int epoch) {
             HeadBlock& bb = branches_[set * 6 + l].blocks.back();
             HeadBlock& cb = branches_[set * 6 + 3 + l].blocks.back();
             lv[l] = LevelIO{bb.y.base, cb.y.base, bb.g.base, cb.g.base, bb.y.pitch, cb.y.pitch, levels_[l],
-                            (float)(8 << l)};
+                            (float)(8 << l), bb.b.has_bias ? grads_ + bb.b_off : nullptr,
+                            cb.b.has_bias ? grads_ + cb.b_off : nullptr};
         }
         LossOut lo{d_loss_ + (size_t)4 * B_ * set, d_pos_ + (size_t)B_ * set, d_conn_ + (size_t)B_ * set, nullptr,
                    nullptr, d_ties_ + (size_t)B_ * set};

@@ -193,7 +193,6 @@ private:
     float* feat_stage_ = nullptr;
     float* bn_stats_all_ = nullptr;
     long bn_channels_ = 0;
-    float* bias_part_ = nullptr;
     float* bn_part_ = nullptr;       // per-32-row-group BatchNorm partials written by conv epilogues
     void* loss_ws_ = nullptr;
     TruthBox* d_truth_ = nullptr;
