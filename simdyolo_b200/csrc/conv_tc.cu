@@ -889,11 +889,14 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
                 while (T > 1 && (2 * T * acc_cols > 512 || 2 * stage_bytes(T) + b_min > budget ||
                                  (sub_tiles + T - 1) / T < 2L * num_sms()))
                     T >>= 1;
-                if (!resident && (long)taps * kchunks * b_bytes >= 256 * 1024) {
+                // streamed weights below 512 KB: at most 2 sub-tiles, whose smaller A regions leave the weight
+                // ring more depth (measured on B200 at N = 64 images: 3x3 64->64 at 80x80 94.0 -> 89.4 us,
+                // 128->64 at 40x40 55.6 -> 51.0 us; 80->80 already ran at 2)
+                if (!resident && T > 2 && (long)taps * kchunks * b_bytes < 512 * 1024) T = 2;
+                if (!resident && (long)taps * kchunks * b_bytes >= 512 * 1024) {
                     // large streamed weights are fetched again for every CTA tile, so a small layer may run
                     // faster on fewer, larger tiles: the count of least estimated time among those that fit
-                    // (measured: 18 % faster at 576-720 KB of weights a tile; at 144 KB the deeper weight
-                    // ring of the smaller tile wins, so the rule above stands there)
+                    // (measured: 18 % faster at 576-720 KB of weights a tile)
                     double best = 0.0;
                     int pick = 0;
                     for (int t = 4; t >= 1; t >>= 1) {
