@@ -125,6 +125,38 @@ typedef struct sy_tensor_info {
 
 typedef struct sy_session sy_session;
 
+/* Detection (src/SimdYolo/YoloDetector.cs:139): class, confidence and the box as top-left corner plus
+ * size, in source-image pixels. */
+typedef struct sy_detection {
+    int32_t class_id;
+    float confidence, x, y, width, height;
+} sy_detection;
+
+/* Letterbox (YoloDetector.cs:149): the preprocessing record that maps model pixels back to the source
+ * image, x_source = (x_model - pad_x) / scale_x, clamped to [0, source_width]. */
+typedef struct sy_letterbox {
+    int32_t source_width, source_height, target_width, target_height;
+    float scale_x, scale_y;
+    int32_t pad_x, pad_y;
+} sy_letterbox;
+
+/* DetectorOptions' decode fields (YoloDetector.cs:88-105; defaults 0.25, 0.45, 300, 30000, 0).
+ * DetectionEvaluator.Evaluate uses confidence 0.001, IoU 0.7, 300 detections (DetectionEvaluator.cs:50-51).
+ * max_detections 1 .. 65536; max_candidates >= 1.  sy_cuda_detect* require confidence and iou_threshold in
+ * [0, 1] (the YoloDetector constructor's check); sy_cuda_decode_detections, like the reference's static
+ * decode, takes any value (NaN: no candidate is below the confidence threshold, no overlap above the IoU
+ * threshold). */
+typedef struct sy_detect_options {
+    float confidence, iou_threshold;
+    int32_t max_detections, max_candidates;
+    int32_t class_agnostic;     /* ClassAgnosticNms */
+} sy_detect_options;
+
+#define SY_LAYOUT_AUTO 0            /* OutputLayout (YoloDetector.cs:49-59) */
+#define SY_LAYOUT_CHANNELS_FIRST 1
+#define SY_LAYOUT_CHANNELS_LAST 2
+#define SY_LAYOUT_END_TO_END 3
+
 /* ---- session (replaces YoloTrainer's inner batch loop, YoloTrainer.cs:185-199) ---- */
 SY_API sy_status sy_cuda_nccl_unique_id(uint8_t out[128]);
 SY_API sy_status sy_cuda_create(const sy_config *config, sy_session **out);
@@ -179,6 +211,29 @@ SY_API sy_status sy_cuda_set_optimizer_steps(sy_session *session, const int32_t 
 SY_API sy_status sy_cuda_get_last_gradients(const sy_session *session, float *host, int64_t count);
 /* Frozen features of the last step (NCHW per level), for parity checks. */
 SY_API sy_status sy_cuda_get_last_features(const sy_session *session, int32_t level, float *host, int64_t count);
+/* Raw head outputs of the last step, evaluation or detection (NCHW per level): box logits
+ * [images][4 * reg_max][H_l][W_l] and class logits [images][nc][H_l][W_l] of branch set `set` (0 cv2 / cv3,
+ * 1 one2one_cv2 / one2one_cv3), for parity checks. */
+SY_API sy_status sy_cuda_get_last_head_outputs(const sy_session *session, int32_t set, int32_t level, float *box,
+                                               int64_t box_count, float *cls, int64_t cls_count);
+
+/* ---- inference (YoloDetector.Detect on the session's model, YoloDetector.cs:327-376) ---- */
+
+/* Detection on `images` RGB24 images of S x S (already letterboxed, as for sy_cuda_step): frozen trunk, head
+ * with BatchNorm in evaluation mode (running statistics), decode (CpuHead.DecodeInto, CpuHead.cs:57-120),
+ * then YoloDetector.DecodeIndexed (YoloDetector.cs:539-642): confidence filter, confidence order,
+ * max_candidates, greedy NMS (class-aware unless class_agnostic), max_detections, and the mapping through
+ * transforms[b] (NULL: identity, source S x S).  End-to-end heads use their one-to-one branches and
+ * PtModel.EndToEndTopK (PtModel.cs:530-568, max_det 300) instead of NMS.  out holds
+ * images * max_detections records, image b's counts[b] detections first in its block.  Nothing in the
+ * session's parameters, buffers or optimizer state changes. */
+SY_API sy_status sy_cuda_detect(sy_session *session, const uint8_t *rgb, int32_t images,
+                                const sy_letterbox *transforms, const sy_detect_options *options, sy_detection *out,
+                                int32_t *counts);
+/* The same from cached frozen features (NCHW per level, as for sy_cuda_step_features). */
+SY_API sy_status sy_cuda_detect_features(sy_session *session, const float *const features[3], int32_t images,
+                                         const sy_letterbox *transforms, const sy_detect_options *options,
+                                         sy_detection *out, int32_t *counts);
 
 /* ---- standalone operators (same algorithms as the session, host buffers) ---- */
 
@@ -201,6 +256,28 @@ SY_API sy_status sy_cuda_detection_loss_ex(int32_t device, int32_t images, int32
                                            const int32_t *counts, int32_t topk, int32_t topk2, float grad_scale,
                                            float *out_loss, int32_t *positives, int32_t *assigned, float *scores,
                                            float *const *box_grads, float *const *class_grads);
+
+/* CpuHead.Decode / DecodeInto (CpuHead.cs:50-120) over joined levels, as PtModel.Detect joins them
+ * (PtModel.cs:455-480): box[l] [images][4 * bins][hs[l]][ws[l]] (bins 1 or 16), cls[l] [images][nc][hs[l]][ws[l]]
+ * -> out [images][4 + nc][anchors]: (cx, cy, w, h), or (x1, y1, x2, y2) with xyxy, in model pixels, then the
+ * sigmoid class scores.  levels 1 .. 8. */
+SY_API sy_status sy_cuda_head_decode(int32_t device, int32_t images, int32_t levels, const int32_t *hs,
+                                     const int32_t *ws, const float *strides, int32_t bins, int32_t nc, int32_t xyxy,
+                                     const float *const *box, const float *const *cls, float *out);
+/* PtModel.EndToEndTopK (PtModel.cs:530-568): x [images][fields][anchors] (4 box fields, nc scores, extra
+ * fields) -> out [images][k][6 + fields - nc - 4], k = min(maximum, anchors) (maximum 1 .. 1024): the k
+ * anchors with the largest class maximum, then the k largest (anchor, class) scores among them, ordered by
+ * score, anchor and class; rows (box fields, score, class, extra fields). */
+SY_API sy_status sy_cuda_end_to_end_topk(int32_t device, const float *x, int32_t images, int32_t fields,
+                                         int32_t anchors, int32_t nc, int32_t maximum, float *out);
+/* YoloDetector.DecodeIndexed (YoloDetector.cs:539-642) per image on output [images][dim1][dim2] in
+ * `layout` (SY_LAYOUT_*; AUTO is resolved from class_count and the shape as the reference does);
+ * class_count 0 means every field after the box is a class score.  transforms[images] (NULL: identity with
+ * a source of 2^20 x 2^20); out [images][max_detections], counts[images]. */
+SY_API sy_status sy_cuda_decode_detections(int32_t device, const float *output, int32_t images, int32_t dim1,
+                                           int32_t dim2, int32_t layout, int32_t class_count,
+                                           const sy_letterbox *transforms, const sy_detect_options *options,
+                                           sy_detection *out, int32_t *counts);
 
 /* HeadOperations.Conv (HeadOperations.cs:29-82) batched: x NCHW [n][ic][h][w], w OIHW [oc][ic][k][k],
  * stride 1, padding k/2.  forward: y = conv(x, w) (+ bias);  backward_data: dx = conv^T(dy, w);

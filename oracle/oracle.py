@@ -57,6 +57,22 @@ class StepResult(C.Structure):
                 ("box_has_grad", C.c_int32), ("status", C.c_int32)]
 
 
+class Detection(C.Structure):
+    _fields_ = [("class_id", C.c_int32), ("confidence", C.c_float), ("x", C.c_float), ("y", C.c_float),
+                ("width", C.c_float), ("height", C.c_float)]
+
+
+class Letterbox(C.Structure):
+    _fields_ = [("source_width", C.c_int32), ("source_height", C.c_int32), ("target_width", C.c_int32),
+                ("target_height", C.c_int32), ("scale_x", C.c_float), ("scale_y", C.c_float), ("pad_x", C.c_int32),
+                ("pad_y", C.c_int32)]
+
+
+class DetectOptions(C.Structure):
+    _fields_ = [("confidence", C.c_float), ("iou_threshold", C.c_float), ("max_detections", C.c_int32),
+                ("max_candidates", C.c_int32), ("class_agnostic", C.c_int32)]
+
+
 def build() -> None:
     """Compile liboracle.so with the Makefile beside this file."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
@@ -110,6 +126,18 @@ def lib():
         L.syo_train_step.argtypes = [C.POINTER(BackboneDesc), F32P, C.POINTER(HeadDesc), F32P, F32P, F32P, F32P,
                                      C.POINTER(Optim), C.POINTER(vp), C.POINTER(Box), I32P, C.c_int, C.c_int, vp,
                                      C.POINTER(StepResult)]
+        L.syo_head_eval_outputs.argtypes = [C.POINTER(HeadDesc), F32P, F32P, C.POINTER(vp), C.c_int,
+                                            C.POINTER(vp), C.POINTER(vp)]
+        L.syo_head_eval_outputs.restype = C.c_int
+        L.syo_head_decode.argtypes = [F32P, F32P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, C.c_int,
+                                      F32P, C.c_int, C.c_int]
+        L.syo_end_to_end_topk.argtypes = [F32P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, F32P]
+        L.syo_end_to_end_topk.restype = C.c_int
+        L.syo_decode_detections.argtypes = [F32P, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(Letterbox),
+                                            C.POINTER(DetectOptions), C.POINTER(Detection)]
+        L.syo_decode_detections.restype = C.c_int
+        L.syo_detection_iou.argtypes = [C.POINTER(Detection), C.POINTER(Detection)]
+        L.syo_detection_iou.restype = C.c_float
         _lib = L
     return _lib
 
@@ -257,3 +285,46 @@ def ciou(p, t):
     v = lib().syo_ciou(p.ctypes.data_as(C.POINTER(C.c_float)), t.ctypes.data_as(C.POINTER(C.c_float)),
                        g.ctypes.data_as(C.POINTER(C.c_float)))
     return v, g
+
+
+# ---------------------------------------------------------------- detection post-processing
+
+def head_decode(levels, bins, nc, xyxy=False):
+    """CpuHead.DecodeInto over joined levels: levels = [(box [B][4*bins][h][w], cls [B][nc][h][w], stride)].
+    Returns [B][nc + 4][anchors] float32."""
+    batch = levels[0][0].shape[0]
+    anchors = sum(b.shape[2] * b.shape[3] for b, _, _ in levels)
+    out = np.zeros((batch, nc + 4, anchors), np.float32)
+    start = 0
+    for box, cls, stride in levels:
+        box, cls = _f32(box), _f32(cls)
+        h, w = box.shape[2], box.shape[3]
+        lib().syo_head_decode(box, cls, batch, h, w, bins, nc, stride, int(xyxy), out, anchors, start)
+        start += h * w
+    return out
+
+
+def end_to_end_topk(x, nc, maximum=300):
+    """PtModel.EndToEndTopK: x [B][fields][anchors] -> [B][min(maximum, anchors)][6 + extra]."""
+    x = _f32(x)
+    batch, fields, anchors = x.shape
+    k = min(maximum, anchors)
+    out = np.zeros((batch, k, 6 + fields - nc - 4), np.float32)
+    assert lib().syo_end_to_end_topk(x, batch, fields, anchors, nc, maximum, out) == k
+    return out
+
+
+def decode_detections(output, layout, class_count=0, letterbox=None, confidence=0.25, iou_threshold=0.45,
+                      max_detections=300, max_candidates=30000, class_agnostic=False):
+    """YoloDetector.DecodeIndexed on one image's output [dim1][dim2]; layout 1 channels-first, 2 channels-last,
+    3 end-to-end.  Returns a list of (class_id, confidence, x, y, width, height) in output order."""
+    output = _f32(output)
+    dim1, dim2 = output.shape
+    if letterbox is None:
+        letterbox = Letterbox(1 << 20, 1 << 20, 1 << 20, 1 << 20, 1.0, 1.0, 0, 0)
+    opt = DetectOptions(confidence, iou_threshold, max_detections, max_candidates, int(class_agnostic))
+    out = (Detection * max_detections)()
+    n = lib().syo_decode_detections(output, dim1, dim2, layout, class_count, C.byref(letterbox), C.byref(opt), out)
+    if n < 0:
+        raise ValueError(f"syo_decode_detections: {n}")
+    return [(d.class_id, d.confidence, d.x, d.y, d.width, d.height) for d in out[:n]]

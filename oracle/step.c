@@ -320,6 +320,33 @@ int syo_head_eval_image(const syo_head_desc *d, const float *params, float *buff
     return rc;
 }
 
+/* The branch outputs of DetectionHead.Forward in evaluation mode (Branch.Forward, DetectionHead.cs:146-157,
+ * BatchNorm with the running statistics), the input of the inference decode (PtModel.Detect). */
+int syo_head_eval_outputs(const syo_head_desc *d, const float *params, const float *buffers,
+                          const float *const *features, int set, float *const *box, float *const *cls)
+{
+    if (set < 0 || set >= n_branches(d) / 6) return -1;
+    long nb = syo_head_buffer_count(d);
+    float *stats = (float *)calloc(nb ? nb : 1, sizeof(float));
+    float *scratch = (float *)malloc(sizeof(float) * (nb ? nb : 1));
+    memcpy(scratch, buffers, sizeof(float) * (size_t)nb);
+    for (int kind = 0; kind < 2; kind++)
+        for (int l = 0; l < 3; l++) {
+            const int br = set * 6 + kind * 3 + l;
+            block_slot slots[8];
+            block_state states[8];
+            const int n = slots_for_branch(d, br, slots);
+            const float *y = branch_forward(d, slots, n, params, scratch, stats, features[l], d->hs[l], d->ws[l],
+                                            states, 0);
+            const int oc = slots[n - 1].b->oc;
+            memcpy(kind ? cls[l] : box[l], y, sizeof(float) * (size_t)oc * d->hs[l] * d->ws[l]);
+            free_states(states, n);
+        }
+    free(scratch);
+    free(stats);
+    return 0;
+}
+
 /* ------------------------------------------------------------------ frozen backbone */
 
 static int make_div8(float x)

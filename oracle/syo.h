@@ -13,7 +13,8 @@
  *   src/SimdYolo.Training/DetectionHead.cs     branch / block order, ProgressiveWeight
  *   src/SimdYolo.Training/YoloTrainer.cs       per-batch accumulate -> check -> update
  *   src/SimdYolo/PtModel.cs                    frozen backbone layer semantics (BN folded)
- *   src/SimdYolo/YoloDetector.cs               letterbox at identity scale (u8 / 255)
+ *   src/SimdYolo/YoloDetector.cs               letterbox at identity scale (u8 / 255); DecodeIndexed, Iou
+ *   src/SimdYolo/CpuHead.cs                    head decode (DFL expectation, boxes, sigmoid scores)
  *
  * Transcendental functions used by the assigner (exp, atan) come from detmath.c:
  * double-precision evaluations written from published methods, so the CUDA build can
@@ -114,6 +115,10 @@ int syo_head_image(const syo_head_desc *d, const float *params, float *buffers,
 
 int syo_head_eval_image(const syo_head_desc *d, const float *params, float *buffers, const float *const *features,
                         const syo_box *truth, int n_truth, syo_loss *loss);
+/* The head's raw outputs in evaluation mode (BatchNorm with the running statistics), one image: branch set
+ * `set` (0 cv2 / cv3, 1 one2one_cv2 / one2one_cv3); box[l] receives [4*bins][H_l][W_l], cls[l] [nc][H_l][W_l]. */
+int syo_head_eval_outputs(const syo_head_desc *d, const float *params, const float *buffers,
+                          const float *const *features, int set, float *const *box, float *const *cls);
 
 /* ---- frozen backbone (backbone.c): YOLOv8-family detection trunk with folded BN ---- */
 typedef struct {
@@ -127,6 +132,26 @@ void syo_backbone_feature_channels(const syo_backbone_desc *d, int32_t ch[3]);
 /* rgb: HWC u8 image of size image x image; features out: NCHW per level */
 void syo_backbone_forward(const syo_backbone_desc *d, const float *params, const uint8_t *rgb,
                           float *p3, float *p4, float *p5);
+
+/* ---- detection post-processing (detect.c) ---- */
+typedef struct { int32_t class_id; float confidence, x, y, width, height; } syo_detection;      /* Detection */
+typedef struct { int32_t source_width, source_height, target_width, target_height;
+                 float scale_x, scale_y; int32_t pad_x, pad_y; } syo_letterbox;                 /* Letterbox */
+typedef struct { float confidence, iou_threshold; int32_t max_detections, max_candidates, class_agnostic; }
+    syo_detect_options;
+
+/* CpuHead.DecodeInto, one level: box [batch][4*bins][h][w], cls [batch][nc][h][w] into
+ * out [batch][nc+4][out_anchors] at anchors out_start.. (cx, cy, w, h or x1, y1, x2, y2; sigmoid scores) */
+void syo_head_decode(const float *box, const float *cls, int batch, int h, int w, int bins, int nc, float stride,
+                     int xyxy, float *out, int out_anchors, int out_start);
+/* PtModel.EndToEndTopK: x [batch][fields][anchors] -> out [batch][k][6 + fields - nc - 4]; returns k */
+int syo_end_to_end_topk(const float *x, int batch, int fields, int anchors, int nc, int maximum, float *out);
+/* YoloDetector.DecodeIndexed for one image; layout 1 channels-first, 2 channels-last, 3 end-to-end.
+ * out holds max_detections entries; returns the count, -1 on invalid arguments, -2 when a class id of an
+ * end-to-end row exceeds Int32 (the reference's checked conversion throws). */
+int syo_decode_detections(const float *output, int dim1, int dim2, int layout, int class_count,
+                          const syo_letterbox *t, const syo_detect_options *o, syo_detection *out);
+float syo_detection_iou(const syo_detection *a, const syo_detection *b);
 
 /* ---- full optimizer step (step.c) ---- */
 typedef struct {

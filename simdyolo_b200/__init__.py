@@ -84,6 +84,44 @@ class StepStats(C.Structure):
                 ("device_ms", C.c_double), ("near_ties", C.c_int64)]
 
 
+class Detection(C.Structure):
+    """Detection (YoloDetector.cs:139): class, confidence, top-left corner and size in source pixels."""
+    _fields_ = [("class_id", C.c_int32), ("confidence", C.c_float), ("x", C.c_float), ("y", C.c_float),
+                ("width", C.c_float), ("height", C.c_float)]
+
+
+class Letterbox(C.Structure):
+    """Letterbox (YoloDetector.cs:149): x_source = (x_model - pad_x) / scale_x, clamped to the source."""
+    _fields_ = [("source_width", C.c_int32), ("source_height", C.c_int32), ("target_width", C.c_int32),
+                ("target_height", C.c_int32), ("scale_x", C.c_float), ("scale_y", C.c_float), ("pad_x", C.c_int32),
+                ("pad_y", C.c_int32)]
+
+
+class DetectOptions(C.Structure):
+    """DetectorOptions' decode fields (YoloDetector.cs:88-105)."""
+    _fields_ = [("confidence", C.c_float), ("iou_threshold", C.c_float), ("max_detections", C.c_int32),
+                ("max_candidates", C.c_int32), ("class_agnostic", C.c_int32)]
+
+
+SY_LAYOUT_AUTO, SY_LAYOUT_CHANNELS_FIRST, SY_LAYOUT_CHANNELS_LAST, SY_LAYOUT_END_TO_END = 0, 1, 2, 3
+
+
+def detect_options(confidence: float = 0.25, iou_threshold: float = 0.45, max_detections: int = 300,
+                   max_candidates: int = 30000, class_agnostic: bool = False) -> DetectOptions:
+    """DetectorOptions defaults (YoloDetector.cs:92-104)."""
+    return DetectOptions(confidence, iou_threshold, max_detections, max_candidates, int(class_agnostic))
+
+
+def evaluation_options() -> DetectOptions:
+    """The detector settings of DetectionEvaluator.Evaluate (DetectionEvaluator.cs:50-51)."""
+    return detect_options(0.001, 0.7, 300)
+
+
+def _detections(out, counts, max_det):
+    return [[(d.class_id, d.confidence, d.x, d.y, d.width, d.height) for d in out[b * max_det:b * max_det + int(n)]]
+            for b, n in enumerate(counts)]
+
+
 class TensorInfo(C.Structure):
     _fields_ = [("name", C.c_char * 96), ("kind", C.c_int32), ("rank", C.c_int32), ("shape", C.c_int32 * 4),
                 ("numel", C.c_int64)]
@@ -153,6 +191,16 @@ def lib():
                                            C.POINTER(C.c_int64)]
         L.sy_cuda_conv_profile_launches.argtypes = [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), ip, st,
                                                     C.POINTER(C.c_int32)]
+        dp, lp, op = C.POINTER(Detection), C.POINTER(Letterbox), C.POINTER(DetectOptions)
+        L.sy_cuda_detect.argtypes = [vp, C.POINTER(C.c_uint8), C.c_int32, lp, op, dp, ip]
+        L.sy_cuda_detect_features.argtypes = [vp, C.POINTER(fp), C.c_int32, lp, op, dp, ip]
+        L.sy_cuda_get_last_head_outputs.argtypes = [vp, C.c_int32, C.c_int32, fp, C.c_int64, fp, C.c_int64]
+        L.sy_cuda_head_decode.argtypes = [C.c_int32, C.c_int32, C.c_int32, ip, ip, fp, C.c_int32, C.c_int32,
+                                          C.c_int32, C.POINTER(fp), C.POINTER(fp), fp]
+        L.sy_cuda_end_to_end_topk.argtypes = [C.c_int32, fp, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                              fp]
+        L.sy_cuda_decode_detections.argtypes = [C.c_int32, fp, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                                C.c_int32, lp, op, dp, ip]
         _lib = L
     return _lib
 
@@ -167,7 +215,9 @@ EXPORTED = ["sy_cuda_nccl_unique_id", "sy_cuda_create", "sy_cuda_destroy", "sy_c
             "sy_cuda_conv2d_backward_filter_static", "sy_cuda_conv_profile", "sy_cuda_eval_loss",
             "sy_cuda_eval_loss_features", "sy_cuda_detection_loss_ex", "sy_cuda_set_epoch",
             "sy_cuda_conv_profile_launches", "sy_cuda_get_optimizer_steps", "sy_cuda_set_optimizer_steps",
-            "sy_cuda_wait_limit_selftest"]
+            "sy_cuda_wait_limit_selftest", "sy_cuda_detect", "sy_cuda_detect_features",
+            "sy_cuda_get_last_head_outputs", "sy_cuda_head_decode", "sy_cuda_end_to_end_topk",
+            "sy_cuda_decode_detections"]
 
 
 def _check(status: int, session=None):
@@ -569,6 +619,38 @@ class Session:
         _check(lib().sy_cuda_get_last_features(self._h, level, _fp(out), out.size), self._h)
         return out.reshape(shape)
 
+    def last_head_outputs(self, level: int, images: int, set: int = 0):
+        """Raw (box, class) logits of the latest head forward (over `images` images) at `level`, NCHW."""
+        c = self.config
+        h = c.image_size >> (3 + level)
+        box = np.zeros((images, 4 * c.reg_max, h, h), np.float32)
+        cls = np.zeros((images, c.num_classes, h, h), np.float32)
+        _check(lib().sy_cuda_get_last_head_outputs(self._h, set, level, _fp(box), box.size, _fp(cls), cls.size),
+               self._h)
+        return box, cls
+
+    def _detect(self, fn, source, images, options, transforms):
+        o = options if options is not None else detect_options()
+        tf = None
+        if transforms is not None:
+            tf = (Letterbox * images)(*transforms)
+        out = (Detection * (images * o.max_detections))()
+        counts = np.zeros(images, np.int32)
+        _check(fn(self._h, source, images, tf, C.byref(o), out, _ip(counts)), self._h)
+        return _detections(out, counts, o.max_detections)
+
+    def detect(self, images: np.ndarray, options: DetectOptions = None, transforms=None):
+        """YoloDetector.Detect on letterboxed uint8 [B, S, S, 3] images: per image a list of
+        (class_id, confidence, x, y, width, height) in source pixels (transforms: one Letterbox per image)."""
+        img = np.ascontiguousarray(images, np.uint8)
+        return self._detect(lib().sy_cuda_detect, img.ctypes.data_as(C.POINTER(C.c_uint8)), img.shape[0], options,
+                            transforms)
+
+    def detect_features(self, features, options: DetectOptions = None, transforms=None):
+        feats = [np.ascontiguousarray(f, np.float32) for f in features]
+        ptrs = (C.POINTER(C.c_float) * 3)(*[_fp(f) for f in feats])
+        return self._detect(lib().sy_cuda_detect_features, ptrs, feats[0].shape[0], options, transforms)
+
 
 def wait_limit_selftest(spins: int, device: int = 0) -> int:
     """Runs the bounded-wait check kernel (sy_cuda_wait_limit_selftest): returns the error code the wait
@@ -599,6 +681,48 @@ def nccl_unique_id() -> bytes:
 
 
 # ------------------------------------------------------------------ standalone operators
+
+def head_decode(levels, bins: int, nc: int, xyxy: bool = False, device: int = 0) -> np.ndarray:
+    """CpuHead.DecodeInto over joined levels on the GPU: levels = [(box [B, 4*bins, h, w], cls [B, nc, h, w],
+    stride)].  Returns [B, 4 + nc, anchors]."""
+    bl = [np.ascontiguousarray(b, np.float32) for b, _, _ in levels]
+    cl = [np.ascontiguousarray(c, np.float32) for _, c, _ in levels]
+    B = bl[0].shape[0]
+    hs = np.array([b.shape[2] for b in bl], np.int32)
+    ws = np.array([b.shape[3] for b in bl], np.int32)
+    st = np.array([s for _, _, s in levels], np.float32)
+    out = np.zeros((B, nc + 4, int((hs * ws).sum())), np.float32)
+    P = C.POINTER(C.c_float) * len(bl)
+    _check(lib().sy_cuda_head_decode(device, B, len(bl), _ip(hs), _ip(ws), _fp(st), bins, nc, int(xyxy),
+                                     P(*map(_fp, bl)), P(*map(_fp, cl)), _fp(out)))
+    return out
+
+
+def end_to_end_topk(x, nc: int, maximum: int = 300, device: int = 0) -> np.ndarray:
+    """PtModel.EndToEndTopK on the GPU: x [B, fields, anchors] -> [B, min(maximum, anchors), 6 + extra]."""
+    x = np.ascontiguousarray(x, np.float32)
+    B, fields, anchors = x.shape
+    out = np.zeros((B, min(maximum, anchors), 6 + fields - nc - 4), np.float32)
+    _check(lib().sy_cuda_end_to_end_topk(device, _fp(x), B, fields, anchors, nc, maximum, _fp(out)))
+    return out
+
+
+def decode_detections(output, layout: int = SY_LAYOUT_AUTO, class_count: int = 0, transforms=None,
+                      options: DetectOptions = None, device: int = 0):
+    """YoloDetector.DecodeIndexed on the GPU for output [B, dim1, dim2]: per image a list of
+    (class_id, confidence, x, y, width, height)."""
+    x = np.ascontiguousarray(output, np.float32)
+    if x.ndim == 2:
+        x = x[None]
+    B, d1, d2 = x.shape
+    o = options if options is not None else detect_options()
+    tf = (Letterbox * B)(*transforms) if transforms is not None else None
+    out = (Detection * (B * o.max_detections))()
+    counts = np.zeros(B, np.int32)
+    _check(lib().sy_cuda_decode_detections(device, _fp(x), B, d1, d2, layout, class_count, tf, C.byref(o), out,
+                                           _ip(counts)))
+    return _detections(out, counts, o.max_detections)
+
 
 def detection_loss(boxes, classes, strides, truth, nc, device=0, with_grad=True, reg_max=16, topk=10, topk2=10,
                    grad_scale=1.0):

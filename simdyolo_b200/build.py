@@ -11,7 +11,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libsimdyolo_cuda.so")
-SOURCES = ["capi.cu", "session.cu", "conv_tc.cu", "layout.cu", "bn.cu", "loss.cu", "optim.cu", "noalloc.cu", "dwconv.cu", "attn.cu"]
+SOURCES = ["capi.cu", "session.cu", "conv_tc.cu", "layout.cu", "bn.cu", "loss.cu", "optim.cu", "noalloc.cu", "dwconv.cu", "attn.cu", "detect.cu"]
 HEADERS = ["common.cuh", "kernels.h", "session.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-gencode", "arch=compute_100a,code=sm_100a", "-Xcompiler", "-fPIC",

@@ -212,6 +212,23 @@ sy_status sy_cuda_eval_loss_features(sy_session* session, const float* const fea
                    [&] { return session->impl->evaluate(nullptr, false, features, boxes, counts, images, out); });
 }
 
+sy_status sy_cuda_detect(sy_session* session, const uint8_t* rgb, int32_t images, const sy_letterbox* transforms,
+                         const sy_detect_options* options, sy_detection* out, int32_t* counts) {
+    if (!session || !rgb) return SY_ERR_INVALID_ARGUMENT;
+    return guarded(session, [&] {
+        return session->impl->detect(rgb, false, nullptr, images, transforms, options, out, counts);
+    });
+}
+
+sy_status sy_cuda_detect_features(sy_session* session, const float* const features[3], int32_t images,
+                                  const sy_letterbox* transforms, const sy_detect_options* options, sy_detection* out,
+                                  int32_t* counts) {
+    if (!session || !features) return SY_ERR_INVALID_ARGUMENT;
+    return guarded(session, [&] {
+        return session->impl->detect(nullptr, false, features, images, transforms, options, out, counts);
+    });
+}
+
 int64_t sy_cuda_launch_count(void) { return sy::launch_count(); }
 
 sy_status sy_cuda_conv_profile(sy_session* session, int32_t enable, double* ms, double* gflop, int64_t* launches) {
@@ -336,7 +353,124 @@ sy_status sy_cuda_get_last_features(const sy_session* session, int32_t level, fl
     return guarded(s, [&] { return s->impl->get_last_features(level, host, (long)count); });
 }
 
+sy_status sy_cuda_get_last_head_outputs(const sy_session* session, int32_t set, int32_t level, float* box,
+                                        int64_t box_count, float* cls, int64_t cls_count) {
+    if (!session) return SY_ERR_INVALID_ARGUMENT;
+    sy_session* s = const_cast<sy_session*>(session);
+    return guarded(s, [&] {
+        return s->impl->get_last_head_outputs(set, level, box, (long)box_count, cls, (long)cls_count);
+    });
+}
+
 // ------------------------------------------------------------------ standalone operators
+
+sy_status sy_cuda_head_decode(int32_t device, int32_t images, int32_t levels, const int32_t* hs, const int32_t* ws,
+                              const float* strides, int32_t bins, int32_t nc, int32_t xyxy, const float* const* box,
+                              const float* const* cls, float* out) {
+    return guarded(nullptr, [&] {
+        if (images < 1 || levels < 1 || levels > sy::kMaxDetectLevels || !hs || !ws || !strides || !box || !cls ||
+            !out || nc < 0 || bins < 1)
+            throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "head_decode: bad arguments");
+        check_device(device);
+        Scratch s;
+        long anchors = 0;
+        for (int l = 0; l < levels; l++) {
+            if (hs[l] < 1 || ws[l] < 1 || !box[l] || (nc > 0 && !cls[l]))
+                throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "head_decode: bad level");
+            anchors += (long)hs[l] * ws[l];
+        }
+        if ((nc + 4) * anchors * images > (1L << 31))
+            throw sy::SyError(SY_ERR_UNSUPPORTED_SHAPE, "head_decode: output above 2^31 elements");
+        sy::DetectLevelSrc lv[sy::kMaxDetectLevels];
+        for (int l = 0; l < levels; l++) {
+            const long hw = (long)hs[l] * ws[l];
+            float* db = s.get<float>((size_t)images * 4 * bins * hw);
+            float* dc = s.get<float>((size_t)images * std::max(nc, 1) * hw);
+            CK(cudaMemcpy(db, box[l], sizeof(float) * images * 4 * bins * hw, cudaMemcpyHostToDevice));
+            if (nc > 0) CK(cudaMemcpy(dc, cls[l], sizeof(float) * images * nc * hw, cudaMemcpyHostToDevice));
+            lv[l] = sy::DetectLevelSrc{db, dc, {4L * bins * hw, hw, ws[l], 1}, {(long)nc * hw, hw, ws[l], 1}, hs[l],
+                                       ws[l], strides[l]};
+        }
+        float* dout = s.get<float>((size_t)images * (nc + 4) * anchors);
+        sy::head_decode(lv, levels, images, bins, nc, xyxy ? 1 : 0, dout, 0);
+        CK(cudaMemcpy(out, dout, sizeof(float) * images * (nc + 4) * anchors, cudaMemcpyDeviceToHost));
+        return SY_OK;
+    });
+}
+
+sy_status sy_cuda_end_to_end_topk(int32_t device, const float* x, int32_t images, int32_t fields, int32_t anchors,
+                                  int32_t nc, int32_t maximum, float* out) {
+    return guarded(nullptr, [&] {
+        if (!x || !out || images < 1 || nc < 1 || fields < nc + 4 || anchors < 1 || maximum < 1)
+            throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "end_to_end_topk: bad arguments");
+        if (maximum > sy::kMaxEndToEndTopk)
+            throw sy::SyError(SY_ERR_UNSUPPORTED_SHAPE, "end_to_end_topk: maximum above 1024");
+        if ((long)anchors * nc >= 0xffffffffL || (long)images * fields * anchors > (1L << 31))
+            throw sy::SyError(SY_ERR_UNSUPPORTED_SHAPE, "end_to_end_topk: input too large");
+        check_device(device);
+        Scratch s;
+        const int k = std::min(maximum, anchors), width = 6 + fields - nc - 4;
+        float* dx = s.get<float>((size_t)images * fields * anchors);
+        float* dout = s.get<float>((size_t)images * k * width);
+        void* ws_ = s.get<uint8_t>(sy::end_to_end_workspace_bytes(images, anchors, nc, k));
+        CK(cudaMemcpy(dx, x, sizeof(float) * images * fields * anchors, cudaMemcpyHostToDevice));
+        sy::end_to_end_topk(dx, images, fields, anchors, nc, k, dout, ws_, 0);
+        CK(cudaMemcpy(out, dout, sizeof(float) * images * k * width, cudaMemcpyDeviceToHost));
+        return SY_OK;
+    });
+}
+
+sy_status sy_cuda_decode_detections(int32_t device, const float* output, int32_t images, int32_t dim1, int32_t dim2,
+                                    int32_t layout, int32_t class_count, const sy_letterbox* transforms,
+                                    const sy_detect_options* options, sy_detection* out, int32_t* counts) {
+    return guarded(nullptr, [&] {
+        if (!output || !out || !counts || images < 1 || dim1 < 1 || dim2 < 1 || class_count < 0)
+            throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "decode_detections: bad arguments");
+        const sy::DetectOptions o = sy::detect_options(options, false);
+        // OutputLayout.Auto (YoloDetector.cs:545-555)
+        if (layout == SY_LAYOUT_AUTO) {
+            const int expected = class_count > 0 ? 4 + class_count : 0;
+            if (expected > 0 && dim1 == expected && dim2 != expected) layout = SY_LAYOUT_CHANNELS_FIRST;
+            else if (expected > 0 && dim2 == expected && dim1 != expected) layout = SY_LAYOUT_CHANNELS_LAST;
+            else if (dim2 == 6 && dim1 != 6) layout = SY_LAYOUT_END_TO_END;
+            else if (dim1 >= 5 && dim1 < dim2) layout = SY_LAYOUT_CHANNELS_FIRST;
+            else if (dim2 >= 5 && dim2 < dim1) layout = SY_LAYOUT_CHANNELS_LAST;
+            else throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "ambiguous YOLO output layout; set the layout explicitly");
+        }
+        if (layout < SY_LAYOUT_CHANNELS_FIRST || layout > SY_LAYOUT_END_TO_END)
+            throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "decode_detections: unknown layout");
+        const bool cf = layout == SY_LAYOUT_CHANNELS_FIRST, e2e = layout == SY_LAYOUT_END_TO_END;
+        const int count = cf ? dim2 : dim1, fields = cf ? dim1 : dim2;
+        if (fields < 5 || (e2e && fields != 6)) throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "invalid detection output");
+        const int class_fields = class_count > 0 ? 4 + class_count : fields;
+        if (!e2e && (class_fields < 5 || class_fields > fields))
+            throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "class count does not match the output");
+        if ((long)images * dim1 * dim2 > (1L << 31))
+            throw sy::SyError(SY_ERR_UNSUPPORTED_SHAPE, "decode_detections: output above 2^31 elements");
+        std::vector<sy::DetectTransform> tf(images);
+        for (int b = 0; b < images; b++)
+            tf[b] = sy::detect_transform(transforms ? transforms[b]
+                                                    : sy_letterbox{1 << 20, 1 << 20, 1 << 20, 1 << 20, 1.f, 1.f, 0, 0});
+        check_device(device);
+        Scratch s;
+        float* dx = s.get<float>((size_t)images * dim1 * dim2);
+        sy::DetectTransform* dtf = s.get<sy::DetectTransform>(images);
+        sy::DetOut* dout = s.get<sy::DetOut>((size_t)images * o.max_det);
+        int* dcounts = s.get<int>(images);
+        int* derr = s.get<int>(1);
+        void* ws_ = s.get<uint8_t>(sy::detections_workspace_bytes(images, count, o.max_det));
+        CK(cudaMemcpy(dx, output, sizeof(float) * images * dim1 * dim2, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(dtf, tf.data(), sizeof(sy::DetectTransform) * images, cudaMemcpyHostToDevice));
+        sy::decode_detections(dx, images, (long)dim1 * dim2, cf ? 1 : fields, cf ? count : 1, count, class_fields, e2e,
+                              dtf, o, dout, dcounts, derr, ws_, 0);
+        int err = 0;
+        CK(cudaMemcpy(&err, derr, sizeof(int), cudaMemcpyDeviceToHost));
+        if (err) throw sy::SyError(SY_ERR_INVALID_ARGUMENT, "decode_detections: class id out of Int32 range");
+        CK(cudaMemcpy(counts, dcounts, sizeof(int) * images, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(out, dout, sizeof(sy::DetOut) * images * o.max_det, cudaMemcpyDeviceToHost));
+        return SY_OK;
+    });
+}
 
 sy_status sy_cuda_detection_loss(int32_t device, int32_t images, int32_t levels, const int32_t* hs, const int32_t* ws,
                                  const float* strides, int32_t nc, int32_t reg_max, const float* const* boxes,

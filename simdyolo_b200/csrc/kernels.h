@@ -287,6 +287,48 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
                     const int* box_offsets, int max_boxes, int topk, int topk2, float grad_scale, int backward, void* workspace,
                     const LossOut& out, cudaStream_t stream, bool round_grad = false, bool serial_cls = false);
 
+// ---------------------------------------------------------------- inference post-processing (detect.cu)
+constexpr int kMaxDetectLevels = 8;
+constexpr int kMaxEndToEndTopk = 1024;
+// One level of raw head outputs: element (image, channel, row, column) of the box (4 * bins channels) and
+// class (nc channels) logits at base + the dot product of the index with the strides (in floats).
+struct DetectLevelSrc {
+    const float* box;
+    const float* cls;
+    long box_s[4];
+    long cls_s[4];
+    int h, w;
+    float stride;
+};
+// Letterbox record (model pixels -> source pixels), pads and sizes converted to float.
+struct DetectTransform {
+    float scale_x, scale_y, pad_x, pad_y, source_w, source_h;
+};
+struct DetectOptions {
+    float confidence, iou;
+    int max_det, max_candidates, agnostic;
+};
+struct DetOut {   // same layout as sy_detection
+    int class_id;
+    float confidence, x, y, width, height;
+};
+// CpuHead.DecodeInto over the joined levels: out [batch][4 + nc][anchors]; xyxy for end-to-end heads.
+void head_decode(const DetectLevelSrc* levels, int nlevels, int batch, int bins, int nc, int xyxy, float* out,
+                 cudaStream_t stream);
+// PtModel.EndToEndTopK: x [batch][fields][anchors] -> out [batch][min(k, anchors)][6 + fields - nc - 4];
+// k <= kMaxEndToEndTopk, anchors * nc < 2^32.
+size_t end_to_end_workspace_bytes(int batch, int anchors, int nc, int k);
+void end_to_end_topk(const float* x, int batch, int fields, int anchors, int nc, int k, float* out, void* ws,
+                     cudaStream_t stream);
+// YoloDetector.DecodeIndexed per image: value (anchor a, field f) of image b at
+// x[b * img_stride + a * a_stride + f * f_stride]; class_fields = 4 + classes (raw heads) or unused (e2e:
+// fields x1, y1, x2, y2, score, class).  out [batch][o.max_det], counts [batch]; *err = 1 when an end-to-end
+// class id exceeds Int32.  tf [batch] on the device.
+size_t detections_workspace_bytes(int batch, int count, int max_det);
+void decode_detections(const float* x, int batch, long img_stride, long a_stride, long f_stride, int count,
+                       int class_fields, bool e2e, const DetectTransform* tf, const DetectOptions& o, DetOut* out,
+                       int* counts, int* err, void* ws, cudaStream_t stream);
+
 // ---------------------------------------------------------------- optimizer
 struct ParamSegment {
     long offset, length;

@@ -148,6 +148,7 @@ Session::Session(const sy_config& c) : cfg(c) {
     }
     // loss, truth, outputs
     const int anchors = levels_[0].h * levels_[0].w + levels_[1].h * levels_[1].w + levels_[2].h * levels_[2].w;
+    anchors_ = anchors;
     loss_ws_ = dalloc(loss_workspace_bytes(B_, anchors, std::max(1, c.max_boxes), 10, c.num_classes));
     d_truth_ = static_cast<TruthBox*>(dalloc(sizeof(TruthBox) * (size_t)B_ * std::max(1, c.max_boxes)));
     d_box_off_ = static_cast<int*>(dalloc(sizeof(int) * (B_ + 1)));
@@ -185,6 +186,8 @@ Session::~Session() {
     clear_graphs();
     if (comm_ && nccl_) nccl_->CommDestroy(comm_);   // an aborted communicator is already gone
     for (void* p : allocations_) cudaFree(p);
+    if (det_ws_) cudaFree(det_ws_);
+    if (det_out_) cudaFree(det_out_);
     for (void* p : {(void*)h_truth_, (void*)h_box_off_, (void*)h_flags_, (void*)h_rec_, (void*)h_images_,
                     (void*)h_abs_, (void*)h_rgb_})
         if (p) cudaFreeHost(p);
@@ -1303,6 +1306,134 @@ int Session::evaluate(const uint8_t* rgb, bool rgb_on_device, const float* const
         out->near_ties = near_ties;
         out->device_ms = ms;
     }
+    return SY_OK;
+}
+
+// ------------------------------------------------------------------ inference
+// DecodeIndexed's option checks (YoloDetector.cs:542); with `detector` also the YoloDetector constructor's
+// (:214: confidence and IoU threshold finite and in [0, 1]).  The static decode takes any threshold, NaN
+// included (no candidate is then below the confidence threshold, and no overlap above the IoU threshold).
+DetectOptions detect_options(const sy_detect_options* o, bool detector) {
+    if (!o) throw SyError(SY_ERR_INVALID_ARGUMENT, "detect options missing");
+    if (detector && (!std::isfinite(o->confidence) || o->confidence < 0.0f || o->confidence > 1.0f))
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "confidence must be between 0 and 1");
+    if (detector && (!std::isfinite(o->iou_threshold) || o->iou_threshold < 0.0f || o->iou_threshold > 1.0f))
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "iou_threshold must be between 0 and 1");
+    if (o->max_detections < 1 || o->max_detections > kMaxDetections)
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "max_detections must be in [1, 65536]");
+    if (o->max_candidates < 1) throw SyError(SY_ERR_INVALID_ARGUMENT, "max_candidates must be positive");
+    return DetectOptions{o->confidence, o->iou_threshold, o->max_detections, o->max_candidates,
+                         o->class_agnostic ? 1 : 0};
+}
+
+DetectTransform detect_transform(const sy_letterbox& t) {
+    if (t.source_width <= 0 || t.source_height <= 0 || t.target_width <= 0 || t.target_height <= 0 ||
+        !std::isfinite(t.scale_x) || !std::isfinite(t.scale_y) || t.scale_x <= 0.0f || t.scale_y <= 0.0f)
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "invalid letterbox transform");
+    return DetectTransform{t.scale_x, t.scale_y, (float)t.pad_x, (float)t.pad_y, (float)t.source_width,
+                           (float)t.source_height};
+}
+
+void Session::ensure_detect(int max_det) {
+    const int nc = cfg.num_classes;
+    if (!det_dec_) {
+        det_dec_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)B_ * (nc + 4) * anchors_));
+        if (cfg.end_to_end)
+            det_e2e_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)B_ * std::min(kModelMaxDet, anchors_) * 6));
+        det_tf_ = static_cast<DetectTransform*>(dalloc(sizeof(DetectTransform) * (size_t)B_));
+        det_counts_ = static_cast<int*>(dalloc(sizeof(int) * (size_t)B_));
+        det_err_ = static_cast<int*>(dalloc(sizeof(int)));
+    }
+    if (max_det <= det_cap_) return;
+    if (det_ws_) cudaFree(det_ws_);
+    if (det_out_) cudaFree(det_out_);
+    det_ws_ = nullptr;
+    det_out_ = nullptr;
+    det_cap_ = 0;
+    const int count = cfg.end_to_end ? std::min(kModelMaxDet, anchors_) : anchors_;
+    size_t ws = detections_workspace_bytes(B_, count, max_det);
+    if (cfg.end_to_end) ws = std::max(ws, end_to_end_workspace_bytes(B_, anchors_, nc, kModelMaxDet));
+    SY_CUDA(cudaMalloc(&det_ws_, ws));
+    SY_CUDA(cudaMalloc(&det_out_, sizeof(DetOut) * (size_t)B_ * max_det));
+    det_cap_ = max_det;
+}
+
+// PtModel.Detect (PtModel.cs:444-503) on this head: the one-to-many branches, or the one-to-one branches of
+// an end-to-end head (decoded as x1, y1, x2, y2 and passed through EndToEndTopK with the model's max_det of
+// 300), then YoloDetector.DecodeIndexed with the channels-first (raw) or end-to-end layout.
+int Session::detect(const uint8_t* rgb, bool rgb_on_device, const float* const* features, int images,
+                    const sy_letterbox* transforms, const sy_detect_options* options, sy_detection* out,
+                    int32_t* counts) {
+    static_assert(sizeof(DetOut) == sizeof(sy_detection), "DetOut mirrors sy_detection");
+    if (!out || !counts) throw SyError(SY_ERR_INVALID_ARGUMENT, "detect: output missing");
+    if (images < 1 || images > B_) throw SyError(SY_ERR_INVALID_ARGUMENT, "images out of range");
+    const DetectOptions o = detect_options(options, true);
+    std::vector<DetectTransform> tf(images);
+    for (int b = 0; b < images; b++) {
+        const int s = cfg.image_size;
+        tf[b] = transforms ? detect_transform(transforms[b]) : detect_transform(sy_letterbox{s, s, s, s, 1.f, 1.f, 0, 0});
+    }
+    SY_CUDA(cudaSetDevice(device_));
+    ensure_detect(o.max_det);
+    const std::vector<int32_t> no_boxes(images, 0);
+    const sy_box unused{};
+    prepare_inputs(rgb, rgb_on_device, features, &unused, no_boxes.data(), images);
+    forward_head(images, false);
+    last_batch_ = images;
+    const int nc = cfg.num_classes, set = n_sets_ - 1;
+    const bool e2e = cfg.end_to_end != 0;
+    DetectLevelSrc lv[3];
+    for (int l = 0; l < 3; l++) {
+        const Grid& g = levels_[l];
+        const View& by = branches_[set * 6 + l].blocks.back().y;
+        const View& cy = branches_[set * 6 + 3 + l].blocks.back().y;
+        const long interior = (long)(g.wp + 1);
+        lv[l] = DetectLevelSrc{by.base + interior * by.pitch, cy.base + interior * cy.pitch,
+                               {(long)g.rows * by.pitch, 1, (long)g.wp * by.pitch, by.pitch},
+                               {(long)g.rows * cy.pitch, 1, (long)g.wp * cy.pitch, cy.pitch}, g.h, g.w,
+                               (float)(8 << l)};
+    }
+    SY_CUDA(cudaMemcpyAsync(det_tf_, tf.data(), sizeof(DetectTransform) * images, cudaMemcpyHostToDevice, stream_));
+    SY_CUDA(cudaMemsetAsync(det_err_, 0, sizeof(int), stream_));
+    head_decode(lv, 3, images, cfg.reg_max, nc, e2e ? 1 : 0, det_dec_, stream_);
+    if (e2e) {
+        const int k = std::min(kModelMaxDet, anchors_);
+        end_to_end_topk(det_dec_, images, nc + 4, anchors_, nc, kModelMaxDet, det_e2e_, det_ws_, stream_);
+        decode_detections(det_e2e_, images, (long)k * 6, 6, 1, k, 0, true, det_tf_, o, det_out_, det_counts_,
+                          det_err_, det_ws_, stream_);
+    } else {
+        decode_detections(det_dec_, images, (long)(nc + 4) * anchors_, 1, anchors_, anchors_, nc + 4, false, det_tf_,
+                          o, det_out_, det_counts_, det_err_, det_ws_, stream_);
+    }
+    SY_CUDA(cudaMemcpyAsync(counts, det_counts_, sizeof(int) * images, cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaMemcpyAsync(out, det_out_, sizeof(DetOut) * (size_t)images * o.max_det, cudaMemcpyDeviceToHost,
+                            stream_));
+    SY_CUDA(cudaMemcpyAsync(h_flags_, det_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    SY_CUDA(cudaEventRecord(ev1_, stream_));
+    SY_CUDA(cudaStreamSynchronize(stream_));
+    if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "detect: class id out of Int32 range");
+    return SY_OK;
+}
+
+int Session::get_last_head_outputs(int set, int level, float* box, long box_count, float* cls, long cls_count) const {
+    if (set < 0 || set >= n_sets_ || level < 0 || level > 2 || !box || !cls)
+        throw SyError(SY_ERR_INVALID_ARGUMENT, "set / level / buffers");
+    const Grid& g = levels_[level];
+    const View& by = branches_[set * 6 + level].blocks.back().y;
+    const View& cy = branches_[set * 6 + 3 + level].blocks.back().y;
+    const long nb = (long)last_batch_ * 4 * cfg.reg_max * g.h * g.w, nk = (long)last_batch_ * cfg.num_classes * g.h * g.w;
+    if (box_count != nb || cls_count != nk) throw SyError(SY_ERR_INVALID_ARGUMENT, "head output size mismatch");
+    float* tmp = nullptr;
+    SY_CUDA(cudaMalloc(&tmp, sizeof(float) * std::max(nb, nk)));
+    padded_to_nchw(by, last_batch_, 4 * cfg.reg_max, g, tmp, stream_);
+    cudaError_t e = cudaMemcpyAsync(box, tmp, sizeof(float) * nb, cudaMemcpyDeviceToHost, stream_);
+    if (e == cudaSuccess) {
+        padded_to_nchw(cy, last_batch_, cfg.num_classes, g, tmp, stream_);
+        e = cudaMemcpyAsync(cls, tmp, sizeof(float) * nk, cudaMemcpyDeviceToHost, stream_);
+    }
+    cudaStreamSynchronize(stream_);
+    cudaFree(tmp);
+    SY_CUDA(e);
     return SY_OK;
 }
 

@@ -92,6 +92,11 @@ public:
     // YoloTrainer.EvaluateLoss: BatchNorm with running statistics, loss without gradients, no update.
     int evaluate(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
                  const int32_t* counts, int images, sy_step_stats* out);
+    // Inference (YoloDetector.Detect on this model, src/SimdYolo/YoloDetector.cs:327-376): frozen trunk, head
+    // with BatchNorm in evaluation mode, decode, confidence filter, greedy NMS (none for end-to-end heads,
+    // which take PtModel.EndToEndTopK instead) and letterbox mapping.  out [images][max_detections].
+    int detect(const uint8_t* rgb, bool rgb_on_device, const float* const* features, int images,
+               const sy_letterbox* transforms, const sy_detect_options* options, sy_detection* out, int32_t* counts);
     int set_epoch(int epoch);
     // AdamW steps taken per optimizer group (class branches, cv2, one2one_cv2)
     int get_optimizer_steps(int32_t steps[3]) const;
@@ -103,6 +108,8 @@ public:
     int set_backbone(const float* host, long count);
     int get_last_gradients(float* host, long count) const;
     int get_last_features(int level, float* host, long count) const;
+    // raw outputs (box and class logits, NCHW) of branch set `set` at `level` from the latest head forward
+    int get_last_head_outputs(int set, int level, float* box, long box_count, float* cls, long cls_count) const;
     // Optional CUDA-event timing of every tensor-core convolution launch (forward, stride-2 and
     // data-gradient passes) on the session stream; returns the totals since the previous call.
     int conv_profile(int enable, double* ms, double* gflop, long* launches);
@@ -256,6 +263,25 @@ private:
     void prof_collect();
     NcclApi* nccl_ = nullptr;
     void* comm_ = nullptr;
+    // inference buffers, allocated by the first detect call (the output and workspace grow with
+    // max_detections): decoded head [B][4 + nc][anchors], end-to-end rows [B][k][6], letterbox records
+    void ensure_detect(int max_det);
+    int anchors_ = 0;
+    float* det_dec_ = nullptr;
+    float* det_e2e_ = nullptr;
+    DetectTransform* det_tf_ = nullptr;
+    int* det_counts_ = nullptr;
+    int* det_err_ = nullptr;
+    void* det_ws_ = nullptr;
+    DetOut* det_out_ = nullptr;
+    int det_cap_ = 0;
 };
+
+constexpr int kMaxDetections = 65536;   // max_detections accepted by detect / decode_detections
+constexpr int kModelMaxDet = 300;        // max_det of an end-to-end head (PtModel.Detect's default)
+
+// Validated conversions of the public inference records (YoloDetector option and Letterbox checks).
+DetectOptions detect_options(const sy_detect_options* o, bool detector);
+DetectTransform detect_transform(const sy_letterbox& t);
 
 }  // namespace sy
