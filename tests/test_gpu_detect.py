@@ -214,7 +214,13 @@ def session_with_state(cfg, seed):
     s = sy.Session(cfg)
     rng = np.random.default_rng(seed)
     params, buffers = data.head_params(s, seed, cfg.image_size)
-    params = params + (rng.standard_normal(params.size) * 0.05).astype(np.float32)   # spread the class scores
+    params = params + (rng.standard_normal(params.size) * 0.05).astype(np.float32)
+    off = 0
+    for t in s.tensors:   # class biases around sigmoid(-2.5), so that a few hundred anchors pass 0.01
+        if t["kind"] == 0:
+            if t["name"].endswith(".bias") and not t["name"].endswith("bn.bias") and "cv3" in t["name"].split(".")[0]:
+                params[off:off + t["numel"]] = rng.normal(-2.5, 1.5, t["numel"])
+            off += t["numel"]
     off = 0
     for t in s.tensors:
         if t["kind"] == 1:
