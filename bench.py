@@ -68,6 +68,7 @@ def parse():
     p.add_argument("--model", default=None)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-3x", action="store_true", help="skip the 3xTF32 (FP32 parity) timing loop")
+    p.add_argument("--no-detect", action="store_true", help="skip the inference (sy_cuda_detect) timing loop")
     p.add_argument("--precision", default="tf32", choices=["tf32", "3xtf32"],
                    help="3xtf32: the FP32 parity mode (three split-operand TF32 passes per convolution)")
     p.add_argument("--conv-sweep", action="store_true",
@@ -451,6 +452,48 @@ def run_ours(args, rank, world, local_rank, dist):
               "ms_per_step": ms3 / steps3,
               "how": "same workload and inputs, every convolution as three split-operand TF32 passes (FP32 parity)"}
 
+    # inference (sy_cuda_detect, the detector behind DetectionEvaluator.Evaluate): trunk, head with running
+    # statistics, decode, confidence filter and NMS, pinned host images in, detections out.  The random-init
+    # class biases (-11.5 at stride 8 to -8.8 at stride 32) leave almost no anchor above the evaluator's
+    # confidence of 0.001, so they are set to -6.5 first: thousands of candidates per image reach the NMS.
+    det = None
+    if not args.no_detect:
+        off = 0
+        flat = sess.flat_params()
+        for t in sess.tensors:
+            if t["kind"] == 0:
+                name = t["name"]
+                if name.endswith(".bias") and not name.endswith("bn.bias") and "cv3" in name.split(".")[0]:
+                    flat[off:off + t["numel"]] = -6.5
+                off += t["numel"]
+        sess.set_flat_params(flat)
+        o = sy.evaluation_options()
+        for i in range(2):
+            sess.detect(pinned[i % nbatches].numpy(), o)
+        barrier()
+        dsteps = max(3, min(args.steps, 20))
+        det_ms = post_ms = 0.0
+        ndet = 0
+        wall0 = time.perf_counter()
+        for i in range(dsteps):
+            found = sess.detect(pinned[i % nbatches].numpy(), o)
+            det_ms += sess.last_detect_ms[0]
+            post_ms += sess.last_detect_ms[1]
+            ndet += sum(len(f) for f in found)
+        barrier()
+        det_wall = max_over_ranks(time.perf_counter() - wall0)
+        det_ms = max_over_ranks(det_ms)
+        det = {"value": world * args.batch * dsteps / (det_ms / 1000.0), "unit": "images/s",
+               "wall_value": world * args.batch * dsteps / det_wall, "steps": dsteps,
+               "ms_per_batch": det_ms / dsteps, "postprocess_ms_per_batch": post_ms / dsteps,
+               "detections_per_image": ndet / (dsteps * args.batch),
+               "h2d_bytes_per_step": args.batch * args.image * args.image * 3,
+               "d2h_bytes_per_step": args.batch * (o.max_detections * 24 + 4),
+               "options": {"confidence": 0.001, "iou": 0.7, "max_detections": 300},
+               "how": "sy_cuda_detect with pinned host images: H2D copy, trunk, head (evaluation BatchNorm), decode, "
+                      "candidates + greedy NMS, letterbox mapping, detections D2H; value from CUDA events inside "
+                      "each call, postprocess = decode + NMS kernels, wall_value from the host clock"}
+
     line = None
     if rank == 0:
         peaks, src = measured_peaks()
@@ -490,6 +533,8 @@ def run_ours(args, rank, world, local_rank, dist):
                 "e2e": e2e, "gpu_launches": launches, "wall_s_timed": wall, "roofline": roof}
         if x3 is not None:
             line["3xtf32"] = x3
+        if det is not None:
+            line["detect"] = det
         line["roofline"]["layers"] = layer_classes(per_launch, args.batch, peaks["hbm_gbs"], tf32_sustained)
         if world == 1:
             line["cpu_baseline"] = cpu_baseline(args, cpu_threads())

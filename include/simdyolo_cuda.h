@@ -225,15 +225,17 @@ SY_API sy_status sy_cuda_get_last_head_outputs(const sy_session *session, int32_
  * max_candidates, greedy NMS (class-aware unless class_agnostic), max_detections, and the mapping through
  * transforms[b] (NULL: identity, source S x S).  End-to-end heads use their one-to-one branches and
  * PtModel.EndToEndTopK (PtModel.cs:530-568, max_det 300) instead of NMS.  out holds
- * images * max_detections records, image b's counts[b] detections first in its block.  Nothing in the
- * session's parameters, buffers or optimizer state changes. */
+ * images * max_detections records, image b's counts[b] detections first in its block.  timing (optional,
+ * no counterpart in the reference) receives [0] the call's device ms (upload to detections read back) and
+ * [1] the device ms of the post-processing kernels.  Nothing in the session's parameters, buffers or
+ * optimizer state changes. */
 SY_API sy_status sy_cuda_detect(sy_session *session, const uint8_t *rgb, int32_t images,
                                 const sy_letterbox *transforms, const sy_detect_options *options, sy_detection *out,
-                                int32_t *counts);
+                                int32_t *counts, double *timing);
 /* The same from cached frozen features (NCHW per level, as for sy_cuda_step_features). */
 SY_API sy_status sy_cuda_detect_features(sy_session *session, const float *const features[3], int32_t images,
                                          const sy_letterbox *transforms, const sy_detect_options *options,
-                                         sy_detection *out, int32_t *counts);
+                                         sy_detection *out, int32_t *counts, double *timing);
 
 /* ---- standalone operators (same algorithms as the session, host buffers) ---- */
 

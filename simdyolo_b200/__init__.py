@@ -192,8 +192,9 @@ def lib():
         L.sy_cuda_conv_profile_launches.argtypes = [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), ip, st,
                                                     C.POINTER(C.c_int32)]
         dp, lp, op = C.POINTER(Detection), C.POINTER(Letterbox), C.POINTER(DetectOptions)
-        L.sy_cuda_detect.argtypes = [vp, C.POINTER(C.c_uint8), C.c_int32, lp, op, dp, ip]
-        L.sy_cuda_detect_features.argtypes = [vp, C.POINTER(fp), C.c_int32, lp, op, dp, ip]
+        dbl = C.POINTER(C.c_double)
+        L.sy_cuda_detect.argtypes = [vp, C.POINTER(C.c_uint8), C.c_int32, lp, op, dp, ip, dbl]
+        L.sy_cuda_detect_features.argtypes = [vp, C.POINTER(fp), C.c_int32, lp, op, dp, ip, dbl]
         L.sy_cuda_get_last_head_outputs.argtypes = [vp, C.c_int32, C.c_int32, fp, C.c_int64, fp, C.c_int64]
         L.sy_cuda_head_decode.argtypes = [C.c_int32, C.c_int32, C.c_int32, ip, ip, fp, C.c_int32, C.c_int32,
                                           C.c_int32, C.POINTER(fp), C.POINTER(fp), fp]
@@ -636,7 +637,9 @@ class Session:
             tf = (Letterbox * images)(*transforms)
         out = (Detection * (images * o.max_detections))()
         counts = np.zeros(images, np.int32)
-        _check(fn(self._h, source, images, tf, C.byref(o), out, _ip(counts)), self._h)
+        timing = (C.c_double * 2)()
+        _check(fn(self._h, source, images, tf, C.byref(o), out, _ip(counts), timing), self._h)
+        self.last_detect_ms = (timing[0], timing[1])
         return _detections(out, counts, o.max_detections)
 
     def detect(self, images: np.ndarray, options: DetectOptions = None, transforms=None):

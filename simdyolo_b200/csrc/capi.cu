@@ -213,19 +213,19 @@ sy_status sy_cuda_eval_loss_features(sy_session* session, const float* const fea
 }
 
 sy_status sy_cuda_detect(sy_session* session, const uint8_t* rgb, int32_t images, const sy_letterbox* transforms,
-                         const sy_detect_options* options, sy_detection* out, int32_t* counts) {
+                         const sy_detect_options* options, sy_detection* out, int32_t* counts, double* timing) {
     if (!session || !rgb) return SY_ERR_INVALID_ARGUMENT;
     return guarded(session, [&] {
-        return session->impl->detect(rgb, false, nullptr, images, transforms, options, out, counts);
+        return session->impl->detect(rgb, false, nullptr, images, transforms, options, out, counts, timing);
     });
 }
 
 sy_status sy_cuda_detect_features(sy_session* session, const float* const features[3], int32_t images,
                                   const sy_letterbox* transforms, const sy_detect_options* options, sy_detection* out,
-                                  int32_t* counts) {
+                                  int32_t* counts, double* timing) {
     if (!session || !features) return SY_ERR_INVALID_ARGUMENT;
     return guarded(session, [&] {
-        return session->impl->detect(nullptr, false, features, images, transforms, options, out, counts);
+        return session->impl->detect(nullptr, false, features, images, transforms, options, out, counts, timing);
     });
 }
 

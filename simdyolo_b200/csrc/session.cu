@@ -125,6 +125,7 @@ Session::Session(const sy_config& c) : cfg(c) {
     SY_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     SY_CUDA(cudaEventCreate(&ev0_));
     SY_CUDA(cudaEventCreate(&ev1_));
+    SY_CUDA(cudaEventCreate(&ev_post_));
     B_ = c.max_batch;
     for (int l = 0; l < 3; l++) levels_[l] = make_grid(c.image_size >> (3 + l), c.image_size >> (3 + l));
     if (c.backbone == SY_BACKBONE_YOLOV8 || c.backbone == SY_BACKBONE_YOLO11) {
@@ -193,6 +194,7 @@ Session::~Session() {
         if (p) cudaFreeHost(p);
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
+    if (ev_post_) cudaEventDestroy(ev_post_);
     for (cudaEvent_t e : prof_ev_) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
 }
@@ -1363,7 +1365,7 @@ void Session::ensure_detect(int max_det) {
 // 300), then YoloDetector.DecodeIndexed with the channels-first (raw) or end-to-end layout.
 int Session::detect(const uint8_t* rgb, bool rgb_on_device, const float* const* features, int images,
                     const sy_letterbox* transforms, const sy_detect_options* options, sy_detection* out,
-                    int32_t* counts) {
+                    int32_t* counts, double* timing) {
     static_assert(sizeof(DetOut) == sizeof(sy_detection), "DetOut mirrors sy_detection");
     if (!out || !counts) throw SyError(SY_ERR_INVALID_ARGUMENT, "detect: output missing");
     if (images < 1 || images > B_) throw SyError(SY_ERR_INVALID_ARGUMENT, "images out of range");
@@ -1395,6 +1397,7 @@ int Session::detect(const uint8_t* rgb, bool rgb_on_device, const float* const* 
     }
     SY_CUDA(cudaMemcpyAsync(det_tf_, tf.data(), sizeof(DetectTransform) * images, cudaMemcpyHostToDevice, stream_));
     SY_CUDA(cudaMemsetAsync(det_err_, 0, sizeof(int), stream_));
+    SY_CUDA(cudaEventRecord(ev_post_, stream_));
     head_decode(lv, 3, images, cfg.reg_max, nc, e2e ? 1 : 0, det_dec_, stream_);
     if (e2e) {
         const int k = std::min(kModelMaxDet, anchors_);
@@ -1412,6 +1415,13 @@ int Session::detect(const uint8_t* rgb, bool rgb_on_device, const float* const* 
     SY_CUDA(cudaEventRecord(ev1_, stream_));
     SY_CUDA(cudaStreamSynchronize(stream_));
     if (h_flags_[0]) throw SyError(SY_ERR_DEVICE, "detect: class id out of Int32 range");
+    if (timing) {
+        float all = 0.0f, post = 0.0f;
+        cudaEventElapsedTime(&all, ev0_, ev1_);
+        cudaEventElapsedTime(&post, ev_post_, ev1_);
+        timing[0] = all;
+        timing[1] = post;
+    }
     return SY_OK;
 }
 

@@ -95,8 +95,11 @@ public:
     // Inference (YoloDetector.Detect on this model, src/SimdYolo/YoloDetector.cs:327-376): frozen trunk, head
     // with BatchNorm in evaluation mode, decode, confidence filter, greedy NMS (none for end-to-end heads,
     // which take PtModel.EndToEndTopK instead) and letterbox mapping.  out [images][max_detections].
+    // timing (optional): [0] device ms of the call (inputs up to the detections read back), [1] device ms of
+    // the post-processing kernels (decode, top-k, candidates and NMS).
     int detect(const uint8_t* rgb, bool rgb_on_device, const float* const* features, int images,
-               const sy_letterbox* transforms, const sy_detect_options* options, sy_detection* out, int32_t* counts);
+               const sy_letterbox* transforms, const sy_detect_options* options, sy_detection* out, int32_t* counts,
+               double* timing = nullptr);
     int set_epoch(int epoch);
     // AdamW steps taken per optimizer group (class branches, cv2, one2one_cv2)
     int get_optimizer_steps(int32_t steps[3]) const;
@@ -271,6 +274,7 @@ private:
     float* det_e2e_ = nullptr;
     DetectTransform* det_tf_ = nullptr;
     int* det_counts_ = nullptr;
+    cudaEvent_t ev_post_ = nullptr;     // start of the post-processing kernels
     int* det_err_ = nullptr;
     void* det_ws_ = nullptr;
     DetOut* det_out_ = nullptr;
