@@ -117,9 +117,14 @@ def evaluation_options() -> DetectOptions:
     return detect_options(0.001, 0.7, 300)
 
 
+_DETECTION_DTYPE = np.dtype([("class_id", "<i4"), ("confidence", "<f4"), ("x", "<f4"), ("y", "<f4"),
+                             ("width", "<f4"), ("height", "<f4")])
+
+
 def _detections(out, counts, max_det):
-    return [[(d.class_id, d.confidence, d.x, d.y, d.width, d.height) for d in out[b * max_det:b * max_det + int(n)]]
-            for b, n in enumerate(counts)]
+    """Per image a list of (class_id, confidence, x, y, width, height) from the [images][max_det] records."""
+    arr = np.frombuffer(out, _DETECTION_DTYPE).reshape(len(counts), max_det)
+    return [arr[b, :int(n)].tolist() for b, n in enumerate(counts)]
 
 
 class TensorInfo(C.Structure):

@@ -325,6 +325,13 @@ void end_to_end_topk(const float* x, int batch, int fields, int anchors, int nc,
 // fields x1, y1, x2, y2, score, class).  out [batch][o.max_det], counts [batch]; *err = 1 when an end-to-end
 // class id exceeds Int32.  tf [batch] on the device.
 size_t detections_workspace_bytes(int batch, int count, int max_det);
+// The same candidates and NMS straight from raw head outputs in channels-last rows (levels[l].box / .cls with
+// channel stride 1, 16-byte aligned rows of box_pitch / cls_pitch floats): CpuHead.DecodeInto's scores and
+// boxes fused with DecodeIndexed (raw, non-end-to-end heads); workspace detections_workspace_bytes(batch,
+// anchors, o.max_det).
+void detect_raw(const DetectLevelSrc* levels, int nlevels, int batch, int bins, int nc, int cls_pitch, int box_pitch,
+                const DetectTransform* tf, const DetectOptions& o, DetOut* out, int* counts, void* ws,
+                cudaStream_t stream);
 void decode_detections(const float* x, int batch, long img_stride, long a_stride, long f_stride, int count,
                        int class_fields, bool e2e, const DetectTransform* tf, const DetectOptions& o, DetOut* out,
                        int* counts, int* err, void* ws, cudaStream_t stream);

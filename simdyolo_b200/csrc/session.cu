@@ -1338,10 +1338,11 @@ DetectTransform detect_transform(const sy_letterbox& t) {
 
 void Session::ensure_detect(int max_det) {
     const int nc = cfg.num_classes;
-    if (!det_dec_) {
-        det_dec_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)B_ * (nc + 4) * anchors_));
-        if (cfg.end_to_end)
+    if (!det_tf_) {
+        if (cfg.end_to_end) {
+            det_dec_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)B_ * (nc + 4) * anchors_));
             det_e2e_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)B_ * std::min(kModelMaxDet, anchors_) * 6));
+        }
         det_tf_ = static_cast<DetectTransform*>(dalloc(sizeof(DetectTransform) * (size_t)B_));
         det_counts_ = static_cast<int*>(dalloc(sizeof(int) * (size_t)B_));
         det_err_ = static_cast<int*>(dalloc(sizeof(int)));
@@ -1398,15 +1399,16 @@ int Session::detect(const uint8_t* rgb, bool rgb_on_device, const float* const* 
     SY_CUDA(cudaMemcpyAsync(det_tf_, tf.data(), sizeof(DetectTransform) * images, cudaMemcpyHostToDevice, stream_));
     SY_CUDA(cudaMemsetAsync(det_err_, 0, sizeof(int), stream_));
     SY_CUDA(cudaEventRecord(ev_post_, stream_));
-    head_decode(lv, 3, images, cfg.reg_max, nc, e2e ? 1 : 0, det_dec_, stream_);
     if (e2e) {
         const int k = std::min(kModelMaxDet, anchors_);
+        head_decode(lv, 3, images, cfg.reg_max, nc, 1, det_dec_, stream_);
         end_to_end_topk(det_dec_, images, nc + 4, anchors_, nc, kModelMaxDet, det_e2e_, det_ws_, stream_);
         decode_detections(det_e2e_, images, (long)k * 6, 6, 1, k, 0, true, det_tf_, o, det_out_, det_counts_,
                           det_err_, det_ws_, stream_);
     } else {
-        decode_detections(det_dec_, images, (long)(nc + 4) * anchors_, 1, anchors_, anchors_, nc + 4, false, det_tf_,
-                          o, det_out_, det_counts_, det_err_, det_ws_, stream_);
+        // decode fused into the candidate filter: no decoded [image][4 + nc][anchors] tensor
+        detect_raw(lv, 3, images, cfg.reg_max, nc, branches_[set * 6 + 3].blocks.back().y.pitch,
+                   branches_[set * 6].blocks.back().y.pitch, det_tf_, o, det_out_, det_counts_, det_ws_, stream_);
     }
     SY_CUDA(cudaMemcpyAsync(counts, det_counts_, sizeof(int) * images, cudaMemcpyDeviceToHost, stream_));
     SY_CUDA(cudaMemcpyAsync(out, det_out_, sizeof(DetOut) * (size_t)images * o.max_det, cudaMemcpyDeviceToHost,

@@ -267,7 +267,8 @@ private:
     NcclApi* nccl_ = nullptr;
     void* comm_ = nullptr;
     // inference buffers, allocated by the first detect call (the output and workspace grow with
-    // max_detections): decoded head [B][4 + nc][anchors], end-to-end rows [B][k][6], letterbox records
+    // max_detections): for end-to-end heads the decoded head [B][4 + nc][anchors] and the rows [B][k][6]
+    // (raw heads decode inside the candidate kernel); letterbox records
     void ensure_detect(int max_det);
     int anchors_ = 0;
     float* det_dec_ = nullptr;

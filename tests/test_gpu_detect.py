@@ -141,6 +141,19 @@ def test_decode_raw_head_outputs(case):
         assert len(got[b]) == len(want) and np.array_equal(as_array(got[b]), as_array(want)), b
 
 
+@pytest.mark.parametrize("max_candidates", [30000, 20000])
+def test_decode_more_candidates_than_shared_memory_sorts(max_candidates):
+    """33,600 anchors (a 1280 x 1280 input) all above the threshold: the kernel's second path (radix-select
+    MaxCandidates, then repeated maxima) instead of the shared-memory sort, which holds 16,384 keys."""
+    rng = np.random.default_rng(max_candidates)
+    out = np.stack([D.random_raw_output(rng, 33600, 3, image=1280.0) for _ in range(2)])
+    o = sy.detect_options(0.0, 0.6, 300, max_candidates)
+    got = sy.decode_detections(out, sy.SY_LAYOUT_CHANNELS_FIRST, 3, None, o)
+    lb = (1 << 20, 1 << 20, 1 << 20, 1 << 20, 1., 1., 0, 0)
+    for b in range(2):
+        assert np.array_equal(as_array(got[b]), as_array(oracle_decode(out[b], 1, 3, lb, o))), b
+
+
 def test_decode_end_to_end_rows():
     rng = np.random.default_rng(7)
     rows = rng.uniform(0, 600, (2, 300, 6)).astype(np.float32)
