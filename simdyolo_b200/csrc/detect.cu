@@ -327,6 +327,35 @@ struct RawCandParams {
     CandArrays c;
 };
 
+// Copies rows[an][0, 4 q) (an < n) to stage[an * stride + ...] with float4 loads, eight in flight per thread
+// before their stores.
+__device__ __forceinline__ void stage_rows(const float* const* rows, int n, int q, int stride, float* stage) {
+    const int total = n * q;
+    for (int base = threadIdx.x; base < total; base += 8 * kRawAnchors) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int idx = base + u * kRawAnchors;
+            if (idx < total) {
+                const int an = idx / q, k = idx - an * q;
+                v[u] = __ldg(reinterpret_cast<const float4*>(rows[an]) + k);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int idx = base + u * kRawAnchors;
+            if (idx < total) {
+                const int an = idx / q, k = idx - an * q;
+                float* d = stage + an * stride + 4 * k;
+                d[0] = v[u].x;
+                d[1] = v[u].y;
+                d[2] = v[u].z;
+                d[3] = v[u].w;
+            }
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kRawAnchors) raw_candidates_kernel(const __grid_constant__ RawCandParams p) {
     extern __shared__ float stage[];
     __shared__ const float* row_c[kRawAnchors];
@@ -346,15 +375,7 @@ __global__ void __launch_bounds__(kRawAnchors) raw_candidates_kernel(const __gri
     __syncthreads();
     // class rows
     const int qc = p.cls_pitch >> 2, cs = p.cls_pitch + 1;
-    for (int idx = t; idx < n * qc; idx += kRawAnchors) {
-        const int an = idx / qc, q = idx - an * qc;
-        const float4 v = *reinterpret_cast<const float4*>(row_c[an] + 4 * q);
-        float* d = stage + an * cs + 4 * q;
-        d[0] = v.x;
-        d[1] = v.y;
-        d[2] = v.z;
-        d[3] = v.w;
-    }
+    stage_rows(row_c, n, qc, cs, stage);
     __syncthreads();
     // Strict maximum of the sigmoid scores in class order (first class on ties, NaN never wins).  The
     // sigmoid is monotone (each step of 1 / (1 + exp(-x)) rounds monotonically), so a logit at or below the
@@ -379,15 +400,7 @@ __global__ void __launch_bounds__(kRawAnchors) raw_candidates_kernel(const __gri
     __syncthreads();
     // box rows (only those of passing anchors are needed, all are staged: the loads are coalesced)
     const int qb = p.box_pitch >> 2, bs = p.box_pitch + 1;
-    for (int idx = t; idx < n * qb; idx += kRawAnchors) {
-        const int an = idx / qb, q = idx - an * qb;
-        const float4 v = *reinterpret_cast<const float4*>(row_b[an] + 4 * q);
-        float* d = stage + an * bs + 4 * q;
-        d[0] = v.x;
-        d[1] = v.y;
-        d[2] = v.z;
-        d[3] = v.w;
-    }
+    stage_rows(row_b, n, qb, bs, stage);
     __syncthreads();
     if (a >= p.c.count) return;
     const size_t i = (size_t)b * p.c.count + a;
