@@ -69,6 +69,11 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-3x", action="store_true", help="skip the 3xTF32 (FP32 parity) timing loop")
     p.add_argument("--no-detect", action="store_true", help="skip the inference (sy_cuda_detect) timing loop")
+    p.add_argument("--ncu-steps", type=int, default=0,
+                   help="profiler workload: run this many training steps of the workload and exit (no timing, no line)")
+    p.add_argument("--conv-pass", type=int, nargs=6, metavar=("KIND", "N", "IC", "OC", "HW", "K"),
+                   help="profiler workload: one warm-up and one launch of a conv pass (kind 0 forward, 1 data "
+                        "gradient, 2 weight gradient), then exit")
     p.add_argument("--precision", default="tf32", choices=["tf32", "3xtf32"],
                    help="3xtf32: the FP32 parity mode (three split-operand TF32 passes per convolution)")
     p.add_argument("--conv-sweep", action="store_true",
@@ -544,6 +549,29 @@ def run_ours(args, rank, world, local_rank, dist):
     return line
 
 
+def run_profile_steps(args):
+    """The step workload for profiler captures: `--ncu-steps` training steps on device-resident images."""
+    import torch
+    import simdyolo_b200 as sy
+    from simdyolo_b200 import data
+    cfg = sy.make_config(args.model, image_size=args.image, max_batch=args.batch, max_boxes=args.max_boxes,
+                         num_classes=args.nc, lr=args.lr, weight_decay=args.weight_decay,
+                         optimizer=sy.SY_OPT_ADAMW if args.optimizer == "adamw" else sy.SY_OPT_SGD,
+                         precision=sy.SY_PRECISION_3XTF32 if args.precision == "3xtf32" else sy.SY_PRECISION_TF32)
+    sess = sy.Session(cfg)
+    params, buffers = data.head_params(sess, seed=0)
+    sess.set_flat_params(params)
+    sess.set_flat_buffers(buffers)
+    sess.set_backbone(data.backbone_params(args.model, seed=0))
+    rng = np.random.default_rng(1000)
+    images, truth = data.synthetic_batch(rng, args.batch, args.image, args.nc, args.boxes, args.wh)
+    dev = torch.from_numpy(images).to("cuda:0")
+    for _ in range(args.ncu_steps):
+        sess.step_device(dev.data_ptr(), args.batch, truth)
+    torch.cuda.synchronize()
+    sess.close()
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -552,6 +580,15 @@ def main():
     if args.conv_sweep:
         if rank == 0:
             run_conv_sweep(args)
+        return
+    if args.conv_pass:
+        import simdyolo_b200 as sy
+        kind, n, ic, oc, hw, k = args.conv_pass
+        ms = sy.bench_conv(kind, n, ic, oc, hw, hw, k, iters=1)
+        print(json.dumps({"conv_pass": args.conv_pass, "ms_per_launch": ms}), flush=True)
+        return
+    if args.ncu_steps:
+        run_profile_steps(args)
         return
     if args.impl == "reference":
         # the reference is a single-process CPU trainer: rank 0 runs it, other ranks exit at once
