@@ -191,6 +191,16 @@ SY_API sy_status sy_cuda_step_features(sy_session *session, const float *const f
  * images * S * S * 3 bytes, caller-owned). */
 SY_API sy_status sy_cuda_step_device(sy_session *session, const uint8_t *rgb_device, const sy_box *boxes,
                                      const int32_t *counts, int32_t images, sy_step_stats *out);
+/* Queues a batch of `images` RGB24 images (images * S * S * 3 bytes of host memory) for copying to the
+ * session's GPU and returns at once.  The copy runs on a separate copy stream, started by the next call that
+ * takes inputs (sy_cuda_step, sy_cuda_eval_loss, sy_cuda_detect and their variants) right after that call's
+ * own small uploads, so a host loop that prefetches batch k + 1 before it steps batch k overlaps the copy
+ * with batch k's device work; the call given the same rgb pointer and image count then uses the copy instead
+ * of copying the images itself.  The two most recent prefetches are held; the memory must not change until
+ * the call that uses it has returned.  Page-locked memory is copied directly, pageable memory is first copied
+ * into a page-locked staging buffer of the session (inside this call).  No counterpart in the reference (its
+ * trainer reads images on the host). */
+SY_API sy_status sy_cuda_prefetch_images(sy_session *session, const uint8_t *rgb, int32_t images);
 /* YoloTrainer.EvaluateLoss (YoloTrainer.cs:237-246): the head with BatchNorm in evaluation mode
  * (running mean / variance), the loss without gradients; no parameter, buffer or optimizer state
  * changes.  out->box / cls / dfl / positives are sums over the images of every rank (the reference

@@ -188,6 +188,7 @@ def lib():
                                                             C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
                                                             C.c_void_p]
         L.sy_cuda_step_device.argtypes = [vp, C.c_void_p, C.POINTER(Box), ip, C.c_int32, C.POINTER(StepStats)]
+        L.sy_cuda_prefetch_images.argtypes = [vp, C.POINTER(C.c_uint8), C.c_int32]
         L.sy_cuda_launch_count.argtypes = []
         L.sy_cuda_launch_count.restype = C.c_int64
         L.sy_cuda_bench_conv.argtypes = [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
@@ -223,7 +224,7 @@ EXPORTED = ["sy_cuda_nccl_unique_id", "sy_cuda_create", "sy_cuda_destroy", "sy_c
             "sy_cuda_conv_profile_launches", "sy_cuda_get_optimizer_steps", "sy_cuda_set_optimizer_steps",
             "sy_cuda_wait_limit_selftest", "sy_cuda_detect", "sy_cuda_detect_features",
             "sy_cuda_get_last_head_outputs", "sy_cuda_head_decode", "sy_cuda_end_to_end_topk",
-            "sy_cuda_decode_detections"]
+            "sy_cuda_decode_detections", "sy_cuda_prefetch_images"]
 
 
 def _check(status: int, session=None):
@@ -539,6 +540,16 @@ class Session:
             arr[i] = Box(int(c), float(x1), float(y1), float(x2), float(y2))
         return arr, counts
 
+    def prefetch_images(self, images: np.ndarray):
+        """Starts the host-to-device copy of uint8 [B, S, S, 3] images (sy_cuda_prefetch_images); a later
+        step / eval_loss / detect given this same array uses the copy.  The array must stay unchanged (and
+        alive: the session keeps a reference to the two most recent ones) until then."""
+        if images.dtype != np.uint8 or not images.flags["C_CONTIGUOUS"]:
+            raise ValueError("prefetch_images wants a C-contiguous uint8 array (the pointer identifies the batch)")
+        _check(lib().sy_cuda_prefetch_images(self._h, images.ctypes.data_as(C.POINTER(C.c_uint8)), images.shape[0]),
+               self._h)
+        self._prefetched = ([images] + getattr(self, "_prefetched", []))[:2]
+
     def step(self, images: np.ndarray, boxes_per_image) -> StepStats:
         """images: uint8 [B, S, S, 3] RGB (letterboxed); boxes_per_image: list of (cls, x1, y1, x2, y2)."""
         img = np.ascontiguousarray(images, np.uint8)
@@ -635,29 +646,33 @@ class Session:
                self._h)
         return box, cls
 
-    def _detect(self, fn, source, images, options, transforms):
+    def _detect(self, fn, source, images, options, transforms, as_array):
         o = options if options is not None else detect_options()
         tf = None
         if transforms is not None:
             tf = (Letterbox * images)(*transforms)
-        out = (Detection * (images * o.max_detections))()
+        out = np.zeros((images, o.max_detections), _DETECTION_DTYPE)
         counts = np.zeros(images, np.int32)
         timing = (C.c_double * 2)()
-        _check(fn(self._h, source, images, tf, C.byref(o), out, _ip(counts), timing), self._h)
+        _check(fn(self._h, source, images, tf, C.byref(o), out.ctypes.data_as(C.POINTER(Detection)), _ip(counts),
+                  timing), self._h)
         self.last_detect_ms = (timing[0], timing[1])
-        return _detections(out, counts, o.max_detections)
+        if as_array:
+            return out, counts
+        return [out[b, :int(n)].tolist() for b, n in enumerate(counts)]
 
-    def detect(self, images: np.ndarray, options: DetectOptions = None, transforms=None):
+    def detect(self, images: np.ndarray, options: DetectOptions = None, transforms=None, as_array: bool = False):
         """YoloDetector.Detect on letterboxed uint8 [B, S, S, 3] images: per image a list of
-        (class_id, confidence, x, y, width, height) in source pixels (transforms: one Letterbox per image)."""
+        (class_id, confidence, x, y, width, height) in source pixels (transforms: one Letterbox per image);
+        with as_array, the [B, max_detections] records and the per-image counts as numpy arrays."""
         img = np.ascontiguousarray(images, np.uint8)
         return self._detect(lib().sy_cuda_detect, img.ctypes.data_as(C.POINTER(C.c_uint8)), img.shape[0], options,
-                            transforms)
+                            transforms, as_array)
 
-    def detect_features(self, features, options: DetectOptions = None, transforms=None):
+    def detect_features(self, features, options: DetectOptions = None, transforms=None, as_array: bool = False):
         feats = [np.ascontiguousarray(f, np.float32) for f in features]
         ptrs = (C.POINTER(C.c_float) * 3)(*[_fp(f) for f in feats])
-        return self._detect(lib().sy_cuda_detect_features, ptrs, feats[0].shape[0], options, transforms)
+        return self._detect(lib().sy_cuda_detect_features, ptrs, feats[0].shape[0], options, transforms, as_array)
 
 
 def wait_limit_selftest(spins: int, device: int = 0) -> int:

@@ -229,6 +229,11 @@ sy_status sy_cuda_detect_features(sy_session* session, const float* const featur
     });
 }
 
+sy_status sy_cuda_prefetch_images(sy_session* session, const uint8_t* rgb, int32_t images) {
+    if (!session || !rgb) return SY_ERR_INVALID_ARGUMENT;
+    return guarded(session, [&] { return session->impl->prefetch_images(rgb, images); });
+}
+
 int64_t sy_cuda_launch_count(void) { return sy::launch_count(); }
 
 sy_status sy_cuda_conv_profile(sy_session* session, int32_t enable, double* ms, double* gflop, int64_t* launches) {

@@ -195,6 +195,13 @@ Session::~Session() {
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
     if (ev_post_) cudaEventDestroy(ev_post_);
+    for (ImageSlot& sl : slots_) {
+        if (sl.dev) cudaFree(sl.dev);
+        if (sl.pinned) cudaFreeHost(sl.pinned);
+        if (sl.copied) cudaEventDestroy(sl.copied);
+        if (sl.released) cudaEventDestroy(sl.released);
+    }
+    if (copy_stream_) cudaStreamDestroy(copy_stream_);
     for (cudaEvent_t e : prof_ev_) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
 }
@@ -1023,8 +1030,19 @@ void Session::prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float
     if (rgb) {
         const size_t bytes = (size_t)images * cfg.image_size * cfg.image_size * 3;
         const uint8_t* src = d_rgb_;
+        ImageSlot* slot = nullptr;
+        if (!rgb_on_device)
+            for (ImageSlot& sl : slots_)
+                if (sl.ready && sl.host == rgb && sl.images == images) slot = &sl;
         if (rgb_on_device) {
             src = rgb;
+        } else if (slot) {
+            // prefetched: the compute stream waits for the copy stream's copy of this batch
+            issue_prefetch(*slot);
+            SY_CUDA(cudaStreamWaitEvent(stream_, slot->copied, 0));
+            slot->ready = false;
+            consuming_ = slot;
+            src = slot->dev;
         } else {
             // pinned caller memory is copied directly; pageable memory goes through pinned staging
             cudaPointerAttributes attr;
@@ -1037,6 +1055,9 @@ void Session::prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float
             SY_CUDA(cudaMemcpyAsync(d_rgb_, rgb, bytes, cudaMemcpyHostToDevice, stream_));
         }
         rgb_src_ = src;
+        // the copies of batches prefetched for later calls start now, behind this call's uploads
+        for (ImageSlot& sl : slots_)
+            if (sl.pending) issue_prefetch(sl);
         if (!defer_backbone) forward_backbone(images, src);
     } else {
         rgb_src_ = nullptr;
@@ -1090,6 +1111,7 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
         else
             device_work();
     }
+    release_images();
     // Data-parallel exchange, all enqueued before one host wait: the gradient bucket summed over ranks
     // (so the finiteness check, the checksum and the kept copy all see the global gradient), then one
     // all-gather of every rank's exchange record (loss parts, positives, connections, image count and the
@@ -1267,6 +1289,7 @@ int Session::evaluate(const uint8_t* rgb, bool rgb_on_device, const float* const
                       const int32_t* counts, int images, sy_step_stats* out) {
     prepare_inputs(rgb, rgb_on_device, features, boxes, counts, images);
     forward_head(images, false);
+    release_images();
     // EvaluateLoss passes epoch 0 to DetectionHead.Loss (YoloTrainer.cs:243)
     launch_losses(images, 0, 0);
     // every rank's record head (loss parts, positives, image count) in one all-gather, combined on the host
@@ -1309,6 +1332,63 @@ int Session::evaluate(const uint8_t* rgb, bool rgb_on_device, const float* const
         out->device_ms = ms;
     }
     return SY_OK;
+}
+
+// ------------------------------------------------------------------ image prefetch
+int Session::prefetch_images(const uint8_t* rgb, int images) {
+    if (!rgb) throw SyError(SY_ERR_INVALID_ARGUMENT, "images missing");
+    if (images < 1 || images > B_) throw SyError(SY_ERR_INVALID_ARGUMENT, "images out of range");
+    if (cfg.backbone == SY_BACKBONE_NONE) throw SyError(SY_ERR_INVALID_ARGUMENT, "the session has no trunk");
+    SY_CUDA(cudaSetDevice(device_));
+    for (ImageSlot& sl : slots_)
+        if (sl.ready && sl.host == rgb && sl.images == images) return SY_OK;   // already on its way
+    const size_t cap = (size_t)B_ * cfg.image_size * cfg.image_size * 3;
+    const size_t bytes = (size_t)images * cfg.image_size * cfg.image_size * 3;
+    if (!copy_stream_) SY_CUDA(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
+    ImageSlot& sl = slots_[next_slot_];
+    next_slot_ ^= 1;
+    if (!sl.dev) {
+        SY_CUDA(cudaMalloc(&sl.dev, cap));
+        SY_CUDA(cudaEventCreateWithFlags(&sl.copied, cudaEventDisableTiming));
+        SY_CUDA(cudaEventCreateWithFlags(&sl.released, cudaEventDisableTiming));
+    }
+    sl.ready = false;
+    sl.pending = false;
+    cudaPointerAttributes attr;
+    const bool pinned = cudaPointerGetAttributes(&attr, rgb) == cudaSuccess && attr.type == cudaMemoryTypeHost;
+    cudaGetLastError();
+    const uint8_t* src = rgb;
+    if (!pinned) {
+        // pageable memory: stage it (the staging buffer is free once the previous copy from it ended)
+        if (!sl.pinned) SY_CUDA(cudaMallocHost(&sl.pinned, cap));
+        SY_CUDA(cudaEventSynchronize(sl.copied));
+        std::memcpy(sl.pinned, rgb, bytes);
+        src = sl.pinned;
+    }
+    sl.host = rgb;
+    sl.src = src;
+    sl.images = images;
+    sl.ready = true;
+    sl.pending = true;
+    return SY_OK;
+}
+
+void Session::issue_prefetch(ImageSlot& sl) {
+    if (!sl.pending) return;
+    // the previous batch in this slot has been read by its consumer's device work
+    if (sl.used) SY_CUDA(cudaStreamWaitEvent(copy_stream_, sl.released, 0));
+    const size_t bytes = (size_t)sl.images * cfg.image_size * cfg.image_size * 3;
+    SY_CUDA(cudaMemcpyAsync(sl.dev, sl.src, bytes, cudaMemcpyHostToDevice, copy_stream_));
+    SY_CUDA(cudaEventRecord(sl.copied, copy_stream_));
+    sl.pending = false;
+}
+
+// After the device work that read a prefetched batch has been enqueued: the slot may be refilled once it ends.
+void Session::release_images() {
+    if (!consuming_) return;
+    SY_CUDA(cudaEventRecord(consuming_->released, stream_));
+    consuming_->used = true;
+    consuming_ = nullptr;
 }
 
 // ------------------------------------------------------------------ inference
@@ -1382,6 +1462,7 @@ int Session::detect(const uint8_t* rgb, bool rgb_on_device, const float* const* 
     const sy_box unused{};
     prepare_inputs(rgb, rgb_on_device, features, &unused, no_boxes.data(), images);
     forward_head(images, false);
+    release_images();
     last_batch_ = images;
     const int nc = cfg.num_classes, set = n_sets_ - 1;
     const bool e2e = cfg.end_to_end != 0;

@@ -100,6 +100,9 @@ public:
     int detect(const uint8_t* rgb, bool rgb_on_device, const float* const* features, int images,
                const sy_letterbox* transforms, const sy_detect_options* options, sy_detection* out, int32_t* counts,
                double* timing = nullptr);
+    // Starts the host-to-device copy of a batch of RGB24 images on the copy stream; a later step / evaluate
+    // / detect with the same host pointer and image count takes the copy instead of copying again.
+    int prefetch_images(const uint8_t* rgb, int images);
     int set_epoch(int epoch);
     // AdamW steps taken per optimizer group (class branches, cv2, one2one_cv2)
     int get_optimizer_steps(int32_t steps[3]) const;
@@ -266,6 +269,26 @@ private:
     void prof_collect();
     NcclApi* nccl_ = nullptr;
     void* comm_ = nullptr;
+    // Prefetched image batches: two slots, filled alternately by prefetch_images.  A slot's copy is issued on
+    // copy_stream_ by the next call that prepares inputs, after that call's own small uploads: copies that
+    // share the host-to-device engine run in submission order, so a large copy submitted first would hold
+    // those uploads (and the step behind them) back.  `copied` is recorded after a slot's copy, `released`
+    // after the device work of the call that consumed it (the next copy into that slot waits for it).
+    struct ImageSlot {
+        uint8_t* dev = nullptr;
+        uint8_t* pinned = nullptr;   // staging for pageable sources
+        const uint8_t* host = nullptr;
+        const uint8_t* src = nullptr;   // what the copy reads: host, or pinned
+        int images = 0;
+        bool ready = false, pending = false, used = false;
+        cudaEvent_t copied = nullptr, released = nullptr;
+    };
+    void issue_prefetch(ImageSlot& sl);
+    ImageSlot slots_[2];
+    int next_slot_ = 0;
+    ImageSlot* consuming_ = nullptr;   // slot read by the device work being enqueued
+    cudaStream_t copy_stream_ = nullptr;
+    void release_images();
     // inference buffers, allocated by the first detect call (the output and workspace grow with
     // max_detections): for end-to-end heads the decoded head [B][4 + nc][anchors] and the rows [B][k][6]
     // (raw heads decode inside the candidate kernel); letterbox records
