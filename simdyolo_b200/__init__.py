@@ -443,6 +443,33 @@ def make_config(model: str = "yolov8n", image_size: int = 640, max_batch: int = 
     return cfg
 
 
+# ------------------------------------------------------------------ ground truth
+
+BOX_DTYPE = np.dtype([("class_id", "<i4"), ("x1", "<f4"), ("y1", "<f4"), ("x2", "<f4"), ("y2", "<f4")])
+
+
+class PackedBoxes:
+    """The ground truth of one batch in the C layout (sy_box records, per-image counts), packed once."""
+
+    def __init__(self, records: np.ndarray, counts: np.ndarray):
+        self.records = np.ascontiguousarray(records, BOX_DTYPE)
+        self.counts = np.ascontiguousarray(counts, np.int32)
+        self.pointer = self.records.ctypes.data_as(C.POINTER(Box))
+
+
+def pack_boxes(boxes_per_image) -> PackedBoxes:
+    """Per-image lists of (cls, x1, y1, x2, y2) -> PackedBoxes (TrainingBox records, YoloTrainer's labels)."""
+    counts = np.array([len(b) for b in boxes_per_image], np.int32)
+    n = int(counts.sum())
+    rec = np.zeros(max(1, n), BOX_DTYPE)
+    if n:
+        flat = np.array([bx for b in boxes_per_image for bx in b], np.float64).reshape(n, 5)
+        rec["class_id"][:n] = flat[:, 0].astype(np.int32)
+        for k, f in enumerate(("x1", "y1", "x2", "y2")):
+            rec[f][:n] = flat[:, k + 1]
+    return PackedBoxes(rec, counts)
+
+
 # ------------------------------------------------------------------ session
 
 class Session:
@@ -533,12 +560,12 @@ class Session:
 
     @staticmethod
     def _boxes(boxes_per_image):
-        counts = np.array([len(b) for b in boxes_per_image], np.int32)
-        flat = [bx for b in boxes_per_image for bx in b]
-        arr = (Box * max(1, len(flat)))()
-        for i, (c, x1, y1, x2, y2) in enumerate(flat):
-            arr[i] = Box(int(c), float(x1), float(y1), float(x2), float(y2))
-        return arr, counts
+        """(Box array pointer, counts) from per-image lists of (cls, x1, y1, x2, y2), or from the PackedBoxes
+        that pack_boxes made (then no per-box Python work is left for the call)."""
+        if isinstance(boxes_per_image, PackedBoxes):
+            return boxes_per_image.pointer, boxes_per_image.counts
+        packed = pack_boxes(boxes_per_image)
+        return packed.pointer, packed.counts
 
     def prefetch_images(self, images: np.ndarray):
         """Starts the host-to-device copy of uint8 [B, S, S, 3] images (sy_cuda_prefetch_images); a later

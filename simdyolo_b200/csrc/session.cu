@@ -202,6 +202,7 @@ Session::~Session() {
         if (sl.released) cudaEventDestroy(sl.released);
     }
     if (copy_stream_) cudaStreamDestroy(copy_stream_);
+    if (ev_uploaded_) cudaEventDestroy(ev_uploaded_);
     for (cudaEvent_t e : prof_ev_) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
 }
@@ -1027,6 +1028,7 @@ void Session::prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float
     SY_CUDA(cudaMemsetAsync(d_flags_, 0, sizeof(int) * 16, stream_));
     h_images_[0] = images;
     SY_CUDA(cudaMemcpyAsync(d_images_, h_images_, sizeof(int), cudaMemcpyHostToDevice, stream_));
+    if (copy_stream_) SY_CUDA(cudaEventRecord(ev_uploaded_, stream_));
     if (rgb) {
         const size_t bytes = (size_t)images * cfg.image_size * cfg.image_size * 3;
         const uint8_t* src = d_rgb_;
@@ -1344,7 +1346,11 @@ int Session::prefetch_images(const uint8_t* rgb, int images) {
         if (sl.ready && sl.host == rgb && sl.images == images) return SY_OK;   // already on its way
     const size_t cap = (size_t)B_ * cfg.image_size * cfg.image_size * 3;
     const size_t bytes = (size_t)images * cfg.image_size * cfg.image_size * 3;
-    if (!copy_stream_) SY_CUDA(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
+    if (!copy_stream_) {
+        SY_CUDA(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
+        SY_CUDA(cudaEventCreateWithFlags(&ev_uploaded_, cudaEventDisableTiming));
+        SY_CUDA(cudaEventRecord(ev_uploaded_, stream_));
+    }
     ImageSlot& sl = slots_[next_slot_];
     next_slot_ ^= 1;
     if (!sl.dev) {
@@ -1375,8 +1381,11 @@ int Session::prefetch_images(const uint8_t* rgb, int images) {
 
 void Session::issue_prefetch(ImageSlot& sl) {
     if (!sl.pending) return;
-    // the previous batch in this slot has been read by its consumer's device work
+    // the previous batch in this slot has been read by its consumer's device work, and this call's small
+    // uploads have landed (the copy engine serves eligible copies in turn, so a large copy that became
+    // eligible first would hold them, and the step behind them, for its whole length)
     if (sl.used) SY_CUDA(cudaStreamWaitEvent(copy_stream_, sl.released, 0));
+    SY_CUDA(cudaStreamWaitEvent(copy_stream_, ev_uploaded_, 0));
     const size_t bytes = (size_t)sl.images * cfg.image_size * cfg.image_size * 3;
     SY_CUDA(cudaMemcpyAsync(sl.dev, sl.src, bytes, cudaMemcpyHostToDevice, copy_stream_));
     SY_CUDA(cudaEventRecord(sl.copied, copy_stream_));

@@ -270,9 +270,9 @@ private:
     NcclApi* nccl_ = nullptr;
     void* comm_ = nullptr;
     // Prefetched image batches: two slots, filled alternately by prefetch_images.  A slot's copy is issued on
-    // copy_stream_ by the next call that prepares inputs, after that call's own small uploads: copies that
-    // share the host-to-device engine run in submission order, so a large copy submitted first would hold
-    // those uploads (and the step behind them) back.  `copied` is recorded after a slot's copy, `released`
+    // copy_stream_ by the next call that prepares inputs, and starts after that call's own small uploads have
+    // landed: the host-to-device copy engine serves one copy after another, so a large copy that got there
+    // first would hold those uploads (and the step behind them) back for its whole length.  `copied` is recorded after a slot's copy, `released`
     // after the device work of the call that consumed it (the next copy into that slot waits for it).
     struct ImageSlot {
         uint8_t* dev = nullptr;
@@ -286,6 +286,7 @@ private:
     void issue_prefetch(ImageSlot& sl);
     ImageSlot slots_[2];
     int next_slot_ = 0;
+    cudaEvent_t ev_uploaded_ = nullptr;   // this call's small uploads, which a prefetch copy must not overtake
     ImageSlot* consuming_ = nullptr;   // slot read by the device work being enqueued
     cudaStream_t copy_stream_ = nullptr;
     void release_images();
