@@ -124,6 +124,40 @@ __global__ void bn_apply_kernel(const float* y, int ypitch, const float* mean_p,
     }
 }
 
+// The same for channels in whole float4 groups: a thread keeps one channel group's coefficients in registers and
+// walks the image's rows (blockDim.x / (c / 4) rows in flight per block), so each element costs one load, the
+// arithmetic and one store.  SiLU as x / (1 + exp(-x)) with the fast exponential and division of the conv
+// epilogues.
+__global__ void __launch_bounds__(256) bn_apply_rows_kernel(const float* y, int ypitch, const float* mean_p,
+                                                            const float* inv_p, const float* gamma, const float* beta,
+                                                            int c, Grid g, float* a, int apitch, int rnd) {
+    const int b = blockIdx.y, per_row = c >> 2;
+    const int slots = blockDim.x / per_row;
+    if ((int)threadIdx.x >= slots * per_row) return;
+    const int j = threadIdx.x % per_row, r0 = threadIdx.x / per_row, ch = 4 * j;
+    const float4 mv = *reinterpret_cast<const float4*>(mean_p + (long)b * c + ch);
+    const float4 iv = *reinterpret_cast<const float4*>(inv_p + (long)b * c + ch);
+    const float g0 = gamma[ch], g1 = gamma[ch + 1], g2 = gamma[ch + 2], g3 = gamma[ch + 3];
+    const float b0 = beta[ch], b1 = beta[ch + 1], b2 = beta[ch + 2], b3 = beta[ch + 3];
+    const float inv_wp = 1.0f / (float)g.wp;
+    const long base = (long)b * g.rows;
+    for (int r = blockIdx.x * slots + r0; r < g.rows; r += gridDim.x * slots) {
+        const int py = fast_div(r, inv_wp), px = r - py * g.wp;
+        const bool in = py >= 1 && py <= g.h && px >= 1 && px <= g.w;
+        const long row = base + r;
+        float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (in) {
+            const float4 v = *reinterpret_cast<const float4*>(y + row * ypitch + ch);
+            out.x = silu_fast((v.x - mv.x) * iv.x * g0 + b0);
+            out.y = silu_fast((v.y - mv.y) * iv.y * g1 + b1);
+            out.z = silu_fast((v.z - mv.z) * iv.z * g2 + b2);
+            out.w = silu_fast((v.w - mv.w) * iv.w * g3 + b3);
+            if (rnd) out = make_float4(tf32_rna(out.x), tf32_rna(out.y), tf32_rna(out.z), tf32_rna(out.w));
+        }
+        *reinterpret_cast<float4*>(a + row * apitch + ch) = out;
+    }
+}
+
 // Evaluation mode (HeadOperations.cs:158-166 with training = false): every image normalises with the
 // running mean / variance.
 __global__ void bn_eval_coef_kernel(const float* rm, const float* rv, float eps, long n, int c, float* mean_p,
@@ -226,6 +260,41 @@ __global__ void bn_bwd_apply_kernel(const float* y, int ypitch, const float* dz,
                 out = fb[j] * (n * dz[row * zpitch + j] - rb[2 * j] - (y[row * ypitch + j] - mb[j]) * ib[j] * rb[2 * j + 1]);
             dy[row * dpitch + j] = rnd ? tf32_rna(out) : out;
         }
+    }
+}
+
+// The same for channels in whole float4 groups, coefficients of one channel group per thread in registers
+// (see bn_apply_rows_kernel).
+__global__ void __launch_bounds__(256) bn_bwd_apply_rows_kernel(const float* y, int ypitch, const float* dz, int zpitch,
+                                                                const float* mean_p, const float* inv_p, const float* f_p,
+                                                                const float* red, int c, float n, Grid g, float* dy,
+                                                                int dpitch, int rnd) {
+    const int b = blockIdx.y, per_row = c >> 2;
+    const int slots = blockDim.x / per_row;
+    if ((int)threadIdx.x >= slots * per_row) return;
+    const int j = threadIdx.x % per_row, r0 = threadIdx.x / per_row, ch = 4 * j;
+    const float4 mv = *reinterpret_cast<const float4*>(mean_p + (long)b * c + ch);
+    const float4 iv = *reinterpret_cast<const float4*>(inv_p + (long)b * c + ch);
+    const float4 fv = *reinterpret_cast<const float4*>(f_p + (long)b * c + ch);
+    const float4 q0 = *reinterpret_cast<const float4*>(red + (long)b * c * 2 + 8 * j);
+    const float4 q1 = *reinterpret_cast<const float4*>(red + (long)b * c * 2 + 8 * j + 4);
+    const float inv_wp = 1.0f / (float)g.wp;
+    const long base = (long)b * g.rows;
+    for (int r = blockIdx.x * slots + r0; r < g.rows; r += gridDim.x * slots) {
+        const int py = fast_div(r, inv_wp), px = r - py * g.wp;
+        const bool in = py >= 1 && py <= g.h && px >= 1 && px <= g.w;
+        const long row = base + r;
+        float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (in) {
+            const float4 yv = *reinterpret_cast<const float4*>(y + row * ypitch + ch);
+            const float4 zv = *reinterpret_cast<const float4*>(dz + row * zpitch + ch);
+            out.x = fv.x * (n * zv.x - q0.x - (yv.x - mv.x) * iv.x * q0.y);
+            out.y = fv.y * (n * zv.y - q0.z - (yv.y - mv.y) * iv.y * q0.w);
+            out.z = fv.z * (n * zv.z - q1.x - (yv.z - mv.z) * iv.z * q1.y);
+            out.w = fv.w * (n * zv.w - q1.z - (yv.w - mv.w) * iv.w * q1.w);
+            if (rnd) out = make_float4(tf32_rna(out.x), tf32_rna(out.y), tf32_rna(out.z), tf32_rna(out.w));
+        }
+        *reinterpret_cast<float4*>(dy + row * dpitch + ch) = out;
     }
 }
 
@@ -458,7 +527,10 @@ void bn_silu_apply(const View& y, const float* coef, const float* gamma, const f
     const long per_image = (long)g.rows * (vec ? c / 4 : c);
     if (per_image >= (1L << 22)) throw std::runtime_error("bn_silu_apply: image too large");
     const float* inv = coef + (long)batch * c;
-    if (vec)
+    if (vec && c / 4 <= 256)
+        bn_apply_rows_kernel<<<image_grid(per_image, batch), 256, 0, stream>>>(y.base, y.pitch, coef, inv, gamma, beta,
+                                                                                c, g, a.base, a.pitch, rnd);
+    else if (vec)
         bn_apply_kernel<true><<<image_grid(per_image, batch), 256, 0, stream>>>(y.base, y.pitch, coef, inv, gamma,
                                                                                 beta, c, g, a.base, a.pitch, rnd);
     else
@@ -502,7 +574,10 @@ void bn_backward_apply(const View& y, const View& dz, const float* coef, const f
     const float* inv = coef + (long)batch * c;
     const float* red = bcoef + (long)batch * c;
     const float n = (float)(g.h * g.w);
-    if (vec)
+    if (vec && c / 4 <= 256)
+        bn_bwd_apply_rows_kernel<<<image_grid(per_image, batch), 256, 0, stream>>>(
+            y.base, y.pitch, dz.base, dz.pitch, coef, inv, bcoef, red, c, n, g, dy.base, dy.pitch, rnd);
+    else if (vec)
         bn_bwd_apply_kernel<true><<<image_grid(per_image, batch), 256, 0, stream>>>(
             y.base, y.pitch, dz.base, dz.pitch, coef, inv, bcoef, red, c, n, g, dy.base, dy.pitch, rnd);
     else

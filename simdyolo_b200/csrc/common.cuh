@@ -130,6 +130,8 @@ __device__ __forceinline__ float det_pow6(float x) {
 }
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
+// The same with the fast division (within 2 ulp; v / inf = -0 for the very negative v)
+__device__ __forceinline__ float silu_fast(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
 // x rounded to the nearest TF32 value (10 explicit mantissa bits, ties away from zero).  The tensor
 // core reads an FP32 operand of a kind::tf32 MMA by dropping its low 13 mantissa bits, which shrinks

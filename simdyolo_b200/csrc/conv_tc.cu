@@ -150,8 +150,6 @@ __host__ __device__ constexpr int fwd_threads(int epi_warps) { return 32 * (kEpi
 constexpr int kMmaBar = 1, kMmaBarThreads = 32 * (1 + kMmaWarps);   // waiter + MMA warps
 constexpr int kTileM = 128;
 
-__device__ __forceinline__ float silu_fast(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
-
 // Sums of 16 per-lane values over the 32 lanes of a warp in 16 shuffles (each butterfly step hands
 // half of the remaining channels to the partner lane): on return every lane L holds the sum of
 // channel L >> 1.  The order of additions is fixed, so results are deterministic.
