@@ -10,6 +10,7 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <functional>
 #include <array>
 #include <chrono>
 #include <cmath>
@@ -195,6 +196,11 @@ Session::~Session() {
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
     if (ev_post_) cudaEventDestroy(ev_post_);
+    for (int l = 0; l < 3; l++) {
+        if (l > 0 && lanes_[l].stream) cudaStreamDestroy(lanes_[l].stream);
+        if (lanes_[l].done) cudaEventDestroy(lanes_[l].done);
+    }
+    if (ev_fork_) cudaEventDestroy(ev_fork_);
     for (ImageSlot& sl : slots_) {
         if (sl.dev) cudaFree(sl.dev);
         if (sl.pinned) cudaFreeHost(sl.pinned);
@@ -689,6 +695,7 @@ void Session::build_head() {
     // activations and gradients
     size_t ws = 0;
     size_t bn_part_floats = 0;
+    size_t lvl_ws[3] = {0, 0, 0}, lvl_part[3] = {0, 0, 0};
     for (auto& branch : branches_) {
         const Grid& g = levels_[branch.level];
         View x = features_[branch.level];
@@ -705,11 +712,14 @@ void Session::build_head() {
                 hb.coef = static_cast<float*>(dalloc(sizeof(float) * 2 * B_ * b.oc));
                 hb.bcoef = static_cast<float*>(dalloc(sizeof(float) * 3 * B_ * b.oc));
                 bn_part_floats = std::max(bn_part_floats, bn_partial_floats(B_, g, b.oc));
+                lvl_part[branch.level] = std::max(lvl_part[branch.level], bn_partial_floats(B_, g, b.oc));
             } else {
                 hb.dy = hb.g;
             }
             if (hb.dw) {
                 ws = std::max(ws, dw_wgrad_workspace_floats(b.oc, hb.taps, (long)B_ * g.rows));
+                lvl_ws[branch.level] = std::max(lvl_ws[branch.level],
+                                                dw_wgrad_workspace_floats(b.oc, hb.taps, (long)B_ * g.rows));
             } else {
                 hb.kpad_in = round_up(b.ic, 32);
                 hb.kpad_out = round_up(b.oc, 32);
@@ -718,6 +728,8 @@ void Session::build_head() {
                 wsp_floats_ = std::max(wsp_floats_, std::max((size_t)b.oc * hb.taps * hb.kpad_in,
                                                              (size_t)b.ic * hb.taps * hb.kpad_out));
                 ws = std::max(ws, wgrad_workspace_floats(b.ic, b.oc, hb.taps, (long)B_ * g.rows));
+                lvl_ws[branch.level] = std::max(lvl_ws[branch.level],
+                                                wgrad_workspace_floats(b.ic, b.oc, hb.taps, (long)B_ * g.rows));
             }
             x = b.has_bn ? hb.a : hb.y;
         }
@@ -779,6 +791,38 @@ void Session::build_head() {
             sizeof(float) * center_workspace_floats(B_, std::max({max_first_oc, feat_ch_[0], feat_ch_[1], feat_ch_[2]}))));
     }
     bn_part_ = static_cast<float*>(dalloc(sizeof(float) * std::max<size_t>(bn_part_floats, 1)));
+    // level lanes (TF32 mode): lane 0 is stream_ with the shared scratch, lanes 1 and 2 get their own
+    lanes_[0] = LevelLane{stream_, bn_part_, wgrad_ws_, nullptr};
+    if (!x3_) {
+        SY_CUDA(cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming));
+        SY_CUDA(cudaEventCreateWithFlags(&lanes_[0].done, cudaEventDisableTiming));
+        for (int l = 1; l < 3; l++) {
+            SY_CUDA(cudaStreamCreateWithFlags(&lanes_[l].stream, cudaStreamNonBlocking));
+            SY_CUDA(cudaEventCreateWithFlags(&lanes_[l].done, cudaEventDisableTiming));
+            lanes_[l].bn_part = static_cast<float*>(dalloc(sizeof(float) * std::max<size_t>(lvl_part[l], 1)));
+            lanes_[l].wgrad_ws = static_cast<float*>(dalloc(sizeof(float) * std::max<size_t>(lvl_ws[l], 1)));
+        }
+    }
+}
+
+void Session::fork_levels() {
+    SY_CUDA(cudaEventRecord(ev_fork_, lanes_[0].stream));
+    for (int l = 1; l < 3; l++) SY_CUDA(cudaStreamWaitEvent(lanes_[l].stream, ev_fork_, 0));
+}
+
+void Session::join_levels() {
+    use_lane(0);
+    for (int l = 1; l < 3; l++) {
+        SY_CUDA(cudaEventRecord(lanes_[l].done, lanes_[l].stream));
+        SY_CUDA(cudaStreamWaitEvent(lanes_[0].stream, lanes_[l].done, 0));
+    }
+}
+
+// Launches that follow go to level l's stream with its scratch.
+void Session::use_lane(int l) {
+    stream_ = lanes_[l].stream;
+    bn_part_ = lanes_[l].bn_part;
+    wgrad_ws_ = lanes_[l].wgrad_ws;
 }
 
 void Session::refresh_head_weights() {
@@ -807,8 +851,25 @@ static View rows_of(View v, int batch, const Grid& g) {
     return v;
 }
 
+// Puts stream_ and the scratch back to lane 0 when a head pass leaves early.
+struct LaneGuard {
+    std::function<void()> restore;
+    ~LaneGuard() {
+        if (restore) restore();
+    }
+};
+
 void Session::forward_head(int batch, bool training) {
+    const bool lanes = level_lanes();
+    LaneGuard guard;
+    if (lanes) {
+        guard.restore = [this] { use_lane(0); };
+        fork_levels();
+    }
+    for (int lv = 0; lv < 3; lv++)
     for (auto& branch : branches_) {
+        if (branch.level != lv) continue;
+        if (lanes) use_lane(lv);
         const Grid& g = levels_[branch.level];
         for (auto& hb : branch.blocks) {
             ConvEpilogue ep;
@@ -838,6 +899,7 @@ void Session::forward_head(int batch, bool training) {
             }
         }
     }
+    if (lanes) join_levels();
 }
 
 void Session::backward_head(int batch) {
@@ -845,9 +907,16 @@ void Session::backward_head(int batch) {
         if (feat_mean_[l])
             center_features(rows_of(features_[l], batch, levels_[l]), batch, levels_[l], feat_mean_[l], center_ws_,
                             rows_of(feat_c_[l], batch, levels_[l]), rnd_, stream_);
-    for (int set = n_sets_ - 1; set >= 0; set--)
-        for (int l = 2; l >= 0; l--)
+    const bool lanes = level_lanes();
+    LaneGuard guard;
+    if (lanes) {
+        guard.restore = [this] { use_lane(0); };
+        fork_levels();
+    }
+    for (int l = 2; l >= 0; l--)
+        for (int set = n_sets_ - 1; set >= 0; set--)
             for (int kind = 1; kind >= 0; kind--) {
+                if (lanes) use_lane(l);
                 Branch& branch = branches_[set * 6 + kind * 3 + l];
                 const Grid& g = levels_[l];
                 for (int i = (int)branch.blocks.size() - 1; i >= 0; i--) {
@@ -900,6 +969,7 @@ void Session::backward_head(int batch) {
                     }
                 }
             }
+    if (lanes) join_levels();
     // BatchNorm gamma / beta gradients of every layer, images folded in order (deferred from the folds)
     if (n_bn_jobs_ > 0) bn_param_grad_batch(d_bn_jobs_, n_bn_jobs_, bn_max_c_, batch, stream_);
 }

@@ -152,6 +152,22 @@ private:
     void wait_stream(const char* what);
     [[noreturn]] void abort_comm(const std::string& reason);
     void backward_head(int batch);
+    // The head's three pyramid levels are independent between the trunk and the loss (forward) and between
+    // the loss and the parameter-gradient fold (backward): in TF32 mode, unprofiled, each level runs on its
+    // own stream with its own BatchNorm-partial and weight-gradient scratch, forked from and joined back to
+    // stream_ (inside the step's CUDA graph as well), so the small levels fill the SMs the large one leaves.
+    struct LevelLane {
+        cudaStream_t stream = nullptr;   // lane 0 is stream_
+        float* bn_part = nullptr;
+        float* wgrad_ws = nullptr;
+        cudaEvent_t done = nullptr;
+    };
+    LevelLane lanes_[3];
+    cudaEvent_t ev_fork_ = nullptr;
+    bool level_lanes() const { return lanes_[1].stream != nullptr && !x3_ && !prof_; }
+    void fork_levels();
+    void join_levels();
+    void use_lane(int l);
     void refresh_head_weights();
     BnFoldJob* d_bn_jobs_ = nullptr;             // one job per head BatchNorm layer
     int n_bn_jobs_ = 0, bn_max_c_ = 0;
