@@ -201,6 +201,8 @@ Session::~Session() {
         if (lanes_[l].done) cudaEventDestroy(lanes_[l].done);
     }
     if (ev_fork_) cudaEventDestroy(ev_fork_);
+    for (cudaEvent_t e : ev_feat_)
+        if (e) cudaEventDestroy(e);
     for (ImageSlot& sl : slots_) {
         if (sl.dev) cudaFree(sl.dev);
         if (sl.pinned) cudaFreeHost(sl.pinned);
@@ -501,6 +503,9 @@ void Session::build_backbone() {
         for (int l = 0; l < 3; l++) read |= overlaps(features_[l], op.out);
         op.plain_out = read || x3_;   // 3xTF32 passes accumulate in the plain output
     }
+    for (int i = 0; i < (int)bops_.size(); i++)
+        for (int l = 0; l < 3; l++)
+            if (overlaps(features_[l], bops_[i].out)) feat_op_[l] = i;
     n_backbone = tk_poff_;
     backbone_params_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)tk_poff_));
     for (auto& op : bops_) {
@@ -531,7 +536,9 @@ int Session::set_backbone(const float* host, long count) {
 }
 
 void Session::forward_backbone(int batch, const uint8_t* rgb_device) {
-    for (auto& op : bops_) {
+    const bool events = level_lanes() && ev_feat_[0];
+    for (int i = 0; i < (int)bops_.size(); i++) {
+        const BackboneOp& op = bops_[i];
         View in = op.in, out = op.out;
         if (op.type == 0 && !op.plain_out) out.base = nullptr;
         if (op.type == 0 && in.base == img_.base) {
@@ -577,7 +584,11 @@ void Session::forward_backbone(int batch, const uint8_t* rgb_device) {
                          {1, op.ic, op.oc, 9, op.gout.h, op.gout.w});
             }
         }
+        if (events)
+            for (int l = 0; l < 2; l++)
+                if (i == feat_op_[l]) SY_CUDA(cudaEventRecord(ev_feat_[l], stream_));
     }
+    feat_events_ = events;
 }
 
 // ------------------------------------------------------------------ head plan
@@ -795,6 +806,8 @@ void Session::build_head() {
     lanes_[0] = LevelLane{stream_, bn_part_, wgrad_ws_, nullptr};
     if (!x3_) {
         SY_CUDA(cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming));
+        if (feat_op_[0] >= 0 && feat_op_[1] >= 0)
+            for (int l = 0; l < 2; l++) SY_CUDA(cudaEventCreateWithFlags(&ev_feat_[l], cudaEventDisableTiming));
         SY_CUDA(cudaEventCreateWithFlags(&lanes_[0].done, cudaEventDisableTiming));
         for (int l = 1; l < 3; l++) {
             SY_CUDA(cudaStreamCreateWithFlags(&lanes_[l].stream, cudaStreamNonBlocking));
@@ -818,9 +831,9 @@ void Session::join_levels() {
     }
 }
 
-// Launches that follow go to level l's stream with its scratch.
-void Session::use_lane(int l) {
-    stream_ = lanes_[l].stream;
+// Launches that follow go to lane stream_lane's stream (level l's own by default) with level l's scratch.
+void Session::use_lane(int l, int stream_lane) {
+    stream_ = lanes_[stream_lane < 0 ? l : stream_lane].stream;
     bn_part_ = lanes_[l].bn_part;
     wgrad_ws_ = lanes_[l].wgrad_ws;
 }
@@ -864,12 +877,17 @@ void Session::forward_head(int batch, bool training) {
     LaneGuard guard;
     if (lanes) {
         guard.restore = [this] { use_lane(0); };
-        fork_levels();
+        if (feat_events_) {
+            for (int l = 0; l < 2; l++) SY_CUDA(cudaStreamWaitEvent(lanes_[l + 1].stream, ev_feat_[l], 0));
+        } else {
+            fork_levels();
+        }
     }
+    feat_events_ = false;
     for (int lv = 0; lv < 3; lv++)
     for (auto& branch : branches_) {
         if (branch.level != lv) continue;
-        if (lanes) use_lane(lv);
+        if (lanes) use_lane(lv, (lv + 1) % 3);
         const Grid& g = levels_[branch.level];
         for (auto& hb : branch.blocks) {
             ConvEpilogue ep;
@@ -1073,6 +1091,7 @@ void Session::prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float
     if (images < 1 || images > B_) throw SyError(SY_ERR_INVALID_ARGUMENT, "images out of range");
     if (!counts || (!boxes && images > 0)) throw SyError(SY_ERR_INVALID_ARGUMENT, "counts / boxes missing");
     SY_CUDA(cudaSetDevice(device_));
+    feat_events_ = false;
     // validate and stage ground truth (TrainingDataset.ParseLabels guarantees, DetectionLoss.cs:51)
     long k = 0;
     h_box_off_[0] = 0;

@@ -164,10 +164,16 @@ private:
     };
     LevelLane lanes_[3];
     cudaEvent_t ev_fork_ = nullptr;
+    // In the forward pass level l runs on lane (l + 1) % 3's stream (level 2, which needs the whole trunk,
+    // stays on stream_), and when the trunk ran just before, levels 0 and 1 start as soon as the trunk op
+    // that finishes their feature map has (ev_feat_), overlapping the trunk's remaining bottom-up layers.
+    int feat_op_[3] = {-1, -1, -1};   // index in bops_ of the last op writing features_[l]
+    cudaEvent_t ev_feat_[2] = {nullptr, nullptr};
+    bool feat_events_ = false;        // ev_feat_ recorded by the trunk pass the next forward_head follows
     bool level_lanes() const { return lanes_[1].stream != nullptr && !x3_ && !prof_; }
     void fork_levels();
     void join_levels();
-    void use_lane(int l);
+    void use_lane(int l, int stream_lane = -1);
     void refresh_head_weights();
     BnFoldJob* d_bn_jobs_ = nullptr;             // one job per head BatchNorm layer
     int n_bn_jobs_ = 0, bn_max_c_ = 0;
