@@ -848,8 +848,8 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         const int b_bytes = n * 128;
         const int acc_cols = pow2_at_least(n);
         const int res_bytes = taps * kchunks * b_bytes;
-        const bool resident = res_bytes <= 72 * 1024;
-        const int b_min = resident ? res_bytes : 2 * b_bytes;
+        bool resident = res_bytes <= 72 * 1024;
+        int b_min = resident ? res_bytes : 2 * b_bytes;
         int ngroups = 0, g_lo[kMaxGroups], g_span[kMaxGroups], g_ntaps[kMaxGroups], tap_t[9], tap_off[9];
         int T = 0, a_stage = 0;
         auto stage_bytes = [&](int t_sub) {
@@ -918,6 +918,13 @@ static void launch_fwd(const View& in, long m_rows, const int* shift, int taps, 
         // the direct stores, which measured faster for them
         int kSmemBudget = kSmemTotal, stage_total = 0;
         plan(kSmemTotal);
+        // weights that fit beside two A regions of one sub-tile stay resident too: a streamed ring fetches
+        // them again for every CTA tile, resident ones once per CTA
+        if (!resident && T > 0 && res_bytes + 2 * stage_bytes(1) <= kSmemTotal) {
+            resident = true;
+            b_min = res_bytes;
+            plan(kSmemTotal);
+        }
         if (plain_epilogue && out.base && T > 0 && n_valid > 16) {
             const int T_full = T, groups_full = ngroups, staged = 8 * 4096;
             auto a_ring_depth = [&](int budget) { return std::min(4, (budget - res_bytes) / a_stage); };

@@ -796,14 +796,15 @@ void Session::build_head() {
         }
         max_first_oc = std::max(max_first_oc, hb.b.oc);
     }
+    const size_t center_ws_floats =
+        center_workspace_floats(B_, std::max({max_first_oc, feat_ch_[0], feat_ch_[1], feat_ch_[2]}));
     if (max_first_oc > 0) {
         tap_sums_ = static_cast<float*>(dalloc(sizeof(float) * (size_t)B_ * 9 * max_first_oc));
-        center_ws_ = static_cast<float*>(dalloc(
-            sizeof(float) * center_workspace_floats(B_, std::max({max_first_oc, feat_ch_[0], feat_ch_[1], feat_ch_[2]}))));
+        center_ws_ = static_cast<float*>(dalloc(sizeof(float) * center_ws_floats));
     }
     bn_part_ = static_cast<float*>(dalloc(sizeof(float) * std::max<size_t>(bn_part_floats, 1)));
     // level lanes (TF32 mode): lane 0 is stream_ with the shared scratch, lanes 1 and 2 get their own
-    lanes_[0] = LevelLane{stream_, bn_part_, wgrad_ws_, nullptr};
+    lanes_[0] = LevelLane{stream_, bn_part_, wgrad_ws_, nullptr, tap_sums_, center_ws_};
     if (!x3_) {
         SY_CUDA(cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming));
         if (feat_op_[0] >= 0 && feat_op_[1] >= 0)
@@ -814,6 +815,10 @@ void Session::build_head() {
             SY_CUDA(cudaEventCreateWithFlags(&lanes_[l].done, cudaEventDisableTiming));
             lanes_[l].bn_part = static_cast<float*>(dalloc(sizeof(float) * std::max<size_t>(lvl_part[l], 1)));
             lanes_[l].wgrad_ws = static_cast<float*>(dalloc(sizeof(float) * std::max<size_t>(lvl_ws[l], 1)));
+            if (max_first_oc > 0) {
+                lanes_[l].tap_sums = static_cast<float*>(dalloc(sizeof(float) * (size_t)B_ * 9 * max_first_oc));
+                lanes_[l].center_ws = static_cast<float*>(dalloc(sizeof(float) * center_ws_floats));
+            }
         }
     }
 }
@@ -836,6 +841,8 @@ void Session::use_lane(int l, int stream_lane) {
     stream_ = lanes_[stream_lane < 0 ? l : stream_lane].stream;
     bn_part_ = lanes_[l].bn_part;
     wgrad_ws_ = lanes_[l].wgrad_ws;
+    tap_sums_ = lanes_[l].tap_sums;
+    center_ws_ = lanes_[l].center_ws;
 }
 
 void Session::refresh_head_weights() {

@@ -154,13 +154,15 @@ private:
     void backward_head(int batch);
     // The head's three pyramid levels are independent between the trunk and the loss (forward) and between
     // the loss and the parameter-gradient fold (backward): in TF32 mode, unprofiled, each level runs on its
-    // own stream with its own BatchNorm-partial and weight-gradient scratch, forked from and joined back to
+    // own stream with its own BatchNorm-partial, weight-gradient and centring scratch, forked from and joined back to
     // stream_ (inside the step's CUDA graph as well), so the small levels fill the SMs the large one leaves.
     struct LevelLane {
         cudaStream_t stream = nullptr;   // lane 0 is stream_
         float* bn_part = nullptr;
         float* wgrad_ws = nullptr;
         cudaEvent_t done = nullptr;
+        float* tap_sums = nullptr;    // the first convs' centred weight gradient (tap_border_sums)
+        float* center_ws = nullptr;
     };
     LevelLane lanes_[3];
     cudaEvent_t ev_fork_ = nullptr;
