@@ -1648,7 +1648,7 @@ void Session::wait_stream(const char* what) {
     using clock = std::chrono::steady_clock;
     const auto start = clock::now();
     const auto deadline = start + std::chrono::milliseconds(comm_timeout_ms_);
-    for (long polls = 0;; polls++) {
+    for (;;) {
         const cudaError_t e = cudaStreamQuery(stream_);
         if (e == cudaSuccess) return;
         if (e != cudaErrorNotReady) SY_CUDA(e);
@@ -1659,7 +1659,12 @@ void Session::wait_stream(const char* what) {
         if (clock::now() > deadline)
             abort_comm(std::string(what) + " did not complete within " + std::to_string(comm_timeout_ms_) +
                        " ms (a peer rank stopped or died)");
-        if (polls > 1000) std::this_thread::sleep_for(std::chrono::microseconds(50));
+        // a step's device work takes milliseconds: poll without sleeping for the first 50 ms (a sleep would
+        // add its own wake-up latency to every step), then every 50 us
+        if (clock::now() - start < std::chrono::milliseconds(50))
+            std::this_thread::yield();
+        else
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
 }
 
