@@ -193,52 +193,57 @@ struct StemParams {
     float b[OC];
 };
 
-// One thread per output pixel of the stem: 27 inputs (u8 / 255) x OC outputs, bias, SiLU.
+// One thread per output pixel of the stem: 27 inputs (u8 / 255) x OC outputs, bias, SiLU.  Grid (pixel
+// blocks of one image, images): the pixel's row and column come from a float reciprocal of the output width
+// (exact for fewer than 2^22 pixels an image) instead of 64-bit divisions, and each input row's address is
+// formed once.
 template <int OC>
-__global__ void __launch_bounds__(256) stem_conv_kernel(const uint8_t* rgb, int batch, int size,
-                                                        const StemParams<OC> sp, float* out, int out_pitch,
-                                                        Grid gout, PhaseOut phase, int has_phase, int rnd) {
+__global__ void __launch_bounds__(256) stem_conv_kernel(const uint8_t* rgb, int size, const StemParams<OC> sp,
+                                                        float* out, int out_pitch, Grid gout, PhaseOut phase,
+                                                        int has_phase, int rnd, float inv_wo) {
     const int ho = gout.h, wo = gout.w;
-    const long total = (long)batch * ho * wo;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const int b = (int)(i / ((long)ho * wo));
-        const int rem = (int)(i - (long)b * ho * wo);
-        const int oy = rem / wo, ox = rem - oy * wo;
-        float in[27];
+    const int rem = blockIdx.x * blockDim.x + threadIdx.x;
+    if (rem >= ho * wo) return;
+    const int b = blockIdx.y;
+    const int oy = __float2int_rd(((float)rem + 0.5f) * inv_wo), ox = rem - oy * wo;
+    float in[27];
 #pragma unroll
-        for (int ky = 0; ky < 3; ky++)
+    for (int ky = 0; ky < 3; ky++) {
+        const int iy = 2 * oy + ky - 1;
+        const bool row_ok = iy >= 0 && iy < size;
+        const uint8_t* rp = rgb + ((long)b * size + (row_ok ? iy : 0)) * size * 3;
 #pragma unroll
-            for (int kx = 0; kx < 3; kx++) {
-                const int iy = 2 * oy + ky - 1, ix = 2 * ox + kx - 1;
-                const bool ok = iy >= 0 && iy < size && ix >= 0 && ix < size;
-                const uint8_t* p = rgb + (((long)b * size + (ok ? iy : 0)) * size + (ok ? ix : 0)) * 3;
+        for (int kx = 0; kx < 3; kx++) {
+            const int ix = 2 * ox + kx - 1;
+            const bool ok = row_ok && ix >= 0 && ix < size;
+            const uint8_t* p = rp + (ok ? ix : 0) * 3;
 #pragma unroll
-                for (int c = 0; c < 3; c++) in[c * 9 + ky * 3 + kx] = ok ? byte_over_255(p[c]) : 0.0f;
-            }
-        float acc[OC];
-#pragma unroll
-        for (int o = 0; o < OC; o++) {
-            float s = 0.0f;
-#pragma unroll
-            for (int q = 0; q < 27; q++) s = fmaf(sp.w[o * 27 + q], in[q], s);
-            acc[o] = silu_f(s + sp.b[o]);
-            if (rnd) acc[o] = tf32_rna(acc[o]);
+            for (int c = 0; c < 3; c++) in[c * 9 + ky * 3 + kx] = ok ? byte_over_255(p[c]) : 0.0f;
         }
-        if (out) {
-            float* dst = out + ((long)b * gout.rows + gout.row(oy, ox)) * out_pitch;
+    }
+    float acc[OC];
 #pragma unroll
-            for (int o = 0; o < OC; o += 4)
-                *reinterpret_cast<float4*>(dst + o) = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
-        }
-        if (has_phase) {
-            const int py = oy + 1, px = ox + 1;
-            float* pd = phase.base + (((py & 1) * 2 + (px & 1)) * phase.plane_rows + (long)b * phase.consumer.rows +
-                                      (long)(py >> 1) * phase.consumer.wp + (px >> 1)) *
-                                         phase.pitch;
+    for (int o = 0; o < OC; o++) {
+        float s = 0.0f;
 #pragma unroll
-            for (int o = 0; o < OC; o += 4)
-                *reinterpret_cast<float4*>(pd + o) = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
-        }
+        for (int q = 0; q < 27; q++) s = fmaf(sp.w[o * 27 + q], in[q], s);
+        acc[o] = silu_fast(s + sp.b[o]);
+        if (rnd) acc[o] = tf32_rna(acc[o]);
+    }
+    if (out) {
+        float* dst = out + ((long)b * gout.rows + gout.row(oy, ox)) * out_pitch;
+#pragma unroll
+        for (int o = 0; o < OC; o += 4)
+            *reinterpret_cast<float4*>(dst + o) = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
+    }
+    if (has_phase) {
+        const int py = oy + 1, px = ox + 1;
+        float* pd = phase.base + (((py & 1) * 2 + (px & 1)) * phase.plane_rows + (long)b * phase.consumer.rows +
+                                  (long)(py >> 1) * phase.consumer.wp + (px >> 1)) *
+                                     phase.pitch;
+#pragma unroll
+        for (int o = 0; o < OC; o += 4)
+            *reinterpret_cast<float4*>(pd + o) = make_float4(acc[o], acc[o + 1], acc[o + 2], acc[o + 3]);
     }
 }
 
@@ -376,12 +381,13 @@ void upsample2_padded(const View& in, const Grid& gin, const View& out, const Gr
 
 template <int OC>
 static void launch_stem(const uint8_t* rgb, int batch, int size, const float* w_host, const float* b_host,
-                        const View& out, const Grid& gout, const PhaseOut& ph, int hp, int blocks, cudaStream_t stream,
-                        int rnd) {
+                        const View& out, const Grid& gout, const PhaseOut& ph, int hp, cudaStream_t stream, int rnd) {
     StemParams<OC> sp;
     for (int i = 0; i < OC * 27; i++) sp.w[i] = w_host[i];
     for (int i = 0; i < OC; i++) sp.b[i] = b_host[i];
-    stem_conv_kernel<OC><<<blocks, 256, 0, stream>>>(rgb, batch, size, sp, out.base, out.pitch, gout, ph, hp, rnd);
+    const dim3 grid((unsigned)((gout.h * gout.w + 255) / 256), (unsigned)batch);
+    stem_conv_kernel<OC><<<grid, 256, 0, stream>>>(rgb, size, sp, out.base, out.pitch, gout, ph, hp, rnd,
+                                                   1.0f / (float)gout.w);
 }
 
 void stem_conv(const uint8_t* rgb, int batch, int size, const float* w_host, const float* bias_host, int oc,
@@ -389,16 +395,15 @@ void stem_conv(const uint8_t* rgb, int batch, int size, const float* w_host, con
     if (out.pitch % 4 != 0 || (phase && phase->pitch % 4 != 0))
         throw std::runtime_error("stem_conv: pitches must be multiples of 4");
     if (!out.base && !phase) throw std::runtime_error("stem_conv: no output");
-    const long n = (long)batch * gout.h * gout.w;
-    const int blocks = (int)std::min<long>(148L * 8, std::max<long>(1, (n + 255) / 256));
+    if ((long)gout.h * gout.w >= (1L << 22) || batch > 65535) throw std::runtime_error("stem_conv: image too large");
     const PhaseOut ph = phase ? *phase : PhaseOut{};
     const int hp = phase ? 1 : 0;
     const int rnd = round_tf32 ? 1 : 0;
     switch (oc) {
-        case 16: launch_stem<16>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream, rnd); break;
-        case 32: launch_stem<32>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream, rnd); break;
-        case 48: launch_stem<48>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream, rnd); break;
-        case 64: launch_stem<64>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, blocks, stream, rnd); break;
+        case 16: launch_stem<16>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, stream, rnd); break;
+        case 32: launch_stem<32>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, stream, rnd); break;
+        case 48: launch_stem<48>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, stream, rnd); break;
+        case 64: launch_stem<64>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, stream, rnd); break;
         default: throw std::runtime_error("stem_conv: output channels must be 16, 32, 48 or 64");
     }
     launch_check("stem_conv_kernel");
