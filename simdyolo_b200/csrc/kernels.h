@@ -283,9 +283,18 @@ size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int topk, int
 // round_grad: the logit gradients are stored rounded to the nearest TF32 (operands of TF32 convs).
 // serial_cls: the per-image class loss is the reference's float running sum (one term at a time, in its
 // order) instead of the exact sum of the same terms (about 1e-3 apart at 640 x 640).
+// Class part on a second stream: with `split`, the class-logit BCE, its bias-gradient fold and the per-image
+// loss totals run on split->cls_stream once the assignment is done (event `assigned`), while `stream` goes on
+// with the box terms and their gradients and records `box`; `cls_done` is recorded on cls_stream after the
+// totals.  The caller orders later work on these events.
+struct LossSplit {
+    cudaStream_t cls_stream;
+    cudaEvent_t assigned, box, cls_done;
+};
 void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int bins, const TruthBox* truth,
                     const int* box_offsets, int max_boxes, int topk, int topk2, float grad_scale, int backward, void* workspace,
-                    const LossOut& out, cudaStream_t stream, bool round_grad = false, bool serial_cls = false);
+                    const LossOut& out, cudaStream_t stream, bool round_grad = false, bool serial_cls = false,
+                    const LossSplit* split = nullptr);
 
 // ---------------------------------------------------------------- inference post-processing (detect.cu)
 constexpr int kMaxDetectLevels = 8;

@@ -763,9 +763,14 @@ size_t loss_workspace_bytes(int batch, int anchors, int max_boxes, int topk, int
     return s;
 }
 
+static void split_check(cudaError_t e) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string("detection_loss: ") + cudaGetErrorString(e));
+}
+
 void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int bins, const TruthBox* truth,
                     const int* box_offsets, int max_boxes, int topk, int topk2, float grad_scale, int backward, void* workspace,
-                    const LossOut& out, cudaStream_t stream, bool round_grad, bool serial_cls) {
+                    const LossOut& out, cudaStream_t stream, bool round_grad, bool serial_cls, const LossSplit* split) {
+    if (split && serial_cls) throw std::runtime_error("detection_loss: the serial class sum runs on one stream");
     LossParams p;
     p.round_grad = round_grad ? 1 : 0;
     p.serial_cls = serial_cls ? 1 : 0;
@@ -833,6 +838,13 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
     if (owner_bytes > 160 * 1024) throw std::runtime_error("detection_loss: too many anchors");
     assign_kernel<<<batch, 256, owner_bytes, stream>>>(p);
     launch_check("assign_kernel");
+    // class part (BCE, class bias fold) on cls, box part on stream; one stream unless split
+    cudaStream_t cls = stream;
+    if (split) {
+        cls = split->cls_stream;
+        split_check(cudaEventRecord(split->assigned, stream));
+        split_check(cudaStreamWaitEvent(cls, split->assigned, 0));
+    }
     if (backward)
         for (int l = 0; l < nlevels; l++) {
             const LevelIO& L = levels[l];
@@ -840,14 +852,14 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
             cudaMemsetAsync(L.dbox, 0, (size_t)batch * L.grid.rows * L.box_pitch * sizeof(float), stream);
         }
     if (nc <= 96)
-        bce_kernel<3><<<dim3(kBceBlocks, batch), 256, 0, stream>>>(p, p.out.assigned, p.out.scores);
+        bce_kernel<3><<<dim3(kBceBlocks, batch), 256, 0, cls>>>(p, p.out.assigned, p.out.scores);
     else
-        bce_kernel<8><<<dim3(kBceBlocks, batch), 256, 0, stream>>>(p, p.out.assigned, p.out.scores);
+        bce_kernel<8><<<dim3(kBceBlocks, batch), 256, 0, cls>>>(p, p.out.assigned, p.out.scores);
     launch_check("bce_kernel");
     box_kernel<<<dim3((max_boxes * topk + 7) / 8 > 0 ? (max_boxes * topk + 7) / 8 : 1, batch), 256, 0, stream>>>(p);
     launch_check("box_kernel");
     if (cls_bias) {
-        cls_bias_fold_kernel<<<dim3((nc + 31) / 32, nlevels), 256, 0, stream>>>(p);
+        cls_bias_fold_kernel<<<dim3((nc + 31) / 32, nlevels), 256, 0, cls>>>(p);
         launch_check("cls_bias_fold_kernel");
     }
     if (box_bias) {
@@ -856,8 +868,14 @@ void detection_loss(const LevelIO* levels, int nlevels, int batch, int nc, int b
         box_bias_fold_kernel<<<dim3(1, nlevels), 64, 0, stream>>>(p);
         launch_check("box_bias_fold_kernel");
     }
-    finalize_kernel<<<batch, 32, 0, stream>>>(p);
+    if (split) {
+        // the per-image totals need both parts
+        split_check(cudaEventRecord(split->box, stream));
+        split_check(cudaStreamWaitEvent(cls, split->box, 0));
+    }
+    finalize_kernel<<<batch, 32, 0, cls>>>(p);
     launch_check("finalize_kernel");
+    if (split) split_check(cudaEventRecord(split->cls_done, cls));
     if (serial_cls) {
         const size_t smem = 2 * (size_t)kSerialChunk * nc * sizeof(float);
         if (smem > 48 * 1024) throw std::runtime_error("detection_loss: too many classes for the serial class sum");

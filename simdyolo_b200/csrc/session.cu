@@ -201,6 +201,9 @@ Session::~Session() {
         if (lanes_[l].done) cudaEventDestroy(lanes_[l].done);
     }
     if (ev_fork_) cudaEventDestroy(ev_fork_);
+    for (cudaEvent_t e : {ev_assigned_, ev_box_, ev_cls_})
+        if (e) cudaEventDestroy(e);
+    if (loss_stream_) cudaStreamDestroy(loss_stream_);
     for (cudaEvent_t e : ev_feat_)
         if (e) cudaEventDestroy(e);
     for (ImageSlot& sl : slots_) {
@@ -810,6 +813,9 @@ void Session::build_head() {
         if (feat_op_[0] >= 0 && feat_op_[1] >= 0)
             for (int l = 0; l < 2; l++) SY_CUDA(cudaEventCreateWithFlags(&ev_feat_[l], cudaEventDisableTiming));
         SY_CUDA(cudaEventCreateWithFlags(&lanes_[0].done, cudaEventDisableTiming));
+        SY_CUDA(cudaStreamCreateWithFlags(&loss_stream_, cudaStreamNonBlocking));
+        for (cudaEvent_t* e : {&ev_assigned_, &ev_box_, &ev_cls_})
+            SY_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
         for (int l = 1; l < 3; l++) {
             SY_CUDA(cudaStreamCreateWithFlags(&lanes_[l].stream, cudaStreamNonBlocking));
             SY_CUDA(cudaEventCreateWithFlags(&lanes_[l].done, cudaEventDisableTiming));
@@ -938,10 +944,17 @@ void Session::backward_head(int batch) {
         guard.restore = [this] { use_lane(0); };
         fork_levels();
     }
-    for (int l = 2; l >= 0; l--)
+    // per level: box branches first (their gradient comes from the loss's box part), then the class
+    // branches, which wait for the class part when it ran on its own stream
+    for (int l = 2; l >= 0; l--) {
+        bool cls_waited = false;
         for (int set = n_sets_ - 1; set >= 0; set--)
-            for (int kind = 1; kind >= 0; kind--) {
+            for (int kind = 0; kind <= 1; kind++) {
                 if (lanes) use_lane(l);
+                if (kind == 1 && cls_pending_ && !cls_waited) {
+                    SY_CUDA(cudaStreamWaitEvent(stream_, ev_cls_, 0));
+                    cls_waited = true;
+                }
                 Branch& branch = branches_[set * 6 + kind * 3 + l];
                 const Grid& g = levels_[l];
                 for (int i = (int)branch.blocks.size() - 1; i >= 0; i--) {
@@ -994,6 +1007,8 @@ void Session::backward_head(int batch) {
                     }
                 }
             }
+    }
+    cls_pending_ = false;
     if (lanes) join_levels();
     // BatchNorm gamma / beta gradients of every layer, images folded in order (deferred from the folds)
     if (n_bn_jobs_ > 0) bn_param_grad_batch(d_bn_jobs_, n_bn_jobs_, bn_max_c_, batch, stream_);
@@ -1019,6 +1034,8 @@ void Session::loss_weights(int epoch, float w[2]) const {
 void Session::launch_losses(int images, int backward, int epoch) {
     float w[2];
     loss_weights(epoch, w);
+    const bool split = level_lanes() && loss_stream_;
+    const LossSplit sp{loss_stream_, ev_assigned_, ev_box_, ev_cls_};
     for (int set = 0; set < n_sets_; set++) {
         LevelIO lv[3];
         for (int l = 0; l < 3; l++) {
@@ -1032,8 +1049,12 @@ void Session::launch_losses(int images, int backward, int epoch) {
                    nullptr, d_ties_ + (size_t)B_ * set};
         const int topk = set == 0 ? 10 : (progressive_ ? 7 : 1), topk2 = set == 0 ? 10 : 1;
         detection_loss(lv, 3, images, cfg.num_classes, cfg.reg_max, d_truth_, d_box_off_, std::max(1, cfg.max_boxes),
-                       topk, topk2, cfg.end_to_end ? w[set] : 1.0f, backward, loss_ws_, lo, stream_, rnd_, x3_);
+                       topk, topk2, cfg.end_to_end ? w[set] : 1.0f, backward, loss_ws_, lo, stream_, rnd_, x3_,
+                       split ? &sp : nullptr);
+        // the next set reuses the workspace; without a backward nothing else waits for the class part
+        if (split && (set + 1 < n_sets_ || !backward)) SY_CUDA(cudaStreamWaitEvent(stream_, ev_cls_, 0));
     }
+    cls_pending_ = split && backward;
 }
 
 // Per image the reported parts are a.Part * w0 + b.Part * w1 in float (DetectionHead.cs:114), summed

@@ -172,6 +172,12 @@ private:
     int feat_op_[3] = {-1, -1, -1};   // index in bops_ of the last op writing features_[l]
     cudaEvent_t ev_feat_[2] = {nullptr, nullptr};
     bool feat_events_ = false;        // ev_feat_ recorded by the trunk pass the next forward_head follows
+    // The loss's class part (BCE, class-bias fold, per-image totals) runs on loss_stream_ beside its box part;
+    // the backward starts the box branches after the box part and each level's class branches after
+    // ev_cls_ (cls_pending_: the last launch_losses left that wait to the backward).
+    cudaStream_t loss_stream_ = nullptr;
+    cudaEvent_t ev_assigned_ = nullptr, ev_box_ = nullptr, ev_cls_ = nullptr;
+    bool cls_pending_ = false;
     bool level_lanes() const { return lanes_[1].stream != nullptr && !x3_ && !prof_; }
     void fork_levels();
     void join_levels();
