@@ -182,8 +182,9 @@ void rgb_to_phase(const uint8_t* rgb, int batch, int size, const PhaseOut& dst, 
 // Stem of the trunk straight from RGB24: 3x3 stride-2 conv, 3 -> oc (<= 64) channels, folded-BN bias
 // and SiLU, on CUDA cores (27 MACs per output channel is too narrow for the tensor cores).  Writes the
 // padded output (skipped when out.base is null) and, when `phase` is given, its parity-split copy.
-// w_host / bias_host: HOST copies, OIHW [oc][3][3][3] (they travel as kernel parameters).
-void stem_conv(const uint8_t* rgb, int batch, int size, const float* w_host, const float* bias_host, int oc,
+// w_host / bias_host: HOST copies, OIHW [oc][3][3][3] (they travel as kernel parameters).  rgb_ref: DEVICE
+// memory holding the address of the device images (read by the kernel, so a captured launch serves any buffer).
+void stem_conv(const uint8_t* const* rgb_ref, int batch, int size, const float* w_host, const float* bias_host, int oc,
                const View& out, const Grid& gout, const PhaseOut* phase, cudaStream_t stream, bool round_tf32 = false);
 // OIHW -> [oc][t][kpad] (forward) and OIHW -> [ic][t][kpad_o] (data gradient)
 void weights_fwd_layout(const float* oihw, int oc, int ic, int taps, int kpad, float* dst, cudaStream_t stream,

@@ -198,9 +198,10 @@ struct StemParams {
 // (exact for fewer than 2^22 pixels an image) instead of 64-bit divisions, and each input row's address is
 // formed once.
 template <int OC>
-__global__ void __launch_bounds__(256) stem_conv_kernel(const uint8_t* rgb, int size, const StemParams<OC> sp,
-                                                        float* out, int out_pitch, Grid gout, PhaseOut phase,
-                                                        int has_phase, int rnd, float inv_wo) {
+__global__ void __launch_bounds__(256) stem_conv_kernel(const uint8_t* const* rgb_ref, int size,
+                                                        const StemParams<OC> sp, float* out, int out_pitch, Grid gout,
+                                                        PhaseOut phase, int has_phase, int rnd, float inv_wo) {
+    const uint8_t* const rgb = *rgb_ref;
     const int ho = gout.h, wo = gout.w;
     const int rem = blockIdx.x * blockDim.x + threadIdx.x;
     if (rem >= ho * wo) return;
@@ -380,17 +381,17 @@ void upsample2_padded(const View& in, const Grid& gin, const View& out, const Gr
 }
 
 template <int OC>
-static void launch_stem(const uint8_t* rgb, int batch, int size, const float* w_host, const float* b_host,
+static void launch_stem(const uint8_t* const* rgb_ref, int batch, int size, const float* w_host, const float* b_host,
                         const View& out, const Grid& gout, const PhaseOut& ph, int hp, cudaStream_t stream, int rnd) {
     StemParams<OC> sp;
     for (int i = 0; i < OC * 27; i++) sp.w[i] = w_host[i];
     for (int i = 0; i < OC; i++) sp.b[i] = b_host[i];
     const dim3 grid((unsigned)((gout.h * gout.w + 255) / 256), (unsigned)batch);
-    stem_conv_kernel<OC><<<grid, 256, 0, stream>>>(rgb, size, sp, out.base, out.pitch, gout, ph, hp, rnd,
+    stem_conv_kernel<OC><<<grid, 256, 0, stream>>>(rgb_ref, size, sp, out.base, out.pitch, gout, ph, hp, rnd,
                                                    1.0f / (float)gout.w);
 }
 
-void stem_conv(const uint8_t* rgb, int batch, int size, const float* w_host, const float* bias_host, int oc,
+void stem_conv(const uint8_t* const* rgb_ref, int batch, int size, const float* w_host, const float* bias_host, int oc,
                const View& out, const Grid& gout, const PhaseOut* phase, cudaStream_t stream, bool round_tf32) {
     if (out.pitch % 4 != 0 || (phase && phase->pitch % 4 != 0))
         throw std::runtime_error("stem_conv: pitches must be multiples of 4");
@@ -400,10 +401,10 @@ void stem_conv(const uint8_t* rgb, int batch, int size, const float* w_host, con
     const int hp = phase ? 1 : 0;
     const int rnd = round_tf32 ? 1 : 0;
     switch (oc) {
-        case 16: launch_stem<16>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, stream, rnd); break;
-        case 32: launch_stem<32>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, stream, rnd); break;
-        case 48: launch_stem<48>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, stream, rnd); break;
-        case 64: launch_stem<64>(rgb, batch, size, w_host, bias_host, out, gout, ph, hp, stream, rnd); break;
+        case 16: launch_stem<16>(rgb_ref, batch, size, w_host, bias_host, out, gout, ph, hp, stream, rnd); break;
+        case 32: launch_stem<32>(rgb_ref, batch, size, w_host, bias_host, out, gout, ph, hp, stream, rnd); break;
+        case 48: launch_stem<48>(rgb_ref, batch, size, w_host, bias_host, out, gout, ph, hp, stream, rnd); break;
+        case 64: launch_stem<64>(rgb_ref, batch, size, w_host, bias_host, out, gout, ph, hp, stream, rnd); break;
         default: throw std::runtime_error("stem_conv: output channels must be 16, 32, 48 or 64");
     }
     launch_check("stem_conv_kernel");

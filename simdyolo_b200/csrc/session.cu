@@ -161,6 +161,8 @@ Session::Session(const sy_config& c) : cfg(c) {
     SY_CUDA(cudaMallocHost(&h_flags_, sizeof(int) * 16));
     SY_CUDA(cudaMallocHost(&h_rec_, sizeof(float) * (size_t)head_floats_ * c.world_size));
     SY_CUDA(cudaMallocHost(&h_images_, sizeof(int) * 4));
+    SY_CUDA(cudaMallocHost(&h_rgb_ref_, sizeof(void*)));
+    d_rgb_ref_ = static_cast<const uint8_t**>(dalloc(sizeof(void*)));
     SY_CUDA(cudaMallocHost(&h_abs_, sizeof(double) * kAbsSumBlocks));
     if (c.backbone != SY_BACKBONE_NONE) {
         SY_CUDA(cudaMallocHost(&h_rgb_, (size_t)B_ * c.image_size * c.image_size * 3));
@@ -190,7 +192,7 @@ Session::~Session() {
     for (void* p : allocations_) cudaFree(p);
     if (det_ws_) cudaFree(det_ws_);
     if (det_out_) cudaFree(det_out_);
-    for (void* p : {(void*)h_truth_, (void*)h_box_off_, (void*)h_flags_, (void*)h_rec_, (void*)h_images_,
+    for (void* p : {(void*)h_truth_, (void*)h_box_off_, (void*)h_flags_, (void*)h_rec_, (void*)h_images_, (void*)h_rgb_ref_,
                     (void*)h_abs_, (void*)h_rgb_})
         if (p) cudaFreeHost(p);
     if (ev0_) cudaEventDestroy(ev0_);
@@ -538,14 +540,14 @@ int Session::set_backbone(const float* host, long count) {
     return SY_OK;
 }
 
-void Session::forward_backbone(int batch, const uint8_t* rgb_device) {
+void Session::forward_backbone(int batch) {
     const bool events = level_lanes() && ev_feat_[0];
     for (int i = 0; i < (int)bops_.size(); i++) {
         const BackboneOp& op = bops_[i];
         View in = op.in, out = op.out;
         if (op.type == 0 && !op.plain_out) out.base = nullptr;
         if (op.type == 0 && in.base == img_.base) {
-            stem_conv(rgb_device, batch, cfg.image_size, stem_host_.data(), stem_host_.data() + (long)op.oc * op.ic * 9,
+            stem_conv(d_rgb_ref_, batch, cfg.image_size, stem_host_.data(), stem_host_.data() + (long)op.oc * op.ic * 9,
                       op.oc, out, op.gout, op.has_phase_out ? &op.phase_out : nullptr, stream_, rnd_);
         } else if (op.type == 1) {
             maxpool5_padded(in, out, batch, op.gin, stream_);
@@ -1137,6 +1139,32 @@ void Session::prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float
     }
     if (rgb && (cfg.backbone == SY_BACKBONE_NONE || !backbone_ready_))
         throw SyError(SY_ERR_INVALID_ARGUMENT, "backbone weights not set");
+    // where this step's images come from: the caller's device buffer, a prefetched copy, or a copy made now
+    // (pinned caller memory directly, pageable memory through pinned staging)
+    const size_t bytes = rgb ? (size_t)images * cfg.image_size * cfg.image_size * 3 : 0;
+    const uint8_t* src = nullptr;
+    ImageSlot* slot = nullptr;
+    bool copy_now = false;
+    if (rgb) {
+        if (!rgb_on_device)
+            for (ImageSlot& sl : slots_)
+                if (sl.ready && sl.host == rgb && sl.images == images) slot = &sl;
+        if (rgb_on_device) {
+            src = rgb;
+        } else if (slot) {
+            src = slot->dev;
+        } else {
+            cudaPointerAttributes attr;
+            const bool pinned = cudaPointerGetAttributes(&attr, rgb) == cudaSuccess && attr.type == cudaMemoryTypeHost;
+            cudaGetLastError();
+            if (!pinned) {
+                std::memcpy(h_rgb_, rgb, bytes);
+                rgb = h_rgb_;
+            }
+            src = d_rgb_;
+            copy_now = true;
+        }
+    }
     prof_n_ = 0;
     SY_CUDA(cudaEventRecord(ev0_, stream_));
     if (k > 0)
@@ -1145,41 +1173,26 @@ void Session::prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float
     SY_CUDA(cudaMemsetAsync(d_flags_, 0, sizeof(int) * 16, stream_));
     h_images_[0] = images;
     SY_CUDA(cudaMemcpyAsync(d_images_, h_images_, sizeof(int), cudaMemcpyHostToDevice, stream_));
+    if (rgb) {
+        *h_rgb_ref_ = src;
+        SY_CUDA(cudaMemcpyAsync(d_rgb_ref_, h_rgb_ref_, sizeof(void*), cudaMemcpyHostToDevice, stream_));
+    }
     if (copy_stream_) SY_CUDA(cudaEventRecord(ev_uploaded_, stream_));
     if (rgb) {
-        const size_t bytes = (size_t)images * cfg.image_size * cfg.image_size * 3;
-        const uint8_t* src = d_rgb_;
-        ImageSlot* slot = nullptr;
-        if (!rgb_on_device)
-            for (ImageSlot& sl : slots_)
-                if (sl.ready && sl.host == rgb && sl.images == images) slot = &sl;
-        if (rgb_on_device) {
-            src = rgb;
-        } else if (slot) {
+        if (slot) {
             // prefetched: the compute stream waits for the copy stream's copy of this batch
             issue_prefetch(*slot);
             SY_CUDA(cudaStreamWaitEvent(stream_, slot->copied, 0));
             slot->ready = false;
             consuming_ = slot;
-            src = slot->dev;
-        } else {
-            // pinned caller memory is copied directly; pageable memory goes through pinned staging
-            cudaPointerAttributes attr;
-            const bool pinned = cudaPointerGetAttributes(&attr, rgb) == cudaSuccess && attr.type == cudaMemoryTypeHost;
-            cudaGetLastError();
-            if (!pinned) {
-                std::memcpy(h_rgb_, rgb, bytes);
-                rgb = h_rgb_;
-            }
+        } else if (copy_now) {
             SY_CUDA(cudaMemcpyAsync(d_rgb_, rgb, bytes, cudaMemcpyHostToDevice, stream_));
         }
-        rgb_src_ = src;
         // the copies of batches prefetched for later calls start now, behind this call's uploads
         for (ImageSlot& sl : slots_)
             if (sl.pending) issue_prefetch(sl);
-        if (!defer_backbone) forward_backbone(images, src);
+        if (!defer_backbone) forward_backbone(images);
     } else {
-        rgb_src_ = nullptr;
         if (!features) throw SyError(SY_ERR_INVALID_ARGUMENT, "features missing");
         for (int l = 0; l < 3; l++) {
             const Grid& g = levels_[l];
@@ -1196,7 +1209,7 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
     prepare_inputs(rgb, rgb_on_device, features, boxes, counts, images, graph);
     const bool trunk = rgb != nullptr;
     auto device_work = [&] {
-        if (graph && trunk) forward_backbone(images, rgb_src_);
+        if (graph && trunk) forward_backbone(images);
         forward_head(images);
         launch_losses(images, 1, epoch_);
         backward_head(images);
@@ -1206,7 +1219,8 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
     } else {
         float w[2];
         loss_weights(epoch_, w);
-        const GraphKey key{images, trunk ? (const void*)rgb_src_ : nullptr, w[0], w[1]};
+        // the stem reads the image address from d_rgb_ref_: one graph for every image buffer
+        const GraphKey key{images, trunk ? (const void*)d_rgb_ref_ : nullptr, w[0], w[1]};
         auto it = graphs_.find(key);
         if (it == graphs_.end() && graph_seen_[key]++ > 0 && graphs_.size() < 16) {
             cudaGraph_t g = nullptr;

@@ -138,7 +138,7 @@ private:
     void tk_upsample(const View& in, const Grid& gin, const View& out, const Grid& gout);
     long tk_poff_ = 0;
     void build_head();
-    void forward_backbone(int batch, const uint8_t* rgb_device);
+    void forward_backbone(int batch);   // stem input: the images at *d_rgb_ref_
     void prepare_inputs(const uint8_t* rgb, bool rgb_on_device, const float* const* features, const sy_box* boxes,
                         const int32_t* counts, int images, bool defer_backbone = false);
     void forward_head(int batch, bool training = true);
@@ -250,6 +250,10 @@ private:
     float* h_rec_ = nullptr;
     int* h_images_ = nullptr;
     int* d_images_ = nullptr;
+    // the current step's device image address, uploaded with the step's other small inputs: the stem reads
+    // it from device memory, so one captured graph serves every image buffer
+    const uint8_t** h_rgb_ref_ = nullptr;
+    const uint8_t** d_rgb_ref_ = nullptr;
     int* d_ties_ = nullptr;
     int comm_timeout_ms_ = 300000;
     float* d_loss_ = nullptr;
@@ -273,7 +277,6 @@ private:
     std::map<GraphKey, cudaGraphExec_t> graphs_;
     std::map<GraphKey, int> graph_seen_;
     bool use_graphs_ = true;
-    const uint8_t* rgb_src_ = nullptr;   // device images of the current step (deferred trunk forward)
     void clear_graphs();
     int last_batch_ = 0;
     // 3xTF32 operand split scratch: activations (4 buffers) and weights (2 buffers)

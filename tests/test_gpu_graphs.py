@@ -49,3 +49,38 @@ def test_graph_replay_is_bit_identical_to_eager_steps(backbone):
     assert eager[0] == graph[0]
     for a, b in zip(eager[1:], graph[1:]):
         assert a.tobytes() == b.tobytes()
+
+
+def run_rotating(graphs: bool, buffers=3, steps=7):
+    """Steps over several device image buffers in turn (a data loader's batches): the graph captured on
+    one buffer replays on the others, since the stem reads the image address from device memory."""
+    old = os.environ.get("SIMDYOLO_CUDA_GRAPHS")
+    os.environ["SIMDYOLO_CUDA_GRAPHS"] = "1" if graphs else "0"
+    try:
+        cfg = sy.make_config("yolov8n", image_size=128, max_batch=3, max_boxes=6)
+        s = sy.Session(cfg)
+    finally:
+        if old is None:
+            del os.environ["SIMDYOLO_CUDA_GRAPHS"]
+        else:
+            os.environ["SIMDYOLO_CUDA_GRAPHS"] = old
+    params, buffers_ = data.head_params(s, 5)
+    s.set_flat_params(params)
+    s.set_flat_buffers(buffers_)
+    s.set_backbone(data.backbone_params("yolov8n", 1))
+    rng = np.random.default_rng(21)
+    batches = [data.synthetic_batch(rng, 3, 128, 80, (1, 5), (8.0, 64.0)) for _ in range(buffers)]
+    devs = [torch.from_numpy(imgs).cuda() for imgs, _ in batches]
+    out = []
+    for i in range(steps):
+        st = s.step_device(devs[i % buffers].data_ptr(), 3, batches[i % buffers][1])
+        out.append((st.box, st.cls, st.dfl, st.positives))
+    return out, s.flat_params(), s.flat_buffers(), s.flat_velocity()
+
+
+def test_graph_replays_on_other_image_buffers_bit_identically():
+    eager = run_rotating(False)
+    graph = run_rotating(True)
+    assert eager[0] == graph[0]
+    for a, b in zip(eager[1:], graph[1:]):
+        assert a.tobytes() == b.tobytes()
