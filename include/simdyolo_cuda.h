@@ -321,7 +321,8 @@ SY_API sy_status sy_cuda_conv2d_backward_filter_static(int32_t device, const flo
 SY_API sy_status sy_cuda_matmul(int32_t device, const float *a, const float *b, float *c, int32_t m, int32_t n, int32_t k);
 
 /* Measurement helpers (no counterpart in the reference, which times with Stopwatch).
- * sy_cuda_launch_count: kernels this library has launched in the process so far.
+ * sy_cuda_launch_count: kernels this library has launched in the process so far (a CUDA graph replay
+ * counts every kernel node of the graph).
  * sy_cuda_bench_conv: device time in ms per launch (CUDA events, `iters` back-to-back launches after
  * one warm-up) of one convolution pass on device-resident data: kind 0 forward, 1 data gradient,
  * 2 weight gradient; shapes as in sy_cuda_conv2d_*. */

@@ -43,6 +43,8 @@ void set_max_dynamic_smem(K* kernel, int bytes, const char* what) {
     if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 long long launch_count();
+// Kernels run by a CUDA graph replay (counted once at capture, so replays add their node count).
+void add_launches(long long n);
 
 // ---------------------------------------------------------------- tensor views
 // A channels-last activation view: `base` points at channel 0 of the view in row 0,

@@ -306,6 +306,7 @@ void launch_check(const char* what) {
 }
 
 long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
+void add_launches(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 void nchw_to_padded(const float* src, int batch, int c, const Grid& g, const View& dst, cudaStream_t stream,
                     bool round_tf32) {

@@ -183,6 +183,7 @@ void Session::clear_graphs() {
     for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
     graphs_.clear();
     graph_seen_.clear();
+    graph_nodes_.clear();
 }
 
 Session::~Session() {
@@ -1222,8 +1223,10 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
         // the stem reads the image address from d_rgb_ref_: one graph for every image buffer
         const GraphKey key{images, trunk ? (const void*)d_rgb_ref_ : nullptr, w[0], w[1]};
         auto it = graphs_.find(key);
+        bool captured = false;
         if (it == graphs_.end() && graph_seen_[key]++ > 0 && graphs_.size() < 16) {
             cudaGraph_t g = nullptr;
+            const long long launches0 = launch_count();
             SY_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
             try {
                 device_work();
@@ -1238,11 +1241,16 @@ int Session::step(const uint8_t* rgb, bool rgb_on_device, const float* const* fe
             cudaGraphDestroy(g);
             SY_CUDA(e);
             it = graphs_.emplace(key, exec).first;
+            // the capture counted the graph's kernel nodes once (launch_count): replays add them again
+            graph_nodes_[key] = launch_count() - launches0;
+            captured = true;
         }
-        if (it != graphs_.end())
+        if (it != graphs_.end()) {
             SY_CUDA(cudaGraphLaunch(it->second, stream_));
-        else
+            if (!captured) add_launches(graph_nodes_[key]);
+        } else {
             device_work();
+        }
     }
     release_images();
     // Data-parallel exchange, all enqueued before one host wait: the gradient bucket summed over ranks

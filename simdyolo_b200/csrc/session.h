@@ -276,6 +276,7 @@ private:
     using GraphKey = std::tuple<int, const void*, float, float>;
     std::map<GraphKey, cudaGraphExec_t> graphs_;
     std::map<GraphKey, int> graph_seen_;
+    std::map<GraphKey, long long> graph_nodes_;   // kernel launches inside each graph
     bool use_graphs_ = true;
     void clear_graphs();
     int last_batch_ = 0;

@@ -84,3 +84,24 @@ def test_graph_replays_on_other_image_buffers_bit_identically():
     assert eager[0] == graph[0]
     for a, b in zip(eager[1:], graph[1:]):
         assert a.tobytes() == b.tobytes()
+
+
+def test_launch_count_includes_graph_replays():
+    """sy_cuda_launch_count counts the kernels a replayed graph runs, so a replayed step adds as many
+    launches as the eager step it was captured from."""
+    cfg = sy.make_config("yolov8n", image_size=128, max_batch=3, max_boxes=6)
+    s = sy.Session(cfg)
+    params, buffers = data.head_params(s, 5)
+    s.set_flat_params(params)
+    s.set_flat_buffers(buffers)
+    s.set_backbone(data.backbone_params("yolov8n", 1))
+    rng = np.random.default_rng(4)
+    imgs, truth = data.synthetic_batch(rng, 3, 128, 80, (1, 5), (8.0, 64.0))
+    dev = torch.from_numpy(imgs).cuda()
+    deltas = []
+    for _ in range(4):   # eager, capture + launch, replay, replay
+        n0 = sy.launch_count()
+        s.step_device(dev.data_ptr(), 3, truth)
+        deltas.append(sy.launch_count() - n0)
+    assert deltas[0] > 100
+    assert deltas[1] == deltas[2] == deltas[3] == deltas[0]
