@@ -188,6 +188,10 @@ void rgb_to_phase(const uint8_t* rgb, int batch, int size, const PhaseOut& dst, 
 // memory holding the address of the device images (read by the kernel, so a captured launch serves any buffer).
 void stem_conv(const uint8_t* const* rgb_ref, int batch, int size, const float* w_host, const float* bias_host, int oc,
                const View& out, const Grid& gout, const PhaseOut* phase, cudaStream_t stream, bool round_tf32 = false);
+// Grouped conv weights [oc][ic / groups][taps] to block-diagonal dense [oc][ic][taps] (zeros between the
+// groups), and the diagonal blocks of a dense [oc][ic][taps] weight gradient back to the grouped layout.
+void grouped_to_dense(const float* w, int oc, int ic, int groups, int taps, float* dense, cudaStream_t stream);
+void dense_to_grouped(const float* dense, int oc, int ic, int groups, int taps, float* w, cudaStream_t stream);
 // OIHW -> [oc][t][kpad] (forward) and OIHW -> [ic][t][kpad_o] (data gradient)
 void weights_fwd_layout(const float* oihw, int oc, int ic, int taps, int kpad, float* dst, cudaStream_t stream,
                         bool round_tf32 = false);

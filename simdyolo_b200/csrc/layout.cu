@@ -305,6 +305,31 @@ void launch_check(const char* what) {
     if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+// Grouped conv weights [oc][ic / groups][taps] <-> block-diagonal dense [oc][ic][taps]: output channel o
+// belongs to group o / (oc / groups), which reads input channels [g ic / groups, (g + 1) ic / groups).
+__global__ void grouped_to_dense_kernel(const float* w, int oc, int ic, int groups, int taps, float* dense) {
+    const int icg = ic / groups, ocg = oc / groups;
+    const long total = (long)oc * ic * taps;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int t = (int)(i % taps);
+        const long oc_c = i / taps;
+        const int c = (int)(oc_c % ic), o = (int)(oc_c / ic);
+        const int g = o / ocg;
+        dense[i] = (c / icg == g) ? w[((long)o * icg + (c - g * icg)) * taps + t] : 0.0f;
+    }
+}
+
+__global__ void dense_to_grouped_kernel(const float* dense, int oc, int ic, int groups, int taps, float* w) {
+    const int icg = ic / groups, ocg = oc / groups;
+    const long total = (long)oc * icg * taps;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int t = (int)(i % taps);
+        const long o_cl = i / taps;
+        const int cl = (int)(o_cl % icg), o = (int)(o_cl / icg);
+        w[i] = dense[((long)o * ic + (o / ocg) * icg + cl) * taps + t];
+    }
+}
+
 long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 void add_launches(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
@@ -439,6 +464,20 @@ void rgb_to_phase(const uint8_t* rgb, int batch, int size, const PhaseOut& dst, 
     const long n = (long)batch * size * size;
     rgb_to_phase_kernel<<<blocks_for(n), 256, 0, stream>>>(rgb, batch, size, dst);
     launch_check("rgb_to_phase_kernel");
+}
+
+void grouped_to_dense(const float* w, int oc, int ic, int groups, int taps, float* dense, cudaStream_t stream) {
+    const long total = (long)oc * ic * taps;
+    grouped_to_dense_kernel<<<(int)std::min<long>(148L * 8, (total + 255) / 256), 256, 0, stream>>>(w, oc, ic, groups,
+                                                                                                 taps, dense);
+    launch_check("grouped_to_dense_kernel");
+}
+
+void dense_to_grouped(const float* dense, int oc, int ic, int groups, int taps, float* w, cudaStream_t stream) {
+    const long total = (long)oc * (ic / groups) * taps;
+    dense_to_grouped_kernel<<<(int)std::min<long>(148L * 8, (total + 255) / 256), 256, 0, stream>>>(dense, oc, ic,
+                                                                                                 groups, taps, w);
+    launch_check("dense_to_grouped_kernel");
 }
 
 }  // namespace sy

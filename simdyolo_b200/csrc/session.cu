@@ -632,12 +632,13 @@ void Session::build_head() {
             HeadBlock hb;
             hb.b = blocks[i];
             const sy_block& b = hb.b;
-            hb.dw = b.groups > 1;
-            if (b.ic != ic || b.oc < 1 || b.oc > 512 || !(b.k == 1 || b.k == 3) ||
-                !(b.groups == 1 || (b.groups == b.ic && b.ic == b.oc)) || (b.groups == 1 && b.oc > 256))
+            hb.dw = b.groups > 1 && b.groups == b.ic && b.ic == b.oc;
+            hb.grouped = b.groups > 1 && !hb.dw;
+            if (b.ic != ic || b.oc < 1 || b.oc > 512 || !(b.k == 1 || b.k == 3) || b.groups < 1 ||
+                b.ic % b.groups != 0 || b.oc % b.groups != 0 || (!hb.dw && b.oc > 256))
                 throw SyError(SY_ERR_UNSUPPORTED_SHAPE,
-                              "head conv must be k 1 or 3, groups 1 (<= 256 channels) or depthwise (groups = channels "
-                              "<= 512), chained channels (" + prefix + ")");
+                              "head conv must be k 1 or 3 with groups dividing both channel counts, at most 256 output "
+                              "channels (depthwise, groups = channels: 512), chained channels (" + prefix + ")");
             if (hb.dw && (b.has_bias || b.oc % 4 != 0))
                 throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "depthwise head convs need BatchNorm and a multiple of 4 channels");
             if ((i == n - 1) == (b.has_bn != 0)) throw SyError(SY_ERR_UNSUPPORTED_SHAPE, "only the last block is a Conv2d");
@@ -742,6 +743,10 @@ void Session::build_head() {
                 hb.kpad_out = round_up(b.oc, 32);
                 hb.w_fwd = static_cast<float*>(dalloc(sizeof(float) * (size_t)b.oc * hb.taps * hb.kpad_in));
                 hb.w_dgrad = static_cast<float*>(dalloc(sizeof(float) * (size_t)b.ic * hb.taps * hb.kpad_out));
+                if (hb.grouped) {
+                    hb.w_dense = static_cast<float*>(dalloc(sizeof(float) * (size_t)b.oc * b.ic * hb.taps));
+                    hb.wg_dense = static_cast<float*>(dalloc(sizeof(float) * (size_t)b.oc * b.ic * hb.taps));
+                }
                 wsp_floats_ = std::max(wsp_floats_, std::max((size_t)b.oc * hb.taps * hb.kpad_in,
                                                              (size_t)b.ic * hb.taps * hb.kpad_out));
                 ws = std::max(ws, wgrad_workspace_floats(b.ic, b.oc, hb.taps, (long)B_ * g.rows));
@@ -862,8 +867,8 @@ void Session::refresh_head_weights() {
         for (auto& branch : branches_)
             for (auto& hb : branch.blocks) {
                 if (hb.dw) continue;
-                jobs.push_back(WeightLayoutJob{params_ + hb.w_off, hb.b.oc, hb.b.ic, hb.taps, hb.kpad_in, hb.kpad_out,
-                                               hb.w_fwd, hb.w_dgrad});
+                jobs.push_back(WeightLayoutJob{hb.grouped ? hb.w_dense : params_ + hb.w_off, hb.b.oc, hb.b.ic, hb.taps,
+                                               hb.kpad_in, hb.kpad_out, hb.w_fwd, hb.w_dgrad});
                 layout_max_elems_ = std::max(layout_max_elems_, (long)hb.taps * (hb.b.oc * hb.kpad_in +
                                                                                   hb.b.ic * hb.kpad_out));
             }
@@ -872,6 +877,10 @@ void Session::refresh_head_weights() {
         d_layout_jobs_ = static_cast<WeightLayoutJob*>(dalloc(sizeof(WeightLayoutJob) * jobs.size()));
         SY_CUDA(cudaMemcpy(d_layout_jobs_, jobs.data(), sizeof(WeightLayoutJob) * jobs.size(), cudaMemcpyHostToDevice));
     }
+    for (auto& branch : branches_)
+        for (auto& hb : branch.blocks)
+            if (hb.grouped)
+                grouped_to_dense(params_ + hb.w_off, hb.b.oc, hb.b.ic, hb.b.groups, hb.taps, hb.w_dense, stream_);
     if (n_layout_jobs_ > 0) weights_layout_batch(d_layout_jobs_, n_layout_jobs_, layout_max_elems_, stream_, rnd_);
 }
 
@@ -980,10 +989,13 @@ void Session::backward_head(int batch) {
                                         tap_sums_, stream_);
                         const WgradCenter center{feat_mean_[l], tap_sums_, batch};
                         conv_wgrad(rows_of(feat_c_[l], batch, g), rows_of(hb.dy, batch, g), hb.taps, g,
-                                   grads_ + hb.w_off, &center);
+                                   hb.grouped ? hb.wg_dense : grads_ + hb.w_off, &center);
                     } else {
-                        conv_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g, grads_ + hb.w_off);
+                        conv_wgrad(rows_of(hb.x, batch, g), rows_of(hb.dy, batch, g), hb.taps, g,
+                                   hb.grouped ? hb.wg_dense : grads_ + hb.w_off);
                     }
+                    if (hb.grouped)
+                        dense_to_grouped(hb.wg_dense, hb.b.oc, hb.b.ic, hb.b.groups, hb.taps, grads_ + hb.w_off, stream_);
                     if (i > 0) {
                         HeadBlock& prev = branch.blocks[i - 1];
                         ConvEpilogue ep;

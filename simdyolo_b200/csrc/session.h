@@ -37,6 +37,11 @@ struct HeadBlock {
     sy_block b;
     int taps;
     bool dw = false;            // depthwise (groups = channels): CUDA-core kernels, weights [c][taps]
+    // other group counts: the tensor-core conv with block-diagonal dense weights (zeros between the groups);
+    // the weight gradient is computed dense and its diagonal blocks are the parameter gradient
+    bool grouped = false;
+    float* w_dense = nullptr;   // [oc][ic][taps], refreshed from the [oc][ic / groups][taps] parameters
+    float* wg_dense = nullptr;  // dense weight gradient [oc][ic][taps]
     long w_off = -1, b_off = -1, g_off = -1, be_off = -1;
     long rm_off = -1, rv_off = -1, nt_off = -1;
     float* w_fwd = nullptr;     // [oc][taps][kpad_in]
