@@ -50,7 +50,9 @@ typedef struct sy_box {
 
 /* One block of a head branch (DetectionHead.cs:28-75, validated like TrainingHeadSchema.cs:36-46):
  * Conv/DWConv (has_bn = 1: conv without bias -> BatchNorm -> SiLU) or the final Conv2d
- * (has_bn = 0, has_bias = 1).  Kernel 1 or 3, stride 1, same padding. */
+ * (has_bn = 0, has_bias = 1).  Kernel 1 or 3, stride 1, same padding.  groups must divide ic and oc:
+ * groups = ic = oc is depthwise (up to 512 channels, BatchNorm, a multiple of 4 channels); other convs have
+ * at most 256 output channels.  Anything else is SY_ERR_UNSUPPORTED_SHAPE at sy_cuda_create. */
 typedef struct sy_block {
     int32_t ic, oc, k, groups, has_bn, has_bias;
 } sy_block;
