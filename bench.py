@@ -8,9 +8,10 @@ DFL + CIoU + BCE loss with the task-aligned assigner, NCCL all-reduce (N > 1) an
   python bench.py [--gpus N --steps K --warmup W]            this implementation (CUDA, sm_100a)
   python bench.py --impl reference [...]                     the reference's CPU algorithm
 
-Prints ONE JSON line on rank 0.  `value` times the step with the images already resident in HBM;
-`e2e` times the public C-ABI call with pinned host images (host->device copy and the result read
-inside every step).  Both are device times from CUDA events, max over ranks.
+Prints ONE JSON line on rank 0.  `value` times the step with the images already resident in HBM (CUDA
+events around each step's device work, summed, max over ranks); `e2e` times the public C-ABI call with
+pinned host images (every batch's host->device copy and the result read inside the loop) on the host clock
+around the whole loop, max over ranks.
 """
 from __future__ import annotations
 
@@ -93,7 +94,7 @@ def parse():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms while the timed region runs."""
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -106,7 +107,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.idx), "-lms", "200"], stdout=subprocess.PIPE,
+                                          "-i", str(self.idx), "-lms", "50"], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
